@@ -1,0 +1,294 @@
+"""ctypes bindings for the CPU checkers -- TEST INFRASTRUCTURE ONLY.
+
+Loads ``liborc.so`` (this repository's C restatement of the path, ``k3_oracle.c``) and,
+when present, ``_ref/libk3ref.so`` (the reference engine's own ``src/core/k3_ops.c``,
+compiled by ``oracle/Makefile``) and ``_ref/libk3ref_bench.so`` (the timed CPU baseline).
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU legs import this
+module. The product path never does.
+
+Also holds the numpy compositions the tests use to pin the C restatement against the
+reference's whole-module fixtures (``mla.json``, ``moe.json``, ``kda_layer8.json``): each
+composes orc_* kernels in the order the reference's module does, citing it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_orc = None
+_ref = None
+_refb = None
+
+f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
+i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+
+
+def build() -> None:
+    """Compile liborc.so (and _ref/ when the reference tree is present)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def orc():
+    """The restatement library, built on first use."""
+    global _orc
+    if _orc is None:
+        path = os.path.join(HERE, "liborc.so")
+        if not os.path.exists(path):
+            build()
+        lib = C.CDLL(path)
+        I, F = C.c_int, C.c_float
+        sig = {
+            "orc_rmsnorm": [f32p, f32p, f32p, I, F],
+            "orc_situ_glu": [f32p, f32p, I, F, F],
+            "orc_swiglu": [f32p, f32p, I],
+            "orc_router": [i32p, f32p, f32p, f32p, C.c_void_p, I, I, I, I, F],
+            "orc_router_scores": [f32p, f32p, f32p, I, I],
+            "orc_mxfp4_dequant": [f32p, u8p, u8p, I, I],
+            "orc_matmul_mxfp4": [f32p, f32p, u8p, u8p, I, I],
+            "orc_bank_layout": [i64p, I, I],
+            "orc_expert": [f32p, f32p, u8p, i64p, I, I, I, F, F],
+            "orc_moe_routed": [f32p, f32p, i32p, f32p, u8p, i64p, I, I, I, I, I, I, I, F, F,
+                               C.c_void_p, F],
+            "orc_kda_step": [f32p, f32p, f32p, f32p, f32p, f32p, F, I, I],
+            "orc_kda_verify": [f32p, f32p, f32p, f32p, f32p, f32p, f32p, I, I, I, F],
+            "orc_kda_commit": [f32p, f32p, f32p, f32p, f32p, I, I, I],
+            "orc_shortconv": [f32p, f32p, f32p, C.c_void_p, I, I, I],
+            "orc_l2norm": [f32p, I, F],
+            "orc_kda_decay": [f32p, f32p, f32p, f32p, f32p, I, I, F],
+            "orc_kda_prologue": [f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p,
+                                 C.c_void_p, f32p, f32p, I, I, I, I, F],
+            "orc_kda_commit_conv": [f32p, f32p, I, I, I],
+            "orc_kda_norm_gate": [f32p, f32p, f32p, I, I, I, F],
+            "orc_mla_absorbed": [f32p, f32p, f32p, f32p, f32p, f32p, I, I, I, I, I, I, I,
+                                 u64p, F],
+            "orc_attn_res": [f32p, f32p, f32p, I, I, F],
+            "orc_spec_draft": [i32p, I, I, I, I, i32p],
+            "orc_argmax": [f32p, I],
+            "orc_accept_greedy": [i32p, C.POINTER(C.c_int), i32p, f32p, i32p, I, I],
+            "orc_emit_keep": [i32p, I, I, I, I, I, C.c_void_p, I],
+        }
+        for name, args in sig.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = None
+        lib.orc_spec_draft.restype = C.c_int
+        lib.orc_argmax.restype = C.c_int
+        lib.orc_accept_greedy.restype = C.c_int
+        lib.orc_emit_keep.restype = C.c_int
+        _orc = lib
+    return _orc
+
+
+def ref():
+    """The reference engine's own numeric core, or None when it was not built here."""
+    global _ref
+    if _ref is None:
+        path = os.path.join(HERE, "_ref", "libk3ref.so")
+        if not os.path.exists(path):
+            return None
+        lib = C.CDLL(path)
+        I, F = C.c_int, C.c_float
+        lib.k3_router.argtypes = [i32p, f32p, f32p, f32p, C.c_void_p, I, I, I, I, F]
+        lib.k3_matmul_mxfp4.argtypes = [f32p, f32p, u8p, u8p, I, I, I]
+        lib.k3_mxfp4_dequant.argtypes = [f32p, u8p, u8p, I, I, I]
+        lib.k3_kda_step.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, F, I, I]
+        lib.k3_situ_glu.argtypes = [f32p, f32p, I, F, F]
+        lib.k3_rmsnorm.argtypes = [f32p, f32p, f32p, I, F]
+        lib.k3_shortconv.argtypes = [f32p, f32p, f32p, C.c_void_p, I, I, I]
+        lib.k3_kda_decay.argtypes = [f32p, f32p, f32p, f32p, f32p, I, I, F]
+        for n in ("k3_router", "k3_matmul_mxfp4", "k3_mxfp4_dequant", "k3_kda_step",
+                  "k3_situ_glu", "k3_rmsnorm", "k3_shortconv", "k3_kda_decay"):
+            getattr(lib, n).restype = None
+        _ref = lib
+    return _ref
+
+
+def ref_bench():
+    """The reference-kernel CPU baseline harness, or None when it was not built here."""
+    global _refb
+    if _refb is None:
+        path = os.path.join(HERE, "_ref", "libk3ref_bench.so")
+        if not os.path.exists(path):
+            return None
+        lib = C.CDLL(path)
+        I, F = C.c_int, C.c_float
+        lib.ref_moe_layer.argtypes = [f32p, i32p, f32p, f32p, f32p, C.c_void_p, u8p, i64p,
+                                      I, I, I, I, I, I, I, F, F, I]
+        lib.ref_moe_layer.restype = C.c_int
+        _refb = lib
+    return _refb
+
+
+# ------------------------------------------------------------------ thin wrappers --
+
+def _f(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def router(x, W, bias, topk, renorm=1, scale=1.0, lib=None):
+    """Route every row of x: (idx [T][topk] int32, w [T][topk] float32)."""
+    lib = lib or orc()
+    x, W = _f(x), _f(W)
+    T, E = x.shape
+    n = W.shape[0]
+    idx = np.zeros((T, topk), np.int32)
+    w = np.zeros((T, topk), np.float32)
+    b = _f(bias) if bias is not None else None
+    fn = lib.orc_router if lib is orc() else lib.k3_router
+    for t in range(T):
+        it = np.zeros(topk, np.int32)
+        wt = np.zeros(topk, np.float32)
+        fn(it, wt, np.ascontiguousarray(x[t]), W,
+           b.ctypes.data_as(C.c_void_p) if b is not None else None, E, n, topk, renorm,
+           float(scale))
+        idx[t], w[t] = it, wt
+    return idx, w
+
+
+def bank_layout(L, I):
+    lay = np.zeros(7, np.int64)
+    orc().orc_bank_layout(lay, L, I)
+    return lay
+
+
+def mxfp4_quant(w: np.ndarray):
+    """Quantise [R][C] fp32 to (packed [R][C/2] u8, scales [R][C/32] u8) by the rule of
+    the reference's tiny-checkpoint generator (tools/make_tiny_checkpoint.py:88-138):
+    scale = 2^(floor(log2 amax) - 2) per 32, nibble = nearest E2M1 magnitude (argmin,
+    first index on ties), sign from the element, low nibble = even element."""
+    w = np.asarray(w, np.float32)
+    R, Cc = w.shape
+    g = Cc // 32
+    blocks = w.reshape(R, g, 32)
+    amax = np.abs(blocks).max(axis=2)
+    ex = (np.floor(np.log2(np.maximum(amax, 1e-30))) - 2).astype(np.int32)
+    ex = np.clip(ex, -127, 127)
+    scales = (ex + 127).astype(np.uint8)
+    mult = np.exp2(ex.astype(np.float32)).reshape(R, g, 1)
+    xq = blocks / mult
+    lut = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
+    idx = np.argmin(np.abs(np.abs(xq)[..., None] - lut), axis=-1).astype(np.uint8)
+    nib = np.where(xq < 0, idx | 0x8, idx).astype(np.uint8)
+    packed = (nib[:, :, 0::2] | (nib[:, :, 1::2] << 4)).reshape(R, Cc // 2)
+    return np.ascontiguousarray(packed), np.ascontiguousarray(scales)
+
+
+def make_bank(rng, n_experts, L, I, std=0.02, w13_std=None):
+    """A contiguous MXFP4 expert bank in the reference's per-expert run layout."""
+    lay = bank_layout(L, I)
+    stride = int(lay[6])
+    bank = np.zeros(n_experts * stride, np.uint8)
+    for e in range(n_experts):
+        base = e * stride
+        s13 = w13_std if w13_std is not None else std
+        for (po, so, rows, cols, sd) in ((lay[0], lay[1], I, L, s13), (lay[2], lay[3], L, I, std),
+                                         (lay[4], lay[5], I, L, s13)):
+            w = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sd)
+            p, s = mxfp4_quant(w)
+            bank[base + po: base + po + p.size] = p.ravel()
+            bank[base + so: base + so + s.size] = s.ravel()
+    return bank, lay
+
+
+def moe_routed(z, idx, wt, bank, lay, L, I, topk, n_routed, n_shared, act, b1=4.0, b2=25.0,
+               latent_norm=None, eps=1e-5):
+    z = _f(z)
+    T = z.shape[0]
+    acc = np.zeros((T, L), np.float32)
+    ln = _f(latent_norm) if latent_norm is not None else None
+    orc().orc_moe_routed(acc, z, np.ascontiguousarray(idx, np.int32), _f(wt), bank, lay, T, L,
+                         I, topk, n_routed, n_shared, act, float(b1), float(b2),
+                         ln.ctypes.data_as(C.c_void_p) if ln is not None else None, float(eps))
+    return acc
+
+
+def kda_verify(state, q, k, v, alpha, beta, qscale):
+    T, H, D = q.shape
+    o = np.zeros((T, H, D), np.float32)
+    orc().orc_kda_verify(o, _f(state), _f(q), _f(k), _f(v), _f(alpha), _f(beta), T, H, D,
+                         float(qscale))
+    return o
+
+
+def kda_commit(state, k, v, alpha, beta, n):
+    st = _f(state).copy()
+    H, D = st.shape[0], st.shape[1]
+    orc().orc_kda_commit(st, _f(k), _f(v), _f(alpha), _f(beta), int(n), H, D)
+    return st
+
+
+def mla_absorbed(q_nope, q_rope, kv_b, lat, rope, cached, mask, scale, vh):
+    T, H, qn = q_nope.shape
+    qr = q_rope.shape[2]
+    kvl = lat.shape[1]
+    out = np.zeros((T, H, vh), np.float32)
+    orc().orc_mla_absorbed(out, _f(q_nope), _f(q_rope), _f(kv_b), _f(lat), _f(rope), T, H, qn,
+                           qr, vh, kvl, int(cached),
+                           np.ascontiguousarray(mask, np.uint64), float(scale))
+    return out
+
+
+def chain_masks(T):
+    """Causal chain: query t sees new rows 0..t."""
+    return np.array([(1 << (t + 1)) - 1 for t in range(T)], np.uint64)
+
+
+def tree_masks(parent):
+    """Ancestor masks for a draft tree given parent[i] (-1 for the root): node i sees
+    itself and every ancestor."""
+    T = len(parent)
+    m = np.zeros(T, np.uint64)
+    for i in range(T):
+        bits, j = 0, i
+        while j >= 0:
+            bits |= 1 << j
+            j = parent[j]
+        m[i] = bits
+    return m
+
+
+def rmsnorm(x, w, eps):
+    x = _f(x)
+    y = np.empty_like(x)
+    flat, yf = x.reshape(-1, x.shape[-1]), y.reshape(-1, x.shape[-1])
+    for r in range(flat.shape[0]):
+        out = np.empty(flat.shape[1], np.float32)
+        orc().orc_rmsnorm(out, np.ascontiguousarray(flat[r]), _f(w), flat.shape[1], float(eps))
+        yf[r] = out
+    return y
+
+
+def matmul_d(x, W):
+    """y = W x with a double accumulator per output (the reference's fp32 k3_matmul
+    contract up to its 16-accumulator partition, k3_ops.c:363-399), rounded to float."""
+    return (np.asarray(x, np.float64) @ np.asarray(W, np.float64).T).astype(np.float32)
+
+
+def mla_forward(x, wts, cfg):
+    """The whole gated NoPE MLA of the reference's k3_mla (src/core/k3_ops.c:1115-1615)
+    in absorbed form over positions 0..T-1 of one sequence: q_a -> RMSNorm -> q_b;
+    kv_a -> RMSNorm on the latent (not the rope slot); the absorbed core (orc_mla_absorbed)
+    with the causal chain; sigmoid output gate then o_proj. Used to pin orc_mla_absorbed
+    against the reference's mla.json fixture."""
+    H, qn, qr, vh, kvl = cfg["n_heads"], cfg["qk_nope"], cfg["qk_rope"], cfg["v_head"], cfg["kv_lora"]
+    T = x.shape[0]
+    ql = rmsnorm(matmul_d(x, wts["q_a"]), wts["q_a_norm"], cfg["eps"])
+    q = matmul_d(ql, wts["q_b"]).reshape(T, H, qn + qr)
+    ct = matmul_d(x, wts["kv_a"])
+    lat = rmsnorm(ct[:, :kvl], wts["kv_a_norm"], cfg["eps"])
+    rope = np.ascontiguousarray(ct[:, kvl:])
+    scale = np.float32(1.0) / np.sqrt(np.float32(qn + qr))
+    acc = mla_absorbed(np.ascontiguousarray(q[:, :, :qn]), np.ascontiguousarray(q[:, :, qn:]),
+                       wts["kv_b"], lat, rope, 0, chain_masks(T), scale, vh)
+    acc = acc.reshape(T, H * vh)
+    if wts.get("g") is not None:
+        g = matmul_d(x, wts["g"])
+        acc = acc * (np.float32(1) / (np.float32(1) + np.exp(-g, dtype=np.float32)))
+    return matmul_d(acc, wts["o"])
