@@ -1,0 +1,422 @@
+#!/usr/bin/env python3
+"""Benchmark: one K3-shaped MoE layer in verify mode.
+
+A step is one verify pass of the layer over B*(1+k) tokens -- B sequences, each feeding
+its pending token plus k drafts -- through the library's C ABI: the sigmoid router with
+bias-steered top-8 over 384 experts, the grouped MXFP4 expert FFN (d_model 7168, FFN
+2048, SwiGLU) with the shared expert, and the top-k-ordered combine. Weights are
+N(0, 0.02) quantised to packed E2M1 + E8M0/32 (the reference's quantisation rule),
+activations bf16 N(0, 1), router bias N(0, 0.01); all synthetic and seeded.
+
+value  verified tokens/s with inputs resident in HBM (device-timed, CUDA events)
+e2e    the same through the public call with host buffers: pinned host x -> device,
+       the layer, device -> host of the layer output and routing
+N > 1  expert parallel: 384 experts sharded 384/N per GPU, each rank verifies its own
+       B*(1+k) tokens (weak scaling), NCCL all-to-all dispatch and combine.
+
+--impl reference times the reference engine's own C kernels (k3_router, k3_matmul_mxfp4,
+compiled from its sources into oracle/_ref) on the host cores, same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L_DIM, I_DIM, N_ROUTED, N_SHARED, TOPK = 7168, 2048, 384, 1, 8
+METRIC = "accepted tok/s (spec decode) & verify-step ms; expert-GEMM HBM GB/s vs peak"
+
+
+def load_pkg():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("k3b200", os.path.join(ROOT, "kimi-k3-for-me_b200", "__init__.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["k3b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------- workload ----
+def bank_layout(L, I):
+    pw, sw, pd, sd = I * (L // 2), I * (L // 32), L * (I // 2), L * (I // 32)
+    offs = dict(p1=0, s1=pw, p2=pw + sw, s2=pw + sw + pd, p3=pw + sw + pd + sd,
+                s3=pw + sw + pd + sd + pw)
+    run = pw + sw + pd + sd + pw + sw
+    return offs, (run + 255) // 256 * 256
+
+
+def quant_mxfp4_torch(w):
+    """MXFP4 by the reference generator's rule (tools/make_tiny_checkpoint.py:88-138):
+    per 32 elements scale 2^(floor(log2 amax) - 2), nearest E2M1 magnitude (lower level
+    on exact ties), low nibble = even element. Returns (packed u8 [R][C/2], scales u8)."""
+    import torch
+    R, Cc = w.shape
+    g = w.view(R, Cc // 32, 32)
+    amax = g.abs().amax(dim=2).clamp_min(1e-30)
+    ex = (torch.floor(torch.log2(amax)) - 2).clamp(-127, 127)
+    scales = (ex + 127).to(torch.uint8)
+    xq = g / torch.exp2(ex).unsqueeze(2)
+    mids = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], device=w.device)
+    mag = torch.bucketize(xq.abs().contiguous(), mids, right=False).to(torch.uint8)
+    nib = mag | ((xq < 0).to(torch.uint8) << 3)
+    nib = nib.view(R, Cc)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).contiguous()
+    return packed, scales.view(R, Cc // 32).contiguous()
+
+
+def make_bank_device(n_experts, L, I, seed, device):
+    import torch
+    offs, stride = bank_layout(L, I)
+    bank = torch.empty(n_experts * stride, dtype=torch.uint8, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    for e in range(n_experts):
+        base = e * stride
+        for (po, so, rows, cols) in ((offs["p1"], offs["s1"], I, L), (offs["p2"], offs["s2"], L, I),
+                                     (offs["p3"], offs["s3"], I, L)):
+            w = torch.randn((rows, cols), generator=gen, device=device) * 0.02
+            p, s = quant_mxfp4_torch(w)
+            bank[base + po: base + po + p.numel()] = p.view(-1)
+            bank[base + so: base + so + s.numel()] = s.view(-1)
+    return bank, offs, stride
+
+
+def make_inputs(M, seed, device):
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    x = torch.randn((M, L_DIM), generator=gen, device=device).to(torch.bfloat16).float()
+    gate = torch.randn((N_ROUTED, L_DIM), generator=gen, device=device) * 0.02
+    bias = torch.randn((N_ROUTED,), generator=gen, device=device) * 0.01
+    return x.contiguous(), gate.contiguous(), bias.contiguous()
+
+
+def unique_experts_bytes(idx_np, stride_bytes_per_expert):
+    u = len(np.unique(idx_np[idx_np >= 0]))
+    return u, u * stride_bytes_per_expert
+
+
+# ------------------------------------------------------------------------ clocks ---
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline ---
+def cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nthreads):
+    """The reference's kernels over T tokens on the host; returns (seconds, out, idx)."""
+    from oracle import oracle as O
+    lib = O.ref_bench()
+    if lib is None:
+        return None
+    lay = np.array([offs["p1"], offs["s1"], offs["p2"], offs["s2"], offs["p3"], offs["s3"], stride],
+                   np.int64)
+    out = np.zeros((T, L_DIM), np.float32)
+    idx = np.zeros((T, TOPK), np.int32)
+    wt = np.zeros((T, TOPK), np.float32)
+    t0 = time.perf_counter()
+    rc = lib.ref_moe_layer(out, idx, wt, np.ascontiguousarray(x_np[:T]), gate_np,
+                           bias_np.ctypes.data, bank_np, lay, T, L_DIM, I_DIM, N_ROUTED, N_SHARED,
+                           TOPK, 1, 4.0, 25.0, nthreads)
+    dt = time.perf_counter() - t0
+    if rc != 0:
+        return None
+    return dt, out, idx
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------- arms ------
+def run_reference(args):
+    """--impl reference: the reference's own C kernels on all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+    from oracle import oracle as O
+    if O.ref_bench() is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libk3ref_bench.so was not built (reference sources absent when built)"}))
+        return 0
+    M = args.B * (1 + args.k)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    bank, offs, stride = (make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, dev)
+                          if dev == "cuda" else make_bank_cpu(args.seed))
+    x, gate, bias = make_inputs(M, args.seed + 1, dev)
+    bank_np = bank.cpu().numpy()
+    x_np, gate_np, bias_np = x.cpu().numpy(), gate.cpu().numpy(), bias.cpu().numpy()
+    del bank
+    nth = host_threads()
+    T = min(M, args.ref_tokens) if args.ref_tokens else M
+    for _ in range(args.warmup):
+        cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nth)
+    times = []
+    for _ in range(args.steps):
+        dt, _, _ = cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nth)
+        times.append(dt)
+    ms = 1000.0 * statistics.median(times)
+    val = T / (ms / 1000.0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms * M / T, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64-accumulate MXFP4 x fp32 (reference CPU)",
+        "data": "synthetic (seeded)",
+        "config": workload_config(args, M),
+        "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": nth, "kind": "reference",
+                         "sample": f"{T} of {M} tokens per step through the reference's k3_router + "
+                                   f"k3_matmul_mxfp4 expert loop, {nth} host threads, no OpenMP"},
+        "e2e": {"value": round(val, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "all_step_ms": [round(1000 * t, 3) for t in times],
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def make_bank_cpu(seed):
+    raise SystemExit("the reference arm builds its weights on the GPU box; no CUDA device here")
+
+
+def workload_config(args, M):
+    return {"workload": f"K3 MoE layer verify (BASELINE config 2): B={args.B} sequences x (1+k={1 + args.k}) "
+                        f"= {M} tokens/step/GPU",
+            "d_model": L_DIM, "experts": N_ROUTED, "shared": N_SHARED, "topk": TOPK,
+            "ffn": I_DIM, "act": "SwiGLU", "weights": "MXFP4 (E2M1 + E8M0/32), N(0,0.02)",
+            "activations": "bf16 N(0,1) (fp32 containers)", "B": args.B, "k": args.k,
+            "tokens_per_step": M * args.gpus,
+            "parallelism": f"ep{args.gpus}" if args.gpus > 1 else "single",
+            "l2": "weights streamed per step (GBs) exceed the 126 MB L2; no flush needed"}
+
+
+def run_b200(args):
+    import torch
+    k3 = load_pkg()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        import ep
+        return ep.run_ep(args, k3, rank, world, dev)
+
+    M = args.B * (1 + args.k)
+    bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, dev)
+    x, gate, bias = make_inputs(M, args.seed + 1, dev)
+    kb = k3.ExpertBank(bank, N_ROUTED + N_SHARED, L_DIM, I_DIM)
+    ws = k3.workspace(k3.lib.k3gpu_moe_workspace(M, TOPK, N_SHARED, L_DIM, I_DIM, N_ROUTED), dev)
+    out = torch.empty((M, L_DIM), dtype=torch.float32, device=dev)
+    idx = torch.empty((M, TOPK), dtype=torch.int32, device=dev)
+    wt = torch.empty((M, TOPK), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        k3.moe_layer(x, gate, bias, kb, TOPK, N_ROUTED, N_SHARED, k3.ACT_SWIGLU, ws=ws, out=out,
+                     idx=idx, wt=wt, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dev_ms = ev0.elapsed_time(ev1) / args.steps
+
+    # end to end through the public call with host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((M, L_DIM), dtype=torch.float32).pin_memory()
+    idx_host = torch.empty((M, TOPK), dtype=torch.int32).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        k3.moe_layer(x_dev, gate, bias, kb, TOPK, N_ROUTED, N_SHARED, k3.ACT_SWIGLU, ws=ws,
+                     out=out, idx=idx, wt=wt, stream=stream)
+        out_host.copy_(out, non_blocking=True)
+        idx_host.copy_(idx, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / args.steps
+    clk = clocks.stop()
+
+    # roofline of the dominant kernel (gate/up expert stream), timed live with events
+    k3.moe_phase_timing(True)
+    phases = []
+    for _ in range(max(3, min(args.steps, 10))):
+        step()
+        phases.append(k3.moe_phase_ms())
+    k3.moe_phase_timing(False)
+    ph = np.median(np.array(phases), axis=0).tolist()
+    idx_np = idx.cpu().numpy()
+    u_routed = len(np.unique(idx_np))
+    u = u_routed + N_SHARED
+    pairs = M * (TOPK + N_SHARED)
+    w13 = 2 * I_DIM * (L_DIM // 2 + L_DIM // 32)
+    w2 = L_DIM * (I_DIM // 2 + I_DIM // 32)
+    gateup_bytes = u * w13 + M * L_DIM * 4 + pairs * I_DIM * 4
+    down_bytes = u * w2 + pairs * I_DIM * 4 + pairs * L_DIM * 4
+    hbm, peak_kind = peaks()
+    achieved = gateup_bytes / (ph[2] * 1e-3) / 1e9
+    expert_gbs = (gateup_bytes + down_bytes) / ((ph[2] + ph[3]) * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("bytes_per_launch_scaled")
+        except (OSError, ValueError):
+            traffic = None
+
+    # CPU baseline: the reference's kernels on a bounded sample of the same workload
+    cpu = None
+    if not args.no_cpu:
+        Ts = min(M, args.cpu_tokens)
+        bank_np = bank.cpu().numpy()
+        r = cpu_reference_run(x.cpu().numpy(), gate.cpu().numpy(), bias.cpu().numpy(), bank_np,
+                              offs, stride, Ts, host_threads())
+        del bank_np
+        if r is not None:
+            dt, ref_out, ref_idx = r
+            got = out.cpu().numpy()[:Ts]
+            same_idx = bool(np.array_equal(ref_idx, idx_np[:Ts]))
+            err = float(np.linalg.norm(got - ref_out) / max(np.linalg.norm(ref_out), 1e-30))
+            cpu = {"value": round(Ts / dt, 3), "unit": "tok/s", "cores": host_threads(),
+                   "kind": "reference",
+                   "sample": f"{Ts} of {M} tokens of the same step through the reference's k3_router + "
+                             f"k3_matmul_mxfp4 expert loop ({dt:.2f} s)",
+                   "routing_bitexact": same_idx, "out_rel_l2_vs_gpu": err}
+
+    line = {
+        "metric": METRIC, "value": round(M / (dev_ms * 1e-3), 3), "unit": "tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "MXFP4 weights x fp32 activations, fp32 accumulate", "data": "synthetic (seeded)",
+        "config": workload_config(args, M),
+        "e2e": {"value": round(M / (e2e_ms * 1e-3), 3), "unit": "tok/s",
+                "h2d_bytes_per_step": int(x.numel() * 4),
+                "d2h_bytes_per_step": int(out.numel() * 4 + idx.numel() * 4), "ms_per_step": round(e2e_ms, 4)},
+        "roofline": {"bound": "hbm", "kernel": "moe_gateup_kernel", "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": traffic, "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": int(gateup_bytes)},
+        "expert_gemm": {"gbs": round(expert_gbs, 1), "frac": round(expert_gbs / hbm, 4),
+                        "unique_experts": u, "bytes": int(gateup_bytes + down_bytes)},
+        "phase_ms": {"router": round(ph[0], 4), "plan": round(ph[1], 4), "gateup": round(ph[2], 4),
+                     "down": round(ph[3], 4), "combine": round(ph[4], 4)},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clk,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--B", type=int, default=8, help="sequences per GPU")
+    ap.add_argument("--k", type=int, default=8, help="drafts per sequence")
+    ap.add_argument("--seed", type=int, default=2024)
+    ap.add_argument("--cpu-tokens", type=int, default=72, help="tokens in the CPU baseline sample")
+    ap.add_argument("--ref-tokens", type=int, default=0, help="tokens per reference-arm step (0 = all)")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

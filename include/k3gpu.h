@@ -1,0 +1,250 @@
+/* k3gpu.h -- the C ABI of the B200 speculative-verification library (libk3gpu.so).
+ *
+ * This is the drop-in boundary between the reference engine's C99 host (its k3_* API,
+ * include/k3/k3.h of andrewd780/kimi-k3-for-me, and its CLI's verify sweep,
+ * src/cli/k3_run.c:2860-2966) and hand-written sm_100a CUDA kernels. Each entry point
+ * names the reference function it replaces (file:line in the reference tree).
+ *
+ * Conventions, for every k3gpu_* function that takes a `stream`:
+ *   - pointers are DEVICE pointers unless the comment says "host";
+ *   - `stream` is a cudaStream_t passed as void * (NULL = the legacy default stream), so
+ *     this header needs no CUDA include; work is enqueued, never synchronised, unless the
+ *     comment says otherwise;
+ *   - the return value is a status: K3GPU_OK, or a negative code. Arguments are checked
+ *     on the host before anything is enqueued; a failed check enqueues nothing and
+ *     leaves every output untouched. Nothing aborts and nothing traps on the device:
+ *     where a kernel itself detects a bad index it records it in the library's device
+ *     status word (k3gpu_device_status) and skips the access;
+ *   - all buffers, scratch included, are caller-owned; *_workspace() returns the bytes
+ *     a call needs (the reference's own ownership rule, docs/API.md:47-64, with
+ *     k3_*_scratch() sizing);
+ *   - calls are reentrant; concurrent calls on different streams must not share a
+ *     workspace.
+ */
+#ifndef K3GPU_H
+#define K3GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status ---- */
+enum {
+    K3GPU_OK = 0,
+    K3GPU_EINVAL = -1,     /* null pointer, size out of range, misaligned buffer        */
+    K3GPU_ECAPACITY = -2,  /* workspace, log or cache capacity too small                */
+    K3GPU_ECUDA = -3,      /* a CUDA launch/runtime error; see k3gpu_last_cuda_error()  */
+    K3GPU_EDEVICE = -4     /* a device-side check failed; see k3gpu_device_status()     */
+};
+
+const char *k3gpu_strerror(int status);
+/* The cudaError_t behind the last K3GPU_ECUDA returned on this thread. */
+int k3gpu_last_cuda_error(void);
+/* Library version, major*10000 + minor*100 + patch. */
+int k3gpu_version(void);
+/* Read (host, synchronous on the given device's default stream) and clear the device
+ * status word: 0 when no kernel has flagged an out-of-range index since the last call. */
+int k3gpu_device_status(int device, int *status_out);
+
+/* ------------------------------------------------------------------ router ---- */
+/* Replaces k3_router (include/k3/k3.h:311-313, src/core/k3_ops.c:1624-1719) for T tokens
+ * in one call. x [T][hidden] fp32, W [n_experts][hidden] fp32 row-major, bias
+ * [n_experts] fp32 or NULL -> idx [T][topk] int32 and w [T][topk] fp32 in descending
+ * selection order. Same arithmetic as the reference: one double chain per (token,
+ * expert) in ascending i, score = 1/(1+exp(-(float)acc)) with a correctly rounded exp,
+ * selection on score+bias by repeated max with first-index ties, weights from the
+ * UNBIASED scores, double renormaliser 1/(sum+1e-20) rounded to float, * routed_scale.
+ * Limits: 1 <= topk <= 64, topk <= n_experts <= 1024, hidden >= 1. The workspace holds
+ * the [T][n_experts] scores (k3gpu_router_workspace bytes). */
+size_t k3gpu_router_workspace(int T, int n_experts);
+int k3gpu_router(int *idx, float *w, const float *x, const float *W, const float *bias,
+                 int T, int hidden, int n_experts, int topk, int renorm, float routed_scale,
+                 void *workspace, size_t ws_bytes, void *stream);
+
+/* ------------------------------------------------------------ expert bank ---- */
+/* Device-resident MXFP4 experts. Expert e is the byte run base + e*stride holding, at
+ * the given offsets, the six tensors the reference's loader reads as one contiguous run
+ * (src/io/k3_load.h:1-22; K3ExpertQ, include/k3/k3.h:512-516):
+ *   p1 [I][L/2]  s1 [I][L/32]   w1, gate    (low nibble = EVEN element, E8M0 per 32)
+ *   p2 [L][I/2]  s2 [L][I/32]   w2, down
+ *   p3 [I][L/2]  s3 [I][L/32]   w3, up
+ * Runs n_routed .. n_routed+n_shared-1 are the shared experts. L and I are multiples of
+ * 32; base, stride and every offset are multiples of 16 bytes. */
+typedef struct {
+    const uint8_t *base;
+    int64_t stride;
+    int64_t p1, s1, p2, s2, p3, s3;
+    int n_experts;          /* runs in the bank: routed + shared */
+    int L, I;               /* expert input/output width, intermediate width */
+} K3GpuExpertBank;
+
+/* Fill the offsets and stride of the packed run layout above (stride rounded up to 256
+ * bytes); leaves base and n_experts to the caller. Host only. */
+void k3gpu_bank_layout(K3GpuExpertBank *bank, int L, int I);
+
+/* Replaces k3_mxfp4_dequant (include/k3/k3.h:863-864) for group 32: out [rows][in] fp32
+ * from packed [rows][in/2] and scales [rows][in/32]; the same nibble decode and E8M0
+ * scaling the expert kernels apply in registers (exact: no rounding anywhere).
+ * in % 32 == 0; packed 16-byte aligned. */
+int k3gpu_mxfp4_dequant(float *out, const uint8_t *packed, const uint8_t *scales, int rows,
+                        int in, void *stream);
+
+/* Activation of the expert FFN, applied to [gate | up]. */
+enum { K3GPU_ACT_SITU = 0, K3GPU_ACT_SWIGLU = 1 };
+
+/* ------------------------------------------------------------------- MoE ----- */
+/* Workspace bytes for k3gpu_moe_experts / k3gpu_moe_layer. */
+size_t k3gpu_moe_workspace(int T, int topk, int n_shared, int L, int I, int n_routed);
+
+/* Replaces the routed half of k3_moe_prefill (src/core/k3_ops.c:2058-2132) plus the
+ * shared experts, on device-resident MXFP4 experts. z [T][L] fp32 expert inputs,
+ * idx/wt [T][topk] from k3gpu_router -> out [T][L] fp32:
+ *   out[t] = RMSNorm?( sum_j wt[t][j] * expert_{idx[t][j]}(z[t]) )  (sum in top-k order)
+ *          + sum_s shared_s(z[t])                                     (unweighted)
+ * expert(z) = W2 . act(W1 z, W3 z). latent_norm [L] or NULL skips the RMSNorm (eps).
+ * idx < 0 drops that slot, as the reference does for a failed expert. b1, b2 are the
+ * SiTU caps (ignored for SwiGLU). Each unique expert's weights are read once per call.
+ * Limits: T*(topk+n_shared) <= 1<<20, n_routed+n_shared == bank->n_experts <= 4096. */
+int k3gpu_moe_experts(float *out, const float *z, const int *idx, const float *wt,
+                      const K3GpuExpertBank *bank, int T, int topk, int n_routed,
+                      int n_shared, int act, float b1, float b2, const float *latent_norm,
+                      float eps, void *workspace, size_t ws_bytes, void *stream);
+
+/* One MoE layer of the single-layer verify configuration (no latent projections, so
+ * L == hidden): k3gpu_router on x, then k3gpu_moe_experts with z = x and no latent
+ * norm. idx/wt [T][topk] receive the routing decisions. */
+int k3gpu_moe_layer(float *out, int *idx, float *wt, const float *x, const float *gate_W,
+                    const float *bias, const K3GpuExpertBank *bank, int T, int topk,
+                    int n_routed, int n_shared, int act, float b1, float b2, int renorm,
+                    float routed_scale, void *workspace, size_t ws_bytes, void *stream);
+
+/* Per-phase timing of the MoE calls, for roofline reporting. When enabled (host, per
+ * process), every k3gpu_moe_experts / k3gpu_moe_layer call records CUDA events on its
+ * stream around its kernels; k3gpu_moe_phase_ms then waits for the last call and writes
+ * the device milliseconds of its phases into ms[0..n): 0 router (0 for
+ * k3gpu_moe_experts), 1 plan, 2 gate/up expert stream, 3 down expert stream, 4 combine.
+ * Returns the number written. Not for concurrent calls. */
+int k3gpu_moe_phase_timing(int enable);
+int k3gpu_moe_phase_ms(float *ms, int n);
+
+/* --------------------------------------------------------------------- KDA ----- */
+/* The KDA recurrence of a tentative verify sweep, k3_kda_layer_log's step 6
+ * (src/core/k3_ops.c:2342-2364) for B sequences. state [B][H][D][D] fp32 is READ ONLY
+ * (the sweep never touches the carried state; include/k3/k3.h:662-700). q, k, v, alpha
+ * [B][T][H][D], beta [B][T][H] -> o [B][T][H][D]; q is multiplied by qscale in float
+ * first. Bit-identical to k3_kda_step chained over t (same float operations in the same
+ * order, zero rows of k and q skipped as the reference skips them). The operands k, v,
+ * alpha, beta ARE the log a commit replays. D in {16, 32, 64, 128}; 1 <= T <= 64. */
+int k3gpu_kda_verify(float *o, const float *state, const float *q, const float *k,
+                     const float *v, const float *alpha, const float *beta, int B, int T,
+                     int H, int D, float qscale, void *stream);
+
+/* Replaces k3_kda_advance's recurrence (src/core/k3_ops.c:2391-2409): commit the first
+ * n[b] logged positions of sequence b into state[b] in place, bit-identical to feeding
+ * those positions alone. n is a DEVICE array [B] (so an on-device accept can feed it
+ * without a host round trip); entries outside 0..T are clamped to that range and
+ * flagged in the device status word. The log operands are those given to
+ * k3gpu_kda_verify, [B][T][H][D] (beta [B][T][H]). */
+int k3gpu_kda_commit(float *state, const float *k, const float *v, const float *alpha,
+                     const float *beta, const int *n, int B, int T, int H, int D,
+                     void *stream);
+
+/* The KDA prologue, src/core/k3_ops.c:2286-2303 for B sequences: from the projection
+ * outputs q, k, v [B][T][P] (P = H*D), z [B][T][P] (f_b output, before dt_bias) and
+ * b [B][T][H], with the carried ShortConv history hist [B][3][P][K-1] (read only):
+ * ShortConv+SiLU on q, k, v in place, L2 norm of q and k per head (sum of squares in
+ * double, eps 1e-6), alpha = exp(lb*sigmoid(exp(A_log[h])*(z+dt_bias))) [B][T][P] and
+ * beta = sigmoid(b) [B][T][H]. pre [B][T][3][P] receives the PRE-conv q, k, v, the rows
+ * the conv-history commit replays (K3KdaLog rows, include/k3/k3.h:716-724).
+ * 2 <= K <= 8. */
+int k3gpu_kda_prologue(float *q, float *k, float *v, float *alpha, float *beta, float *pre,
+                       const float *z, const float *b, const float *q_conv,
+                       const float *k_conv, const float *v_conv, const float *hist,
+                       const float *A_log, const float *dt_bias, int B, int T, int H, int D,
+                       int K, float lb, void *stream);
+
+/* Replaces kda_replay_conv_ (src/core/k3_ops.c:2207-2223): advance the ShortConv history
+ * hist [B][3][P][K-1] in place by the first n[b] pre-conv rows of pre [B][T][3][P].
+ * n is a device array [B], clamped to 0..T. */
+int k3gpu_kda_commit_conv(float *hist, const float *pre, const int *n, int B, int T, int H,
+                          int D, int K, void *stream);
+
+/* src/core/k3_ops.c:2375-2379: per-head RMSNorm over D (double sum) then the sigmoid
+ * gate, in place on o [R][H][D] with gate [R][H*D], R = B*T rows. */
+int k3gpu_kda_norm_gate(float *o, const float *gate, const float *o_norm, int R, int H,
+                        int D, float eps, void *stream);
+
+/* --------------------------------------------------------------------- MLA ----- */
+/* Workspace bytes for k3gpu_mla_absorbed. */
+size_t k3gpu_mla_workspace(int B, int T, int H, int kv_lora, int max_ctx);
+
+/* Absorbed MLA over the compressed cache with a chain or tree mask, the --mla-absorb
+ * branch of k3_mla_cached (src/core/k3_ops.c:1417-1540) for B sequences of T query
+ * nodes each:
+ *   q_abs[h] = W_uk[h]^T q_nope[h]
+ *   score[s] = scale * (q_abs[h] . lat[s] + q_rope[h] . rope[s])   for visible s
+ *   u[h]     = sum_s softmax(score)[s] * lat[s]
+ *   out[h]   = W_uv[h] u[h]
+ * q_nope [B][T][H][qk_nope], q_rope [B][T][H][qk_rope] fp32; kv_b [H*(qk_nope+v_head)]
+ * [kv_lora] fp32 (the reference's kv_b rows: key rows then value rows per head);
+ * lat [B][cap][kv_lora] and rope [B][cap][qk_rope] bf16 (uint16 bit patterns) hold
+ * positions 0..cached[b]+T-1 (the T new rows already appended at cached[b]..);
+ * cached is a DEVICE array [B]; mask [T] uint64 (host-side meaning, device array):
+ * query t sees every row below cached[b] and new row j iff bit j of mask[t] is set
+ * (chain: bits 0..t; tree: the node's ancestors and itself). out [B][T][H][v_head] fp32
+ * is the attention output before the output gate. T <= 64, kv_lora in {128, 256, 512},
+ * qk_rope <= 64, qk_nope and v_head <= 256. */
+int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *q_rope,
+                       const float *kv_b, const uint16_t *lat, const uint16_t *rope,
+                       const int *cached, const uint64_t *mask, int B, int T, int H,
+                       int qk_nope, int qk_rope, int v_head, int kv_lora, int cap,
+                       int max_ctx, float scale, void *workspace, size_t ws_bytes,
+                       void *stream);
+
+/* ----------------------------------------------------------------- accept ------ */
+/* The greedy verify-and-accept of the CLI's sweep (src/cli/k3_run.c:2924-2928 with
+ * argmax_ :138-139) for B sequences on the device: arg[b][i] = first index of the
+ * maximum of logits [B][nd+1][vocab]; m = longest prefix with arg[b][i] == d[b][i]
+ * (drafts [B][nd]); emit[b][0..m) = d, emit[b][m] = arg[b][m] (the bonus token);
+ * n_emit[b] = m + 1. nd_b [B] (device, may be NULL = nd for all) limits each sequence's
+ * draft count. emit/arg are [B][nd+1]. */
+int k3gpu_accept_greedy(int *emit, int *n_emit, int *arg, const float *logits,
+                        const int *drafts, const int *nd_b, int B, int nd, int vocab,
+                        void *stream);
+
+/* Greedy acceptance over a draft TREE of T nodes (node 0 = the pending token, parent[0]
+ * = -1, parent[i] < i; tok[i] the drafted id of node i, tok[0] unused). A child i is
+ * accepted when its parent is accepted and tok[i] == argmax of the parent's logits;
+ * among accepted children of one node the lowest index wins. The accepted path is
+ * emitted in order, then the bonus argmax of its last node. logits [B][T][vocab];
+ * parent/tok are device arrays [T] and [B][T]; path [B][T] receives the accepted node
+ * indices (root first), emit [B][T] the emitted ids, n_emit [B] their count. */
+int k3gpu_accept_tree_greedy(int *emit, int *n_emit, int *path, int *arg,
+                             const float *logits, const int *tok, const int *parent, int B,
+                             int T, int vocab, void *stream);
+
+/* Temperature sampling with the speculative rejection rule for point-mass drafts (the
+ * n-gram drafter proposes one id per position with probability 1): position i's draft
+ * d is accepted with probability p_i(d) = softmax(logits_i / temp)(d), drawn with
+ * Philox4x32-10 (Salmon et al., SC'11) keyed by seed and counter (offset, b, i); on the
+ * first rejection the replacement is drawn from p_i with d removed and renormalised, and
+ * after a full acceptance the bonus is drawn from p_nd. Shapes as k3gpu_accept_greedy.
+ * temp > 0. */
+int k3gpu_accept_sample(int *emit, int *n_emit, const float *logits, const int *drafts,
+                        const int *nd_b, int B, int nd, int vocab, float temp,
+                        uint64_t seed, uint64_t offset, void *stream);
+
+/* ---------------------------------------------------------------- drafter ------ */
+/* Host C (no GPU): the reference's n-gram drafter, spec_draft (src/cli/k3_run.c:450-491),
+ * with the n range and cap as parameters (the reference fixes n = 4 then 3 and clamps
+ * cap to K3_SPEC_MAX = 8). seq [T] host, out [cap] host; returns the draft count. */
+int k3_spec_draft_ngram(const int *seq, int T, int cap, int nmax, int nmin, int *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* K3GPU_H */

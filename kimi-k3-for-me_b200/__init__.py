@@ -1,0 +1,293 @@
+"""Python view of libk3gpu.so, the B200 speculative-verification library.
+
+This mirrors the C ABI of ``include/k3gpu.h`` one function at a time (ctypes, device
+pointers taken from torch CUDA tensors). torch is only the plumbing here -- device
+memory and streams; every computation runs in the library's own sm_100a kernels. There
+is no CPU fallback: importing this module on a box without the built library, or calling
+it without a CUDA device, raises.
+
+The directory name is not a Python identifier, so callers load it by path::
+
+    spec = importlib.util.spec_from_file_location("k3b200", "<repo>/kimi-k3-for-me_b200/__init__.py")
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libk3gpu.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is missing: build it with `python {os.path.join(PKG, 'build.py')}` "
+        "(there is no CPU fallback for this library)")
+
+lib = C.CDLL(LIB_PATH)
+
+VP, I, F, SZ = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+U64 = C.c_uint64
+
+K3GPU_OK, K3GPU_EINVAL, K3GPU_ECAPACITY, K3GPU_ECUDA, K3GPU_EDEVICE = 0, -1, -2, -3, -4
+ACT_SITU, ACT_SWIGLU = 0, 1
+
+
+class K3GpuExpertBank(C.Structure):
+    _fields_ = [("base", VP), ("stride", C.c_int64), ("p1", C.c_int64), ("s1", C.c_int64),
+                ("p2", C.c_int64), ("s2", C.c_int64), ("p3", C.c_int64), ("s3", C.c_int64),
+                ("n_experts", I), ("L", I), ("I", I)]
+
+
+_SIGS = {
+    "k3gpu_strerror": ([I], C.c_char_p),
+    "k3gpu_last_cuda_error": ([], I),
+    "k3gpu_version": ([], I),
+    "k3gpu_device_status": ([I, C.POINTER(I)], I),
+    "k3gpu_router_workspace": ([I, I], SZ),
+    "k3gpu_router": ([VP, VP, VP, VP, VP, I, I, I, I, I, F, VP, SZ, VP], I),
+    "k3gpu_bank_layout": ([C.POINTER(K3GpuExpertBank), I, I], None),
+    "k3gpu_mxfp4_dequant": ([VP, VP, VP, I, I, VP], I),
+    "k3gpu_moe_workspace": ([I, I, I, I, I, I], SZ),
+    "k3gpu_moe_experts": ([VP, VP, VP, VP, C.POINTER(K3GpuExpertBank), I, I, I, I, I, F, F, VP,
+                           F, VP, SZ, VP], I),
+    "k3gpu_moe_layer": ([VP, VP, VP, VP, VP, VP, C.POINTER(K3GpuExpertBank), I, I, I, I, I, F, F,
+                         I, F, VP, SZ, VP], I),
+    "k3gpu_moe_phase_timing": ([I], I),
+    "k3gpu_moe_phase_ms": ([C.POINTER(F), I], I),
+    "k3gpu_kda_verify": ([VP, VP, VP, VP, VP, VP, VP, I, I, I, I, F, VP], I),
+    "k3gpu_kda_commit": ([VP, VP, VP, VP, VP, VP, I, I, I, I, VP], I),
+    "k3gpu_kda_prologue": ([VP] * 14 + [I, I, I, I, I, F, VP], I),
+    "k3gpu_kda_commit_conv": ([VP, VP, VP, I, I, I, I, I, VP], I),
+    "k3gpu_kda_norm_gate": ([VP, VP, VP, I, I, I, F, VP], I),
+    "k3gpu_mla_workspace": ([I, I, I, I, I], SZ),
+    "k3gpu_mla_absorbed": ([VP] * 8 + [I] * 9 + [F, VP, SZ, VP], I),
+    "k3gpu_accept_greedy": ([VP, VP, VP, VP, VP, VP, I, I, I, VP], I),
+    "k3gpu_accept_tree_greedy": ([VP] * 7 + [I, I, I, VP], I),
+    "k3gpu_accept_sample": ([VP] * 5 + [I, I, I, F, U64, U64, VP], I),
+    "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
+}
+for _name, (_args, _res) in _SIGS.items():
+    _fn = getattr(lib, _name)
+    _fn.argtypes = _args
+    _fn.restype = _res
+
+
+class K3Error(RuntimeError):
+    pass
+
+
+def check(status: int, what: str = "") -> None:
+    if status != K3GPU_OK:
+        msg = lib.k3gpu_strerror(status).decode()
+        if status == K3GPU_ECUDA:
+            msg += f" (cudaError {lib.k3gpu_last_cuda_error()})"
+        raise K3Error(f"{what}: {msg} [{status}]")
+
+
+def ptr(t):
+    """Device pointer of a CUDA tensor (None -> NULL)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise K3Error("expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise K3Error("expected a contiguous tensor")
+    return C.c_void_p(t.data_ptr())
+
+
+def stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def device_status(device: int = 0) -> int:
+    v = C.c_int(0)
+    check(lib.k3gpu_device_status(device, C.byref(v)), "device_status")
+    return v.value
+
+
+def workspace(nbytes: int, device="cuda") -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+# ------------------------------------------------------------------------- router --
+def router(x, W, bias, topk, renorm=1, routed_scale=1.0, ws=None, stream=None):
+    T, hidden = x.shape
+    n = W.shape[0]
+    idx = torch.empty((T, topk), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, topk), dtype=torch.float32, device=x.device)
+    need = lib.k3gpu_router_workspace(T, n)
+    ws = ws if ws is not None else workspace(need, x.device)
+    check(lib.k3gpu_router(ptr(idx), ptr(w), ptr(x), ptr(W), ptr(bias), T, hidden, n, topk,
+                           renorm, float(routed_scale), ptr(ws), ws.numel(), stream_ptr(stream)),
+          "k3gpu_router")
+    return idx, w
+
+
+# ----------------------------------------------------------------------- experts ---
+def mxfp4_dequant(packed, scales, stream=None):
+    rows, half = packed.shape
+    out = torch.empty((rows, 2 * half), dtype=torch.float32, device=packed.device)
+    check(lib.k3gpu_mxfp4_dequant(ptr(out), ptr(packed), ptr(scales), rows, 2 * half,
+                                  stream_ptr(stream)), "k3gpu_mxfp4_dequant")
+    return out
+
+
+class ExpertBank:
+    """MXFP4 experts resident in HBM in the reference's per-expert run layout."""
+
+    def __init__(self, bank_bytes: torch.Tensor, n_experts: int, L: int, I_: int):
+        self.bytes = bank_bytes
+        self.desc = K3GpuExpertBank()
+        lib.k3gpu_bank_layout(C.byref(self.desc), L, I_)
+        self.desc.base = bank_bytes.data_ptr()
+        self.desc.n_experts = n_experts
+        self.n_experts, self.L, self.I = n_experts, L, I_
+
+    @staticmethod
+    def layout(L, I_):
+        d = K3GpuExpertBank()
+        lib.k3gpu_bank_layout(C.byref(d), L, I_)
+        return d
+
+
+def moe_experts(z, idx, wt, bank: ExpertBank, topk, n_routed, n_shared, act, b1=4.0, b2=25.0,
+                latent_norm=None, eps=1e-5, ws=None, stream=None):
+    T, L = z.shape
+    out = torch.empty((T, L), dtype=torch.float32, device=z.device)
+    need = lib.k3gpu_moe_workspace(T, topk, n_shared, L, bank.I, n_routed)
+    ws = ws if ws is not None else workspace(need, z.device)
+    check(lib.k3gpu_moe_experts(ptr(out), ptr(z), ptr(idx), ptr(wt), C.byref(bank.desc), T, topk,
+                                n_routed, n_shared, act, float(b1), float(b2), ptr(latent_norm),
+                                float(eps), ptr(ws), ws.numel(), stream_ptr(stream)),
+          "k3gpu_moe_experts")
+    return out
+
+
+def moe_layer(x, gate_W, bias, bank: ExpertBank, topk, n_routed, n_shared, act, b1=4.0, b2=25.0,
+              renorm=1, routed_scale=1.0, ws=None, out=None, idx=None, wt=None, stream=None):
+    T, L = x.shape
+    out = out if out is not None else torch.empty((T, L), dtype=torch.float32, device=x.device)
+    idx = idx if idx is not None else torch.empty((T, topk), dtype=torch.int32, device=x.device)
+    wt = wt if wt is not None else torch.empty((T, topk), dtype=torch.float32, device=x.device)
+    need = lib.k3gpu_moe_workspace(T, topk, n_shared, L, bank.I, n_routed)
+    ws = ws if ws is not None else workspace(need, x.device)
+    check(lib.k3gpu_moe_layer(ptr(out), ptr(idx), ptr(wt), ptr(x), ptr(gate_W), ptr(bias),
+                              C.byref(bank.desc), T, topk, n_routed, n_shared, act, float(b1),
+                              float(b2), renorm, float(routed_scale), ptr(ws), ws.numel(),
+                              stream_ptr(stream)), "k3gpu_moe_layer")
+    return out, idx, wt
+
+
+def moe_phase_timing(enable: bool) -> None:
+    check(lib.k3gpu_moe_phase_timing(1 if enable else 0), "k3gpu_moe_phase_timing")
+
+
+def moe_phase_ms():
+    """[router, plan, gate/up, down, combine] device ms of the last MoE call."""
+    buf = (F * 5)()
+    n = lib.k3gpu_moe_phase_ms(buf, 5)
+    if n < 0:
+        check(n, "k3gpu_moe_phase_ms")
+    return list(buf[:n])
+
+
+# --------------------------------------------------------------------------- KDA ---
+def kda_verify(state, q, k, v, alpha, beta, qscale, stream=None):
+    B, T, H, D = q.shape
+    o = torch.empty_like(q)
+    check(lib.k3gpu_kda_verify(ptr(o), ptr(state), ptr(q), ptr(k), ptr(v), ptr(alpha), ptr(beta),
+                               B, T, H, D, float(qscale), stream_ptr(stream)), "k3gpu_kda_verify")
+    return o
+
+
+def kda_commit(state, k, v, alpha, beta, n, stream=None):
+    B, T, H, D = k.shape
+    check(lib.k3gpu_kda_commit(ptr(state), ptr(k), ptr(v), ptr(alpha), ptr(beta), ptr(n), B, T,
+                               H, D, stream_ptr(stream)), "k3gpu_kda_commit")
+
+
+def kda_prologue(q, k, v, z, b, q_conv, k_conv, v_conv, hist, A_log, dt_bias, H, D, K, lb,
+                 stream=None):
+    B, T, P = q.shape
+    alpha = torch.empty_like(q)
+    beta = torch.empty((B, T, H), dtype=torch.float32, device=q.device)
+    pre = torch.empty((B, T, 3, P), dtype=torch.float32, device=q.device)
+    check(lib.k3gpu_kda_prologue(ptr(q), ptr(k), ptr(v), ptr(alpha), ptr(beta), ptr(pre), ptr(z),
+                                 ptr(b), ptr(q_conv), ptr(k_conv), ptr(v_conv), ptr(hist),
+                                 ptr(A_log), ptr(dt_bias), B, T, H, D, K, float(lb),
+                                 stream_ptr(stream)), "k3gpu_kda_prologue")
+    return alpha, beta, pre
+
+
+def kda_commit_conv(hist, pre, n, H, D, K, stream=None):
+    B, T = pre.shape[0], pre.shape[1]
+    check(lib.k3gpu_kda_commit_conv(ptr(hist), ptr(pre), ptr(n), B, T, H, D, K,
+                                    stream_ptr(stream)), "k3gpu_kda_commit_conv")
+
+
+def kda_norm_gate(o, gate, o_norm, H, D, eps, stream=None):
+    R = o.numel() // (H * D)
+    check(lib.k3gpu_kda_norm_gate(ptr(o), ptr(gate), ptr(o_norm), R, H, D, float(eps),
+                                  stream_ptr(stream)), "k3gpu_kda_norm_gate")
+
+
+# --------------------------------------------------------------------------- MLA ---
+def mla_absorbed(q_nope, q_rope, kv_b, lat, rope, cached, mask, v_head, max_ctx, scale,
+                 ws=None, stream=None):
+    B, T, H, qn = q_nope.shape
+    qr = q_rope.shape[3]
+    cap, kvl = lat.shape[1], lat.shape[2]
+    out = torch.empty((B, T, H, v_head), dtype=torch.float32, device=q_nope.device)
+    need = lib.k3gpu_mla_workspace(B, T, H, kvl, max_ctx)
+    ws = ws if ws is not None else workspace(need, q_nope.device)
+    check(lib.k3gpu_mla_absorbed(ptr(out), ptr(q_nope), ptr(q_rope), ptr(kv_b), ptr(lat),
+                                 ptr(rope), ptr(cached), ptr(mask), B, T, H, qn, qr, v_head, kvl,
+                                 cap, max_ctx, float(scale), ptr(ws), ws.numel(),
+                                 stream_ptr(stream)), "k3gpu_mla_absorbed")
+    return out
+
+
+# ------------------------------------------------------------------------ accept ---
+def accept_greedy(logits, drafts, nd_b=None, stream=None):
+    B, T, V = logits.shape
+    nd = T - 1
+    emit = torch.empty((B, T), dtype=torch.int32, device=logits.device)
+    arg = torch.empty((B, T), dtype=torch.int32, device=logits.device)
+    n_emit = torch.empty((B,), dtype=torch.int32, device=logits.device)
+    check(lib.k3gpu_accept_greedy(ptr(emit), ptr(n_emit), ptr(arg), ptr(logits), ptr(drafts),
+                                  ptr(nd_b), B, nd, V, stream_ptr(stream)), "k3gpu_accept_greedy")
+    return emit, n_emit, arg
+
+
+def accept_tree_greedy(logits, tok, parent, stream=None):
+    B, T, V = logits.shape
+    emit = torch.empty((B, T), dtype=torch.int32, device=logits.device)
+    path = torch.empty((B, T), dtype=torch.int32, device=logits.device)
+    arg = torch.empty((B, T), dtype=torch.int32, device=logits.device)
+    n_emit = torch.empty((B,), dtype=torch.int32, device=logits.device)
+    check(lib.k3gpu_accept_tree_greedy(ptr(emit), ptr(n_emit), ptr(path), ptr(arg), ptr(logits),
+                                       ptr(tok), ptr(parent), B, T, V, stream_ptr(stream)),
+          "k3gpu_accept_tree_greedy")
+    return emit, n_emit, path, arg
+
+
+def accept_sample(logits, drafts, temp, seed, offset=0, nd_b=None, stream=None):
+    B, T, V = logits.shape
+    nd = T - 1
+    emit = torch.full((B, T), -1, dtype=torch.int32, device=logits.device)
+    n_emit = torch.empty((B,), dtype=torch.int32, device=logits.device)
+    check(lib.k3gpu_accept_sample(ptr(emit), ptr(n_emit), ptr(logits), ptr(drafts), ptr(nd_b), B,
+                                  nd, V, float(temp), int(seed), int(offset), stream_ptr(stream)),
+          "k3gpu_accept_sample")
+    return emit, n_emit
+
+
+# ----------------------------------------------------------------------- drafter ---
+def spec_draft(seq, cap=8, nmax=4, nmin=3):
+    arr = (C.c_int * max(len(seq), 1))(*seq)
+    out = (C.c_int * max(cap, 1))()
+    nd = lib.k3_spec_draft_ngram(arr, len(seq), cap, nmax, nmin, out)
+    return list(out[:nd])

@@ -567,6 +567,134 @@ ORC_API int orc_accept_greedy(int *emit, int *accepted, int *arg, const float *l
     return m + 1;
 }
 
+/* Greedy acceptance over a draft tree (no reference: the reference verifies chains only,
+ * src/cli/k3_run.c:2924-2928; parity for trees is against this restatement). Node 0 is
+ * the pending token; from the current node c the accepted child is the lowest-index
+ * child i (parent[i] == c) with tok[i] == argmax(logits of c). Emits the path's drafted
+ * ids, then the bonus argmax of the last accepted node. Returns the emitted count. */
+ORC_API int orc_accept_tree_greedy(int *emit, int *path, const float *logits, const int *tok,
+                                   const int *parent, int T, int vocab)
+{
+    int c = 0, depth = 0;
+    path[0] = 0;
+    for (;;) {
+        const int a = orc_argmax(logits + (size_t)c * vocab, vocab);
+        int next = -1;
+        for (int i = c + 1; i < T; i++)
+            if (parent[i] == c && tok[i] == a) { next = i; break; }
+        if (next < 0) {
+            emit[depth] = a;
+            return depth + 1;
+        }
+        emit[depth++] = tok[next];
+        path[depth] = next;
+        c = next;
+    }
+}
+
+/* Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11, "Parallel random numbers: as easy as
+ * 1, 2, 3"): ten rounds of the two published multipliers with Weyl key increments. */
+static void orc_philox(uint32_t c[4], uint32_t k0, uint32_t k1)
+{
+    for (int r = 0; r < 10; r++) {
+        const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+        const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+        const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+        const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+        c[1] = (uint32_t)p1;
+        c[3] = (uint32_t)p0;
+        c[0] = n0;
+        c[2] = n2;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+}
+
+ORC_API double orc_philox_uniform(uint64_t seed, uint64_t offset, int b, int i, int which)
+{
+    uint32_t c[4] = {(uint32_t)offset, (uint32_t)(offset >> 32), (uint32_t)b,
+                     (uint32_t)(2 * i + which)};
+    orc_philox(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+    const uint64_t bits = ((uint64_t)(c[0] >> 5) << 26) | (uint64_t)(c[1] >> 6);
+    return (double)bits * (1.0 / 9007199254740992.0);
+}
+
+#define ORC_SAMPLE_CHUNKS 256
+
+static float orc_samp_e(float l, float m, float temp)
+{
+    return (float)exp((double)((l - m) / temp));
+}
+
+/* Chunked sums in the fixed order of the device kernel: chunk t = [t*C, (t+1)*C) summed
+ * ascending in double, chunks added in order; `skip` and NaN logits are left out. */
+static double orc_chunk_sums(double *cs, const float *l, int vocab, float m, float temp, int skip)
+{
+    const int C = (vocab + ORC_SAMPLE_CHUNKS - 1) / ORC_SAMPLE_CHUNKS;
+    double tot = 0.0;
+    for (int t = 0; t < ORC_SAMPLE_CHUNKS; t++) {
+        double s = 0.0;
+        for (int v = t * C; v < vocab && v < (t + 1) * C; v++)
+            if (v != skip && l[v] == l[v]) s += (double)orc_samp_e(l[v], m, temp);
+        cs[t] = s;
+    }
+    for (int t = 0; t < ORC_SAMPLE_CHUNKS; t++) tot += cs[t];
+    return tot;
+}
+
+static int orc_chunk_pick(const double *cs, const float *l, int vocab, float m, float temp,
+                          int skip, double r)
+{
+    const int C = (vocab + ORC_SAMPLE_CHUNKS - 1) / ORC_SAMPLE_CHUNKS;
+    double run = 0.0;
+    for (int t = 0; t < ORC_SAMPLE_CHUNKS; t++) {
+        if (run + cs[t] > r) {
+            for (int v = t * C; v < vocab && v < (t + 1) * C; v++) {
+                if (v == skip || l[v] != l[v]) continue;
+                run += (double)orc_samp_e(l[v], m, temp);
+                if (run > r) return v;
+            }
+            break;
+        }
+        run += cs[t];
+    }
+    for (int v = vocab - 1; v >= 0; v--)
+        if (v != skip && l[v] == l[v] && orc_samp_e(l[v], m, temp) > 0.0f) return v;
+    return 0;
+}
+
+/* Temperature sampling with the speculative rejection rule for point-mass drafts (no
+ * reference: the reference decodes greedily only). Position i's draft d is kept when
+ * u < p_i(d), p = softmax(logits / temp); on the first rejection the emitted id is drawn
+ * from p_i without d, renormalised; after nd acceptances the bonus is drawn from p_nd.
+ * Uniforms come from Philox4x32-10 keyed by (seed, offset, b, i). Returns the count. */
+ORC_API int orc_accept_sample(int *emit, const float *logits, const int *d, int nd, int vocab,
+                              float temp, uint64_t seed, uint64_t offset, int b)
+{
+    double cs[ORC_SAMPLE_CHUNKS];
+    for (int i = 0; i <= nd; i++) {
+        const float *l = logits + (size_t)i * vocab;
+        float m = -INFINITY;
+        for (int v = 0; v < vocab; v++) if (l[v] == l[v] && l[v] > m) m = l[v];
+        const double Z = orc_chunk_sums(cs, l, vocab, m, temp, -1);
+        if (i == nd) {
+            const double r = orc_philox_uniform(seed, offset, b, i, 1) * Z;
+            emit[i] = orc_chunk_pick(cs, l, vocab, m, temp, -1, r);
+            return i + 1;
+        }
+        const int di = d[i];
+        const int ok = di >= 0 && di < vocab && l[di] == l[di];
+        const double pd = ok ? (double)orc_samp_e(l[di], m, temp) / Z : 0.0;
+        const double u = orc_philox_uniform(seed, offset, b, i, 0);
+        if (u < pd) { emit[i] = di; continue; }
+        const double Zr = orc_chunk_sums(cs, l, vocab, m, temp, ok ? di : -1);
+        const double r = orc_philox_uniform(seed, offset, b, i, 1) * Zr;
+        emit[i] = orc_chunk_pick(cs, l, vocab, m, temp, ok ? di : -1, r);
+        return i + 1;
+    }
+    return nd + 1;
+}
+
 /* src/cli/k3_run.c:1307-1317 (emit_keep). */
 ORC_API int orc_emit_keep(const int *emit, int emitn, int nout, int gen, int T, int Tmax,
                           const int *stop_id, int n_stop)

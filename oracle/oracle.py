@@ -78,6 +78,12 @@ def orc():
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = None
+        lib.orc_accept_tree_greedy.argtypes = [i32p, i32p, f32p, i32p, i32p, I, I]
+        lib.orc_accept_tree_greedy.restype = C.c_int
+        lib.orc_philox_uniform.argtypes = [C.c_uint64, C.c_uint64, I, I, I]
+        lib.orc_philox_uniform.restype = C.c_double
+        lib.orc_accept_sample.argtypes = [i32p, f32p, i32p, I, I, F, C.c_uint64, C.c_uint64, I]
+        lib.orc_accept_sample.restype = C.c_int
         lib.orc_spec_draft.restype = C.c_int
         lib.orc_argmax.restype = C.c_int
         lib.orc_accept_greedy.restype = C.c_int
