@@ -64,6 +64,28 @@ int k3gpu_router(int *idx, float *w, const float *x, const float *W, const float
                  int T, int hidden, int n_experts, int topk, int renorm, float routed_scale,
                  void *workspace, size_t ws_bytes, void *stream);
 
+/* The router for callers that cannot allocate device memory. No counterpart in the
+ * reference (its k3_router mallocs its score arrays on the host per call); this entry
+ * point exists for hosts that own all device memory up front -- a serving process whose
+ * allocator has already reserved the HBM, or a caller on a latency-critical thread where
+ * cudaMalloc, which may synchronise the device, is not allowed -- and so cannot provide
+ * the workspace k3gpu_router needs. Same inputs, outputs and arithmetic as
+ * k3gpu_router; the [T][n_experts] scores live instead in a fixed array inside the
+ * library (K3GPU_ROUTER_NOALLOC_MAX_SCORES floats, 2 MiB, held by every GPU that loads
+ * the library until the process exits).
+ *   - T * n_experts above the maximum returns K3GPU_ECAPACITY and enqueues nothing.
+ *   - The first call on a device looks up that device's copy of the array (set-up, once
+ *     per device); make that first call before any stream capture.
+ *   - Every call shares the one array: two calls whose kernels overlap on the same GPU
+ *     (different streams, or host threads) race and may return wrong results. Calls on
+ *     one stream are ordered and safe. Nothing in the array needs clearing: each call
+ *     writes every score it reads before reading it.
+ * It allocates nothing: no cudaMalloc, no cudaFree, no allocating library routine. */
+#define K3GPU_ROUTER_NOALLOC_MAX_SCORES 524288
+int k3gpu_router_noalloc(int *idx, float *w, const float *x, const float *W,
+                         const float *bias, int T, int hidden, int n_experts, int topk,
+                         int renorm, float routed_scale, void *stream);
+
 /* ------------------------------------------------------------ expert bank ---- */
 /* Device-resident MXFP4 experts. Expert e is the byte run base + e*stride holding, at
  * the given offsets, the six tensors the reference's loader reads as one contiguous run

@@ -47,6 +47,7 @@ _SIGS = {
     "k3gpu_device_status": ([I, C.POINTER(I)], I),
     "k3gpu_router_workspace": ([I, I], SZ),
     "k3gpu_router": ([VP, VP, VP, VP, VP, I, I, I, I, I, F, VP, SZ, VP], I),
+    "k3gpu_router_noalloc": ([VP, VP, VP, VP, VP, I, I, I, I, I, F, VP], I),
     "k3gpu_bank_layout": ([C.POINTER(K3GpuExpertBank), I, I], None),
     "k3gpu_mxfp4_dequant": ([VP, VP, VP, I, I, VP], I),
     "k3gpu_moe_workspace": ([I, I, I, I, I, I], SZ),

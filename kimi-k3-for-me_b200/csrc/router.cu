@@ -15,6 +15,8 @@
 // which are exact.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace k3 {
@@ -141,6 +143,55 @@ int router_launch(int *idx, float *w, const float *x, const float *W, const floa
 }
 
 }  // namespace k3
+
+// ---- the allocation-free router (k3gpu_router_noalloc) ------------------------------
+// Callers that cannot allocate device memory (their allocator owns the HBM, or they run
+// where cudaMalloc's possible device synchronisation is forbidden) get the score scratch
+// from this fixed array instead of a workspace. Every GPU that loads the library holds
+// one copy (2 MiB) until the process exits.
+namespace k3 {
+static __device__ __align__(256) float g_router_noalloc_scores[K3GPU_ROUTER_NOALLOC_MAX_SCORES];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static float *g_noalloc_addr[NOALLOC_MAX_DEVICES] = {};
+
+// In host code the array's name is only a host-side stand-in, not a device address, so
+// the kernels get the address cudaGetSymbolAddress returns for the current device. The
+// lookup is the per-device set-up, done by the first call on each device.
+static int noalloc_scores(float **out)
+{
+    int dev = 0;
+    int st = cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return K3GPU_EINVAL;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void *p = nullptr;
+        st = cuda_status(cudaGetSymbolAddress(&p, g_router_noalloc_scores));
+        if (st) return st;
+        g_noalloc_addr[dev] = static_cast<float *>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return K3GPU_OK;
+}
+}  // namespace k3
+
+extern "C" int k3gpu_router_noalloc(int *idx, float *w, const float *x, const float *W,
+                                    const float *bias, int T, int hidden, int n_experts,
+                                    int topk, int renorm, float routed_scale, void *stream)
+{
+    if (!idx || !w || !x || !W) return K3GPU_EINVAL;
+    if (T <= 0 || hidden <= 0 || n_experts <= 0 || n_experts > 1024 || topk < 1 || topk > 64 ||
+        topk > n_experts)
+        return K3GPU_EINVAL;
+    if ((long long)T * n_experts > K3GPU_ROUTER_NOALLOC_MAX_SCORES) return K3GPU_ECAPACITY;
+    float *scores = nullptr;
+    const int st = k3::noalloc_scores(&scores);
+    if (st) return st;
+    return k3::router_launch(idx, w, x, W, bias, T, hidden, n_experts, topk, renorm,
+                             routed_scale, scores, k3::as_stream(stream));
+}
 
 extern "C" size_t k3gpu_router_workspace(int T, int n_experts)
 {
