@@ -399,6 +399,7 @@ def run_b200(args):
 
 
 def main():
+    global N_ROUTED
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
@@ -410,7 +411,10 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=72, help="tokens in the CPU baseline sample")
     ap.add_argument("--ref-tokens", type=int, default=0, help="tokens per reference-arm step (0 = all)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--n-routed", type=int, default=N_ROUTED,
+                    help="routed experts (smaller values give small cases for ncu captures)")
     args = ap.parse_args()
+    N_ROUTED = args.n_routed
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
     if args.impl == "reference":
