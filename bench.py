@@ -61,7 +61,10 @@ def bank_layout(L, I):
     offs = dict(p1=0, s1=pw, p2=pw + sw, s2=pw + sw + pd, p3=pw + sw + pd + sd,
                 s3=pw + sw + pd + sd + pw)
     run = pw + sw + pd + sd + pw + sw
-    return offs, (run + 255) // 256 * 256
+    # the library's stride (k3gpu_bank_layout): run rounded up to lcm(L/2, I/2, 256)
+    import math
+    q = math.lcm(256, L // 2, I // 2)
+    return offs, (run + q - 1) // q * q
 
 
 def quant_mxfp4_torch(w):
@@ -278,6 +281,7 @@ def run_b200(args):
     bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, dev)
     x, gate, bias = make_inputs(M, args.seed + 1, dev)
     kb = k3.ExpertBank(bank, N_ROUTED + N_SHARED, L_DIM, I_DIM)
+    n_unsafe = kb.scan() if not args.no_tc else None   # certify experts for the tcgen05 kernels
     ws = k3.workspace(k3.lib.k3gpu_moe_workspace(M, TOPK, N_SHARED, L_DIM, I_DIM, N_ROUTED), dev)
     out = torch.empty((M, L_DIM), dtype=torch.float32, device=dev)
     idx = torch.empty((M, TOPK), dtype=torch.int32, device=dev)
@@ -390,7 +394,8 @@ def run_b200(args):
                         "unique_experts": u, "bytes": int(gateup_bytes + down_bytes)},
         "phase_ms": {"router": round(ph[0], 4), "plan": round(ph[1], 4), "gateup": round(ph[2], 4),
                      "down": round(ph[3], 4), "combine": round(ph[4], 4)},
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": 9 * args.steps,
+        "expert_kernels": "mma.sync" if args.no_tc else f"tcgen05 ({n_unsafe} experts on mma.sync)",
         "clocks": clk,
         "cpu_baseline": cpu,
     }
@@ -411,6 +416,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=72, help="tokens in the CPU baseline sample")
     ap.add_argument("--ref-tokens", type=int, default=0, help="tokens per reference-arm step (0 = all)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-tc", action="store_true", help="skip the bank scan: mma.sync expert kernels only")
     ap.add_argument("--n-routed", type=int, default=N_ROUTED,
                     help="routed experts (smaller values give small cases for ncu captures)")
     args = ap.parse_args()

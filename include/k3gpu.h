@@ -101,10 +101,24 @@ typedef struct {
     int64_t p1, s1, p2, s2, p3, s3;
     int n_experts;          /* runs in the bank: routed + shared */
     int L, I;               /* expert input/output width, intermediate width */
+    /* Filled by k3gpu_bank_scan (NULL / 0 until then): a device array [n_experts], 1 where
+     * every E8M0 byte of the expert lies in 104..140 (or is the NaN byte 255), so that
+     * scale * E2M1 is exact in f16 and the expert can run on the tcgen05 kernels; and the
+     * number of experts that are not. */
+    const uint8_t *f16_safe;
+    int n_f16_unsafe;
 } K3GpuExpertBank;
 
-/* Fill the offsets and stride of the packed run layout above (stride rounded up to 256
- * bytes); leaves base and n_experts to the caller. Host only. */
+/* One-time certification of a bank for the tcgen05 expert kernels (host, synchronous on
+ * `stream`): writes safe_dev [n_experts] (device) and sets bank->f16_safe and
+ * bank->n_f16_unsafe. Experts that fail the check keep running on the mma.sync kernels;
+ * a bank never scanned runs entirely on those. */
+int k3gpu_bank_scan(K3GpuExpertBank *bank, uint8_t *safe_dev, void *stream);
+
+/* Fill the offsets and stride of the packed run layout above (the stride is the run
+ * rounded up to a multiple of lcm(L/2, I/2, 256) bytes, so every matrix starts on a whole
+ * row of the expert kernels' tensor maps); leaves base and n_experts to the caller.
+ * Host only. */
 void k3gpu_bank_layout(K3GpuExpertBank *bank, int L, int I);
 
 /* Replaces k3_mxfp4_dequant (include/k3/k3.h:863-864) for group 32: out [rows][in] fp32
@@ -142,6 +156,11 @@ int k3gpu_moe_layer(float *out, int *idx, float *wt, const float *x, const float
                     const float *bias, const K3GpuExpertBank *bank, int T, int topk,
                     int n_routed, int n_shared, int act, float b1, float b2, int renorm,
                     float routed_scale, void *workspace, size_t ws_bytes, void *stream);
+
+/* Expert-kernel selection (host, per process): 0 (default) runs the tensor-core expert
+ * stream wherever L and I are multiples of 512 and the CUDA-core stream elsewhere; 1
+ * forces the CUDA-core stream everywhere (the two agree to fp32 rounding). */
+int k3gpu_moe_select_kernels(int which);
 
 /* Per-phase timing of the MoE calls, for roofline reporting. When enabled (host, per
  * process), every k3gpu_moe_experts / k3gpu_moe_layer call records CUDA events on its

@@ -37,7 +37,7 @@ ACT_SITU, ACT_SWIGLU = 0, 1
 class K3GpuExpertBank(C.Structure):
     _fields_ = [("base", VP), ("stride", C.c_int64), ("p1", C.c_int64), ("s1", C.c_int64),
                 ("p2", C.c_int64), ("s2", C.c_int64), ("p3", C.c_int64), ("s3", C.c_int64),
-                ("n_experts", I), ("L", I), ("I", I)]
+                ("n_experts", I), ("L", I), ("I", I), ("f16_safe", VP), ("n_f16_unsafe", I)]
 
 
 _SIGS = {
@@ -50,11 +50,13 @@ _SIGS = {
     "k3gpu_router_noalloc": ([VP, VP, VP, VP, VP, I, I, I, I, I, F, VP], I),
     "k3gpu_bank_layout": ([C.POINTER(K3GpuExpertBank), I, I], None),
     "k3gpu_mxfp4_dequant": ([VP, VP, VP, I, I, VP], I),
+    "k3gpu_bank_scan": ([C.POINTER(K3GpuExpertBank), VP, VP], I),
     "k3gpu_moe_workspace": ([I, I, I, I, I, I], SZ),
     "k3gpu_moe_experts": ([VP, VP, VP, VP, C.POINTER(K3GpuExpertBank), I, I, I, I, I, F, F, VP,
                            F, VP, SZ, VP], I),
     "k3gpu_moe_layer": ([VP, VP, VP, VP, VP, VP, C.POINTER(K3GpuExpertBank), I, I, I, I, I, F, F,
                          I, F, VP, SZ, VP], I),
+    "k3gpu_moe_select_kernels": ([I], I),
     "k3gpu_moe_phase_timing": ([I], I),
     "k3gpu_moe_phase_ms": ([C.POINTER(F), I], I),
     "k3gpu_kda_verify": ([VP, VP, VP, VP, VP, VP, VP, I, I, I, I, F, VP], I),
@@ -146,6 +148,14 @@ class ExpertBank:
         self.desc.base = bank_bytes.data_ptr()
         self.desc.n_experts = n_experts
         self.n_experts, self.L, self.I = n_experts, L, I_
+        self.safe = None
+
+    def scan(self, stream=None):
+        """Certify the experts for the tcgen05 kernels (one-time, synchronous)."""
+        self.safe = torch.empty(self.n_experts, dtype=torch.uint8, device=self.bytes.device)
+        check(lib.k3gpu_bank_scan(C.byref(self.desc), ptr(self.safe), stream_ptr(stream)),
+              "k3gpu_bank_scan")
+        return self.desc.n_f16_unsafe
 
     @staticmethod
     def layout(L, I_):

@@ -53,7 +53,13 @@ extern "C" void k3gpu_bank_layout(K3GpuExpertBank *b, int L, int I)
     b->p3 = pw + sw + pd + sd;
     b->s3 = pw + sw + pd + sd + pw;
     const int64_t run = pw + sw + pd + sd + pw + sw;
-    b->stride = (run + 255) & ~(int64_t)255;
+    // runs start on a whole row of both tensor-map pitches (L/2 and I/2 bytes) and on a
+    // 256-byte boundary: stride = run rounded up to lcm(L/2, I/2, 256)
+    auto gcd = [](int64_t a, int64_t c) { while (c) { const int64_t r = a % c; a = c; c = r; } return a; };
+    int64_t q = 256;
+    for (int64_t v : {(int64_t)L / 2, (int64_t)I / 2})
+        if (v > 0) q = q / gcd(q, v) * v;
+    b->stride = (run + q - 1) / q * q;
     b->L = L;
     b->I = I;
 }

@@ -20,6 +20,7 @@ enum : unsigned int {
     DEV_BAD_INDEX = 1u,     // an expert index or row index outside its range was skipped
     DEV_BAD_COUNT = 2u,     // a commit length outside 0..T was clamped
     DEV_BAD_POSITION = 4u,  // a cache position outside 0..cap-1 was skipped
+    DEV_TIMEOUT = 8u,       // a bounded wait on a pipeline barrier gave up
 };
 
 inline __device__ void flag(unsigned int code) { atomicOr(&g_device_status, code); }

@@ -24,44 +24,9 @@
 #include <cuda_fp4.h>
 #include <math.h>
 
-#include "common.cuh"
+#include "moe.cuh"
 
 namespace k3 {
-
-struct MoePlan {
-    int *cnt;        // [E]
-    int *fill;       // [E]
-    int *off;        // [E+1]
-    int *act;        // [E] active expert ids, ascending
-    int *n_active;   // [1]
-    int *pair_tok;   // [P] token of sorted pair p
-    int *pair_dst;   // [P] contribution row (t*S + s) of sorted pair p
-    float *H;        // [P][I] activations after act()
-    float *contrib;  // [T*S][L]
-};
-
-static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
-
-static size_t plan_bytes(int T, int S, int E, int L, int I, MoePlan *p, char *base)
-{
-    const size_t P = (size_t)T * S;
-    size_t o = 0;
-    auto take = [&](size_t bytes) {
-        char *r = base ? base + o : nullptr;
-        o += align256(bytes);
-        return r;
-    };
-    char *cnt = take(sizeof(int) * E), *fill = take(sizeof(int) * E);
-    char *off = take(sizeof(int) * (E + 1)), *act = take(sizeof(int) * E);
-    char *na = take(sizeof(int)), *pt = take(sizeof(int) * P), *pd = take(sizeof(int) * P);
-    char *H = take(sizeof(float) * P * I), *C = take(sizeof(float) * P * L);
-    if (p) {
-        p->cnt = (int *)cnt; p->fill = (int *)fill; p->off = (int *)off; p->act = (int *)act;
-        p->n_active = (int *)na; p->pair_tok = (int *)pt; p->pair_dst = (int *)pd;
-        p->H = (float *)H; p->contrib = (float *)C;
-    }
-    return o;
-}
 
 // Expert of slot s of token t, or -1 when the slot is dropped (idx < 0) or out of range.
 __device__ __forceinline__ int slot_expert(const int *idx, int t, int s, int topk, int n_routed)
@@ -97,6 +62,8 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlan p, const int *__
             p.off[e] = run;
             p.cnt[e] = c;
             p.fill[e] = 0;
+            p.elo[e] = 0;
+            p.elo[E + e] = 0;
             run += c;
             if (c > 0) p.act[na++] = e;
         }
@@ -114,14 +81,8 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlan p, const int *__
         const int pos = p.off[e] + atomicAdd(&p.fill[e], 1);
         p.pair_tok[pos] = t;
         p.pair_dst[pos] = i;
+        p.pair_exp[pos] = e;
     }
-}
-
-__device__ __forceinline__ float e8m0_scale(unsigned b)
-{
-    if (b == 255u) return 0.0f;                  // NaN by the OCP MX spec -> zero group
-    if (b == 0u) return __int_as_float(0x00400000);   // 2^-127, subnormal
-    return __int_as_float((int)(b << 23));
 }
 
 __device__ __forceinline__ uint4 ld_stream(const uint8_t *p)
@@ -232,17 +193,6 @@ __device__ __forceinline__ float stream_rows16(const uint8_t *const (&prow)[16],
         }
     }
     return v[0];
-}
-
-__device__ __forceinline__ float act_situ(float g, float u, float b1, float b2)
-{
-    const float a = b1 * tanhf(g / b1) * (1.0f / (1.0f + expf(-g)));
-    return a * (b2 * tanhf(u / b2));
-}
-
-__device__ __forceinline__ float act_swiglu(float g, float u)
-{
-    return (g * (1.0f / (1.0f + expf(-g)))) * u;
 }
 
 constexpr int MOE_WARPS = 8;
@@ -448,6 +398,9 @@ int moe_check(const K3GpuExpertBank *bank, int T, int topk, int n_routed, int n_
 // Optional phase timing (k3gpu_moe_phase_timing): events 0..5 bracket router, plan,
 // gate/up, down, combine.
 constexpr int N_PHASE_EV = 6;
+// The tensor-core expert kernels (moe_mma.cu) run whenever the shapes allow; the
+// CUDA-core kernels above cover the rest. k3gpu_moe_select_kernels can force the latter.
+static bool g_use_mma = true;
 static bool g_phase_on = false;
 static bool g_phase_router = false;
 static cudaEvent_t g_phase_ev[N_PHASE_EV];
@@ -470,13 +423,30 @@ int moe_launch(float *out, const float *z, const int *idx, const float *wt,
     moe_plan_kernel<<<1, 1024, sizeof(int) * E, s>>>(p, idx, T, topk, n_routed, n_shared);
     int st = launch_status();
     if (st) return st;
-    const int grid = num_sms() * 2;
-    phase_mark(2, s);
-    moe_gateup_kernel<<<grid, 256, 0, s>>>(p, z, *bank, act, b1, b2);
-    if ((st = launch_status())) return st;
-    phase_mark(3, s);
-    moe_down_kernel<<<grid, 256, 0, s>>>(p, *bank);
-    if ((st = launch_status())) return st;
+    if (g_use_mma && mma_bank_ok(*bank)) {
+        // tensor-core paths: tcgen05 on the experts the bank scan certified, mma.sync on
+        // the rest (all of them when the bank was never scanned)
+        const int P = T * S, E = bank->n_experts;
+        const bool tc = tc_bank_ok(*bank);
+        const bool sync_path = !tc || bank->n_f16_unsafe > 0;
+        if ((st = tc_pack_pairs_launch(p, z, bank->L, P, E, s))) return st;
+        phase_mark(2, s);
+        if (tc && (st = tc_phase_launch(0, p, *bank, P, act, b1, b2, s))) return st;
+        if (sync_path && (st = mma_phase_launch(0, p, *bank, act, b1, b2, s))) return st;
+        phase_mark(3, s);
+        act_pack_rows_launch(p, bank->I, P, E, s);
+        if ((st = launch_status())) return st;
+        if (tc && (st = tc_phase_launch(1, p, *bank, P, act, b1, b2, s))) return st;
+        if (sync_path && (st = mma_phase_launch(1, p, *bank, act, b1, b2, s))) return st;
+    } else {
+        const int grid = num_sms() * 2;
+        phase_mark(2, s);
+        moe_gateup_kernel<<<grid, 256, 0, s>>>(p, z, *bank, act, b1, b2);
+        if ((st = launch_status())) return st;
+        phase_mark(3, s);
+        moe_down_kernel<<<grid, 256, 0, s>>>(p, *bank);
+        if ((st = launch_status())) return st;
+    }
     phase_mark(4, s);
     moe_combine_kernel<<<T, CMB_THREADS, 0, s>>>(out, p.contrib, idx, wt, latent_norm, eps,
                                                  bank->L, topk, n_routed, n_shared);
@@ -495,6 +465,36 @@ int router_launch(int *idx, float *w, const float *x, const float *W, const floa
                   cudaStream_t s);
 
 }  // namespace k3
+
+extern "C" int k3gpu_bank_scan(K3GpuExpertBank *bank, uint8_t *safe_dev, void *stream)
+{
+    if (!bank || !bank->base || !safe_dev || bank->n_experts <= 0) return K3GPU_EINVAL;
+    if (bank->L <= 0 || bank->I <= 0 || bank->L % 32 || bank->I % 32) return K3GPU_EINVAL;
+    cudaStream_t s = k3::as_stream(stream);
+    int st = k3::tc_bank_scan(*bank, safe_dev, s);
+    if (st) return st;
+    // count on the host: a one-time, synchronous certification
+    const int n = bank->n_experts;
+    uint8_t *h = static_cast<uint8_t *>(malloc((size_t)n));
+    if (!h) return K3GPU_ECAPACITY;
+    st = k3::cuda_status(cudaMemcpyAsync(h, safe_dev, (size_t)n, cudaMemcpyDeviceToHost, s));
+    if (!st) st = k3::cuda_status(cudaStreamSynchronize(s));
+    if (!st) {
+        int bad = 0;
+        for (int e = 0; e < n; e++) bad += h[e] ? 0 : 1;
+        bank->f16_safe = safe_dev;
+        bank->n_f16_unsafe = bad;
+    }
+    free(h);
+    return st;
+}
+
+extern "C" int k3gpu_moe_select_kernels(int which)
+{
+    if (which != 0 && which != 1) return K3GPU_EINVAL;
+    k3::g_use_mma = which == 0;
+    return K3GPU_OK;
+}
 
 extern "C" int k3gpu_moe_phase_timing(int enable)
 {

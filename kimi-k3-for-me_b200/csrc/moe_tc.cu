@@ -1,0 +1,638 @@
+// moe_tc.cu -- the tcgen05 expert FFN: MXFP4 weights decoded straight into tensor memory.
+//
+// The verify batch's expert GEMM is a weight stream (most experts see one or two of the
+// step's tokens), so the work per weight byte must be small. This kernel makes it one
+// hardware nibble-pair conversion plus one f16 multiply per two weights:
+//
+//   TMA       packed E2M1 rows (128-byte swizzled boxes), their E8M0 bytes, and the
+//             activation tiles (f16 hi/lo, K-major, 128-byte swizzle) -> shared memory
+//   decode    eight warps, one thread per weight row: cvt.rn.f16x2.e2m1x2 (exact), times
+//             the group's power of two 2^(S-127) as an f16 (exact for 104 <= S <= 140, which
+//             bank_scan certifies per expert), tcgen05.st into a TMEM A buffer
+//   MMA       one thread: tcgen05.mma kind::f16, A from TMEM (128 rows x 16 K), B from
+//             shared memory (K x 16 tokens), fp32 accumulator in TMEM; hi and lo halves of
+//             the activations accumulate into the same D
+//   epilogue  four warps: tcgen05.ld of D, row exponent, activation (gate/up) or the
+//             contribution store (down)
+//
+// Shared memory carries only packed bytes and activation tiles; the f16 weights live in
+// tensor memory, so the shared-memory bandwidth is not a ceiling. Every wait is bounded;
+// TMEM is freed on every exit path. No TMA multicast anywhere.
+//
+// Units: gate/up = 64 rows of w1 (TMEM lanes 0..63) and the same 64 rows of w3 (lanes
+// 64..127) of one expert; down = 128 rows of w2. Up to 16 tokens per pass (MMA N = 16).
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "moe.cuh"
+
+namespace k3 {
+
+constexpr int TC_DEQ_WARPS = 8;          // warps 0..7: decode (two per TMEM lane quarter)
+constexpr int TC_EPI_WARP0 = 8;          // warps 8..11: epilogue
+constexpr int TC_TMA_WARP = 12;
+constexpr int TC_MMA_WARP = 13;
+constexpr int TC_THREADS = 14 * 32;
+constexpr int TC_KC = 512;               // K elements per shared-memory stage
+constexpr int TC_N = 16;                 // tokens per pass (MMA N)
+constexpr int TC_W_BYTES = 128 * 256;    // packed weights of a stage (32 KB)
+constexpr int TC_S_BYTES = 128 * 16;     // E8M0 bytes of a stage
+constexpr int TC_B_BYTES = (TC_KC / 64) * TC_N * 128;   // 16 KB: 8 atoms x 16 rows x 128 B
+constexpr int TC_STAGE = TC_W_BYTES + TC_S_BYTES + 2 * TC_B_BYTES + 1024 - TC_S_BYTES % 1024;
+constexpr int TC_NS = 3;
+constexpr int TC_NA = 3;                 // TMEM A buffers (128 columns = 256 K each)
+constexpr int TC_ACOL0 = 64;             // first A column; stage partials at columns 0 and 32
+constexpr int TC_XCH_BYTES = 64 * TC_N * 4;   // gate/up exchange in the epilogue
+// barriers: full[NS] empty[NS] aready[NA] afree[NA] pfull[2] pfree[2] (stage partials)
+constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 4;
+constexpr int TC_TAB = 1024;             // active-expert table entries kept in shared memory
+constexpr int TC_SMEM = TC_NS * TC_STAGE + TC_XCH_BYTES + TC_NBAR * 8 + 16 + TC_TAB * 16;
+constexpr long long TC_SPIN = 1LL << 24;
+
+static_assert(TC_STAGE % 1024 == 0, "stage alignment");
+
+__device__ __forceinline__ uint32_t s_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bar_init(uint32_t b, uint32_t n)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint32_t b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint32_t b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+}
+__device__ __forceinline__ bool bar_wait(uint32_t b, uint32_t parity)
+{
+    for (long long i = 0; i < TC_SPIN; i++) {
+        uint32_t ok;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                     " selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(ok)
+                     : "r"(b), "r"(parity)
+                     : "memory");
+        if (ok) return true;
+        if (i > 32) __nanosleep(32);
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap *m, int x, int y, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void cvt4h(uint32_t w, uint32_t (&h)[4])
+{
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+        : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+        : "r"(w));
+}
+
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b)
+{
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// E8M0 byte -> the f16x2 pair (2^(S-127), 2^(S-127)); exact for 104 <= S <= 140 (the
+// range bank_scan certifies); 255 (NaN by the MX spec) -> 0, as the reference.
+__device__ __forceinline__ uint32_t scale_h2(uint32_t S)
+{
+    uint32_t h;
+    if (S == 255u) h = 0u;
+    else if (S >= 113u) h = (S - 112u) << 10;          // normal f16
+    else h = 1u << (S - 103u);                         // subnormal f16, S in 104..112
+    return h | (h << 16);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+// K-major, 128-byte swizzle shared-memory matrix descriptor (tcgen05 version 1): start
+// address, leading offset 16 B (unused for this layout), stride 1024 B between 8-row
+// groups, layout type 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A f16, B f16, both K-major, N, M = 128.
+__host__ __device__ constexpr uint32_t f16_idesc(int N)
+{
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | (8u << 24);
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+struct TcArgs {
+    int K;              // reduction width (L for gate/up, I for down)
+    int UE;             // units per expert
+    long long wy1, wy3, wys;   // weights map: first w1 (w2) row, first w3 row, rows per run
+    long long sy1, sy3, sys;   // scales map: same for the E8M0 rows
+    const uint8_t *safe;       // per-expert: 1 when every scale byte is in 104..140 or 255
+};
+
+template <int PHASE>   // 0 = gate/up (activation fused), 1 = down
+__global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_constant__ CUtensorMap wmap,
+                                                               const __grid_constant__ CUtensorMap smap,
+                                                               const __grid_constant__ CUtensorMap bhmap,
+                                                               const __grid_constant__ CUtensorMap blmap,
+                                                               MoePlan p, K3GpuExpertBank bank, TcArgs ta,
+                                                               int act, float b1, float b2)
+{
+    // declared 1024-aligned (the 128-byte TMA swizzle repeats every 1024 bytes) and used
+    // as is, so every access below stays a shared-memory access
+    extern __shared__ __align__(1024) unsigned char smem[];
+    if ((s_addr(smem) & 1023u) != 0u) {   // never expected: refuse rather than mis-swizzle
+        if (threadIdx.x == 0) flag(DEV_BAD_INDEX);
+        return;
+    }
+    float *xch = reinterpret_cast<float *>(smem + (size_t)TC_NS * TC_STAGE);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)TC_NS * TC_STAGE + TC_XCH_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + TC_NBAR);
+    int4 *tab = reinterpret_cast<int4 *>(bars + TC_NBAR + 2);   // [TC_TAB] {e, cnt, off, flags}
+    uint64_t *b_full = bars, *b_empty = bars + TC_NS;
+    uint64_t *b_aready = bars + 2 * TC_NS, *b_afree = bars + 2 * TC_NS + TC_NA;
+    uint64_t *b_pfull = bars + 2 * TC_NS + 2 * TC_NA, *b_pfree = b_pfull + 2;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < TC_NS; s++) {
+            bar_init(s_addr(&b_full[s]), 1);
+            bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + 1);   // decode warps + the MMA commit
+        }
+        for (int a = 0; a < TC_NA; a++) {
+            bar_init(s_addr(&b_aready[a]), 4);                  // the four warps of that K half
+            bar_init(s_addr(&b_afree[a]), 1);                   // MMA commit
+        }
+        for (int d = 0; d < 2; d++) {
+            bar_init(s_addr(&b_pfull[d]), 1);                   // MMA commit
+            bar_init(s_addr(&b_pfree[d]), 4);                   // epilogue warps
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // the active experts of this call, once per CTA: {expert, tokens, first pair, flags}
+    // with flags bit 0 = some input row has a lo half, bit 1 = left to the mma.sync path
+    const int na = *p.n_active;
+    for (int a = tid; a < na && a < TC_TAB; a += TC_THREADS) {
+        const int e = p.act[a];
+        const int lo = p.elo[(PHASE == 0 ? 0 : bank.n_experts) + e];
+        const int skip = (ta.safe && !ta.safe[e]) ? 2 : 0;
+        tab[a] = make_int4(e, p.cnt[e], p.off[e], (lo ? 1 : 0) | skip);
+    }
+    if (warp == 0) {   // 512 TMEM columns: stage partials at 0 and 32, A buffers from 64
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    const int K = ta.K, NK = K / TC_KC, G = K / 32;
+    const int n_units = *p.n_active * ta.UE;
+    const int *Xe = PHASE == 0 ? p.ze : p.he;
+    bool failed = false;
+
+// the unit/pass/stage sequence every role walks identically
+#define TC_FOR_UNITS(...)                                                                   \
+    {                                                                                        \
+        int item = 0, unit_i = 0;                                                            \
+        for (int u = blockIdx.x; u < n_units && !failed; u += gridDim.x) {                  \
+            const int4 ent = unit_entry(u / ta.UE);                                          \
+            if (ent.w & 2) continue;                                                         \
+            const int e = ent.x, ub = u % ta.UE, nt = ent.y, q0 = ent.z;                      \
+            const bool lo_any = (ent.w & 1) != 0;                                            \
+            for (int tb = 0; tb < nt && !failed; tb += TC_N, unit_i++) {                     \
+                const int npt = min(TC_N, nt - tb);                                          \
+                __VA_ARGS__                                                                  \
+            }                                                                                \
+        }                                                                                    \
+    }
+    auto unit_entry = [&](int a) -> int4 {
+        if (a < TC_TAB) return tab[a];
+        const int e = p.act[a];
+        const int lo = p.elo[(PHASE == 0 ? 0 : bank.n_experts) + e];
+        return make_int4(e, p.cnt[e], p.off[e], (lo ? 1 : 0) | ((ta.safe && !ta.safe[e]) ? 2 : 0));
+    };
+    (void)na;
+
+    if (warp == TC_TMA_WARP) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
+            TC_FOR_UNITS({
+                for (int kc = 0; kc < NK && !failed; kc++, item++) {
+                    const int st = item % TC_NS;
+                    const uint32_t par = (uint32_t)((item / TC_NS) & 1);
+                    if (!bar_wait(s_addr(&b_empty[st]), par ^ 1u)) { failed = true; break; }
+                    unsigned char *sw = smem + (size_t)st * TC_STAGE;
+                    unsigned char *ssb = sw + TC_W_BYTES;
+                    unsigned char *sbh = sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024);
+                    unsigned char *sbl = sbh + TC_B_BYTES;
+                    const uint32_t full = s_addr(&b_full[st]);
+                    bar_expect(full, (uint32_t)(TC_W_BYTES + TC_S_BYTES + TC_B_BYTES * (lo_any ? 2 : 1)));
+                    const int x0 = kc * 256, xs = kc * 16;
+                    if (PHASE == 0) {
+                        const int y1 = (int)(e * ta.wys + ta.wy1 + ub * 64), y3 = (int)(e * ta.wys + ta.wy3 + ub * 64);
+                        tma2d(s_addr(sw), &wmap, x0, y1, full);
+                        tma2d(s_addr(sw + 8192), &wmap, x0 + 128, y1, full);
+                        tma2d(s_addr(sw + 16384), &wmap, x0, y3, full);
+                        tma2d(s_addr(sw + 24576), &wmap, x0 + 128, y3, full);
+                        tma2d(s_addr(ssb), &smap, xs, (int)(e * ta.sys + ta.sy1 + ub * 64), full);
+                        tma2d(s_addr(ssb + 1024), &smap, xs, (int)(e * ta.sys + ta.sy3 + ub * 64), full);
+                    } else {
+                        const int y1 = (int)(e * ta.wys + ta.wy1 + ub * 128);
+                        tma2d(s_addr(sw), &wmap, x0, y1, full);
+                        tma2d(s_addr(sw + 16384), &wmap, x0 + 128, y1, full);
+                        tma2d(s_addr(ssb), &smap, xs, (int)(e * ta.sys + ta.sy1 + ub * 128), full);
+                    }
+                    // activation tiles: 8 atoms of 64 K x 16 pair rows (rows past the expert
+                    // belong to the next one or lie past the tensor: those columns are
+                    // never read back; out-of-range rows are filled with zeros)
+                    for (int a = 0; a < TC_KC / 64; a++) {
+                        tma2d(s_addr(sbh + a * (TC_N * 128)), &bhmap, kc * TC_KC + a * 64, q0 + tb, full);
+                        if (lo_any) tma2d(s_addr(sbl + a * (TC_N * 128)), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
+                    }
+                }
+            });
+            if (failed) flag(DEV_TIMEOUT);
+        }
+    } else if (warp == TC_MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t idesc = f16_idesc(TC_N);
+            int ahalf = 0;   // running count of A-buffer fills (two per stage)
+            TC_FOR_UNITS({
+                for (int kc = 0; kc < NK && !failed; kc++, item++) {
+                    const int st = item % TC_NS;
+                    const uint32_t par = (uint32_t)((item / TC_NS) & 1);
+                    // each stage accumulates into a fresh TMEM partial (double-buffered);
+                    // the epilogue warps sum the partials in fp32
+                    const int pb = item & 1;
+                    if (!bar_wait(s_addr(&b_pfree[pb]), (uint32_t)(((item >> 1) & 1) ^ 1))) { failed = true; break; }
+                    if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t dtm = tmem + (uint32_t)(pb * 32);
+                    const unsigned char *sw = smem + (size_t)st * TC_STAGE;
+                    const uint32_t bh = s_addr(sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
+                    const uint32_t bl = bh + TC_B_BYTES;
+                    for (int h = 0; h < 2 && !failed; h++, ahalf++) {
+                        const int ab = ahalf % TC_NA;
+                        const uint32_t apar = (uint32_t)((ahalf / TC_NA) & 1);
+                        if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const uint32_t atm = tmem + (uint32_t)(TC_ACOL0 + ab * 128);
+                        for (int s = 0; s < 16; s++) {            // K16 steps of the half
+                            const int kk = h * 256 + s * 16;      // K offset in the stage
+                            const uint32_t boff = (uint32_t)((kk >> 6) * (TC_N * 128) + (kk & 63) * 2);
+                            mma_ts(dtm, atm + (uint32_t)(s * 8), sw128_desc(bh + boff), idesc, (h | s) ? 1u : 0u);
+                            if (lo_any) mma_ts(dtm, atm + (uint32_t)(s * 8), sw128_desc(bl + boff), idesc, 1u);
+                        }
+                        mma_commit(s_addr(&b_afree[ab]));
+                    }
+                    mma_commit(s_addr(&b_empty[st]));
+                    mma_commit(s_addr(&b_pfull[pb]));
+                }
+            });
+            if (failed) flag(DEV_TIMEOUT);
+        }
+    } else if (warp < TC_DEQ_WARPS) {
+        // ------------------------------------------------------------------ decode
+        const int quarter = warp & 3, h = warp >> 2;     // TMEM lanes 32*quarter.., K half h
+        const int r = quarter * 32 + lane;                // weight row of the unit = TMEM lane
+        // shared-memory rows of this thread: box row and box base inside the stage
+        int boxrow, boxbase;
+        if (PHASE == 0) { boxrow = r & 63; boxbase = r < 64 ? 0 : 16384; }
+        else { boxrow = r; boxbase = 0; }
+        const int hbox = PHASE == 0 ? 8192 : 16384;       // the second (hi-K) box
+        const int swz = boxrow & 7;
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        int ahalf = 0;
+        TC_FOR_UNITS({
+            for (int kc = 0; kc < NK && !failed; kc++, item++) {
+                const int st = item % TC_NS;
+                const uint32_t par = (uint32_t)((item / TC_NS) & 1);
+                // the A buffer this warp fills: half h of this stage
+                const int fill = 2 * item + h;
+                const int ab = fill % TC_NA;
+                const uint32_t apar = (uint32_t)((fill / TC_NA) & 1);
+                if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
+                if (!bar_wait(s_addr(&b_afree[ab]), apar ^ 1u)) { failed = true; break; }
+                const unsigned char *sw = smem + (size_t)st * TC_STAGE;
+                const unsigned char *row = sw + boxbase + h * hbox + boxrow * 128;
+                const uint2 sc = *reinterpret_cast<const uint2 *>(sw + TC_W_BYTES + r * 16 + h * 8);
+                const uint32_t atm = tmem + lane_addr + (uint32_t)(TC_ACOL0 + ab * 128);
+_Pragma("unroll")
+                for (int g8 = 0; g8 < 8; g8++) {          // 8 groups of 32 in this K half
+                    const uint4 pk = *reinterpret_cast<const uint4 *>(row + ((g8 ^ swz) << 4));
+                    const uint32_t S = ((g8 < 4 ? sc.x : sc.y) >> (8 * (g8 & 3))) & 0xFFu;
+                    const uint32_t s2 = scale_h2(S);
+                    uint32_t v[16];
+                    uint32_t t4[4];
+                    cvt4h(pk.x, t4);
+                    v[0] = hmul2u(t4[0], s2); v[1] = hmul2u(t4[1], s2); v[2] = hmul2u(t4[2], s2); v[3] = hmul2u(t4[3], s2);
+                    cvt4h(pk.y, t4);
+                    v[4] = hmul2u(t4[0], s2); v[5] = hmul2u(t4[1], s2); v[6] = hmul2u(t4[2], s2); v[7] = hmul2u(t4[3], s2);
+                    cvt4h(pk.z, t4);
+                    v[8] = hmul2u(t4[0], s2); v[9] = hmul2u(t4[1], s2); v[10] = hmul2u(t4[2], s2); v[11] = hmul2u(t4[3], s2);
+                    cvt4h(pk.w, t4);
+                    v[12] = hmul2u(t4[0], s2); v[13] = hmul2u(t4[1], s2); v[14] = hmul2u(t4[2], s2); v[15] = hmul2u(t4[3], s2);
+                    tmem_st16(atm + (uint32_t)(g8 * 16), v);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    bar_arrive(s_addr(&b_aready[ab]));
+                    bar_arrive(s_addr(&b_empty[st]));
+                }
+            }
+        });
+        if (failed && lane == 0) flag(DEV_TIMEOUT);
+    } else if (warp >= TC_EPI_WARP0 && warp < TC_EPI_WARP0 + 4) {
+        // ---------------------------------------------------------------- epilogue
+        const int quarter = warp - TC_EPI_WARP0;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        TC_FOR_UNITS({
+            // the pass's per-token metadata, one token per lane, fetched before the stages
+            const int nl = lane & (TC_N - 1);
+            const bool vl = nl < npt;
+            const int ex_l = vl ? Xe[q0 + tb + nl] : 0;
+            const int dst_l = (PHASE == 1 && vl) ? p.pair_dst[q0 + tb + nl] : 0;
+            float acc[TC_N];
+_Pragma("unroll")
+            for (int n = 0; n < TC_N; n++) acc[n] = 0.0f;
+            for (int kc = 0; kc < NK && !failed; kc++, item++) {
+                const int pb = item & 1;
+                if (!bar_wait(s_addr(&b_pfull[pb]), (uint32_t)((item >> 1) & 1))) { failed = true; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                uint32_t dv[16];
+                tmem_ld16(tmem + lane_addr + (uint32_t)(pb * 32), dv);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(s_addr(&b_pfree[pb]));
+_Pragma("unroll")
+                for (int n = 0; n < TC_N; n++) acc[n] += __uint_as_float(dv[n]);
+            }
+            if (failed) break;
+            if (PHASE == 0) {
+                // lanes 64..127 hold the up rows: hand them to the gate lanes 0..63
+                if (r >= 64)
+                    for (int n = 0; n < TC_N; n++) xch[(r - 64) * TC_N + n] = acc[n];
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                if (r < 64) {
+                    for (int n = 0; n < npt; n++) {
+                        const int q = q0 + tb + n;
+                        const int ex = __shfl_sync(0xffffffffu, ex_l, n);
+                        const float gv = ldexpf(acc[n], ex);
+                        const float uv = ldexpf(xch[r * TC_N + n], ex);
+                        const float hv = act == K3GPU_ACT_SITU ? act_situ(gv, uv, b1, b2) : act_swiglu(gv, uv);
+                        p.H[(size_t)q * bank.I + ub * 64 + r] = hv;
+                    }
+                }
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+            } else {
+                for (int n = 0; n < npt; n++) {
+                    const int ex = __shfl_sync(0xffffffffu, ex_l, n);
+                    const int dst = __shfl_sync(0xffffffffu, dst_l, n);
+                    p.contrib[(size_t)dst * bank.L + ub * 128 + r] = ldexpf(acc[n], ex);
+                }
+            }
+        });
+        if (failed && lane == 0) flag(DEV_TIMEOUT);
+    }
+#undef TC_FOR_UNITS
+    // every role reaches here (waits are bounded); free TMEM before leaving
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+// Gather the expert inputs into pair order as exact f16 hi/lo rows with the row's
+// power-of-two exponent (the gate/up B operand): row q = z[pair_tok[q]].
+__global__ void __launch_bounds__(256) tc_pack_pairs_kernel(__half *__restrict__ hi, __half *__restrict__ lo,
+                                                            int *__restrict__ ex, int *__restrict__ lf,
+                                                            const float *__restrict__ z,
+                                                            const int *__restrict__ pair_tok,
+                                                            const int *__restrict__ pair_exp,
+                                                            int *__restrict__ elo,
+                                                            const int *__restrict__ nrows, int K)
+{
+    __shared__ float redm[8];
+    __shared__ int redf[8];
+    const int q = blockIdx.x;
+    if (q >= *nrows) return;
+    const float *xr = z + (size_t)pair_tok[q] * K;
+    float m = 0.f;
+    for (int i = threadIdx.x; i < K; i += 256) m = fmaxf(m, fabsf(xr[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) redm[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = redm[0];
+    for (int w = 1; w < 8; w++) m = fmaxf(m, redm[w]);
+    int e = 0;
+    if (m > 0.f && m <= 3.4e38f) e = max(-126, min(127, ilogbf(m) - 14));
+    int any = 0;
+    for (int i = threadIdx.x; i < K; i += 256) {
+        const float y = ldexpf(xr[i], -e);
+        const __half h = __float2half_rn(y);
+        const __half l = __float2half_rn(y - __half2float(h));
+        hi[(size_t)q * K + i] = h;
+        lo[(size_t)q * K + i] = l;
+        any |= __half_as_ushort(l) != 0;
+    }
+    any = __any_sync(0xffffffffu, any);
+    if ((threadIdx.x & 31) == 0) redf[threadIdx.x >> 5] = any;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int f = 0;
+        for (int w = 0; w < 8; w++) f |= redf[w];
+        ex[q] = e;
+        lf[q] = f;
+        if (f) atomicOr(&elo[pair_exp[q]], 1);
+    }
+}
+
+// One CTA per expert: 1 when every E8M0 byte of its three matrices lies in 104..140 or is
+// 255, i.e. when scale * E2M1 is exact in f16 for every weight.
+__global__ void __launch_bounds__(256) tc_bank_scan_kernel(uint8_t *__restrict__ safe, K3GpuExpertBank b)
+{
+    __shared__ int bad;
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    const uint8_t *run = b.base + (size_t)blockIdx.x * b.stride;
+    const long long n1 = (long long)b.I * (b.L / 32), n2 = (long long)b.L * (b.I / 32);
+    int mybad = 0;
+    for (long long i = threadIdx.x; i < n1; i += 256) {
+        const unsigned s1 = run[b.s1 + i], s3 = run[b.s3 + i];
+        mybad |= (s1 != 255u && (s1 < 104u || s1 > 140u)) | (s3 != 255u && (s3 < 104u || s3 > 140u));
+    }
+    for (long long i = threadIdx.x; i < n2; i += 256) {
+        const unsigned s2 = run[b.s2 + i];
+        mybad |= s2 != 255u && (s2 < 104u || s2 > 140u);
+    }
+    if (mybad) atomicOr(&bad, 1);
+    __syncthreads();
+    if (threadIdx.x == 0) safe[blockIdx.x] = bad ? 0 : 1;
+}
+
+// ---- host side ---------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn2)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn2 tc_encode()
+{
+    static EncodeTiledFn2 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *q = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn2>(q);
+    });
+    return fn;
+}
+
+static int tc_map(CUtensorMap *m, CUtensorMapDataType dt, int esize, const void *base, long long cols,
+                  long long rows, int box_w, int box_rows, CUtensorMapSwizzle swz)
+{
+    EncodeTiledFn2 fn = tc_encode();
+    if (!fn) return K3GPU_ECUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * esize)};
+    cuuint32_t box[2] = {(cuuint32_t)box_w, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        g_last_cuda_error = (int)r;
+        return K3GPU_ECUDA;
+    }
+    return K3GPU_OK;
+}
+
+bool tc_bank_ok(const K3GpuExpertBank &b)
+{
+    return b.f16_safe != nullptr && mma_bank_ok(b);
+}
+
+static int g_tc_ready_dev = -1;
+
+int tc_pack_pairs_launch(const MoePlan &p, const float *z, int L, int P, int E, cudaStream_t s)
+{
+    tc_pack_pairs_kernel<<<P, 256, 0, s>>>(p.zh, p.zl, p.ze, p.zf, z, p.pair_tok, p.pair_exp, p.elo,
+                                           p.off + E, L);
+    return launch_status();
+}
+
+int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, int P, int act, float b1,
+                    float b2, cudaStream_t s)
+{
+    const int L = bank.L, I = bank.I;
+    const unsigned long long bytes = (unsigned long long)bank.n_experts * (unsigned long long)bank.stride;
+    CUtensorMap wm, sm, bh, bl;
+    int st;
+    if (phase == 0) {
+        st = tc_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, L / 2, (long long)(bytes / (L / 2)), 128, 64,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, L / 32, (long long)(bytes / (L / 32)), 16, 64,
+                             CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zh, L, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zl, L, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+        st = tc_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, I / 2, (long long)(bytes / (I / 2)), 128, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, I / 32, (long long)(bytes / (I / 32)), 16, 128,
+                             CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hh, I, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hl, I, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (st) return st;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (g_tc_ready_dev != dev) {
+        st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+        if (!st) st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+        if (st) return st;
+        g_tc_ready_dev = dev;
+    }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long pl = L / 2, pi = I / 2, ql = L / 32, qi = I / 32;
+    TcArgs a;
+    a.safe = bank.f16_safe;
+    if (phase == 0) {
+        a.K = L; a.UE = I / 64;
+        a.wys = bank.stride / pl; a.wy1 = bank.p1 / pl; a.wy3 = bank.p3 / pl;
+        a.sys = bank.stride / ql; a.sy1 = bank.s1 / ql; a.sy3 = bank.s3 / ql;
+        moe_tc_kernel<0><<<sms, TC_THREADS, TC_SMEM, s>>>(wm, sm, bh, bl, p, bank, a, act, b1, b2);
+    } else {
+        a.K = I; a.UE = L / 128;
+        a.wys = bank.stride / pi; a.wy1 = bank.p2 / pi; a.wy3 = 0;
+        a.sys = bank.stride / qi; a.sy1 = bank.s2 / qi; a.sy3 = 0;
+        moe_tc_kernel<1><<<sms, TC_THREADS, TC_SMEM, s>>>(wm, sm, bh, bl, p, bank, a, act, b1, b2);
+    }
+    return launch_status();
+}
+
+int tc_bank_scan(const K3GpuExpertBank &b, uint8_t *safe, cudaStream_t s)
+{
+    tc_bank_scan_kernel<<<b.n_experts, 256, 0, s>>>(safe, b);
+    return launch_status();
+}
+
+}  // namespace k3

@@ -176,7 +176,15 @@ ORC_API void orc_bank_layout(OrcBankLayout *lay, int L, int I)
     lay->p3 = pw + sw + pd + sd;
     lay->s3 = pw + sw + pd + sd + pw;
     int64_t run = pw + sw + pd + sd + pw + sw;
-    lay->stride = (run + 255) & ~(int64_t)255;
+    /* the device library's stride: run rounded up to lcm(L/2, I/2, 256) */
+    int64_t q = 256;
+    const int64_t vs[2] = {(int64_t)L / 2, (int64_t)I / 2};
+    for (int k = 0; k < 2; k++) {
+        int64_t a = q, c = vs[k];
+        while (c) { const int64_t r = a % c; a = c; c = r; }
+        q = q / a * vs[k];
+    }
+    lay->stride = (run + q - 1) / q * q;
 }
 
 /* One routed expert on one latent row, the loop body of src/core/k3_ops.c:1923-1926

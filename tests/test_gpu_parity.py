@@ -144,6 +144,88 @@ def test_moe_c2_width_vs_oracle(k3):
     assert rel_l2(host(out), ref) < 1e-5, rel_l2(host(out), ref)
 
 
+@pytest.mark.parametrize("which", [0, 1], ids=["tensor", "cudacore"])
+def test_moe_expert_kernels_fp32_inputs_many_tokens(k3, which):
+    """Both expert streams on tensor-core-eligible shapes (L, I multiples of 512) with
+    fp32 (not bf16) inputs, so the lo half of the f16 split is live, and up to 48 tokens
+    per expert: several 8-token chunks and a second pass over the weights."""
+    L, I, n, ns, k, T = 1024, 512, 4, 1, 3, 64
+    rng = np.random.default_rng(21)
+    bank, lay = O.make_bank(rng, n + ns, L, I, std=0.05, w13_std=0.1)
+    x = rng.standard_normal((T, L), dtype=np.float32)
+    W = rng.standard_normal((n, L), dtype=np.float32) * np.float32(0.02)
+    bias = np.zeros(n, np.float32)
+    kb = k3.ExpertBank(dev(bank), n + ns, L, I)
+    k3.check(k3.lib.k3gpu_moe_select_kernels(which), "select")
+    try:
+        out, idx, wt = k3.moe_layer(dev(x), dev(W), dev(bias), kb, k, n, ns, 1)
+    finally:
+        k3.check(k3.lib.k3gpu_moe_select_kernels(0), "select")
+    ri, rw = O.router(x, W, bias, k)
+    np.testing.assert_array_equal(host(idx), ri)
+    ref = O.moe_routed(x, ri, rw, bank, lay, L, I, k, n, ns, 1)
+    assert rel_l2(host(out), ref) < 1e-5, rel_l2(host(out), ref)
+    assert_clean(k3)
+
+
+@pytest.mark.parametrize("fp32_inputs", [False, True], ids=["bf16in", "fp32in"])
+def test_moe_tcgen05_path_vs_oracle(k3, fp32_inputs):
+    """The tcgen05 expert kernels (bank certified by k3gpu_bank_scan): BASELINE config-2
+    widths on 24 experts, then a 1024/512 case with up to 48 tokens per expert (three
+    16-token passes) and, for fp32 inputs, the lo halves of the f16 split."""
+    for (L, I, n, ns, k, T, seed) in ((7168, 2048, 24, 1, 8, 6, 31), (1024, 512, 4, 1, 3, 64, 32)):
+        rng = np.random.default_rng(seed)
+        bank, lay = O.make_bank(rng, n + ns, L, I, std=0.05, w13_std=0.1)
+        x = rng.standard_normal((T, L), dtype=np.float32)
+        if not fp32_inputs:
+            x = GI.bf16_round(x)
+        W = rng.standard_normal((n, L), dtype=np.float32) * np.float32(0.02)
+        bias = rng.standard_normal(n, dtype=np.float32) * np.float32(0.01)
+        kb = k3.ExpertBank(dev(bank), n + ns, L, I)
+        assert kb.scan() == 0                       # every expert certified
+        out, idx, wt = k3.moe_layer(dev(x), dev(W), dev(bias), kb, k, n, ns, 1)
+        ri, rw = O.router(x, W, bias, k)
+        np.testing.assert_array_equal(host(idx), ri)
+        ref = O.moe_routed(x, ri, rw, bank, lay, L, I, k, n, ns, 1)
+        assert rel_l2(host(out), ref) < 1e-5, (L, rel_l2(host(out), ref))
+    assert_clean(k3)
+
+
+def test_moe_mixed_bank_tcgen05_and_sync_paths(k3):
+    """One expert carries E8M0 bytes outside the f16-exact range (141), so the scan leaves
+    it to the mma.sync kernels while the rest run on tcgen05; the sum must not care."""
+    L, I, n, ns, k, T = 1024, 512, 6, 1, 2, 24
+    rng = np.random.default_rng(33)
+    bank, lay = O.make_bank(rng, n + ns, L, I, std=0.05, w13_std=0.1)
+    stride = int(lay[6])
+    bank[2 * stride + int(lay[1]) + 5] = 141          # expert 2, one w1 scale byte
+    x = GI.bf16_round(rng.standard_normal((T, L), dtype=np.float32))
+    W = rng.standard_normal((n, L), dtype=np.float32) * np.float32(0.02)
+    bias = np.zeros(n, np.float32)
+    kb = k3.ExpertBank(dev(bank), n + ns, L, I)
+    assert kb.scan() == 1
+    assert host(kb.safe).tolist() == [1, 1, 0, 1, 1, 1, 1]
+    out, idx, wt = k3.moe_layer(dev(x), dev(W), dev(bias), kb, k, n, ns, 1)
+    ri, rw = O.router(x, W, bias, k)
+    ref = O.moe_routed(x, ri, rw, bank, lay, L, I, k, n, ns, 1)
+    assert rel_l2(host(out), ref) < 1e-5, rel_l2(host(out), ref)
+    assert_clean(k3)
+
+
+def test_moe_c2_width_cudacore_path(k3):
+    L, I, n, ns, k, T = 7168, 2048, 12, 1, 8, 3
+    bank, lay, x, W, bias = moe_case(19, L, I, n, ns, k, T, 1)
+    kb = k3.ExpertBank(dev(bank), n + ns, L, I)
+    k3.check(k3.lib.k3gpu_moe_select_kernels(1), "select")
+    try:
+        out, idx, wt = k3.moe_layer(dev(x), dev(W), dev(bias), kb, k, n, ns, 1)
+    finally:
+        k3.check(k3.lib.k3gpu_moe_select_kernels(0), "select")
+    ri, rw = O.router(x, W, bias, k)
+    ref = O.moe_routed(x, ri, rw, bank, lay, L, I, k, n, ns, 1)
+    assert rel_l2(host(out), ref) < 1e-5
+
+
 def test_moe_many_tokens_per_expert(k3):
     """Odd and even token counts per expert (the 2-token and 1-token paths)."""
     L, I, n, ns, k, T = 256, 64, 4, 1, 3, 33
