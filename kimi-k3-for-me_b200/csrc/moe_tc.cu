@@ -9,11 +9,12 @@
 //   decode    eight warps, one thread per weight row: cvt.rn.f16x2.e2m1x2 (exact), times
 //             the group's power of two 2^(S-127) as an f16 (exact for 104 <= S <= 140, which
 //             bank_scan certifies per expert), tcgen05.st into a TMEM A buffer
-//   MMA       one thread: tcgen05.mma kind::f16, A from TMEM (128 rows x 16 K), B from
-//             shared memory (K x 16 tokens), fp32 accumulator in TMEM; hi and lo halves of
-//             the activations accumulate into the same D
-//   epilogue  four warps: tcgen05.ld of D, row exponent, activation (gate/up) or the
-//             contribution store (down)
+//   MMA       four issuer warps, one K quarter of the stage each: tcgen05.mma kind::f16,
+//             A from TMEM (128 rows x 16 K), B from shared memory (K x 16 tokens), fp32
+//             accumulator in TMEM, one per issuer; hi and lo halves of the activations
+//             accumulate into the same D
+//   epilogue  four warps: tcgen05.ld of the four stage partials, fp32 sum, row exponent,
+//             activation (gate/up) or the contribution store (down)
 //
 // Shared memory carries only packed bytes and activation tiles; the f16 weights live in
 // tensor memory, so the shared-memory bandwidth is not a ceiling. Every wait is bounded;
@@ -33,8 +34,9 @@ namespace k3 {
 constexpr int TC_DEQ_WARPS = 8;          // warps 0..7: decode (two per TMEM lane quarter)
 constexpr int TC_EPI_WARP0 = 8;          // warps 8..11: epilogue
 constexpr int TC_TMA_WARP = 12;
-constexpr int TC_MMA_WARP = 13;
-constexpr int TC_THREADS = 14 * 32;
+constexpr int TC_MMA_WARP0 = 13;         // warps 13..16: MMA issuers, one K quarter of a stage each
+constexpr int TC_NMMA = 4;
+constexpr int TC_THREADS = (TC_MMA_WARP0 + TC_NMMA) * 32;
 constexpr int TC_KC = 512;               // K elements per shared-memory stage
 constexpr int TC_N = 16;                 // tokens per pass (MMA N)
 constexpr int TC_W_BYTES = 128 * 256;    // packed weights of a stage (32 KB)
@@ -43,7 +45,8 @@ constexpr int TC_B_BYTES = (TC_KC / 64) * TC_N * 128;   // 16 KB: 8 atoms x 16 r
 constexpr int TC_STAGE = TC_W_BYTES + TC_S_BYTES + 2 * TC_B_BYTES + 1024 - TC_S_BYTES % 1024;
 constexpr int TC_NS = 3;
 constexpr int TC_NA = 3;                 // TMEM A buffers (128 columns = 256 K each)
-constexpr int TC_ACOL0 = 64;             // first A column; stage partials at columns 0 and 32
+constexpr int TC_PCOLS = TC_NMMA * TC_N;  // one stage-partial set: a 16-column D per issuer
+constexpr int TC_ACOL0 = 2 * TC_PCOLS;   // first A column; partial sets at columns 0 and 64
 constexpr int TC_XCH_BYTES = 64 * TC_N * 4;   // gate/up exchange in the epilogue
 // barriers: full[NS] empty[NS] aready[NA] afree[NA] pfull[2] pfree[2] (stage partials)
 constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 4;
@@ -202,14 +205,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     if (tid == 0) {
         for (int s = 0; s < TC_NS; s++) {
             bar_init(s_addr(&b_full[s]), 1);
-            bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + 1);   // decode warps + the MMA commit
+            bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + TC_NMMA);   // decode warps + MMA commits
         }
         for (int a = 0; a < TC_NA; a++) {
             bar_init(s_addr(&b_aready[a]), 4);                  // the four warps of that K half
-            bar_init(s_addr(&b_afree[a]), 1);                   // MMA commit
+            bar_init(s_addr(&b_afree[a]), 2);                   // commits of the half's two issuers
         }
         for (int d = 0; d < 2; d++) {
-            bar_init(s_addr(&b_pfull[d]), 1);                   // MMA commit
+            bar_init(s_addr(&b_pfull[d]), TC_NMMA);             // MMA commits
             bar_init(s_addr(&b_pfree[d]), 4);                   // epilogue warps
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         const int skip = (ta.safe && !ta.safe[e]) ? 2 : 0;
         tab[a] = make_int4(e, p.cnt[e], p.off[e], (lo ? 1 : 0) | skip);
     }
-    if (warp == 0) {   // 512 TMEM columns: stage partials at 0 and 32, A buffers from 64
+    if (warp == 0) {   // 512 TMEM columns: partial sets at 0 and 64, A buffers from 128
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -302,38 +305,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
             });
             if (failed) flag(DEV_TIMEOUT);
         }
-    } else if (warp == TC_MMA_WARP) {
+    } else if (warp >= TC_MMA_WARP0 && warp < TC_MMA_WARP0 + TC_NMMA) {
+        // One thread issues an MMA about every 55 clocks however small N is, while the
+        // tensor pipe finishes an M128 x N16 x K16 step in about 9: four issuer warps, each
+        // with its own accumulator, keep the pipe fed. Issuer i takes K steps 8j..8j+7 of
+        // stage half h (i = 2h + j); every stage starts fresh partials (double-buffered)
+        // that the epilogue warps sum in fp32.
         if (lane == 0) {
+            const int mi = warp - TC_MMA_WARP0, h = mi >> 1, j = mi & 1;
             const uint32_t idesc = f16_idesc(TC_N);
-            int ahalf = 0;   // running count of A-buffer fills (two per stage)
             TC_FOR_UNITS({
                 for (int kc = 0; kc < NK && !failed; kc++, item++) {
                     const int st = item % TC_NS;
                     const uint32_t par = (uint32_t)((item / TC_NS) & 1);
-                    // each stage accumulates into a fresh TMEM partial (double-buffered);
-                    // the epilogue warps sum the partials in fp32
                     const int pb = item & 1;
+                    const int fill = 2 * item + h;   // the A buffer the decode warps filled
+                    const int ab = fill % TC_NA;
+                    const uint32_t apar = (uint32_t)((fill / TC_NA) & 1);
                     if (!bar_wait(s_addr(&b_pfree[pb]), (uint32_t)(((item >> 1) & 1) ^ 1))) { failed = true; break; }
                     if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
+                    if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t dtm = tmem + (uint32_t)(pb * 32);
+                    const uint32_t dtm = tmem + (uint32_t)(pb * TC_PCOLS + mi * TC_N);
                     const unsigned char *sw = smem + (size_t)st * TC_STAGE;
                     const uint32_t bh = s_addr(sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
                     const uint32_t bl = bh + TC_B_BYTES;
-                    for (int h = 0; h < 2 && !failed; h++, ahalf++) {
-                        const int ab = ahalf % TC_NA;
-                        const uint32_t apar = (uint32_t)((ahalf / TC_NA) & 1);
-                        if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
-                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const uint32_t atm = tmem + (uint32_t)(TC_ACOL0 + ab * 128);
-                        for (int s = 0; s < 16; s++) {            // K16 steps of the half
-                            const int kk = h * 256 + s * 16;      // K offset in the stage
-                            const uint32_t boff = (uint32_t)((kk >> 6) * (TC_N * 128) + (kk & 63) * 2);
-                            mma_ts(dtm, atm + (uint32_t)(s * 8), sw128_desc(bh + boff), idesc, (h | s) ? 1u : 0u);
-                            if (lo_any) mma_ts(dtm, atm + (uint32_t)(s * 8), sw128_desc(bl + boff), idesc, 1u);
-                        }
-                        mma_commit(s_addr(&b_afree[ab]));
+                    const uint32_t atm = tmem + (uint32_t)(TC_ACOL0 + ab * 128);
+_Pragma("unroll")
+                    for (int t = 0; t < 8; t++) {                 // K16 steps of this quarter
+                        const int s16 = j * 8 + t;                // step within the half
+                        const int kk = h * 256 + s16 * 16;        // K offset in the stage
+                        const uint32_t boff = (uint32_t)((kk >> 6) * (TC_N * 128) + (kk & 63) * 2);
+                        mma_ts(dtm, atm + (uint32_t)(s16 * 8), sw128_desc(bh + boff), idesc, t ? 1u : 0u);
+                        if (lo_any) mma_ts(dtm, atm + (uint32_t)(s16 * 8), sw128_desc(bl + boff), idesc, 1u);
                     }
+                    mma_commit(s_addr(&b_afree[ab]));
                     mma_commit(s_addr(&b_empty[st]));
                     mma_commit(s_addr(&b_pfull[pb]));
                 }
@@ -351,7 +357,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         const int hbox = PHASE == 0 ? 8192 : 16384;       // the second (hi-K) box
         const int swz = boxrow & 7;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-        int ahalf = 0;
         TC_FOR_UNITS({
             for (int kc = 0; kc < NK && !failed; kc++, item++) {
                 const int st = item % TC_NS;
@@ -411,14 +416,20 @@ _Pragma("unroll")
                 const int pb = item & 1;
                 if (!bar_wait(s_addr(&b_pfull[pb]), (uint32_t)((item >> 1) & 1))) { failed = true; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                uint32_t dv[16];
-                tmem_ld16(tmem + lane_addr + (uint32_t)(pb * 32), dv);
+                uint32_t d0[16], d1[16], d2[16], d3[16];
+                const uint32_t pt = tmem + lane_addr + (uint32_t)(pb * TC_PCOLS);
+                tmem_ld16(pt, d0);
+                tmem_ld16(pt + TC_N, d1);
+                tmem_ld16(pt + 2 * TC_N, d2);
+                tmem_ld16(pt + 3 * TC_N, d3);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) bar_arrive(s_addr(&b_pfree[pb]));
 _Pragma("unroll")
-                for (int n = 0; n < TC_N; n++) acc[n] += __uint_as_float(dv[n]);
+                for (int n = 0; n < TC_N; n++)
+                    acc[n] += (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
+                              (__uint_as_float(d2[n]) + __uint_as_float(d3[n]));
             }
             if (failed) break;
             if (PHASE == 0) {
