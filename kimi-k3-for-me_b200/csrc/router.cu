@@ -1,13 +1,17 @@
 // router.cu -- the MoE router (k3_router, src/core/k3_ops.c:1624-1719 of the reference)
 // for a whole verify batch.
 //
-// Scores: a register-tiled double-precision GEMM whose K loop runs in order inside each
-// thread, so every (token, expert) score is ONE double chain over i = 0..hidden-1 -- the
-// reference's chain (its 8-expert blocking changes issue order only). A float times a
-// float is exact in double, so fma(w, x, acc) == acc + w*x rounded once, exactly the
-// reference's `acc += (double)w * (double)x`. Tiles: 64 experts x 8 tokens per CTA,
-// 256 threads, each owning 2 experts x 1 token (two independent chains for the double
-// pipeline), operands staged through shared memory 64 columns at a time.
+// Scores: every (token, expert) score is ONE double chain over i = 0..hidden-1, in order,
+// inside one thread -- the reference's chain (its 8-expert blocking changes issue order
+// only). A float times a float is exact in double, so fma(w, x, acc) == acc + w*x rounded
+// once, exactly the reference's `acc += (double)w * (double)x`. The chain length sets the
+// floor (hidden dependent FMAs), so the kernel's job is to keep every chain issuing: a CTA
+// owns 24 experts x 8 tokens (one chain per thread), K tiles of 128 columns arrive by
+// cp.async two tiles ahead, and each tile is widened to double once in shared memory.
+// Measured on B200 the loop runs at about 20 clocks a step against the 8-clock FMA
+// latency: each warp-step moves four shared-memory wavefronts (operands re-read by the
+// lanes that share an expert or token), and the float-to-double widening is slow. Register
+// blocking over tokens and a widened copy made once per call are the way down.
 //
 // Selection: one warp per token, repeated max with the first-index tie rule, taken
 // entries set to -inf, weights from the unbiased scores, renormalised by one double sum
@@ -21,48 +25,117 @@
 
 namespace k3 {
 
-constexpr int RT_E = 64;     // experts per CTA
+constexpr int RT_E = 24;     // experts per CTA (384 experts x 72 tokens -> 144 CTAs)
 constexpr int RT_T = 8;      // tokens per CTA
-constexpr int RT_K = 64;     // hidden columns staged per step
+constexpr int RT_R = RT_E + RT_T;
+constexpr int RT_THREADS = RT_E * RT_T;   // one chain per thread
+constexpr int RT_K = 128;    // hidden columns per tile
+constexpr int RT_NS = 3;     // cp.async stages (float tiles in flight)
+constexpr int RT_LD = RT_K + 2;   // double tile row stride: rows land on distinct banks
+constexpr int RT_F_TILE = RT_R * RT_K;                      // floats per stage
+constexpr int RT_SMEM = RT_NS * RT_F_TILE * 4 + 2 * RT_R * RT_LD * 8;
 
-__global__ void __launch_bounds__(256) router_scores_kernel(float *__restrict__ score,
-                                                            const float *__restrict__ x,
-                                                            const float *__restrict__ W,
-                                                            int T, int hidden, int n)
+// one cp.async of V floats (V = 4: 16 bytes; V = 1: 4 bytes), zero-filled when !valid
+template <int V>
+__device__ __forceinline__ void cp_async_f(float *dst, const float *src, bool valid)
 {
-    __shared__ float ws[RT_E][RT_K + 1];
-    __shared__ float xs[RT_T][RT_K + 1];
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    const int n = valid ? 4 * V : 0;
+    if (V == 4)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+
+// eight chain steps from registers: acc += w[i] * x[i], i = 0..7 in order
+__device__ __forceinline__ double chain8(double acc, const double2 (&w)[4], const double2 (&x)[4])
+{
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        asm volatile("fma.rn.f64 %0, %1, %2, %0;" : "+d"(acc) : "d"(w[i].x), "d"(x[i].x));
+        asm volatile("fma.rn.f64 %0, %1, %2, %0;" : "+d"(acc) : "d"(w[i].y), "d"(x[i].y));
+    }
+    return acc;
+}
+
+__device__ __forceinline__ void load8(double2 (&w)[4], double2 (&x)[4], const double *wr, const double *xr)
+{
+    const uint32_t ws = (uint32_t)__cvta_generic_to_shared(wr), xs = (uint32_t)__cvta_generic_to_shared(xr);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(w[i].x), "=d"(w[i].y) : "r"(ws + 16 * i));
+        asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(x[i].x), "=d"(x[i].y) : "r"(xs + 16 * i));
+    }
+}
+
+template <int V>   // V = 4 when hidden % 4 == 0 and x, W are 16-byte aligned, else 1
+__global__ void __launch_bounds__(RT_THREADS) router_scores_kernel(float *__restrict__ score,
+                                                                   const float *__restrict__ x,
+                                                                   const float *__restrict__ W,
+                                                                   int T, int hidden, int n)
+{
+    extern __shared__ __align__(16) unsigned char rsm[];
+    float *fst = reinterpret_cast<float *>(rsm);                            // [NS][R][K]
+    double *dt = reinterpret_cast<double *>(rsm + RT_NS * RT_F_TILE * 4);   // [2][R][LD]
     const int e0 = blockIdx.x * RT_E, t0 = blockIdx.y * RT_T;
     const int tid = threadIdx.x;
-    const int tl = tid & 7;          // token within the tile
-    const int el = tid >> 3;         // experts el and el + 32
-    double acc0 = 0.0, acc1 = 0.0;
-    for (int k0 = 0; k0 < hidden; k0 += RT_K) {
-        const int kn = min(RT_K, hidden - k0);
-        for (int i = tid; i < RT_E * RT_K; i += 256) {
-            const int r = i / RT_K, c = i % RT_K;
-            const int e = e0 + r;
-            ws[r][c] = (e < n && c < kn) ? W[(size_t)e * hidden + k0 + c] : 0.0f;
+    const int tl = tid & 7;          // token of this thread's chain
+    const int el = tid >> 3;         // expert of this thread's chain
+    const int nt = (hidden + RT_K - 1) / RT_K;
+    constexpr int CPR = RT_K / V;    // copies per tile row
+
+    auto issue = [&](int kt) {
+        if (kt < nt) {
+            float *f = fst + (kt % RT_NS) * RT_F_TILE;
+            const int k0 = kt * RT_K;
+            for (int i = tid; i < RT_R * CPR; i += RT_THREADS) {
+                const int r = i / CPR, c = (i % CPR) * V;
+                const bool is_w = r < RT_E;
+                const int row = is_w ? e0 + r : t0 + (r - RT_E);
+                const bool ok = (is_w ? row < n : row < T) && k0 + c < hidden;
+                const float *src = is_w ? W : x;
+                if (ok) src += (size_t)row * hidden + k0 + c;
+                cp_async_f<V>(f + r * RT_K + c, src, ok);
+            }
         }
-        for (int i = tid; i < RT_T * RT_K; i += 256) {
-            const int r = i / RT_K, c = i % RT_K;
-            const int t = t0 + r;
-            xs[r][c] = (t < T && c < kn) ? x[(size_t)t * hidden + k0 + c] : 0.0f;
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int kt = 0; kt < RT_NS - 1; kt++) issue(kt);
+
+    double acc = 0.0;
+    for (int kt = 0; kt < nt; kt++) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(RT_NS - 2) : "memory");
+        __syncthreads();                       // tile kt landed for every thread's copies
+        issue(kt + RT_NS - 1);                 // into the stage tile kt-1 used
+        const float *f = fst + (kt % RT_NS) * RT_F_TILE;
+        double *d = dt + (kt & 1) * RT_R * RT_LD;
+        for (int i = tid; i < RT_F_TILE / 4; i += RT_THREADS) {   // widen once, 4 at a time
+            const float4 v = reinterpret_cast<const float4 *>(f)[i];
+            double *o = d + (i / (RT_K / 4)) * RT_LD + (i % (RT_K / 4)) * 4;
+            reinterpret_cast<double2 *>(o)[0] = make_double2(v.x, v.y);
+            reinterpret_cast<double2 *>(o)[1] = make_double2(v.z, v.w);
         }
         __syncthreads();
-        for (int c = 0; c < kn; c++) {
-            const double xv = (double)xs[tl][c];
-            acc0 = fma((double)ws[el][c], xv, acc0);
-            acc1 = fma((double)ws[el + 32][c], xv, acc1);
+        const double *wr = d + el * RT_LD;
+        const double *xr = d + (RT_E + tl) * RT_LD;
+        const int kn = min(RT_K, hidden - kt * RT_K);
+        if (kn == RT_K) {
+            double2 wa[4], xa[4], wb[4], xb[4];
+            load8(wa, xa, wr, xr);
+#pragma unroll
+            for (int c = 0; c < RT_K; c += 16) {
+                load8(wb, xb, wr + c + 8, xr + c + 8);
+                acc = chain8(acc, wa, xa);
+                if (c + 16 < RT_K) load8(wa, xa, wr + c + 16, xr + c + 16);
+                acc = chain8(acc, wb, xb);
+            }
+        } else {
+            for (int c = 0; c < kn; c++) acc = fma(wr[c], xr[c], acc);
         }
-        __syncthreads();
     }
-    const int t = t0 + tl;
-    if (t < T) {
-        const int ea = e0 + el, eb = e0 + el + 32;
-        if (ea < n) score[(size_t)t * n + ea] = sigmoid_cr(__double2float_rn(acc0));
-        if (eb < n) score[(size_t)t * n + eb] = sigmoid_cr(__double2float_rn(acc1));
-    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    const int t = t0 + tl, e = e0 + el;
+    if (t < T && e < n) score[(size_t)t * n + e] = sigmoid_cr(__double2float_rn(acc));
 }
 
 // One warp per token; scores [T][n] -> idx/w [T][topk]. Each lane keeps the selection
@@ -129,12 +202,35 @@ __global__ void __launch_bounds__(128) router_topk_kernel(int *__restrict__ idx,
     }
 }
 
+// The opt-in to more than 48 KB of dynamic shared memory, once per device and variant.
+static int router_smem_optin(bool v4)
+{
+    static std::mutex mu;
+    static bool done[64][2] = {};
+    int dev = 0;
+    int st = cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev][v4]) {
+        st = cuda_status(v4 ? cudaFuncSetAttribute(router_scores_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM)
+                            : cudaFuncSetAttribute(router_scores_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM));
+        if (st) return st;
+        done[dev][v4] = true;
+    }
+    return K3GPU_OK;
+}
+
 int router_launch(int *idx, float *w, const float *x, const float *W, const float *bias, int T,
                   int hidden, int n, int topk, int renorm, float routed_scale, float *score,
                   cudaStream_t s)
 {
     dim3 g1(ceil_div(n, RT_E), ceil_div(T, RT_T));
-    router_scores_kernel<<<g1, 256, 0, s>>>(score, x, W, T, hidden, n);
+    const bool v4 = hidden % 4 == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)W & 15u) == 0;
+    int st0 = router_smem_optin(v4);
+    if (st0) return st0;
+    if (v4) router_scores_kernel<4><<<g1, RT_THREADS, RT_SMEM, s>>>(score, x, W, T, hidden, n);
+    else router_scores_kernel<1><<<g1, RT_THREADS, RT_SMEM, s>>>(score, x, W, T, hidden, n);
     int st = launch_status();
     if (st) return st;
     router_topk_kernel<<<ceil_div(T, 4), 128, 0, s>>>(idx, w, score, bias, T, n, topk, renorm,

@@ -179,8 +179,11 @@ def mxfp4_quant(w: np.ndarray):
     scales = (ex + 127).astype(np.uint8)
     mult = np.exp2(ex.astype(np.float32)).reshape(R, g, 1)
     xq = blocks / mult
-    lut = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
-    idx = np.argmin(np.abs(np.abs(xq)[..., None] - lut), axis=-1).astype(np.uint8)
+    # nearest of {0, .5, 1, 1.5, 2, 3, 4, 6} with ties to the lower code: the count of
+    # midpoints strictly below |xq| (each |xq - lut| the argmin compares is exact in fp32,
+    # so this equals the generator's argmin, first index on ties)
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    idx = np.searchsorted(mids, np.abs(xq).ravel(), side="left").astype(np.uint8).reshape(xq.shape)
     nib = np.where(xq < 0, idx | 0x8, idx).astype(np.uint8)
     packed = (nib[:, :, 0::2] | (nib[:, :, 1::2] << 4)).reshape(R, Cc // 2)
     return np.ascontiguousarray(packed), np.ascontiguousarray(scales)
