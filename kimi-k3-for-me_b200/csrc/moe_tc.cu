@@ -371,9 +371,17 @@ _Pragma("unroll")
                 const unsigned char *row = sw + boxbase + h * hbox + boxrow * 128;
                 const uint2 sc = *reinterpret_cast<const uint2 *>(sw + TC_W_BYTES + r * 16 + h * 8);
                 const uint32_t atm = tmem + lane_addr + (uint32_t)(TC_ACOL0 + ab * 128);
+                // 8 groups of 32 in this K half, four at a time: the four loads go first (a
+                // load placed after a tcgen05.st would wait for it)
 _Pragma("unroll")
-                for (int g8 = 0; g8 < 8; g8++) {          // 8 groups of 32 in this K half
-                    const uint4 pk = *reinterpret_cast<const uint4 *>(row + ((g8 ^ swz) << 4));
+                for (int g4 = 0; g4 < 8; g4 += 4) {
+                uint4 pks[4];
+_Pragma("unroll")
+                for (int i = 0; i < 4; i++) pks[i] = *reinterpret_cast<const uint4 *>(row + (((g4 + i) ^ swz) << 4));
+_Pragma("unroll")
+                for (int i = 0; i < 4; i++) {
+                    const int g8 = g4 + i;
+                    const uint4 pk = pks[i];
                     const uint32_t S = ((g8 < 4 ? sc.x : sc.y) >> (8 * (g8 & 3))) & 0xFFu;
                     const uint32_t s2 = scale_h2(S);
                     uint32_t v[16];
@@ -387,6 +395,7 @@ _Pragma("unroll")
                     cvt4h(pk.w, t4);
                     v[12] = hmul2u(t4[0], s2); v[13] = hmul2u(t4[1], s2); v[14] = hmul2u(t4[2], s2); v[15] = hmul2u(t4[3], s2);
                     tmem_st16(atm + (uint32_t)(g8 * 16), v);
+                }
                 }
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -438,21 +447,28 @@ _Pragma("unroll")
                     for (int n = 0; n < TC_N; n++) xch[(r - 64) * TC_N + n] = acc[n];
                 asm volatile("bar.sync 2, 128;" ::: "memory");
                 if (r < 64) {
-                    for (int n = 0; n < npt; n++) {
-                        const int q = q0 + tb + n;
-                        const int ex = __shfl_sync(0xffffffffu, ex_l, n);
-                        const float gv = ldexpf(acc[n], ex);
-                        const float uv = ldexpf(xch[r * TC_N + n], ex);
-                        const float hv = act == K3GPU_ACT_SITU ? act_situ(gv, uv, b1, b2) : act_swiglu(gv, uv);
-                        p.H[(size_t)q * bank.I + ub * 64 + r] = hv;
+                    // n runs over all TC_N with a warp-uniform guard: acc stays in registers
+_Pragma("unroll")
+                    for (int n = 0; n < TC_N; n++) {
+                        if (n < npt) {
+                            const int q = q0 + tb + n;
+                            const int ex = __shfl_sync(0xffffffffu, ex_l, n);
+                            const float gv = ldexpf(acc[n], ex);
+                            const float uv = ldexpf(xch[r * TC_N + n], ex);
+                            const float hv = act == K3GPU_ACT_SITU ? act_situ(gv, uv, b1, b2) : act_swiglu(gv, uv);
+                            p.H[(size_t)q * bank.I + ub * 64 + r] = hv;
+                        }
                     }
                 }
                 asm volatile("bar.sync 2, 128;" ::: "memory");
             } else {
-                for (int n = 0; n < npt; n++) {
-                    const int ex = __shfl_sync(0xffffffffu, ex_l, n);
-                    const int dst = __shfl_sync(0xffffffffu, dst_l, n);
-                    p.contrib[(size_t)dst * bank.L + ub * 128 + r] = ldexpf(acc[n], ex);
+_Pragma("unroll")
+                for (int n = 0; n < TC_N; n++) {
+                    if (n < npt) {
+                        const int ex = __shfl_sync(0xffffffffu, ex_l, n);
+                        const int dst = __shfl_sync(0xffffffffu, dst_l, n);
+                        p.contrib[(size_t)dst * bank.L + ub * 128 + r] = ldexpf(acc[n], ex);
+                    }
                 }
             }
         });
