@@ -344,6 +344,50 @@ __global__ void __launch_bounds__(CMB_THREADS) moe_combine_kernel(
     }
 }
 
+// The combine without the latent RMSNorm (no row reduction): the same float operations in
+// the same order as moe_combine_kernel, four columns a thread and a grid over (token,
+// 1024-column block), with each batch of four slots' loads issued before their adds.
+__global__ void __launch_bounds__(CMB_THREADS) moe_combine_flat_kernel(
+    float *__restrict__ out, const float *__restrict__ contrib, const int *__restrict__ idx,
+    const float *__restrict__ wt, int L, int topk, int n_routed, int n_shared)
+{
+    const int t = blockIdx.x;
+    const int i = (blockIdx.y * CMB_THREADS + threadIdx.x) * 4;
+    if (i >= L) return;
+    const int S = topk + n_shared;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float *base = contrib + (size_t)t * S * L + i;
+    for (int j0 = 0; j0 < topk; j0 += 4) {
+        float4 c[4];
+        float w[4];
+        bool ok[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int j = j0 + u;
+            const int e = j < topk ? idx[(size_t)t * topk + j] : -1;
+            ok[u] = e >= 0 && e < n_routed;
+            w[u] = ok[u] ? wt[(size_t)t * topk + j] : 0.f;
+            c[u] = ok[u] ? *reinterpret_cast<const float4 *>(base + (size_t)j * L) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (!ok[u]) continue;
+            a.x = __fadd_rn(a.x, __fmul_rn(w[u], c[u].x));
+            a.y = __fadd_rn(a.y, __fmul_rn(w[u], c[u].y));
+            a.z = __fadd_rn(a.z, __fmul_rn(w[u], c[u].z));
+            a.w = __fadd_rn(a.w, __fmul_rn(w[u], c[u].w));
+        }
+    }
+    for (int sidx = topk; sidx < S; sidx++) {
+        const float4 c = *reinterpret_cast<const float4 *>(base + (size_t)sidx * L);
+        a.x = __fadd_rn(a.x, c.x);
+        a.y = __fadd_rn(a.y, c.y);
+        a.z = __fadd_rn(a.z, c.z);
+        a.w = __fadd_rn(a.w, c.w);
+    }
+    *reinterpret_cast<float4 *>(out + (size_t)t * L + i) = a;
+}
+
 // one thread per 32-element group: the expert kernels' decode, written out as floats
 __global__ void mxfp4_dequant_kernel(float *__restrict__ out, const uint8_t *__restrict__ packed,
                                      const uint8_t *__restrict__ scales, long long groups)
@@ -448,8 +492,14 @@ int moe_launch(float *out, const float *z, const int *idx, const float *wt,
         if ((st = launch_status())) return st;
     }
     phase_mark(4, s);
-    moe_combine_kernel<<<T, CMB_THREADS, 0, s>>>(out, p.contrib, idx, wt, latent_norm, eps,
-                                                 bank->L, topk, n_routed, n_shared);
+    if (latent_norm || (reinterpret_cast<uintptr_t>(out) & 15u)) {
+        moe_combine_kernel<<<T, CMB_THREADS, 0, s>>>(out, p.contrib, idx, wt, latent_norm, eps,
+                                                     bank->L, topk, n_routed, n_shared);
+    } else {
+        const dim3 g(T, ceil_div(bank->L, 4 * CMB_THREADS));
+        moe_combine_flat_kernel<<<g, CMB_THREADS, 0, s>>>(out, p.contrib, idx, wt, bank->L, topk,
+                                                          n_routed, n_shared);
+    }
     st = launch_status();
     phase_mark(5, s);
     return st;

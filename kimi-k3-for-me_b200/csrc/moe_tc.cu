@@ -52,7 +52,8 @@ constexpr int TC_XCH_BYTES = 64 * TC_N * 4;   // gate/up exchange in the epilogu
 constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 4;
 constexpr int TC_TAB = 1024;             // active-expert table entries kept in shared memory
 constexpr int TC_SMEM = TC_NS * TC_STAGE + TC_XCH_BYTES + TC_NBAR * 8 + 16 + TC_TAB * 16;
-constexpr long long TC_SPIN = 1LL << 24;
+constexpr long long TC_SPIN = 1LL << 22;
+constexpr int TC_SUSPEND_NS = 1000;
 
 static_assert(TC_STAGE % 1024 == 0, "stage alignment");
 
@@ -70,17 +71,20 @@ __device__ __forceinline__ void bar_arrive(uint32_t b)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
 }
+// A bounded wait on an mbarrier phase. Each try lets the hardware suspend the warp until
+// the phase completes or TC_SUSPEND_NS pass, so waiting warps (most of the epilogue's time,
+// a good part of everyone else's) do not take issue slots from the decode warps beside
+// them; TC_SPIN tries bound the whole wait (about 4 s).
 __device__ __forceinline__ bool bar_wait(uint32_t b, uint32_t parity)
 {
     for (long long i = 0; i < TC_SPIN; i++) {
         uint32_t ok;
-        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
                      " selp.u32 %0, 1, 0, p;\n}"
                      : "=r"(ok)
-                     : "r"(b), "r"(parity)
+                     : "r"(b), "r"(parity), "n"(TC_SUSPEND_NS)
                      : "memory");
         if (ok) return true;
-        if (i > 32) __nanosleep(32);
     }
     return false;
 }
