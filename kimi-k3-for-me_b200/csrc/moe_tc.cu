@@ -51,7 +51,8 @@ constexpr int TC_XCH_BYTES = 64 * TC_N * 4;   // gate/up exchange in the epilogu
 // barriers: full[NS] empty[NS] aready[NA] afree[NA] pfull[2] pfree[2] (stage partials)
 constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 4;
 constexpr int TC_TAB = 1024;             // active-expert table entries kept in shared memory
-constexpr int TC_SMEM = TC_NS * TC_STAGE + TC_XCH_BYTES + TC_NBAR * 8 + 16 + TC_TAB * 16;
+// after the expert table: the E8M0 byte -> f16x2 scale pair table (256 entries)
+constexpr int TC_SMEM = TC_NS * TC_STAGE + TC_XCH_BYTES + TC_NBAR * 8 + 16 + TC_TAB * 16 + 256 * 4;
 constexpr long long TC_SPIN = 1LL << 22;
 constexpr int TC_SUSPEND_NS = 1000;
 
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)TC_NS * TC_STAGE + TC_XCH_BYTES);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + TC_NBAR);
     int4 *tab = reinterpret_cast<int4 *>(bars + TC_NBAR + 2);   // [TC_TAB] {e, cnt, off, flags}
+    uint32_t *stab = reinterpret_cast<uint32_t *>(tab + TC_TAB);   // [256] scale_h2 of each byte
     uint64_t *b_full = bars, *b_empty = bars + TC_NS;
     uint64_t *b_aready = bars + 2 * TC_NS, *b_afree = bars + 2 * TC_NS + TC_NA;
     uint64_t *b_pfull = bars + 2 * TC_NS + 2 * TC_NA, *b_pfree = b_pfull + 2;
@@ -230,6 +232,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         const int skip = (ta.safe && !ta.safe[e]) ? 2 : 0;
         tab[a] = make_int4(e, p.cnt[e], p.off[e], (lo ? 1 : 0) | skip);
     }
+    for (int b = tid; b < 256; b += TC_THREADS)   // only certified bytes are ever looked up
+        stab[b] = (b == 255 || (b >= 104 && b <= 140)) ? scale_h2((uint32_t)b) : 0u;
     if (warp == 0) {   // 512 TMEM columns: partial sets at 0 and 64, A buffers from 128
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
                      : "memory");
@@ -387,7 +391,7 @@ _Pragma("unroll")
                     const int g8 = g4 + i;
                     const uint4 pk = pks[i];
                     const uint32_t S = ((g8 < 4 ? sc.x : sc.y) >> (8 * (g8 & 3))) & 0xFFu;
-                    const uint32_t s2 = scale_h2(S);
+                    const uint32_t s2 = stab[S];          // one shared load instead of ~8 ALU ops
                     uint32_t v[16];
                     uint32_t t4[4];
                     cvt4h(pk.x, t4);
