@@ -48,8 +48,8 @@ constexpr int TC_NA = 3;                 // TMEM A buffers (128 columns = 256 K 
 constexpr int TC_PCOLS = TC_NMMA * TC_N;  // one stage-partial set: a 16-column D per issuer
 constexpr int TC_ACOL0 = 2 * TC_PCOLS;   // first A column; partial sets at columns 0 and 64
 constexpr int TC_XCH_BYTES = 64 * TC_N * 4;   // gate/up exchange in the epilogue
-// barriers: full[NS] empty[NS] aready[NA] afree[NA] pfull[2] pfree[2] (stage partials)
-constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 4;
+// barriers: full[NS] empty[NS] aready[NA] afree[NA] pfree[2] (stage partials)
+constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 2;
 constexpr int TC_TAB = 1024;             // active-expert table entries kept in shared memory
 // after the expert table: the E8M0 byte -> f16x2 scale pair table (256 entries)
 constexpr int TC_SMEM = TC_NS * TC_STAGE + TC_XCH_BYTES + TC_NBAR * 8 + 16 + TC_TAB * 16 + 256 * 4;
@@ -57,6 +57,8 @@ constexpr long long TC_SPIN = 1LL << 22;
 constexpr int TC_SUSPEND_NS = 1000;
 
 static_assert(TC_STAGE % 1024 == 0, "stage alignment");
+static_assert((TC_NS * TC_STAGE + TC_XCH_BYTES + (TC_NBAR + 2) * 8) % 16 == 0, "int4 expert table alignment");
+static_assert(TC_SMEM <= 227 * 1024, "shared memory");
 
 __device__ __forceinline__ uint32_t s_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     uint32_t *stab = reinterpret_cast<uint32_t *>(tab + TC_TAB);   // [256] scale_h2 of each byte
     uint64_t *b_full = bars, *b_empty = bars + TC_NS;
     uint64_t *b_aready = bars + 2 * TC_NS, *b_afree = bars + 2 * TC_NS + TC_NA;
-    uint64_t *b_pfull = bars + 2 * TC_NS + 2 * TC_NA, *b_pfree = b_pfull + 2;
+    uint64_t *b_pfree = bars + 2 * TC_NS + 2 * TC_NA;   // partial buffers: epilogue -> MMA
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
@@ -218,7 +220,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
             bar_init(s_addr(&b_afree[a]), 2);                   // commits of the half's two issuers
         }
         for (int d = 0; d < 2; d++) {
-            bar_init(s_addr(&b_pfull[d]), TC_NMMA);             // MMA commits
             bar_init(s_addr(&b_pfree[d]), 4);                   // epilogue warps
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -348,8 +349,7 @@ _Pragma("unroll")
                         if (lo_any) mma_ts(dtm, atm + (uint32_t)(s16 * 8), sw128_desc(bl + boff), idesc, 1u);
                     }
                     mma_commit(s_addr(&b_afree[ab]));
-                    mma_commit(s_addr(&b_empty[st]));
-                    mma_commit(s_addr(&b_pfull[pb]));
+                    mma_commit(s_addr(&b_empty[st]));   // also tells the epilogue (no pfull commit)
                 }
             });
             if (failed) flag(DEV_TIMEOUT);
@@ -431,7 +431,10 @@ _Pragma("unroll")
             for (int n = 0; n < TC_N; n++) acc[n] = 0.0f;
             for (int kc = 0; kc < NK && !failed; kc++, item++) {
                 const int pb = item & 1;
-                if (!bar_wait(s_addr(&b_pfull[pb]), (uint32_t)((item >> 1) & 1))) { failed = true; break; }
+                // empty[st] completes once all four issuers' MMAs of the stage are done: the
+                // partials are final. (The MMAs run at most two stages ahead of this wait --
+                // they need pfree -- so the phase cannot be lapped.)
+                if (!bar_wait(s_addr(&b_empty[item % TC_NS]), (uint32_t)((item / TC_NS) & 1))) { failed = true; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 uint32_t d0[16], d1[16], d2[16], d3[16];
                 const uint32_t pt = tmem + lane_addr + (uint32_t)(pb * TC_PCOLS);
