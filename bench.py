@@ -471,12 +471,15 @@ def run_b200(args):
     hbm, peak_kind = peaks()
     achieved = gateup_bytes / (ph[2] * 1e-3) / 1e9
     expert_gbs = (gateup_bytes + down_bytes) / ((ph[2] + ph[3]) * 1e-3) / 1e9
+    # ncu DRAM bytes of the gate/up kernel over its algorithmic bytes, from a capture of a
+    # smaller case (profiles/), applied to this launch's algorithmic bytes
     traffic = None
     tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
     if os.path.exists(tp):
         try:
-            traffic = json.load(open(tp)).get("bytes_per_launch_scaled")
-        except (OSError, ValueError):
+            ratio = float(json.load(open(tp))["traffic_over_algorithmic"])
+            traffic = int(ratio * gateup_bytes)
+        except (OSError, ValueError, KeyError, TypeError):
             traffic = None
 
     # CPU baseline: the reference's kernels on a bounded sample of the same workload
@@ -507,7 +510,7 @@ def run_b200(args):
         "e2e": {"value": round(M / (e2e_ms * 1e-3), 3), "unit": "tok/s",
                 "h2d_bytes_per_step": int(x.numel() * 4),
                 "d2h_bytes_per_step": int(out.numel() * 4 + idx.numel() * 4), "ms_per_step": round(e2e_ms, 4)},
-        "roofline": {"bound": "hbm", "kernel": "moe_gateup_kernel", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<0> (gate/up)", "achieved": round(achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "traffic": traffic, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": int(gateup_bytes)},
