@@ -46,7 +46,10 @@ int k3gpu_last_cuda_error(void);
 /* Library version, major*10000 + minor*100 + patch. */
 int k3gpu_version(void);
 /* Read (host, synchronous on the given device's default stream) and clear the device
- * status word: 0 when no kernel has flagged an out-of-range index since the last call. */
+ * status word: 0 when no kernel has flagged an out-of-range index since the last call.
+ * Bits: 1 an index outside its range was skipped, 2 a count outside its range was
+ * clamped, 4 a cache position outside its range was skipped, 8 a bounded device wait
+ * ran out. */
 int k3gpu_device_status(int device, int *status_out);
 
 /* ------------------------------------------------------------------ router ---- */
@@ -277,6 +280,37 @@ int k3gpu_accept_tree_greedy(int *emit, int *n_emit, int *path, int *arg,
 int k3gpu_accept_sample(int *emit, int *n_emit, const float *logits, const int *drafts,
                         const int *nd_b, int B, int nd, int vocab, float temp,
                         uint64_t seed, uint64_t offset, void *stream);
+
+/* ------------------------------------------------------- trunk matmul ---------- */
+/* Workspace bytes for k3gpu_matmul_bf16_batch (independent of T beyond 256). */
+size_t k3gpu_matmul_bf16_workspace(int T, int in, int out);
+
+/* k3_matmul_bf16_batch_ld (src/core/k3_ops.c:953; the k3_mmw_batch_ld bf16 case,
+ * include/k3/k3.h:449-484) on tcgen05: Y[t*ldy + o] = sum_i W[o*in + i] * X[t*ldx + i]
+ * for t < T, o < out. W bf16 bits [out][in] (16-byte aligned, in % 8 == 0), X fp32, Y fp32;
+ * Y must not overlap X. The activations enter the tensor cores as two bf16 pieces
+ * (x = hi + lo to 2^-17), the products are exact and the sums fp32, so Y matches the
+ * reference's double sums to about 1e-5 relative, not bit for bit. */
+int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ldx, const uint16_t *W,
+                            int in, int out, int T, void *workspace, size_t ws_bytes,
+                            void *stream);
+
+/* ------------------------------------------------------- norms and AttnRes ------ */
+/* k3_rmsnorm (src/core/k3_ops.c:132-140) over T rows: x, y [T][n] (y may be x), w [n];
+ * double sum of squares, 1/sqrt(ss/n + eps) rounded to float, y = (w * x) * inv. */
+int k3gpu_rmsnorm(float *y, const float *x, const float *w, int T, int n, float eps,
+                  void *stream);
+
+/* k3_attn_res (src/core/k3_ops.c:1722-1753) for the T positions of a sweep, with the
+ * decoder layer's source stack (src/core/k3_ops.c:2514-2557) read in place: position t's
+ * sources are block_residual[t][0..n_blocks[t]) ([T][maxb][n]) and then cur[t] ([T][n]);
+ * fold [n] = norm weight * scoring projection; out [T][n]. n_blocks is a device array [T];
+ * a count outside 0..maxb is clamped and flagged (device status bit 2). maxb + 1 <= 256.
+ * The double sums run as block reductions, so results agree with the reference to an
+ * ulp of float. */
+int k3gpu_attn_res(float *out, const float *block_residual, const float *cur,
+                   const float *fold, const int *n_blocks, int T, int maxb, int n, float eps,
+                   void *stream);
 
 /* ---------------------------------------------------------------- drafter ------ */
 /* Host C (no GPU): the reference's n-gram drafter, spec_draft (src/cli/k3_run.c:450-491),

@@ -69,6 +69,10 @@ _SIGS = {
     "k3gpu_accept_greedy": ([VP, VP, VP, VP, VP, VP, I, I, I, VP], I),
     "k3gpu_accept_tree_greedy": ([VP] * 7 + [I, I, I, VP], I),
     "k3gpu_accept_sample": ([VP] * 5 + [I, I, I, F, U64, U64, VP], I),
+    "k3gpu_rmsnorm": ([VP, VP, VP, I, I, F, VP], I),
+    "k3gpu_matmul_bf16_workspace": ([I, I, I], SZ),
+    "k3gpu_matmul_bf16_batch": ([VP, I, VP, I, VP, I, I, I, VP, SZ, VP], I),
+    "k3gpu_attn_res": ([VP, VP, VP, VP, VP, I, I, I, F, VP], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
 }
 for _name, (_args, _res) in _SIGS.items():
@@ -283,6 +287,42 @@ def accept_tree_greedy(logits, tok, parent, stream=None):
                                        ptr(tok), ptr(parent), B, T, V, stream_ptr(stream)),
           "k3gpu_accept_tree_greedy")
     return emit, n_emit, path, arg
+
+
+# ------------------------------------------------------------ trunk matmul ---------
+def matmul_bf16(X, W, out=None, ws=None, stream=None):
+    """k3_matmul_bf16_batch: Y [T][out] = X [T][in] . W^T with W bf16 [out][in]
+    (torch.bfloat16 or int16/uint16 bit patterns). X and Y may be row slices of wider
+    tensors (their row strides are passed as ldx / ldy)."""
+    T, n_in = X.shape
+    n_out = W.shape[0]
+    Y = out if out is not None else torch.empty((T, n_out), dtype=torch.float32, device=X.device)
+    need = lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out)
+    ws = ws if ws is not None else workspace(need, X.device)
+    check(lib.k3gpu_matmul_bf16_batch(Y.data_ptr(), Y.stride(0), X.data_ptr(), X.stride(0), ptr(W), n_in,
+                                      n_out, T, ptr(ws), ws.numel(), stream_ptr(stream)),
+          "k3gpu_matmul_bf16_batch")
+    return Y
+
+
+# ----------------------------------------------------------------- norms ---------
+def rmsnorm(x, w, eps, out=None, stream=None):
+    """k3_rmsnorm over the rows of x [T][n]."""
+    T, n = x.shape
+    y = out if out is not None else torch.empty_like(x)
+    check(lib.k3gpu_rmsnorm(ptr(y), ptr(x), ptr(w), T, n, float(eps), stream_ptr(stream)), "k3gpu_rmsnorm")
+    return y
+
+
+def attn_res(block_residual, cur, fold, n_blocks, eps, stream=None):
+    """k3_attn_res per position: sources block_residual[t][:n_blocks[t]] then cur[t].
+    block_residual [T][maxb][n] (maxb may be 0: pass None), cur [T][n], n_blocks int32 [T]."""
+    T, n = cur.shape
+    maxb = 0 if block_residual is None else block_residual.shape[1]
+    out = torch.empty_like(cur)
+    check(lib.k3gpu_attn_res(ptr(out), ptr(block_residual), ptr(cur), ptr(fold), ptr(n_blocks), T,
+                             maxb, n, float(eps), stream_ptr(stream)), "k3gpu_attn_res")
+    return out
 
 
 def accept_sample(logits, drafts, temp, seed, offset=0, nd_b=None, stream=None):

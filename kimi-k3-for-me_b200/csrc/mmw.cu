@@ -1,0 +1,411 @@
+// mmw.cu -- the bf16 trunk matmul of a verify sweep on tcgen05:
+//   Y[t][o] = sum_i W[o][i] * X[t][i],  W bf16 [out][in], X fp32 [T][in], Y fp32 [T][out]
+// (k3_matmul_bf16_batch_ld, src/core/k3_ops.c:953, tiles :700-937; the reference takes each
+// product in double and its sums in a fixed 16-accumulator order).
+//
+// The activations are split exactly enough into two bf16 pieces, hi = bf16(x) and
+// lo = bf16(x - hi) (x = hi + lo to 2^-17 relative; only hi when x is already bf16), and
+// the products W * piece are exact in the tensor core's fp32 accumulator. The sums run in
+// that accumulator over the K range of a unit, so results agree with the reference's
+// double sums to about 1e-5 relative (the sweep's logits tolerance is 1e-3 rel-L2).
+//
+// A verify sweep has T <= 256 positions: every output row block is a weight stream. One
+// persistent CTA per SM walks units (128 output rows, one K split), 7 warps:
+//   warp 0     TMA: a 64-K stage = one 128-byte-swizzled box of 128 weight rows (16 KB)
+//              and one box per activation piece (Np rows, Np = T rounded up to 16)
+//   warps 1-2  MMA issuers: issuer i owns K16 steps 2i, 2i+1 of every stage and its own
+//              fp32 accumulator in TMEM (two issuers: one thread issues an MMA about every
+//              55-75 clocks); tcgen05.mma kind::f16 with bf16 A and B from shared memory
+//   warps 3-6  epilogue: tcgen05.ld of both accumulators at the end of a unit, summed,
+//              written to Y (one split) or to a split partial that a second kernel sums in
+//              split order.
+// Every wait is bounded; TMEM is freed on every exit path. No TMA multicast.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace k3 {
+namespace mmw {
+
+constexpr int THREADS = 7 * 32;
+constexpr int KB = 64;                    // K per stage: one 128-byte swizzled box row
+constexpr int W_BYTES = 128 * 128;        // 128 weight rows x 128 bytes
+constexpr int MAX_NS = 4;
+constexpr int MAX_NP = 256;               // positions per pass (MMA N <= 256)
+constexpr int MAX_SPLIT = 8;
+constexpr long long SPIN = 1LL << 22;
+constexpr int SUSPEND_NS = 1000;
+
+__device__ __forceinline__ uint32_t s_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bar_init(uint32_t b, uint32_t n)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint32_t b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint32_t b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+}
+// bounded: each try may suspend the warp until the phase completes or SUSPEND_NS pass
+__device__ __forceinline__ bool bar_wait(uint32_t b, uint32_t parity)
+{
+    for (long long i = 0; i < SPIN; i++) {
+        uint32_t ok;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                     " selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(ok)
+                     : "r"(b), "r"(parity), "n"(SUSPEND_NS)
+                     : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap *m, int x, int y, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+// K-major, 128-byte swizzle shared-memory descriptor: start, LBO 16 B (unused), SBO 1024 B
+// between 8-row groups, version 1, layout SWIZZLE_128B
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// kind::f16 instruction descriptor: D f32, A bf16, B bf16, both K-major, N, M = 128
+__host__ __device__ constexpr uint32_t bf16_idesc(int N)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (8u << 24);
+}
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+struct Args {
+    float *Y;            // [T][ldy] (one split) or nullptr
+    float *part;         // [nsplit][T][out] split partials, or nullptr
+    const int *lo_flag;  // 1 when some activation needs its lo piece
+    int T, Np, in, out, ldy;
+    int nsplit, kst;     // K splits; 64-K stages per split
+    int n_units, NS, stage_bytes;
+};
+
+__global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constant__ CUtensorMap wmap,
+                                                            const __grid_constant__ CUtensorMap xmap, Args a)
+{
+    extern __shared__ __align__(1024) unsigned char smem[];
+    if ((s_addr(smem) & 1023u) != 0u) {   // never expected: refuse rather than mis-swizzle
+        if (threadIdx.x == 0) flag(DEV_BAD_INDEX);
+        return;
+    }
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)a.NS * a.stage_bytes);
+    uint64_t *b_full = bars, *b_empty = bars + MAX_NS, *b_dfull = bars + 2 * MAX_NS, *b_dfree = b_dfull + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * MAX_NS + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < a.NS; s++) {
+            bar_init(s_addr(&b_full[s]), 1);
+            bar_init(s_addr(&b_empty[s]), 2);      // both issuers' commits
+        }
+        bar_init(s_addr(b_dfull), 2);              // both issuers, end of a unit
+        bar_init(s_addr(b_dfree), 4);              // the four epilogue warps
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {   // 512 columns: issuer i's accumulator at column 256 i
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    const int P = *a.lo_flag ? 2 : 1;            // activation pieces in use
+    const int nkb = (a.in + KB - 1) / KB;
+    bool failed = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+            int item = 0;
+            for (int u = blockIdx.x; u < a.n_units && !failed; u += gridDim.x) {
+                const int rb = u / a.nsplit, ks = u % a.nsplit;
+                const int kb1 = min(nkb, (ks + 1) * a.kst);
+                for (int kb = ks * a.kst; kb < kb1; kb++, item++) {
+                    const int st = item % a.NS;
+                    const uint32_t par = (uint32_t)((item / a.NS) & 1);
+                    if (!bar_wait(s_addr(&b_empty[st]), par ^ 1u)) { failed = true; break; }
+                    unsigned char *sw = smem + (size_t)st * a.stage_bytes;
+                    const uint32_t full = s_addr(&b_full[st]);
+                    bar_expect(full, (uint32_t)(W_BYTES + P * a.Np * 128));
+                    tma2d(s_addr(sw), &wmap, kb * KB, rb * 128, full);
+                    for (int p = 0; p < P; p++) tma2d(s_addr(sw + W_BYTES + p * a.Np * 128), &xmap, kb * KB, p * a.Np, full);
+                }
+            }
+            if (failed) flag(DEV_TIMEOUT);
+        }
+    } else if (warp <= 2) {
+        if (lane == 0) {
+            const int i = warp - 1;
+            const uint32_t idesc = bf16_idesc(a.Np);
+            const uint32_t dt = tmem + (uint32_t)(i * 256);
+            int item = 0, unit_i = 0;
+            for (int u = blockIdx.x; u < a.n_units && !failed; u += gridDim.x, unit_i++) {
+                const int ks = u % a.nsplit;
+                const int kb1 = min(nkb, (ks + 1) * a.kst);
+                // the epilogue has drained both accumulators of the previous unit
+                if (!bar_wait(s_addr(b_dfree), (uint32_t)((unit_i & 1) ^ 1))) { failed = true; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                uint32_t acc = 0;
+                for (int kb = ks * a.kst; kb < kb1; kb++, item++) {
+                    const int st = item % a.NS;
+                    const uint32_t par = (uint32_t)((item / a.NS) & 1);
+                    if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t sw = s_addr(smem + (size_t)st * a.stage_bytes);
+#pragma unroll
+                    for (int t = 2 * i; t < 2 * i + 2; t++) {
+                        const uint64_t ad = sw128_desc(sw + t * 32);
+                        for (int p = 0; p < P; p++) {
+                            mma_ss(dt, ad, sw128_desc(sw + W_BYTES + p * a.Np * 128 + t * 32), idesc, acc);
+                            acc = 1;
+                        }
+                    }
+                    mma_commit(s_addr(&b_empty[st]));
+                }
+                if (failed) break;
+                mma_commit(s_addr(b_dfull));
+            }
+            if (failed) flag(DEV_TIMEOUT);
+        }
+    } else {
+        const int q = warp & 3;                   // TMEM lane quarter of this warp
+        const int r = q * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        int unit_i = 0;
+        for (int u = blockIdx.x; u < a.n_units && !failed; u += gridDim.x, unit_i++) {
+            const int rb = u / a.nsplit, ks = u % a.nsplit;
+            const int row = rb * 128 + r;
+            if (!bar_wait(s_addr(b_dfull), (uint32_t)(unit_i & 1))) { failed = true; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            for (int c0 = 0; c0 < a.Np; c0 += 16) {
+                uint32_t v0[16], v1[16];
+                tmem_ld16(tmem + lane_addr + (uint32_t)c0, v0);
+                tmem_ld16(tmem + lane_addr + 256u + (uint32_t)c0, v1);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (row < a.out) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int t = c0 + j;
+                        if (t < a.T) {
+                            const float y = __fadd_rn(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
+                            if (a.part) a.part[((size_t)ks * a.T + t) * a.out + row] = y;
+                            else a.Y[(size_t)t * a.ldy + row] = y;
+                        }
+                    }
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) bar_arrive(s_addr(b_dfree));
+        }
+        if (failed && lane == 0) flag(DEV_TIMEOUT);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+// hi/lo bf16 pieces of X, [2][Np][in_pad], zero past T and past in; lo_flag |= any lo != 0
+__global__ void __launch_bounds__(256) split_kernel(__nv_bfloat16 *__restrict__ xp, int *__restrict__ lo_flag,
+                                                   const float *__restrict__ X, int ldx, int T, int Np,
+                                                   int in, int in_pad)
+{
+    const int t = blockIdx.y;
+    const int k = blockIdx.x * 256 + threadIdx.x;
+    if (k >= in_pad) return;
+    const float x = (t < T && k < in) ? X[(size_t)t * ldx + k] : 0.0f;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+    xp[(size_t)t * in_pad + k] = hi;
+    xp[((size_t)Np + t) * in_pad + k] = lo;
+    const int nz = __bfloat16_as_ushort(lo) & 0x7FFF;
+    if (__any_sync(0xffffffffu, nz != 0) && (threadIdx.x & 31) == 0) atomicOr(lo_flag, 1);
+}
+
+// Y[t][o] = sum over splits in order
+__global__ void __launch_bounds__(256) reduce_kernel(float *__restrict__ Y, const float *__restrict__ part,
+                                                    int T, int out, int ldy, int nsplit)
+{
+    const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+    if (i >= (long long)T * out) return;
+    const int t = (int)(i / out), o = (int)(i % out);
+    float y = part[i];
+    for (int s = 1; s < nsplit; s++) y = __fadd_rn(y, part[(size_t)s * T * out + i]);
+    Y[(size_t)t * ldy + o] = y;
+}
+
+// ---- host ----------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *q = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(q);
+    });
+    return fn;
+}
+
+static int bf16_map(CUtensorMap *m, const void *base, long long cols, long long rows, int box_rows)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return K3GPU_ECUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)KB, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        g_last_cuda_error = (int)r;
+        return K3GPU_ECUDA;
+    }
+    return K3GPU_OK;
+}
+
+struct Plan {
+    int Np, in_pad, nkb, nsplit, kst, rowblocks, n_units;
+    size_t xp_bytes, part_bytes;
+};
+
+static Plan plan(int Tc, int in, int out, int sms)
+{
+    Plan p;
+    p.Np = (Tc + 15) / 16 * 16;
+    p.in_pad = (in + KB - 1) / KB * KB;
+    p.nkb = p.in_pad / KB;
+    p.rowblocks = (out + 127) / 128;
+    int want = (2 * sms + p.rowblocks - 1) / p.rowblocks;      // about two units per SM
+    want = std::max(1, std::min(want, std::min(MAX_SPLIT, p.nkb / 4 > 0 ? p.nkb / 4 : 1)));
+    p.kst = (p.nkb + want - 1) / want;
+    p.nsplit = (p.nkb + p.kst - 1) / p.kst;                    // every split non-empty
+    p.n_units = p.rowblocks * p.nsplit;
+    p.xp_bytes = (size_t)2 * MAX_NP * p.in_pad * 2;
+    p.part_bytes = (size_t)MAX_SPLIT * MAX_NP * out * 4;
+    return p;
+}
+
+static int g_attr_dev = -1;
+static std::mutex g_attr_mu;
+
+}  // namespace mmw
+}  // namespace k3
+
+extern "C" size_t k3gpu_matmul_bf16_workspace(int T, int in, int out)
+{
+    if (T <= 0 || in <= 0 || out <= 0) return 0;
+    const k3::mmw::Plan p = k3::mmw::plan(std::min(T, k3::mmw::MAX_NP), in, out, 148);
+    return ((p.xp_bytes + 255) & ~(size_t)255) + ((p.part_bytes + 255) & ~(size_t)255) + 256;
+}
+
+extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ldx, const uint16_t *W, int in,
+                                       int out, int T, void *workspace, size_t ws_bytes, void *stream)
+{
+    using namespace k3::mmw;
+    if (!Y || !X || !W || !workspace || T <= 0 || in <= 0 || out <= 0) return K3GPU_EINVAL;
+    if (in % 8 || ldy < out || ldx < in || (reinterpret_cast<uintptr_t>(W) & 15u)) return K3GPU_EINVAL;
+    if (ws_bytes < k3gpu_matmul_bf16_workspace(T, in, out)) return K3GPU_ECAPACITY;
+    cudaStream_t s = k3::as_stream(stream);
+    int dev = 0, st = k3::cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    {
+        std::lock_guard<std::mutex> lock(g_attr_mu);
+        if (g_attr_dev != dev) {
+            st = k3::cuda_status(cudaFuncSetAttribute(mmw_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      220 * 1024));
+            if (st) return st;
+            g_attr_dev = dev;
+        }
+    }
+    const Plan full = plan(std::min(T, MAX_NP), in, out, sms);
+    char *ws = static_cast<char *>(workspace);
+    __nv_bfloat16 *xp = reinterpret_cast<__nv_bfloat16 *>(ws);
+    float *part = reinterpret_cast<float *>(ws + ((full.xp_bytes + 255) & ~(size_t)255));
+    int *lo_flag = reinterpret_cast<int *>(ws + ((full.xp_bytes + 255) & ~(size_t)255) +
+                                           ((full.part_bytes + 255) & ~(size_t)255));
+    CUtensorMap wm;
+    if ((st = bf16_map(&wm, W, in, out, 128))) return st;
+    for (int t0 = 0; t0 < T; t0 += MAX_NP) {           // passes of up to 256 positions
+        const int Tc = std::min(MAX_NP, T - t0);
+        const Plan p = plan(Tc, in, out, sms);
+        if ((st = k3::cuda_status(cudaMemsetAsync(lo_flag, 0, sizeof(int), s)))) return st;
+        split_kernel<<<dim3((p.in_pad + 255) / 256, p.Np), 256, 0, s>>>(xp, lo_flag, X + (size_t)t0 * ldx, ldx, Tc,
+                                                                         p.Np, in, p.in_pad);
+        if ((st = k3::launch_status())) return st;
+        CUtensorMap xm;
+        if ((st = bf16_map(&xm, xp, p.in_pad, 2LL * p.Np, p.Np))) return st;
+        Args a;
+        a.Y = p.nsplit == 1 ? Y + (size_t)t0 * ldy : nullptr;
+        a.part = p.nsplit == 1 ? nullptr : part;
+        a.lo_flag = lo_flag;
+        a.T = Tc; a.Np = p.Np; a.in = in; a.out = out; a.ldy = ldy;
+        a.nsplit = p.nsplit; a.kst = p.kst; a.n_units = p.n_units;
+        a.stage_bytes = W_BYTES + 2 * p.Np * 128;
+        a.NS = std::min(MAX_NS, (200 * 1024) / a.stage_bytes);
+        // at least 120 KB, so one CTA per SM: each allocates all 512 TMEM columns
+        const int smem = std::max(120 * 1024, a.NS * a.stage_bytes + (2 * MAX_NS + 2) * 8 + 16);
+        mmw_tc_kernel<<<std::min(p.n_units, sms), THREADS, smem, s>>>(wm, xm, a);
+        if ((st = k3::launch_status())) return st;
+        if (p.nsplit > 1) {
+            const long long n = (long long)Tc * out;
+            reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(Y + (size_t)t0 * ldy, part, Tc, out, ldy,
+                                                                      p.nsplit);
+            if ((st = k3::launch_status())) return st;
+        }
+    }
+    return K3GPU_OK;
+}

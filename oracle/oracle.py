@@ -109,8 +109,10 @@ def ref():
         lib.k3_rmsnorm.argtypes = [f32p, f32p, f32p, I, F]
         lib.k3_shortconv.argtypes = [f32p, f32p, f32p, C.c_void_p, I, I, I]
         lib.k3_kda_decay.argtypes = [f32p, f32p, f32p, f32p, f32p, I, I, F]
+        lib.k3_matmul_bf16_batch_ld.argtypes = [f32p, I, f32p, I, C.c_void_p, I, I, I]
         for n in ("k3_router", "k3_matmul_mxfp4", "k3_mxfp4_dequant", "k3_kda_step",
-                  "k3_situ_glu", "k3_rmsnorm", "k3_shortconv", "k3_kda_decay"):
+                  "k3_situ_glu", "k3_rmsnorm", "k3_shortconv", "k3_kda_decay",
+                  "k3_matmul_bf16_batch_ld"):
             getattr(lib, n).restype = None
         _ref = lib
     return _ref
@@ -272,6 +274,25 @@ def rmsnorm(x, w, eps):
         orc().orc_rmsnorm(out, np.ascontiguousarray(flat[r]), _f(w), flat.shape[1], float(eps))
         yf[r] = out
     return y
+
+
+def matmul_bf16_ref(X, Wbits):
+    """The reference's own k3_matmul_bf16_batch_ld (oracle/_ref) on X [T][in] fp32 and
+    W bf16 bits [out][in] uint16, or None when oracle/_ref was not built."""
+    lib = ref()
+    if lib is None:
+        return None
+    X = _f(X)
+    Wb = np.ascontiguousarray(Wbits, np.uint16)
+    T, n_in = X.shape
+    n_out = Wb.shape[0]
+    Y = np.empty((T, n_out), np.float32)
+    lib.k3_matmul_bf16_batch_ld(Y, n_out, X, n_in, Wb.ctypes.data_as(C.c_void_p), n_in, n_out, T)
+    return Y
+
+
+def bf16_bits_to_f32(Wbits):
+    return (np.asarray(Wbits, np.uint32) << 16).view(np.float32)
 
 
 def matmul_d(x, W):
