@@ -312,6 +312,75 @@ int k3gpu_attn_res(float *out, const float *block_residual, const float *cur,
                    const float *fold, const int *n_blocks, int T, int maxb, int n, float eps,
                    void *stream);
 
+/* ------------------------------------------------------------ decoder layer ------ */
+/* The configuration a layer needs (the K3Cfg fields it reads, include/k3/k3.h). */
+typedef struct {
+    int hidden;          /* E */
+    int kda_heads;       /* H */
+    int kda_head_dim;    /* D */
+    int conv_k;          /* ShortConv width, 2..8 */
+    float gate_lb;       /* KDA decay lower bound */
+    float rms_eps;
+    int attn_res_block;  /* a layer with layer_idx % attn_res_block == 0 snapshots */
+    int max_blocks;      /* maxb: the block_residual stride */
+    int n_routed, n_shared, topk, moe_inter, act, renorm;
+    float routed_scale, situ_b1, situ_b2;
+} K3GpuLayerCfg;
+
+/* KDA weights (K3KdaW, include/k3/k3.h): projections bf16 [out][in]; q, k, v, g: [P][E];
+ * b: [H][E]; f_a: [D][E]; f_b: [P][D]; o: [E][P] (P = H*D). q_conv, k_conv, v_conv
+ * [P][K]; A_log [H]; dt_bias [P]; o_norm [D]. All device pointers. */
+typedef struct {
+    const uint16_t *q, *k, *v, *b, *f_a, *f_b, *g, *o;
+    const float *q_conv, *k_conv, *v_conv, *A_log, *dt_bias, *o_norm;
+} K3GpuKdaW;
+
+/* The log of a tentative KDA sweep (K3KdaLog, include/k3/k3.h:716-732, as arrays): the
+ * layer writes the recurrence operands k, v, alpha [B][T][P], beta [B][T][H] and the
+ * pre-conv rows pre [B][T][3][P]; k3gpu_kda_commit / k3gpu_kda_commit_conv replay them. */
+typedef struct {
+    float *k, *v, *alpha, *beta, *pre;
+} K3GpuKdaLog;
+
+/* A KDA + MoE decoder layer (K3LayerW): the AttnRes folds [E] (norm weight times
+ * scoring projection, folded at load as the reference does per call,
+ * src/core/k3_ops.c:2504-2507), the input and post norms [E], the KDA weights, and the
+ * MoE in its single-layer form (router gate_W [n_routed][E], gate_bias [n_routed]; the
+ * expert bank at L = E, I = moe_inter, routed then shared). */
+typedef struct {
+    const float *attn_res_fold, *mlp_res_fold, *in_norm, *post_norm;
+    K3GpuKdaW kda;
+    const float *gate_W, *gate_bias;
+    const K3GpuExpertBank *bank;
+} K3GpuKdaLayerW;
+
+size_t k3gpu_kda_layer_workspace(const K3GpuLayerCfg *c, int B, int T);
+
+/* k3_kda_layer_log (src/core/k3_ops.c:2231-2385) for B sequences of T positions:
+ * x [B*T][E] -> out [B*T][E]. state [B][H][D][D] and conv_hist [B][3][P][K-1] are the
+ * carried state, read only (the sweep is tentative); the log receives the operands a
+ * commit replays. Projections run on k3gpu_matmul_bf16_batch (agreement ~1e-5 relative);
+ * the recurrence is bit-identical to the reference's kernel on the same operands. */
+int k3gpu_kda_layer_verify(float *out, const float *x, const K3GpuKdaW *w,
+                           const K3GpuLayerCfg *c, const float *state, const float *conv_hist,
+                           const K3GpuKdaLog *log, int B, int T, void *workspace,
+                           size_t ws_bytes, void *stream);
+
+size_t k3gpu_decoder_layer_workspace(const K3GpuLayerCfg *c, int B, int T);
+
+/* k3_decoder_layer_inc_log (src/core/k3_ops.c:2594-2602 -> core :2485-2592) for a KDA +
+ * MoE layer over B sequences of T positions, in place on h [B*T][E]: AttnRes before
+ * attention over block_residual [B*T][max_blocks][E] with per-position counts n_blocks
+ * [B*T] (device); on a block-boundary layer the running residual is snapshotted and
+ * n_blocks incremented on the device; input RMSNorm, the KDA layer (tentative, logged),
+ * AttnRes before the MLP, post RMSNorm, the MoE layer (moe_idx/moe_wt [B*T][topk]
+ * receive the routing), and the residual. */
+int k3gpu_decoder_layer_kda_verify(float *h, float *block_residual, int *n_blocks, int *moe_idx,
+                                   float *moe_wt, const K3GpuKdaLayerW *w,
+                                   const K3GpuLayerCfg *c, int layer_idx, const float *state,
+                                   const float *conv_hist, const K3GpuKdaLog *log, int B, int T,
+                                   void *workspace, size_t ws_bytes, void *stream);
+
 /* ---------------------------------------------------------------- drafter ------ */
 /* Host C (no GPU): the reference's n-gram drafter, spec_draft (src/cli/k3_run.c:450-491),
  * with the n range and cap as parameters (the reference fixes n = 4 then 3 and clamps

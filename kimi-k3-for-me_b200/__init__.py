@@ -40,6 +40,27 @@ class K3GpuExpertBank(C.Structure):
                 ("n_experts", I), ("L", I), ("I", I), ("f16_safe", VP), ("n_f16_unsafe", I)]
 
 
+class K3GpuLayerCfg(C.Structure):
+    _fields_ = [("hidden", I), ("kda_heads", I), ("kda_head_dim", I), ("conv_k", I), ("gate_lb", F),
+                ("rms_eps", F), ("attn_res_block", I), ("max_blocks", I), ("n_routed", I), ("n_shared", I),
+                ("topk", I), ("moe_inter", I), ("act", I), ("renorm", I), ("routed_scale", F), ("situ_b1", F),
+                ("situ_b2", F)]
+
+
+class K3GpuKdaW(C.Structure):
+    _fields_ = [(n, VP) for n in ("q", "k", "v", "b", "f_a", "f_b", "g", "o", "q_conv", "k_conv", "v_conv",
+                                  "A_log", "dt_bias", "o_norm")]
+
+
+class K3GpuKdaLog(C.Structure):
+    _fields_ = [(n, VP) for n in ("k", "v", "alpha", "beta", "pre")]
+
+
+class K3GpuKdaLayerW(C.Structure):
+    _fields_ = [("attn_res_fold", VP), ("mlp_res_fold", VP), ("in_norm", VP), ("post_norm", VP),
+                ("kda", K3GpuKdaW), ("gate_W", VP), ("gate_bias", VP), ("bank", C.POINTER(K3GpuExpertBank))]
+
+
 _SIGS = {
     "k3gpu_strerror": ([I], C.c_char_p),
     "k3gpu_last_cuda_error": ([], I),
@@ -73,6 +94,12 @@ _SIGS = {
     "k3gpu_matmul_bf16_workspace": ([I, I, I], SZ),
     "k3gpu_matmul_bf16_batch": ([VP, I, VP, I, VP, I, I, I, VP, SZ, VP], I),
     "k3gpu_attn_res": ([VP, VP, VP, VP, VP, I, I, I, F, VP], I),
+    "k3gpu_kda_layer_workspace": ([C.POINTER(K3GpuLayerCfg), I, I], SZ),
+    "k3gpu_kda_layer_verify": ([VP, VP, C.POINTER(K3GpuKdaW), C.POINTER(K3GpuLayerCfg), VP, VP,
+                                C.POINTER(K3GpuKdaLog), I, I, VP, SZ, VP], I),
+    "k3gpu_decoder_layer_workspace": ([C.POINTER(K3GpuLayerCfg), I, I], SZ),
+    "k3gpu_decoder_layer_kda_verify": ([VP, VP, VP, VP, VP, C.POINTER(K3GpuKdaLayerW), C.POINTER(K3GpuLayerCfg), I,
+                                        VP, VP, C.POINTER(K3GpuKdaLog), I, I, VP, SZ, VP], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
 }
 for _name, (_args, _res) in _SIGS.items():
@@ -303,6 +330,65 @@ def matmul_bf16(X, W, out=None, ws=None, stream=None):
                                       n_out, T, ptr(ws), ws.numel(), stream_ptr(stream)),
           "k3gpu_matmul_bf16_batch")
     return Y
+
+
+# ------------------------------------------------------------- decoder layer -------
+def layer_cfg(**kw) -> K3GpuLayerCfg:
+    c = K3GpuLayerCfg()
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def kda_weights(w: dict) -> K3GpuKdaW:
+    """w: q, k, v, b, f_a, f_b, g, o (bf16 bit tensors [out][in]), q_conv, k_conv, v_conv,
+    A_log, dt_bias, o_norm (fp32) -- CUDA tensors, kept alive by the caller."""
+    kw = K3GpuKdaW()
+    for n, _ in K3GpuKdaW._fields_:
+        setattr(kw, n, ptr(w[n]))
+    return kw
+
+
+def kda_log(B, T, H, D, device="cuda"):
+    P = H * D
+    z = lambda *s: torch.empty(s, dtype=torch.float32, device=device)
+    t = {"k": z(B, T, P), "v": z(B, T, P), "alpha": z(B, T, P), "beta": z(B, T, H), "pre": z(B, T, 3, P)}
+    lg = K3GpuKdaLog(*(ptr(t[n]) for n, _ in K3GpuKdaLog._fields_))
+    return lg, t
+
+
+def kda_layer_verify(x, w: dict, cfg: K3GpuLayerCfg, state, conv_hist, B, T, stream=None):
+    """k3_kda_layer_log for B sequences: x [B*T][E] -> (out [B*T][E], log tensors)."""
+    out = torch.empty_like(x)
+    kw = kda_weights(w)
+    lg, lt = kda_log(B, T, cfg.kda_heads, cfg.kda_head_dim, x.device)
+    ws = workspace(lib.k3gpu_kda_layer_workspace(C.byref(cfg), B, T), x.device)
+    check(lib.k3gpu_kda_layer_verify(ptr(out), ptr(x), C.byref(kw), C.byref(cfg), ptr(state), ptr(conv_hist),
+                                     C.byref(lg), B, T, ptr(ws), ws.numel(), stream_ptr(stream)),
+          "k3gpu_kda_layer_verify")
+    return out, lt
+
+
+def decoder_layer_kda_verify(h, block_residual, n_blocks, w: dict, bank: "ExpertBank", cfg: K3GpuLayerCfg,
+                             layer_idx, state, conv_hist, B, T, stream=None):
+    """k3_decoder_layer_inc_log for a KDA + MoE layer, in place on h [B*T][E];
+    block_residual [B*T][maxb][E] and n_blocks int32 [B*T] are updated on a boundary layer.
+    Returns (moe idx, moe wt, log tensors)."""
+    lw = K3GpuKdaLayerW()
+    for n in ("attn_res_fold", "mlp_res_fold", "in_norm", "post_norm", "gate_W", "gate_bias"):
+        setattr(lw, n, ptr(w[n]))
+    lw.kda = kda_weights(w)
+    lw.bank = C.pointer(bank.desc)
+    R = B * T
+    idx = torch.empty((R, cfg.topk), dtype=torch.int32, device=h.device)
+    wt = torch.empty((R, cfg.topk), dtype=torch.float32, device=h.device)
+    lg, lt = kda_log(B, T, cfg.kda_heads, cfg.kda_head_dim, h.device)
+    ws = workspace(lib.k3gpu_decoder_layer_workspace(C.byref(cfg), B, T), h.device)
+    check(lib.k3gpu_decoder_layer_kda_verify(ptr(h), ptr(block_residual), ptr(n_blocks), ptr(idx), ptr(wt),
+                                             C.byref(lw), C.byref(cfg), layer_idx, ptr(state), ptr(conv_hist),
+                                             C.byref(lg), B, T, ptr(ws), ws.numel(), stream_ptr(stream)),
+          "k3gpu_decoder_layer_kda_verify")
+    return idx, wt, lt
 
 
 # ----------------------------------------------------------------- norms ---------

@@ -1,0 +1,169 @@
+"""The KDA layer and the KDA + MoE decoder layer (k3gpu_kda_layer_verify,
+k3gpu_decoder_layer_kda_verify) against an oracle composition.
+
+The oracle side composes the pinned restatements in the reference's order
+(k3_kda_layer_log, src/core/k3_ops.c:2231-2385; k3_decoder_layer_core, :2485-2592):
+projections as double matmuls of the same bf16 weights (k3_matmul_bf16_batch's contract),
+orc_kda_prologue, orc_kda_verify, orc_kda_norm_gate, orc_attn_res, orc_rmsnorm, the router
+and the MoE. The device projections agree with double sums to ~1e-5 relative, so the bar
+is rel-L2 <= 1e-4 on layer outputs and log operands (the sweep's logits tolerance is
+1e-3, the KDA state's 1e-4); the routing is checked for identity.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(HERE))
+from k3lib import load  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+E, H, D, K = 512, 4, 64, 4
+P = H * D
+LB, EPS = -5.0, 1e-5
+
+
+@pytest.fixture(scope="module")
+def k3():
+    return load()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def rel(got, ref):
+    return float(np.linalg.norm(np.asarray(got, np.float64) - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+def bf16_bits(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def kda_weights(rng):
+    w = {}
+    for n, shape, sd in (("q", (P, E), 0.05), ("k", (P, E), 0.05), ("v", (P, E), 0.05), ("b", (H, E), 0.05),
+                         ("f_a", (D, E), 0.05), ("f_b", (P, D), 0.1), ("g", (P, E), 0.05), ("o", (E, P), 0.05)):
+        w[n] = bf16_bits(rng.standard_normal(shape, dtype=np.float32) * np.float32(sd))
+    for n in ("q_conv", "k_conv", "v_conv"):
+        w[n] = rng.standard_normal((P, K), dtype=np.float32) * np.float32(0.4)
+    w["A_log"] = np.linspace(-0.4, 1.2, H).astype(np.float32)
+    w["dt_bias"] = rng.standard_normal(P, dtype=np.float32) * np.float32(0.5)
+    w["o_norm"] = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    return w
+
+
+def to_dev(w):
+    return {n: (dev(a.view(np.int16)) if a.dtype == np.uint16 else dev(a)) for n, a in w.items()}
+
+
+def mmd(x, wbits):
+    return O.matmul_d(x, O.bf16_bits_to_f32(wbits))
+
+
+def oracle_kda_layer(x, w, state, hist):
+    """One sequence: x [T][E] -> out [T][E], log (k, v, alpha, beta)."""
+    T = x.shape[0]
+    q, k, v = mmd(x, w["q"]), mmd(x, w["k"]), mmd(x, w["v"])
+    bt = mmd(x, w["b"])
+    z = mmd(mmd(x, w["f_a"]), w["f_b"])
+    al, be = np.zeros((T, P), np.float32), np.zeros((T, H), np.float32)
+    h = np.ascontiguousarray(hist.copy())
+    O.orc().orc_kda_prologue(q, k, v, al, be, z, bt, w["q_conv"], w["k_conv"], w["v_conv"], h.ctypes.data,
+                             w["A_log"], w["dt_bias"], T, H, D, K, LB)
+    hd = lambda a: np.ascontiguousarray(a.reshape(T, H, D))
+    o = O.kda_verify(state, hd(q), hd(k), hd(v), hd(al), be, np.float32(1.0) / np.sqrt(np.float32(D)))
+    o = np.ascontiguousarray(o.reshape(T, P))
+    g = mmd(x, w["g"])
+    O.orc().orc_kda_norm_gate(o, g, w["o_norm"], T, H, D, EPS)
+    return mmd(o, w["o"]), (k, v, al, be)
+
+
+def cfg(k3, **kw):
+    base = dict(hidden=E, kda_heads=H, kda_head_dim=D, conv_k=K, gate_lb=LB, rms_eps=EPS, attn_res_block=2,
+                max_blocks=4, n_routed=16, n_shared=1, topk=2, moe_inter=256, act=k3.ACT_SWIGLU, renorm=1,
+                routed_scale=1.0, situ_b1=4.0, situ_b2=25.0)
+    base.update(kw)
+    return k3.layer_cfg(**base)
+
+
+def test_kda_layer_verify_vs_oracle(k3):
+    B, T = 2, 5
+    rng = np.random.default_rng(11)
+    w = kda_weights(rng)
+    x = rng.standard_normal((B * T, E), dtype=np.float32)
+    state = rng.standard_normal((B, H, D, D), dtype=np.float32) * np.float32(0.1)
+    hist = rng.standard_normal((B, 3, P, K - 1), dtype=np.float32)
+    wd = to_dev(w)
+    out, lt = k3.kda_layer_verify(dev(x), wd, cfg(k3), dev(state), dev(hist), B, T)
+    got = out.cpu().numpy()
+    for b in range(B):
+        ref, (k, v, al, be) = oracle_kda_layer(x[b * T:(b + 1) * T], w, state[b], hist[b])
+        assert rel(got[b * T:(b + 1) * T], ref) < 1e-4
+        assert rel(lt["k"].cpu().numpy()[b], k) < 1e-4
+        assert rel(lt["v"].cpu().numpy()[b], v) < 1e-4
+        assert rel(lt["alpha"].cpu().numpy()[b], al) < 1e-4
+        assert rel(lt["beta"].cpu().numpy()[b], be) < 1e-4
+
+
+@pytest.mark.parametrize("layer_idx", [2, 3], ids=["boundary", "inner"])
+def test_decoder_layer_kda_verify_vs_oracle(k3, layer_idx):
+    B, T, maxb = 2, 4, 4
+    R = B * T
+    c = cfg(k3)
+    rng = np.random.default_rng(20 + layer_idx)
+    w = kda_weights(rng)
+    for n in ("attn_res_fold", "mlp_res_fold"):
+        w[n] = rng.standard_normal(E, dtype=np.float32) * np.float32(0.05)
+    for n in ("in_norm", "post_norm"):
+        w[n] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+    w["gate_W"] = rng.standard_normal((c.n_routed, E), dtype=np.float32) * np.float32(0.2)
+    w["gate_bias"] = rng.standard_normal(c.n_routed, dtype=np.float32) * np.float32(0.01)
+    bank, lay = O.make_bank(rng, c.n_routed + c.n_shared, E, c.moe_inter, std=0.05, w13_std=0.3)
+    h0 = rng.standard_normal((R, E), dtype=np.float32)
+    br0 = rng.standard_normal((R, maxb, E), dtype=np.float32)
+    nb0 = np.array([0, 1, 2, 3, 1, 2, 0, 3], np.int32)
+    state = rng.standard_normal((B, H, D, D), dtype=np.float32) * np.float32(0.1)
+    hist = rng.standard_normal((B, 3, P, K - 1), dtype=np.float32)
+
+    wd = to_dev(w)
+    kb = k3.ExpertBank(dev(bank), c.n_routed + c.n_shared, E, c.moe_inter)
+    h, br, nb = dev(h0), dev(br0), dev(nb0)
+    idx, wt, _ = k3.decoder_layer_kda_verify(h, br, nb, wd, kb, c, layer_idx, dev(state), dev(hist), B, T)
+
+    # the oracle composition of k3_decoder_layer_core
+    def attn_res(fold, brr, nbr, cur):
+        out = np.empty_like(cur)
+        for t in range(R):
+            src = np.ascontiguousarray(np.concatenate([brr[t, :nbr[t]], cur[t:t + 1]]))
+            O.orc().orc_attn_res(out[t], src, fold, src.shape[0], E, EPS)
+        return out
+
+    pref = h0.copy()
+    hh = attn_res(w["attn_res_fold"], br0, nb0, pref)
+    brr, nbr = br0.copy(), nb0.copy()
+    boundary = layer_idx % c.attn_res_block == 0
+    if boundary:
+        for t in range(R):
+            brr[t, nbr[t]] = pref[t]
+            nbr[t] += 1
+    hin = O.rmsnorm(hh, w["in_norm"], EPS)
+    tmp = np.concatenate([oracle_kda_layer(hin[b * T:(b + 1) * T], w, state[b], hist[b])[0] for b in range(B)])
+    pref = tmp if boundary else pref + tmp
+    hh = attn_res(w["mlp_res_fold"], brr, nbr, pref)
+    hin = O.rmsnorm(hh, w["post_norm"], EPS)
+    ri, rw = O.router(hin, w["gate_W"], w["gate_bias"], c.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    moe = O.moe_routed(hin, ri, rw, bank, lay, E, c.moe_inter, c.topk, c.n_routed, c.n_shared, c.act)
+    ref = pref + moe
+
+    assert rel(h.cpu().numpy(), ref) < 1e-4
+    np.testing.assert_array_equal(nb.cpu().numpy(), nbr)
+    np.testing.assert_array_equal(br.cpu().numpy(), brr)
