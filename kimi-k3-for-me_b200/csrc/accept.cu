@@ -11,7 +11,7 @@
 
 namespace k3 {
 
-constexpr int AM_THREADS = 256;
+constexpr int AM_THREADS = 1024;   // a verify sweep has few rows: wide CTAs, 16-byte loads
 
 __device__ __forceinline__ bool better(float ov, int oi, float bv, int bi)
 {
@@ -20,7 +20,10 @@ __device__ __forceinline__ bool better(float ov, int oi, float bv, int bi)
     return ov > bv || (ov == bv && oi < bi);
 }
 
-// grid (rows), block 256: arg[row] = argmax of logits[row][0..vocab)
+// grid (rows), block 1024: arg[row] = argmax of logits[row][0..vocab). Each thread scans
+// its elements in ascending order with strict '>', so within a thread the first index of
+// its maximum wins; across threads ties go to the smaller index -- together the first
+// index of the row maximum over non-NaN values, as the sequential scan finds it.
 __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(int *__restrict__ arg,
                                                             const float *__restrict__ logits,
                                                             int vocab)
@@ -31,9 +34,20 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(int *__restrict__ ar
     const float *l = logits + row * (size_t)vocab;
     float bv = -INFINITY;
     int bi = -1;
-    for (int i = threadIdx.x; i < vocab; i += AM_THREADS) {
-        const float x = l[i];
+    auto take = [&](float x, int i) {
         if (x == x && (bi < 0 || x > bv)) { bv = x; bi = i; }   // NaN never a candidate
+    };
+    if ((vocab & 3) == 0 && (reinterpret_cast<uintptr_t>(l) & 15u) == 0) {
+        const float4 *l4 = reinterpret_cast<const float4 *>(l);
+        for (int j = threadIdx.x; j < vocab / 4; j += AM_THREADS) {
+            const float4 x = __ldg(l4 + j);
+            take(x.x, 4 * j);
+            take(x.y, 4 * j + 1);
+            take(x.z, 4 * j + 2);
+            take(x.w, 4 * j + 3);
+        }
+    } else {
+        for (int i = threadIdx.x; i < vocab; i += AM_THREADS) take(l[i], i);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -43,15 +57,21 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(int *__restrict__ ar
     }
     if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float v = sv[0];
-        int b = si[0];
-        for (int w = 1; w < AM_THREADS / 32; w++)
-            if (better(sv[w], si[w], v, b)) { v = sv[w]; b = si[w]; }
-        // the sequential scan keeps index 0 if l[0] is NaN (no value compares greater)
-        // and when every value is NaN
-        if (l[0] != l[0] || b < 0) b = 0;
-        arg[row] = b;
+    if (threadIdx.x < 32) {
+        float v = sv[threadIdx.x];
+        int b = si[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, b, o);
+            if (better(ov, oi, v, b)) { v = ov; b = oi; }
+        }
+        if (threadIdx.x == 0) {
+            // the sequential scan keeps index 0 if l[0] is NaN (no value compares greater)
+            // and when every value is NaN
+            if (l[0] != l[0] || b < 0) b = 0;
+            arg[row] = b;
+        }
     }
 }
 
