@@ -312,6 +312,35 @@ int k3gpu_attn_res(float *out, const float *block_residual, const float *cur,
                    const float *fold, const int *n_blocks, int T, int maxb, int n, float eps,
                    void *stream);
 
+/* ------------------------------------------------------------ K3 MoE (latent) ---- */
+/* The K3 MoE block (k3_moe_prefill, src/core/k3_ops.c:2008-2053 with moe_shared
+ * :1848-1860): routing on the full-width x, the routed MXFP4 experts on the latent
+ * down-projection z, their top-k-ordered sum RMS-normalised over the latent, the
+ * up-projection, plus the dense bf16 shared expert on x. */
+typedef struct {
+    int hidden, latent, moe_inter;   /* E, L, I (routed experts: L -> I -> L) */
+    int shared_inter;                /* SI = moe_inter * n_shared; 0 = no shared expert */
+    int n_routed, topk, act, renorm;
+    float routed_scale, situ_b1, situ_b2, rms_eps;
+} K3GpuMoeCfg;
+
+/* bf16 [out][in]: down [L][E], up [E][L], sh1, sh3 [SI][E], sh2 [E][SI]; gate_W
+ * [n_routed][E] fp32 and gate_bias [n_routed]; latent_norm [L] or NULL; the routed
+ * experts' bank at L, I (n_experts == n_routed). */
+typedef struct {
+    const uint16_t *down, *up, *sh1, *sh3, *sh2;
+    const float *gate_W, *gate_bias, *latent_norm;
+    const K3GpuExpertBank *bank;
+} K3GpuMoeW;
+
+size_t k3gpu_moe_prefill_workspace(const K3GpuMoeCfg *c, int T);
+
+/* out [T][E] = up(RMSNorm(sum_j wt_j expert_j(down(x)))) + sh2(act(sh1 x, sh3 x)) for
+ * x [T][E]; idx/wt [T][topk] receive the routing (indices bit-exact). */
+int k3gpu_moe_prefill(float *out, int *idx, float *wt, const float *x, const K3GpuMoeW *w,
+                      const K3GpuMoeCfg *c, int T, void *workspace, size_t ws_bytes,
+                      void *stream);
+
 /* ------------------------------------------------------------ decoder layer ------ */
 /* The configuration a layer needs (the K3Cfg fields it reads, include/k3/k3.h). */
 typedef struct {
@@ -325,6 +354,7 @@ typedef struct {
     int max_blocks;      /* maxb: the block_residual stride */
     int n_routed, n_shared, topk, moe_inter, act, renorm;
     float routed_scale, situ_b1, situ_b2;
+    int latent, shared_inter;   /* the K3 MoE form (K3GpuKdaLayerW.moe): L and SI */
 } K3GpuLayerCfg;
 
 /* KDA weights (K3KdaW, include/k3/k3.h): projections bf16 [out][in]; q, k, v, g: [P][E];
@@ -346,12 +376,13 @@ typedef struct {
  * scoring projection, folded at load as the reference does per call,
  * src/core/k3_ops.c:2504-2507), the input and post norms [E], the KDA weights, and the
  * MoE in its single-layer form (router gate_W [n_routed][E], gate_bias [n_routed]; the
- * expert bank at L = E, I = moe_inter, routed then shared). */
+ * expert bank at L = E, I = moe_inter, routed then shared) or, with moe set, the K3 form. */
 typedef struct {
     const float *attn_res_fold, *mlp_res_fold, *in_norm, *post_norm;
     K3GpuKdaW kda;
     const float *gate_W, *gate_bias;
     const K3GpuExpertBank *bank;
+    const K3GpuMoeW *moe;   /* non-NULL: the K3 MoE form (latent, k3gpu_moe_prefill) instead */
 } K3GpuKdaLayerW;
 
 size_t k3gpu_kda_layer_workspace(const K3GpuLayerCfg *c, int B, int T);

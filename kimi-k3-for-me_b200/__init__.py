@@ -44,7 +44,17 @@ class K3GpuLayerCfg(C.Structure):
     _fields_ = [("hidden", I), ("kda_heads", I), ("kda_head_dim", I), ("conv_k", I), ("gate_lb", F),
                 ("rms_eps", F), ("attn_res_block", I), ("max_blocks", I), ("n_routed", I), ("n_shared", I),
                 ("topk", I), ("moe_inter", I), ("act", I), ("renorm", I), ("routed_scale", F), ("situ_b1", F),
-                ("situ_b2", F)]
+                ("situ_b2", F), ("latent", I), ("shared_inter", I)]
+
+
+class K3GpuMoeCfg(C.Structure):
+    _fields_ = [("hidden", I), ("latent", I), ("moe_inter", I), ("shared_inter", I), ("n_routed", I), ("topk", I),
+                ("act", I), ("renorm", I), ("routed_scale", F), ("situ_b1", F), ("situ_b2", F), ("rms_eps", F)]
+
+
+class K3GpuMoeW(C.Structure):
+    _fields_ = [(n, VP) for n in ("down", "up", "sh1", "sh3", "sh2", "gate_W", "gate_bias", "latent_norm")] + \
+               [("bank", C.POINTER(K3GpuExpertBank))]
 
 
 class K3GpuKdaW(C.Structure):
@@ -58,7 +68,8 @@ class K3GpuKdaLog(C.Structure):
 
 class K3GpuKdaLayerW(C.Structure):
     _fields_ = [("attn_res_fold", VP), ("mlp_res_fold", VP), ("in_norm", VP), ("post_norm", VP),
-                ("kda", K3GpuKdaW), ("gate_W", VP), ("gate_bias", VP), ("bank", C.POINTER(K3GpuExpertBank))]
+                ("kda", K3GpuKdaW), ("gate_W", VP), ("gate_bias", VP), ("bank", C.POINTER(K3GpuExpertBank)),
+                ("moe", C.POINTER(K3GpuMoeW))]
 
 
 _SIGS = {
@@ -94,6 +105,8 @@ _SIGS = {
     "k3gpu_matmul_bf16_workspace": ([I, I, I], SZ),
     "k3gpu_matmul_bf16_batch": ([VP, I, VP, I, VP, I, I, I, VP, SZ, VP], I),
     "k3gpu_attn_res": ([VP, VP, VP, VP, VP, I, I, I, F, VP], I),
+    "k3gpu_moe_prefill_workspace": ([C.POINTER(K3GpuMoeCfg), I], SZ),
+    "k3gpu_moe_prefill": ([VP, VP, VP, VP, C.POINTER(K3GpuMoeW), C.POINTER(K3GpuMoeCfg), I, VP, SZ, VP], I),
     "k3gpu_kda_layer_workspace": ([C.POINTER(K3GpuLayerCfg), I, I], SZ),
     "k3gpu_kda_layer_verify": ([VP, VP, C.POINTER(K3GpuKdaW), C.POINTER(K3GpuLayerCfg), VP, VP,
                                 C.POINTER(K3GpuKdaLog), I, I, VP, SZ, VP], I),
@@ -369,8 +382,31 @@ def kda_layer_verify(x, w: dict, cfg: K3GpuLayerCfg, state, conv_hist, B, T, str
     return out, lt
 
 
+def moe_weights(w: dict, bank: "ExpertBank") -> K3GpuMoeW:
+    """w: down, up, sh1, sh3, sh2 (bf16 bit tensors; the sh* may be absent), gate_W,
+    gate_bias, latent_norm (may be absent) -- CUDA tensors kept alive by the caller."""
+    mw = K3GpuMoeW()
+    for n in ("down", "up", "sh1", "sh3", "sh2", "gate_W", "gate_bias", "latent_norm"):
+        setattr(mw, n, ptr(w.get(n)))
+    mw.bank = C.pointer(bank.desc)
+    return mw
+
+
+def moe_prefill(x, w: dict, bank: "ExpertBank", cfg: K3GpuMoeCfg, stream=None):
+    """The K3 MoE block (k3_moe_prefill): x [T][E] -> (out [T][E], idx, wt)."""
+    T = x.shape[0]
+    out = torch.empty_like(x)
+    idx = torch.empty((T, cfg.topk), dtype=torch.int32, device=x.device)
+    wt = torch.empty((T, cfg.topk), dtype=torch.float32, device=x.device)
+    mw = moe_weights(w, bank)
+    ws = workspace(lib.k3gpu_moe_prefill_workspace(C.byref(cfg), T), x.device)
+    check(lib.k3gpu_moe_prefill(ptr(out), ptr(idx), ptr(wt), ptr(x), C.byref(mw), C.byref(cfg), T, ptr(ws),
+                                ws.numel(), stream_ptr(stream)), "k3gpu_moe_prefill")
+    return out, idx, wt
+
+
 def decoder_layer_kda_verify(h, block_residual, n_blocks, w: dict, bank: "ExpertBank", cfg: K3GpuLayerCfg,
-                             layer_idx, state, conv_hist, B, T, stream=None):
+                             layer_idx, state, conv_hist, B, T, moe: dict = None, stream=None):
     """k3_decoder_layer_inc_log for a KDA + MoE layer, in place on h [B*T][E];
     block_residual [B*T][maxb][E] and n_blocks int32 [B*T] are updated on a boundary layer.
     Returns (moe idx, moe wt, log tensors)."""
@@ -379,6 +415,9 @@ def decoder_layer_kda_verify(h, block_residual, n_blocks, w: dict, bank: "Expert
         setattr(lw, n, ptr(w[n]))
     lw.kda = kda_weights(w)
     lw.bank = C.pointer(bank.desc)
+    if moe is not None:                      # the K3 MoE form; `bank` then holds the latent experts
+        mw = moe_weights(moe, bank)
+        lw.moe = C.pointer(mw)
     R = B * T
     idx = torch.empty((R, cfg.topk), dtype=torch.int32, device=h.device)
     wt = torch.empty((R, cfg.topk), dtype=torch.float32, device=h.device)

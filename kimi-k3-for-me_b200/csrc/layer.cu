@@ -11,9 +11,13 @@
 // k3gpu_decoder_layer_kda_verify is k3_decoder_layer_core (src/core/k3_ops.c:2485-2592)
 // for that layer: AttnRes before attention over each position's block-residual snapshots,
 // the block-boundary snapshot (then the running residual restarts from the attention
-// output), input RMSNorm, the KDA layer, AttnRes before the MLP, post RMSNorm, the MoE
-// layer (single-layer form: experts at the hidden width), and the residual.
+// output), input RMSNorm, the KDA layer, AttnRes before the MLP, post RMSNorm, the MoE, and
+// the residual. The MoE is either the single-layer form (router and MXFP4 experts at the
+// hidden width, shared experts in the bank) or the K3 form of k3_moe_prefill
+// (src/core/k3_ops.c:2008-2053, 1848-1860): routing on x, the MXFP4 experts on the latent
+// down-projection, the latent RMSNorm, the up-projection, and the dense bf16 shared expert.
 #include "common.cuh"
+#include "moe.cuh"
 
 namespace k3 {
 
@@ -36,9 +40,8 @@ __global__ void __launch_bounds__(256) snapshot_kernel(float *__restrict__ block
     if (threadIdx.x == 0) n_blocks[t] = nb + 1;
 }
 
-// y = a + b in float
-__global__ void __launch_bounds__(256) add_kernel(float *__restrict__ y, const float *__restrict__ a,
-                                                  const float *__restrict__ b, long long n)
+// y = a + b in float (y may be a)
+__global__ void __launch_bounds__(256) add_kernel(float *y, const float *a, const float *b, long long n)
 {
     const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
     if (i < n) y[i] = __fadd_rn(a[i], b[i]);
@@ -48,6 +51,54 @@ static int add_launch(float *y, const float *a, const float *b, long long n, cud
 {
     add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, a, b, n);
     return launch_status();
+}
+
+// y = act(g, u) elementwise (the shared expert's [gate | up] -> act; y may be g)
+__global__ void __launch_bounds__(256) glu_kernel(float *y, const float *g, const float *u, long long n, int act,
+                                                  float b1, float b2)
+{
+    const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+    if (i < n) y[i] = act == K3GPU_ACT_SITU ? act_situ(g[i], u[i], b1, b2) : act_swiglu(g[i], u[i]);
+}
+
+struct MoeWs {
+    float *z, *acc, *g, *u, *d;
+    char *router, *experts, *mm;
+    size_t router_bytes, experts_bytes, mm_bytes;
+};
+
+static size_t moe_ws_layout(const K3GpuMoeCfg *c, int T, MoeWs *w, char *base)
+{
+    const int E = c->hidden, L = c->latent, SI = c->shared_inter;
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        char *r = base ? base + o : nullptr;
+        o += (bytes + 255) & ~(size_t)255;
+        return r;
+    };
+    MoeWs t;
+    t.z = (float *)take((size_t)T * L * 4);
+    t.acc = (float *)take((size_t)T * L * 4);
+    t.g = (float *)take((size_t)T * (SI > 0 ? SI : 1) * 4);
+    t.u = (float *)take((size_t)T * (SI > 0 ? SI : 1) * 4);
+    t.d = (float *)take((size_t)T * E * 4);
+    t.router_bytes = k3gpu_router_workspace(T, c->n_routed);
+    t.router = take(t.router_bytes);
+    t.experts_bytes = k3gpu_moe_workspace(T, c->topk, 0, L, c->moe_inter, c->n_routed);
+    t.experts = take(t.experts_bytes);
+    size_t mm = std::max(k3gpu_matmul_bf16_workspace(T, E, L), k3gpu_matmul_bf16_workspace(T, L, E));
+    if (SI > 0)
+        mm = std::max(mm, std::max(k3gpu_matmul_bf16_workspace(T, E, SI), k3gpu_matmul_bf16_workspace(T, SI, E)));
+    t.mm_bytes = mm;
+    t.mm = take(mm);
+    if (w) *w = t;
+    return o;
+}
+
+static bool moe_cfg_ok(const K3GpuMoeCfg *c)
+{
+    return c && c->hidden > 0 && c->latent > 0 && c->moe_inter > 0 && c->shared_inter >= 0 && c->n_routed > 0 &&
+           c->topk > 0 && c->topk <= c->n_routed;
 }
 
 struct KdaWs {
@@ -87,6 +138,55 @@ static bool cfg_ok(const K3GpuLayerCfg *c)
 }
 
 }  // namespace k3
+
+extern "C" size_t k3gpu_moe_prefill_workspace(const K3GpuMoeCfg *c, int T)
+{
+    if (!k3::moe_cfg_ok(c) || T <= 0) return 0;
+    return k3::moe_ws_layout(c, T, nullptr, nullptr);
+}
+
+extern "C" int k3gpu_moe_prefill(float *out, int *idx, float *wt, const float *x, const K3GpuMoeW *w,
+                                 const K3GpuMoeCfg *c, int T, void *workspace, size_t ws_bytes, void *stream)
+{
+    using namespace k3;
+    if (!out || !idx || !wt || !x || !w || !moe_cfg_ok(c) || !workspace || T <= 0) return K3GPU_EINVAL;
+    if (!w->down || !w->up || !w->gate_W || !w->bank) return K3GPU_EINVAL;
+    if (c->shared_inter > 0 && (!w->sh1 || !w->sh2 || !w->sh3)) return K3GPU_EINVAL;
+    if (w->bank->L != c->latent || w->bank->I != c->moe_inter || w->bank->n_experts != c->n_routed)
+        return K3GPU_EINVAL;
+    if (ws_bytes < k3gpu_moe_prefill_workspace(c, T)) return K3GPU_ECAPACITY;
+    const int E = c->hidden, L = c->latent, SI = c->shared_inter;
+    cudaStream_t s = as_stream(stream);
+    MoeWs m;
+    moe_ws_layout(c, T, &m, static_cast<char *>(workspace));
+    int st;
+    auto mm = [&](float *Y, const float *X, const uint16_t *W, int n_in, int n_out) {
+        return k3gpu_matmul_bf16_batch(Y, n_out, X, n_in, W, n_in, n_out, T, m.mm, m.mm_bytes, stream);
+    };
+    // 2. down-projection (routing reads x, not z, so the order changes nothing)
+    if ((st = mm(m.z, x, w->down, E, L))) return st;
+    // 1. route on the full-width x
+    if ((st = k3gpu_router(idx, wt, x, w->gate_W, w->gate_bias, T, E, c->n_routed, c->topk, c->renorm,
+                           c->routed_scale, m.router, m.router_bytes, stream)))
+        return st;
+    // 3, 4. the routed experts at the latent width, summed in top-k order, then the norm
+    if ((st = k3gpu_moe_experts(m.acc, m.z, idx, wt, w->bank, T, c->topk, c->n_routed, 0, c->act, c->situ_b1,
+                                c->situ_b2, w->latent_norm, c->rms_eps, m.experts, m.experts_bytes, stream)))
+        return st;
+    // 5. up-projection
+    if ((st = mm(out, m.acc, w->up, L, E))) return st;
+    // 6. the dense shared expert on x, added unweighted
+    if (SI > 0) {
+        if ((st = mm(m.g, x, w->sh1, E, SI))) return st;
+        if ((st = mm(m.u, x, w->sh3, E, SI))) return st;
+        const long long n = (long long)T * SI;
+        glu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m.g, m.g, m.u, n, c->act, c->situ_b1, c->situ_b2);
+        if ((st = launch_status())) return st;
+        if ((st = mm(m.d, m.g, w->sh2, SI, E))) return st;
+        if ((st = add_launch(out, out, m.d, (long long)T * E, s))) return st;
+    }
+    return K3GPU_OK;
+}
 
 extern "C" size_t k3gpu_kda_layer_workspace(const K3GpuLayerCfg *c, int B, int T)
 {
@@ -141,6 +241,15 @@ struct LayerWs {
     size_t kda_bytes, moe_bytes;
 };
 
+static K3GpuMoeCfg moe_cfg_of(const K3GpuLayerCfg *c)
+{
+    K3GpuMoeCfg m;
+    m.hidden = c->hidden; m.latent = c->latent; m.moe_inter = c->moe_inter; m.shared_inter = c->shared_inter;
+    m.n_routed = c->n_routed; m.topk = c->topk; m.act = c->act; m.renorm = c->renorm;
+    m.routed_scale = c->routed_scale; m.situ_b1 = c->situ_b1; m.situ_b2 = c->situ_b2; m.rms_eps = c->rms_eps;
+    return m;
+}
+
 static size_t layer_ws_layout(const K3GpuLayerCfg *c, int B, int T, LayerWs *w, char *base)
 {
     const int E = c->hidden, R = B * T;
@@ -157,6 +266,10 @@ static size_t layer_ws_layout(const K3GpuLayerCfg *c, int B, int T, LayerWs *w, 
     t.kda_bytes = k3gpu_kda_layer_workspace(c, B, T);
     t.kda = take(t.kda_bytes);
     t.moe_bytes = k3gpu_moe_workspace(R, c->topk, c->n_shared, E, c->moe_inter, c->n_routed);
+    if (c->latent > 0) {
+        const K3GpuMoeCfg mc = moe_cfg_of(c);
+        t.moe_bytes = std::max(t.moe_bytes, k3gpu_moe_prefill_workspace(&mc, R));
+    }
     t.moe = take(t.moe_bytes);
     if (w) *w = t;
     return o;
@@ -179,7 +292,8 @@ extern "C" int k3gpu_decoder_layer_kda_verify(float *h, float *block_residual, i
     if (!h || !block_residual || !n_blocks || !moe_idx || !moe_wt || !w || !cfg_ok(c) || !workspace)
         return K3GPU_EINVAL;
     if (B <= 0 || T <= 0 || layer_idx < 0 || c->attn_res_block <= 0 || c->max_blocks <= 0) return K3GPU_EINVAL;
-    if (!w->bank || w->bank->L != c->hidden || w->bank->I != c->moe_inter) return K3GPU_EINVAL;
+    if (!w->moe && (!w->bank || w->bank->L != c->hidden || w->bank->I != c->moe_inter)) return K3GPU_EINVAL;
+    if (w->moe && c->latent <= 0) return K3GPU_EINVAL;
     if (ws_bytes < k3gpu_decoder_layer_workspace(c, B, T)) return K3GPU_ECAPACITY;
     const int E = c->hidden, R = B * T, maxb = c->max_blocks;
     const long long n = (long long)R * E;
@@ -213,10 +327,16 @@ extern "C" int k3gpu_decoder_layer_kda_verify(float *h, float *block_residual, i
                              stream)))
         return st;
     if ((st = k3gpu_rmsnorm(ws.hin, h, w->post_norm, R, E, c->rms_eps, stream))) return st;
-    // the MoE (single-layer form: router and experts at the hidden width)
-    if ((st = k3gpu_moe_layer(ws.tmp, moe_idx, moe_wt, ws.hin, w->gate_W, w->gate_bias, w->bank, R, c->topk,
-                              c->n_routed, c->n_shared, c->act, c->situ_b1, c->situ_b2, c->renorm, c->routed_scale,
-                              ws.moe, ws.moe_bytes, stream)))
-        return st;
+    // the MoE: the K3 form (latent projections, dense shared expert) or the single-layer
+    // form (router and experts at the hidden width)
+    if (w->moe) {
+        const K3GpuMoeCfg mc = moe_cfg_of(c);
+        st = k3gpu_moe_prefill(ws.tmp, moe_idx, moe_wt, ws.hin, w->moe, &mc, R, ws.moe, ws.moe_bytes, stream);
+    } else {
+        st = k3gpu_moe_layer(ws.tmp, moe_idx, moe_wt, ws.hin, w->gate_W, w->gate_bias, w->bank, R, c->topk,
+                             c->n_routed, c->n_shared, c->act, c->situ_b1, c->situ_b2, c->renorm, c->routed_scale,
+                             ws.moe, ws.moe_bytes, stream);
+    }
+    if (st) return st;
     return add_launch(h, ws.pref, ws.tmp, n, s);
 }

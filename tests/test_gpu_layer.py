@@ -167,3 +167,94 @@ def test_decoder_layer_kda_verify_vs_oracle(k3, layer_idx):
     assert rel(h.cpu().numpy(), ref) < 1e-4
     np.testing.assert_array_equal(nb.cpu().numpy(), nbr)
     np.testing.assert_array_equal(br.cpu().numpy(), brr)
+
+
+def oracle_moe_k3(x, w, bank, lay, L, I, topk, n_routed, SI, act, eps=EPS):
+    """k3_moe_prefill composed from the oracle: route on x, experts on down(x) at L with
+    the latent norm, up-projection, plus the dense shared expert on x."""
+    z = mmd(x, w["down"])
+    ri, rw = O.router(x, w["gate_W"], w["gate_bias"], topk)
+    acc = O.moe_routed(z, ri, rw, bank, lay, L, I, topk, n_routed, 0, act, latent_norm=w.get("latent_norm"),
+                       eps=eps)
+    out = mmd(acc, w["up"])
+    if SI:
+        gu = np.ascontiguousarray(np.concatenate([mmd(x, w["sh1"]), mmd(x, w["sh3"])], axis=1))
+        a = np.empty((x.shape[0], SI), np.float32)
+        for t in range(x.shape[0]):
+            if act == 0:
+                O.orc().orc_situ_glu(a[t], np.ascontiguousarray(gu[t]), SI, 4.0, 25.0)
+            else:
+                O.orc().orc_swiglu(a[t], np.ascontiguousarray(gu[t]), SI)
+        out = out + mmd(a, w["sh2"])
+    return out, ri
+
+
+def k3_moe_weights(rng, E, L, SI, n_routed):
+    w = {"down": bf16_bits(rng.standard_normal((L, E), dtype=np.float32) * np.float32(0.05)),
+         "up": bf16_bits(rng.standard_normal((E, L), dtype=np.float32) * np.float32(0.05)),
+         "sh1": bf16_bits(rng.standard_normal((SI, E), dtype=np.float32) * np.float32(0.05)),
+         "sh3": bf16_bits(rng.standard_normal((SI, E), dtype=np.float32) * np.float32(0.05)),
+         "sh2": bf16_bits(rng.standard_normal((E, SI), dtype=np.float32) * np.float32(0.05)),
+         "gate_W": rng.standard_normal((n_routed, E), dtype=np.float32) * np.float32(0.2),
+         "gate_bias": rng.standard_normal(n_routed, dtype=np.float32) * np.float32(0.01),
+         "latent_norm": (1 + 0.1 * rng.standard_normal(L)).astype(np.float32)}
+    return w
+
+
+def test_moe_prefill_k3_form_vs_oracle(k3):
+    """E 1024, latent 512, FFN 512 (tensor-core experts), 8 experts top-2, a 512-wide
+    dense SiTU shared expert, 12 positions."""
+    E2, L, I, n_routed, topk, SI, T = 1024, 512, 512, 8, 2, 512, 12
+    rng = np.random.default_rng(31)
+    w = k3_moe_weights(rng, E2, L, SI, n_routed)
+    bank, lay = O.make_bank(rng, n_routed, L, I, std=0.05, w13_std=0.1)
+    x = rng.standard_normal((T, E2), dtype=np.float32)
+    c = k3.K3GpuMoeCfg(hidden=E2, latent=L, moe_inter=I, shared_inter=SI, n_routed=n_routed, topk=topk, act=0,
+                       renorm=1, routed_scale=1.0, situ_b1=4.0, situ_b2=25.0, rms_eps=EPS)
+    kb = k3.ExpertBank(dev(bank), n_routed, L, I)
+    kb.scan()
+    out, idx, _ = k3.moe_prefill(dev(x), to_dev(w), kb, c)
+    ref, ri = oracle_moe_k3(x, w, bank, lay, L, I, topk, n_routed, SI, 0)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    assert rel(out.cpu().numpy(), ref) < 1e-4
+
+
+def test_decoder_layer_with_k3_moe_form(k3):
+    B, T, maxb = 2, 3, 4
+    R = B * T
+    L, I, SI = 256, 256, 256
+    c = cfg(k3, latent=L, shared_inter=SI, moe_inter=I, n_routed=8, topk=2, act=0)
+    rng = np.random.default_rng(41)
+    w = kda_weights(rng)
+    for n in ("attn_res_fold", "mlp_res_fold"):
+        w[n] = rng.standard_normal(E, dtype=np.float32) * np.float32(0.05)
+    for n in ("in_norm", "post_norm"):
+        w[n] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+    m = k3_moe_weights(rng, E, L, SI, c.n_routed)
+    w["gate_W"], w["gate_bias"] = m["gate_W"], m["gate_bias"]
+    bank, lay = O.make_bank(rng, c.n_routed, L, I, std=0.05, w13_std=0.3)
+    h0 = rng.standard_normal((R, E), dtype=np.float32)
+    br0 = rng.standard_normal((R, maxb, E), dtype=np.float32)
+    nb0 = np.array([1, 0, 2, 3, 1, 2], np.int32)
+    state = rng.standard_normal((B, H, D, D), dtype=np.float32) * np.float32(0.1)
+    hist = rng.standard_normal((B, 3, P, K - 1), dtype=np.float32)
+    kb = k3.ExpertBank(dev(bank), c.n_routed, L, I)
+    h, br, nb = dev(h0), dev(br0), dev(nb0)
+    idx, _, _ = k3.decoder_layer_kda_verify(h, br, nb, to_dev(w), kb, c, 3, dev(state), dev(hist), B, T,
+                                            moe=to_dev(m))
+
+    def attn_res(fold, cur):
+        out = np.empty_like(cur)
+        for t in range(R):
+            src = np.ascontiguousarray(np.concatenate([br0[t, :nb0[t]], cur[t:t + 1]]))
+            O.orc().orc_attn_res(out[t], src, fold, src.shape[0], E, EPS)
+        return out
+
+    pref = h0.copy()                                   # layer 3: not a block boundary
+    hin = O.rmsnorm(attn_res(w["attn_res_fold"], pref), w["in_norm"], EPS)
+    pref = pref + np.concatenate([oracle_kda_layer(hin[b * T:(b + 1) * T], w, state[b], hist[b])[0]
+                                  for b in range(B)])
+    hin = O.rmsnorm(attn_res(w["mlp_res_fold"], pref), w["post_norm"], EPS)
+    moe, ri = oracle_moe_k3(hin, m, bank, lay, L, I, c.topk, c.n_routed, SI, 0)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    assert rel(h.cpu().numpy(), pref + moe) < 1e-4
