@@ -323,6 +323,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         if (lane == 0) {
             const int mi = warp - TC_MMA_WARP0, h = mi >> 1, j = mi & 1;
             const uint32_t idesc = f16_idesc(TC_N);
+            // this issuer's eight B offsets, in 16-byte descriptor units: the descriptor of a
+            // stage's tile is built once and advanced by these (the 14-bit start field does
+            // not carry: shared addresses stay below 256 KB)
+            uint32_t boff16[8];
+_Pragma("unroll")
+            for (int t = 0; t < 8; t++) {
+                const int kk = h * 256 + (j * 8 + t) * 16;
+                boff16[t] = (uint32_t)(((kk >> 6) * (TC_N * 128) + (kk & 63) * 2) >> 4);
+            }
             TC_FOR_UNITS({
                 for (int kc = 0; kc < NK && !failed; kc++, item++) {
                     const int st = item % TC_NS;
@@ -339,14 +348,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
                     const unsigned char *sw = smem + (size_t)st * TC_STAGE;
                     const uint32_t bh = s_addr(sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
                     const uint32_t bl = bh + TC_B_BYTES;
-                    const uint32_t atm = tmem + (uint32_t)(TC_ACOL0 + ab * 128);
+                    const uint32_t atm = tmem + (uint32_t)(TC_ACOL0 + ab * 128 + j * 64);
+                    const uint64_t dh = sw128_desc(bh), dl = sw128_desc(bl);
+                    if (!lo_any) {
 _Pragma("unroll")
-                    for (int t = 0; t < 8; t++) {                 // K16 steps of this quarter
-                        const int s16 = j * 8 + t;                // step within the half
-                        const int kk = h * 256 + s16 * 16;        // K offset in the stage
-                        const uint32_t boff = (uint32_t)((kk >> 6) * (TC_N * 128) + (kk & 63) * 2);
-                        mma_ts(dtm, atm + (uint32_t)(s16 * 8), sw128_desc(bh + boff), idesc, t ? 1u : 0u);
-                        if (lo_any) mma_ts(dtm, atm + (uint32_t)(s16 * 8), sw128_desc(bl + boff), idesc, 1u);
+                        for (int t = 0; t < 8; t++)               // K16 steps of this quarter
+                            mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
+                    } else {
+_Pragma("unroll")
+                        for (int t = 0; t < 8; t++) {
+                            mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
+                            mma_ts(dtm, atm + (uint32_t)(t * 8), dl + boff16[t], idesc, 1u);
+                        }
                     }
                     mma_commit(s_addr(&b_afree[ab]));
                     mma_commit(s_addr(&b_empty[st]));   // also tells the epilogue (no pfull commit)
