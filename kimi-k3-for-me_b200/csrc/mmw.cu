@@ -33,7 +33,7 @@ namespace mmw {
 constexpr int THREADS = 7 * 32;
 constexpr int KB = 64;                    // K per stage: one 128-byte swizzled box row
 constexpr int W_BYTES = 128 * 128;        // 128 weight rows x 128 bytes
-constexpr int MAX_NS = 4;
+constexpr int MAX_NS = 8;
 constexpr int MAX_NP = 256;               // positions per pass (MMA N <= 256)
 constexpr int MAX_SPLIT = 8;
 constexpr long long SPIN = 1LL << 22;
@@ -192,14 +192,16 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
                     const uint32_t par = (uint32_t)((item / a.NS) & 1);
                     if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t sw = s_addr(smem + (size_t)st * a.stage_bytes);
+                    // one descriptor per stage, advanced by 16-byte offsets (the 14-bit start
+                    // field does not carry: shared addresses stay below 256 KB)
+                    const uint64_t d0 = sw128_desc(s_addr(smem + (size_t)st * a.stage_bytes));
+                    const uint32_t b0 = W_BYTES >> 4, bp = (uint32_t)(a.Np * 128) >> 4;
 #pragma unroll
-                    for (int t = 2 * i; t < 2 * i + 2; t++) {
-                        const uint64_t ad = sw128_desc(sw + t * 32);
-                        for (int p = 0; p < P; p++) {
-                            mma_ss(dt, ad, sw128_desc(sw + W_BYTES + p * a.Np * 128 + t * 32), idesc, acc);
-                            acc = 1;
-                        }
+                    for (int u = 0; u < 2; u++) {
+                        const uint32_t tk = (uint32_t)((2 * i + u) * 32) >> 4;
+                        mma_ss(dt, d0 + tk, d0 + b0 + tk, idesc, acc);
+                        acc = 1;
+                        if (P == 2) mma_ss(dt, d0 + tk, d0 + b0 + bp + tk, idesc, 1u);
                     }
                     mma_commit(s_addr(&b_empty[st]));
                 }
