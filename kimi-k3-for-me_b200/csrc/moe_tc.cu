@@ -44,9 +44,19 @@ constexpr int TC_S_BYTES = 128 * 16;     // E8M0 bytes of a stage
 constexpr int TC_B_BYTES = (TC_KC / 64) * TC_N * 128;   // 16 KB: 8 atoms x 16 rows x 128 B
 constexpr int TC_STAGE = TC_W_BYTES + TC_S_BYTES + 2 * TC_B_BYTES + 1024 - TC_S_BYTES % 1024;
 constexpr int TC_NS = 3;
-constexpr int TC_NA = 3;                 // TMEM A buffers (128 columns = 256 K each)
-constexpr int TC_PCOLS = TC_NMMA * TC_N;  // one stage-partial set: a 16-column D per issuer
-constexpr int TC_ACOL0 = 2 * TC_PCOLS;   // first A column; partial sets at columns 0 and 64
+constexpr int TC_NA = 3;                 // most TMEM A buffers (128 columns = 256 K each)
+constexpr int TC_ATOM = 2 * TC_N * 128;  // a B atom pair in shared memory: 64 K x 16 hi rows, then the lo rows
+// TMEM per phase. Gate/up (lo halves rare): three A buffers, a 16-column D per issuer.
+// Down (its fp32 inputs nearly always need the lo half): one N = 32 MMA takes the hi and
+// lo rows of an atom pair together (half the issues), so a D per issuer is 32 columns and
+// two A buffers leave room for the double-buffered partials.
+template <int PHASE> struct TcTmem {
+    static constexpr int NA = PHASE ? 2 : 3;
+    static constexpr int PW = PHASE ? 2 * TC_N : TC_N;      // D columns per issuer
+    static constexpr int PCOLS = TC_NMMA * PW;              // one stage-partial set
+    static constexpr int ACOL0 = 2 * PCOLS;                 // first A column
+    static_assert(ACOL0 + NA * 128 <= 512, "TMEM columns");
+};
 constexpr int TC_XCH_BYTES = 64 * TC_N * 4;   // gate/up exchange in the epilogue
 // barriers: full[NS] empty[NS] aready[NA] afree[NA] pfree[2] (stage partials)
 constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 2;
@@ -285,7 +295,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
                     unsigned char *sw = smem + (size_t)st * TC_STAGE;
                     unsigned char *ssb = sw + TC_W_BYTES;
                     unsigned char *sbh = sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024);
-                    unsigned char *sbl = sbh + TC_B_BYTES;
                     const uint32_t full = s_addr(&b_full[st]);
                     bar_expect(full, (uint32_t)(TC_W_BYTES + TC_S_BYTES + TC_B_BYTES * (lo_any ? 2 : 1)));
                     const int x0 = kc * 256, xs = kc * 16;
@@ -307,8 +316,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
                     // belong to the next one or lie past the tensor: those columns are
                     // never read back; out-of-range rows are filled with zeros)
                     for (int a = 0; a < TC_KC / 64; a++) {
-                        tma2d(s_addr(sbh + a * (TC_N * 128)), &bhmap, kc * TC_KC + a * 64, q0 + tb, full);
-                        if (lo_any) tma2d(s_addr(sbl + a * (TC_N * 128)), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
+                        tma2d(s_addr(sbh + a * TC_ATOM), &bhmap, kc * TC_KC + a * 64, q0 + tb, full);
+                        if (lo_any) tma2d(s_addr(sbh + a * TC_ATOM + TC_N * 128), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
                     }
                 }
             });
@@ -322,7 +331,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         // that the epilogue warps sum in fp32.
         if (lane == 0) {
             const int mi = warp - TC_MMA_WARP0, h = mi >> 1, j = mi & 1;
-            const uint32_t idesc = f16_idesc(TC_N);
+            const uint32_t idesc = f16_idesc(TC_N), idesc2 = f16_idesc(2 * TC_N);
+            using TM = TcTmem<PHASE>;
             // this issuer's eight B offsets, in 16-byte descriptor units: the descriptor of a
             // stage's tile is built once and advanced by these (the 14-bit start field does
             // not carry: shared addresses stay below 256 KB)
@@ -330,7 +340,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
 _Pragma("unroll")
             for (int t = 0; t < 8; t++) {
                 const int kk = h * 256 + (j * 8 + t) * 16;
-                boff16[t] = (uint32_t)(((kk >> 6) * (TC_N * 128) + (kk & 63) * 2) >> 4);
+                boff16[t] = (uint32_t)(((kk >> 6) * TC_ATOM + (kk & 63) * 2) >> 4);
             }
             TC_FOR_UNITS({
                 for (int kc = 0; kc < NK && !failed; kc++, item++) {
@@ -338,22 +348,27 @@ _Pragma("unroll")
                     const uint32_t par = (uint32_t)((item / TC_NS) & 1);
                     const int pb = item & 1;
                     const int fill = 2 * item + h;   // the A buffer the decode warps filled
-                    const int ab = fill % TC_NA;
-                    const uint32_t apar = (uint32_t)((fill / TC_NA) & 1);
+                    const int ab = fill % TM::NA;
+                    const uint32_t apar = (uint32_t)((fill / TM::NA) & 1);
                     if (!bar_wait(s_addr(&b_pfree[pb]), (uint32_t)(((item >> 1) & 1) ^ 1))) { failed = true; break; }
                     if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
                     if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t dtm = tmem + (uint32_t)(pb * TC_PCOLS + mi * TC_N);
+                    const uint32_t dtm = tmem + (uint32_t)(pb * TM::PCOLS + mi * TM::PW);
                     const unsigned char *sw = smem + (size_t)st * TC_STAGE;
                     const uint32_t bh = s_addr(sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
-                    const uint32_t bl = bh + TC_B_BYTES;
-                    const uint32_t atm = tmem + (uint32_t)(TC_ACOL0 + ab * 128 + j * 64);
-                    const uint64_t dh = sw128_desc(bh), dl = sw128_desc(bl);
+                    const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * 128 + j * 64);
+                    const uint64_t dh = sw128_desc(bh), dl = sw128_desc(bh + TC_N * 128);
                     if (!lo_any) {
 _Pragma("unroll")
                         for (int t = 0; t < 8; t++)               // K16 steps of this quarter
                             mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
+                    } else if (PHASE == 1) {
+                        // the 16 hi rows and the 16 lo rows of the atom pair as one N = 32
+                        // operand: D columns 0..15 take the hi products, 16..31 the lo
+_Pragma("unroll")
+                        for (int t = 0; t < 8; t++)
+                            mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc2, t ? 1u : 0u);
                     } else {
 _Pragma("unroll")
                         for (int t = 0; t < 8; t++) {
@@ -384,14 +399,14 @@ _Pragma("unroll")
                 const uint32_t par = (uint32_t)((item / TC_NS) & 1);
                 // the A buffer this warp fills: half h of this stage
                 const int fill = 2 * item + h;
-                const int ab = fill % TC_NA;
-                const uint32_t apar = (uint32_t)((fill / TC_NA) & 1);
+                const int ab = fill % TcTmem<PHASE>::NA;
+                const uint32_t apar = (uint32_t)((fill / TcTmem<PHASE>::NA) & 1);
                 if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
                 if (!bar_wait(s_addr(&b_afree[ab]), apar ^ 1u)) { failed = true; break; }
                 const unsigned char *sw = smem + (size_t)st * TC_STAGE;
                 const unsigned char *row = sw + boxbase + h * hbox + boxrow * 128;
                 const uint2 sc = *reinterpret_cast<const uint2 *>(sw + TC_W_BYTES + r * 16 + h * 8);
-                const uint32_t atm = tmem + lane_addr + (uint32_t)(TC_ACOL0 + ab * 128);
+                const uint32_t atm = tmem + lane_addr + (uint32_t)(TcTmem<PHASE>::ACOL0 + ab * 128);
                 // 8 groups of 32 in this K half, four at a time: the four loads go first (a
                 // load placed after a tcgen05.st would wait for it)
 _Pragma("unroll")
@@ -449,20 +464,37 @@ _Pragma("unroll")
                 // they need pfree -- so the phase cannot be lapped.)
                 if (!bar_wait(s_addr(&b_empty[item % TC_NS]), (uint32_t)((item / TC_NS) & 1))) { failed = true; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                uint32_t d0[16], d1[16], d2[16], d3[16];
-                const uint32_t pt = tmem + lane_addr + (uint32_t)(pb * TC_PCOLS);
-                tmem_ld16(pt, d0);
-                tmem_ld16(pt + TC_N, d1);
-                tmem_ld16(pt + 2 * TC_N, d2);
-                tmem_ld16(pt + 3 * TC_N, d3);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                using TM = TcTmem<PHASE>;
+                const uint32_t pt = tmem + lane_addr + (uint32_t)(pb * TM::PCOLS);
+                if (PHASE == 1 && lo_any) {
+                    // four issuers x (hi products, lo products), two issuers at a time
+                    for (int i2 = 0; i2 < TC_NMMA; i2 += 2) {
+                        uint32_t d0[16], d1[16], d2[16], d3[16];
+                        tmem_ld16(pt + i2 * TM::PW, d0);
+                        tmem_ld16(pt + i2 * TM::PW + TC_N, d1);
+                        tmem_ld16(pt + (i2 + 1) * TM::PW, d2);
+                        tmem_ld16(pt + (i2 + 1) * TM::PW + TC_N, d3);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+_Pragma("unroll")
+                        for (int n = 0; n < TC_N; n++)
+                            acc[n] += (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
+                                      (__uint_as_float(d2[n]) + __uint_as_float(d3[n]));
+                    }
+                } else {
+                    uint32_t d0[16], d1[16], d2[16], d3[16];
+                    tmem_ld16(pt, d0);
+                    tmem_ld16(pt + TM::PW, d1);
+                    tmem_ld16(pt + 2 * TM::PW, d2);
+                    tmem_ld16(pt + 3 * TM::PW, d3);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+_Pragma("unroll")
+                    for (int n = 0; n < TC_N; n++)
+                        acc[n] += (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
+                                  (__uint_as_float(d2[n]) + __uint_as_float(d3[n]));
+                }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) bar_arrive(s_addr(&b_pfree[pb]));
-_Pragma("unroll")
-                for (int n = 0; n < TC_N; n++)
-                    acc[n] += (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
-                              (__uint_as_float(d2[n]) + __uint_as_float(d3[n]));
             }
             if (failed) break;
             if (PHASE == 0) {
