@@ -251,33 +251,51 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
     }
 }
 
-// hi/lo bf16 pieces of X, [2][Np][in_pad], zero past T and past in; lo_flag |= any lo != 0
+// hi/lo bf16 pieces of X, [2][Np][in_pad], zero past T and past in; lo_flag = 1 when any
+// lo != 0 (one plain store per block that saw one: every writer writes the same value)
 __global__ void __launch_bounds__(256) split_kernel(__nv_bfloat16 *__restrict__ xp, int *__restrict__ lo_flag,
                                                    const float *__restrict__ X, int ldx, int T, int Np,
                                                    int in, int in_pad)
 {
     const int t = blockIdx.y;
     const int k = blockIdx.x * 256 + threadIdx.x;
-    if (k >= in_pad) return;
-    const float x = (t < T && k < in) ? X[(size_t)t * ldx + k] : 0.0f;
-    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
-    const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
-    xp[(size_t)t * in_pad + k] = hi;
-    xp[((size_t)Np + t) * in_pad + k] = lo;
-    const int nz = __bfloat16_as_ushort(lo) & 0x7FFF;
-    if (__any_sync(0xffffffffu, nz != 0) && (threadIdx.x & 31) == 0) atomicOr(lo_flag, 1);
+    int nz = 0;
+    if (k < in_pad) {
+        const float x = (t < T && k < in) ? X[(size_t)t * ldx + k] : 0.0f;
+        const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+        xp[(size_t)t * in_pad + k] = hi;
+        xp[((size_t)Np + t) * in_pad + k] = lo;
+        nz = __bfloat16_as_ushort(lo) & 0x7FFF;
+    }
+    if (__syncthreads_or(nz) && threadIdx.x == 0) *lo_flag = 1;
 }
 
-// Y[t][o] = sum over splits in order
+// Y[t][o] = sum over splits in order; block (x, t) covers 4 * 256 outputs of row t
 __global__ void __launch_bounds__(256) reduce_kernel(float *__restrict__ Y, const float *__restrict__ part,
                                                     int T, int out, int ldy, int nsplit)
 {
-    const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
-    if (i >= (long long)T * out) return;
-    const int t = (int)(i / out), o = (int)(i % out);
-    float y = part[i];
-    for (int s = 1; s < nsplit; s++) y = __fadd_rn(y, part[(size_t)s * T * out + i]);
-    Y[(size_t)t * ldy + o] = y;
+    const int t = blockIdx.y;
+    const int o = (blockIdx.x * 256 + threadIdx.x) * 4;
+    if (o >= out) return;
+    const size_t plane = (size_t)T * out;
+    const float *src = part + (size_t)t * out + o;
+    float *dst = Y + (size_t)t * ldy + o;
+    if (o + 4 <= out && (out & 3) == 0 && (ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(Y) & 15u) == 0) {
+        float4 y = *reinterpret_cast<const float4 *>(src);
+        for (int s = 1; s < nsplit; s++) {
+            const float4 v = *reinterpret_cast<const float4 *>(src + s * plane);
+            y.x = __fadd_rn(y.x, v.x); y.y = __fadd_rn(y.y, v.y);
+            y.z = __fadd_rn(y.z, v.z); y.w = __fadd_rn(y.w, v.w);
+        }
+        *reinterpret_cast<float4 *>(dst) = y;
+    } else {
+        for (int j = 0; j < 4 && o + j < out; j++) {
+            float y = src[j];
+            for (int s = 1; s < nsplit; s++) y = __fadd_rn(y, src[s * plane + j]);
+            dst[j] = y;
+        }
+    }
 }
 
 // ---- host ----------------------------------------------------------------------------
@@ -403,9 +421,8 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
         mmw_tc_kernel<<<std::min(p.n_units, sms), THREADS, smem, s>>>(wm, xm, a);
         if ((st = k3::launch_status())) return st;
         if (p.nsplit > 1) {
-            const long long n = (long long)Tc * out;
-            reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(Y + (size_t)t0 * ldy, part, Tc, out, ldy,
-                                                                      p.nsplit);
+            reduce_kernel<<<dim3((unsigned)((out + 1023) / 1024), (unsigned)Tc), 256, 0, s>>>(
+                Y + (size_t)t0 * ldy, part, Tc, out, ldy, p.nsplit);
             if ((st = k3::launch_status())) return st;
         }
     }
