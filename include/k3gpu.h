@@ -240,7 +240,9 @@ size_t k3gpu_mla_workspace(int B, int T, int H, int kv_lora, int max_ctx);
  * query t sees every row below cached[b] and new row j iff bit j of mask[t] is set
  * (chain: bits 0..t; tree: the node's ancestors and itself). out [B][T][H][v_head] fp32
  * is the attention output before the output gate. T <= 64, kv_lora in {128, 256, 512},
- * qk_rope <= 64, qk_nope and v_head <= 256. */
+ * qk_rope <= 64 (q_rope and rope may be NULL when it is 0), qk_nope and v_head <= 256.
+ * kv_lora in {128, 256, 512} with qk_rope in {0, 64} and 16-byte aligned lat/rope run on
+ * the tensor cores (tcgen05); other shapes on a CUDA-core kernel. */
 int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *q_rope,
                        const float *kv_b, const uint16_t *lat, const uint16_t *rope,
                        const int *cached, const uint64_t *mask, int B, int T, int H,

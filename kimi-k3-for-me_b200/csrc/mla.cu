@@ -18,7 +18,10 @@
 #include <cuda_bf16.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace k3 {
 
@@ -37,13 +40,13 @@ struct MlaWs {
     float *pm;     // [B][T][H][nsplit] running max
     float *pl;     // [B][T][H][nsplit] running sum
     float *pu;     // [B][T][H][nsplit][kvl]
+    uint16_t *qh, *ql;   // tensor-core path: [B][T][H][kvl + qr] bf16 pieces of [q_abs | q_rope]
 };
 
 static size_t a256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-static size_t mla_ws_layout(int B, int T, int H, int kvl, int max_ctx, MlaWs *w, char *base)
+static size_t mla_ws_layout(int B, int T, int H, int kvl, int qr, int ns, MlaWs *w, char *base)
 {
-    const int ns = (max_ctx + MLA_SPLIT - 1) / MLA_SPLIT;
     const size_t rows = (size_t)B * T * H;
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -53,7 +56,11 @@ static size_t mla_ws_layout(int B, int T, int H, int kvl, int max_ctx, MlaWs *w,
     };
     char *qa = take(rows * kvl * 4), *pm = take(rows * ns * 4), *pl = take(rows * ns * 4);
     char *pu = take(rows * ns * (size_t)kvl * 4);
-    if (w) { w->qabs = (float *)qa; w->pm = (float *)pm; w->pl = (float *)pl; w->pu = (float *)pu; }
+    char *qh = take(rows * (size_t)(kvl + qr) * 2), *ql = take(rows * (size_t)(kvl + qr) * 2);
+    if (w) {
+        w->qabs = (float *)qa; w->pm = (float *)pm; w->pl = (float *)pl; w->pu = (float *)pu;
+        w->qh = (uint16_t *)qh; w->ql = (uint16_t *)ql;
+    }
     return o;
 }
 
@@ -202,14 +209,14 @@ __global__ void __launch_bounds__(256) mla_combine_kernel(float *__restrict__ ou
                                                           const float *__restrict__ kv_b,
                                                           const int *__restrict__ cached, int T,
                                                           int H, int qn, int vh, int kvl,
-                                                          int nsplit)
+                                                          int nsplit, int split_len)
 {
     __shared__ float su[MLA_MAXL];
     __shared__ float sw[MLA_MAXSPLIT];
     const int bt = blockIdx.x, h = blockIdx.y;
     const int b = bt / T;
     const int n_ctx = cached[b] + T;
-    const int nsu = min(nsplit, (n_ctx + MLA_SPLIT - 1) / MLA_SPLIT);
+    const int nsu = max(0, min(nsplit, (n_ctx + split_len - 1) / split_len));
     const size_t base = ((size_t)bt * H + h) * nsplit;
     if (threadIdx.x == 0) {
         float M = -INFINITY;
@@ -242,12 +249,446 @@ __global__ void __launch_bounds__(256) mla_combine_kernel(float *__restrict__ ou
     }
 }
 
+// ------------------------------------------------------------------ tensor cores -----
+// The same attention on tcgen05 for kv_lora in {128, 256, 512} and qk_rope in {0, 64}. All
+// H heads of a query node read the same latent rows, so one sequence's T*H query rows
+// against its cache rows is a pair of GEMMs with a softmax between them:
+//   S [rows x positions] = [q_abs | q_rope] . [lat | rope]^T        (K = kvl + qr)
+//   u [rows x kvl]      += softmax(S) . lat                          (K = positions)
+// A CTA takes 128 query rows, one half of u's kvl columns and one slice of positions
+// (flash-decoding: slices merge in mla_combine_kernel), 128 positions per tile:
+//   warp 0     TMA: per tile the score stages (a 64-column atom of Q hi, Q lo and the cache,
+//              16 KB each), then the value stages (the tile's latent atoms of this half)
+//   warp 1     MMA issue (one thread): S = Qhi.C + Qlo.C into a TMEM buffer (two, so the
+//              next tile's scores overlap this tile's softmax); then u += Phi.V + Plo.V
+//              with V read as an MN-major operand straight from the cache tile
+//   warps 2-5  softmax, one thread per query row (= its TMEM lane): masked scores, a
+//              running max that moves only when a tile's max exceeds it by more than e^8
+//              (then the row of u in TMEM is rescaled), exps summed in fp32, P split into
+//              exact-enough bf16 hi and lo pieces in shared memory (128-byte swizzle); at
+//              the end the row's m, l and u go to the workspace
+// The fp32 queries enter as bf16 hi + lo (x = hi + lo to 2^-17 relative) and the cache is
+// bf16, so every product is exact in the fp32 accumulator; P likewise. TMEM: S buffers at
+// columns 0 and 128, u's half at 256..511. Every wait is bounded; TMEM is freed on every
+// exit path; no TMA multicast.
+namespace mlatc {
+using namespace tc;
+
+constexpr int NP = 128;                     // positions per tile
+constexpr int ATOM = 128 * 128;             // 128 rows x 128 bytes
+constexpr int STAGE = 3 * ATOM;             // Q hi, Q lo, cache atom (a value stage: first atom)
+constexpr int NS = 3;
+constexpr int P_OFF = NS * STAGE;           // P hi (2 atoms), P lo (2 atoms)
+constexpr int BAR_OFF = P_OFF + 4 * ATOM;
+constexpr int NBAR = 2 * NS + 4 + 4;        // full, empty, s_full[2], s_free[2], p_full, p_free, o_full, fin
+constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;   // + room to align the base to 1024
+constexpr int THREADS = 6 * 32;
+constexpr float RESCALE_AT = 8.0f;
+constexpr int SMS_PLAN = 148;               // the split plan assumes a full B200
+
+struct Args {
+    float *pm, *pl, *pu;                    // workspace partial states
+    const int *cached;
+    const uint64_t *mask;
+    int T, H, R, kvl, qr, cap, nsplit, split_len, qa;
+    float scale;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo_elem, float hi_elem)
+{
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo_elem, hi_elem);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// grid B*R, block 128: [q_abs | q_rope] -> bf16 hi, lo pieces
+__global__ void __launch_bounds__(128) prep_kernel(uint16_t *__restrict__ qh, uint16_t *__restrict__ ql,
+                                                   const float *__restrict__ qabs,
+                                                   const float *__restrict__ q_rope, int kvl, int qr)
+{
+    const size_t row = blockIdx.x;
+    const int kq = kvl + qr;
+    for (int d = threadIdx.x; d < kq; d += blockDim.x) {
+        const float x = d < kvl ? qabs[row * kvl + d] : q_rope[row * qr + (d - kvl)];
+        const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+        qh[row * kq + d] = __bfloat16_as_ushort(hi);
+        ql[row * kq + d] = __bfloat16_as_ushort(lo);
+    }
+}
+
+__global__ void __launch_bounds__(THREADS, 1) attend_kernel(const __grid_constant__ CUtensorMap qhmap,
+                                                            const __grid_constant__ CUtensorMap qlmap,
+                                                            const __grid_constant__ CUtensorMap latmap,
+                                                            const __grid_constant__ CUtensorMap ropemap, Args a)
+{
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = s_addr(smem_raw);
+    unsigned char *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + BAR_OFF);
+    uint64_t *b_full = bars, *b_empty = bars + NS, *b_sfull = bars + 2 * NS, *b_sfree = b_sfull + 2;
+    uint64_t *b_pfull = b_sfree + 2, *b_pfree = b_pfull + 1, *b_ofull = b_pfree + 1, *b_fin = b_ofull + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int sp = blockIdx.x, qt = blockIdx.y >> 1, hf = blockIdx.y & 1, b = blockIdx.z;
+    const int q0 = qt * 128;
+    const int va = a.kvl / 128;                 // value atoms of this half
+    const int c = a.cached[b];
+    const int n_ctx = c + a.T;
+    const bool bad = c < 0 || n_ctx > a.cap;    // the new rows would lie outside the cache
+    const int begin = sp * a.split_len;
+    const int end = bad ? begin : min(n_ctx, begin + a.split_len);
+    const int ntile = end > begin ? (end - begin + NP - 1) / NP : 0;
+    if (bad && tid == 0 && sp == 0 && blockIdx.y == 0) flag(DEV_BAD_POSITION);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; s++) {
+            bar_init(s_addr(&b_full[s]), 1);
+            bar_init(s_addr(&b_empty[s]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            bar_init(s_addr(&b_sfull[i]), 1);
+            bar_init(s_addr(&b_sfree[i]), 4);
+        }
+        bar_init(s_addr(b_pfull), 4);
+        bar_init(s_addr(b_pfree), 1);
+        bar_init(s_addr(b_ofull), 1);
+        bar_init(s_addr(b_fin), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool failed = false;
+    unsigned char *pbuf = smem + P_OFF;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA
+        if (lane == 0 && ntile > 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&qhmap) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&latmap) : "memory");
+            const int yq = b * a.R + q0, yc = b * a.cap;
+            const int latoms = a.kvl / 64;
+            int item = 0;
+            for (int j = 0; j <= ntile && !failed; j++) {
+                for (int at = 0; j < ntile && at < a.qa && !failed; at++, item++) {
+                    const int st = item % NS;
+                    if (!bar_wait(s_addr(&b_empty[st]), (uint32_t)(((item / NS) & 1) ^ 1))) { failed = true; break; }
+                    const uint32_t sw = s_addr(smem + (size_t)st * STAGE), full = s_addr(&b_full[st]);
+                    bar_expect(full, 3 * ATOM);
+                    tma2d(sw, &qhmap, at * 64, yq, full);
+                    tma2d(sw + ATOM, &qlmap, at * 64, yq, full);
+                    if (at < latoms) tma2d(sw + 2 * ATOM, &latmap, at * 64, yc + begin + j * NP, full);
+                    else tma2d(sw + 2 * ATOM, &ropemap, 0, yc + begin + j * NP, full);
+                }
+                for (int v = 0; j >= 1 && v < va && !failed; v++, item++) {
+                    const int st = item % NS;
+                    if (!bar_wait(s_addr(&b_empty[st]), (uint32_t)(((item / NS) & 1) ^ 1))) { failed = true; break; }
+                    const uint32_t sw = s_addr(smem + (size_t)st * STAGE), full = s_addr(&b_full[st]);
+                    bar_expect(full, ATOM);
+                    tma2d(sw, &latmap, (hf * va + v) * 64, yc + begin + (j - 1) * NP, full);
+                }
+            }
+            // let the copies in flight land before the CTA can exit
+            for (int k = max(0, item - NS); k < item; k++)
+                if (!bar_wait(s_addr(&b_full[k % NS]), (uint32_t)((k / NS) & 1))) failed = true;
+            if (failed) flag(DEV_TIMEOUT);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issue
+        if (ntile > 0) {
+            const uint32_t idq = bf16_idesc(NP, false), idv = bf16_idesc(64, true);
+            const uint32_t pbase = s_addr(pbuf);
+            int item = 0;
+            for (int j = 0; j <= ntile && !failed; j++) {
+                if (j < ntile) {
+                    const int sb = j & 1;
+                    if (!bar_wait(s_addr(&b_sfree[sb]), (uint32_t)(((j >> 1) & 1) ^ 1))) { failed = true; break; }
+                    fence_after();
+                    const uint32_t s_tm = tmem + (uint32_t)(sb * NP);
+                    for (int at = 0; at < a.qa; at++, item++) {
+                        const int st = item % NS;
+                        if (!bar_wait(s_addr(&b_full[st]), (uint32_t)((item / NS) & 1))) { failed = true; break; }
+                        fence_after();
+                        if (lane == 0) {
+                            const uint64_t d0 = sw128_desc(s_addr(smem + (size_t)st * STAGE));
+                            const uint32_t ql = ATOM >> 4, cc = (2 * ATOM) >> 4;
+#pragma unroll
+                            for (int k = 0; k < 4; k++) {
+                                mma_ss(s_tm, d0 + 2 * k, d0 + cc + 2 * k, idq, (at | k) ? 1u : 0u);
+                                mma_ss(s_tm, d0 + ql + 2 * k, d0 + cc + 2 * k, idq, 1u);
+                            }
+                            mma_commit(s_addr(&b_empty[st]));
+                        }
+                        __syncwarp();
+                    }
+                    if (failed) break;
+                    if (lane == 0) mma_commit(s_addr(&b_sfull[sb]));
+                    __syncwarp();
+                }
+                if (j >= 1) {
+                    const int i = j - 1;
+                    if (!bar_wait(s_addr(b_pfull), (uint32_t)(i & 1))) { failed = true; break; }
+                    fence_after();
+                    const int p0 = begin + i * NP;
+                    const int nv = min(NP, end - p0);      // rows past it lie at or past n_ctx
+                    for (int v = 0; v < va; v++, item++) {
+                        const int st = item % NS;
+                        if (!bar_wait(s_addr(&b_full[st]), (uint32_t)((item / NS) & 1))) { failed = true; break; }
+                        fence_after();
+                        unsigned char *sv = smem + (size_t)st * STAGE;
+                        if (nv < NP) {
+                            // the cache past n_ctx is unspecified: zero it, so 0 * row stays 0
+                            for (int x = nv * 8 + lane; x < NP * 8; x += 32)
+                                *reinterpret_cast<uint4 *>(sv + (size_t)x * 16) = make_uint4(0, 0, 0, 0);
+                            fence_async_smem();
+                            __syncwarp();
+                        }
+                        if (lane == 0) {
+                            const uint32_t d_tm = tmem + 256u + (uint32_t)(v * 64);
+                            const uint32_t vb = s_addr(sv);
+#pragma unroll
+                            for (int kk = 0; kk < NP / 16; kk++) {
+                                const uint64_t ph = sw128_desc(pbase + (uint32_t)((kk >> 2) * ATOM)) + (uint64_t)((kk & 3) * 2);
+                                const uint64_t pl = sw128_desc(pbase + (uint32_t)((2 + (kk >> 2)) * ATOM)) + (uint64_t)((kk & 3) * 2);
+                                const uint64_t vd = sw128_mn_desc(vb + (uint32_t)(kk * 2048), ATOM);
+                                mma_ss(d_tm, ph, vd, idv, (i > 0 || kk > 0) ? 1u : 0u);
+                                mma_ss(d_tm, pl, vd, idv, 1u);
+                            }
+                            mma_commit(s_addr(&b_empty[st]));
+                        }
+                        __syncwarp();
+                    }
+                    if (failed) break;
+                    if (lane == 0) mma_commit(s_addr(b_pfree));
+                    __syncwarp();
+                }
+            }
+            if (lane == 0) {
+                mma_commit(s_addr(b_ofull));
+                mma_commit(s_addr(b_fin));
+                // every MMA of this CTA has completed before TMEM can be freed
+                if (!bar_wait(s_addr(b_fin), 0)) failed = true;
+                if (failed) flag(DEV_TIMEOUT);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ softmax
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int rg = q0 + row;
+        const bool row_ok = rg < a.R;
+        const int t = row_ok ? rg / a.H : 0;
+        const uint64_t mk = a.mask[t];
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        float m_run = -INFINITY, l_run = 0.0f;
+        for (int j = 0; j < ntile && !failed; j++) {
+            const int sb = j & 1;
+            const int p0 = begin + j * NP;
+            if (!bar_wait(s_addr(&b_sfull[sb]), (uint32_t)((j >> 1) & 1))) { failed = true; break; }
+            fence_after();
+            const uint32_t s_tm = tmem + lane_addr + (uint32_t)(sb * NP);
+            // a position is visible when it lies below end and is an old row or a new row
+            // whose bit is set in the node's mask
+            const bool all_old = p0 + NP <= min(c, end);
+            auto visible = [&](int s) -> bool {
+                return s < end && (s < c || ((mk >> (s - c)) & 1ull) != 0);
+            };
+            float mt = -INFINITY;
+            for (int ch = 0; ch < NP / 16; ch++) {
+                uint32_t v[16];
+                tmem_ld16(s_tm + (uint32_t)(ch * 16), v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int n = 0; n < 16; n++) {
+                    const int s = p0 + ch * 16 + n;
+                    if (all_old || visible(s)) mt = fmaxf(mt, __fmul_rn(__uint_as_float(v[n]), a.scale));
+                }
+            }
+            if (!row_ok) mt = -INFINITY;
+            // P and u belong to the previous tile's values product until it completes
+            if (!bar_wait(s_addr(b_pfree), (uint32_t)((j & 1) ^ 1))) { failed = true; break; }
+            fence_after();
+            const bool upd = mt > -INFINITY && (m_run == -INFINITY || mt > m_run + RESCALE_AT);
+            const bool resc = upd && m_run != -INFINITY;
+            const float al = resc ? __expf(m_run - mt) : 1.0f;
+            if (upd) m_run = mt;
+            if (__any_sync(0xffffffffu, resc)) {
+                // warp-wide TMEM access: lanes whose max stayed scale by 1
+                for (int ch = 0; ch < va * 4; ch++) {
+                    uint32_t v[16];
+                    const uint32_t ot = tmem + lane_addr + 256u + (uint32_t)(ch * 16);
+                    tmem_ld16(ot, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int n = 0; n < 16; n++) v[n] = __float_as_uint(__uint_as_float(v[n]) * al);
+                    tmem_st16(ot, v);
+                }
+                tmem_wait_st();
+            }
+            if (resc) l_run *= al;
+            for (int ch = 0; ch < NP / 16; ch++) {
+                uint32_t v[16];
+                tmem_ld16(s_tm + (uint32_t)(ch * 16), v);
+                tmem_wait_ld();
+                float pv[16];
+#pragma unroll
+                for (int n = 0; n < 16; n++) {
+                    const int s = p0 + ch * 16 + n;
+                    const bool vis = row_ok && (all_old || visible(s));
+                    pv[n] = vis ? __expf(__fmul_rn(__uint_as_float(v[n]), a.scale) - m_run) : 0.0f;
+                }
+#pragma unroll
+                for (int n = 0; n < 16; n++) l_run += pv[n];
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    uint32_t h4[4], l4[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const float x0 = pv[hh * 8 + 2 * q], x1 = pv[hh * 8 + 2 * q + 1];
+                        const float h0 = __bfloat162float(__float2bfloat16_rn(x0));
+                        const float h1 = __bfloat162float(__float2bfloat16_rn(x1));
+                        h4[q] = pack_bf16x2(h0, h1);
+                        l4[q] = pack_bf16x2(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+                    }
+                    const int kp = ch * 16 + hh * 8;                 // position within the tile
+                    const int off = (kp >> 6) * ATOM + row * 128 + ((((kp & 63) >> 3) ^ (row & 7)) << 4);
+                    *reinterpret_cast<uint4 *>(pbuf + off) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+                    *reinterpret_cast<uint4 *>(pbuf + 2 * ATOM + off) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
+                }
+            }
+            fence_async_smem();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                bar_arrive(s_addr(&b_sfree[sb]));
+                bar_arrive(s_addr(b_pfull));
+            }
+        }
+        // the row's partial state for this slice
+        if (ntile > 0 && !failed) {
+            if (!bar_wait(s_addr(b_ofull), 0)) failed = true;
+            fence_after();
+        }
+        if (failed) {
+            if (lane == 0) flag(DEV_TIMEOUT);
+        } else {
+            const size_t pi = ((size_t)b * a.R + (size_t)(row_ok ? rg : 0)) * a.nsplit + sp;
+            if (row_ok && hf == 0) {
+                a.pm[pi] = m_run;
+                a.pl[pi] = l_run;
+            }
+            float *dst = a.pu + pi * a.kvl + hf * va * 64;
+            for (int ch = 0; ch < va * 4; ch++) {
+                uint32_t v[16];
+                if (ntile > 0) {
+                    tmem_ld16(tmem + lane_addr + 256u + (uint32_t)(ch * 16), v);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int n = 0; n < 16; n++) v[n] = 0u;
+                }
+                if (row_ok) {
+#pragma unroll
+                    for (int n = 0; n < 16; n += 4)
+                        *reinterpret_cast<float4 *>(dst + ch * 16 + n) =
+                            make_float4(__uint_as_float(v[n]), __uint_as_float(v[n + 1]), __uint_as_float(v[n + 2]),
+                                        __uint_as_float(v[n + 3]));
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+// Slices: the number of 128-position tiles per slice that minimises (waves of CTAs) x
+// (tiles per slice + a fixed cost per slice), on a full B200.
+static int plan(int B, int R, int max_ctx, int *split_len)
+{
+    const int tiles = ceil_div(max_ctx, NP);
+    const long long combos = (long long)B * ceil_div(R, 128) * 2;
+    double best = 1e300;
+    int best_tl = tiles;
+    for (int ns = 1; ns <= std::min(tiles, MLA_MAXSPLIT); ns++) {
+        const int tl = ceil_div(tiles, ns);
+        const int nsr = ceil_div(tiles, tl);
+        const long long waves = (combos * nsr + SMS_PLAN - 1) / SMS_PLAN;
+        const double cost = (double)waves * (tl + 1.5);
+        if (cost < best - 1e-9) { best = cost; best_tl = tl; }
+    }
+    *split_len = best_tl * NP;
+    return ceil_div(tiles, best_tl);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *q = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(q);
+    });
+    return fn;
+}
+
+// bf16 [rows][cols] (row stride cols) in boxes of 64 columns x 128 rows, 128-byte swizzle
+static int map_bf16(CUtensorMap *m, const void *base, long long cols, long long rows)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return K3GPU_ECUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {64u, 128u};
+    cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        g_last_cuda_error = (int)r;
+        return K3GPU_ECUDA;
+    }
+    return K3GPU_OK;
+}
+
+static bool usable(int kvl, int qr, const void *lat, const void *rope)
+{
+    return (kvl == 128 || kvl == 256 || kvl == 512) && (qr == 0 || qr == 64) && aligned(lat, 16) &&
+           (qr == 0 || aligned(rope, 16));
+}
+
+static int g_attr_dev = -1;
+static std::mutex g_attr_mu;
+
+}  // namespace mlatc
+
 }  // namespace k3
 
 extern "C" size_t k3gpu_mla_workspace(int B, int T, int H, int kv_lora, int max_ctx)
 {
     if (B <= 0 || T <= 0 || H <= 0 || kv_lora <= 0 || max_ctx <= 0) return 0;
-    return k3::mla_ws_layout(B, T, H, kv_lora, max_ctx, nullptr, nullptr);
+    // room for either path: the CUDA-core slices of MLA_SPLIT positions or the
+    // tensor-core plan's slices (the rope width is at most MLA_MAXR)
+    int sl = 0;
+    const int ns_tc = k3::mlatc::plan(B, T * H, max_ctx, &sl);
+    const int ns = std::max(k3::ceil_div(max_ctx, k3::MLA_SPLIT), ns_tc);
+    return k3::mla_ws_layout(B, T, H, kv_lora, k3::MLA_MAXR, ns, nullptr, nullptr);
 }
 
 extern "C" int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *q_rope,
@@ -257,35 +698,74 @@ extern "C" int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *
                                   int max_ctx, float scale, void *workspace, size_t ws_bytes,
                                   void *stream)
 {
-    if (!out || !q_nope || !q_rope || !kv_b || !lat || !rope || !cached || !mask || !workspace)
+    if (!out || !q_nope || !kv_b || !lat || !cached || !mask || !workspace ||
+        (qk_rope > 0 && (!q_rope || !rope)))
         return K3GPU_EINVAL;
     if (B <= 0 || T <= 0 || T > 64 || H <= 0 || H > 4096 || qk_nope <= 0 || qk_nope > 256 ||
         qk_rope < 0 || qk_rope > k3::MLA_MAXR || v_head <= 0 || v_head > 256 ||
         (kv_lora != 128 && kv_lora != 256 && kv_lora != 512) || cap <= 0 || max_ctx <= 0 ||
         max_ctx > cap || k3::ceil_div(max_ctx, k3::MLA_SPLIT) > k3::MLA_MAXSPLIT)
         return K3GPU_EINVAL;
+    const int ns_cc = k3::ceil_div(max_ctx, k3::MLA_SPLIT);
+    int split_len = 0;
+    const int ns_tc = k3::mlatc::plan(B, T * H, max_ctx, &split_len);
     k3::MlaWs w;
-    const size_t need = k3::mla_ws_layout(B, T, H, kv_lora, max_ctx, &w, static_cast<char *>(workspace));
+    const size_t need = k3::mla_ws_layout(B, T, H, kv_lora, k3::MLA_MAXR, std::max(ns_cc, ns_tc), &w,
+                                          static_cast<char *>(workspace));
     if (ws_bytes < need) return K3GPU_ECAPACITY;
     cudaStream_t s = k3::as_stream(stream);
-    const int ns = k3::ceil_div(max_ctx, k3::MLA_SPLIT);
     k3::mla_qabs_kernel<<<dim3(B * T, H), 256, 0, s>>>(w.qabs, q_nope, kv_b, H, qk_nope, v_head,
                                                       kv_lora);
     int st = k3::launch_status();
     if (st) return st;
-    static bool attr_set = false;   // one-time opt-in to >48 KB of dynamic shared memory
-    if (!attr_set) {
-        st = k3::cuda_status(cudaFuncSetAttribute(k3::mla_attend_kernel,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  (int)k3::MLA_SMEM));
-        if (st) return st;
-        attr_set = true;
+    int ns = ns_cc, sl = k3::MLA_SPLIT;
+    if (k3::mlatc::usable(kv_lora, qk_rope, lat, rope)) {
+        using namespace k3::mlatc;
+        const int R = T * H, kq = kv_lora + qk_rope;
+        prep_kernel<<<B * R, 128, 0, s>>>(w.qh, w.ql, w.qabs, q_rope, kv_lora, qk_rope);
+        if ((st = k3::launch_status())) return st;
+        CUtensorMap qhm, qlm, latm, ropem;
+        if ((st = map_bf16(&qhm, w.qh, kq, (long long)B * R))) return st;
+        if ((st = map_bf16(&qlm, w.ql, kq, (long long)B * R))) return st;
+        if ((st = map_bf16(&latm, lat, kv_lora, (long long)B * cap))) return st;
+        if ((st = map_bf16(&ropem, qk_rope ? (const void *)rope : (const void *)lat, qk_rope ? 64 : kv_lora,
+                           (long long)B * cap)))
+            return st;
+        int dev = 0;
+        if ((st = k3::cuda_status(cudaGetDevice(&dev)))) return st;
+        {
+            std::lock_guard<std::mutex> lock(g_attr_mu);
+            if (g_attr_dev != dev) {
+                st = k3::cuda_status(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+                if (st) return st;
+                g_attr_dev = dev;
+            }
+        }
+        Args a;
+        a.pm = w.pm; a.pl = w.pl; a.pu = w.pu;
+        a.cached = cached; a.mask = mask;
+        a.T = T; a.H = H; a.R = R; a.kvl = kv_lora; a.qr = qk_rope; a.cap = cap;
+        a.nsplit = ns_tc; a.split_len = split_len; a.qa = kv_lora / 64 + (qk_rope ? 1 : 0);
+        a.scale = scale;
+        attend_kernel<<<dim3(ns_tc, k3::ceil_div(R, 128) * 2, B), THREADS, SMEM, s>>>(qhm, qlm, latm, ropem, a);
+        if ((st = k3::launch_status())) return st;
+        ns = ns_tc;
+        sl = split_len;
+    } else {
+        static bool attr_set = false;   // one-time opt-in to >48 KB of dynamic shared memory
+        if (!attr_set) {
+            st = k3::cuda_status(cudaFuncSetAttribute(k3::mla_attend_kernel,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      (int)k3::MLA_SMEM));
+            if (st) return st;
+            attr_set = true;
+        }
+        k3::mla_attend_kernel<<<dim3(ns, B * T, k3::ceil_div(H, k3::MLA_HT)), k3::MLA_THREADS,
+                                k3::MLA_SMEM, s>>>(
+            w, q_rope, lat, rope, cached, mask, T, H, qk_rope, kv_lora, cap, ns, scale);
+        if ((st = k3::launch_status())) return st;
     }
-    k3::mla_attend_kernel<<<dim3(ns, B * T, k3::ceil_div(H, k3::MLA_HT)), k3::MLA_THREADS,
-                            k3::MLA_SMEM, s>>>(
-        w, q_rope, lat, rope, cached, mask, T, H, qk_rope, kv_lora, cap, ns, scale);
-    if ((st = k3::launch_status())) return st;
     k3::mla_combine_kernel<<<dim3(B * T, H), 256, 0, s>>>(out, w, kv_b, cached, T, H, qk_nope,
-                                                         v_head, kv_lora, ns);
+                                                         v_head, kv_lora, ns, sl);
     return k3::launch_status();
 }

@@ -1,0 +1,116 @@
+// tc.cuh -- tcgen05, TMA and mbarrier helpers shared by the tensor-core kernels that
+// include it (inline PTX for sm_100a). Every wait is bounded: a wait that gives up returns
+// false and the caller records DEV_TIMEOUT and unwinds.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace k3 {
+namespace tc {
+
+constexpr long long SPIN = 1LL << 22;
+constexpr int SUSPEND_NS = 1000;
+
+__device__ __forceinline__ uint32_t s_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bar_init(uint32_t b, uint32_t n)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint32_t b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint32_t b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+}
+// bounded: each try may suspend the warp until the phase completes or SUSPEND_NS pass
+__device__ __forceinline__ bool bar_wait(uint32_t b, uint32_t parity)
+{
+    for (long long i = 0; i < SPIN; i++) {
+        uint32_t ok;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                     " selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(ok)
+                     : "r"(b), "r"(parity), "n"(SUSPEND_NS)
+                     : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+// 2-D tiled TMA load into this CTA's shared memory (no multicast)
+__device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap *m, int x, int y, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+// generic-proxy shared-memory writes -> visible to the tensor core and TMA
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptors, 128-byte swizzle (atoms of 8 rows x 128 bytes, 1024 B):
+// start >> 4, LBO >> 4 at bit 16, SBO >> 4 at bit 32, version 1 at bit 46, layout 2 at 61.
+//   K-major:  rows are M (or N) indices, 128 bytes = 64 K elements per row; SBO = 1024 is
+//             the step between 8-row groups; LBO unused.
+//   MN-major: rows are K indices, 128 bytes = 64 M/N elements per row; SBO = 1024 is the
+//             step between 8-K-row groups, LBO the step between 64-element M/N blocks.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// kind::f16 instruction descriptor, M = 128: D f32 (bit 4), A and B bf16 (bits 7, 10),
+// B MN-major when b_mn (bit 16), N >> 3 at bit 17, M >> 4 at bit 24
+__host__ __device__ constexpr uint32_t bf16_idesc(int N, bool b_mn)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(N >> 3) << 17) |
+           (8u << 24);
+}
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+}  // namespace tc
+}  // namespace k3

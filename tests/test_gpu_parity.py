@@ -359,6 +359,43 @@ def test_mla_absorbed_vs_oracle(k3, tree):
     assert_clean(k3)
 
 
+# The tcgen05 path (kv_lora 128/256/512, qk_rope 0 or 64): ragged 128-row query tiles,
+# several context slices, a partial last tile, and NaN garbage in the cache rows past
+# cached + T (the kernel zeroes them before they enter the value product). The bar is
+# relative L2 1e-4 (5e-4 for the wide-score case, whose scores spread over +-40 and whose
+# running max is rescaled along the context).
+@pytest.mark.parametrize("kvl,qr,B,T,H,cached,tree,qscale", [
+    (512, 64, 2, 9, 16, [700, 37], True, 1.0),     # K3 widths, 2 query tiles (144 rows)
+    (128, 0, 1, 5, 8, [3000], False, 1.0),         # no rope, many slices
+    (256, 64, 1, 4, 32, [5000], True, 4.0),        # wide scores: lazy-max rescale
+    (512, 64, 1, 64, 4, [130], False, 1.0),        # 64 chain nodes, cache shorter than a tile pair
+], ids=["k3_2seq", "norope_slices", "rescale", "t64"])
+def test_mla_absorbed_tensor_core(k3, kvl, qr, B, T, H, cached, tree, qscale):
+    qn, vh = 32, 48
+    qnope, qrope, kvb, lat, rope, cap = mla_case(17 + kvl + T, B, T, H, qn, qr, vh, kvl, cached)
+    qnope *= np.float32(qscale)
+    for b in range(B):                      # unspecified rows past the new ones
+        lat[b, cached[b] + T:] = np.nan
+        rope[b, cached[b] + T:] = np.nan
+    if tree:
+        parent = [-1] + [(i - 1) // 2 for i in range(1, T)]
+        masks = O.tree_masks(parent)
+    else:
+        masks = O.chain_masks(T)
+    scale = 1.0 / np.sqrt(qn + qr)
+    # qk_rope = 0: empty rope tensors (NULL pointers at the C ABI)
+    out = k3.mla_absorbed(dev(qnope), dev(qrope), dev(kvb), dev(to_bf16_bits(lat).view(np.int16)),
+                          dev(to_bf16_bits(rope).view(np.int16)), dev(np.array(cached, np.int32)),
+                          dev(masks.view(np.int64)), vh, cap, scale)
+    got = host(out)
+    tol = 5e-4 if qscale > 1 else 1e-4
+    for b in range(B):
+        ref = O.mla_absorbed(qnope[b], qrope[b], kvb, lat[b], rope[b], cached[b], masks, scale, vh)
+        assert np.isfinite(got[b]).all()
+        assert rel_l2(got[b], ref) < tol, rel_l2(got[b], ref)
+    assert_clean(k3)
+
+
 # ------------------------------------------------------------------------- accept --
 def test_accept_greedy_every_acceptance_count(k3):
     B, nd, V = 6, 5, 1000
