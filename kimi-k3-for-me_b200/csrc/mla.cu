@@ -257,34 +257,46 @@ __global__ void __launch_bounds__(256) mla_combine_kernel(float *__restrict__ ou
 //   u [rows x kvl]      += softmax(S) . lat                          (K = positions)
 // A CTA takes 128 query rows, one half of u's kvl columns and one slice of positions
 // (flash-decoding: slices merge in mla_combine_kernel), 128 positions per tile:
-//   warp 0     TMA: per tile the score stages (a 64-column atom of Q hi, Q lo and the cache,
-//              16 KB each), then the value stages (the tile's latent atoms of this half)
-//   warp 1     MMA issue (one thread): S = Qhi.C + Qlo.C into a TMEM buffer (two, so the
-//              next tile's scores overlap this tile's softmax); then u += Phi.V + Plo.V
-//              with V read as an MN-major operand straight from the cache tile
-//   warps 2-5  softmax, one thread per query row (= its TMEM lane): masked scores, a
-//              running max that moves only when a tile's max exceeds it by more than e^8
-//              (then the row of u in TMEM is rescaled), exps summed in fp32, P split into
-//              exact-enough bf16 hi and lo pieces in shared memory (128-byte swizzle); at
-//              the end the row's m, l and u go to the workspace
-// The fp32 queries enter as bf16 hi + lo (x = hi + lo to 2^-17 relative) and the cache is
-// bf16, so every product is exact in the fp32 accumulator; P likewise. TMEM: S buffers at
-// columns 0 and 128, u's half at 256..511. Every wait is bounded; TMEM is freed on every
-// exit path; no TMA multicast.
+//   warp 0      TMA, score ring: per tile and 64-column atom, Q hi, Q lo and the cache atom
+//   warp 1      TMA, value ring: the tile's latent atoms of this half, two per stage
+//   warp 2      score MMAs (one thread): S = Qhi.C + Qlo.C into one of two TMEM buffers
+//   warp 3      value MMAs (one thread): u += Phi.V + Plo.V with P read from TMEM and V an
+//               MN-major operand straight from the cache tile (N = 128: two atoms per MMA)
+//   warps 4-11  softmax, two warps per TMEM lane quarter (64 positions each), one query row
+//               per lane: masked scores, a running max in log2 units that moves only when
+//               a tile's max exceeds it by more than 2^11 (then the row of u in TMEM is
+//               rescaled), exps summed in fp32, P split into exact-enough bf16 hi and lo
+//               pieces written over the scores they came from; at the end the row's m, l
+//               and u go to the workspace
+// A tile's S/P buffer is reused two tiles later, once its value MMAs have completed, so
+// the softmax of tile j+1 overlaps the value product of tile j. The fp32 queries enter as
+// bf16 hi + lo (x = hi + lo to 2^-17 relative) and the cache is bf16, so every product is
+// exact in the fp32 accumulator; P likewise. TMEM: S/P buffers at columns 0 and 128, u's
+// half at 256..511 (P of 32 positions: 16 columns of hi pairs, then 16 of lo pairs, in
+// place of those positions' scores). Every wait is bounded; TMEM is freed on every exit
+// path; no TMA multicast.
 namespace mlatc {
 using namespace tc;
 
 constexpr int NP = 128;                     // positions per tile
 constexpr int ATOM = 128 * 128;             // 128 rows x 128 bytes
-constexpr int STAGE = 3 * ATOM;             // Q hi, Q lo, cache atom (a value stage: first atom)
-constexpr int NS = 3;
-constexpr int P_OFF = NS * STAGE;           // P hi (2 atoms), P lo (2 atoms)
-constexpr int BAR_OFF = P_OFF + 4 * ATOM;
-constexpr int NBAR = 2 * NS + 4 + 4;        // full, empty, s_full[2], s_free[2], p_full, p_free, o_full, fin
+constexpr int QSTAGE = 3 * ATOM;            // Q hi, Q lo, cache atom
+constexpr int NSQ = 3;
+constexpr int VSTAGE = 2 * ATOM;            // two latent atoms (128 columns of u)
+constexpr int NSV = 2;
+constexpr int V_OFF = NSQ * QSTAGE;
+constexpr int X_OFF = V_OFF + NSV * VSTAGE; // row max exchange [2][2][128], row sums [128]
+constexpr int BAR_OFF = X_OFF + 5 * 128 * 4;
+// qfull, qempty, vfull, vempty, s_full[2], p_full[2], pv_done[2], o_full, fin_q, fin_v
+constexpr int NBAR = 2 * NSQ + 2 * NSV + 6 + 3;
 constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;   // + room to align the base to 1024
-constexpr int THREADS = 6 * 32;
-constexpr float RESCALE_AT = 8.0f;
+constexpr int NSOFT = 8;
+constexpr int THREADS = (4 + NSOFT) * 32;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+constexpr float RESCALE_AT = 11.0f;         // log2 units
 constexpr int SMS_PLAN = 148;               // the split plan assumes a full B200
+static_assert(SMEM <= 227 * 1024, "shared memory");
 
 struct Args {
     float *pm, *pl, *pu;                    // workspace partial states
@@ -298,6 +310,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo_elem, float hi_elem)
 {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo_elem, hi_elem);
     return *reinterpret_cast<const uint32_t *>(&v);
+}
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // grid B*R, block 128: [q_abs | q_rope] -> bf16 hi, lo pieces
@@ -325,13 +343,18 @@ __global__ void __launch_bounds__(THREADS, 1) attend_kernel(const __grid_constan
     const uint32_t raw = s_addr(smem_raw);
     unsigned char *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + BAR_OFF);
-    uint64_t *b_full = bars, *b_empty = bars + NS, *b_sfull = bars + 2 * NS, *b_sfree = b_sfull + 2;
-    uint64_t *b_pfull = b_sfree + 2, *b_pfree = b_pfull + 1, *b_ofull = b_pfree + 1, *b_fin = b_ofull + 1;
+    uint64_t *b_qfull = bars, *b_qempty = bars + NSQ, *b_vfull = bars + 2 * NSQ, *b_vempty = b_vfull + NSV;
+    uint64_t *b_sfull = b_vempty + NSV, *b_pfull = b_sfull + 2, *b_pvdone = b_pfull + 2;
+    uint64_t *b_ofull = b_pvdone + 2, *b_finq = b_ofull + 1, *b_finv = b_finq + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
+    float *xmax = reinterpret_cast<float *>(smem + X_OFF);     // [2 tiles][2 halves][128]
+    float *xsum = xmax + 4 * 128;                              // [128]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int sp = blockIdx.x, qt = blockIdx.y >> 1, hf = blockIdx.y & 1, b = blockIdx.z;
     const int q0 = qt * 128;
-    const int va = a.kvl / 128;                 // value atoms of this half
+    const int va = a.kvl / 128;                 // latent atoms of this half
+    const int vw = va < 2 ? va : 2;             // atoms per value stage
+    const int nvs = va / vw;                    // value stages per tile
     const int c = a.cached[b];
     const int n_ctx = c + a.T;
     const bool bad = c < 0 || n_ctx > a.cap;    // the new rows would lie outside the cache
@@ -341,21 +364,25 @@ __global__ void __launch_bounds__(THREADS, 1) attend_kernel(const __grid_constan
     if (bad && tid == 0 && sp == 0 && blockIdx.y == 0) flag(DEV_BAD_POSITION);
 
     if (tid == 0) {
-        for (int s = 0; s < NS; s++) {
-            bar_init(s_addr(&b_full[s]), 1);
-            bar_init(s_addr(&b_empty[s]), 1);
+        for (int s = 0; s < NSQ; s++) {
+            bar_init(s_addr(&b_qfull[s]), 1);
+            bar_init(s_addr(&b_qempty[s]), 1);
+        }
+        for (int s = 0; s < NSV; s++) {
+            bar_init(s_addr(&b_vfull[s]), 1);
+            bar_init(s_addr(&b_vempty[s]), 1);
         }
         for (int i = 0; i < 2; i++) {
             bar_init(s_addr(&b_sfull[i]), 1);
-            bar_init(s_addr(&b_sfree[i]), 4);
+            bar_init(s_addr(&b_pfull[i]), NSOFT);
+            bar_init(s_addr(&b_pvdone[i]), 1);
         }
-        bar_init(s_addr(b_pfull), 4);
-        bar_init(s_addr(b_pfree), 1);
         bar_init(s_addr(b_ofull), 1);
-        bar_init(s_addr(b_fin), 1);
+        bar_init(s_addr(b_finq), 1);
+        bar_init(s_addr(b_finv), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {
+    if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -365,164 +392,204 @@ __global__ void __launch_bounds__(THREADS, 1) attend_kernel(const __grid_constan
     fence_after();
     const uint32_t tmem = *tmem_slot;
     bool failed = false;
-    unsigned char *pbuf = smem + P_OFF;
+    const int yc = b * a.cap;
 
     if (warp == 0) {
-        // ------------------------------------------------------------------ TMA
+        // ------------------------------------------------------------------ TMA, scores
         if (lane == 0 && ntile > 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&qhmap) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&latmap) : "memory");
-            const int yq = b * a.R + q0, yc = b * a.cap;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&qlmap) : "memory");
+            const int yq = b * a.R + q0;
             const int latoms = a.kvl / 64;
             int item = 0;
-            for (int j = 0; j <= ntile && !failed; j++) {
-                for (int at = 0; j < ntile && at < a.qa && !failed; at++, item++) {
-                    const int st = item % NS;
-                    if (!bar_wait(s_addr(&b_empty[st]), (uint32_t)(((item / NS) & 1) ^ 1))) { failed = true; break; }
-                    const uint32_t sw = s_addr(smem + (size_t)st * STAGE), full = s_addr(&b_full[st]);
-                    bar_expect(full, 3 * ATOM);
+            for (int j = 0; j < ntile && !failed; j++)
+                for (int at = 0; at < a.qa; at++, item++) {
+                    const int st = item % NSQ;
+                    if (!bar_wait(s_addr(&b_qempty[st]), (uint32_t)(((item / NSQ) & 1) ^ 1))) { failed = true; break; }
+                    const uint32_t sw = s_addr(smem + (size_t)st * QSTAGE), full = s_addr(&b_qfull[st]);
+                    bar_expect(full, QSTAGE);
                     tma2d(sw, &qhmap, at * 64, yq, full);
                     tma2d(sw + ATOM, &qlmap, at * 64, yq, full);
                     if (at < latoms) tma2d(sw + 2 * ATOM, &latmap, at * 64, yc + begin + j * NP, full);
                     else tma2d(sw + 2 * ATOM, &ropemap, 0, yc + begin + j * NP, full);
                 }
-                for (int v = 0; j >= 1 && v < va && !failed; v++, item++) {
-                    const int st = item % NS;
-                    if (!bar_wait(s_addr(&b_empty[st]), (uint32_t)(((item / NS) & 1) ^ 1))) { failed = true; break; }
-                    const uint32_t sw = s_addr(smem + (size_t)st * STAGE), full = s_addr(&b_full[st]);
-                    bar_expect(full, ATOM);
-                    tma2d(sw, &latmap, (hf * va + v) * 64, yc + begin + (j - 1) * NP, full);
-                }
-            }
             // let the copies in flight land before the CTA can exit
-            for (int k = max(0, item - NS); k < item; k++)
-                if (!bar_wait(s_addr(&b_full[k % NS]), (uint32_t)((k / NS) & 1))) failed = true;
+            for (int k = max(0, item - NSQ); k < item; k++)
+                if (!bar_wait(s_addr(&b_qfull[k % NSQ]), (uint32_t)((k / NSQ) & 1))) failed = true;
             if (failed) flag(DEV_TIMEOUT);
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------------ MMA issue
-        if (ntile > 0) {
-            const uint32_t idq = bf16_idesc(NP, false), idv = bf16_idesc(64, true);
-            const uint32_t pbase = s_addr(pbuf);
+        // ------------------------------------------------------------------ TMA, values
+        if (lane == 0 && ntile > 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&latmap) : "memory");
             int item = 0;
-            for (int j = 0; j <= ntile && !failed; j++) {
-                if (j < ntile) {
-                    const int sb = j & 1;
-                    if (!bar_wait(s_addr(&b_sfree[sb]), (uint32_t)(((j >> 1) & 1) ^ 1))) { failed = true; break; }
+            for (int i = 0; i < ntile && !failed; i++)
+                for (int vs = 0; vs < nvs; vs++, item++) {
+                    const int st = item % NSV;
+                    if (!bar_wait(s_addr(&b_vempty[st]), (uint32_t)(((item / NSV) & 1) ^ 1))) { failed = true; break; }
+                    const uint32_t sv = s_addr(smem + V_OFF + (size_t)st * VSTAGE), full = s_addr(&b_vfull[st]);
+                    bar_expect(full, (uint32_t)(vw * ATOM));
+                    for (int x = 0; x < vw; x++)
+                        tma2d(sv + x * ATOM, &latmap, (hf * va + vs * vw + x) * 64, yc + begin + i * NP, full);
+                }
+            for (int k = max(0, item - NSV); k < item; k++)
+                if (!bar_wait(s_addr(&b_vfull[k % NSV]), (uint32_t)((k / NSV) & 1))) failed = true;
+            if (failed) flag(DEV_TIMEOUT);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------------ score MMAs
+        if (ntile > 0) {
+            const uint32_t idq = bf16_idesc(NP, false);
+            int item = 0;
+            for (int j = 0; j < ntile && !failed; j++) {
+                const int sb = j & 1;
+                // the buffer's previous tile (j - 2) has left it: its value MMAs are done
+                if (!bar_wait(s_addr(&b_pvdone[sb]), (uint32_t)(((j >> 1) & 1) ^ 1))) { failed = true; break; }
+                fence_after();
+                const uint32_t s_tm = tmem + (uint32_t)(sb * NP);
+                for (int at = 0; at < a.qa; at++, item++) {
+                    const int st = item % NSQ;
+                    if (!bar_wait(s_addr(&b_qfull[st]), (uint32_t)((item / NSQ) & 1))) { failed = true; break; }
                     fence_after();
-                    const uint32_t s_tm = tmem + (uint32_t)(sb * NP);
-                    for (int at = 0; at < a.qa; at++, item++) {
-                        const int st = item % NS;
-                        if (!bar_wait(s_addr(&b_full[st]), (uint32_t)((item / NS) & 1))) { failed = true; break; }
-                        fence_after();
-                        if (lane == 0) {
-                            const uint64_t d0 = sw128_desc(s_addr(smem + (size_t)st * STAGE));
-                            const uint32_t ql = ATOM >> 4, cc = (2 * ATOM) >> 4;
+                    if (lane == 0) {
+                        const uint64_t d0 = sw128_desc(s_addr(smem + (size_t)st * QSTAGE));
+                        constexpr uint32_t ql = ATOM >> 4, cc = (2 * ATOM) >> 4;
 #pragma unroll
-                            for (int k = 0; k < 4; k++) {
-                                mma_ss(s_tm, d0 + 2 * k, d0 + cc + 2 * k, idq, (at | k) ? 1u : 0u);
-                                mma_ss(s_tm, d0 + ql + 2 * k, d0 + cc + 2 * k, idq, 1u);
-                            }
-                            mma_commit(s_addr(&b_empty[st]));
+                        for (int k = 0; k < 4; k++) {
+                            mma_ss(s_tm, d0 + 2 * k, d0 + cc + 2 * k, idq, (at | k) ? 1u : 0u);
+                            mma_ss(s_tm, d0 + ql + 2 * k, d0 + cc + 2 * k, idq, 1u);
                         }
-                        __syncwarp();
+                        mma_commit(s_addr(&b_qempty[st]));
                     }
-                    if (failed) break;
-                    if (lane == 0) mma_commit(s_addr(&b_sfull[sb]));
                     __syncwarp();
                 }
-                if (j >= 1) {
-                    const int i = j - 1;
-                    if (!bar_wait(s_addr(b_pfull), (uint32_t)(i & 1))) { failed = true; break; }
+                if (failed) break;
+                if (lane == 0) mma_commit(s_addr(&b_sfull[sb]));
+                __syncwarp();
+            }
+            if (lane == 0) {
+                mma_commit(s_addr(b_finq));
+                // every MMA of this warp has completed before TMEM can be freed
+                if (!bar_wait(s_addr(b_finq), 0)) failed = true;
+                if (failed) flag(DEV_TIMEOUT);
+            }
+        }
+    } else if (warp == 3) {
+        // ------------------------------------------------------------------ value MMAs
+        if (ntile > 0) {
+            const uint32_t idv = bf16_idesc(vw * 64, true);
+            int item = 0;
+            for (int i = 0; i < ntile && !failed; i++) {
+                const int sb = i & 1;
+                if (!bar_wait(s_addr(&b_pfull[sb]), (uint32_t)((i >> 1) & 1))) { failed = true; break; }
+                fence_after();
+                const int nv = min(NP, end - (begin + i * NP));   // rows past it lie at or past n_ctx
+                const uint32_t p_tm = tmem + (uint32_t)(sb * NP);
+                for (int vs = 0; vs < nvs; vs++, item++) {
+                    const int st = item % NSV;
+                    if (!bar_wait(s_addr(&b_vfull[st]), (uint32_t)((item / NSV) & 1))) { failed = true; break; }
                     fence_after();
-                    const int p0 = begin + i * NP;
-                    const int nv = min(NP, end - p0);      // rows past it lie at or past n_ctx
-                    for (int v = 0; v < va; v++, item++) {
-                        const int st = item % NS;
-                        if (!bar_wait(s_addr(&b_full[st]), (uint32_t)((item / NS) & 1))) { failed = true; break; }
-                        fence_after();
-                        unsigned char *sv = smem + (size_t)st * STAGE;
-                        if (nv < NP) {
-                            // the cache past n_ctx is unspecified: zero it, so 0 * row stays 0
-                            for (int x = nv * 8 + lane; x < NP * 8; x += 32)
-                                *reinterpret_cast<uint4 *>(sv + (size_t)x * 16) = make_uint4(0, 0, 0, 0);
-                            fence_async_smem();
-                            __syncwarp();
-                        }
-                        if (lane == 0) {
-                            const uint32_t d_tm = tmem + 256u + (uint32_t)(v * 64);
-                            const uint32_t vb = s_addr(sv);
-#pragma unroll
-                            for (int kk = 0; kk < NP / 16; kk++) {
-                                const uint64_t ph = sw128_desc(pbase + (uint32_t)((kk >> 2) * ATOM)) + (uint64_t)((kk & 3) * 2);
-                                const uint64_t pl = sw128_desc(pbase + (uint32_t)((2 + (kk >> 2)) * ATOM)) + (uint64_t)((kk & 3) * 2);
-                                const uint64_t vd = sw128_mn_desc(vb + (uint32_t)(kk * 2048), ATOM);
-                                mma_ss(d_tm, ph, vd, idv, (i > 0 || kk > 0) ? 1u : 0u);
-                                mma_ss(d_tm, pl, vd, idv, 1u);
-                            }
-                            mma_commit(s_addr(&b_empty[st]));
-                        }
+                    unsigned char *sv = smem + V_OFF + (size_t)st * VSTAGE;
+                    if (nv < NP) {
+                        // the cache past n_ctx is unspecified: zero it, so 0 * row stays 0
+                        for (int x = 0; x < vw; x++)
+                            for (int e = nv * 8 + lane; e < NP * 8; e += 32)
+                                *reinterpret_cast<uint4 *>(sv + (size_t)x * ATOM + (size_t)e * 16) = make_uint4(0, 0, 0, 0);
+                        fence_async_smem();
                         __syncwarp();
                     }
-                    if (failed) break;
-                    if (lane == 0) mma_commit(s_addr(b_pfree));
+                    if (lane == 0) {
+                        const uint32_t d_tm = tmem + 256u + (uint32_t)(vs * vw * 64);
+                        const uint32_t vb = s_addr(sv);
+#pragma unroll
+                        for (int kk = 0; kk < NP / 16; kk++) {
+                            // positions 16 kk.. : chunk kk / 2 of 32, hi pairs then lo pairs
+                            const uint32_t pa = p_tm + (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8);
+                            const uint64_t vd = sw128_mn_desc(vb + (uint32_t)(kk * 2048), ATOM);
+                            mma_ts(d_tm, pa, vd, idv, (i > 0 || kk > 0) ? 1u : 0u);
+                            mma_ts(d_tm, pa + 16u, vd, idv, 1u);
+                        }
+                        mma_commit(s_addr(&b_vempty[st]));
+                    }
                     __syncwarp();
                 }
+                if (failed) break;
+                if (lane == 0) mma_commit(s_addr(&b_pvdone[sb]));
+                __syncwarp();
             }
             if (lane == 0) {
                 mma_commit(s_addr(b_ofull));
-                mma_commit(s_addr(b_fin));
-                // every MMA of this CTA has completed before TMEM can be freed
-                if (!bar_wait(s_addr(b_fin), 0)) failed = true;
+                mma_commit(s_addr(b_finv));
+                if (!bar_wait(s_addr(b_finv), 0)) failed = true;
                 if (failed) flag(DEV_TIMEOUT);
             }
         }
     } else {
         // ------------------------------------------------------------------ softmax
         const int quarter = warp & 3;
+        const int half = (warp - 4) >> 2;      // which 64 positions of a tile
         const int row = quarter * 32 + lane;
         const int rg = q0 + row;
         const bool row_ok = rg < a.R;
         const int t = row_ok ? rg / a.H : 0;
         const uint64_t mk = a.mask[t];
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-        float m_run = -INFINITY, l_run = 0.0f;
-        for (int j = 0; j < ntile && !failed; j++) {
+        const float sl2 = a.scale * LOG2E;
+        const int ocols = va * 32;              // this warp's share of u's half
+        float m_run = -INFINITY, l_part = 0.0f;   // log2 units
+        // A warp whose wait gave up keeps stepping (without waiting) so that all eight reach
+        // every named barrier; the slice is then reported through the status word only.
+        for (int j = 0; j < ntile; j++) {
             const int sb = j & 1;
-            const int p0 = begin + j * NP;
-            if (!bar_wait(s_addr(&b_sfull[sb]), (uint32_t)((j >> 1) & 1))) { failed = true; break; }
+            const int p0 = begin + j * NP + half * 64;
+            if (!failed && !bar_wait(s_addr(&b_sfull[sb]), (uint32_t)((j >> 1) & 1))) failed = true;
             fence_after();
-            const uint32_t s_tm = tmem + lane_addr + (uint32_t)(sb * NP);
+            const uint32_t s_tm = tmem + lane_addr + (uint32_t)(sb * NP + half * 64);
+            uint32_t sv[64];
+            {
+                uint32_t (&v0)[16] = *reinterpret_cast<uint32_t (*)[16]>(&sv[0]);
+                uint32_t (&v1)[16] = *reinterpret_cast<uint32_t (*)[16]>(&sv[16]);
+                uint32_t (&v2)[16] = *reinterpret_cast<uint32_t (*)[16]>(&sv[32]);
+                uint32_t (&v3)[16] = *reinterpret_cast<uint32_t (*)[16]>(&sv[48]);
+                tmem_ld16(s_tm, v0);
+                tmem_ld16(s_tm + 16u, v1);
+                tmem_ld16(s_tm + 32u, v2);
+                tmem_ld16(s_tm + 48u, v3);
+                tmem_wait_ld();
+            }
             // a position is visible when it lies below end and is an old row or a new row
             // whose bit is set in the node's mask
-            const bool all_old = p0 + NP <= min(c, end);
+            const bool all_old = p0 + 64 <= min(c, end);
             auto visible = [&](int s) -> bool {
                 return s < end && (s < c || ((mk >> (s - c)) & 1ull) != 0);
             };
             float mt = -INFINITY;
-            for (int ch = 0; ch < NP / 16; ch++) {
-                uint32_t v[16];
-                tmem_ld16(s_tm + (uint32_t)(ch * 16), v);
-                tmem_wait_ld();
+            if (all_old) {
 #pragma unroll
-                for (int n = 0; n < 16; n++) {
-                    const int s = p0 + ch * 16 + n;
-                    if (all_old || visible(s)) mt = fmaxf(mt, __fmul_rn(__uint_as_float(v[n]), a.scale));
-                }
+                for (int n = 0; n < 64; n++) mt = fmaxf(mt, __uint_as_float(sv[n]));
+            } else {
+#pragma unroll
+                for (int n = 0; n < 64; n++)
+                    if (visible(p0 + n)) mt = fmaxf(mt, __uint_as_float(sv[n]));
             }
-            if (!row_ok) mt = -INFINITY;
-            // P and u belong to the previous tile's values product until it completes
-            if (!bar_wait(s_addr(b_pfree), (uint32_t)((j & 1) ^ 1))) { failed = true; break; }
-            fence_after();
-            const bool upd = mt > -INFINITY && (m_run == -INFINITY || mt > m_run + RESCALE_AT);
+            // both halves of the row agree on the tile max (scale > 0)
+            xmax[((j & 1) * 2 + half) * 128 + row] = mt;
+            asm volatile("bar.sync 1, %0;" ::"n"(NSOFT * 32) : "memory");
+            mt = fmaxf(xmax[((j & 1) * 2) * 128 + row], xmax[((j & 1) * 2 + 1) * 128 + row]);
+            const float mt2 = (row_ok && mt > -INFINITY) ? mt * sl2 : -INFINITY;
+            const bool upd = mt2 > -INFINITY && (m_run == -INFINITY || mt2 > m_run + RESCALE_AT);
             const bool resc = upd && m_run != -INFINITY;
-            const float al = resc ? __expf(m_run - mt) : 1.0f;
-            if (upd) m_run = mt;
+            const float al = resc ? ex2(m_run - mt2) : 1.0f;
+            if (upd) m_run = mt2;
             if (__any_sync(0xffffffffu, resc)) {
-                // warp-wide TMEM access: lanes whose max stayed scale by 1
-                for (int ch = 0; ch < va * 4; ch++) {
+                // u holds the value products up to tile j - 1: wait for them, then scale
+                // this warp's columns of the row (lanes whose max stayed scale by 1)
+                if (!failed && j >= 1 && !bar_wait(s_addr(&b_pvdone[(j - 1) & 1]), (uint32_t)(((j - 1) >> 1) & 1)))
+                    failed = true;
+                fence_after();
+                for (int ch = 0; ch < ocols / 16; ch++) {
                     uint32_t v[16];
-                    const uint32_t ot = tmem + lane_addr + 256u + (uint32_t)(ch * 16);
+                    const uint32_t ot = tmem + lane_addr + 256u + (uint32_t)(half * ocols + ch * 16);
                     tmem_ld16(ot, v);
                     tmem_wait_ld();
 #pragma unroll
@@ -531,63 +598,55 @@ __global__ void __launch_bounds__(THREADS, 1) attend_kernel(const __grid_constan
                 }
                 tmem_wait_st();
             }
-            if (resc) l_run *= al;
-            for (int ch = 0; ch < NP / 16; ch++) {
-                uint32_t v[16];
-                tmem_ld16(s_tm + (uint32_t)(ch * 16), v);
-                tmem_wait_ld();
-                float pv[16];
+            if (resc) l_part *= al;
+            const float mneg = -m_run;
 #pragma unroll
-                for (int n = 0; n < 16; n++) {
-                    const int s = p0 + ch * 16 + n;
-                    const bool vis = row_ok && (all_old || visible(s));
-                    pv[n] = vis ? __expf(__fmul_rn(__uint_as_float(v[n]), a.scale) - m_run) : 0.0f;
+            for (int cc = 0; cc < 2; cc++) {        // two chunks of 32 positions
+                uint32_t hw[16], lw[16];
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    const int n0 = cc * 32 + 2 * q;
+                    float x0 = 0.0f, x1 = 0.0f;
+                    const bool v0 = row_ok && (all_old || visible(p0 + n0));
+                    const bool v1 = row_ok && (all_old || visible(p0 + n0 + 1));
+                    if (v0) x0 = ex2(fmaf(__uint_as_float(sv[n0]), sl2, mneg));
+                    if (v1) x1 = ex2(fmaf(__uint_as_float(sv[n0 + 1]), sl2, mneg));
+                    l_part += x0;
+                    l_part += x1;
+                    const uint32_t h = pack_bf16x2(x0, x1);
+                    hw[q] = h;
+                    lw[q] = pack_bf16x2(__fsub_rn(x0, __uint_as_float(h << 16)),
+                                        __fsub_rn(x1, __uint_as_float(h & 0xFFFF0000u)));
                 }
-#pragma unroll
-                for (int n = 0; n < 16; n++) l_run += pv[n];
-#pragma unroll
-                for (int hh = 0; hh < 2; hh++) {
-                    uint32_t h4[4], l4[4];
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const float x0 = pv[hh * 8 + 2 * q], x1 = pv[hh * 8 + 2 * q + 1];
-                        const float h0 = __bfloat162float(__float2bfloat16_rn(x0));
-                        const float h1 = __bfloat162float(__float2bfloat16_rn(x1));
-                        h4[q] = pack_bf16x2(h0, h1);
-                        l4[q] = pack_bf16x2(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
-                    }
-                    const int kp = ch * 16 + hh * 8;                 // position within the tile
-                    const int off = (kp >> 6) * ATOM + row * 128 + ((((kp & 63) >> 3) ^ (row & 7)) << 4);
-                    *reinterpret_cast<uint4 *>(pbuf + off) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
-                    *reinterpret_cast<uint4 *>(pbuf + 2 * ATOM + off) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
-                }
+                const uint32_t pt = s_tm + (uint32_t)(cc * 32);
+                tmem_st16(pt, hw);
+                tmem_st16(pt + 16u, lw);
             }
-            fence_async_smem();
+            tmem_wait_st();
             fence_before();
             __syncwarp();
-            if (lane == 0) {
-                bar_arrive(s_addr(&b_sfree[sb]));
-                bar_arrive(s_addr(b_pfull));
-            }
+            if (lane == 0) bar_arrive(s_addr(&b_pfull[sb]));
         }
         // the row's partial state for this slice
         if (ntile > 0 && !failed) {
             if (!bar_wait(s_addr(b_ofull), 0)) failed = true;
             fence_after();
         }
+        if (half == 1) xsum[row] = l_part;
+        asm volatile("bar.sync 1, %0;" ::"n"(NSOFT * 32) : "memory");
         if (failed) {
             if (lane == 0) flag(DEV_TIMEOUT);
         } else {
             const size_t pi = ((size_t)b * a.R + (size_t)(row_ok ? rg : 0)) * a.nsplit + sp;
-            if (row_ok && hf == 0) {
-                a.pm[pi] = m_run;
-                a.pl[pi] = l_run;
+            if (row_ok && hf == 0 && half == 0) {
+                a.pm[pi] = m_run == -INFINITY ? -INFINITY : m_run * LN2;
+                a.pl[pi] = l_part + xsum[row];
             }
-            float *dst = a.pu + pi * a.kvl + hf * va * 64;
-            for (int ch = 0; ch < va * 4; ch++) {
+            float *dst = a.pu + pi * a.kvl + hf * va * 64 + half * ocols;
+            for (int ch = 0; ch < ocols / 16; ch++) {
                 uint32_t v[16];
                 if (ntile > 0) {
-                    tmem_ld16(tmem + lane_addr + 256u + (uint32_t)(ch * 16), v);
+                    tmem_ld16(tmem + lane_addr + 256u + (uint32_t)(half * ocols + ch * 16), v);
                     tmem_wait_ld();
                 } else {
 #pragma unroll
@@ -605,7 +664,7 @@ __global__ void __launch_bounds__(THREADS, 1) attend_kernel(const __grid_constan
     }
     fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 2) {
         fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
