@@ -64,19 +64,34 @@ static size_t mla_ws_layout(int B, int T, int H, int kvl, int qr, int ns, MlaWs 
     return o;
 }
 
-// grid (B*T, H), block 256: qabs[j] = sum_i W[h*kvd + i][j] * q_nope[i], i ascending
+// grid (H, ceil(B*T / QA_TT)), block 256: qabs[bt][h][j] = sum_i W[h*kvd + i][j] *
+// q_nope[bt][h][i], i ascending (one fma chain per output). A block reads its head's W_uk
+// once for QA_TT query nodes.
+constexpr int QA_TT = 16;
 __global__ void __launch_bounds__(256) mla_qabs_kernel(float *__restrict__ qabs,
                                                        const float *__restrict__ q_nope,
-                                                       const float *__restrict__ kv_b, int H,
+                                                       const float *__restrict__ kv_b, int BT, int H,
                                                        int qn, int vh, int kvl)
 {
-    const int bt = blockIdx.x, h = blockIdx.y;
+    __shared__ float sq[QA_TT][256];
+    const int h = blockIdx.x, bt0 = blockIdx.y * QA_TT;
+    const int nt = min(QA_TT, BT - bt0);
     const int kvd = qn + vh;
-    const float *q = q_nope + ((size_t)bt * H + h) * qn;
+    for (int x = threadIdx.x; x < QA_TT * qn; x += blockDim.x) {
+        const int t = x / qn, i = x % qn;
+        sq[t][i] = t < nt ? q_nope[((size_t)(bt0 + t) * H + h) * qn + i] : 0.0f;
+    }
+    __syncthreads();
     for (int j = threadIdx.x; j < kvl; j += blockDim.x) {
-        float a = 0.0f;
-        for (int i = 0; i < qn; i++) a = fmaf(kv_b[((size_t)h * kvd + i) * kvl + j], q[i], a);
-        qabs[((size_t)bt * H + h) * kvl + j] = a;
+        float acc[QA_TT];
+#pragma unroll
+        for (int t = 0; t < QA_TT; t++) acc[t] = 0.0f;
+        for (int i = 0; i < qn; i++) {
+            const float wv = kv_b[((size_t)h * kvd + i) * kvl + j];
+#pragma unroll
+            for (int t = 0; t < QA_TT; t++) acc[t] = fmaf(wv, sq[t][i], acc[t]);
+        }
+        for (int t = 0; t < nt; t++) qabs[((size_t)(bt0 + t) * H + h) * kvl + j] = acc[t];
     }
 }
 
@@ -204,48 +219,69 @@ __global__ void __launch_bounds__(MLA_THREADS) mla_attend_kernel(
     }
 }
 
-// grid (B*T, H), block 256: merge the slices, then out = W_uv[h] u
+// grid (H, ceil(B*T / CB_TT)), block 256: merge the slices of CB_TT query nodes of head h,
+// then out = W_uv[h] u (a block reads its head's W_uv once). Per output the operation order
+// is the same as one node at a time: merge weights serially, u[j] as one fma chain over
+// the slices, out[r] as 32 lane chains over j then a butterfly.
+constexpr int CB_TT = 8;
 __global__ void __launch_bounds__(256) mla_combine_kernel(float *__restrict__ out, MlaWs w,
                                                           const float *__restrict__ kv_b,
                                                           const int *__restrict__ cached, int T,
-                                                          int H, int qn, int vh, int kvl,
+                                                          int BT, int H, int qn, int vh, int kvl,
                                                           int nsplit, int split_len)
 {
-    __shared__ float su[MLA_MAXL];
-    __shared__ float sw[MLA_MAXSPLIT];
-    const int bt = blockIdx.x, h = blockIdx.y;
-    const int b = bt / T;
-    const int n_ctx = cached[b] + T;
-    const int nsu = max(0, min(nsplit, (n_ctx + split_len - 1) / split_len));
-    const size_t base = ((size_t)bt * H + h) * nsplit;
-    if (threadIdx.x == 0) {
+    __shared__ float su[CB_TT][MLA_MAXL];
+    __shared__ float sw[CB_TT][MLA_MAXSPLIT];
+    __shared__ int snu[CB_TT];
+    const int h = blockIdx.x, bt0 = blockIdx.y * CB_TT;
+    const int nt = min(CB_TT, BT - bt0);
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0 && wid < nt) {
+        const int bt = bt0 + wid;
+        const int n_ctx = cached[bt / T] + T;
+        const int nsu = max(0, min(nsplit, (n_ctx + split_len - 1) / split_len));
+        const size_t base = ((size_t)bt * H + h) * nsplit;
         float M = -INFINITY;
         for (int s = 0; s < nsu; s++) M = fmaxf(M, w.pm[base + s]);
         float Lsum = 0.0f;
         for (int s = 0; s < nsu; s++) {
             const float f = w.pm[base + s] == -INFINITY ? 0.0f : __expf(w.pm[base + s] - M);
-            sw[s] = f;
+            sw[wid][s] = f;
             Lsum += f * w.pl[base + s];
         }
         const float inv = Lsum > 0.0f ? 1.0f / Lsum : 0.0f;
-        for (int s = 0; s < nsu; s++) sw[s] *= inv;
+        for (int s = 0; s < nsu; s++) sw[wid][s] *= inv;
+        snu[wid] = nsu;
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < kvl; j += blockDim.x) {
-        float a = 0.0f;
-        for (int s = 0; s < nsu; s++) a = fmaf(sw[s], w.pu[(base + s) * kvl + j], a);
-        su[j] = a;
+    for (int t = 0; t < nt; t++) {
+        const size_t base = ((size_t)(bt0 + t) * H + h) * nsplit;
+        const int nsu = snu[t];
+        for (int j = threadIdx.x; j < kvl; j += blockDim.x) {
+            float a = 0.0f;
+            for (int s = 0; s < nsu; s++) a = fmaf(sw[t][s], w.pu[(base + s) * kvl + j], a);
+            su[t][j] = a;
+        }
     }
     __syncthreads();
     const int kvd = qn + vh;
-    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int r = wid; r < vh; r += blockDim.x / 32) {
         const float *wr = kv_b + ((size_t)h * kvd + qn + r) * kvl;
-        float a = 0.0f;
-        for (int j = lane; j < kvl; j += 32) a = fmaf(wr[j], su[j], a);
+        float a[CB_TT];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) out[((size_t)bt * H + h) * vh + r] = a;
+        for (int t = 0; t < CB_TT; t++) a[t] = 0.0f;
+        for (int j = lane; j < kvl; j += 32) {
+            const float wv = wr[j];
+#pragma unroll
+            for (int t = 0; t < CB_TT; t++) a[t] = fmaf(wv, su[t][j], a[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < CB_TT; t++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a[t] += __shfl_xor_sync(0xffffffffu, a[t], o);
+        }
+        if (lane == 0)
+            for (int t = 0; t < nt; t++) out[((size_t)(bt0 + t) * H + h) * vh + r] = a[t];
     }
 }
 
@@ -773,8 +809,8 @@ extern "C" int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *
                                           static_cast<char *>(workspace));
     if (ws_bytes < need) return K3GPU_ECAPACITY;
     cudaStream_t s = k3::as_stream(stream);
-    k3::mla_qabs_kernel<<<dim3(B * T, H), 256, 0, s>>>(w.qabs, q_nope, kv_b, H, qk_nope, v_head,
-                                                      kv_lora);
+    k3::mla_qabs_kernel<<<dim3(H, k3::ceil_div(B * T, k3::QA_TT)), 256, 0, s>>>(w.qabs, q_nope, kv_b, B * T, H,
+                                                                               qk_nope, v_head, kv_lora);
     int st = k3::launch_status();
     if (st) return st;
     int ns = ns_cc, sl = k3::MLA_SPLIT;
@@ -824,7 +860,7 @@ extern "C" int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *
             w, q_rope, lat, rope, cached, mask, T, H, qk_rope, kv_lora, cap, ns, scale);
         if ((st = k3::launch_status())) return st;
     }
-    k3::mla_combine_kernel<<<dim3(B * T, H), 256, 0, s>>>(out, w, kv_b, cached, T, H, qk_nope,
-                                                         v_head, kv_lora, ns, sl);
+    k3::mla_combine_kernel<<<dim3(H, k3::ceil_div(B * T, k3::CB_TT)), 256, 0, s>>>(
+        out, w, kv_b, cached, T, B * T, H, qk_nope, v_head, kv_lora, ns, sl);
     return k3::launch_status();
 }
