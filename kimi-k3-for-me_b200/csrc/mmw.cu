@@ -117,6 +117,7 @@ struct Args {
     int T, Np, in, out, ldy;
     int nsplit, kst;     // K splits; 64-K stages per split
     int n_units, NS, stage_bytes;
+    int dbuf;            // Np <= 128: two accumulator sets, so a unit's epilogue overlaps the next unit
 };
 
 __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constant__ CUtensorMap wmap,
@@ -128,19 +129,21 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
         return;
     }
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)a.NS * a.stage_bytes);
-    uint64_t *b_full = bars, *b_empty = bars + MAX_NS, *b_dfull = bars + 2 * MAX_NS, *b_dfree = b_dfull + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * MAX_NS + 2);
+    uint64_t *b_full = bars, *b_empty = bars + MAX_NS, *b_dfull = bars + 2 * MAX_NS, *b_dfree = b_dfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * MAX_NS + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < a.NS; s++) {
             bar_init(s_addr(&b_full[s]), 1);
             bar_init(s_addr(&b_empty[s]), 2);      // both issuers' commits
         }
-        bar_init(s_addr(b_dfull), 2);              // both issuers, end of a unit
-        bar_init(s_addr(b_dfree), 4);              // the four epilogue warps
+        for (int d = 0; d < 2; d++) {
+            bar_init(s_addr(&b_dfull[d]), 2);      // both issuers, end of a unit
+            bar_init(s_addr(&b_dfree[d]), 4);      // the four epilogue warps
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {   // 512 columns: issuer i's accumulator at column 256 i
+    if (warp == 0) {   // 512 columns: issuer i's accumulators at column 256 i (+ 128 for the second set)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -178,13 +181,14 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
         if (lane == 0) {
             const int i = warp - 1;
             const uint32_t idesc = bf16_idesc(a.Np);
-            const uint32_t dt = tmem + (uint32_t)(i * 256);
             int item = 0, unit_i = 0;
             for (int u = blockIdx.x; u < a.n_units && !failed; u += gridDim.x, unit_i++) {
                 const int ks = u % a.nsplit;
                 const int kb1 = min(nkb, (ks + 1) * a.kst);
-                // the epilogue has drained both accumulators of the previous unit
-                if (!bar_wait(s_addr(b_dfree), (uint32_t)((unit_i & 1) ^ 1))) { failed = true; break; }
+                const int db = a.dbuf ? (unit_i & 1) : 0, use = a.dbuf ? (unit_i >> 1) : unit_i;
+                const uint32_t dt = tmem + (uint32_t)(i * 256 + db * 128);
+                // the epilogue has drained this accumulator set's previous unit
+                if (!bar_wait(s_addr(&b_dfree[db]), (uint32_t)((use & 1) ^ 1))) { failed = true; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 uint32_t acc = 0;
                 for (int kb = ks * a.kst; kb < kb1; kb++, item++) {
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
                     mma_commit(s_addr(&b_empty[st]));
                 }
                 if (failed) break;
-                mma_commit(s_addr(b_dfull));
+                mma_commit(s_addr(&b_dfull[db]));
             }
             if (failed) flag(DEV_TIMEOUT);
         }
@@ -218,12 +222,14 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
         for (int u = blockIdx.x; u < a.n_units && !failed; u += gridDim.x, unit_i++) {
             const int rb = u / a.nsplit, ks = u % a.nsplit;
             const int row = rb * 128 + r;
-            if (!bar_wait(s_addr(b_dfull), (uint32_t)(unit_i & 1))) { failed = true; break; }
+            const int db = a.dbuf ? (unit_i & 1) : 0, use = a.dbuf ? (unit_i >> 1) : unit_i;
+            if (!bar_wait(s_addr(&b_dfull[db]), (uint32_t)(use & 1))) { failed = true; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t dcol = (uint32_t)(db * 128);
             for (int c0 = 0; c0 < a.Np; c0 += 16) {
                 uint32_t v0[16], v1[16];
-                tmem_ld16(tmem + lane_addr + (uint32_t)c0, v0);
-                tmem_ld16(tmem + lane_addr + 256u + (uint32_t)c0, v1);
+                tmem_ld16(tmem + lane_addr + dcol + (uint32_t)c0, v0);
+                tmem_ld16(tmem + lane_addr + 256u + dcol + (uint32_t)c0, v1);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (row < a.out) {
 #pragma unroll
@@ -239,7 +245,7 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
-            if (lane == 0) bar_arrive(s_addr(b_dfree));
+            if (lane == 0) bar_arrive(s_addr(&b_dfree[db]));
         }
         if (failed && lane == 0) flag(DEV_TIMEOUT);
     }
@@ -347,9 +353,19 @@ static Plan plan(int Tc, int in, int out, int sms)
     p.in_pad = (in + KB - 1) / KB * KB;
     p.nkb = p.in_pad / KB;
     p.rowblocks = (out + 127) / 128;
-    int want = (2 * sms + p.rowblocks - 1) / p.rowblocks;      // about two units per SM
-    want = std::max(1, std::min(want, std::min(MAX_SPLIT, p.nkb / 4 > 0 ? p.nkb / 4 : 1)));
-    p.kst = (p.nkb + want - 1) / want;
+    // K splits: minimise the busiest CTA's stages (units are handed out round-robin), with
+    // a cost per unit (accumulator drain) and, when split, the partial-sum pass
+    const int max_ns = std::max(1, std::min(MAX_SPLIT, p.nkb / 4));
+    double best = 1e300;
+    p.kst = p.nkb;
+    for (int ns = 1; ns <= max_ns; ns++) {
+        const int kst = (p.nkb + ns - 1) / ns;
+        const int nsr = (p.nkb + kst - 1) / kst;
+        const long long per_cta = ((long long)p.rowblocks * nsr + sms - 1) / sms;
+        double cost = (double)per_cta * (kst + 2.0);
+        if (nsr > 1) cost += 3.0 + (double)nsr * Tc * out * 4.0 / 2.5e6;   // stage ~ 0.45 us
+        if (cost < best - 1e-9) { best = cost; p.kst = kst; }
+    }
     p.nsplit = (p.nkb + p.kst - 1) / p.kst;                    // every split non-empty
     p.n_units = p.rowblocks * p.nsplit;
     p.xp_bytes = (size_t)2 * MAX_NP * p.in_pad * 2;
@@ -414,10 +430,11 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
         a.lo_flag = lo_flag;
         a.T = Tc; a.Np = p.Np; a.in = in; a.out = out; a.ldy = ldy;
         a.nsplit = p.nsplit; a.kst = p.kst; a.n_units = p.n_units;
+        a.dbuf = p.Np <= 128 ? 1 : 0;
         a.stage_bytes = W_BYTES + 2 * p.Np * 128;
         a.NS = std::min(MAX_NS, (200 * 1024) / a.stage_bytes);
         // at least 120 KB, so one CTA per SM: each allocates all 512 TMEM columns
-        const int smem = std::max(120 * 1024, a.NS * a.stage_bytes + (2 * MAX_NS + 2) * 8 + 16);
+        const int smem = std::max(120 * 1024, a.NS * a.stage_bytes + (2 * MAX_NS + 4) * 8 + 16);
         mmw_tc_kernel<<<std::min(p.n_units, sms), THREADS, smem, s>>>(wm, xm, a);
         if ((st = k3::launch_status())) return st;
         if (p.nsplit > 1) {
