@@ -357,6 +357,8 @@ typedef struct {
     int n_routed, n_shared, topk, moe_inter, act, renorm;
     float routed_scale, situ_b1, situ_b2;
     int latent, shared_inter;   /* the K3 MoE form (K3GpuKdaLayerW.moe): L and SI */
+    /* MLA layers (K3Cfg n_heads, q_lora, kv_lora, qk_nope, qk_rope, v_head) */
+    int mla_heads, q_lora, kv_lora, qk_nope, qk_rope, v_head;
 } K3GpuLayerCfg;
 
 /* KDA weights (K3KdaW, include/k3/k3.h): projections bf16 [out][in]; q, k, v, g: [P][E];
@@ -389,6 +391,32 @@ typedef struct {
 
 size_t k3gpu_kda_layer_workspace(const K3GpuLayerCfg *c, int B, int T);
 
+/* MLA weights (K3MlaW, include/k3/k3.h): projections bf16 [out][in]: q_a [q_lora][E],
+ * q_b [H*(qk_nope+qk_rope)][q_lora], kv_a [kv_lora+qk_rope][E], g [H*v_head][E] (NULL: no
+ * output gate), o [E][H*v_head]; norms q_a_norm [q_lora], kv_a_norm [kv_lora] fp32; kv_b
+ * [H*(qk_nope+v_head)][kv_lora] fp32 (the absorbed attention reads its key and value rows
+ * whole, widened once at load). All device pointers. */
+typedef struct {
+    const uint16_t *q_a, *q_b, *kv_a, *g, *o;
+    const float *q_a_norm, *kv_a_norm, *kv_b;
+} K3GpuMlaW;
+
+size_t k3gpu_mla_layer_workspace(const K3GpuLayerCfg *c, int B, int T, int max_ctx);
+
+/* k3_mla_cached (src/core/k3_ops.c:1115-1615; the --mla-absorb latent layout) for B
+ * sequences of T query nodes, x [B*T][E] -> out [B*T][E]: q_a, its RMSNorm, q_b; kv_a, the
+ * RMSNorm of its latent part; the new rows (latent, then the unrotated rope slot) appended
+ * to the bf16 caches lat [B][cap][kv_lora] and rope [B][cap][qk_rope] at positions
+ * cached[b] + t; absorbed attention with the node masks (k3gpu_mla_absorbed, scale
+ * (qk_nope+qk_rope)^-1/2); the sigmoid gate g x, then o. cached [B] and mask [T] are device
+ * arrays; cached[b] + T <= max_ctx <= cap. A verify sweep writes its T rows where the
+ * reference writes them; the accepted ones are already in place for a chain, and a tree's
+ * accepted path is compacted by the caller before the next sweep. */
+int k3gpu_mla_layer_verify(float *out, const float *x, const K3GpuMlaW *w, const K3GpuLayerCfg *c,
+                           uint16_t *lat, uint16_t *rope, int cap, const int *cached,
+                           const uint64_t *mask, int max_ctx, int B, int T, void *workspace,
+                           size_t ws_bytes, void *stream);
+
 /* k3_kda_layer_log (src/core/k3_ops.c:2231-2385) for B sequences of T positions:
  * x [B*T][E] -> out [B*T][E]. state [B][H][D][D] and conv_hist [B][3][P][K-1] are the
  * carried state, read only (the sweep is tentative); the log receives the operands a
@@ -412,6 +440,27 @@ int k3gpu_decoder_layer_kda_verify(float *h, float *block_residual, int *n_block
                                    float *moe_wt, const K3GpuKdaLayerW *w,
                                    const K3GpuLayerCfg *c, int layer_idx, const float *state,
                                    const float *conv_hist, const K3GpuKdaLog *log, int B, int T,
+                                   void *workspace, size_t ws_bytes, void *stream);
+
+/* An MLA + MoE decoder layer (K3LayerW with an MLA block): as K3GpuKdaLayerW with the MLA
+ * weights in place of the KDA ones. */
+typedef struct {
+    const float *attn_res_fold, *mlp_res_fold, *in_norm, *post_norm;
+    K3GpuMlaW mla;
+    const float *gate_W, *gate_bias;
+    const K3GpuExpertBank *bank;
+    const K3GpuMoeW *moe;
+} K3GpuMlaLayerW;
+
+size_t k3gpu_decoder_layer_mla_workspace(const K3GpuLayerCfg *c, int B, int T, int max_ctx);
+
+/* k3_decoder_layer_inc_log for an MLA + MoE layer: k3gpu_decoder_layer_kda_verify's steps
+ * with k3gpu_mla_layer_verify as the attention (cache arguments as there). */
+int k3gpu_decoder_layer_mla_verify(float *h, float *block_residual, int *n_blocks, int *moe_idx,
+                                   float *moe_wt, const K3GpuMlaLayerW *w,
+                                   const K3GpuLayerCfg *c, int layer_idx, uint16_t *lat,
+                                   uint16_t *rope, int cap, const int *cached,
+                                   const uint64_t *mask, int max_ctx, int B, int T,
                                    void *workspace, size_t ws_bytes, void *stream);
 
 /* ---------------------------------------------------------------- drafter ------ */

@@ -44,7 +44,8 @@ class K3GpuLayerCfg(C.Structure):
     _fields_ = [("hidden", I), ("kda_heads", I), ("kda_head_dim", I), ("conv_k", I), ("gate_lb", F),
                 ("rms_eps", F), ("attn_res_block", I), ("max_blocks", I), ("n_routed", I), ("n_shared", I),
                 ("topk", I), ("moe_inter", I), ("act", I), ("renorm", I), ("routed_scale", F), ("situ_b1", F),
-                ("situ_b2", F), ("latent", I), ("shared_inter", I)]
+                ("situ_b2", F), ("latent", I), ("shared_inter", I), ("mla_heads", I), ("q_lora", I),
+                ("kv_lora", I), ("qk_nope", I), ("qk_rope", I), ("v_head", I)]
 
 
 class K3GpuMoeCfg(C.Structure):
@@ -69,6 +70,16 @@ class K3GpuKdaLog(C.Structure):
 class K3GpuKdaLayerW(C.Structure):
     _fields_ = [("attn_res_fold", VP), ("mlp_res_fold", VP), ("in_norm", VP), ("post_norm", VP),
                 ("kda", K3GpuKdaW), ("gate_W", VP), ("gate_bias", VP), ("bank", C.POINTER(K3GpuExpertBank)),
+                ("moe", C.POINTER(K3GpuMoeW))]
+
+
+class K3GpuMlaW(C.Structure):
+    _fields_ = [(n, VP) for n in ("q_a", "q_b", "kv_a", "g", "o", "q_a_norm", "kv_a_norm", "kv_b")]
+
+
+class K3GpuMlaLayerW(C.Structure):
+    _fields_ = [("attn_res_fold", VP), ("mlp_res_fold", VP), ("in_norm", VP), ("post_norm", VP),
+                ("mla", K3GpuMlaW), ("gate_W", VP), ("gate_bias", VP), ("bank", C.POINTER(K3GpuExpertBank)),
                 ("moe", C.POINTER(K3GpuMoeW))]
 
 
@@ -113,6 +124,12 @@ _SIGS = {
     "k3gpu_decoder_layer_workspace": ([C.POINTER(K3GpuLayerCfg), I, I], SZ),
     "k3gpu_decoder_layer_kda_verify": ([VP, VP, VP, VP, VP, C.POINTER(K3GpuKdaLayerW), C.POINTER(K3GpuLayerCfg), I,
                                         VP, VP, C.POINTER(K3GpuKdaLog), I, I, VP, SZ, VP], I),
+    "k3gpu_mla_layer_workspace": ([C.POINTER(K3GpuLayerCfg), I, I, I], SZ),
+    "k3gpu_mla_layer_verify": ([VP, VP, C.POINTER(K3GpuMlaW), C.POINTER(K3GpuLayerCfg), VP, VP, I, VP, VP, I, I, I,
+                                VP, SZ, VP], I),
+    "k3gpu_decoder_layer_mla_workspace": ([C.POINTER(K3GpuLayerCfg), I, I, I], SZ),
+    "k3gpu_decoder_layer_mla_verify": ([VP, VP, VP, VP, VP, C.POINTER(K3GpuMlaLayerW), C.POINTER(K3GpuLayerCfg), I,
+                                        VP, VP, I, VP, VP, I, I, I, VP, SZ, VP], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
 }
 for _name, (_args, _res) in _SIGS.items():
@@ -428,6 +445,54 @@ def decoder_layer_kda_verify(h, block_residual, n_blocks, w: dict, bank: "Expert
                                              C.byref(lg), B, T, ptr(ws), ws.numel(), stream_ptr(stream)),
           "k3gpu_decoder_layer_kda_verify")
     return idx, wt, lt
+
+
+def mla_weights(w: dict) -> K3GpuMlaW:
+    """w: q_a, q_b, kv_a, g (or absent / None: no gate), o (bf16 bit tensors [out][in]),
+    q_a_norm, kv_a_norm, kv_b (fp32) -- CUDA tensors, kept alive by the caller."""
+    mw = K3GpuMlaW()
+    for n, _ in K3GpuMlaW._fields_:
+        setattr(mw, n, ptr(w.get(n)))
+    return mw
+
+
+def mla_layer_verify(x, w: dict, cfg: K3GpuLayerCfg, lat, rope, cached, mask, max_ctx, B, T, stream=None):
+    """k3_mla_cached (absorbed latent layout) for B sequences of T query nodes: x [B*T][E] ->
+    out [B*T][E]; the new rows are appended to lat [B][cap][kv_lora] / rope [B][cap][qk_rope]
+    (bf16 bits) at cached[b] + t. cached int32 [B], mask int64 [T] (device)."""
+    mw = mla_weights(w)
+    out = torch.empty_like(x)
+    cap = lat.shape[1]
+    ws = workspace(lib.k3gpu_mla_layer_workspace(C.byref(cfg), B, T, max_ctx), x.device)
+    check(lib.k3gpu_mla_layer_verify(ptr(out), ptr(x), C.byref(mw), C.byref(cfg), ptr(lat), ptr(rope), cap,
+                                     ptr(cached), ptr(mask), max_ctx, B, T, ptr(ws), ws.numel(), stream_ptr(stream)),
+          "k3gpu_mla_layer_verify")
+    return out
+
+
+def decoder_layer_mla_verify(h, block_residual, n_blocks, w: dict, bank: "ExpertBank", cfg: K3GpuLayerCfg,
+                             layer_idx, lat, rope, cached, mask, max_ctx, B, T, moe: dict = None, stream=None):
+    """k3_decoder_layer_inc_log for an MLA + MoE layer, in place on h [B*T][E] (cache
+    arguments as mla_layer_verify). Returns (moe idx, moe wt)."""
+    lw = K3GpuMlaLayerW()
+    for n in ("attn_res_fold", "mlp_res_fold", "in_norm", "post_norm", "gate_W", "gate_bias"):
+        setattr(lw, n, ptr(w[n]))
+    lw.mla = mla_weights(w)
+    lw.bank = C.pointer(bank.desc)
+    if moe is not None:
+        mw = moe_weights(moe, bank)
+        lw.moe = C.pointer(mw)
+    R = B * T
+    idx = torch.empty((R, cfg.topk), dtype=torch.int32, device=h.device)
+    wt = torch.empty((R, cfg.topk), dtype=torch.float32, device=h.device)
+    cap = lat.shape[1]
+    ws = workspace(lib.k3gpu_decoder_layer_mla_workspace(C.byref(cfg), B, T, max_ctx), h.device)
+    check(lib.k3gpu_decoder_layer_mla_verify(ptr(h), ptr(block_residual), ptr(n_blocks), ptr(idx), ptr(wt),
+                                             C.byref(lw), C.byref(cfg), layer_idx, ptr(lat), ptr(rope), cap,
+                                             ptr(cached), ptr(mask), max_ctx, B, T, ptr(ws), ws.numel(),
+                                             stream_ptr(stream)),
+          "k3gpu_decoder_layer_mla_verify")
+    return idx, wt
 
 
 # ----------------------------------------------------------------- norms ---------

@@ -258,3 +258,137 @@ def test_decoder_layer_with_k3_moe_form(k3):
     moe, ri = oracle_moe_k3(hin, m, bank, lay, L, I, c.topk, c.n_routed, SI, 0)
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     assert rel(h.cpu().numpy(), pref + moe) < 1e-4
+
+
+# ---------------------------------------------------------------------------- MLA --
+# k3_mla_cached (src/core/k3_ops.c:1115-1615) in the absorbed latent layout: the oracle
+# composes the double matmuls of the bf16 weights, orc_rmsnorm, the bf16 rounding of the
+# appended cache rows (this library's cache is bf16), orc_mla_absorbed with the node masks,
+# the sigmoid gate and o. Bar: rel-L2 <= 1e-4 on the output; the appended rows agree to a
+# bf16 ulp plus 1e-4 of the row scale (their inputs come from the device projection, whose
+# error is relative to the row); every other cache row untouched.
+MH, QL, QN, VH = 4, 128, 32, 32
+
+
+def mla_weights(rng, kvl, qr):
+    w = {"q_a": bf16_bits(rng.standard_normal((QL, E), dtype=np.float32) * np.float32(0.05)),
+         "q_b": bf16_bits(rng.standard_normal((MH * (QN + qr), QL), dtype=np.float32) * np.float32(0.1)),
+         "kv_a": bf16_bits(rng.standard_normal((kvl + qr, E), dtype=np.float32) * np.float32(0.05)),
+         "g": bf16_bits(rng.standard_normal((MH * VH, E), dtype=np.float32) * np.float32(0.05)),
+         "o": bf16_bits(rng.standard_normal((E, MH * VH), dtype=np.float32) * np.float32(0.1)),
+         "q_a_norm": (1 + 0.1 * rng.standard_normal(QL)).astype(np.float32),
+         "kv_a_norm": (1 + 0.1 * rng.standard_normal(kvl)).astype(np.float32),
+         "kv_b": rng.standard_normal((MH * (QN + VH), kvl), dtype=np.float32) * np.float32(0.1)}
+    return w
+
+
+def mla_cfg(k3, kvl, qr, **kw):
+    return cfg(k3, mla_heads=MH, q_lora=QL, kv_lora=kvl, qk_nope=QN, qk_rope=qr, v_head=VH, **kw)
+
+
+def bf16_round(a):
+    return O.bf16_bits_to_f32(bf16_bits(a))
+
+
+def oracle_mla_layer(x, w, lat, rope, cached, masks, kvl, qr):
+    """One sequence: x [T][E] -> out [T][E]; lat/rope [cap][.] float, updated in place."""
+    T = x.shape[0]
+    q = mmd(O.rmsnorm(mmd(x, w["q_a"]), w["q_a_norm"], EPS), w["q_b"]).reshape(T, MH, QN + qr)
+    ct = mmd(x, w["kv_a"])
+    lat[cached:cached + T] = bf16_round(O.rmsnorm(np.ascontiguousarray(ct[:, :kvl]), w["kv_a_norm"], EPS))
+    rope[cached:cached + T] = bf16_round(ct[:, kvl:])
+    acc = O.mla_absorbed(np.ascontiguousarray(q[..., :QN]), np.ascontiguousarray(q[..., QN:]), w["kv_b"], lat,
+                         rope, cached, masks, 1.0 / np.sqrt(np.float32(QN + qr)), VH).reshape(T, MH * VH)
+    g = mmd(x, w["g"])
+    acc = (acc * (1.0 / (1.0 + np.exp(-g.astype(np.float64))))).astype(np.float32)
+    return mmd(acc, w["o"])
+
+
+@pytest.mark.parametrize("kvl,qr,tree", [(512, 64, True), (128, 64, False), (128, 16, True)],
+                         ids=["k3_tree", "chain", "cudacore_rope16"])
+def test_mla_layer_verify_vs_oracle(k3, kvl, qr, tree):
+    B, T = 2, 9
+    cached = [300, 41]
+    cap = max(cached) + T + 5
+    rng = np.random.default_rng(60 + kvl + qr)
+    w = mla_weights(rng, kvl, qr)
+    x = rng.standard_normal((B * T, E), dtype=np.float32)
+    lat0 = bf16_round(rng.standard_normal((B, cap, kvl), dtype=np.float32))
+    rope0 = bf16_round(rng.standard_normal((B, cap, qr), dtype=np.float32))
+    for b in range(B):                                  # unspecified rows past the new ones
+        lat0[b, cached[b] + T:] = np.nan
+        rope0[b, cached[b] + T:] = np.nan
+    masks = O.tree_masks([-1, 0, 0, 1, 1, 2, 2, 3, 3]) if tree else O.chain_masks(T)
+    lat_d, rope_d = dev(bf16_bits(lat0).view(np.int16)), dev(bf16_bits(rope0).view(np.int16))
+    out = k3.mla_layer_verify(dev(x), to_dev(w), mla_cfg(k3, kvl, qr), lat_d, rope_d,
+                              dev(np.array(cached, np.int32)), dev(masks.view(np.int64)), cap, B, T)
+    got = out.cpu().numpy()
+    lat_g = O.bf16_bits_to_f32(lat_d.cpu().numpy().view(np.uint16))
+    rope_g = O.bf16_bits_to_f32(rope_d.cpu().numpy().view(np.uint16))
+    for b in range(B):
+        lat, rope = lat0[b].copy(), rope0[b].copy()
+        ref = oracle_mla_layer(x[b * T:(b + 1) * T], w, lat, rope, cached[b], masks, kvl, qr)
+        assert np.isfinite(got[b * T:(b + 1) * T]).all()
+        assert rel(got[b * T:(b + 1) * T], ref) < 1e-4, rel(got[b * T:(b + 1) * T], ref)
+        new = slice(cached[b], cached[b] + T)
+        for gc, rc in ((lat_g[b], lat), (rope_g[b], rope)):
+            # a bf16 ulp, plus the projection's ~1e-5 error measured on the row scale
+            np.testing.assert_allclose(gc[new], rc[new], rtol=2 ** -7, atol=1e-4 * np.abs(rc[new]).max())
+            keep = np.r_[0:cached[b]]
+            np.testing.assert_array_equal(gc[keep], rc[keep])
+            assert np.isnan(gc[cached[b] + T:]).all()
+    assert k3.device_status(0) == 0
+
+
+def test_decoder_layer_mla_verify_vs_oracle(k3):
+    """An MLA + MoE decoder layer on a block-boundary layer index (snapshot taken)."""
+    B, T, maxb = 2, 4, 4
+    R = B * T
+    kvl, qr = 512, 64
+    c = mla_cfg(k3, kvl, qr)
+    cached = [200, 33]
+    cap = max(cached) + T
+    rng = np.random.default_rng(71)
+    w = mla_weights(rng, kvl, qr)
+    for n in ("attn_res_fold", "mlp_res_fold"):
+        w[n] = rng.standard_normal(E, dtype=np.float32) * np.float32(0.05)
+    for n in ("in_norm", "post_norm"):
+        w[n] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+    w["gate_W"] = rng.standard_normal((c.n_routed, E), dtype=np.float32) * np.float32(0.2)
+    w["gate_bias"] = rng.standard_normal(c.n_routed, dtype=np.float32) * np.float32(0.01)
+    bank, lay = O.make_bank(rng, c.n_routed + c.n_shared, E, c.moe_inter, std=0.05, w13_std=0.3)
+    h0 = rng.standard_normal((R, E), dtype=np.float32)
+    br0 = rng.standard_normal((R, maxb, E), dtype=np.float32)
+    nb0 = np.array([0, 1, 2, 3, 1, 2, 0, 3], np.int32)
+    lat0 = bf16_round(rng.standard_normal((B, cap, kvl), dtype=np.float32))
+    rope0 = bf16_round(rng.standard_normal((B, cap, qr), dtype=np.float32))
+    masks = O.chain_masks(T)
+    kb = k3.ExpertBank(dev(bank), c.n_routed + c.n_shared, E, c.moe_inter)
+    h, br, nb = dev(h0), dev(br0), dev(nb0)
+    lat_d, rope_d = dev(bf16_bits(lat0).view(np.int16)), dev(bf16_bits(rope0).view(np.int16))
+    idx, _ = k3.decoder_layer_mla_verify(h, br, nb, to_dev(w), kb, c, 2, lat_d, rope_d,
+                                         dev(np.array(cached, np.int32)), dev(masks.view(np.int64)), cap, B, T)
+
+    def attn_res(fold, brr, nbr, cur):
+        out = np.empty_like(cur)
+        for t in range(R):
+            src = np.ascontiguousarray(np.concatenate([brr[t, :nbr[t]], cur[t:t + 1]]))
+            O.orc().orc_attn_res(out[t], src, fold, src.shape[0], E, EPS)
+        return out
+
+    pref = h0.copy()
+    hh = attn_res(w["attn_res_fold"], br0, nb0, pref)
+    brr, nbr = br0.copy(), nb0.copy()
+    for t in range(R):                                   # layer 2: a block boundary
+        brr[t, nbr[t]] = pref[t]
+        nbr[t] += 1
+    hin = O.rmsnorm(hh, w["in_norm"], EPS)
+    pref = np.concatenate([oracle_mla_layer(hin[b * T:(b + 1) * T], w, lat0[b].copy(), rope0[b].copy(), cached[b],
+                                            masks, kvl, qr) for b in range(B)])
+    hin = O.rmsnorm(attn_res(w["mlp_res_fold"], brr, nbr, pref), w["post_norm"], EPS)
+    ri, rw = O.router(hin, w["gate_W"], w["gate_bias"], c.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    moe = O.moe_routed(hin, ri, rw, bank, lay, E, c.moe_inter, c.topk, c.n_routed, c.n_shared, c.act)
+    assert rel(h.cpu().numpy(), pref + moe) < 1e-4
+    np.testing.assert_array_equal(nb.cpu().numpy(), nbr)
+    np.testing.assert_array_equal(br.cpu().numpy(), brr)
