@@ -457,12 +457,17 @@ def measure_rows(k3, dev, hbm, tflops_peak):
         mask = torch.tensor(masks, dtype=torch.int64, device=dev)
         ws = k3.workspace(k3.lib.k3gpu_mla_workspace(B, T, H, kvl, cap), dev)
         us = timed(lambda: k3.mla_absorbed(qnope, qrope, kvb, lat, rope, cached, mask, vh, cap,
-                                            1.0 / (qn + qr) ** 0.5, ws=ws), n=3)
+                                            1.0 / (qn + qr) ** 0.5, ws=ws), n=10)
         flop = 2.0 * B * T * H * ctx * ((kvl + qr) + kvl)
         tf = flop / (us * 1e-6) / 1e12
+        # the tcgen05 kernel issues 3.06x the algorithmic MMA work: hi and lo bf16 pieces of
+        # the queries and of P, and the score product once per half of the latent output
+        mma_factor = (4.0 * (kvl + qr) + 2.0 * kvl) / ((kvl + qr) + kvl)
         rows["mla_absorbed_c4"] = {"us": round(us, 1), "tflops": round(tf, 2), "frac_tensor": round(tf / tflops_peak, 4),
                                    "bound": "tensor", "shape": "64-node tree, 32k cache, H=64, kv_lora 512, rope 64",
-                                   "note": "CUDA-core v1 kernel"}
+                                   "mma_work_factor": round(mma_factor, 3),
+                                   "issued_frac_tensor": round(tf * mma_factor / tflops_peak, 4),
+                                   "note": "tcgen05 flash-decoding (q_abs, attend, merge kernels together)"}
     except Exception as ex:  # noqa: BLE001
         rows["mla_absorbed_c4"] = {"error": str(ex)[:200]}
 
@@ -477,6 +482,19 @@ def measure_rows(k3, dev, hbm, tflops_peak):
         rows["trunk_matmul_bf16"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 7168")
     except Exception as ex:  # noqa: BLE001
         rows["trunk_matmul_bf16"] = {"error": str(ex)[:200]}
+
+    # lm_head: T = 72 positions through the c4 vocabulary (163840 x 7168 bf16, 2.35 GB)
+    try:
+        T, n_in, n_out = 72, 7168, 163840
+        X = torch.randn((T, n_in), generator=g, device=dev)
+        W = (torch.randn((n_out, n_in), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        Y = torch.empty((T, n_out), device=dev)
+        ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
+        us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
+        rows["lm_head_bf16_c4"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 163840")
+        del W, Y
+    except Exception as ex:  # noqa: BLE001
+        rows["lm_head_bf16_c4"] = {"error": str(ex)[:200]}
 
     # greedy accept over the K3 vocabulary: 8 sequences x 9 positions x 163840
     try:

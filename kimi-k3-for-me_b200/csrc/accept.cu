@@ -5,13 +5,17 @@
 // argmax follows the reference's argmax_ (src/cli/k3_run.c:138-139): a sequential scan
 // with strict '>' from index 0, i.e. the first index of the maximum over non-NaN values,
 // and index 0 whenever v[0] is NaN (nothing then compares greater than it).
+#include <cooperative_groups.h>
 #include <math.h>
 
 #include "common.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace k3 {
 
-constexpr int AM_THREADS = 1024;   // a verify sweep has few rows: wide CTAs, 16-byte loads
+constexpr int AM_THREADS = 512;
+constexpr int AM_CLUSTER = 8;      // CTAs per row: a verify sweep has too few rows to fill the GPU
 
 __device__ __forceinline__ bool better(float ov, int oi, float bv, int bi)
 {
@@ -20,58 +24,80 @@ __device__ __forceinline__ bool better(float ov, int oi, float bv, int bi)
     return ov > bv || (ov == bv && oi < bi);
 }
 
-// grid (rows), block 1024: arg[row] = argmax of logits[row][0..vocab). Each thread scans
-// its elements in ascending order with strict '>', so within a thread the first index of
-// its maximum wins; across threads ties go to the smaller index -- together the first
-// index of the row maximum over non-NaN values, as the sequential scan finds it.
-__global__ void __launch_bounds__(AM_THREADS) argmax_kernel(int *__restrict__ arg,
-                                                            const float *__restrict__ logits,
-                                                            int vocab)
+__device__ __forceinline__ void warp_best(float &v, int &b)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, b, o);
+        if (better(ov, oi, v, b)) { v = ov; b = oi; }
+    }
+}
+
+// grid (AM_CLUSTER, min(rows, 65535)), clusters of AM_CLUSTER CTAs along x, block 512:
+// arg[row] = argmax of logits[row][0..vocab). CTA r of a cluster scans chunk r of the row,
+// each thread its elements in ascending order with strict '>', so within a thread the
+// first index of its maximum wins; across threads and chunks ties go to the smaller index
+// -- together the first index of the row maximum over non-NaN values, as the sequential
+// scan finds it. Rank 0 merges the chunks' bests through distributed shared memory.
+__global__ void __cluster_dims__(AM_CLUSTER, 1, 1) __launch_bounds__(AM_THREADS)
+    argmax_kernel(int *__restrict__ arg, const float *__restrict__ logits, int vocab, long long rows)
 {
     __shared__ float sv[AM_THREADS / 32];
     __shared__ int si[AM_THREADS / 32];
-    const size_t row = blockIdx.x;
-    const float *l = logits + row * (size_t)vocab;
-    float bv = -INFINITY;
-    int bi = -1;
-    auto take = [&](float x, int i) {
-        if (x == x && (bi < 0 || x > bv)) { bv = x; bi = i; }   // NaN never a candidate
-    };
-    if ((vocab & 3) == 0 && (reinterpret_cast<uintptr_t>(l) & 15u) == 0) {
-        const float4 *l4 = reinterpret_cast<const float4 *>(l);
-        for (int j = threadIdx.x; j < vocab / 4; j += AM_THREADS) {
-            const float4 x = __ldg(l4 + j);
-            take(x.x, 4 * j);
-            take(x.y, 4 * j + 1);
-            take(x.z, 4 * j + 2);
-            take(x.w, 4 * j + 3);
+    __shared__ float cv;
+    __shared__ int ci;
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank();
+    for (long long row = blockIdx.y; row < rows; row += gridDim.y) {   // uniform over the cluster
+        const float *l = logits + (size_t)row * (size_t)vocab;
+        float bv = -INFINITY;
+        int bi = -1;
+        auto take = [&](float x, int i) {
+            if (x == x && (bi < 0 || x > bv)) { bv = x; bi = i; }   // NaN never a candidate
+        };
+        if ((vocab & 3) == 0 && (reinterpret_cast<uintptr_t>(l) & 15u) == 0) {
+            const float4 *l4 = reinterpret_cast<const float4 *>(l);
+            const int n4 = vocab / 4, per = (n4 + AM_CLUSTER - 1) / AM_CLUSTER;
+            const int j1 = min(n4, (rank + 1) * per);
+            for (int j = rank * per + (int)threadIdx.x; j < j1; j += AM_THREADS) {
+                const float4 x = __ldg(l4 + j);
+                take(x.x, 4 * j);
+                take(x.y, 4 * j + 1);
+                take(x.z, 4 * j + 2);
+                take(x.w, 4 * j + 3);
+            }
+        } else {
+            const int per = (vocab + AM_CLUSTER - 1) / AM_CLUSTER;
+            const int i1 = min(vocab, (rank + 1) * per);
+            for (int i = rank * per + (int)threadIdx.x; i < i1; i += AM_THREADS) take(l[i], i);
         }
-    } else {
-        for (int i = threadIdx.x; i < vocab; i += AM_THREADS) take(l[i], i);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-    }
-    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = sv[threadIdx.x];
-        int b = si[threadIdx.x];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, b, o);
-            if (better(ov, oi, v, b)) { v = ov; b = oi; }
+        warp_best(bv, bi);
+        if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float v = threadIdx.x < AM_THREADS / 32 ? sv[threadIdx.x] : -INFINITY;
+            int b = threadIdx.x < AM_THREADS / 32 ? si[threadIdx.x] : -1;
+            warp_best(v, b);
+            if (threadIdx.x == 0) { cv = v; ci = b; }
         }
-        if (threadIdx.x == 0) {
-            // the sequential scan keeps index 0 if l[0] is NaN (no value compares greater)
-            // and when every value is NaN
-            if (l[0] != l[0] || b < 0) b = 0;
-            arg[row] = b;
+        cl.sync();
+        if (rank == 0 && threadIdx.x < 32) {
+            float v = -INFINITY;
+            int b = -1;
+            if (threadIdx.x < AM_CLUSTER) {
+                v = *cl.map_shared_rank(&cv, threadIdx.x);
+                b = *cl.map_shared_rank(&ci, threadIdx.x);
+            }
+            warp_best(v, b);
+            if (threadIdx.x == 0) {
+                // the sequential scan keeps index 0 if l[0] is NaN (no value compares greater)
+                // and when every value is NaN
+                if (l[0] != l[0] || b < 0) b = 0;
+                arg[row] = b;
+            }
         }
+        cl.sync();   // the chunks' bests stay readable until rank 0 has merged them
     }
 }
 
@@ -308,8 +334,9 @@ extern "C" int k3gpu_accept_greedy(int *emit, int *n_emit, int *arg, const float
     if (!emit || !n_emit || !arg || !logits || (!drafts && nd > 0)) return K3GPU_EINVAL;
     if (B <= 0 || nd < 0 || nd > 1024 || vocab <= 0) return K3GPU_EINVAL;
     cudaStream_t s = k3::as_stream(stream);
-    k3::argmax_kernel<<<(unsigned)((long long)B * (nd + 1)), k3::AM_THREADS, 0, s>>>(arg, logits,
-                                                                                    vocab);
+    const long long rows = (long long)B * (nd + 1);
+    k3::argmax_kernel<<<dim3(k3::AM_CLUSTER, (unsigned)std::min(rows, 65535LL)), k3::AM_THREADS, 0, s>>>(
+        arg, logits, vocab, rows);
     int st = k3::launch_status();
     if (st) return st;
     k3::accept_chain_kernel<<<k3::ceil_div(B, 128), 128, 0, s>>>(emit, n_emit, arg, drafts, nd_b,
@@ -324,7 +351,9 @@ extern "C" int k3gpu_accept_tree_greedy(int *emit, int *n_emit, int *path, int *
     if (!emit || !n_emit || !path || !arg || !logits || !tok || !parent) return K3GPU_EINVAL;
     if (B <= 0 || T <= 0 || T > 4096 || vocab <= 0) return K3GPU_EINVAL;
     cudaStream_t s = k3::as_stream(stream);
-    k3::argmax_kernel<<<(unsigned)((long long)B * T), k3::AM_THREADS, 0, s>>>(arg, logits, vocab);
+    const long long rows = (long long)B * T;
+    k3::argmax_kernel<<<dim3(k3::AM_CLUSTER, (unsigned)std::min(rows, 65535LL)), k3::AM_THREADS, 0, s>>>(
+        arg, logits, vocab, rows);
     int st = k3::launch_status();
     if (st) return st;
     k3::accept_tree_kernel<<<k3::ceil_div(B, 128), 128, 0, s>>>(emit, n_emit, path, arg, tok,

@@ -422,6 +422,30 @@ def test_accept_greedy_every_acceptance_count(k3):
         np.testing.assert_array_equal(arg[b], a)
 
 
+@pytest.mark.parametrize("V", [163840, 1001, 5], ids=["c4_vocab", "ragged", "tiny"])
+def test_argmax_ties_nans_and_chunk_edges(k3, V):
+    """The row is scanned by several CTAs in chunks: ties that straddle chunk edges, NaN at
+    index 0 (the sequential scan keeps 0), NaNs elsewhere, an all-NaN row, and vocab sizes
+    with empty chunks or no 16-byte path must all give the reference's argmax_."""
+    rows = 7
+    rng = np.random.default_rng(V)
+    lg = rng.standard_normal((rows, V), dtype=np.float32)
+    per = -(-V // 8)                       # chunk width of the 8-CTA split (elements)
+    top = np.float32(50.0)
+    lg[0, [V - 1, min(per, V - 1), 0]] = top            # tie: index 0 must win
+    if V > 2:
+        lg[1, [V - 2, V - 1]] = top                     # tie inside the last chunk
+    lg[2, 0] = np.nan                                   # NaN first: index 0
+    lg[3, 1::2] = np.nan                                # scattered NaNs
+    lg[4, :] = np.nan                                   # all NaN: index 0
+    lg[5, -1] = top                                     # maximum at the very end
+    lg[6, :] = top                                      # all equal: index 0
+    emit, n_emit, arg = k3.accept_greedy(dev(lg.reshape(1, rows, V)), dev(np.zeros((1, rows - 1), np.int32)))
+    got = host(arg).reshape(-1)
+    want = [O.orc().orc_argmax(np.ascontiguousarray(lg[r]), V) for r in range(rows)]
+    np.testing.assert_array_equal(got, want)
+
+
 def test_accept_tree_greedy_vs_oracle(k3):
     # 64-node tree, branching 4, depth 3 (+ root): BASELINE config 4's draft tree shape
     parent = [-1]
