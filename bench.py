@@ -389,7 +389,7 @@ def run_ep(args, k3, rank, world, dev):
     return 0
 
 
-def measure_rows(k3, dev, hbm, tflops_peak):
+def measure_rows(k3, dev, hbm, tflops_peak, only=None):
     """The other SURVEY 8(a) rows at their BASELINE shapes, device-timed (CUDA events, 3
     warm-up and 10 timed calls, synthetic seeded inputs), with the bound each is graded
     against. A row that fails reports its error instead of a number."""
@@ -416,95 +416,100 @@ def measure_rows(k3, dev, hbm, tflops_peak):
                 "bound": "hbm", "shape": shape}
 
     # c3 KDA verify + commit: 8 sequences x (1+k = 9), 32 heads x 128
-    try:
-        B, T, H, D = 8, 9, 32, 128
-        st = torch.randn((B, H, D, D), generator=g, device=dev) * 0.1
-        q = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
-        kk = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
-        v = torch.randn((B, T, H, D), generator=g, device=dev)
-        al = 0.9 + 0.099 * torch.rand((B, T, H, D), generator=g, device=dev)
-        be = torch.sigmoid(torch.randn((B, T, H), generator=g, device=dev))
-        qs = 1.0 / D ** 0.5
-        us = timed(lambda: k3.kda_verify(st, q, kk, v, al, be, qs))
-        nbytes = st.numel() * 4 + 4 * q.numel() * 4 + be.numel() * 4 + q.numel() * 4
-        rows["kda_verify_c3"] = hbm_row(us, nbytes, "B=8 T=9 H=32 D=128")
-        n = torch.full((B,), 5, dtype=torch.int32, device=dev)
-        sc = st.clone()
-        us = timed(lambda: k3.kda_commit(sc, kk, v, al, be, n))
-        rows["kda_commit_c3"] = hbm_row(us, 2 * st.numel() * 4 + 3 * q.numel() * 4 + be.numel() * 4,
-                                        "B=8 T=9 H=32 D=128, keep 5")
-    except Exception as ex:  # noqa: BLE001
-        rows["kda_c3"] = {"error": str(ex)[:200]}
+    if only is None or only == "kda_c3":
+        try:
+            B, T, H, D = 8, 9, 32, 128
+            st = torch.randn((B, H, D, D), generator=g, device=dev) * 0.1
+            q = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
+            kk = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
+            v = torch.randn((B, T, H, D), generator=g, device=dev)
+            al = 0.9 + 0.099 * torch.rand((B, T, H, D), generator=g, device=dev)
+            be = torch.sigmoid(torch.randn((B, T, H), generator=g, device=dev))
+            qs = 1.0 / D ** 0.5
+            us = timed(lambda: k3.kda_verify(st, q, kk, v, al, be, qs))
+            nbytes = st.numel() * 4 + 4 * q.numel() * 4 + be.numel() * 4 + q.numel() * 4
+            rows["kda_verify_c3"] = hbm_row(us, nbytes, "B=8 T=9 H=32 D=128")
+            n = torch.full((B,), 5, dtype=torch.int32, device=dev)
+            sc = st.clone()
+            us = timed(lambda: k3.kda_commit(sc, kk, v, al, be, n))
+            rows["kda_commit_c3"] = hbm_row(us, 2 * st.numel() * 4 + 3 * q.numel() * 4 + be.numel() * 4,
+                                            "B=8 T=9 H=32 D=128, keep 5")
+        except Exception as ex:  # noqa: BLE001
+            rows["kda_c3"] = {"error": str(ex)[:200]}
 
     # c4 MLA absorbed: 64-node tree (branching 4) over a 32k bf16 latent cache, 64 heads
-    try:
-        B, T, H, qn, qr, vh, kvl, ctx = 1, 64, 64, 128, 64, 128, 512, 32768
-        cap = ctx + T
-        qnope = torch.randn((B, T, H, qn), generator=g, device=dev)
-        qrope = torch.randn((B, T, H, qr), generator=g, device=dev)
-        kvb = torch.randn((H * (qn + vh), kvl), generator=g, device=dev) * 0.05
-        lat = torch.randn((B, cap, kvl), generator=g, device=dev).to(torch.bfloat16).view(torch.int16)
-        rope = torch.randn((B, cap, qr), generator=g, device=dev).to(torch.bfloat16).view(torch.int16)
-        cached = torch.tensor([ctx], dtype=torch.int32, device=dev)
-        parent = [-1] + [(i - 1) // 4 for i in range(1, T)]
-        masks = []
-        for i in range(T):                          # ancestor bitmask of node i (itself included)
-            m, j = 0, i
-            while j >= 0:
-                m |= 1 << j
-                j = parent[j]
-            masks.append(m - (1 << 64) if m >= (1 << 63) else m)
-        mask = torch.tensor(masks, dtype=torch.int64, device=dev)
-        ws = k3.workspace(k3.lib.k3gpu_mla_workspace(B, T, H, kvl, cap), dev)
-        us = timed(lambda: k3.mla_absorbed(qnope, qrope, kvb, lat, rope, cached, mask, vh, cap,
-                                            1.0 / (qn + qr) ** 0.5, ws=ws), n=10)
-        flop = 2.0 * B * T * H * ctx * ((kvl + qr) + kvl)
-        tf = flop / (us * 1e-6) / 1e12
-        # the tcgen05 kernel issues 3.06x the algorithmic MMA work: hi and lo bf16 pieces of
-        # the queries and of P, and the score product once per half of the latent output
-        mma_factor = (4.0 * (kvl + qr) + 2.0 * kvl) / ((kvl + qr) + kvl)
-        rows["mla_absorbed_c4"] = {"us": round(us, 1), "tflops": round(tf, 2), "frac_tensor": round(tf / tflops_peak, 4),
-                                   "bound": "tensor", "shape": "64-node tree, 32k cache, H=64, kv_lora 512, rope 64",
-                                   "mma_work_factor": round(mma_factor, 3),
-                                   "issued_frac_tensor": round(tf * mma_factor / tflops_peak, 4),
-                                   "note": "tcgen05 flash-decoding (q_abs, attend, merge kernels together)"}
-    except Exception as ex:  # noqa: BLE001
-        rows["mla_absorbed_c4"] = {"error": str(ex)[:200]}
+    if only is None or only == "mla_absorbed_c4":
+        try:
+            B, T, H, qn, qr, vh, kvl, ctx = 1, 64, 64, 128, 64, 128, 512, 32768
+            cap = ctx + T
+            qnope = torch.randn((B, T, H, qn), generator=g, device=dev)
+            qrope = torch.randn((B, T, H, qr), generator=g, device=dev)
+            kvb = torch.randn((H * (qn + vh), kvl), generator=g, device=dev) * 0.05
+            lat = torch.randn((B, cap, kvl), generator=g, device=dev).to(torch.bfloat16).view(torch.int16)
+            rope = torch.randn((B, cap, qr), generator=g, device=dev).to(torch.bfloat16).view(torch.int16)
+            cached = torch.tensor([ctx], dtype=torch.int32, device=dev)
+            parent = [-1] + [(i - 1) // 4 for i in range(1, T)]
+            masks = []
+            for i in range(T):                          # ancestor bitmask of node i (itself included)
+                m, j = 0, i
+                while j >= 0:
+                    m |= 1 << j
+                    j = parent[j]
+                masks.append(m - (1 << 64) if m >= (1 << 63) else m)
+            mask = torch.tensor(masks, dtype=torch.int64, device=dev)
+            ws = k3.workspace(k3.lib.k3gpu_mla_workspace(B, T, H, kvl, cap), dev)
+            us = timed(lambda: k3.mla_absorbed(qnope, qrope, kvb, lat, rope, cached, mask, vh, cap,
+                                                1.0 / (qn + qr) ** 0.5, ws=ws), n=10)
+            flop = 2.0 * B * T * H * ctx * ((kvl + qr) + kvl)
+            tf = flop / (us * 1e-6) / 1e12
+            # the tcgen05 kernel issues 3.06x the algorithmic MMA work: hi and lo bf16 pieces of
+            # the queries and of P, and the score product once per half of the latent output
+            mma_factor = (4.0 * (kvl + qr) + 2.0 * kvl) / ((kvl + qr) + kvl)
+            rows["mla_absorbed_c4"] = {"us": round(us, 1), "tflops": round(tf, 2), "frac_tensor": round(tf / tflops_peak, 4),
+                                       "bound": "tensor", "shape": "64-node tree, 32k cache, H=64, kv_lora 512, rope 64",
+                                       "mma_work_factor": round(mma_factor, 3),
+                                       "issued_frac_tensor": round(tf * mma_factor / tflops_peak, 4),
+                                       "note": "tcgen05 flash-decoding (q_abs, attend, merge kernels together)"}
+        except Exception as ex:  # noqa: BLE001
+            rows["mla_absorbed_c4"] = {"error": str(ex)[:200]}
 
     # trunk projection: T = 72 positions through a 7168 x 7168 bf16 matrix (tcgen05)
-    try:
-        T, n_in, n_out = 72, 7168, 7168
-        X = torch.randn((T, n_in), generator=g, device=dev)
-        W = (torch.randn((n_out, n_in), generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        Y = torch.empty((T, n_out), device=dev)
-        ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
-        us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
-        rows["trunk_matmul_bf16"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 7168")
-    except Exception as ex:  # noqa: BLE001
-        rows["trunk_matmul_bf16"] = {"error": str(ex)[:200]}
+    if only is None or only == "trunk_matmul_bf16":
+        try:
+            T, n_in, n_out = 72, 7168, 7168
+            X = torch.randn((T, n_in), generator=g, device=dev)
+            W = (torch.randn((n_out, n_in), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            Y = torch.empty((T, n_out), device=dev)
+            ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
+            us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
+            rows["trunk_matmul_bf16"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 7168")
+        except Exception as ex:  # noqa: BLE001
+            rows["trunk_matmul_bf16"] = {"error": str(ex)[:200]}
 
     # lm_head: T = 72 positions through the c4 vocabulary (163840 x 7168 bf16, 2.35 GB)
-    try:
-        T, n_in, n_out = 72, 7168, 163840
-        X = torch.randn((T, n_in), generator=g, device=dev)
-        W = (torch.randn((n_out, n_in), generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        Y = torch.empty((T, n_out), device=dev)
-        ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
-        us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
-        rows["lm_head_bf16_c4"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 163840")
-        del W, Y
-    except Exception as ex:  # noqa: BLE001
-        rows["lm_head_bf16_c4"] = {"error": str(ex)[:200]}
+    if only is None or only == "lm_head_bf16_c4":
+        try:
+            T, n_in, n_out = 72, 7168, 163840
+            X = torch.randn((T, n_in), generator=g, device=dev)
+            W = (torch.randn((n_out, n_in), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            Y = torch.empty((T, n_out), device=dev)
+            ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
+            us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
+            rows["lm_head_bf16_c4"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 163840")
+            del W, Y
+        except Exception as ex:  # noqa: BLE001
+            rows["lm_head_bf16_c4"] = {"error": str(ex)[:200]}
 
     # greedy accept over the K3 vocabulary: 8 sequences x 9 positions x 163840
-    try:
-        B, T, V = 8, 9, 163840
-        lg = torch.randn((B, T, V), generator=g, device=dev)
-        d = lg[:, :T - 1].argmax(dim=2).to(torch.int32)
-        us = timed(lambda: k3.accept_greedy(lg, d))
-        rows["accept_greedy_vocab"] = hbm_row(us, lg.numel() * 4, "B=8 T=9 vocab=163840")
-    except Exception as ex:  # noqa: BLE001
-        rows["accept_greedy_vocab"] = {"error": str(ex)[:200]}
+    if only is None or only == "accept_greedy_vocab":
+        try:
+            B, T, V = 8, 9, 163840
+            lg = torch.randn((B, T, V), generator=g, device=dev)
+            d = lg[:, :T - 1].argmax(dim=2).to(torch.int32)
+            us = timed(lambda: k3.accept_greedy(lg, d))
+            rows["accept_greedy_vocab"] = hbm_row(us, lg.numel() * 4, "B=8 T=9 vocab=163840")
+        except Exception as ex:  # noqa: BLE001
+            rows["accept_greedy_vocab"] = {"error": str(ex)[:200]}
     return rows
 
 
@@ -674,6 +679,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-rows", action="store_true", help="skip the other rows' kernel timings")
     ap.add_argument("--no-tc", action="store_true", help="skip the bank scan: mma.sync expert kernels only")
+    ap.add_argument("--only-row", default=None,
+                    choices=["kda_c3", "mla_absorbed_c4", "trunk_matmul_bf16", "lm_head_bf16_c4", "accept_greedy_vocab"],
+                    help="time one of the other rows alone and print it (for profiling captures)")
     ap.add_argument("--n-routed", type=int, default=N_ROUTED,
                     help="routed experts (smaller values give small cases for ncu captures)")
     args = ap.parse_args()
@@ -682,6 +690,11 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.only_row:
+        k3 = load_pkg()
+        hbm, _ = peaks()
+        print(json.dumps(measure_rows(k3, "cuda", hbm, peaks_tensor(), only=args.only_row)))
+        return 0
     return run_b200(args)
 
 
