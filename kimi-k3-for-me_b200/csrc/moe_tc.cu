@@ -10,9 +10,9 @@
 //             the group's power of two 2^(S-127) as an f16 (exact for 104 <= S <= 140, which
 //             bank_scan certifies per expert), tcgen05.st into a TMEM A buffer
 //   MMA       four issuer warps, one K quarter of the stage each: tcgen05.mma kind::f16,
-//             A from TMEM (128 rows x 16 K), B from shared memory (K x 16 tokens), fp32
-//             accumulator in TMEM, one per issuer; hi and lo halves of the activations
-//             accumulate into the same D
+//             A from TMEM (128 rows x 16 K), B from shared memory (K x the pass's 8 token
+//             rows, then their 8 lo halves: one N = 16 MMA gives both), fp32 accumulator in
+//             TMEM, one per issuer
 //   epilogue  four warps: tcgen05.ld of the four stage partials, fp32 sum, row exponent,
 //             activation (gate/up) or the contribution store (down)
 //
@@ -21,7 +21,9 @@
 // TMEM is freed on every exit path. No TMA multicast anywhere.
 //
 // Units: gate/up = 64 rows of w1 (TMEM lanes 0..63) and the same 64 rows of w3 (lanes
-// 64..127) of one expert; down = 128 rows of w2. Up to 16 tokens per pass (MMA N = 16).
+// 64..127) of one expert; down = 128 rows of w2. Up to 8 tokens per pass: a verify step
+// gives most experts one to three, and the half-height activation tile leaves room for a
+// fourth stage of weights in flight.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -38,26 +40,29 @@ constexpr int TC_MMA_WARP0 = 13;         // warps 13..16: MMA issuers, one K qua
 constexpr int TC_NMMA = 4;
 constexpr int TC_THREADS = (TC_MMA_WARP0 + TC_NMMA) * 32;
 constexpr int TC_KC = 512;               // K elements per shared-memory stage
-constexpr int TC_N = 16;                 // tokens per pass (MMA N)
+constexpr int TC_NP = 8;                 // tokens per pass
+constexpr int TC_N = 2 * TC_NP;          // MMA N: the pass's 8 hi rows, then their 8 lo rows
 constexpr int TC_W_BYTES = 128 * 256;    // packed weights of a stage (32 KB)
 constexpr int TC_S_BYTES = 128 * 16;     // E8M0 bytes of a stage
-constexpr int TC_B_BYTES = (TC_KC / 64) * TC_N * 128;   // 16 KB: 8 atoms x 16 rows x 128 B
+constexpr int TC_B_BYTES = (TC_KC / 64) * TC_NP * 128;  // 8 KB: one piece, 8 atoms x 8 rows x 128 B
 constexpr int TC_STAGE = TC_W_BYTES + TC_S_BYTES + 2 * TC_B_BYTES + 1024 - TC_S_BYTES % 1024;
-constexpr int TC_NS = 3;
-constexpr int TC_NA = 3;                 // most TMEM A buffers (128 columns = 256 K each)
-constexpr int TC_ATOM = 2 * TC_N * 128;  // a B atom pair in shared memory: 64 K x 16 hi rows, then the lo rows
-// TMEM per phase. Gate/up (lo halves rare): three A buffers, a 16-column D per issuer.
-// Down (its fp32 inputs nearly always need the lo half): one N = 32 MMA takes the hi and
-// lo rows of an atom pair together (half the issues), so a D per issuer is 32 columns and
-// two A buffers leave room for the double-buffered partials.
+// Four stages: the weight bytes in flight per SM, not any unit's rate, set the stream's
+// pace (at the loaded latency of ~3.4 us, 3 x 32 KB of weights allow ~30 GB/s per SM)
+constexpr int TC_NS = 4;
+constexpr int TC_NA = 3;                 // TMEM A buffers (128 columns = 256 K each)
+// a B atom pair in shared memory: 64 K x 8 hi rows, then the same 8 rows' lo halves, so
+// one N = 16 MMA (SBO = 1024 between the two 8-row groups) yields the hi products in D
+// columns 0..7 and the lo products in 8..15; without lo halves columns 8..15 are unused
+constexpr int TC_ATOM = 2 * TC_NP * 128;
+// TMEM: two stage-partial sets of four 16-column D (one per issuer), three A buffers
 template <int PHASE> struct TcTmem {
-    static constexpr int NA = PHASE ? 2 : 3;
-    static constexpr int PW = PHASE ? 2 * TC_N : TC_N;      // D columns per issuer
+    static constexpr int NA = TC_NA;
+    static constexpr int PW = TC_N;                         // D columns per issuer
     static constexpr int PCOLS = TC_NMMA * PW;              // one stage-partial set
     static constexpr int ACOL0 = 2 * PCOLS;                 // first A column
     static_assert(ACOL0 + NA * 128 <= 512, "TMEM columns");
 };
-constexpr int TC_XCH_BYTES = 64 * TC_N * 4;   // gate/up exchange in the epilogue
+constexpr int TC_XCH_BYTES = 64 * TC_NP * 4;   // gate/up exchange in the epilogue
 // barriers: full[NS] empty[NS] aready[NA] afree[NA] pfree[2] (stage partials)
 constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 2;
 constexpr int TC_TAB = 1024;             // active-expert table entries kept in shared memory
@@ -269,8 +274,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
             if (ent.w & 2) continue;                                                         \
             const int e = ent.x, ub = u % ta.UE, nt = ent.y, q0 = ent.z;                      \
             const bool lo_any = (ent.w & 1) != 0;                                            \
-            for (int tb = 0; tb < nt && !failed; tb += TC_N, unit_i++) {                     \
-                const int npt = min(TC_N, nt - tb);                                          \
+            for (int tb = 0; tb < nt && !failed; tb += TC_NP, unit_i++) {                    \
+                const int npt = min(TC_NP, nt - tb);                                         \
                 __VA_ARGS__                                                                  \
             }                                                                                \
         }                                                                                    \
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
                     // never read back; out-of-range rows are filled with zeros)
                     for (int a = 0; a < TC_KC / 64; a++) {
                         tma2d(s_addr(sbh + a * TC_ATOM), &bhmap, kc * TC_KC + a * 64, q0 + tb, full);
-                        if (lo_any) tma2d(s_addr(sbh + a * TC_ATOM + TC_N * 128), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
+                        if (lo_any) tma2d(s_addr(sbh + a * TC_ATOM + TC_NP * 128), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
                     }
                 }
             });
@@ -331,7 +336,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         // that the epilogue warps sum in fp32.
         if (lane == 0) {
             const int mi = warp - TC_MMA_WARP0, h = mi >> 1, j = mi & 1;
-            const uint32_t idesc = f16_idesc(TC_N), idesc2 = f16_idesc(2 * TC_N);
+            const uint32_t idesc = f16_idesc(TC_N);
             using TM = TcTmem<PHASE>;
             // this issuer's eight B offsets, in 16-byte descriptor units: the descriptor of a
             // stage's tile is built once and advanced by these (the 14-bit start field does
@@ -358,24 +363,11 @@ _Pragma("unroll")
                     const unsigned char *sw = smem + (size_t)st * TC_STAGE;
                     const uint32_t bh = s_addr(sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
                     const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * 128 + j * 64);
-                    const uint64_t dh = sw128_desc(bh), dl = sw128_desc(bh + TC_N * 128);
-                    if (!lo_any) {
+                    const uint64_t dh = sw128_desc(bh);
+                    // the atom pair's hi and lo rows as one N = 16 operand
 _Pragma("unroll")
-                        for (int t = 0; t < 8; t++)               // K16 steps of this quarter
-                            mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
-                    } else if (PHASE == 1) {
-                        // the 16 hi rows and the 16 lo rows of the atom pair as one N = 32
-                        // operand: D columns 0..15 take the hi products, 16..31 the lo
-_Pragma("unroll")
-                        for (int t = 0; t < 8; t++)
-                            mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc2, t ? 1u : 0u);
-                    } else {
-_Pragma("unroll")
-                        for (int t = 0; t < 8; t++) {
-                            mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
-                            mma_ts(dtm, atm + (uint32_t)(t * 8), dl + boff16[t], idesc, 1u);
-                        }
-                    }
+                    for (int t = 0; t < 8; t++)                   // K16 steps of this quarter
+                        mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
                     mma_commit(s_addr(&b_afree[ab]));
                     mma_commit(s_addr(&b_empty[st]));   // also tells the epilogue (no pfull commit)
                 }
@@ -450,13 +442,13 @@ _Pragma("unroll")
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         TC_FOR_UNITS({
             // the pass's per-token metadata, one token per lane, fetched before the stages
-            const int nl = lane & (TC_N - 1);
+            const int nl = lane & (TC_NP - 1);
             const bool vl = nl < npt;
             const int ex_l = vl ? Xe[q0 + tb + nl] : 0;
             const int dst_l = (PHASE == 1 && vl) ? p.pair_dst[q0 + tb + nl] : 0;
-            float acc[TC_N];
+            float acc[TC_NP];
 _Pragma("unroll")
-            for (int n = 0; n < TC_N; n++) acc[n] = 0.0f;
+            for (int n = 0; n < TC_NP; n++) acc[n] = 0.0f;
             for (int kc = 0; kc < NK && !failed; kc++, item++) {
                 const int pb = item & 1;
                 // empty[st] completes once all four issuers' MMAs of the stage are done: the
@@ -466,21 +458,8 @@ _Pragma("unroll")
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 using TM = TcTmem<PHASE>;
                 const uint32_t pt = tmem + lane_addr + (uint32_t)(pb * TM::PCOLS);
-                if (PHASE == 1 && lo_any) {
-                    // four issuers x (hi products, lo products), two issuers at a time
-                    for (int i2 = 0; i2 < TC_NMMA; i2 += 2) {
-                        uint32_t d0[16], d1[16], d2[16], d3[16];
-                        tmem_ld16(pt + i2 * TM::PW, d0);
-                        tmem_ld16(pt + i2 * TM::PW + TC_N, d1);
-                        tmem_ld16(pt + (i2 + 1) * TM::PW, d2);
-                        tmem_ld16(pt + (i2 + 1) * TM::PW + TC_N, d3);
-                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-_Pragma("unroll")
-                        for (int n = 0; n < TC_N; n++)
-                            acc[n] += (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
-                                      (__uint_as_float(d2[n]) + __uint_as_float(d3[n]));
-                    }
-                } else {
+                {
+                    // four issuers x (hi products in columns 0..7, lo products in 8..15)
                     uint32_t d0[16], d1[16], d2[16], d3[16];
                     tmem_ld16(pt, d0);
                     tmem_ld16(pt + TM::PW, d1);
@@ -488,9 +467,14 @@ _Pragma("unroll")
                     tmem_ld16(pt + 3 * TM::PW, d3);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 _Pragma("unroll")
-                    for (int n = 0; n < TC_N; n++)
-                        acc[n] += (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
+                    for (int n = 0; n < TC_NP; n++) {
+                        float v = (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
                                   (__uint_as_float(d2[n]) + __uint_as_float(d3[n]));
+                        if (lo_any)
+                            v += (__uint_as_float(d0[n + TC_NP]) + __uint_as_float(d1[n + TC_NP])) +
+                                 (__uint_as_float(d2[n + TC_NP]) + __uint_as_float(d3[n + TC_NP]));
+                        acc[n] += v;
+                    }
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
@@ -500,17 +484,17 @@ _Pragma("unroll")
             if (PHASE == 0) {
                 // lanes 64..127 hold the up rows: hand them to the gate lanes 0..63
                 if (r >= 64)
-                    for (int n = 0; n < TC_N; n++) xch[(r - 64) * TC_N + n] = acc[n];
+                    for (int n = 0; n < TC_NP; n++) xch[(r - 64) * TC_NP + n] = acc[n];
                 asm volatile("bar.sync 2, 128;" ::: "memory");
                 if (r < 64) {
-                    // n runs over all TC_N with a warp-uniform guard: acc stays in registers
+                    // n runs over all TC_NP with a warp-uniform guard: acc stays in registers
 _Pragma("unroll")
-                    for (int n = 0; n < TC_N; n++) {
+                    for (int n = 0; n < TC_NP; n++) {
                         if (n < npt) {
                             const int q = q0 + tb + n;
                             const int ex = __shfl_sync(0xffffffffu, ex_l, n);
                             const float gv = ldexpf(acc[n], ex);
-                            const float uv = ldexpf(xch[r * TC_N + n], ex);
+                            const float uv = ldexpf(xch[r * TC_NP + n], ex);
                             const float hv = act == K3GPU_ACT_SITU ? act_situ(gv, uv, b1, b2) : act_swiglu(gv, uv);
                             p.H[(size_t)q * bank.I + ub * 64 + r] = hv;
                         }
@@ -519,7 +503,7 @@ _Pragma("unroll")
                 asm volatile("bar.sync 2, 128;" ::: "memory");
             } else {
 _Pragma("unroll")
-                for (int n = 0; n < TC_N; n++) {
+                for (int n = 0; n < TC_NP; n++) {
                     if (n < npt) {
                         const int ex = __shfl_sync(0xffffffffu, ex_l, n);
                         const int dst = __shfl_sync(0xffffffffu, dst_l, n);
@@ -674,15 +658,15 @@ int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, in
                     CU_TENSOR_MAP_SWIZZLE_128B);
         if (!st) st = tc_map(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, L / 32, (long long)(bytes / (L / 32)), 16, 64,
                              CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zh, L, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zl, L, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zh, L, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zl, L, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
         st = tc_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, I / 2, (long long)(bytes / (I / 2)), 128, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B);
         if (!st) st = tc_map(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, I / 32, (long long)(bytes / (I / 32)), 16, 128,
                              CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hh, I, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hl, I, P, 64, TC_N, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hh, I, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hl, I, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (st) return st;
     int dev = 0;
