@@ -463,6 +463,46 @@ int k3gpu_decoder_layer_mla_verify(float *h, float *block_residual, int *n_block
                                    const uint64_t *mask, int max_ctx, int B, int T,
                                    void *workspace, size_t ws_bytes, void *stream);
 
+/* ------------------------------------------------------- expert parallel ------ */
+/* The routed experts of a layer split over `world` ranks, one process per GPU, the token
+ * rows exchanged through peer memory (NVLink / NVSwitch) instead of all-to-all calls:
+ * each rank cudaMallocs an exchange arena (k3gpu_ep_arena_alloc) and shares it by CUDA IPC
+ * (k3gpu_ep_ipc_handle on the owner, k3gpu_ep_ipc_open on every other rank). A step with
+ * sequence number seq (1, 2, ... the same on every rank) is, on every rank:
+ *   k3gpu_ep_dispatch  this rank's token rows to the ranks owning their experts
+ *   k3gpu_ep_receive   wait for every source; the receive region (k3gpu_ep_recv_views,
+ *                      world*cap rows, unused ones dropped) is then the input of
+ *                      k3gpu_moe_experts over this rank's n_local experts
+ *   k3gpu_ep_return    the experts' [world*cap][L] output rows back to their sources
+ *   k3gpu_ep_combine   wait for every owner; out[t] += its rows' partial sums (owner order)
+ * No host synchronisation; every wait is bounded (DEV_TIMEOUT in k3gpu_device_status, the
+ * missing peer's rows counted as empty). */
+#define K3GPU_EP_MAX_WORLD 8
+#define K3GPU_EP_HANDLE_BYTES 64
+typedef struct {
+    void *arena[K3GPU_EP_MAX_WORLD];   /* every rank's arena as mapped here; own at [rank] */
+    int world, rank;
+    int cap;                           /* most token rows a rank sends in a step */
+    int L, K, n_local;                 /* row width, top-k, experts per rank */
+} K3GpuEpGroup;
+
+size_t k3gpu_ep_arena_bytes(int world, int cap, int L, int K);
+int k3gpu_ep_arena_alloc(void **arena, size_t bytes);   /* zeroed */
+int k3gpu_ep_arena_free(void *arena);
+int k3gpu_ep_ipc_handle(const void *arena, void *handle);   /* K3GPU_EP_HANDLE_BYTES out */
+int k3gpu_ep_ipc_open(const void *handle, void **peer);
+int k3gpu_ep_ipc_close(void *peer);
+int k3gpu_ep_recv_views(const K3GpuEpGroup *g, float **x_recv, int **idx_recv, float **wt_recv);
+/* x [T][L], idx/wt [T][K] (global expert ids, -1 dropped), T <= cap; pos [world][T]
+ * (device workspace) receives each token's slot on each rank, for the combine. */
+int k3gpu_ep_dispatch(const K3GpuEpGroup *g, const float *x, const int *idx, const float *wt,
+                      int T, unsigned seq, int *pos, void *stream);
+int k3gpu_ep_receive(const K3GpuEpGroup *g, unsigned seq, void *stream);
+int k3gpu_ep_return(const K3GpuEpGroup *g, const float *part, unsigned seq, void *stream);
+/* ok [world] (device) receives 1 per owner whose rows arrived. */
+int k3gpu_ep_combine(const K3GpuEpGroup *g, float *out, const int *pos, int T, unsigned seq,
+                     int *ok, void *stream);
+
 /* ---------------------------------------------------------------- drafter ------ */
 /* Host C (no GPU): the reference's n-gram drafter, spec_draft (src/cli/k3_run.c:450-491),
  * with the n range and cap as parameters (the reference fixes n = 4 then 3 and clamps

@@ -83,6 +83,15 @@ class K3GpuMlaLayerW(C.Structure):
                 ("moe", C.POINTER(K3GpuMoeW))]
 
 
+EP_MAX_WORLD = 8
+EP_HANDLE_BYTES = 64
+
+
+class K3GpuEpGroup(C.Structure):
+    _fields_ = [("arena", VP * EP_MAX_WORLD), ("world", I), ("rank", I), ("cap", I), ("L", I), ("K", I),
+                ("n_local", I)]
+
+
 _SIGS = {
     "k3gpu_strerror": ([I], C.c_char_p),
     "k3gpu_last_cuda_error": ([], I),
@@ -130,6 +139,17 @@ _SIGS = {
     "k3gpu_decoder_layer_mla_workspace": ([C.POINTER(K3GpuLayerCfg), I, I, I], SZ),
     "k3gpu_decoder_layer_mla_verify": ([VP, VP, VP, VP, VP, C.POINTER(K3GpuMlaLayerW), C.POINTER(K3GpuLayerCfg), I,
                                         VP, VP, I, VP, VP, I, I, I, VP, SZ, VP], I),
+    "k3gpu_ep_arena_bytes": ([I, I, I, I], SZ),
+    "k3gpu_ep_arena_alloc": ([C.POINTER(VP), SZ], I),
+    "k3gpu_ep_arena_free": ([VP], I),
+    "k3gpu_ep_ipc_handle": ([VP, VP], I),
+    "k3gpu_ep_ipc_open": ([VP, C.POINTER(VP)], I),
+    "k3gpu_ep_ipc_close": ([VP], I),
+    "k3gpu_ep_recv_views": ([C.POINTER(K3GpuEpGroup), C.POINTER(VP), C.POINTER(VP), C.POINTER(VP)], I),
+    "k3gpu_ep_dispatch": ([C.POINTER(K3GpuEpGroup), VP, VP, VP, I, C.c_uint, VP, VP], I),
+    "k3gpu_ep_receive": ([C.POINTER(K3GpuEpGroup), C.c_uint, VP], I),
+    "k3gpu_ep_return": ([C.POINTER(K3GpuEpGroup), VP, C.c_uint, VP], I),
+    "k3gpu_ep_combine": ([C.POINTER(K3GpuEpGroup), VP, VP, I, C.c_uint, VP, VP], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
 }
 for _name, (_args, _res) in _SIGS.items():
@@ -235,6 +255,18 @@ def moe_experts(z, idx, wt, bank: ExpertBank, topk, n_routed, n_shared, act, b1=
                                 n_routed, n_shared, act, float(b1), float(b2), ptr(latent_norm),
                                 float(eps), ptr(ws), ws.numel(), stream_ptr(stream)),
           "k3gpu_moe_experts")
+    return out
+
+
+def moe_experts_ptrs(out, z_ptr, idx_ptr, wt_ptr, T, bank: ExpertBank, topk, n_routed, n_shared, act, b1=4.0,
+                     b2=25.0, ws=None, stream=None):
+    """k3gpu_moe_experts on raw device pointers for the inputs (e.g. a peer-exchange
+    arena's receive region); out is a [T][L] tensor."""
+    need = lib.k3gpu_moe_workspace(T, topk, n_shared, bank.L, bank.I, n_routed)
+    ws = ws if ws is not None else workspace(need, out.device)
+    check(lib.k3gpu_moe_experts(ptr(out), z_ptr, idx_ptr, wt_ptr, C.byref(bank.desc), T, topk, n_routed,
+                                n_shared, act, float(b1), float(b2), None, 1e-5, ptr(ws), ws.numel(),
+                                stream_ptr(stream)), "k3gpu_moe_experts")
     return out
 
 

@@ -18,8 +18,14 @@ each rank's own tokens is
 
 The sum over a token's experts is therefore taken per owning rank and then across ranks,
 not in top-k order as on one GPU: the results agree to fp32 rounding, not bit for bit.
-The backend is whatever the process group is (NCCL on GPUs, gloo in the CPU tests); the
-row counts make one device-to-host copy per step (the all-to-all split sizes).
+
+Two transports. `EPMoELayer` exchanges through the process group (NCCL on GPUs, gloo in
+the CPU tests): all-to-all of the row counts, one device-to-host copy of them (the split
+sizes), all-to-all of the packed rows and back. `P2PMoELayer` is the B200 path: every rank
+maps every other rank's exchange arena (CUDA IPC over NVLink / NVSwitch) and the library's
+k3gpu_ep_* kernels store rows straight into the owners' arenas and signal with
+system-scope flags (bounded waits), so a step has no collective and no host round trip;
+the process group is used once, to share the IPC handles.
 """
 from __future__ import annotations
 
@@ -132,3 +138,107 @@ class EPMoELayer:
         return out, idx, wt
 
     __call__ = forward
+
+
+class P2PMoELayer:
+    """The routed experts sharded across `group`, token rows exchanged through peer memory
+    by the library's k3gpu_ep_* kernels (no collective on the data path).
+
+    cap: the most token rows one rank sends in a step (its token count bound)."""
+
+    def __init__(self, k3, bank_local, shared_bank, gate_W, bias, n_routed, topk, act, cap, b1=4.0, b2=25.0,
+                 renorm=1, routed_scale=1.0, group=None, stream=None):
+        import ctypes as C
+        self.k3, self.C = k3, C
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if n_routed % self.world:
+            raise ValueError(f"{n_routed} routed experts do not split over {self.world} ranks")
+        if self.world > k3.EP_MAX_WORLD:
+            raise ValueError(f"at most {k3.EP_MAX_WORLD} ranks")
+        self.n_local = n_routed // self.world
+        self.topk, self.act, self.b1, self.b2 = topk, act, b1, b2
+        self.renorm, self.routed_scale = renorm, routed_scale
+        self.bank_local, self.shared_bank = bank_local, shared_bank
+        self.gate_W, self.bias, self.stream = gate_W, bias, stream
+        self.cap, self.L = cap, bank_local.L
+        lib = k3.lib
+        nbytes = lib.k3gpu_ep_arena_bytes(self.world, cap, self.L, topk)
+        arena = C.c_void_p()
+        k3.check(lib.k3gpu_ep_arena_alloc(C.byref(arena), nbytes), "k3gpu_ep_arena_alloc")
+        self.arena = arena
+        h = (C.c_uint8 * k3.EP_HANDLE_BYTES)()
+        k3.check(lib.k3gpu_ep_ipc_handle(arena, h), "k3gpu_ep_ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        g = k3.K3GpuEpGroup()
+        g.world, g.rank, g.cap, g.L, g.K, g.n_local = self.world, self.rank, cap, self.L, topk, self.n_local
+        self.peers = []
+        for r in range(self.world):
+            if r == self.rank:
+                g.arena[r] = arena.value
+                continue
+            hb = (C.c_uint8 * k3.EP_HANDLE_BYTES).from_buffer_copy(handles[r])
+            peer = C.c_void_p()
+            k3.check(lib.k3gpu_ep_ipc_open(hb, C.byref(peer)), "k3gpu_ep_ipc_open")
+            g.arena[r] = peer.value
+            self.peers.append(peer)
+        self.group_desc = g
+        xr, ir, wr = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        k3.check(lib.k3gpu_ep_recv_views(C.byref(g), C.byref(xr), C.byref(ir), C.byref(wr)), "k3gpu_ep_recv_views")
+        self.views = (xr, ir, wr)
+        dev = gate_W.device
+        self.pos = torch.empty(self.world * cap, dtype=torch.int32, device=dev)
+        self.ok = torch.empty(self.world, dtype=torch.int32, device=dev)
+        self.part = torch.empty((self.world * cap, self.L), dtype=torch.float32, device=dev)
+        self.ws = k3.workspace(lib.k3gpu_moe_workspace(self.world * cap, topk, 0, self.L, bank_local.I,
+                                                       self.n_local), dev)
+        self.seq = 0
+        # every rank's arena exists and is mapped before the first dispatch writes into it
+        dist.barrier(group=group)
+
+    def forward(self, x: torch.Tensor):
+        """x [T][L] fp32 (T <= cap) -> (out [T][L], idx, wt)."""
+        k3, C, lib = self.k3, self.C, self.k3.lib
+        T = x.shape[0]
+        if T > self.cap:
+            raise ValueError(f"{T} tokens exceed the exchange capacity {self.cap}")
+        self.seq += 1
+        seq = self.seq
+        g = C.byref(self.group_desc)
+        sp = k3.stream_ptr(self.stream)
+        idx, wt = k3.router(x, self.gate_W, self.bias, self.topk, self.renorm, self.routed_scale, stream=self.stream)
+        k3.check(lib.k3gpu_ep_dispatch(g, k3.ptr(x), k3.ptr(idx), k3.ptr(wt), T, seq, k3.ptr(self.pos), sp),
+                 "k3gpu_ep_dispatch")
+        # the shared experts on this rank's own tokens while the rows travel
+        if self.shared_bank is not None:
+            ns = self.shared_bank.n_experts
+            sidx = torch.arange(ns, device=x.device, dtype=torch.int32).repeat(T, 1)
+            swt = torch.ones((T, ns), device=x.device, dtype=torch.float32)
+            out = k3.moe_experts(x, sidx, swt, self.shared_bank, ns, ns, 0, self.act, self.b1, self.b2,
+                                 stream=self.stream)
+        else:
+            out = torch.zeros_like(x)
+        k3.check(lib.k3gpu_ep_receive(g, seq, sp), "k3gpu_ep_receive")
+        xr, ir, wr = self.views
+        k3.moe_experts_ptrs(self.part, xr, ir, wr, self.world * self.cap, self.bank_local, self.topk, self.n_local,
+                            0, self.act, self.b1, self.b2, ws=self.ws, stream=self.stream)
+        k3.check(lib.k3gpu_ep_return(g, k3.ptr(self.part), seq, sp), "k3gpu_ep_return")
+        k3.check(lib.k3gpu_ep_combine(g, k3.ptr(out), k3.ptr(self.pos), T, seq, k3.ptr(self.ok), sp),
+                 "k3gpu_ep_combine")
+        return out, idx, wt
+
+    __call__ = forward
+
+    def close(self):
+        """Unmap the peers' arenas and free this rank's (after a barrier, so no rank still
+        writes into it)."""
+        lib = self.k3.lib
+        torch.cuda.synchronize()
+        dist.barrier()
+        for p in self.peers:
+            lib.k3gpu_ep_ipc_close(p)
+        self.peers = []
+        if self.arena is not None:
+            lib.k3gpu_ep_arena_free(self.arena)
+            self.arena = None
