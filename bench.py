@@ -280,8 +280,9 @@ def load_ep():
 
 def run_ep(args, k3, rank, world, dev):
     """--gpus N: the layer with its 384 routed experts sharded 384/N per GPU (expert
-    parallel), each rank verifying its own B*(1+k) tokens (weak scaling); NCCL all-to-all
-    dispatch and combine. Times are device events per rank, the max over ranks."""
+    parallel), each rank verifying its own B*(1+k) tokens (weak scaling). The token rows
+    travel through peer memory (the library's k3gpu_ep_* kernels over NVLink; --ep-transport
+    nccl uses NCCL all-to-all instead). Times are device events per rank, the max over ranks."""
     import torch
     import torch.distributed as dist
     ep = load_ep()
@@ -299,7 +300,20 @@ def run_ep(args, k3, rank, world, dev):
     if not args.no_tc:
         n_unsafe = kb_l.scan() + kb_s.scan()
     stream = torch.cuda.current_stream()
-    layer = ep.EPMoELayer.from_k3(k3, kb_l, kb_s, gate, bias, N_ROUTED, TOPK, k3.ACT_SWIGLU, stream=stream)
+    if args.ep_transport == "p2p":
+        layer = ep.P2PMoELayer(k3, kb_l, kb_s, gate, bias, N_ROUTED, TOPK, k3.ACT_SWIGLU, cap=M, stream=stream)
+    else:
+        layer = ep.EPMoELayer.from_k3(k3, kb_l, kb_s, gate, bias, N_ROUTED, TOPK, k3.ACT_SWIGLU, stream=stream)
+    try:
+        return _run_ep_timed(args, k3, rank, world, dev, layer, x, n_local, M, n_unsafe, stream)
+    finally:
+        if hasattr(layer, "close"):
+            layer.close()
+
+
+def _run_ep_timed(args, k3, rank, world, dev, layer, x, n_local, M, n_unsafe, stream):
+    import torch
+    import torch.distributed as dist
 
     def timed(fn, steps):
         dist.barrier()
@@ -380,8 +394,10 @@ def run_ep(args, k3, rank, world, dev):
                          "peak_source": peak_kind, "note": "min over ranks, rank 0's bytes model"},
             "phase_ms_rank0_local_experts": {"plan": round(ph[1], 4), "gateup": round(ph[2], 4),
                                              "down": round(ph[3], 4), "combine": round(ph[4], 4)},
-            # router 2 + shared experts 6 + local experts 6 (+2 each for mma.sync leftovers)
-            "gpu_launches": (14 + (4 if n_unsafe else 0)) * args.steps,
+            # router 2 + shared experts 6 + local experts 6 (+2 each for mma.sync leftovers),
+            # + 8 exchange kernels on the peer-memory transport
+            "gpu_launches": (14 + (4 if n_unsafe else 0) + (8 if args.ep_transport == "p2p" else 0)) * args.steps,
+            "ep_transport": "peer memory (k3gpu_ep_*, NVLink)" if args.ep_transport == "p2p" else "NCCL all_to_all",
             "clocks": clk,
             "cpu_baseline": None,
         }
@@ -679,6 +695,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-rows", action="store_true", help="skip the other rows' kernel timings")
     ap.add_argument("--no-tc", action="store_true", help="skip the bank scan: mma.sync expert kernels only")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="--gpus N > 1: token rows through peer memory (default) or NCCL all-to-all")
     ap.add_argument("--only-row", default=None,
                     choices=["kda_c3", "mla_absorbed_c4", "trunk_matmul_bf16", "lm_head_bf16_c4", "accept_greedy_vocab"],
                     help="time one of the other rows alone and print it (for profiling captures)")
