@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark: one K3-shaped MoE layer in verify mode.
+"""Benchmark: one K3-shaped MoE layer in verify mode (benchmark configuration 2).
 
 A step is one verify pass of the layer over B*(1+k) tokens -- B sequences, each feeding
 its pending token plus k drafts -- through the library's C ABI: the sigmoid router with
@@ -260,7 +260,7 @@ def make_bank_cpu(seed):
 
 
 def workload_config(args, M):
-    return {"workload": f"K3 MoE layer verify (BASELINE config 2): B={args.B} sequences x (1+k={1 + args.k}) "
+    return {"workload": f"K3 MoE layer verify (benchmark config 2): B={args.B} sequences x (1+k={1 + args.k}) "
                         f"= {M} tokens/step/GPU",
             "d_model": L_DIM, "experts": N_ROUTED, "shared": N_SHARED, "topk": TOPK,
             "ffn": I_DIM, "act": "SwiGLU", "weights": "MXFP4 (E2M1 + E8M0/32), N(0,0.02)",
@@ -406,7 +406,7 @@ def _run_ep_timed(args, k3, rank, world, dev, layer, x, n_local, M, n_unsafe, st
 
 
 def measure_rows(k3, dev, hbm, tflops_peak, only=None):
-    """The other SURVEY 8(a) rows at their BASELINE shapes, device-timed (CUDA events, 3
+    """The other rows of the verify path at their benchmark shapes, device-timed (CUDA events, 3
     warm-up and 10 timed calls, synthetic seeded inputs), with the bound each is graded
     against. A row that fails reports its error instead of a number."""
     import torch

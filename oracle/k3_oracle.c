@@ -525,7 +525,7 @@ ORC_API void orc_attn_res(float *out, const float *src, const float *fold, int n
 /* src/cli/k3_run.c:450-491 (spec_draft): suffix n-gram, n = 4 then 3; the two most recent
  * earlier occurrences; draft the continuation of the most recent one while the second
  * agrees; stop at cap (the reference clamps cap to K3_SPEC_MAX = 8, :210,466; here cap
- * is the caller's, and nmax/nmin give the n range so the BASELINE's n = 3 rule is the
+ * is the caller's, and nmax/nmin give the n range so the benchmark's n = 3 rule is the
  * same function with nmax = nmin = 3). */
 ORC_API int orc_spec_draft(const int *seq, int T, int cap, int nmax, int nmin, int *out)
 {

@@ -22,9 +22,9 @@ def bf16_round(a: np.ndarray) -> np.ndarray:
 
 
 ROUTER_CASES = [
-    # BASELINE config 2 router: 384 experts over d_model 7168, top-8, 16 tokens
+    # Benchmark config 2 router: 384 experts over d_model 7168, top-8, 16 tokens
     dict(name="c2_t16", seed=11, T=16, hidden=7168, n=384, topk=8, wstd=0.02, bstd=0.01),
-    # BASELINE config 1 router: 16 experts over 512, top-2
+    # Benchmark config 1 router: 16 experts over 512, top-2
     dict(name="c1_t9", seed=12, T=9, hidden=512, n=16, topk=2, wstd=0.02, bstd=0.01),
     # exact ties: duplicated gate rows and a zero bias, so the first-index rule decides
     dict(name="ties", seed=13, T=8, hidden=96, n=64, topk=6, wstd=0.05, bstd=0.0, dup=True),
@@ -57,7 +57,7 @@ def mxfp4_inputs(case):
 
 
 KDA_CASES = [
-    # BASELINE config 3 geometry (head dim 128) at k = 16, two heads to keep files small
+    # Benchmark config 3 geometry (head dim 128) at k = 16, two heads to keep files small
     dict(name="d128_k16", seed=31, T=17, H=2, D=128, commits=[0, 1, 5, 9, 17]),
     dict(name="d64_k4", seed=32, T=5, H=4, D=64, commits=[0, 2, 5]),
 ]

@@ -63,7 +63,7 @@ def convert_fixtures(ref: str) -> None:
 
 
 def gen_router(lib) -> None:
-    """k3_router on BASELINE config-2 shapes (384 x 7168, top-8) and a near-tie stress."""
+    """k3_router on benchmark config-2 shapes (384 x 7168, top-8) and a near-tie stress."""
     res = {}
     for case in GI.ROUTER_CASES:
         x, W, bias = GI.router_inputs(case)

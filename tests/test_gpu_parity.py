@@ -106,7 +106,7 @@ def moe_case(seed, L, I, n_routed, n_shared, topk, T, act, std=0.02, w13_std=Non
 
 @pytest.mark.parametrize("act", [0, 1], ids=["situ", "swiglu"])
 def test_moe_layer_tiny_config_vs_oracle(k3, act):
-    """BASELINE config 1 MoE shape: d 512, 16 experts top-2, 1 shared, FFN 256."""
+    """Benchmark config 1 MoE shape: d 512, 16 experts top-2, 1 shared, FFN 256."""
     L, I, n, ns, k, T = 512, 256, 16, 1, 2, 5
     bank, lay, x, W, bias = moe_case(7, L, I, n, ns, k, T, act, std=0.05, w13_std=0.3)
     kb = k3.ExpertBank(dev(bank), n + ns, L, I)
@@ -133,7 +133,7 @@ def test_moe_latent_norm_and_dropped_slot(k3):
 
 
 def test_moe_c2_width_vs_oracle(k3):
-    """BASELINE config 2 widths (d 7168, FFN 2048, SwiGLU) on 24 experts, 5 tokens."""
+    """Benchmark config 2 widths (d 7168, FFN 2048, SwiGLU) on 24 experts, 5 tokens."""
     L, I, n, ns, k, T = 7168, 2048, 24, 1, 8, 5
     bank, lay, x, W, bias = moe_case(9, L, I, n, ns, k, T, 1)
     kb = k3.ExpertBank(dev(bank), n + ns, L, I)
@@ -170,7 +170,7 @@ def test_moe_expert_kernels_fp32_inputs_many_tokens(k3, which):
 
 @pytest.mark.parametrize("fp32_inputs", [False, True], ids=["bf16in", "fp32in"])
 def test_moe_tcgen05_path_vs_oracle(k3, fp32_inputs):
-    """The tcgen05 expert kernels (bank certified by k3gpu_bank_scan): BASELINE config-2
+    """The tcgen05 expert kernels (bank certified by k3gpu_bank_scan): benchmark config-2
     widths on 24 experts, then a 1024/512 case with up to 48 tokens per expert (three
     16-token passes) and, for fp32 inputs, the lo halves of the f16 split."""
     for (L, I, n, ns, k, T, seed) in ((7168, 2048, 24, 1, 8, 6, 31), (1024, 512, 4, 1, 3, 64, 32)):
@@ -258,7 +258,7 @@ def test_kda_verify_commit_bitexact_vs_reference(k3, case):
 
 
 def test_kda_batched_rollback_c3_shape(k3):
-    """32 heads x 128, chunk 1+k = 9, four sequences, rollback
+    """Benchmark config 3: 32 heads x 128, chunk 1+k = 9, four sequences, rollback
     lengths drawn in [0, k]; each sequence bit-identical to the oracle."""
     B, T, H, D = 4, 9, 32, 128
     rng = np.random.default_rng(77)
@@ -447,7 +447,7 @@ def test_argmax_ties_nans_and_chunk_edges(k3, V):
 
 
 def test_accept_tree_greedy_vs_oracle(k3):
-    # 64-node tree, branching 4, depth 3 (+ root): BASELINE config 4's draft tree shape
+    # 64-node tree, branching 4, depth 3 (+ root): benchmark config 4's draft tree shape
     parent = [-1]
     level = [0]
     while len(parent) < 64:

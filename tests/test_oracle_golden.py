@@ -257,7 +257,7 @@ def test_spec_draft_rules():
     # no 4-gram match but a 3-gram one (n = 4 then 3)
     s = [0, 2, 3, 4, 5, 6, 9, 2, 3, 4]
     assert draft(s) == [5, 6, 9, 2, 3, 4]
-    # the BASELINE rule n = 3 only
+    # the benchmark's rule n = 3 only
     assert draft([5, 1, 2, 3, 9, 1, 2, 3], nmax=3) == [9, 1, 2, 3]
     assert draft([1, 2]) == []
 

@@ -43,7 +43,7 @@ def test_router_noalloc_matches_workspace_router_twice():
         pytest.skip("no CUDA device")
     k3 = k3lib.load()
     # two different calls in a row: the second must not see anything the first left in
-    # the shared array (BASELINE config 2 router shape, then a larger batch)
+    # the shared array (benchmark config 2 router shape, then a larger batch)
     for case in (dict(name="a", seed=11, T=16, hidden=7168, n=384, topk=8, wstd=0.02, bstd=0.01),
                  dict(name="b", seed=91, T=72, hidden=7168, n=384, topk=8, wstd=0.02, bstd=0.01)):
         x, W, b = GI.router_inputs(case)
