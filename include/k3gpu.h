@@ -509,6 +509,27 @@ int k3gpu_ep_combine(const K3GpuEpGroup *g, float *out, const int *pos, int T, u
  * cap to K3_SPEC_MAX = 8). seq [T] host, out [cap] host; returns the draft count. */
 int k3_spec_draft_ngram(const int *seq, int T, int cap, int nmax, int nmin, int *out);
 
+/* Host C: the reference drafting study's P1 (tools/spec_replay.py:174-184): the most
+ * recent earlier occurrence of the history's suffix 4-gram, else 3-gram, else 2-gram, and
+ * the ids that followed it, up to cap (<= 8) and the end of the history; no agreement
+ * gate. seq [T] host, out [cap]; returns the draft count. */
+int k3_spec_draft_eager(const int *seq, int T, int cap, int *out);
+
+/* Host C: the study's P2 (tools/spec_replay.py:256-336, 442-449) as an incremental
+ * drafter: an online suffix automaton over the history. push appends ids; draft proposes,
+ * after the history seq[0..T), the continuation of the longest suffix that also ends
+ * earlier: with e its most recent earlier end, out[i] = seq[e + 1 + i % (T - 1 - e)] for
+ * i < cap (<= 8), a copy that continues periodically past the end of the history. It
+ * fires (returns cap) when that suffix has at least min_len ids, else returns 0;
+ * match_len and period receive its length and T - 1 - e (0 when there is none). */
+typedef struct K3SuffixDrafter K3SuffixDrafter;
+K3SuffixDrafter *k3_suffix_drafter_create(int capacity);   /* most ids it will hold */
+void k3_suffix_drafter_free(K3SuffixDrafter *d);
+int k3_suffix_drafter_push(K3SuffixDrafter *d, const int *ids, int n);
+int k3_suffix_drafter_length(const K3SuffixDrafter *d);
+int k3_suffix_drafter_draft(const K3SuffixDrafter *d, int cap, int min_len, int *out,
+                            int *match_len, int *period);
+
 #ifdef __cplusplus
 }
 #endif

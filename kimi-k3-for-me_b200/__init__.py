@@ -151,6 +151,12 @@ _SIGS = {
     "k3gpu_ep_return": ([C.POINTER(K3GpuEpGroup), VP, C.c_uint, VP], I),
     "k3gpu_ep_combine": ([C.POINTER(K3GpuEpGroup), VP, VP, I, C.c_uint, VP, VP], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
+    "k3_spec_draft_eager": ([VP, I, I, VP], I),
+    "k3_suffix_drafter_create": ([I], VP),
+    "k3_suffix_drafter_free": ([VP], None),
+    "k3_suffix_drafter_push": ([VP, VP, I], I),
+    "k3_suffix_drafter_length": ([VP], I),
+    "k3_suffix_drafter_draft": ([VP, I, I, VP, C.POINTER(I), C.POINTER(I)], I),
 }
 for _name, (_args, _res) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -564,3 +570,48 @@ def spec_draft(seq, cap=8, nmax=4, nmin=3):
     out = (C.c_int * max(cap, 1))()
     nd = lib.k3_spec_draft_ngram(arr, len(seq), cap, nmax, nmin, out)
     return list(out[:nd])
+
+
+def spec_draft_eager(seq, cap=8):
+    """The drafting study's P1 (k3_spec_draft_eager): host C, no GPU."""
+    arr = (C.c_int * max(len(seq), 1))(*seq)
+    out = (C.c_int * max(cap, 1))()
+    nd = lib.k3_spec_draft_eager(arr, len(seq), cap, out)
+    return list(out[:nd])
+
+
+class SuffixDrafter:
+    """The drafting study's P2 as an incremental host drafter (k3_suffix_drafter_*): push
+    ids as they are accepted, draft() after each step. No GPU."""
+
+    def __init__(self, capacity: int):
+        self._d = lib.k3_suffix_drafter_create(capacity)
+        if not self._d:
+            raise K3Error(f"k3_suffix_drafter_create({capacity}) failed")
+
+    def push(self, ids) -> None:
+        ids = list(ids)
+        arr = (C.c_int * max(len(ids), 1))(*ids)
+        check(lib.k3_suffix_drafter_push(self._d, arr, len(ids)), "k3_suffix_drafter_push")
+
+    def __len__(self) -> int:
+        return lib.k3_suffix_drafter_length(self._d)
+
+    def draft(self, cap=8, min_len=1):
+        """(draft ids, match length, period); the draft is empty when the longest earlier
+        match is shorter than min_len."""
+        out = (C.c_int * max(cap, 1))()
+        L, g = C.c_int(0), C.c_int(0)
+        nd = lib.k3_suffix_drafter_draft(self._d, cap, min_len, out, C.byref(L), C.byref(g))
+        return list(out[:nd]), L.value, g.value
+
+    def close(self) -> None:
+        if self._d:
+            lib.k3_suffix_drafter_free(self._d)
+            self._d = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 -- interpreter shutdown may have unloaded the library
+            pass

@@ -1,0 +1,250 @@
+// draft.cu -- host drafters beyond the engine's n-gram rule (host C++, no device code).
+//
+// The reference's drafting study (tools/spec_replay.py) defines two deterministic
+// policies besides the engine's spec_draft:
+//
+//   P1  eager most-recent match (:174-184): the most recent earlier occurrence of the
+//       history's suffix 4-gram, else 3-gram, else 2-gram; the ids that followed it, up to
+//       the cap and the end of the history; no agreement gate.
+//   P2  longest suffix match (:256-336, used at :442-449): the longest suffix of the
+//       history that also ends earlier, its most recent earlier end e, and the ids after e
+//       continued with period g = (T - 1) - e past the end of the history (an LZ77-style
+//       overlapping copy); it fires when the match is at least min_len ids.
+//
+// P2 keeps an online suffix automaton over the token ids. Every state carries its
+// largest end position and occurrence count; those are advanced along the suffix-link
+// path one position late (the tool's commit after reading), so at a draft point they
+// describe the history before its last id. Transitions live in one open-addressing hash
+// table keyed by (state, id), with each state's transitions also chained in a list for the
+// clone step.
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "k3gpu.h"
+
+namespace {
+
+constexpr int SPEC_MAX = 8;   // K3_SPEC_MAX, the engine's draft cap
+
+struct Trans {
+    uint64_t key;   // (state << 32) | id
+    int to;
+    int next;       // next transition of the same state, -1 ends the list
+};
+
+}  // namespace
+
+struct K3SuffixDrafter {
+    int cap;             // most ids
+    int n;               // ids pushed
+    int pending;         // 1 when the last id's commit is still due
+    int last;            // state of the whole history
+    int n_states;
+    int *seq, *len, *link, *last_end, *cnt, *head;   // head: first transition of a state
+    Trans *tr;
+    int n_tr, tr_cap;
+    int *table;          // hash slot -> transition index, -1 empty
+    uint64_t mask;
+};
+
+namespace {
+
+uint64_t key_of(int state, int id) { return ((uint64_t)(uint32_t)state << 32) | (uint32_t)id; }
+
+uint64_t hash64(uint64_t k)
+{
+    k ^= k >> 33;
+    k *= 0xff51afd7ed558ccdULL;
+    k ^= k >> 33;
+    k *= 0xc4ceb9fe1a85ec53ULL;
+    k ^= k >> 33;
+    return k;
+}
+
+// slot of key (its transition, or the empty slot where it would go)
+uint64_t find_slot(const K3SuffixDrafter *d, uint64_t key)
+{
+    uint64_t s = hash64(key) & d->mask;
+    while (d->table[s] >= 0 && d->tr[d->table[s]].key != key) s = (s + 1) & d->mask;
+    return s;
+}
+
+int get(const K3SuffixDrafter *d, int state, int id)
+{
+    const uint64_t s = find_slot(d, key_of(state, id));
+    return d->table[s] >= 0 ? d->tr[d->table[s]].to : -1;
+}
+
+// a new transition (the key is known to be absent); capacity was reserved up front
+void add(K3SuffixDrafter *d, int state, int id, int to)
+{
+    const uint64_t key = key_of(state, id);
+    const uint64_t s = find_slot(d, key);
+    const int t = d->n_tr++;
+    d->tr[t].key = key;
+    d->tr[t].to = to;
+    d->tr[t].next = d->head[state];
+    d->head[state] = t;
+    d->table[s] = t;
+}
+
+void redirect(K3SuffixDrafter *d, int state, int id, int to)
+{
+    const uint64_t s = find_slot(d, key_of(state, id));
+    d->tr[d->table[s]].to = to;
+}
+
+// the tool's commit(pos): occurrence figures of every proper suffix state of the history
+void commit(K3SuffixDrafter *d, int pos)
+{
+    int v = d->link[d->last];
+    while (v > 0) {
+        d->last_end[v] = pos;
+        d->cnt[v] += 1;
+        v = d->link[v];
+    }
+}
+
+// the tool's extend(c, pos)
+void extend(K3SuffixDrafter *d, int c, int pos)
+{
+    const int cur = d->n_states++;
+    d->len[cur] = d->len[d->last] + 1;
+    d->link[cur] = 0;
+    d->head[cur] = -1;
+    d->last_end[cur] = pos;
+    d->cnt[cur] = 1;
+    int p = d->last;
+    while (p != -1 && get(d, p, c) < 0) {
+        add(d, p, c, cur);
+        p = d->link[p];
+    }
+    if (p != -1) {
+        const int q = get(d, p, c);
+        if (d->len[p] + 1 == d->len[q]) {
+            d->link[cur] = q;
+        } else {
+            const int clone = d->n_states++;
+            d->len[clone] = d->len[p] + 1;
+            d->link[clone] = d->link[q];
+            d->head[clone] = -1;
+            for (int t = d->head[q]; t >= 0; t = d->tr[t].next)
+                add(d, clone, (int)(uint32_t)(d->tr[t].key & 0xffffffffu), d->tr[t].to);
+            d->last_end[clone] = d->last_end[q];
+            d->cnt[clone] = d->cnt[q];
+            while (p != -1 && get(d, p, c) == q) {
+                redirect(d, p, c, clone);
+                p = d->link[p];
+            }
+            d->link[q] = clone;
+            d->link[cur] = clone;
+        }
+    }
+    d->last = cur;
+}
+
+}  // namespace
+
+extern "C" int k3_spec_draft_eager(const int *seq, int T, int cap, int *out)
+{
+    if (!seq || T < 0 || cap < 0 || (cap > 0 && !out)) return 0;
+    if (cap > SPEC_MAX) cap = SPEC_MAX;
+    for (int n = 4; n >= 2; n--) {
+        if (T < n + 1) continue;
+        for (int j = T - n - 1; j >= 0; j--) {
+            int hit = 1;
+            for (int i = 0; i < n && hit; i++) hit = seq[j + i] == seq[T - n + i];
+            if (!hit) continue;
+            int nd = 0;
+            while (nd < cap && j + n + nd < T) {
+                out[nd] = seq[j + n + nd];
+                nd++;
+            }
+            return nd;
+        }
+    }
+    return 0;
+}
+
+extern "C" K3SuffixDrafter *k3_suffix_drafter_create(int capacity)
+{
+    if (capacity <= 0 || capacity > (1 << 28)) return nullptr;
+    K3SuffixDrafter *d = (K3SuffixDrafter *)calloc(1, sizeof(K3SuffixDrafter));
+    if (!d) return nullptr;
+    const int ns = 2 * capacity + 2;            // a suffix automaton has < 2n states
+    d->cap = capacity;
+    d->tr_cap = 3 * capacity + 4;               // and < 3n transitions
+    uint64_t slots = 16;
+    while (slots < (uint64_t)2 * d->tr_cap) slots <<= 1;
+    d->mask = slots - 1;
+    d->seq = (int *)malloc(sizeof(int) * (size_t)capacity);
+    d->len = (int *)malloc(sizeof(int) * (size_t)ns);
+    d->link = (int *)malloc(sizeof(int) * (size_t)ns);
+    d->last_end = (int *)malloc(sizeof(int) * (size_t)ns);
+    d->cnt = (int *)malloc(sizeof(int) * (size_t)ns);
+    d->head = (int *)malloc(sizeof(int) * (size_t)ns);
+    d->tr = (Trans *)malloc(sizeof(Trans) * (size_t)d->tr_cap);
+    d->table = (int *)malloc(sizeof(int) * (size_t)slots);
+    if (!d->seq || !d->len || !d->link || !d->last_end || !d->cnt || !d->head || !d->tr || !d->table) {
+        k3_suffix_drafter_free(d);
+        return nullptr;
+    }
+    memset(d->table, 0xff, sizeof(int) * (size_t)slots);
+    d->n_states = 1;                            // the root
+    d->len[0] = 0;
+    d->link[0] = -1;
+    d->last_end[0] = -1;
+    d->cnt[0] = 0;
+    d->head[0] = -1;
+    return d;
+}
+
+extern "C" void k3_suffix_drafter_free(K3SuffixDrafter *d)
+{
+    if (!d) return;
+    free(d->seq);
+    free(d->len);
+    free(d->link);
+    free(d->last_end);
+    free(d->cnt);
+    free(d->head);
+    free(d->tr);
+    free(d->table);
+    free(d);
+}
+
+extern "C" int k3_suffix_drafter_push(K3SuffixDrafter *d, const int *ids, int n)
+{
+    if (!d || n < 0 || (n > 0 && !ids)) return K3GPU_EINVAL;
+    if (n > d->cap - d->n) return K3GPU_ECAPACITY;
+    for (int i = 0; i < n; i++) {
+        if (d->pending) commit(d, d->n - 1);
+        d->seq[d->n] = ids[i];
+        extend(d, ids[i], d->n);
+        d->n++;
+        d->pending = 1;
+    }
+    return K3GPU_OK;
+}
+
+extern "C" int k3_suffix_drafter_length(const K3SuffixDrafter *d) { return d ? d->n : 0; }
+
+extern "C" int k3_suffix_drafter_draft(const K3SuffixDrafter *d, int cap, int min_len, int *out, int *match_len,
+                                       int *period)
+{
+    if (match_len) *match_len = 0;
+    if (period) *period = 0;
+    if (!d || d->n == 0 || cap <= 0 || !out) return 0;
+    if (cap > SPEC_MAX) cap = SPEC_MAX;
+    // the longest suffix that also ends earlier: the whole history's suffix link
+    const int v = d->link[d->last];
+    if (v <= 0) return 0;
+    const int L = d->len[v], e = d->last_end[v], pos = d->n - 1;
+    if (match_len) *match_len = L;
+    const int g = pos - e;
+    if (period) *period = g;
+    if (L < min_len || g <= 0) return 0;
+    for (int i = 0; i < cap; i++) out[i] = d->seq[e + 1 + (i % g)];
+    return cap;
+}

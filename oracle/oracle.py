@@ -322,3 +322,37 @@ def mla_forward(x, wts, cfg):
         g = matmul_d(x, wts["g"])
         acc = acc * (np.float32(1) / (np.float32(1) + np.exp(-g, dtype=np.float32)))
     return matmul_d(acc, wts["o"])
+
+
+# ---------------------------------------------------------------- drafting policies ---
+def eager_draft(seq, T, cap=8):
+    """P1 of the reference's drafting study (tools/spec_replay.py:174-184): the most recent
+    earlier occurrence of the suffix 4-gram, else 3-gram, else 2-gram, and the ids after it
+    up to cap (<= 8) and the end of the history."""
+    cap = min(cap, 8)
+    for n in (4, 3, 2):
+        if T < n + 1:
+            continue
+        for j in range(T - n - 1, -1, -1):
+            if all(seq[j + i] == seq[T - n + i] for i in range(n)):
+                return [seq[j + n + i] for i in range(cap) if j + n + i < T]
+    return []
+
+
+def longest_suffix_draft(seq, T, cap=8):
+    """P2 of the study (tools/spec_replay.py:319-336, 442-449) by brute force: the longest
+    suffix of seq[0..T) that also ends at some e <= T-2, its most recent such end, and
+    seq[e + 1 + i % (T - 1 - e)] for i < cap. Returns (draft, L, g); ([], 0, 0) without a
+    match."""
+    best = (0, -1)
+    for L in range(1, T):
+        suf = list(seq[T - L:T])
+        ends = [e for e in range(L - 1, T - 1) if list(seq[e - L + 1:e + 1]) == suf]
+        if not ends:
+            break
+        best = (L, max(ends))
+    L, e = best
+    if L == 0:
+        return [], 0, 0
+    g = (T - 1) - e
+    return [seq[e + 1 + (i % g)] for i in range(min(cap, 8))], L, g

@@ -1,0 +1,93 @@
+"""Generate tests/golden/ref_drafters.npz from the reference's drafting study
+(tools/spec_replay.py), run here where the reference tree exists.
+
+For seeded id sequences with planted repeats (copies of earlier spans, periodic runs), at
+every draft point T (the history seq[0..T), after the tool's SuffixAutomaton.extend of id
+T-1 and before its commit, exactly as analyze_sequence steps, tools/spec_replay.py:408-469):
+  p1[T]      eager_draft(seq, T, 8)  (P1, :174-184), -1 padded, with its length
+  L2[T]      the suffix automaton's match length (0: none)
+  g2[T]      its period pos - last_end (0: none)
+  p2[T]      periodic_copy(seq, last_end + 1, g, 8)  (P2, :333-336, 442-449), -1 padded
+
+Usage: python tests/golden/make_drafter_golden.py [--ref /root/reference]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CAP = 8
+
+
+def sequences(rng):
+    out = []
+    for n, vocab in ((400, 12), (600, 50), (500, 2000), (300, 3)):
+        s = list(rng.integers(0, vocab, 40))
+        while len(s) < n:
+            r = rng.random()
+            if r < 0.45 and len(s) > 8:                     # copy an earlier span
+                a = int(rng.integers(0, len(s) - 4))
+                ln = int(rng.integers(3, 24))
+                s.extend(s[a:a + ln])
+            elif r < 0.6:                                   # a periodic run
+                per = int(rng.integers(1, 5))
+                base = list(rng.integers(0, vocab, per))
+                s.extend((base * 10)[:int(rng.integers(4, 20))])
+            else:
+                s.extend(rng.integers(0, vocab, int(rng.integers(1, 10))))
+        out.append(np.asarray(s[:n], np.int32))
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    a = ap.parse_args()
+    spec = importlib.util.spec_from_file_location("spec_replay", os.path.join(a.ref, "tools", "spec_replay.py"))
+    sr = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(sr)
+    rng = np.random.default_rng(20260)
+    arrays = {}
+    for si, seq in enumerate(sequences(rng)):
+        s = [int(v) for v in seq]
+        n = len(s)
+        p1 = np.full((n + 1, CAP), -1, np.int32)
+        p1n = np.zeros(n + 1, np.int32)
+        p2 = np.full((n + 1, CAP), -1, np.int32)
+        L2 = np.zeros(n + 1, np.int32)
+        g2 = np.zeros(n + 1, np.int32)
+        sam = sr.SuffixAutomaton()
+        for pos in range(n):
+            v = sam.extend(s[pos], pos)
+            T = pos + 1
+            d = sr.eager_draft(s, T, CAP)
+            p1[T, :len(d)] = d
+            p1n[T] = len(d)
+            if v > 0:
+                e = sam.last_end[v]
+                g = pos - e
+                L2[T] = sam.length[v]
+                g2[T] = g
+                p2[T] = sr.periodic_copy(s, e + 1, g, CAP)
+                # the tool's own brute-force check of the automaton
+                bl, be, _ = sr.longest_suffix_match(s, T)
+                assert (bl, be) == (sam.length[v], e), (si, T)
+            sam.commit(pos)
+        arrays[f"s{si}/seq"] = seq
+        arrays[f"s{si}/p1"] = p1
+        arrays[f"s{si}/p1n"] = p1n
+        arrays[f"s{si}/p2"] = p2
+        arrays[f"s{si}/L2"] = L2
+        arrays[f"s{si}/g2"] = g2
+    arrays["n_seq"] = np.int32(len(sequences(np.random.default_rng(20260))))
+    path = os.path.join(HERE, "ref_drafters.npz")
+    np.savez_compressed(path, **arrays)
+    print(path, os.path.getsize(path), "bytes")
+
+
+if __name__ == "__main__":
+    main()
