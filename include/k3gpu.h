@@ -118,6 +118,18 @@ typedef struct {
  * a bank never scanned runs entirely on those. */
 int k3gpu_bank_scan(K3GpuExpertBank *bank, uint8_t *safe_dev, void *stream);
 
+/* Host C: routed experts [e0, e0 + n) of MoE layer `layer` from the checkpoint's
+ * safetensors shards (files: the shard paths, any order; the format of the reference's
+ * src/io/k3_st.h:7-13) into host_bank laid out as this bank (k3gpu_bank_layout(L, I): run
+ * e - e0 at (e - e0) * stride), ready for one copy to the device. Reads the six U8 tensors
+ * language_model.model.layers.<layer>.block_sparse_moe.experts.<e>.<w1|w2|w3>.<weight_packed|
+ * weight_scale> (src/io/k3_load.c:11) after checking their dtype and shapes ([I][L/2],
+ * [I][L/32] for w1 and w3; [L][I/2], [L][I/32] for w2). K3GPU_EINVAL for a missing,
+ * mis-shaped or unreadable tensor or a malformed header, K3GPU_ECAPACITY when host_bytes
+ * is short of n * stride. */
+int k3_bank_read_safetensors(const char *const *files, int n_files, int layer, int e0, int n,
+                             int L, int I, uint8_t *host_bank, size_t host_bytes);
+
 /* Fill the offsets and stride of the packed run layout above (the stride is the run
  * rounded up to a multiple of lcm(L/2, I/2, 256) bytes, so every matrix starts on a whole
  * row of the expert kernels' tensor maps); leaves base and n_experts to the caller.

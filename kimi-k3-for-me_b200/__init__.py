@@ -152,6 +152,7 @@ _SIGS = {
     "k3gpu_ep_combine": ([C.POINTER(K3GpuEpGroup), VP, VP, I, C.c_uint, VP, VP], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
     "k3_spec_draft_eager": ([VP, I, I, VP], I),
+    "k3_bank_read_safetensors": ([C.POINTER(C.c_char_p), I, I, I, I, I, I, VP, SZ], I),
     "k3_suffix_drafter_create": ([I], VP),
     "k3_suffix_drafter_free": ([VP], None),
     "k3_suffix_drafter_push": ([VP, VP, I], I),
@@ -570,6 +571,19 @@ def spec_draft(seq, cap=8, nmax=4, nmin=3):
     out = (C.c_int * max(cap, 1))()
     nd = lib.k3_spec_draft_ngram(arr, len(seq), cap, nmax, nmin, out)
     return list(out[:nd])
+
+
+def bank_read_safetensors(files, layer, e0, n, L, I_):
+    """Routed experts [e0, e0 + n) of a MoE layer from safetensors shards into a host
+    uint8 array in the device bank layout (k3_bank_read_safetensors); upload it with one
+    copy (e.g. torch.from_numpy(...).cuda()) and wrap it in an ExpertBank."""
+    import numpy as np
+    lay = ExpertBank.layout(L, I_)
+    buf = np.zeros(n * lay.stride, np.uint8)
+    arr = (C.c_char_p * len(files))(*[os.fsencode(f) for f in files])
+    check(lib.k3_bank_read_safetensors(arr, len(files), layer, e0, n, L, I_, buf.ctypes.data, buf.nbytes),
+          "k3_bank_read_safetensors")
+    return buf
 
 
 def spec_draft_eager(seq, cap=8):

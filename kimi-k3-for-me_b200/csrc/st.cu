@@ -1,0 +1,288 @@
+// st.cu -- host C++: one MoE layer's routed experts from the checkpoint's safetensors
+// shards into a host buffer laid out as the device expert bank (no device code).
+//
+// The checkpoint format (src/io/k3_st.h:7-13 of the reference): [8-byte little-endian N]
+// [N bytes of JSON header][data]; each header entry is {"dtype", "shape", "data_offsets":
+// [start, end]} with offsets relative to the end of the header; "__metadata__" may appear.
+// A routed expert is six U8 tensors (src/io/k3_load.h:1-22, names src/io/k3_load.c:11):
+//   language_model.model.layers.<layer>.block_sparse_moe.experts.<e>.<w>.weight_packed
+//   language_model.model.layers.<layer>.block_sparse_moe.experts.<e>.<w>.weight_scale
+// for w = w1, w2, w3, with w1/w3 [I][L/2] + [I][L/32] and w2 [L][I/2] + [L][I/32]. The
+// device bank keeps them in the same order (k3gpu_bank_layout), so each expert lands with
+// one read per tensor, or one read per expert when the six are contiguous in the file.
+#include <fcntl.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "k3gpu.h"
+
+namespace {
+
+struct Entry {
+    int file;
+    int64_t off, bytes;      // absolute file offset and length
+    std::string dtype;
+    std::vector<int64_t> shape;
+};
+
+// a JSON scanner for safetensors headers: objects, arrays, strings (with escapes),
+// numbers, true/false/null; entries are recorded for objects that have data_offsets
+struct Scan {
+    const char *p, *e;
+    bool ok = true;
+
+    void ws()
+    {
+        while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) p++;
+    }
+    bool eat(char c)
+    {
+        ws();
+        if (p < e && *p == c) {
+            p++;
+            return true;
+        }
+        return false;
+    }
+    static int hexv(char c)
+    {
+        if (c >= '0' && c <= '9') return c - '0';
+        if (c >= 'a' && c <= 'f') return c - 'a' + 10;
+        if (c >= 'A' && c <= 'F') return c - 'A' + 10;
+        return -1;
+    }
+    void utf8(std::string &s, unsigned cp)
+    {
+        if (cp < 0x80) {
+            s += (char)cp;
+        } else if (cp < 0x800) {
+            s += (char)(0xC0 | (cp >> 6));
+            s += (char)(0x80 | (cp & 0x3F));
+        } else if (cp < 0x10000) {
+            s += (char)(0xE0 | (cp >> 12));
+            s += (char)(0x80 | ((cp >> 6) & 0x3F));
+            s += (char)(0x80 | (cp & 0x3F));
+        } else {
+            s += (char)(0xF0 | (cp >> 18));
+            s += (char)(0x80 | ((cp >> 12) & 0x3F));
+            s += (char)(0x80 | ((cp >> 6) & 0x3F));
+            s += (char)(0x80 | (cp & 0x3F));
+        }
+    }
+    unsigned hex4()
+    {
+        if (e - p < 4) { ok = false; return 0; }
+        unsigned v = 0;
+        for (int i = 0; i < 4; i++) {
+            const int h = hexv(p[i]);
+            if (h < 0) { ok = false; return 0; }
+            v = v * 16 + (unsigned)h;
+        }
+        p += 4;
+        return v;
+    }
+    std::string str()
+    {
+        std::string s;
+        if (!eat('"')) { ok = false; return s; }
+        while (p < e && *p != '"') {
+            if (*p != '\\') { s += *p++; continue; }
+            if (++p >= e) { ok = false; return s; }
+            const char c = *p++;
+            switch (c) {
+                case '"': s += '"'; break;
+                case '\\': s += '\\'; break;
+                case '/': s += '/'; break;
+                case 'b': s += '\b'; break;
+                case 'f': s += '\f'; break;
+                case 'n': s += '\n'; break;
+                case 'r': s += '\r'; break;
+                case 't': s += '\t'; break;
+                case 'u': {
+                    unsigned cp = hex4();
+                    if (cp >= 0xD800 && cp < 0xDC00 && e - p >= 6 && p[0] == '\\' && p[1] == 'u') {
+                        p += 2;
+                        const unsigned lo = hex4();
+                        cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
+                    }
+                    utf8(s, cp);
+                    break;
+                }
+                default: ok = false; return s;
+            }
+        }
+        if (p >= e) { ok = false; return s; }
+        p++;   // closing quote
+        return s;
+    }
+    bool number(int64_t *v)
+    {
+        ws();
+        const char *q = p;
+        if (q < e && (*q == '-' || *q == '+')) q++;
+        bool digits = false, integral = true;
+        while (q < e && ((*q >= '0' && *q <= '9') || *q == '.' || *q == 'e' || *q == 'E' || *q == '-' || *q == '+')) {
+            if (*q >= '0' && *q <= '9') digits = true;
+            else integral = false;
+            q++;
+        }
+        if (!digits) { ok = false; return false; }
+        if (v) *v = integral ? strtoll(std::string(p, q).c_str(), nullptr, 10) : -1;
+        p = q;
+        return integral;
+    }
+    void skip_value()
+    {
+        ws();
+        if (p >= e) { ok = false; return; }
+        if (*p == '"') { str(); return; }
+        if (*p == '{') {
+            p++;
+            if (eat('}')) return;
+            do {
+                str();
+                if (!eat(':')) { ok = false; return; }
+                skip_value();
+            } while (ok && eat(','));
+            if (!eat('}')) ok = false;
+            return;
+        }
+        if (*p == '[') {
+            p++;
+            if (eat(']')) return;
+            do skip_value();
+            while (ok && eat(','));
+            if (!eat(']')) ok = false;
+            return;
+        }
+        for (const char *lit : {"true", "false", "null"}) {
+            const size_t n = strlen(lit);
+            if ((size_t)(e - p) >= n && !strncmp(p, lit, n)) { p += n; return; }
+        }
+        number(nullptr);
+    }
+    std::vector<int64_t> int_array()
+    {
+        std::vector<int64_t> v;
+        if (!eat('[')) { ok = false; return v; }
+        if (eat(']')) return v;
+        do {
+            int64_t x;
+            if (!number(&x)) { ok = false; return v; }
+            v.push_back(x);
+        } while (ok && eat(','));
+        if (!eat(']')) ok = false;
+        return v;
+    }
+    // one tensor entry's object; returns false for objects without data_offsets
+    bool entry(Entry *t)
+    {
+        bool has_off = false;
+        if (!eat('{')) { ok = false; return false; }
+        if (eat('}')) return false;
+        do {
+            const std::string k = str();
+            if (!eat(':')) { ok = false; return false; }
+            if (k == "dtype") t->dtype = str();
+            else if (k == "shape") t->shape = int_array();
+            else if (k == "data_offsets") {
+                const std::vector<int64_t> o = int_array();
+                if (o.size() != 2 || o[0] < 0 || o[1] < o[0]) { ok = false; return false; }
+                t->off = o[0];
+                t->bytes = o[1] - o[0];
+                has_off = true;
+            } else skip_value();
+        } while (ok && eat(','));
+        if (!eat('}')) ok = false;
+        return ok && has_off;
+    }
+};
+
+int read_header(int fd, int file, std::unordered_map<std::string, Entry> *index, int64_t *file_bytes)
+{
+    uint8_t nb[8];
+    if (pread(fd, nb, 8, 0) != 8) return K3GPU_EINVAL;
+    uint64_t n = 0;
+    for (int i = 7; i >= 0; i--) n = (n << 8) | nb[i];
+    if (n == 0 || n > (1ull << 30)) return K3GPU_EINVAL;
+    std::vector<char> h(n);
+    if (pread(fd, h.data(), n, 8) != (ssize_t)n) return K3GPU_EINVAL;
+    const off_t end = lseek(fd, 0, SEEK_END);
+    *file_bytes = (int64_t)end;
+    Scan s{h.data(), h.data() + n};
+    if (!s.eat('{')) return K3GPU_EINVAL;
+    if (s.eat('}')) return K3GPU_OK;
+    do {
+        const std::string name = s.str();
+        if (!s.ok || !s.eat(':')) return K3GPU_EINVAL;
+        Entry t;
+        t.file = file;
+        t.off = t.bytes = 0;
+        if (s.entry(&t)) {
+            t.off += 8 + (int64_t)n;
+            if (t.off + t.bytes > *file_bytes) return K3GPU_EINVAL;   // data past the file
+            (*index)[name] = t;
+        }
+    } while (s.ok && s.eat(','));
+    return (s.ok && s.eat('}')) ? K3GPU_OK : K3GPU_EINVAL;
+}
+
+}  // namespace
+
+extern "C" int k3_bank_read_safetensors(const char *const *files, int n_files, int layer, int e0, int n, int L, int I,
+                                        uint8_t *host_bank, size_t host_bytes)
+{
+    if (!files || n_files <= 0 || layer < 0 || e0 < 0 || n <= 0 || !host_bank) return K3GPU_EINVAL;
+    if (L <= 0 || I <= 0 || L % 32 || I % 32) return K3GPU_EINVAL;
+    K3GpuExpertBank lay;
+    memset(&lay, 0, sizeof lay);
+    k3gpu_bank_layout(&lay, L, I);
+    if ((uint64_t)n * (uint64_t)lay.stride > host_bytes) return K3GPU_ECAPACITY;
+    int st = K3GPU_OK;
+    std::vector<int> fds;
+    std::unordered_map<std::string, Entry> index;
+    for (int f = 0; f < n_files && st == K3GPU_OK; f++) {
+        const int fd = files[f] ? open(files[f], O_RDONLY) : -1;
+        if (fd < 0) { st = K3GPU_EINVAL; break; }
+        fds.push_back(fd);
+        int64_t fb = 0;
+        st = read_header(fd, f, &index, &fb);
+    }
+    // the six tensors of an expert in run order, with their shapes and bank offsets
+    struct Part {
+        const char *w, *kind;
+        int64_t rows, cols, dst;
+    };
+    const Part parts[6] = {{"w1", "weight_packed", I, L / 2, lay.p1}, {"w1", "weight_scale", I, L / 32, lay.s1},
+                           {"w2", "weight_packed", L, I / 2, lay.p2}, {"w2", "weight_scale", L, I / 32, lay.s2},
+                           {"w3", "weight_packed", I, L / 2, lay.p3}, {"w3", "weight_scale", I, L / 32, lay.s3}};
+    char name[256];
+    for (int e = e0; e < e0 + n && st == K3GPU_OK; e++) {
+        uint8_t *run = host_bank + (size_t)(e - e0) * (size_t)lay.stride;
+        for (const Part &pt : parts) {
+            snprintf(name, sizeof name, "language_model.model.layers.%d.block_sparse_moe.experts.%d.%s.%s", layer, e,
+                     pt.w, pt.kind);
+            const auto it = index.find(name);
+            if (it == index.end()) { st = K3GPU_EINVAL; break; }
+            const Entry &t = it->second;
+            if (t.dtype != "U8" || t.shape.size() != 2 || t.shape[0] != pt.rows || t.shape[1] != pt.cols ||
+                t.bytes != pt.rows * pt.cols) {
+                st = K3GPU_EINVAL;
+                break;
+            }
+            if (pread(fds[t.file], run + pt.dst, (size_t)t.bytes, t.off) != (ssize_t)t.bytes) {
+                st = K3GPU_EINVAL;
+                break;
+            }
+        }
+    }
+    for (int fd : fds) close(fd);
+    return st;
+}

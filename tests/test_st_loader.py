@@ -1,0 +1,145 @@
+"""The safetensors expert loader (k3_bank_read_safetensors), CPU only.
+
+Shards are written here in the checkpoint format the reference documents (src/io/k3_st.h:
+7-13: 8-byte little-endian header length, JSON header, data with offsets relative to the
+header's end) with the expert tensor names of src/io/k3_load.c:11, and the awkward header
+cases a hand-written scanner gets wrong (escaped names, __metadata__, a scalar shape, a
+zero-element tensor, other dtypes). The bank bytes must be the tensors exactly, in the
+run order w1.packed w1.scale w2.packed w2.scale w3.packed w3.scale (src/io/k3_load.h:1-22).
+"""
+import json
+import os
+import struct
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+from k3lib import load  # noqa: E402
+
+L, I, LAYER = 64, 96, 3
+NAME = "language_model.model.layers.{}.block_sparse_moe.experts.{}.{}.{}"
+
+
+@pytest.fixture(scope="module")
+def k3():
+    return load()
+
+
+def expert_tensors(rng, e):
+    t = {}
+    for w, rows, cols in (("w1", I, L), ("w2", L, I), ("w3", I, L)):
+        t[(w, "weight_packed")] = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+        t[(w, "weight_scale")] = rng.integers(0, 256, (rows, cols // 32), dtype=np.uint8)
+    return t
+
+
+def write_shard(path, tensors, metadata=None, order=None):
+    """tensors: name -> (dtype string, shape list, raw bytes)."""
+    names = order or list(tensors)
+    header, blobs, off = {}, [], 0
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    for n in names:
+        dt, shape, raw = tensors[n]
+        header[n] = {"dtype": dt, "shape": shape, "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    h = json.dumps(header, ensure_ascii=True).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+def u8(a):
+    return ("U8", list(a.shape), a.tobytes())
+
+
+def build_shards(tmp_path, rng, n_exp=4):
+    ex = [expert_tensors(rng, e) for e in range(n_exp)]
+    a, b = {}, {}
+    for e in range(n_exp):
+        dst = a if e < 2 else b
+        for (w, kind), arr in ex[e].items():
+            dst[NAME.format(LAYER, e, w, kind)] = u8(arr)
+    # other tensors and awkward entries in shard A
+    a["language_model.model.layers.3.input_layernorm.weight"] = ("BF16", [L], np.zeros(L, np.uint16).tobytes())
+    a['odd "name" with \\ escapes and é'] = ("F32", [], np.float32(1.5).tobytes())
+    a["an.empty.tensor"] = ("F16", [0, 7], b"")
+    # shard B stores expert 3's tensors in reversed order (not one contiguous run)
+    order_b = [k for k in b if ".experts.2." in k] + list(reversed([k for k in b if ".experts.3." in k]))
+    pa, pb = str(tmp_path / "model-00001-of-00002.safetensors"), str(tmp_path / "model-00002-of-00002.safetensors")
+    write_shard(pa, a, metadata={"format": "pt", "note": "escapes \" \\ / \n"})
+    write_shard(pb, b, order=order_b)
+    return ex, [pb, pa]                                  # any order
+
+
+def check_run(k3, run, tens):
+    lay = k3.ExpertBank.layout(L, I)
+    for (w, kind), arr in tens.items():
+        off = {("w1", "weight_packed"): lay.p1, ("w1", "weight_scale"): lay.s1,
+               ("w2", "weight_packed"): lay.p2, ("w2", "weight_scale"): lay.s2,
+               ("w3", "weight_packed"): lay.p3, ("w3", "weight_scale"): lay.s3}[(w, kind)]
+        np.testing.assert_array_equal(run[off:off + arr.size], arr.reshape(-1))
+
+
+def test_run_order_is_the_checkpoint_order(k3):
+    lay = k3.ExpertBank.layout(L, I)
+    offs = [lay.p1, lay.s1, lay.p2, lay.s2, lay.p3, lay.s3]
+    sizes = [I * L // 2, I * L // 32, L * I // 2, L * I // 32, I * L // 2, I * L // 32]
+    assert offs == sorted(offs) and offs[0] == 0
+    assert all(offs[i] + sizes[i] <= offs[i + 1] for i in range(5)) and offs[5] + sizes[5] <= lay.stride
+
+
+def test_reads_experts_across_shards(k3, tmp_path):
+    ex, files = build_shards(tmp_path, np.random.default_rng(1))
+    lay = k3.ExpertBank.layout(L, I)
+    buf = k3.bank_read_safetensors(files, LAYER, 1, 3, L, I)    # experts 1, 2, 3
+    assert buf.size == 3 * lay.stride
+    for j, e in enumerate((1, 2, 3)):
+        check_run(k3, buf[j * lay.stride:(j + 1) * lay.stride], ex[e])
+
+
+def test_errors(k3, tmp_path):
+    ex, files = build_shards(tmp_path, np.random.default_rng(2))
+    lay = k3.ExpertBank.layout(L, I)
+    lib = k3.lib
+    C = k3.C
+    arr = (C.c_char_p * 2)(*[os.fsencode(f) for f in files])
+    buf = np.zeros(4 * lay.stride, np.uint8)
+    # an expert that is not there, a layer that is not there
+    assert lib.k3_bank_read_safetensors(arr, 2, LAYER, 3, 2, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    assert lib.k3_bank_read_safetensors(arr, 2, LAYER + 1, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    # too small a buffer
+    assert lib.k3_bank_read_safetensors(arr, 2, LAYER, 0, 4, L, I, buf.ctypes.data, 3 * lay.stride) == \
+        k3.K3GPU_ECAPACITY
+    # wrong geometry: the tensors are [I][L/2], not [L][I/2]
+    assert lib.k3_bank_read_safetensors(arr, 2, LAYER, 0, 1, I, L, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    # a wrong dtype, data past the end of the file, a malformed header
+    t = expert_tensors(np.random.default_rng(3), 0)
+    bad = {NAME.format(LAYER, 0, w, kind): u8(a) for (w, kind), a in t.items()}
+    key = NAME.format(LAYER, 0, "w2", "weight_scale")
+    bad[key] = ("I8",) + bad[key][1:]
+    p = str(tmp_path / "bad_dtype.safetensors")
+    write_shard(p, bad)
+    one = (C.c_char_p * 1)(os.fsencode(p))
+    assert lib.k3_bank_read_safetensors(one, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    good = {NAME.format(LAYER, 0, w, kind): u8(a) for (w, kind), a in t.items()}
+    p = str(tmp_path / "short.safetensors")
+    write_shard(p, good)
+    with open(p, "r+b") as f:
+        f.truncate(os.path.getsize(p) - 10)
+    one = (C.c_char_p * 1)(os.fsencode(p))
+    assert lib.k3_bank_read_safetensors(one, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    p = str(tmp_path / "junk.safetensors")
+    with open(p, "wb") as f:
+        h = b'{"a": {"dtype": "U8", "shape": [1], "data_offsets": [0, 1]'
+        f.write(struct.pack("<Q", len(h)) + h + b"\0")
+    one = (C.c_char_p * 1)(os.fsencode(p))
+    assert lib.k3_bank_read_safetensors(one, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    missing = (C.c_char_p * 1)(os.fsencode(str(tmp_path / "absent.safetensors")))
+    assert lib.k3_bank_read_safetensors(missing, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
