@@ -475,6 +475,35 @@ int k3gpu_decoder_layer_mla_verify(float *h, float *block_residual, int *n_block
                                    const uint64_t *mask, int max_ctx, int B, int T,
                                    void *workspace, size_t ws_bytes, void *stream);
 
+/* ---------------------------------------------------- conversation state ------ */
+/* Host C: the conversation state file, K3ST version 2 byte for byte as the reference's
+ * k3_state_save / k3_state_peek / k3_state_load (src/cli/k3_run.c:162-407) write and read
+ * it, so a session saved by either engine resumes on the other. The layout fields are the
+ * header's (fp = k3_state_fp: hidden, n_layers, vocab, kda_heads, kda_head_dim, conv_k,
+ * n_heads, qk_nope, qk_rope, v_head, n_experts, topk; kper = KDA floats per layer slot,
+ * the matrices [H][D][D] then the ShortConv history [3][P][K-1]; kvpp / ropepp = cache and
+ * rope floats per position per MLA layer) and the layer-loop record's (count 0: none). ks
+ * [kper * slots] (slots = loop_nv with a loop, else n_bound), kvc [n_mla][kv_cap][kvpp] and
+ * ropec [n_mla][kv_cap][ropepp] are host fp32 arrays (this library's bf16 MLA cache widens
+ * exactly into them). A save holds the cached positions' ids and at most one pending id.
+ * load refuses (K3GPU_EINVAL) another loop, fingerprint, layer count or cache width, a
+ * malformed or truncated file; K3GPU_ECAPACITY when the file holds more positions than
+ * kv_cap or more ids than seq_cap. */
+typedef struct {
+    int32_t fp[12];
+    int32_t n_bound, n_mla;
+    int64_t kper, kvpp, ropepp;
+    int32_t loop_a, loop_b, loop_count, loop_nv;
+    double loop_eps;
+} K3StateLayout;
+int k3_state_save(const char *path, const K3StateLayout *layout, const int *seq, int nseq,
+                  int cached, const float *ks, const float *kvc, const float *ropec, int kv_cap,
+                  const int *pcached, const int *passes);
+int k3_state_peek(const char *path, K3StateLayout *layout, int *cached, int *nseq);
+int k3_state_load(const char *path, const K3StateLayout *expect, int *seq, int seq_cap,
+                  float *ks, float *kvc, float *ropec, int kv_cap, int *pcached, int *passes,
+                  int *cached, int *nseq);
+
 /* ------------------------------------------------------- expert parallel ------ */
 /* The routed experts of a layer split over `world` ranks, one process per GPU, the token
  * rows exchanged through peer memory (NVLink / NVSwitch) instead of all-to-all calls:

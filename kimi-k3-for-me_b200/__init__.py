@@ -87,6 +87,12 @@ EP_MAX_WORLD = 8
 EP_HANDLE_BYTES = 64
 
 
+class K3StateLayout(C.Structure):
+    _fields_ = [("fp", I * 12), ("n_bound", I), ("n_mla", I), ("kper", C.c_int64), ("kvpp", C.c_int64),
+                ("ropepp", C.c_int64), ("loop_a", I), ("loop_b", I), ("loop_count", I), ("loop_nv", I),
+                ("loop_eps", C.c_double)]
+
+
 class K3GpuEpGroup(C.Structure):
     _fields_ = [("arena", VP * EP_MAX_WORLD), ("world", I), ("rank", I), ("cap", I), ("L", I), ("K", I),
                 ("n_local", I)]
@@ -153,6 +159,10 @@ _SIGS = {
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
     "k3_spec_draft_eager": ([VP, I, I, VP], I),
     "k3_bank_read_safetensors": ([C.POINTER(C.c_char_p), I, I, I, I, I, I, VP, SZ], I),
+    "k3_state_save": ([C.c_char_p, C.POINTER(K3StateLayout), VP, I, I, VP, VP, VP, I, VP, VP], I),
+    "k3_state_peek": ([C.c_char_p, C.POINTER(K3StateLayout), C.POINTER(I), C.POINTER(I)], I),
+    "k3_state_load": ([C.c_char_p, C.POINTER(K3StateLayout), VP, I, VP, VP, VP, I, VP, VP, C.POINTER(I),
+                       C.POINTER(I)], I),
     "k3_suffix_drafter_create": ([I], VP),
     "k3_suffix_drafter_free": ([VP], None),
     "k3_suffix_drafter_push": ([VP, VP, I], I),
