@@ -570,6 +570,15 @@ int k3_suffix_drafter_push(K3SuffixDrafter *d, const int *ids, int n);
 int k3_suffix_drafter_length(const K3SuffixDrafter *d);
 int k3_suffix_drafter_draft(const K3SuffixDrafter *d, int cap, int min_len, int *out,
                             int *match_len, int *period);
+/* A draft TREE for tree verification (no counterpart in the reference, whose drafts are
+ * chains): node 0 is the pending id; a node's children are the ids that followed its
+ * context in the history, most frequent first (at most `branch`), the context backing off
+ * to shorter suffixes of at least min_len ids when it has no continuation; nodes are
+ * added best-first by the product of relative frequencies along their path, up to
+ * max_nodes and max_depth. tok/parent [max_nodes] in the order of
+ * k3gpu_accept_tree_greedy (parents first, parent[0] = -1); returns the node count. */
+int k3_suffix_drafter_tree(const K3SuffixDrafter *d, int max_nodes, int branch, int max_depth,
+                           int min_len, int *tok, int *parent);
 
 #ifdef __cplusplus
 }

@@ -168,6 +168,7 @@ _SIGS = {
     "k3_suffix_drafter_push": ([VP, VP, I], I),
     "k3_suffix_drafter_length": ([VP], I),
     "k3_suffix_drafter_draft": ([VP, I, I, VP, C.POINTER(I), C.POINTER(I)], I),
+    "k3_suffix_drafter_tree": ([VP, I, I, I, I, VP, VP], I),
 }
 for _name, (_args, _res) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -628,6 +629,13 @@ class SuffixDrafter:
         L, g = C.c_int(0), C.c_int(0)
         nd = lib.k3_suffix_drafter_draft(self._d, cap, min_len, out, C.byref(L), C.byref(g))
         return list(out[:nd]), L.value, g.value
+
+    def tree(self, max_nodes=64, branch=4, max_depth=8, min_len=1):
+        """(tok, parent) of a draft tree rooted at the pending id (k3_suffix_drafter_tree)."""
+        tok = (C.c_int * max_nodes)()
+        par = (C.c_int * max_nodes)()
+        n = lib.k3_suffix_drafter_tree(self._d, max_nodes, branch, max_depth, min_len, tok, par)
+        return list(tok[:n]), list(par[:n])
 
     def close(self) -> None:
         if self._d:

@@ -248,3 +248,99 @@ extern "C" int k3_suffix_drafter_draft(const K3SuffixDrafter *d, int cap, int mi
     for (int i = 0; i < cap; i++) out[i] = d->seq[e + 1 + (i % g)];
     return cap;
 }
+
+// A draft tree for tree verification. Node 0 is the pending id (the last of the history);
+// its context is the longest suffix that occurred before (state link[last]). A node's
+// children are the ids that followed its context in the history, most often first (ties:
+// the smaller id), at most `branch` of them, each with probability k / n: k the times the
+// context was followed by that id, n the times it was followed by anything. A context
+// that was never followed backs off to its longest suffix with more occurrences (its
+// suffix link) while that suffix keeps >= min_len ids. Nodes are added best-first by the
+// product of the probabilities along their path (ties: the earliest candidate), up to
+// max_nodes nodes and max_depth below the root. tok/parent [max_nodes]; parents precede
+// their children; parent[0] = -1. Returns the node count (1: the root alone).
+//
+// Occurrence counts: cnt[] of a state counts its end positions up to the last commit; the
+// commit for the newest position is deferred to the next push, so the proper suffix
+// states of the history (the link path from link[last]) each lack that one occurrence.
+// It is added back here, which makes k exact.
+extern "C" int k3_suffix_drafter_tree(const K3SuffixDrafter *d, int max_nodes, int branch, int max_depth,
+                                      int min_len, int *tok, int *parent)
+{
+    if (!d || d->n == 0 || max_nodes < 1 || !tok || !parent) return 0;
+    if (branch < 1) branch = 1;
+    if (branch > 16) branch = 16;
+    tok[0] = d->seq[d->n - 1];
+    parent[0] = -1;
+    int n = 1;
+    const int v0 = d->link[d->last];
+    if (v0 <= 0 || d->len[v0] < min_len || max_depth < 1 || max_nodes == 1) return n;
+    // the link path from v0 (strictly decreasing len): the states owed the deferred commit
+    int np = 0;
+    for (int v = v0; v > 0; v = d->link[v]) np++;
+    int *path = (int *)malloc(sizeof(int) * (size_t)np);
+    struct Cand {
+        double p;
+        int par, id, state, depth;
+    };
+    const int max_c = max_nodes * branch + 1;
+    Cand *cand = (Cand *)malloc(sizeof(Cand) * (size_t)max_c);
+    if (!path || !cand) {
+        free(path);
+        free(cand);
+        return n;
+    }
+    np = 0;
+    for (int v = v0; v > 0; v = d->link[v]) path[np++] = v;
+    auto count = [&](int w) {
+        int lo = 0, hi = np;   // binary search by len (decreasing along the path)
+        while (lo < hi) {
+            const int mid = (lo + hi) / 2;
+            if (d->len[path[mid]] > d->len[w]) lo = mid + 1;
+            else hi = mid;
+        }
+        return d->cnt[w] + ((d->pending && lo < np && path[lo] == w) ? 1 : 0);
+    };
+    int nc = 0;
+    // the continuations of node `node` (context state `st`, path probability `pp`)
+    auto expand = [&](int node, int st, double pp, int depth) {
+        while (st > 0 && d->head[st] < 0 && d->link[st] > 0 && d->len[d->link[st]] >= min_len) st = d->link[st];
+        if (st <= 0 || d->head[st] < 0) return;
+        int ids[16], tos[16], ks[16], k = 0;
+        long long total = 0;
+        for (int t = d->head[st]; t >= 0; t = d->tr[t].next) {
+            const int id = (int)(uint32_t)(d->tr[t].key & 0xffffffffu), to = d->tr[t].to, c = count(to);
+            total += c;
+            int pos = k;
+            while (pos > 0 && (ks[pos - 1] < c || (ks[pos - 1] == c && ids[pos - 1] > id))) pos--;
+            if (pos >= branch) continue;
+            for (int q = (k < branch ? k : branch - 1); q > pos; q--) {
+                ids[q] = ids[q - 1];
+                tos[q] = tos[q - 1];
+                ks[q] = ks[q - 1];
+            }
+            ids[pos] = id;
+            tos[pos] = to;
+            ks[pos] = c;
+            if (k < branch) k++;
+        }
+        for (int q = 0; q < k && nc < max_c; q++)
+            cand[nc++] = Cand{pp * ((double)ks[q] / (double)total), node, ids[q], tos[q], depth + 1};
+    };
+    expand(0, v0, 1.0, 0);
+    while (n < max_nodes && nc > 0) {
+        int best = 0;
+        for (int i = 1; i < nc; i++)
+            if (cand[i].p > cand[best].p) best = i;
+        const Cand c = cand[best];
+        for (int i = best; i + 1 < nc; i++) cand[i] = cand[i + 1];
+        nc--;
+        tok[n] = c.id;
+        parent[n] = c.par;
+        const int node = n++;
+        if (c.depth < max_depth) expand(node, c.state, c.p, c.depth);
+    }
+    free(path);
+    free(cand);
+    return n;
+}

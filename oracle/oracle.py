@@ -356,3 +356,66 @@ def longest_suffix_draft(seq, T, cap=8):
         return [], 0, 0
     g = (T - 1) - e
     return [seq[e + 1 + (i % g)] for i in range(min(cap, 8))], L, g
+
+
+def suffix_tree_draft(seq, max_nodes=64, branch=4, max_depth=8, min_len=1):
+    """The draft tree of k3_suffix_drafter_tree by brute-force string counting (a tree
+    extension of P2 with no counterpart in the reference, whose drafts are chains).
+
+    Root: the pending id seq[-1]; its context is the longest suffix of the history that
+    also ends earlier. A context s was followed by id c k(s, c) times (end positions
+    p <= T-2 of s with seq[p+1] == c); its children are the `branch` most frequent c (ties:
+    the smaller id), each with probability k / sum(k). A context never followed backs off
+    to its longest proper suffix with more end positions while that suffix keeps >= min_len
+    ids. Best-first by the product of probabilities (ties: the earliest candidate), up to
+    max_nodes nodes and depth max_depth. Returns (tok, parent)."""
+    seq = list(seq)
+    T = len(seq)
+
+    def ends(s):
+        m = len(s)
+        return [p for p in range(m - 1, T) if seq[p - m + 1:p + 1] == s]
+
+    def follows(s):
+        f = {}
+        for p in ends(s):
+            if p <= T - 2:
+                f[seq[p + 1]] = f.get(seq[p + 1], 0) + 1
+        return f
+
+    def backoff(s):
+        e = len(ends(s))
+        for m in range(len(s) - 1, 0, -1):
+            if len(ends(s[-m:])) != e:
+                return s[-m:]
+        return []
+
+    tok, parent = [seq[-1]], [-1]
+    L = longest_suffix_draft(seq, T, 1)[1]
+    if L == 0 or L < min_len or max_depth < 1 or max_nodes <= 1:
+        return tok, parent
+    cand = []
+
+    def expand(node, s, pp, depth):
+        f = follows(s)
+        while not f:
+            b = backoff(s)
+            if not b or len(b) < min_len:
+                return
+            s, f = b, follows(b)
+        total = sum(f.values())
+        for c, k in sorted(f.items(), key=lambda kv: (-kv[1], kv[0]))[:max(1, min(branch, 16))]:
+            cand.append((pp * (k / total), node, c, s + [c], depth + 1))
+
+    expand(0, seq[T - L:], 1.0, 0)
+    while len(tok) < max_nodes and cand:
+        best = 0
+        for i in range(1, len(cand)):
+            if cand[i][0] > cand[best][0]:
+                best = i
+        p, par, c, s, depth = cand.pop(best)
+        tok.append(c)
+        parent.append(par)
+        if depth < max_depth:
+            expand(len(tok) - 1, s, p, depth)
+    return tok, parent

@@ -92,3 +92,61 @@ def test_suffix_drafter_long_history_is_linear(k3):
     ids, L, g = d.draft(8, min_len=1)
     assert L > 1000 and g == 5000 and ids == seq[len(seq) - 5000:len(seq) - 5000 + 8]
     d.close()
+
+
+@pytest.mark.parametrize("seed,vocab,branch,depth,min_len",
+                         [(11, 2, 2, 8, 1), (12, 3, 4, 6, 1), (13, 6, 4, 8, 2), (14, 20, 3, 5, 1)])
+def test_suffix_tree_vs_oracle_restatement(k3, seed, vocab, branch, depth, min_len):
+    """The draft tree at every history length against the brute-force string-counting
+    restatement: same ids, same parents, same order (exact, including probability ties)."""
+    rng = np.random.default_rng(seed)
+    seq = rng.integers(0, vocab, 90).tolist()
+    seq += seq[10:40]                                   # a planted repeat
+    d = k3.SuffixDrafter(len(seq))
+    for T in range(1, len(seq) + 1):
+        d.push([seq[T - 1]])
+        for nodes in (64, 9):
+            got = d.tree(nodes, branch, depth, min_len)
+            assert got == O.suffix_tree_draft(seq[:T], nodes, branch, depth, min_len), (T, nodes)
+    d.close()
+
+
+def test_suffix_tree_shape_and_verify_masks(k3):
+    """A strictly periodic history gives one chain, P2's periodic draft; a noisy one gives
+    a bushy tree whose parents precede children within the depth and branching limits and
+    which fits the verify masks."""
+    rng = np.random.default_rng(21)
+    base = rng.integers(0, 50, 37).tolist()
+    seq = base * 5 + base[:11]
+    d = k3.SuffixDrafter(len(seq))
+    d.push(seq)
+    tok, par = d.tree(64, 3, 8, 1)
+    assert tok == [seq[-1]] + d.draft(8, 1)[0] and par == list(range(-1, 8))
+    assert d.tree(1, 3, 8, 1) == ([seq[-1]], [-1])
+    assert d.tree(64, 3, 0, 1) == ([seq[-1]], [-1])     # depth 0: the root alone
+    d.close()
+
+    noisy = []
+    for r in range(12):
+        row = list(base)
+        for j in rng.choice(len(row), 4, replace=False):
+            row[j] = int(rng.integers(0, 6))
+        noisy += row
+    d = k3.SuffixDrafter(len(noisy))
+    d.push(noisy)
+    tok, par = d.tree(64, 3, 8, 1)
+    assert tok[0] == noisy[-1] and par[0] == -1 and 9 < len(tok) <= 64
+    depth = [0] * len(tok)
+    for i in range(1, len(tok)):
+        assert 0 <= par[i] < i
+        depth[i] = depth[par[i]] + 1
+        assert depth[i] <= 8
+    assert max(np.bincount(par[1:])) <= 3
+    assert (tok, par) == O.suffix_tree_draft(noisy, 64, 3, 8, 1)
+    masks = O.tree_masks(par)                           # ancestor bitmasks for the verify
+    assert masks.shape[0] == len(tok)
+    d.close()
+    fresh = k3.SuffixDrafter(8)
+    fresh.push([5, 6, 7])                               # nothing repeats: the root alone
+    assert fresh.tree() == ([7], [-1])
+    fresh.close()
