@@ -570,6 +570,31 @@ int k3_suffix_drafter_push(K3SuffixDrafter *d, const int *ids, int n);
 int k3_suffix_drafter_length(const K3SuffixDrafter *d);
 int k3_suffix_drafter_draft(const K3SuffixDrafter *d, int cap, int min_len, int *out,
                             int *match_len, int *period);
+/* P3 of the drafting study (tools/spec_replay.py:340-397, 474-568): P2's draft with an
+ * adaptive length read off an acceptance table q[K3_SPEC_P3_CODES] fitted offline (the
+ * study's fit_acceptance_table). Feature code per draft position: (depth bucket x 13
+ * match-length buckets) x 6 agreement buckets; 255 when the history has no earlier match. */
+#define K3_SPEC_P3_CODES 234
+/* The study's verify-step cost model in units of one plain decode step: a verify over nd
+ * drafts costs a_T + a_E * u(nd + 1) + a_C * (nd + 1) + eps, u(n) = r * (1 - ((r-1)/r)^n)
+ * with r = expert_ratio (routed experts / top-k; 56 for 896 top-16). */
+typedef struct K3SpecCost {
+    double a_T, a_E, a_C, eps, expert_ratio;
+} K3SpecCost;
+/* draft_features: codes[nd] (nd <= 8) for `draft` continuing the current history. */
+int k3_suffix_drafter_features(const K3SuffixDrafter *d, const int *draft, int nd, unsigned char *codes);
+/* adaptive_lengths: cumulative != 0 counts the positions whose cumulative estimate
+ * (product of q over 1..j) exceeds delta; cumulative == 0 the leading positions whose own
+ * estimate does. 0 when codes[0] is 255. */
+int k3_spec_p3_length(const unsigned char *codes, int nd, const double *q, double delta, int cumulative);
+/* cost_aware_lengths: draft j is kept while P_j > S(j+1) - S(j) (+ (P_{j-1} - P_j) R(j-1)
+ * with replay != 0, R the replay pass after a partial acceptance). */
+int k3_spec_p3_cost_length(const unsigned char *codes, int nd, const double *q, const K3SpecCost *cost,
+                           int replay);
+/* The P3 draft: P2's 8-id draft (any match length), its codes, then the delta rule (cost
+ * NULL) or the cost rule; ids out[0..len), len <= cap returned. */
+int k3_suffix_drafter_draft_p3(const K3SuffixDrafter *d, const double *q, double delta, const K3SpecCost *cost,
+                               int replay, int cap, int *out);
 /* A draft TREE for tree verification (no counterpart in the reference, whose drafts are
  * chains): node 0 is the pending id; a node's children are the ids that followed its
  * context in the history, most frequent first (at most `branch`), the context backing off

@@ -93,6 +93,15 @@ class K3StateLayout(C.Structure):
                 ("loop_eps", C.c_double)]
 
 
+class K3SpecCost(C.Structure):
+    """The drafting study's verify-step cost model (units of one plain decode step)."""
+    _fields_ = [("a_T", C.c_double), ("a_E", C.c_double), ("a_C", C.c_double), ("eps", C.c_double),
+                ("expert_ratio", C.c_double)]
+
+
+SPEC_P3_CODES = 234
+
+
 class K3GpuEpGroup(C.Structure):
     _fields_ = [("arena", VP * EP_MAX_WORLD), ("world", I), ("rank", I), ("cap", I), ("L", I), ("K", I),
                 ("n_local", I)]
@@ -169,6 +178,10 @@ _SIGS = {
     "k3_suffix_drafter_length": ([VP], I),
     "k3_suffix_drafter_draft": ([VP, I, I, VP, C.POINTER(I), C.POINTER(I)], I),
     "k3_suffix_drafter_tree": ([VP, I, I, I, I, VP, VP], I),
+    "k3_suffix_drafter_features": ([VP, VP, I, VP], I),
+    "k3_spec_p3_length": ([VP, I, VP, C.c_double, I], I),
+    "k3_spec_p3_cost_length": ([VP, I, VP, VP, I], I),
+    "k3_suffix_drafter_draft_p3": ([VP, VP, C.c_double, VP, I, I, VP], I),
 }
 for _name, (_args, _res) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -605,6 +618,27 @@ def spec_draft_eager(seq, cap=8):
     return list(out[:nd])
 
 
+def _p3_table(q):
+    q = [float(v) for v in q]
+    if len(q) != SPEC_P3_CODES:
+        raise ValueError(f"a P3 acceptance table has {SPEC_P3_CODES} entries, got {len(q)}")
+    return (C.c_double * SPEC_P3_CODES)(*q)
+
+
+def spec_p3_length(codes, q, delta, cumulative=True) -> int:
+    """The study's adaptive_lengths for one draft point (k3_spec_p3_length)."""
+    codes = list(codes)
+    arr = (C.c_ubyte * max(len(codes), 1))(*codes)
+    return lib.k3_spec_p3_length(arr, len(codes), _p3_table(q), float(delta), int(bool(cumulative)))
+
+
+def spec_p3_cost_length(codes, q, cost, replay=False) -> int:
+    """The study's cost_aware_lengths for one draft point (k3_spec_p3_cost_length)."""
+    codes = list(codes)
+    arr = (C.c_ubyte * max(len(codes), 1))(*codes)
+    return lib.k3_spec_p3_cost_length(arr, len(codes), _p3_table(q), C.byref(cost), int(bool(replay)))
+
+
 class SuffixDrafter:
     """The drafting study's P2 as an incremental host drafter (k3_suffix_drafter_*): push
     ids as they are accepted, draft() after each step. No GPU."""
@@ -636,6 +670,24 @@ class SuffixDrafter:
         par = (C.c_int * max_nodes)()
         n = lib.k3_suffix_drafter_tree(self._d, max_nodes, branch, max_depth, min_len, tok, par)
         return list(tok[:n]), list(par[:n])
+
+    def features(self, draft):
+        """P3 feature codes of `draft` continuing the history (k3_suffix_drafter_features);
+        255 at every position when the history has no earlier match."""
+        draft = list(draft)
+        arr = (C.c_int * max(len(draft), 1))(*draft)
+        codes = (C.c_ubyte * max(len(draft), 1))()
+        check(lib.k3_suffix_drafter_features(self._d, arr, len(draft), codes), "k3_suffix_drafter_features")
+        return list(codes[:len(draft)])
+
+    def draft_p3(self, q, delta=0.22, cost=None, replay=False, cap=8):
+        """The P3 draft: P2's draft cut by the acceptance table q (delta rule, or the cost
+        rule when `cost` is a K3SpecCost)."""
+        qa = _p3_table(q)
+        out = (C.c_int * max(cap, 1))()
+        nd = lib.k3_suffix_drafter_draft_p3(self._d, qa, float(delta), C.byref(cost) if cost is not None else None,
+                                            int(bool(replay)), cap, out)
+        return list(out[:nd])
 
     def close(self) -> None:
         if self._d:

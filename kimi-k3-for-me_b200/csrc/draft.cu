@@ -17,6 +17,7 @@
 // describe the history before its last id. Transitions live in one open-addressing hash
 // table keyed by (state, id), with each state's transitions also chained in a list for the
 // clone step.
+#include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -247,6 +248,139 @@ extern "C" int k3_suffix_drafter_draft(const K3SuffixDrafter *d, int cap, int mi
     if (L < min_len || g <= 0) return 0;
     for (int i = 0; i < cap; i++) out[i] = d->seq[e + 1 + (i % g)];
     return cap;
+}
+
+// ---- P3: P2's draft with an adaptive length (tools/spec_replay.py:340-397, 525-568) ----
+// Each draft position j (1-based) gets a feature code from its depth, the effective match
+// length L + j - 1 and the agreement counts of its context (the matched suffix followed
+// by the draft's first j - 1 ids): n, the context's occurrences, and k, those followed by
+// the proposed id, as the automaton's occurrence counts read between extend and commit
+// (the state this drafter keeps between pushes). A table q[code] of acceptance estimates,
+// fitted offline, turns the codes into a length.
+
+namespace {
+
+constexpr int P3_N_ELL = 13, P3_N_AGREE = 6, P3_NO_DRAFT = 255;
+
+int p3_ell_bucket(int ell)
+{
+    static const int edges[P3_N_ELL] = {1, 2, 3, 4, 5, 6, 7, 9, 12, 16, 24, 32, 64};
+    if (ell >= 64) return P3_N_ELL - 1;
+    int b = 0;
+    for (int i = 0; i < P3_N_ELL; i++)
+        if (edges[i] <= ell) b = i;
+    return b;
+}
+
+int p3_agree_bucket(int n, int k)
+{
+    if (k <= 0) return 0;                 // never followed
+    if (n <= 1) return 1;                 // one occurrence
+    if (k >= n) return n <= 3 ? 2 : 3;    // unanimous
+    return 2 * k >= n ? 4 : 5;            // majority / minority
+}
+
+int p3_depth_bucket(int j) { return j == 1 ? 0 : (j <= 3 ? 1 : 2); }
+
+// the cost of a verify step over nd drafts in units of one plain decode step
+// (tools/spec_replay.py:85-96): a_T + a_E * u(nd + 1) + a_C * (nd + 1) + eps, with
+// u(n) = r * (1 - ((r - 1) / r)^n) the expected distinct experts over n positions in units
+// of one position's top-k (r = experts / top-k); a step without drafts costs 1
+double p3_verify_cost(int nd, const K3SpecCost *c, double eps)
+{
+    if (nd <= 0) return 1.0;
+    const int n = nd + 1;
+    const double u = c->expert_ratio * (1.0 - pow((c->expert_ratio - 1.0) / c->expert_ratio, (double)n));
+    return c->a_T + c->a_E * u + c->a_C * n + eps;
+}
+
+// the second pass that restores and replays m + 1 positions after a partial acceptance
+double p3_replay_cost(int m, const K3SpecCost *c)
+{
+    const int n = m + 1;
+    const double u = c->expert_ratio * (1.0 - pow((c->expert_ratio - 1.0) / c->expert_ratio, (double)n));
+    return c->a_T + c->a_E * u + c->a_C * n;
+}
+
+}  // namespace
+
+extern "C" int k3_suffix_drafter_features(const K3SuffixDrafter *d, const int *draft, int nd, uint8_t *codes)
+{
+    if (!d || nd < 0 || nd > SPEC_MAX || (nd > 0 && (!draft || !codes))) return K3GPU_EINVAL;
+    const int v = d->n ? d->link[d->last] : 0;
+    if (v <= 0) {
+        for (int j = 0; j < nd; j++) codes[j] = (uint8_t)P3_NO_DRAFT;
+        return K3GPU_OK;
+    }
+    const int L = d->len[v];
+    int w = v;
+    for (int j = 0; j < nd; j++) {
+        int n = 0, k = 0, w2 = -1;
+        if (w >= 0) {
+            n = d->cnt[w];
+            w2 = get(d, w, draft[j]);
+            k = w2 >= 0 ? d->cnt[w2] : 0;
+        }
+        codes[j] = (uint8_t)((p3_depth_bucket(j + 1) * P3_N_ELL + p3_ell_bucket(L + j)) * P3_N_AGREE +
+                             p3_agree_bucket(n, k));
+        w = w2;
+    }
+    return K3GPU_OK;
+}
+
+extern "C" int k3_spec_p3_length(const uint8_t *codes, int nd, const double *q, double delta, int cumulative)
+{
+    if (!codes || !q || nd <= 0 || codes[0] == P3_NO_DRAFT) return 0;
+    if (nd > SPEC_MAX) nd = SPEC_MAX;
+    int len = 0;
+    double P = 1.0;
+    bool run = true;
+    for (int j = 0; j < nd; j++) {
+        if (codes[j] >= K3_SPEC_P3_CODES) return 0;
+        const double qj = q[codes[j]];
+        if (cumulative) {
+            P = j == 0 ? qj : P * qj;   // positions whose cumulative estimate exceeds delta
+            len += P > delta;
+        } else {
+            run = run && qj > delta;    // the leading positions each above delta
+            len += run;
+        }
+    }
+    return len;
+}
+
+extern "C" int k3_spec_p3_cost_length(const uint8_t *codes, int nd, const double *q, const K3SpecCost *cost,
+                                      int replay)
+{
+    if (!codes || !q || !cost || nd <= 0 || codes[0] == P3_NO_DRAFT) return 0;
+    if (!(cost->expert_ratio >= 1.0)) return 0;
+    if (nd > SPEC_MAX) nd = SPEC_MAX;
+    double prev = 1.0, P = 1.0;
+    for (int j = 1; j <= nd; j++) {
+        if (codes[j - 1] >= K3_SPEC_P3_CODES) return 0;
+        P = j == 1 ? q[codes[0]] : P * q[codes[j - 1]];
+        double extra = p3_verify_cost(j, cost, cost->eps) - p3_verify_cost(j - 1, cost, cost->eps);
+        if (replay) extra = extra + (prev - P) * p3_replay_cost(j - 1, cost);
+        if (!(P > extra)) return j - 1;
+        prev = P;
+    }
+    return nd;
+}
+
+extern "C" int k3_suffix_drafter_draft_p3(const K3SuffixDrafter *d, const double *q, double delta,
+                                          const K3SpecCost *cost, int replay, int cap, int *out)
+{
+    if (!d || !q || cap <= 0 || !out) return 0;
+    if (cap > SPEC_MAX) cap = SPEC_MAX;
+    int draft[SPEC_MAX];
+    uint8_t codes[SPEC_MAX];
+    if (k3_suffix_drafter_draft(d, SPEC_MAX, 1, draft, nullptr, nullptr) != SPEC_MAX) return 0;
+    if (k3_suffix_drafter_features(d, draft, SPEC_MAX, codes) != K3GPU_OK) return 0;
+    int len = cost ? k3_spec_p3_cost_length(codes, SPEC_MAX, q, cost, replay)
+                   : k3_spec_p3_length(codes, SPEC_MAX, q, delta, 1);
+    if (len > cap) len = cap;
+    for (int i = 0; i < len; i++) out[i] = draft[i];
+    return len;
 }
 
 // A draft tree for tree verification. Node 0 is the pending id (the last of the history);

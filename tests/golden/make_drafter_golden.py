@@ -8,6 +8,14 @@ T-1 and before its commit, exactly as analyze_sequence steps, tools/spec_replay.
   L2[T]      the suffix automaton's match length (0: none)
   g2[T]      its period pos - last_end (0: none)
   p2[T]      periodic_copy(seq, last_end + 1, g, 8)  (P2, :333-336, 442-449), -1 padded
+  f3[T]      draft_features of that P2 draft (P3's feature codes, :371-397), 255 without one
+and the P3 lengths of every draft point under three acceptance tables -- the tool's own
+fit_acceptance_table (:474-503) on these sequences' P2 acceptances, and two seeded random
+tables -- by adaptive_lengths (:525-536; delta 0.1, 0.22, 0.55; cumulative and per
+position) and cost_aware_lengths (:539-568; both tiers, with and without replay):
+  q          [3][234] the tables
+  s<i>/p3a   [3][3][2][n+1] adaptive lengths (table, delta, cumulative 1/0)
+  s<i>/p3c   [3][2][2][n+1] cost-aware lengths (table, tier 8GB/128GB, replay 0/1)
 
 Usage: python tests/golden/make_drafter_golden.py [--ref /root/reference]
 """
@@ -52,6 +60,7 @@ def main() -> None:
     spec.loader.exec_module(sr)
     rng = np.random.default_rng(20260)
     arrays = {}
+    feats = []
     for si, seq in enumerate(sequences(rng)):
         s = [int(v) for v in seq]
         n = len(s)
@@ -60,6 +69,8 @@ def main() -> None:
         p2 = np.full((n + 1, CAP), -1, np.int32)
         L2 = np.zeros(n + 1, np.int32)
         g2 = np.zeros(n + 1, np.int32)
+        f3 = np.full((n + 1, CAP), sr.NO_DRAFT, np.uint8)
+        a2 = np.zeros(n + 1, np.int64)
         sam = sr.SuffixAutomaton()
         for pos in range(n):
             v = sam.extend(s[pos], pos)
@@ -73,6 +84,8 @@ def main() -> None:
                 L2[T] = sam.length[v]
                 g2[T] = g
                 p2[T] = sr.periodic_copy(s, e + 1, g, CAP)
+                f3[T] = sr.draft_features(sam, v, sam.length[v], p2[T].tolist())
+                a2[T] = sr._lcp(p2[T].tolist(), s, T, n - T)
                 # the tool's own brute-force check of the automaton
                 bl, be, _ = sr.longest_suffix_match(s, T)
                 assert (bl, be) == (sam.length[v], e), (si, T)
@@ -83,6 +96,29 @@ def main() -> None:
         arrays[f"s{si}/p2"] = p2
         arrays[f"s{si}/L2"] = L2
         arrays[f"s{si}/g2"] = g2
+        arrays[f"s{si}/f3"] = f3
+        feats.append((f3[1:n], a2[1:n], np.arange(n - 1, 0, -1)))
+    # P3 tables: the tool's fit on these draft points, then two seeded random tables
+    F = np.concatenate([f[0] for f in feats])
+    A = np.concatenate([f[1] for f in feats])
+    R = np.concatenate([f[2] for f in feats])
+    q_fit, _ = sr.fit_acceptance_table(F, A, R)
+    qs = np.stack([q_fit, rng.uniform(0.05, 1.0, sr.N_CODES), rng.uniform(0.3, 1.0, sr.N_CODES)])
+    arrays["q"] = qs
+    deltas = (0.1, 0.22, 0.55)
+    for si in range(len(feats)):
+        f3 = arrays[f"s{si}/f3"]
+        p3a = np.zeros((len(qs), len(deltas), 2, len(f3)), np.int32)
+        p3c = np.zeros((len(qs), 2, 2, len(f3)), np.int32)
+        for qi, q in enumerate(qs):
+            for di, dl in enumerate(deltas):
+                p3a[qi, di, 1] = sr.adaptive_lengths(f3, q, dl, cumulative=True)
+                p3a[qi, di, 0] = sr.adaptive_lengths(f3, q, dl, cumulative=False)
+            for ti, tier in enumerate(("8GB", "128GB")):
+                for rp in (0, 1):
+                    p3c[qi, ti, rp] = sr.cost_aware_lengths(f3, q, tier, bool(rp))
+        arrays[f"s{si}/p3a"] = p3a
+        arrays[f"s{si}/p3c"] = p3c
     arrays["n_seq"] = np.int32(len(sequences(np.random.default_rng(20260))))
     path = os.path.join(HERE, "ref_drafters.npz")
     np.savez_compressed(path, **arrays)

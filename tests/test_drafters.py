@@ -150,3 +150,84 @@ def test_suffix_tree_shape_and_verify_masks(k3):
     fresh.push([5, 6, 7])                               # nothing repeats: the root alone
     assert fresh.tree() == ([7], [-1])
     fresh.close()
+
+
+# the study's two verify-cost tiers (tools/spec_replay.py:73-77): trunk streamed from an
+# 8 GB machine, trunk resident at 128 GB; 896 routed experts at top-16 give ratio 56
+TIERS = (("8GB", (0.78, 0.19, 0.03)), ("128GB", (0.44, 0.45, 0.11)))
+DELTAS = (0.1, 0.22, 0.55)
+
+
+def _cost(k3, coef):
+    return k3.K3SpecCost(coef[0], coef[1], coef[2], 0.0, 56.0)
+
+
+@pytest.mark.parametrize("si", range(N_SEQ))
+def test_p3_features_and_lengths_match_reference_tool(k3, si):
+    """P3's feature codes at every draft point, and the adaptive and cost-aware lengths
+    under three tables (the tool's own fit and two random ones), against the tool."""
+    seq = G[f"s{si}/seq"].tolist()
+    f3, p3a, p3c, qs = G[f"s{si}/f3"], G[f"s{si}/p3a"], G[f"s{si}/p3c"], G["q"]
+    d = k3.SuffixDrafter(len(seq))
+    for T in range(1, len(seq) + 1):
+        d.push([seq[T - 1]])
+        ids, L, _ = d.draft(8, min_len=1)
+        codes = d.features(ids if L > 0 else G[f"s{si}/p2"][T].tolist())
+        assert codes == f3[T].tolist(), T
+        for qi, q in enumerate(qs):
+            for di, dl in enumerate(DELTAS):
+                assert k3.spec_p3_length(codes, q, dl, True) == p3a[qi, di, 1, T], (T, qi, dl)
+                assert k3.spec_p3_length(codes, q, dl, False) == p3a[qi, di, 0, T], (T, qi, dl)
+            for ti, (_, coef) in enumerate(TIERS):
+                for rp in (0, 1):
+                    assert k3.spec_p3_cost_length(codes, q, _cost(k3, coef), rp) == p3c[qi, ti, rp, T], \
+                        (T, qi, ti, rp)
+        # the one-call P3 draft is P2's draft cut to the delta-rule length
+        q = qs[0]
+        want = p3a[0, 1, 1, T]
+        assert d.draft_p3(q, 0.22) == (ids[:want] if L > 0 else [])
+        assert d.draft_p3(q, 0.22, cap=2) == (ids[:min(want, 2)] if L > 0 else [])
+        assert d.draft_p3(q, cost=_cost(k3, TIERS[1][1])) == (ids[:p3c[0, 1, 0, T]] if L > 0 else [])
+    d.close()
+
+
+def test_p3_edges(k3):
+    q = np.full(k3.SPEC_P3_CODES, 0.9)
+    assert k3.spec_p3_length([255] * 8, q, 0.1) == 0          # no match: no draft
+    assert k3.spec_p3_length([0] * 8, q, 0.5) == 6             # 0.9^6 = 0.53 > 0.5 > 0.9^7
+    assert k3.spec_p3_length([0] * 8, q, 0.5, cumulative=False) == 8
+    assert k3.spec_p3_length([0] * 3, q, 0.1) == 3             # fewer positions than 8
+    c = k3.K3SpecCost(0.44, 0.45, 0.11, 0.0, 56.0)
+    assert k3.spec_p3_cost_length([0] * 8, np.ones(k3.SPEC_P3_CODES), c) == 8
+    assert k3.spec_p3_cost_length([0] * 8, np.zeros(k3.SPEC_P3_CODES), c) == 0
+    with pytest.raises(ValueError):
+        k3.spec_p3_length([0], q[:10], 0.5)                    # a table of the wrong size
+    d = k3.SuffixDrafter(4)
+    d.push([1, 2, 3])
+    assert d.features([7, 7]) == [255, 255] and d.draft_p3(q) == []
+    d.close()
+
+
+def test_p3_table_fit_matches_reference_tool(k3):
+    """The host fit of the acceptance table reproduces the table the tool fitted on the
+    golden sequences' P2 draft points (codes, accepted prefix, ids left)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "spec_table", os.path.join(os.path.dirname(HERE), "kimi-k3-for-me_b200", "spec_table.py"))
+    st = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(st)
+    F, A, R = [], [], []
+    for si in range(N_SEQ):
+        seq = G[f"s{si}/seq"].tolist()
+        n = len(seq)
+        for T in range(1, n):
+            d = G[f"s{si}/p2"][T].tolist()
+            m = 0
+            while m < min(8, n - T) and seq[T + m] == d[m]:
+                m += 1
+            F.append(G[f"s{si}/f3"][T])
+            A.append(m if G[f"s{si}/L2"][T] > 0 else 0)
+            R.append(n - T)
+    q = st.fit_p3_table(np.array(F), A, R)
+    assert q.shape == (k3.SPEC_P3_CODES,)
+    assert np.array_equal(q, G["q"][0])                  # same operations, same order: exact
