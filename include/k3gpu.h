@@ -37,7 +37,8 @@ enum {
     K3GPU_EINVAL = -1,     /* null pointer, size out of range, misaligned buffer        */
     K3GPU_ECAPACITY = -2,  /* workspace, log or cache capacity too small                */
     K3GPU_ECUDA = -3,      /* a CUDA launch/runtime error; see k3gpu_last_cuda_error()  */
-    K3GPU_EDEVICE = -4     /* a device-side check failed; see k3gpu_device_status()     */
+    K3GPU_EDEVICE = -4,    /* a device-side check failed; see k3gpu_device_status()     */
+    K3GPU_ECALLBACK = -5   /* a caller-supplied callback returned non-zero              */
 };
 
 const char *k3gpu_strerror(int status);
@@ -595,6 +596,63 @@ int k3_spec_p3_cost_length(const unsigned char *codes, int nd, const double *q, 
  * NULL) or the cost rule; ids out[0..len), len <= cap returned. */
 int k3_suffix_drafter_draft_p3(const K3SuffixDrafter *d, const double *q, double delta, const K3SpecCost *cost,
                                int replay, int cap, int *out);
+/* ------------------------------------------------------- speculative decode loop -- */
+/* The engine's incremental decode loop (src/cli/k3_run.c:2812-3047) as a step driver over
+ * two callbacks, so the same bookkeeping drives the device forward:
+ *   verify(ctx, ids, n, base, arg): feed ids[0..n) at positions base..base+n-1, tentatively;
+ *       arg[i] = the model's greedy next id after position base + i; 0 on success.
+ *   commit(ctx, base, keep): keep the first `keep` positions of that verify (the model's
+ *       state advances to base + keep); 0 on success.
+ * Every verify is followed by exactly one commit before the next verify. The first step
+ * reads every id not yet consumed (a prompt, or a resumed pending id plus a new prompt)
+ * and emits the model's next id; later steps draft (policy below) when the context and the
+ * cache have room for spec_n more ids (T + spec_n + 1 < tmax, cached + spec_n + 1 <= kv_cap),
+ * verify the pending id plus the drafts, emit the accepted prefix plus the model's own next
+ * id, and keep what emit_keep allows (gen, tmax, the first stop id; :1300-1317). */
+enum {
+    K3_DRAFT_NONE = 0,   /* serial decode                                       */
+    K3_DRAFT_NGRAM = 1,  /* the engine's spec_draft (n = 4 then 3, agreement)   */
+    K3_DRAFT_EAGER = 2,  /* P1                                                  */
+    K3_DRAFT_SUFFIX = 3, /* P2 (min_len)                                        */
+    K3_DRAFT_P3 = 4      /* P3 (p3_q with p3_delta, or p3_cost and p3_replay)   */
+};
+enum { K3_SPEC_LOOP_GEN = 1, K3_SPEC_LOOP_STOP_ID = 2, K3_SPEC_LOOP_CONTEXT = 3 };
+typedef struct K3SpecLoopCfg {
+    int policy, spec_n, min_len;   /* spec_n <= 8                                          */
+    int gen, tmax, kv_cap;         /* ids to generate; context limit; cache positions      */
+    const int *stop_ids;           /* copied at create                                     */
+    int n_stop;
+    const double *p3_q;            /* [K3_SPEC_P3_CODES], read at every P3 draft           */
+    double p3_delta;
+    const K3SpecCost *p3_cost;     /* NULL: the delta rule                                 */
+    int p3_replay;
+} K3SpecLoopCfg;
+/* The engine's spec counters (:2945-2955) and the histogram of accepted prefixes. */
+typedef struct K3SpecLoopStats {
+    long long steps, sweeps, drafted, accepted, dropped, full, partial, cut;
+    long long hist[9];
+} K3SpecLoopStats;
+/* One step's (nd, m, keep) (the engine's spec_trace, :2946-2949) and the positions fed. */
+typedef struct K3SpecStepTrace {
+    int nd, m, keep, fed;
+} K3SpecStepTrace;
+typedef struct K3SpecLoop K3SpecLoop;
+typedef int (*K3SpecVerifyFn)(void *ctx, const int *ids, int n, int base, int *arg);
+typedef int (*K3SpecCommitFn)(void *ctx, int base, int keep);
+/* ids[0..n_ids): the conversation so far; cached: positions the model has consumed
+ * (0 on a fresh run). NULL on a bad configuration. */
+K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *ids, int n_ids, int cached,
+                                K3SpecVerifyFn verify, K3SpecCommitFn commit, void *ctx);
+void k3_spec_loop_free(K3SpecLoop *L);
+/* One step: out[0..*n_out) the ids kept (<= 9), trace optional. Returns K3GPU_OK, or once
+ * finished K3_SPEC_LOOP_GEN / _STOP_ID / _CONTEXT (this and every later call emit
+ * nothing), or a negative status (K3GPU_ECALLBACK when a callback failed). */
+int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStepTrace *trace);
+/* T, cached, generated count and counters; returns the finished code (0 while running). */
+int k3_spec_loop_state(const K3SpecLoop *L, int *T, int *cached, int *nout, K3SpecLoopStats *stats);
+/* The conversation's ids (ids[0..T), cap >= T); returns T. */
+int k3_spec_loop_ids(const K3SpecLoop *L, int *ids, int cap);
+
 /* A draft TREE for tree verification (no counterpart in the reference, whose drafts are
  * chains): node 0 is the pending id; a node's children are the ids that followed its
  * context in the history, most frequent first (at most `branch`), the context backing off

@@ -101,6 +101,28 @@ class K3SpecCost(C.Structure):
 
 SPEC_P3_CODES = 234
 
+DRAFT_NONE, DRAFT_NGRAM, DRAFT_EAGER, DRAFT_SUFFIX, DRAFT_P3 = range(5)
+SPEC_LOOP_GEN, SPEC_LOOP_STOP_ID, SPEC_LOOP_CONTEXT = 1, 2, 3
+
+
+class K3SpecLoopCfg(C.Structure):
+    _fields_ = [("policy", I), ("spec_n", I), ("min_len", I), ("gen", I), ("tmax", I), ("kv_cap", I),
+                ("stop_ids", VP), ("n_stop", I), ("p3_q", VP), ("p3_delta", C.c_double), ("p3_cost", VP),
+                ("p3_replay", I)]
+
+
+class K3SpecLoopStats(C.Structure):
+    _fields_ = [(n, C.c_longlong) for n in ("steps", "sweeps", "drafted", "accepted", "dropped", "full",
+                                            "partial", "cut")] + [("hist", C.c_longlong * 9)]
+
+
+class K3SpecStepTrace(C.Structure):
+    _fields_ = [("nd", I), ("m", I), ("keep", I), ("fed", I)]
+
+
+SpecVerifyFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_int), C.c_int, C.c_int, C.POINTER(C.c_int))
+SpecCommitFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_int)
+
 
 class K3GpuEpGroup(C.Structure):
     _fields_ = [("arena", VP * EP_MAX_WORLD), ("world", I), ("rank", I), ("cap", I), ("L", I), ("K", I),
@@ -178,6 +200,11 @@ _SIGS = {
     "k3_suffix_drafter_length": ([VP], I),
     "k3_suffix_drafter_draft": ([VP, I, I, VP, C.POINTER(I), C.POINTER(I)], I),
     "k3_suffix_drafter_tree": ([VP, I, I, I, I, VP, VP], I),
+    "k3_spec_loop_create": ([VP, VP, I, I, VP, VP, VP], VP),
+    "k3_spec_loop_free": ([VP], None),
+    "k3_spec_loop_step": ([VP, VP, VP, VP], I),
+    "k3_spec_loop_state": ([VP, VP, VP, VP, VP], I),
+    "k3_spec_loop_ids": ([VP, VP, I], I),
     "k3_suffix_drafter_features": ([VP, VP, I, VP], I),
     "k3_spec_p3_length": ([VP, I, VP, C.c_double, I], I),
     "k3_spec_p3_cost_length": ([VP, I, VP, VP, I], I),
@@ -693,6 +720,102 @@ class SuffixDrafter:
         if self._d:
             lib.k3_suffix_drafter_free(self._d)
             self._d = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 -- interpreter shutdown may have unloaded the library
+            pass
+
+
+class SpecLoop:
+    """The engine's speculative decode loop (k3_spec_loop_*): host bookkeeping over two
+    callables, verify(ids, base) -> the model's next id after each fed position, and
+    commit(base, keep). With device ops behind them it drives the verify forward; on the
+    host it drives any model."""
+
+    def __init__(self, ids, verify, commit, *, cached=0, policy=DRAFT_NGRAM, spec_n=8, min_len=1, gen=64,
+                 tmax=None, kv_cap=None, stop_ids=(), p3_q=None, p3_delta=0.22, p3_cost=None, p3_replay=False):
+        ids = [int(v) for v in ids]
+        tmax = tmax if tmax is not None else len(ids) + gen + 1
+        self._errors = []
+
+        def _verify(_ctx, p, n, base, arg):
+            try:
+                out = verify([p[i] for i in range(n)], base)
+                if len(out) != n:
+                    raise ValueError(f"verify returned {len(out)} ids for {n} positions")
+                for i, v in enumerate(out):
+                    arg[i] = int(v)
+                return 0
+            except Exception as e:  # noqa: BLE001 -- reported by step()
+                self._errors.append(e)
+                return 1
+
+        def _commit(_ctx, base, keep):
+            try:
+                commit(base, keep)
+                return 0
+            except Exception as e:  # noqa: BLE001
+                self._errors.append(e)
+                return 1
+
+        self._L = None
+        self._fns = (SpecVerifyFn(_verify), SpecCommitFn(_commit))
+        self._stop = (C.c_int * max(len(stop_ids), 1))(*stop_ids)
+        self._q = _p3_table(p3_q) if p3_q is not None else None
+        self._cost = p3_cost
+        cfg = K3SpecLoopCfg(policy, spec_n, min_len, gen, tmax, kv_cap if kv_cap is not None else tmax,
+                            C.cast(self._stop, VP), len(stop_ids), C.cast(self._q, VP) if self._q else None,
+                            float(p3_delta), C.cast(C.pointer(p3_cost), VP) if p3_cost is not None else None,
+                            int(bool(p3_replay)))
+        arr = (C.c_int * max(len(ids), 1))(*ids)
+        self._L = lib.k3_spec_loop_create(C.byref(cfg), arr, len(ids), cached,
+                                          C.cast(self._fns[0], VP), C.cast(self._fns[1], VP), None)
+        if not self._L:
+            raise K3Error("k3_spec_loop_create: bad configuration")
+        self.tmax = tmax
+
+    def step(self):
+        """(ids kept this step, trace dict); ([], None) once finished."""
+        out = (C.c_int * 9)()
+        n = C.c_int(0)
+        tr = K3SpecStepTrace()
+        st = lib.k3_spec_loop_step(self._L, out, C.byref(n), C.byref(tr))
+        if st < 0:
+            err = self._errors.pop() if self._errors else None
+            raise K3Error(f"k3_spec_loop_step: {lib.k3gpu_strerror(st).decode()}") from err
+        if st > 0:
+            return [], None
+        return list(out[:n.value]), {"nd": tr.nd, "m": tr.m, "keep": tr.keep, "fed": tr.fed}
+
+    def run(self):
+        """Step until finished; returns (generated ids, per-step traces)."""
+        gen, traces = [], []
+        while True:
+            ids, tr = self.step()
+            if tr is None:
+                return gen, traces
+            gen += ids
+            traces.append(tr)
+
+    def state(self):
+        T, cached, nout = C.c_int(0), C.c_int(0), C.c_int(0)
+        s = K3SpecLoopStats()
+        done = lib.k3_spec_loop_state(self._L, C.byref(T), C.byref(cached), C.byref(nout), C.byref(s))
+        stats = {f: getattr(s, f) for f, _ in K3SpecLoopStats._fields_ if f != "hist"}
+        stats["hist"] = list(s.hist)
+        return {"T": T.value, "cached": cached.value, "nout": nout.value, "done": done, "stats": stats}
+
+    def ids(self):
+        buf = (C.c_int * self.tmax)()
+        T = lib.k3_spec_loop_ids(self._L, buf, self.tmax)
+        return list(buf[:T])
+
+    def close(self) -> None:
+        if self._L:
+            lib.k3_spec_loop_free(self._L)
+            self._L = None
 
     def __del__(self):
         try:

@@ -22,7 +22,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 SOURCES = ["abi.cu", "router.cu", "moe.cu", "moe_mma.cu", "moe_tc.cu", "kda.cu", "mla.cu", "accept.cu",
-           "norm.cu", "mmw.cu", "layer.cu", "ep.cu", "draft.cu", "st.cu", "state.cu"]
+           "norm.cu", "mmw.cu", "layer.cu", "ep.cu", "draft.cu", "st.cu", "state.cu",
+           "loop.cu"]
 
 
 def _stale(target: str, deps: list[str]) -> bool:

@@ -16,6 +16,7 @@ extern "C" const char *k3gpu_strerror(int status)
     case K3GPU_ECAPACITY: return "capacity exceeded (workspace, log or cache too small)";
     case K3GPU_ECUDA: return "CUDA runtime error (see k3gpu_last_cuda_error)";
     case K3GPU_EDEVICE: return "device-side check failed (see k3gpu_device_status)";
+    case K3GPU_ECALLBACK: return "a caller-supplied callback failed";
     default: return "unknown status";
     }
 }

@@ -1,0 +1,200 @@
+// loop.cu -- host C++: the engine's speculative decode loop (src/cli/k3_run.c:2812-3047)
+// as a step driver over two callbacks, so the same bookkeeping runs the device forward.
+//
+// The loop keeps the conversation's ids (seq[0..T)), the positions the model has consumed
+// (cached; the last id stays pending, cached = T - 1 between steps) and the generated ids.
+// A step
+//   * on the first call reads everything not yet consumed (seq[cached..T)) -- the prompt,
+//     or on a resume the carried pending id plus the new prompt -- and emits the model's
+//     next id (k3_run.c:2820-2854);
+//   * later, drafts up to spec_n ids when the context and the cache have room for a full
+//     draft (:2859, the same condition as the engine), verifies the pending id plus the
+//     nd drafts in one pass, accepts the longest prefix the model agrees with and emits it
+//     plus the model's own next id (:2909-2927); with nothing drafted, one serial position
+//     (:2968-2975);
+//   * keeps as many emitted ids as emit_keep allows (--gen, the context limit, the first
+//     stop id; :1300-1317), commits exactly the positions behind them (:2941-2943), and
+//     appends them (:3029-3043).
+// Every verify call is followed by exactly one commit call before the next verify.
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "k3gpu.h"
+
+struct K3SpecLoop {
+    K3SpecLoopCfg cfg;
+    int *stop;                  // a copy of cfg.stop_ids
+    K3SpecVerifyFn verify;
+    K3SpecCommitFn commit;
+    void *ctx;
+    int *seq;                   // [tmax]
+    int T, cached, nout, started, done;
+    int *arg;                   // [max(prefill, spec_n + 1)]
+    int arg_cap;
+    K3SuffixDrafter *sam;       // P2 / P3 history
+    K3SpecLoopStats st;
+};
+
+namespace {
+
+// how many of a step's emitted ids the output keeps (src/cli/k3_run.c:1300-1317)
+int emit_keep(const K3SpecLoop *L, const int *emit, int emitn)
+{
+    int k = 0;
+    while (k < emitn && L->nout + k < L->cfg.gen && L->T + k < L->cfg.tmax) {
+        const int id = emit[k++];
+        for (int s = 0; s < L->cfg.n_stop; s++)
+            if (id == L->stop[s]) return k;
+    }
+    return k;
+}
+
+int draft(K3SpecLoop *L, int *d)
+{
+    const K3SpecLoopCfg &c = L->cfg;
+    switch (c.policy) {
+        case K3_DRAFT_NGRAM: return k3_spec_draft_ngram(L->seq, L->T, c.spec_n, 4, 3, d);
+        case K3_DRAFT_EAGER: return k3_spec_draft_eager(L->seq, L->T, c.spec_n, d);
+        case K3_DRAFT_SUFFIX: return k3_suffix_drafter_draft(L->sam, c.spec_n, c.min_len, d, nullptr, nullptr);
+        case K3_DRAFT_P3:
+            return k3_suffix_drafter_draft_p3(L->sam, c.p3_q, c.p3_delta, c.p3_cost, c.p3_replay, c.spec_n, d);
+        default: return 0;
+    }
+}
+
+// append the kept ids to the history, the output and the drafter
+int append(K3SpecLoop *L, const int *emit, int keep, int *out)
+{
+    for (int i = 0; i < keep; i++) {
+        L->seq[L->T++] = emit[i];
+        if (out) out[i] = emit[i];
+        L->nout++;
+    }
+    if (L->sam && keep > 0 && k3_suffix_drafter_push(L->sam, emit, keep) != K3GPU_OK) return K3GPU_EINVAL;
+    for (int s = 0; keep > 0 && s < L->cfg.n_stop; s++)
+        if (emit[keep - 1] == L->stop[s]) L->done = K3_SPEC_LOOP_STOP_ID;
+    if (!L->done && L->nout >= L->cfg.gen) L->done = K3_SPEC_LOOP_GEN;
+    if (!L->done && L->T >= L->cfg.tmax) L->done = K3_SPEC_LOOP_CONTEXT;
+    return K3GPU_OK;
+}
+
+}  // namespace
+
+extern "C" K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *ids, int n_ids, int cached,
+                                           K3SpecVerifyFn verify, K3SpecCommitFn commit, void *ctx)
+{
+    if (!cfg || !ids || !verify || !commit || n_ids <= 0 || cached < 0 || cached >= n_ids) return nullptr;
+    if (cfg->tmax < n_ids || cfg->gen < 0 || cfg->spec_n < 0 || cfg->spec_n > 8 || cfg->n_stop < 0 ||
+        (cfg->n_stop > 0 && !cfg->stop_ids) || cfg->kv_cap < n_ids)
+        return nullptr;
+    if (cfg->policy < K3_DRAFT_NONE || cfg->policy > K3_DRAFT_P3) return nullptr;
+    if (cfg->policy == K3_DRAFT_P3 && !cfg->p3_q) return nullptr;
+    K3SpecLoop *L = (K3SpecLoop *)calloc(1, sizeof(K3SpecLoop));
+    if (!L) return nullptr;
+    L->cfg = *cfg;
+    L->verify = verify;
+    L->commit = commit;
+    L->ctx = ctx;
+    L->arg_cap = (n_ids - cached) > (cfg->spec_n + 1) ? (n_ids - cached) : (cfg->spec_n + 1);
+    L->seq = (int *)malloc(sizeof(int) * (size_t)cfg->tmax);
+    L->arg = (int *)malloc(sizeof(int) * (size_t)L->arg_cap);
+    L->stop = (int *)malloc(sizeof(int) * (size_t)(cfg->n_stop > 0 ? cfg->n_stop : 1));
+    const bool sam = cfg->policy == K3_DRAFT_SUFFIX || cfg->policy == K3_DRAFT_P3;
+    if (sam) L->sam = k3_suffix_drafter_create(cfg->tmax);
+    if (!L->seq || !L->arg || !L->stop || (sam && !L->sam)) {
+        k3_spec_loop_free(L);
+        return nullptr;
+    }
+    memcpy(L->seq, ids, sizeof(int) * (size_t)n_ids);
+    if (cfg->n_stop > 0) memcpy(L->stop, cfg->stop_ids, sizeof(int) * (size_t)cfg->n_stop);
+    L->cfg.stop_ids = L->stop;
+    L->T = n_ids;
+    L->cached = cached;
+    if (L->sam && k3_suffix_drafter_push(L->sam, ids, n_ids) != K3GPU_OK) {
+        k3_spec_loop_free(L);
+        return nullptr;
+    }
+    return L;
+}
+
+extern "C" void k3_spec_loop_free(K3SpecLoop *L)
+{
+    if (!L) return;
+    free(L->seq);
+    free(L->arg);
+    free(L->stop);
+    k3_suffix_drafter_free(L->sam);
+    free(L);
+}
+
+extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStepTrace *trace)
+{
+    if (n_out) *n_out = 0;
+    if (trace) memset(trace, 0, sizeof *trace);
+    if (!L) return K3GPU_EINVAL;
+    if (L->done) return L->done;
+    int emit[9], emitn = 0, keep = 0;
+    const int base = L->cached;
+    if (!L->started) {
+        // the first step: every position not yet consumed, never tentative in the engine
+        const int n = L->T - base;
+        if (L->verify(L->ctx, L->seq + base, n, base, L->arg) != 0) return K3GPU_ECALLBACK;
+        if (L->commit(L->ctx, base, n) != 0) return K3GPU_ECALLBACK;
+        L->cached = base + n;
+        L->started = 1;
+        emit[emitn++] = L->arg[n - 1];
+        keep = emit_keep(L, emit, emitn);
+        if (trace) *trace = K3SpecStepTrace{0, 0, keep, n};
+    } else {
+        int d[8], nd = 0;
+        const K3SpecLoopCfg &c = L->cfg;
+        if (c.policy != K3_DRAFT_NONE && L->T + c.spec_n + 1 < c.tmax && base + c.spec_n + 1 <= c.kv_cap)
+            nd = draft(L, d);
+        int ids[9];
+        ids[0] = L->seq[base];
+        for (int i = 0; i < nd; i++) ids[1 + i] = d[i];
+        if (L->verify(L->ctx, ids, nd + 1, base, L->arg) != 0) return K3GPU_ECALLBACK;
+        int m = 0;
+        while (m < nd && L->arg[m] == d[m]) m++;
+        for (int i = 0; i < m; i++) emit[emitn++] = d[i];
+        emit[emitn++] = L->arg[m];
+        keep = emit_keep(L, emit, emitn);
+        // a serial step consumes its one position whatever the output keeps (:2972)
+        const int used = nd > 0 ? keep : 1;
+        if (L->commit(L->ctx, base, used) != 0) return K3GPU_ECALLBACK;
+        L->cached = base + used;
+        if (nd > 0) {
+            L->st.sweeps++;
+            L->st.drafted += nd;
+            L->st.accepted += m;
+            L->st.dropped += nd + 1 - keep;
+            if (m == nd) L->st.full++;
+            else L->st.partial++;
+            if (keep < m + 1) L->st.cut++;
+            L->st.hist[m]++;
+        }
+        if (trace) *trace = K3SpecStepTrace{nd, m, keep, nd + 1};
+    }
+    L->st.steps++;
+    if (append(L, emit, keep, out) != K3GPU_OK) return K3GPU_EINVAL;
+    if (n_out) *n_out = keep;
+    return K3GPU_OK;
+}
+
+extern "C" int k3_spec_loop_state(const K3SpecLoop *L, int *T, int *cached, int *nout, K3SpecLoopStats *stats)
+{
+    if (!L) return K3GPU_EINVAL;
+    if (T) *T = L->T;
+    if (cached) *cached = L->cached;
+    if (nout) *nout = L->nout;
+    if (stats) *stats = L->st;
+    return L->done;
+}
+
+extern "C" int k3_spec_loop_ids(const K3SpecLoop *L, int *ids, int cap)
+{
+    if (!L || !ids || cap < L->T) return K3GPU_EINVAL;
+    memcpy(ids, L->seq, sizeof(int) * (size_t)L->T);
+    return L->T;
+}

@@ -419,3 +419,78 @@ def suffix_tree_draft(seq, max_nodes=64, branch=4, max_depth=8, min_len=1):
         if depth < max_depth:
             expand(len(tok) - 1, s, p, depth)
     return tok, parent
+
+
+def emit_keep(emit, nout, gen, T, tmax, stops):
+    """How many of a step's emitted ids the output keeps (src/cli/k3_run.c:1300-1317)."""
+    k = 0
+    while k < len(emit) and nout + k < gen and T + k < tmax:
+        k += 1
+        if emit[k - 1] in stops:
+            return k
+    return k
+
+
+def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, stops):
+    """The engine's incremental speculative loop (src/cli/k3_run.c:2812-3047) over a greedy
+    model given as next_id(context ids) -> id. Policies 0 none, 1 the engine's n-gram
+    spec_draft, 2 P1, 3 P2. Returns (generated ids, [(nd, m, keep, fed)] per step, the
+    engine's counters, cached, ids)."""
+    seq = list(ids)
+    out, trace = [], []
+    st = dict(steps=0, sweeps=0, drafted=0, accepted=0, dropped=0, full=0, partial=0, cut=0)
+    hist = [0] * 9
+    g = 0
+    while len(out) < gen or g == 0:
+        base = cached
+        T = len(seq)
+        if g == 0:                                            # :2820-2854
+            n = T - base
+            emit = [next_id(seq)]
+            cached = T
+            keep = emit_keep(emit, len(out), gen, T, tmax, stops)
+            trace.append((0, 0, keep, n))
+        else:
+            d = []
+            if policy and T + spec_n + 1 < tmax and base + spec_n + 1 <= kv_cap:   # :2859
+                if policy == 1:
+                    buf = np.zeros(max(spec_n, 1), np.int32)
+                    nd = orc().orc_spec_draft(np.asarray(seq, np.int32), T, spec_n, 4, 3, buf)
+                    d = buf[:nd].tolist()
+                elif policy == 2:
+                    d = eager_draft(seq, T, spec_n)
+                elif policy == 3:
+                    dd, L, _ = longest_suffix_draft(seq, T, spec_n)
+                    d = dd if L >= min_len else []
+            nd = len(d)
+            ctx = seq[:base + 1]
+            arg = []
+            for i in range(nd + 1):                           # the verify sweep
+                arg.append(next_id(ctx))
+                if i < nd:
+                    ctx = ctx + [d[i]]
+            m = 0
+            while m < nd and arg[m] == d[m]:
+                m += 1
+            emit = d[:m] + [arg[m]]
+            keep = emit_keep(emit, len(out), gen, T, tmax, stops)
+            cached = base + (keep if nd else 1)
+            if nd:                                            # :2945-2955
+                st["sweeps"] += 1
+                st["drafted"] += nd
+                st["accepted"] += m
+                st["dropped"] += nd + 1 - keep
+                st["full" if m == nd else "partial"] += 1
+                st["cut"] += keep < m + 1
+                hist[m] += 1
+            trace.append((nd, m, keep, nd + 1))
+        st["steps"] += 1
+        g += 1
+        seq += emit[:keep]
+        out += emit[:keep]
+        if keep and emit[keep - 1] in stops:
+            break
+        if len(seq) >= tmax:
+            break
+    st["hist"] = hist
+    return out, trace, st, cached, seq

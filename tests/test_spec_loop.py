@@ -1,0 +1,213 @@
+"""The speculative decode loop (k3_spec_loop_*), host only, over a greedy model on the CPU.
+
+Two checks: the ids it generates equal plain serial greedy decoding of the same model for
+every drafting policy (the property the engine's loop exists to keep,
+src/cli/k3_run.c:2909-2943), and its per-step (nd, m, keep) trace, counters and final
+state equal the oracle's restatement of the engine loop (oracle.spec_loop). The model is a
+deterministic function of the context: mostly an order-2 table over a small vocabulary
+(so drafts are often right), with context-dependent deviations (so they are often wrong).
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(HERE))
+from k3lib import load  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def k3():
+    return load()
+
+
+def make_model(seed, vocab=9, noise=5):
+    rng = np.random.default_rng(seed)
+    table = rng.integers(0, vocab, (vocab, vocab))
+
+    def next_id(ctx):
+        if len(ctx) % noise == 0 and sum(ctx[-3:]) % 3 == 0:
+            return (sum(ctx[-4:]) * 7 + len(ctx)) % vocab
+        return int(table[ctx[-2] if len(ctx) > 1 else 0][ctx[-1]])
+    return next_id
+
+
+class Fake:
+    """A model that holds its consumed positions and checks the verify/commit protocol."""
+
+    def __init__(self, next_id, consumed):
+        self.next_id, self.state, self.pending = next_id, list(consumed), None
+        self.calls = []
+
+    def verify(self, ids, base):
+        assert base == len(self.state) and self.pending is None
+        self.pending = list(ids)
+        self.calls.append(len(ids))
+        return [self.next_id(self.state + ids[:i + 1]) for i in range(len(ids))]
+
+    def commit(self, base, keep):
+        assert base == len(self.state) and self.pending is not None and 0 <= keep <= len(self.pending)
+        self.state += self.pending[:keep]
+        self.pending = None
+
+
+def serial(next_id, ids, gen, tmax, stops):
+    seq, out = list(ids), []
+    while len(out) < gen and len(seq) < tmax:
+        v = next_id(seq)
+        seq.append(v)
+        out.append(v)
+        if v in stops:
+            break
+    return out
+
+
+CASES = [  # policy, spec_n, min_len, gen, stop ids ("late": the ids serial decode first emits late), seed
+    (0, 8, 1, 40, (), 1), (1, 8, 1, 120, (), 2), (2, 8, 1, 120, (), 3), (3, 8, 1, 120, (), 4),
+    (3, 4, 3, 90, (), 5), (1, 3, 1, 200, "late", 6), (2, 8, 1, 200, "late", 7), (3, 8, 2, 200, "late", 8),
+    (1, 8, 1, 7, (), 9), (3, 8, 1, 0, (), 10), (3, 8, 1, 61, (), 14), (3, 8, 1, 77, (), 15),
+    (3, 6, 1, 200, "late", 16), (2, 8, 1, 53, (), 17),
+]
+
+
+def late_stop(nid, prompt, gen):
+    """Among the prompt's ids (so drafts can carry it), the one serial decode first emits
+    latest (after 30 ids)."""
+    out = serial(nid, prompt, gen, len(prompt) + gen + 1, ())
+    first = {}
+    for i, v in enumerate(out):
+        if v in prompt:
+            first.setdefault(v, i)
+    if not first:
+        return ()
+    v, i = max(first.items(), key=lambda kv: kv[1])
+    return (v,) if i >= 30 else ()
+
+
+@pytest.mark.parametrize("policy,spec_n,min_len,gen,stops,seed", CASES)
+def test_loop_equals_serial_decode_and_engine_restatement(k3, policy, spec_n, min_len, gen, stops, seed):
+    nid = make_model(seed, vocab=12 if stops == "late" else 9)
+    rng = np.random.default_rng(100 + seed)
+    prompt = rng.integers(0, 9, 24).tolist()
+    prompt += prompt[4:14]
+    if stops == "late":
+        stops = late_stop(nid, prompt, gen)
+    tmax = len(prompt) + gen + 1 + (20 if seed % 2 == 0 else 0)   # even seeds: headroom past gen
+    m = Fake(nid, [])
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=policy, spec_n=spec_n, min_len=min_len, gen=gen,
+                       tmax=tmax, stop_ids=stops)
+    out, traces = loop.run()
+    assert out == serial(nid, prompt, gen, tmax, stops)
+    rout, rtrace, rst, rcached, rseq = O.spec_loop(nid, prompt, 0, policy, spec_n, min_len, gen, tmax, tmax,
+                                                   set(stops))
+    assert out == rout
+    assert [(t["nd"], t["m"], t["keep"], t["fed"]) for t in traces] == rtrace
+    s = loop.state()
+    assert s["stats"] == rst and s["cached"] == rcached and loop.ids() == rseq
+    assert m.state == rseq[:rcached]                      # the model consumed exactly the kept ids
+    assert s["done"] in (k3.SPEC_LOOP_GEN, k3.SPEC_LOOP_STOP_ID, k3.SPEC_LOOP_CONTEXT)
+    assert loop.step() == ([], None)                       # finished: nothing more
+    if policy and len(out) > 30:
+        assert s["stats"]["sweeps"] > 0 and s["stats"]["accepted"] > 0
+        assert s["stats"]["partial"] > 0                   # the model does reject drafts
+    loop.close()
+
+
+def test_stop_id_inside_an_accepted_draft(k3):
+    """A cyclic model accepts every draft; a stop id in the middle of an accepted draft cuts
+    the sweep there (emit_keep), the state commits only up to it, and decoding ends."""
+    nid = lambda ctx: (ctx[-1] + 1) % 6  # noqa: E731
+    prompt = list(range(6)) * 3 + [0]
+    for policy in (k3.DRAFT_NGRAM, k3.DRAFT_EAGER, k3.DRAFT_SUFFIX):
+        m = Fake(nid, [])
+        loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=policy, gen=50, tmax=200, stop_ids=(4,))
+        out, traces = loop.run()
+        assert out == [1, 2, 3, 4] == serial(nid, prompt, 50, 200, (4,))
+        s = loop.state()
+        # the n-gram drafter (agreement gate) drafts only [2, 3] here: the stop id is the model's own
+        assert s["done"] == k3.SPEC_LOOP_STOP_ID and s["stats"]["cut"] == (policy != k3.DRAFT_NGRAM)
+        assert s["cached"] == len(prompt) + 3 and m.state == loop.ids()[:s["cached"]]
+        rout, rtrace, rst, rcached, _ = O.spec_loop(nid, prompt, 0, policy, 8, 1, 50, 200, 200, {4})
+        assert [(t["nd"], t["m"], t["keep"], t["fed"]) for t in traces] == rtrace and s["stats"] == rst
+        loop.close()
+
+
+def test_cases_reach_the_cut_paths(k3):
+    """Among the cases, some sweep is cut short by the gen limit."""
+    cuts = {"gen": 0, "stop": 0}
+    for policy, spec_n, min_len, gen, stops, seed in CASES:
+        nid = make_model(seed, vocab=12 if stops == "late" else 9)
+        rng = np.random.default_rng(100 + seed)
+        prompt = rng.integers(0, 9, 24).tolist()
+        prompt += prompt[4:14]
+        st = late_stop(nid, prompt, gen) if stops == "late" else stops
+        tmax = len(prompt) + gen + 1 + (20 if seed % 2 == 0 else 0)
+        out, tr, rst, _, _ = O.spec_loop(nid, prompt, 0, policy, spec_n, min_len, gen, tmax, tmax, set(st))
+        if rst["cut"]:
+            cuts["stop" if out and out[-1] in st else "gen"] += 1
+    assert cuts["gen"] > 0, cuts
+
+
+def test_loop_p3_policy_and_context_limits(k3):
+    nid = make_model(11)
+    prompt = list(range(9)) * 3
+    q = np.full(k3.SPEC_P3_CODES, 0.8)
+    for cost in (None, k3.K3SpecCost(0.44, 0.45, 0.11, 0.0, 56.0)):
+        m = Fake(nid, [])
+        loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_P3, gen=80, p3_q=q, p3_cost=cost)
+        out, traces = loop.run()
+        assert out == serial(nid, prompt, 80, len(prompt) + 81, ())
+        assert max(t["nd"] for t in traces) > 0
+        loop.close()
+    # the context limit: drafting stops once T + spec_n + 1 reaches tmax, decoding at tmax
+    m = Fake(nid, [])
+    tmax = len(prompt) + 30
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_SUFFIX, gen=100, tmax=tmax)
+    out, traces = loop.run()
+    assert len(prompt) + len(out) == tmax and out == serial(nid, prompt, 100, tmax, ())
+    assert loop.state()["done"] == k3.SPEC_LOOP_CONTEXT
+    assert all(t["nd"] == 0 for t, T in zip(traces[1:], np.cumsum([len(prompt)] + [t["keep"] for t in traces])[1:])
+               if T + 8 + 1 >= tmax)
+    # a small cache: drafting needs cached + spec_n + 1 <= kv_cap
+    m = Fake(nid, [])
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_SUFFIX, gen=40, kv_cap=len(prompt) + 5)
+    out, traces = loop.run()
+    assert out == serial(nid, prompt, 40, len(prompt) + 41, ()) and all(t["nd"] == 0 for t in traces)
+    loop.close()
+
+
+def test_loop_resume_reads_pending_plus_new_prompt(k3):
+    """A resumed conversation: the model consumed all but the pending id; the first step
+    feeds the pending id plus the new prompt (k3_run.c:2820-2828)."""
+    nid = make_model(12)
+    first = list(range(9)) * 2 + [3, 1, 4]
+    m = Fake(nid, first[:-1])
+    new = [1, 5, 9 % 9, 2, 6]
+    loop = k3.SpecLoop(first + new, m.verify, m.commit, cached=len(first) - 1, policy=k3.DRAFT_NGRAM, gen=30)
+    out, traces = loop.run()
+    assert traces[0]["fed"] == len(new) + 1 and m.calls[0] == len(new) + 1
+    assert out == serial(nid, first + new, 30, len(first + new) + 31, ())
+    loop.close()
+
+
+def test_loop_errors(k3):
+    nid = make_model(13)
+    m = Fake(nid, [])
+    with pytest.raises(k3.K3Error):
+        k3.SpecLoop([1, 2], m.verify, m.commit, cached=2)            # nothing left to read
+    with pytest.raises(k3.K3Error):
+        k3.SpecLoop([1, 2], m.verify, m.commit, spec_n=9)            # above the draft cap
+    with pytest.raises(k3.K3Error):
+        k3.SpecLoop([1, 2], m.verify, m.commit, policy=k3.DRAFT_P3)  # P3 without a table
+
+    def bad_verify(ids, base):
+        raise RuntimeError("device lost")
+    loop = k3.SpecLoop([1, 2, 3], bad_verify, m.commit)
+    with pytest.raises(k3.K3Error) as e:
+        loop.step()
+    assert isinstance(e.value.__cause__, RuntimeError)
+    loop.close()
