@@ -494,3 +494,45 @@ def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, 
             break
     st["hist"] = hist
     return out, trace, st, cached, seq
+
+
+def kda_chunked(state, q, k, v, alpha, beta, qscale, chunk=64):
+    """The chunked parallel form of the KDA recurrence, in float64: the checker for a
+    chunked prefill (the reference runs only the sequential k3_kda_step,
+    src/core/k3_ops.c:303-360, and records the chunked form's properties as properties of
+    the algorithm, include/k3/k3.h:51-60).
+
+    Per chunk of n positions from state S0 (rows = key channels), with g_t the cumulative
+    log decay through position t and ratios r_ts = exp(g_t - g_s) <= 1 for s <= t: the
+    delta-rule writes w_t = beta_t (v_t - S'_t^T k_t) solve the unit lower-triangular
+    system (I + A) W = diag(beta) (V - (Gamma K) S0), A_ts = beta_t sum_i k_s k_t r_ts (s < t,
+    the UT transform; Akk's diagonal is dropped); outputs o_t = S0^T (Gamma_t q_t) +
+    sum_{s <= t} (sum_i k_s q_t r_ts) w_s (Aqk keeps its diagonal: the output reads the
+    updated state); the next state is Gamma_n S0 + sum_s (Gamma_n / Gamma_s k_s) w_s^T.
+    (The delta-rule chunking of Yang et al., "Parallelizing Linear Transformers with the
+    Delta Rule over Sequence Length", NeurIPS 2024, with a per-channel decay.)
+    Returns (o [T][H][D] f32, state [H][D][D] f32)."""
+    T, H, D = q.shape
+    S = np.asarray(state, np.float64).reshape(H, D, D).copy()
+    o = np.zeros((T, H, D))
+    for h in range(H):
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            n = c1 - c0
+            Q = np.asarray(q[c0:c1, h], np.float64) * np.float64(np.float32(qscale))
+            K = np.asarray(k[c0:c1, h], np.float64)
+            V = np.asarray(v[c0:c1, h], np.float64)
+            B = np.asarray(beta[c0:c1, h], np.float64)
+            g = np.cumsum(np.log(np.maximum(np.asarray(alpha[c0:c1, h], np.float64), 1e-300)), axis=0)
+            diff = g[:, None, :] - g[None, :, :]                       # [t][s][i]
+            lower = np.tril(np.ones((n, n), bool))
+            R = np.exp(np.where(lower[:, :, None], diff, -np.inf))
+            Akk = np.tril(np.einsum("si,ti,tsi->ts", K, K, R), -1) * B[:, None]
+            Aqk = np.einsum("si,ti,tsi->ts", K, Q, R)
+            rhs = B[:, None] * (V - (K * np.exp(g)) @ S[h])
+            W = np.zeros((n, D))
+            for t in range(n):                                         # forward substitution
+                W[t] = rhs[t] - Akk[t, :t] @ W[:t]
+            o[c0:c1, h] = (Q * np.exp(g)) @ S[h] + Aqk @ W
+            S[h] = np.exp(g[-1])[:, None] * S[h] + (K * np.exp(g[-1][None, :] - g)).T @ W
+    return o.astype(np.float32), S.astype(np.float32)
