@@ -599,10 +599,13 @@ int k3_suffix_drafter_draft_p3(const K3SuffixDrafter *d, const double *q, double
 /* ------------------------------------------------------- speculative decode loop -- */
 /* The engine's incremental decode loop (src/cli/k3_run.c:2812-3047) as a step driver over
  * two callbacks, so the same bookkeeping drives the device forward:
- *   verify(ctx, ids, n, base, arg): feed ids[0..n) at positions base..base+n-1, tentatively;
- *       arg[i] = the model's greedy next id after position base + i; 0 on success.
- *   commit(ctx, base, keep): keep the first `keep` positions of that verify (the model's
- *       state advances to base + keep); 0 on success.
+ *   verify(ctx, ids, parent, n, base, arg): feed ids[0..n) tentatively from position base;
+ *       parent NULL: a chain at positions base..base+n-1; else a draft tree (parent[0] = -1,
+ *       parent[i] < i; node i sits at depth(i) past base and attends to its ancestors).
+ *       arg[i] = the model's greedy next id after node i; 0 on success.
+ *   commit(ctx, base, path, keep): keep `keep` positions of that verify -- the first keep
+ *       (path NULL) or the tree nodes path[0..keep), root first -- so the model's state
+ *       advances to base + keep; 0 on success.
  * Every verify is followed by exactly one commit before the next verify. The first step
  * reads every id not yet consumed (a prompt, or a resumed pending id plus a new prompt)
  * and emits the model's next id; later steps draft (policy below) when the context and the
@@ -614,7 +617,10 @@ enum {
     K3_DRAFT_NGRAM = 1,  /* the engine's spec_draft (n = 4 then 3, agreement)   */
     K3_DRAFT_EAGER = 2,  /* P1                                                  */
     K3_DRAFT_SUFFIX = 3, /* P2 (min_len)                                        */
-    K3_DRAFT_P3 = 4      /* P3 (p3_q with p3_delta, or p3_cost and p3_replay)   */
+    K3_DRAFT_P3 = 4,     /* P3 (p3_q with p3_delta, or p3_cost and p3_replay)   */
+    K3_DRAFT_TREE = 5    /* a draft tree (k3_suffix_drafter_tree: tree_nodes,
+                            tree_branch, depth spec_n, min_len), accepted as
+                            k3gpu_accept_tree_greedy does                       */
 };
 enum { K3_SPEC_LOOP_GEN = 1, K3_SPEC_LOOP_STOP_ID = 2, K3_SPEC_LOOP_CONTEXT = 3 };
 typedef struct K3SpecLoopCfg {
@@ -626,6 +632,7 @@ typedef struct K3SpecLoopCfg {
     double p3_delta;
     const K3SpecCost *p3_cost;     /* NULL: the delta rule                                 */
     int p3_replay;
+    int tree_nodes, tree_branch;   /* the tree policy: nodes <= 64 per verify, children    */
 } K3SpecLoopCfg;
 /* The engine's spec counters (:2945-2955) and the histogram of accepted prefixes. */
 typedef struct K3SpecLoopStats {
@@ -637,8 +644,8 @@ typedef struct K3SpecStepTrace {
     int nd, m, keep, fed;
 } K3SpecStepTrace;
 typedef struct K3SpecLoop K3SpecLoop;
-typedef int (*K3SpecVerifyFn)(void *ctx, const int *ids, int n, int base, int *arg);
-typedef int (*K3SpecCommitFn)(void *ctx, int base, int keep);
+typedef int (*K3SpecVerifyFn)(void *ctx, const int *ids, const int *parent, int n, int base, int *arg);
+typedef int (*K3SpecCommitFn)(void *ctx, int base, const int *path, int keep);
 /* ids[0..n_ids): the conversation so far; cached: positions the model has consumed
  * (0 on a fresh run). NULL on a bad configuration. */
 K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *ids, int n_ids, int cached,

@@ -101,14 +101,14 @@ class K3SpecCost(C.Structure):
 
 SPEC_P3_CODES = 234
 
-DRAFT_NONE, DRAFT_NGRAM, DRAFT_EAGER, DRAFT_SUFFIX, DRAFT_P3 = range(5)
+DRAFT_NONE, DRAFT_NGRAM, DRAFT_EAGER, DRAFT_SUFFIX, DRAFT_P3, DRAFT_TREE = range(6)
 SPEC_LOOP_GEN, SPEC_LOOP_STOP_ID, SPEC_LOOP_CONTEXT = 1, 2, 3
 
 
 class K3SpecLoopCfg(C.Structure):
     _fields_ = [("policy", I), ("spec_n", I), ("min_len", I), ("gen", I), ("tmax", I), ("kv_cap", I),
                 ("stop_ids", VP), ("n_stop", I), ("p3_q", VP), ("p3_delta", C.c_double), ("p3_cost", VP),
-                ("p3_replay", I)]
+                ("p3_replay", I), ("tree_nodes", I), ("tree_branch", I)]
 
 
 class K3SpecLoopStats(C.Structure):
@@ -120,8 +120,9 @@ class K3SpecStepTrace(C.Structure):
     _fields_ = [("nd", I), ("m", I), ("keep", I), ("fed", I)]
 
 
-SpecVerifyFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_int), C.c_int, C.c_int, C.POINTER(C.c_int))
-SpecCommitFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_int)
+SpecVerifyFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int, C.c_int,
+                           C.POINTER(C.c_int))
+SpecCommitFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_int), C.c_int)
 
 
 class K3GpuEpGroup(C.Structure):
@@ -730,19 +731,21 @@ class SuffixDrafter:
 
 class SpecLoop:
     """The engine's speculative decode loop (k3_spec_loop_*): host bookkeeping over two
-    callables, verify(ids, base) -> the model's next id after each fed position, and
-    commit(base, keep). With device ops behind them it drives the verify forward; on the
-    host it drives any model."""
+    callables, verify(ids, base, parent) -> the model's next id after each fed node
+    (parent None for a chain), and commit(base, keep, path) (path None: the first keep
+    positions; else the accepted tree nodes). With device ops behind them it drives the
+    verify forward; on the host it drives any model."""
 
     def __init__(self, ids, verify, commit, *, cached=0, policy=DRAFT_NGRAM, spec_n=8, min_len=1, gen=64,
-                 tmax=None, kv_cap=None, stop_ids=(), p3_q=None, p3_delta=0.22, p3_cost=None, p3_replay=False):
+                 tmax=None, kv_cap=None, stop_ids=(), p3_q=None, p3_delta=0.22, p3_cost=None, p3_replay=False,
+                 tree_nodes=64, tree_branch=4):
         ids = [int(v) for v in ids]
         tmax = tmax if tmax is not None else len(ids) + gen + 1
         self._errors = []
 
-        def _verify(_ctx, p, n, base, arg):
+        def _verify(_ctx, p, par, n, base, arg):
             try:
-                out = verify([p[i] for i in range(n)], base)
+                out = verify([p[i] for i in range(n)], base, [par[i] for i in range(n)] if par else None)
                 if len(out) != n:
                     raise ValueError(f"verify returned {len(out)} ids for {n} positions")
                 for i, v in enumerate(out):
@@ -752,9 +755,9 @@ class SpecLoop:
                 self._errors.append(e)
                 return 1
 
-        def _commit(_ctx, base, keep):
+        def _commit(_ctx, base, path, keep):
             try:
-                commit(base, keep)
+                commit(base, keep, [path[i] for i in range(keep)] if path else None)
                 return 0
             except Exception as e:  # noqa: BLE001
                 self._errors.append(e)
@@ -768,7 +771,7 @@ class SpecLoop:
         cfg = K3SpecLoopCfg(policy, spec_n, min_len, gen, tmax, kv_cap if kv_cap is not None else tmax,
                             C.cast(self._stop, VP), len(stop_ids), C.cast(self._q, VP) if self._q else None,
                             float(p3_delta), C.cast(C.pointer(p3_cost), VP) if p3_cost is not None else None,
-                            int(bool(p3_replay)))
+                            int(bool(p3_replay)), tree_nodes, tree_branch)
         arr = (C.c_int * max(len(ids), 1))(*ids)
         self._L = lib.k3_spec_loop_create(C.byref(cfg), arr, len(ids), cached,
                                           C.cast(self._fns[0], VP), C.cast(self._fns[1], VP), None)

@@ -16,6 +16,10 @@
 //     stop id; :1300-1317), commits exactly the positions behind them (:2941-2943), and
 //     appends them (:3029-3043).
 // Every verify call is followed by exactly one commit call before the next verify.
+// With the tree policy the draft is a tree (k3_suffix_drafter_tree): verify gets the
+// nodes' parents, acceptance follows k3gpu_accept_tree_greedy (a child is accepted when
+// its parent is and its id is the parent's next id; the lowest-index such child wins),
+// and commit gets the accepted path's nodes.
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -30,8 +34,9 @@ struct K3SpecLoop {
     void *ctx;
     int *seq;                   // [tmax]
     int T, cached, nout, started, done;
-    int *arg;                   // [max(prefill, spec_n + 1)]
+    int *arg;                   // [max(prefill, spec_n + 1, tree_nodes)]
     int arg_cap;
+    int *tok, *parent;          // the tree draft [tree_nodes]
     K3SuffixDrafter *sam;       // P2 / P3 history
     K3SpecLoopStats st;
 };
@@ -63,6 +68,24 @@ int draft(K3SpecLoop *L, int *d)
     }
 }
 
+// greedy acceptance over a draft tree (k3gpu_accept_tree_greedy): path[0] = 0, the root
+int tree_accept(const int *tok, const int *parent, int n, const int *arg, int *path)
+{
+    int len = 1, node = 0;
+    path[0] = 0;
+    for (;;) {
+        int next = -1;
+        for (int c = node + 1; c < n; c++)
+            if (parent[c] == node && tok[c] == arg[node]) {
+                next = c;
+                break;
+            }
+        if (next < 0) return len;
+        path[len++] = next;
+        node = next;
+    }
+}
+
 // append the kept ids to the history, the output and the drafter
 int append(K3SpecLoop *L, const int *emit, int keep, int *out)
 {
@@ -88,7 +111,9 @@ extern "C" K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *
     if (cfg->tmax < n_ids || cfg->gen < 0 || cfg->spec_n < 0 || cfg->spec_n > 8 || cfg->n_stop < 0 ||
         (cfg->n_stop > 0 && !cfg->stop_ids) || cfg->kv_cap < n_ids)
         return nullptr;
-    if (cfg->policy < K3_DRAFT_NONE || cfg->policy > K3_DRAFT_P3) return nullptr;
+    if (cfg->policy < K3_DRAFT_NONE || cfg->policy > K3_DRAFT_TREE) return nullptr;
+    if (cfg->policy == K3_DRAFT_TREE && (cfg->tree_nodes < 1 || cfg->tree_nodes > 64 || cfg->tree_branch < 1))
+        return nullptr;
     if (cfg->policy == K3_DRAFT_P3 && !cfg->p3_q) return nullptr;
     K3SpecLoop *L = (K3SpecLoop *)calloc(1, sizeof(K3SpecLoop));
     if (!L) return nullptr;
@@ -97,12 +122,15 @@ extern "C" K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *
     L->commit = commit;
     L->ctx = ctx;
     L->arg_cap = (n_ids - cached) > (cfg->spec_n + 1) ? (n_ids - cached) : (cfg->spec_n + 1);
+    if (cfg->policy == K3_DRAFT_TREE && L->arg_cap < cfg->tree_nodes) L->arg_cap = cfg->tree_nodes;
     L->seq = (int *)malloc(sizeof(int) * (size_t)cfg->tmax);
     L->arg = (int *)malloc(sizeof(int) * (size_t)L->arg_cap);
     L->stop = (int *)malloc(sizeof(int) * (size_t)(cfg->n_stop > 0 ? cfg->n_stop : 1));
-    const bool sam = cfg->policy == K3_DRAFT_SUFFIX || cfg->policy == K3_DRAFT_P3;
+    const bool sam = cfg->policy == K3_DRAFT_SUFFIX || cfg->policy == K3_DRAFT_P3 || cfg->policy == K3_DRAFT_TREE;
     if (sam) L->sam = k3_suffix_drafter_create(cfg->tmax);
-    if (!L->seq || !L->arg || !L->stop || (sam && !L->sam)) {
+    L->tok = (int *)malloc(sizeof(int) * (size_t)L->arg_cap);
+    L->parent = (int *)malloc(sizeof(int) * (size_t)L->arg_cap);
+    if (!L->seq || !L->arg || !L->stop || !L->tok || !L->parent || (sam && !L->sam)) {
         k3_spec_loop_free(L);
         return nullptr;
     }
@@ -124,6 +152,8 @@ extern "C" void k3_spec_loop_free(K3SpecLoop *L)
     free(L->seq);
     free(L->arg);
     free(L->stop);
+    free(L->tok);
+    free(L->parent);
     k3_suffix_drafter_free(L->sam);
     free(L);
 }
@@ -139,13 +169,44 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
     if (!L->started) {
         // the first step: every position not yet consumed, never tentative in the engine
         const int n = L->T - base;
-        if (L->verify(L->ctx, L->seq + base, n, base, L->arg) != 0) return K3GPU_ECALLBACK;
-        if (L->commit(L->ctx, base, n) != 0) return K3GPU_ECALLBACK;
+        if (L->verify(L->ctx, L->seq + base, nullptr, n, base, L->arg) != 0) return K3GPU_ECALLBACK;
+        if (L->commit(L->ctx, base, nullptr, n) != 0) return K3GPU_ECALLBACK;
         L->cached = base + n;
         L->started = 1;
         emit[emitn++] = L->arg[n - 1];
         keep = emit_keep(L, emit, emitn);
         if (trace) *trace = K3SpecStepTrace{0, 0, keep, n};
+    } else if (L->cfg.policy == K3_DRAFT_TREE) {
+        const K3SpecLoopCfg &c = L->cfg;
+        int n = 1;
+        L->tok[0] = L->seq[base];
+        L->parent[0] = -1;
+        if (L->T + c.spec_n + 1 < c.tmax && base + c.tree_nodes <= c.kv_cap)
+            n = k3_suffix_drafter_tree(L->sam, c.tree_nodes, c.tree_branch, c.spec_n, c.min_len, L->tok, L->parent);
+        if (n < 1) return K3GPU_EINVAL;
+        if (L->verify(L->ctx, L->tok, L->parent, n, base, L->arg) != 0) return K3GPU_ECALLBACK;
+        int path[9];
+        const int plen = tree_accept(L->tok, L->parent, n, L->arg, path);
+        const int m = plen - 1, nd = n - 1;
+        for (int i = 1; i < plen; i++) emit[emitn++] = L->tok[path[i]];
+        emit[emitn++] = L->arg[path[plen - 1]];
+        keep = emit_keep(L, emit, emitn);
+        const int used = nd > 0 ? keep : 1;
+        if (L->commit(L->ctx, base, path, used) != 0) return K3GPU_ECALLBACK;
+        L->cached = base + used;
+        if (nd > 0) {
+            L->st.sweeps++;
+            L->st.drafted += nd;
+            L->st.accepted += m;
+            L->st.dropped += nd + 1 - keep;
+            bool leaf = true;   // full: the accepted path ran to the end of its branch
+            for (int i = path[plen - 1] + 1; i < n && leaf; i++) leaf = L->parent[i] != path[plen - 1];
+            if (leaf) L->st.full++;
+            else L->st.partial++;
+            if (keep < m + 1) L->st.cut++;
+            L->st.hist[m]++;
+        }
+        if (trace) *trace = K3SpecStepTrace{nd, m, keep, n};
     } else {
         int d[8], nd = 0;
         const K3SpecLoopCfg &c = L->cfg;
@@ -154,7 +215,7 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
         int ids[9];
         ids[0] = L->seq[base];
         for (int i = 0; i < nd; i++) ids[1 + i] = d[i];
-        if (L->verify(L->ctx, ids, nd + 1, base, L->arg) != 0) return K3GPU_ECALLBACK;
+        if (L->verify(L->ctx, ids, nullptr, nd + 1, base, L->arg) != 0) return K3GPU_ECALLBACK;
         int m = 0;
         while (m < nd && L->arg[m] == d[m]) m++;
         for (int i = 0; i < m; i++) emit[emitn++] = d[i];
@@ -162,7 +223,7 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
         keep = emit_keep(L, emit, emitn);
         // a serial step consumes its one position whatever the output keeps (:2972)
         const int used = nd > 0 ? keep : 1;
-        if (L->commit(L->ctx, base, used) != 0) return K3GPU_ECALLBACK;
+        if (L->commit(L->ctx, base, nullptr, used) != 0) return K3GPU_ECALLBACK;
         L->cached = base + used;
         if (nd > 0) {
             L->st.sweeps++;

@@ -431,11 +431,14 @@ def emit_keep(emit, nout, gen, T, tmax, stops):
     return k
 
 
-def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, stops):
+def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, stops, tree_nodes=64,
+              tree_branch=4):
     """The engine's incremental speculative loop (src/cli/k3_run.c:2812-3047) over a greedy
     model given as next_id(context ids) -> id. Policies 0 none, 1 the engine's n-gram
-    spec_draft, 2 P1, 3 P2. Returns (generated ids, [(nd, m, keep, fed)] per step, the
-    engine's counters, cached, ids)."""
+    spec_draft, 2 P1, 3 P2, 5 a suffix draft tree (suffix_tree_draft, depth spec_n) with
+    greedy tree acceptance (a child is accepted when its parent is and its id is the
+    parent's next id, the lowest index first). Returns (generated ids,
+    [(nd, m, keep, fed)] per step, the engine's counters, cached, ids)."""
     seq = list(ids)
     out, trace = [], []
     st = dict(steps=0, sweeps=0, drafted=0, accepted=0, dropped=0, full=0, partial=0, cut=0)
@@ -450,6 +453,38 @@ def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, 
             cached = T
             keep = emit_keep(emit, len(out), gen, T, tmax, stops)
             trace.append((0, 0, keep, n))
+        elif policy == 5:
+            tok, par = [seq[base]], [-1]
+            if T + spec_n + 1 < tmax and base + tree_nodes <= kv_cap:
+                tok, par = suffix_tree_draft(seq, tree_nodes, tree_branch, spec_n, min_len)
+            n = len(tok)
+
+            def ctx_of(i):
+                p = []
+                while i >= 0:
+                    p.append(tok[i])
+                    i = par[i]
+                return seq[:base] + p[::-1]
+            arg = [next_id(ctx_of(i)) for i in range(n)]
+            path = [0]
+            while True:
+                kids = [c for c in range(n) if par[c] == path[-1] and tok[c] == arg[path[-1]]]
+                if not kids:
+                    break
+                path.append(kids[0])
+            m, nd = len(path) - 1, n - 1
+            emit = [tok[i] for i in path[1:]] + [arg[path[-1]]]
+            keep = emit_keep(emit, len(out), gen, T, tmax, stops)
+            cached = base + (keep if nd else 1)
+            if nd:
+                st["sweeps"] += 1
+                st["drafted"] += nd
+                st["accepted"] += m
+                st["dropped"] += nd + 1 - keep
+                st["full" if path[-1] not in par else "partial"] += 1
+                st["cut"] += keep < m + 1
+                hist[m] += 1
+            trace.append((nd, m, keep, n))
         else:
             d = []
             if policy and T + spec_n + 1 < tmax and base + spec_n + 1 <= kv_cap:   # :2859

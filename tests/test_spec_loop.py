@@ -43,15 +43,32 @@ class Fake:
         self.next_id, self.state, self.pending = next_id, list(consumed), None
         self.calls = []
 
-    def verify(self, ids, base):
+    def verify(self, ids, base, parent=None):
         assert base == len(self.state) and self.pending is None
-        self.pending = list(ids)
+        self.pending = (list(ids), parent)
         self.calls.append(len(ids))
-        return [self.next_id(self.state + ids[:i + 1]) for i in range(len(ids))]
+        if parent is None:
+            return [self.next_id(self.state + ids[:i + 1]) for i in range(len(ids))]
+        assert parent[0] == -1 and all(0 <= parent[i] < i for i in range(1, len(ids)))
 
-    def commit(self, base, keep):
-        assert base == len(self.state) and self.pending is not None and 0 <= keep <= len(self.pending)
-        self.state += self.pending[:keep]
+        def path(i):
+            p = []
+            while i >= 0:
+                p.append(ids[i])
+                i = parent[i]
+            return p[::-1]
+        return [self.next_id(self.state + path(i)) for i in range(len(ids))]
+
+    def commit(self, base, keep, path=None):
+        assert base == len(self.state) and self.pending is not None
+        ids, parent = self.pending
+        assert 0 <= keep <= len(ids)
+        if path is None:
+            self.state += ids[:keep]
+        else:                                   # a root-first chain of the tree's nodes
+            assert parent is not None and path[0] == 0
+            assert all(parent[path[i]] == path[i - 1] for i in range(1, keep))
+            self.state += [ids[i] for i in path]
         self.pending = None
 
 
@@ -71,6 +88,7 @@ CASES = [  # policy, spec_n, min_len, gen, stop ids ("late": the ids serial deco
     (3, 4, 3, 90, (), 5), (1, 3, 1, 200, "late", 6), (2, 8, 1, 200, "late", 7), (3, 8, 2, 200, "late", 8),
     (1, 8, 1, 7, (), 9), (3, 8, 1, 0, (), 10), (3, 8, 1, 61, (), 14), (3, 8, 1, 77, (), 15),
     (3, 6, 1, 200, "late", 16), (2, 8, 1, 53, (), 17),
+    (5, 8, 1, 120, (), 18), (5, 4, 1, 150, (), 19), (5, 8, 2, 200, "late", 20), (5, 8, 1, 61, (), 22),
 ]
 
 
@@ -204,7 +222,7 @@ def test_loop_errors(k3):
     with pytest.raises(k3.K3Error):
         k3.SpecLoop([1, 2], m.verify, m.commit, policy=k3.DRAFT_P3)  # P3 without a table
 
-    def bad_verify(ids, base):
+    def bad_verify(ids, base, parent=None):
         raise RuntimeError("device lost")
     loop = k3.SpecLoop([1, 2, 3], bad_verify, m.commit)
     with pytest.raises(k3.K3Error) as e:
