@@ -205,6 +205,17 @@ int k3gpu_kda_verify(float *o, const float *state, const float *q, const float *
  * without a host round trip); entries outside 0..T are clamped to that range and
  * flagged in the device status word. The log operands are those given to
  * k3gpu_kda_verify, [B][T][H][D] (beta [B][T][H]). */
+/* A prompt's positions read into the carried state in one launch: the KDA recurrence in
+ * its chunked (UT-transform) form, 32 positions per chunk, for B sequences of T positions
+ * (any T >= 1). state [B][H][D][D] is updated in place to the state after position T-1;
+ * o [B][T][H][D] (may be NULL) receives the outputs; q, k, v, alpha [B][T][H][D], beta
+ * [B][T][H]; q is multiplied by qscale first. Equal to k3_kda_step chained over t to
+ * fp32 rounding (the sums are reordered). D in {32, 64, 128}. The reference has no
+ * chunked path (include/k3/k3.h:51-60); it reads prompts with the sequential step. */
+int k3gpu_kda_prefill(float *state, float *o, const float *q, const float *k, const float *v,
+                      const float *alpha, const float *beta, int B, int T, int H, int D, float qscale,
+                      void *stream);
+
 int k3gpu_kda_commit(float *state, const float *k, const float *v, const float *alpha,
                      const float *beta, const int *n, int B, int T, int H, int D,
                      void *stream);

@@ -151,6 +151,7 @@ _SIGS = {
     "k3gpu_moe_phase_ms": ([C.POINTER(F), I], I),
     "k3gpu_kda_verify": ([VP, VP, VP, VP, VP, VP, VP, I, I, I, I, F, VP], I),
     "k3gpu_kda_commit": ([VP, VP, VP, VP, VP, VP, I, I, I, I, VP], I),
+    "k3gpu_kda_prefill": ([VP] * 7 + [I, I, I, I, F, VP], I),
     "k3gpu_kda_prologue": ([VP] * 14 + [I, I, I, I, I, F, VP], I),
     "k3gpu_kda_commit_conv": ([VP, VP, VP, I, I, I, I, I, VP], I),
     "k3gpu_kda_norm_gate": ([VP, VP, VP, I, I, I, F, VP], I),
@@ -370,6 +371,16 @@ def kda_commit(state, k, v, alpha, beta, n, stream=None):
     B, T, H, D = k.shape
     check(lib.k3gpu_kda_commit(ptr(state), ptr(k), ptr(v), ptr(alpha), ptr(beta), ptr(n), B, T,
                                H, D, stream_ptr(stream)), "k3gpu_kda_commit")
+
+
+def kda_prefill(state, q, k, v, alpha, beta, qscale, outputs=True, stream=None):
+    """Read T positions into the carried state in place (chunked form); returns the
+    outputs [B][T][H][D], or None with outputs=False."""
+    B, T, H, D = q.shape
+    o = torch.empty_like(q) if outputs else None
+    check(lib.k3gpu_kda_prefill(ptr(state), ptr(o) if o is not None else None, ptr(q), ptr(k), ptr(v), ptr(alpha),
+                                ptr(beta), B, T, H, D, float(qscale), stream_ptr(stream)), "k3gpu_kda_prefill")
+    return o
 
 
 def kda_prologue(q, k, v, z, b, q_conv, k_conv, v_conv, hist, A_log, dt_bias, H, D, K, lb,

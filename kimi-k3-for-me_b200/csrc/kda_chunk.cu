@@ -1,0 +1,205 @@
+// kda_chunk.cu -- KDA prefill in the chunked (UT-transform) form: a prompt's positions
+// consumed into the carried state in chunks of KC positions instead of one at a time.
+//
+// The reference reads a prompt with the sequential recurrence only (k3_kda_step,
+// src/core/k3_ops.c:303-360); this is the parallel form of the same recurrence (the
+// delta-rule chunking of Yang et al., NeurIPS 2024, with the per-channel decay). Per
+// chunk of n positions from state S0 (rows = key channels i, columns = value channels j),
+// with g_t[i] the cumulative log2 decay through position t and r_ts[i] = 2^(g_t - g_s):
+//   A_ts  = beta_t sum_i k_s k_t r_ts           (s < t)   the UT transform's matrix
+//   Aq_ts = sum_i k_s q_t r_ts                  (s <= t)  the output's (diagonal kept)
+//   (I + A) W = diag(beta) (V - (2^g . K) S0)             forward substitution
+//   o_t   = S0^T (2^g_t . q_t) + sum_{s<=t} Aq_ts w_s
+//   S     = 2^g_n . S0 + sum_s (2^(g_n - g_s) . k_s) w_s^T
+// Column j of S evolves from k, q, alpha, beta and v[j] alone, so one CTA owns one
+// 32-column slice of one (sequence, head) state, resident in shared memory across the
+// chunks; the chunk's pair sums are recomputed by each slice. fp32 throughout: agrees
+// with the sequential recurrence to rounding (not bit for bit -- the sums are reordered).
+#include <float.h>
+#include <math.h>
+
+#include "common.cuh"
+
+namespace k3 {
+
+constexpr int KC = 32;        // positions per chunk
+constexpr int KSL = 32;       // value columns per CTA
+constexpr int KTHREADS = 256;
+
+template <int D>
+struct KdaChunkSmem {
+    static constexpr int P = D + 1;   // padded row stride: pair sums read rows s = lane
+    static constexpr int K = 0, Q = K + KC * P, G = Q + KC * P, KG = G + KC * P, V = KG + KC * P,
+                         W = V + KC * KSL, A = W + KC * KSL, AQ = A + KC * (KC + 1), S = AQ + KC * (KC + 1),
+                         BETA = S + D * KSL, FLOATS = BETA + KC;
+    static constexpr size_t BYTES = sizeof(float) * FLOATS;
+};
+
+// grid (H, B, D / KSL), block KTHREADS. state [B][H][D][D] updated in place; q, k, v,
+// alpha [B][T][H][D], beta [B][T][H]; o [B][T][H][D] (may be NULL).
+template <int D>
+__global__ void __launch_bounds__(KTHREADS) kda_chunk_kernel(float *__restrict__ state, float *__restrict__ o,
+                                                            const float *__restrict__ q,
+                                                            const float *__restrict__ k,
+                                                            const float *__restrict__ v,
+                                                            const float *__restrict__ al,
+                                                            const float *__restrict__ beta, int T, int H,
+                                                            float qscale)
+{
+    using L = KdaChunkSmem<D>;
+    constexpr int P = L::P;
+    extern __shared__ float sm[];
+    float *sK = sm + L::K, *sQ = sm + L::Q, *sG = sm + L::G, *sKG = sm + L::KG, *sV = sm + L::V,
+          *sW = sm + L::W, *sA = sm + L::A, *sAQ = sm + L::AQ, *sS = sm + L::S, *sB = sm + L::BETA;
+    const int h = blockIdx.x, b = blockIdx.y, j0 = blockIdx.z * KSL;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = KTHREADS / 32;
+
+    float *Sg = state + (((size_t)b * H + h) * D) * D;
+    for (int e = tid; e < D * KSL; e += KTHREADS) {
+        const int i = e / KSL, j = e % KSL;
+        sS[i * KSL + j] = Sg[(size_t)i * D + j0 + j];
+    }
+
+    for (int c0 = 0; c0 < T; c0 += KC) {
+        const int n = T - c0 < KC ? T - c0 : KC;
+        __syncthreads();   // the previous chunk's readers are done
+        // 1. the chunk's rows; positions past the end are zero (alpha 1, beta 0)
+        for (int e = tid; e < KC * D; e += KTHREADS) {
+            const int t = e / D, i = e % D;
+            float kv = 0.0f, qv = 0.0f, lg = 0.0f;
+            if (t < n) {
+                const size_t off = (((size_t)b * T + c0 + t) * H + h) * D + i;
+                kv = k[off];
+                qv = q[off] * qscale;
+                lg = log2f(fmaxf(al[off], FLT_MIN));
+            }
+            sK[t * P + i] = kv;
+            sQ[t * P + i] = qv;
+            sG[t * P + i] = lg;
+        }
+        for (int e = tid; e < KC * KSL; e += KTHREADS) {
+            const int t = e / KSL, j = e % KSL;
+            sV[t * KSL + j] = t < n ? v[(((size_t)b * T + c0 + t) * H + h) * D + j0 + j] : 0.0f;
+        }
+        if (tid < KC) sB[tid] = tid < n ? beta[((size_t)b * T + c0 + tid) * H + h] : 0.0f;
+        __syncthreads();
+        // 2. cumulative log2 decay per channel
+        for (int i = tid; i < D; i += KTHREADS) {
+            float acc = 0.0f;
+            for (int t = 0; t < KC; t++) {
+                acc += sG[t * P + i];
+                sG[t * P + i] = acc;
+            }
+        }
+        __syncthreads();
+        // 3. the pair sums: warp w takes rows t = w, w + NW, ...; lane = s
+        for (int t = warp; t < KC; t += NW) {
+            const int s = lane;
+            float akk = 0.0f, aqk = 0.0f;
+            if (s <= t) {
+                const float *kt = sK + t * P, *qt = sQ + t * P, *gt = sG + t * P;
+                const float *ks = sK + s * P, *gs = sG + s * P;
+                for (int i = 0; i < D; i++) {
+                    const float r = exp2f(gt[i] - gs[i]);
+                    const float kr = ks[i] * r;
+                    akk = fmaf(kr, kt[i], akk);
+                    aqk = fmaf(kr, qt[i], aqk);
+                }
+            }
+            sA[t * (KC + 1) + s] = s < t ? akk * sB[t] : 0.0f;
+            sAQ[t * (KC + 1) + s] = s <= t ? aqk : 0.0f;
+        }
+        __syncthreads();
+        // 4a. the decayed keys and queries (2^g . k, 2^g . q)
+        for (int e = tid; e < KC * D; e += KTHREADS) {
+            const int t = e / D, i = e % D;
+            const float d = exp2f(sG[t * P + i]);
+            sKG[t * P + i] = sK[t * P + i] * d;
+            sQ[t * P + i] *= d;
+        }
+        __syncthreads();
+        // 4b. right-hand side: beta_t (v_t - S0^T (2^g_t . k_t)), column j = lane
+        for (int t = warp; t < KC; t += NW) {
+            const float *kg = sKG + t * P;
+            float acc = 0.0f;
+            for (int i = 0; i < D; i++) acc = fmaf(kg[i], sS[i * KSL + lane], acc);
+            sW[t * KSL + lane] = sB[t] * (sV[t * KSL + lane] - acc);
+        }
+        __syncthreads();
+        // 5. forward substitution (I + A) W = rhs, one column per lane of warp 0
+        if (warp == 0) {
+            float w[KC];
+#pragma unroll
+            for (int t = 0; t < KC; t++) {
+                float x = sW[t * KSL + lane];
+#pragma unroll
+                for (int s = 0; s < t; s++) x = fmaf(-sA[t * (KC + 1) + s], w[s], x);
+                w[t] = x;
+                sW[t * KSL + lane] = x;
+            }
+        }
+        __syncthreads();
+        // 6. outputs; meanwhile the keys decayed to the chunk's end, 2^(g_n - g_s) . k_s
+        if (o) {
+            for (int t = warp; t < n; t += NW) {
+                const float *qg = sQ + t * P;
+                float acc = 0.0f;
+                for (int i = 0; i < D; i++) acc = fmaf(qg[i], sS[i * KSL + lane], acc);
+                for (int s = 0; s <= t; s++) acc = fmaf(sAQ[t * (KC + 1) + s], sW[s * KSL + lane], acc);
+                o[(((size_t)b * T + c0 + t) * H + h) * D + j0 + lane] = acc;
+            }
+        }
+        for (int e = tid; e < KC * D; e += KTHREADS) {
+            const int t = e / D, i = e % D;
+            sKG[t * P + i] = sK[t * P + i] * exp2f(sG[(KC - 1) * P + i] - sG[t * P + i]);
+        }
+        __syncthreads();
+        // 7. the state at the chunk's end, row i = warp + NW r, column = lane
+        for (int i = warp; i < D; i += NW) {
+            float acc = sS[i * KSL + lane] * exp2f(sG[(KC - 1) * P + i]);
+            for (int s = 0; s < n; s++) acc = fmaf(sKG[s * P + i], sW[s * KSL + lane], acc);
+            sS[i * KSL + lane] = acc;
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < D * KSL; e += KTHREADS) {
+        const int i = e / KSL, j = e % KSL;
+        Sg[(size_t)i * D + j0 + j] = sS[i * KSL + j];
+    }
+}
+
+template <int D>
+static int kda_chunk_launch(float *state, float *o, const float *q, const float *k, const float *v,
+                            const float *alpha, const float *beta, int B, int T, int H, float qscale,
+                            cudaStream_t s)
+{
+    const size_t bytes = KdaChunkSmem<D>::BYTES;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(kda_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+            cudaSuccess)
+            return launch_status();
+        attr = true;
+    }
+    dim3 grid(H, B, D / KSL);
+    kda_chunk_kernel<D><<<grid, KTHREADS, bytes, s>>>(state, o, q, k, v, alpha, beta, T, H, qscale);
+    return launch_status();
+}
+
+}  // namespace k3
+
+extern "C" int k3gpu_kda_prefill(float *state, float *o, const float *q, const float *k, const float *v,
+                                 const float *alpha, const float *beta, int B, int T, int H, int D, float qscale,
+                                 void *stream)
+{
+    if (!state || !q || !k || !v || !alpha || !beta) return K3GPU_EINVAL;
+    if (B <= 0 || T <= 0 || H <= 0 || H > 65535 || B > 65535) return K3GPU_EINVAL;
+    cudaStream_t s = k3::as_stream(stream);
+    switch (D) {
+        case 32: return k3::kda_chunk_launch<32>(state, o, q, k, v, alpha, beta, B, T, H, qscale, s);
+        case 64: return k3::kda_chunk_launch<64>(state, o, q, k, v, alpha, beta, B, T, H, qscale, s);
+        case 128: return k3::kda_chunk_launch<128>(state, o, q, k, v, alpha, beta, B, T, H, qscale, s);
+        default: return K3GPU_EINVAL;
+    }
+}
