@@ -453,6 +453,37 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
         except Exception as ex:  # noqa: BLE001
             rows["kda_c3"] = {"error": str(ex)[:200]}
 
+    # KDA prompt read-in: one 4096-position prompt, 32 heads x 128, chunked (one launch)
+    # against the sequential kernels (verify + commit per 64 positions, 128 launches)
+    if only is None or only == "kda_prefill":
+        try:
+            B, T, H, D = 1, 4096, 32, 128
+            st = torch.randn((B, H, D, D), generator=g, device=dev) * 0.1
+            q = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
+            kk = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
+            v = torch.randn((B, T, H, D), generator=g, device=dev)
+            al = 0.9 + 0.099 * torch.rand((B, T, H, D), generator=g, device=dev)
+            be = torch.sigmoid(torch.randn((B, T, H), generator=g, device=dev))
+            qs = 1.0 / D ** 0.5
+            sc = st.clone()
+            us = timed(lambda: k3.kda_prefill(sc, q, kk, v, al, be, qs), n=5)
+            blocks = [tuple(a[:, t0:t0 + 64].contiguous() for a in (q, kk, v, al, be)) for t0 in range(0, T, 64)]
+            n64 = torch.full((B,), 64, dtype=torch.int32, device=dev)
+            ss = st.clone()
+
+            def sequential():
+                for bq, bk, bv, ba, bb in blocks:
+                    k3.kda_verify(ss, bq, bk, bv, ba, bb, qs)
+                    k3.kda_commit(ss, bk, bv, ba, bb, n64)
+            us_seq = timed(sequential, n=3)
+            nbytes = 5 * q.numel() * 4 + be.numel() * 4 + 2 * st.numel() * 4
+            row = hbm_row(us, nbytes, "B=1 T=4096 H=32 D=128 (one prompt)")
+            row.update({"positions_per_s": round(B * T / (us * 1e-6), 1), "sequential_us": round(us_seq, 2),
+                        "speedup_vs_sequential": round(us_seq / us, 2), "compute": "fp32 CUDA cores"})
+            rows["kda_prefill_4k"] = row
+        except Exception as ex:  # noqa: BLE001
+            rows["kda_prefill"] = {"error": str(ex)[:200]}
+
     # c4 MLA absorbed: 64-node tree (branching 4) over a 32k bf16 latent cache, 64 heads
     if only is None or only == "mla_absorbed_c4":
         try:
@@ -698,7 +729,8 @@ def main():
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="--gpus N > 1: token rows through peer memory (default) or NCCL all-to-all")
     ap.add_argument("--only-row", default=None,
-                    choices=["kda_c3", "mla_absorbed_c4", "trunk_matmul_bf16", "lm_head_bf16_c4", "accept_greedy_vocab"],
+                    choices=["kda_c3", "kda_prefill", "mla_absorbed_c4", "trunk_matmul_bf16", "lm_head_bf16_c4",
+                             "accept_greedy_vocab"],
                     help="time one of the other rows alone and print it (for profiling captures)")
     ap.add_argument("--n-routed", type=int, default=N_ROUTED,
                     help="routed experts (smaller values give small cases for ncu captures)")

@@ -61,28 +61,53 @@ __global__ void __launch_bounds__(KTHREADS) kda_chunk_kernel(float *__restrict__
         sS[i * KSL + j] = Sg[(size_t)i * D + j0 + j];
     }
 
+    // the chunk's raw rows are fetched into registers one chunk ahead, so their loads are
+    // in flight while the chunk before computes; positions past the end read as zero keys,
+    // queries and values, decay 1 and beta 0
+    constexpr int NE = KC * D / KTHREADS, NV = KC * KSL / KTHREADS;
+    float rk[NE], rq[NE], ra[NE], rv[NV], rb = 0.0f;
+    auto fetch = [&](int c) {
+        const int m = T - c < KC ? T - c : KC;
+#pragma unroll
+        for (int r = 0; r < NE; r++) {
+            const int e = tid + r * KTHREADS, t = e / D, i = e % D;
+            rk[r] = 0.0f;
+            rq[r] = 0.0f;
+            ra[r] = 1.0f;
+            if (t < m) {
+                const size_t off = (((size_t)b * T + c + t) * H + h) * D + i;
+                rk[r] = k[off];
+                rq[r] = q[off];
+                ra[r] = al[off];
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < NV; r++) {
+            const int e = tid + r * KTHREADS, t = e / KSL, j = e % KSL;
+            rv[r] = t < m ? v[(((size_t)b * T + c + t) * H + h) * D + j0 + j] : 0.0f;
+        }
+        rb = tid < m ? beta[((size_t)b * T + c + tid) * H + h] : 0.0f;
+    };
+    fetch(0);
+
     for (int c0 = 0; c0 < T; c0 += KC) {
         const int n = T - c0 < KC ? T - c0 : KC;
         __syncthreads();   // the previous chunk's readers are done
-        // 1. the chunk's rows; positions past the end are zero (alpha 1, beta 0)
-        for (int e = tid; e < KC * D; e += KTHREADS) {
-            const int t = e / D, i = e % D;
-            float kv = 0.0f, qv = 0.0f, lg = 0.0f;
-            if (t < n) {
-                const size_t off = (((size_t)b * T + c0 + t) * H + h) * D + i;
-                kv = k[off];
-                qv = q[off] * qscale;
-                lg = log2f(fmaxf(al[off], FLT_MIN));
-            }
-            sK[t * P + i] = kv;
-            sQ[t * P + i] = qv;
-            sG[t * P + i] = lg;
+        // 1. the chunk's rows into shared memory, then the next chunk's loads
+#pragma unroll
+        for (int r = 0; r < NE; r++) {
+            const int e = tid + r * KTHREADS, t = e / D, i = e % D;
+            sK[t * P + i] = rk[r];
+            sQ[t * P + i] = rq[r] * qscale;
+            sG[t * P + i] = log2f(fmaxf(ra[r], FLT_MIN));
         }
-        for (int e = tid; e < KC * KSL; e += KTHREADS) {
-            const int t = e / KSL, j = e % KSL;
-            sV[t * KSL + j] = t < n ? v[(((size_t)b * T + c0 + t) * H + h) * D + j0 + j] : 0.0f;
+#pragma unroll
+        for (int r = 0; r < NV; r++) {
+            const int e = tid + r * KTHREADS;
+            sV[(e / KSL) * KSL + e % KSL] = rv[r];
         }
-        if (tid < KC) sB[tid] = tid < n ? beta[((size_t)b * T + c0 + tid) * H + h] : 0.0f;
+        if (tid < KC) sB[tid] = rb;
+        if (c0 + KC < T) fetch(c0 + KC);
         __syncthreads();
         // 2. cumulative log2 decay per channel
         for (int i = tid; i < D; i += KTHREADS) {
