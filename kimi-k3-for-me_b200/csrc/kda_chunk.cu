@@ -28,12 +28,18 @@ constexpr int KTHREADS = 256;
 
 template <int D>
 struct KdaChunkSmem {
-    static constexpr int P = D + 1;   // padded row stride: pair sums read rows s = lane
+    // rows padded by 4 floats: 16-byte aligned, and 128-bit loads of rows s = lane fall on
+    // distinct banks within each quarter warp (row stride = 4 banks)
+    static constexpr int P = D + 4, PA = KC + 4;
     static constexpr int K = 0, Q = K + KC * P, G = Q + KC * P, KG = G + KC * P, V = KG + KC * P,
-                         W = V + KC * KSL, A = W + KC * KSL, AQ = A + KC * (KC + 1), S = AQ + KC * (KC + 1),
+                         W = V + KC * KSL, A = W + KC * KSL, AQ = A + KC * PA, S = AQ + KC * PA,
                          BETA = S + D * KSL, FLOATS = BETA + KC;
     static constexpr size_t BYTES = sizeof(float) * FLOATS;
+    static_assert(P % 4 == 0 && PA % 4 == 0 && Q % 4 == 0 && V % 4 == 0 && A % 4 == 0 && S % 4 == 0,
+                  "128-bit aligned rows");
 };
+
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
 // grid (H, B, D / KSL), block KTHREADS. state [B][H][D][D] updated in place; q, k, v,
 // alpha [B][T][H][D], beta [B][T][H]; o [B][T][H][D] (may be NULL).
@@ -47,8 +53,10 @@ __global__ void __launch_bounds__(KTHREADS) kda_chunk_kernel(float *__restrict__
                                                             float qscale)
 {
     using L = KdaChunkSmem<D>;
-    constexpr int P = L::P;
-    extern __shared__ float sm[];
+    constexpr int P = L::P, PA = L::PA;
+    constexpr int RT = KC / (KTHREADS / 32);   // rows t per warp in the row-blocked phases
+    constexpr int RI = D / (KTHREADS / 32);    // state rows per warp in the update
+    extern __shared__ __align__(16) float sm[];
     float *sK = sm + L::K, *sQ = sm + L::Q, *sG = sm + L::G, *sKG = sm + L::KG, *sV = sm + L::V,
           *sW = sm + L::W, *sA = sm + L::A, *sAQ = sm + L::AQ, *sS = sm + L::S, *sB = sm + L::BETA;
     const int h = blockIdx.x, b = blockIdx.y, j0 = blockIdx.z * KSL;
@@ -118,38 +126,73 @@ __global__ void __launch_bounds__(KTHREADS) kda_chunk_kernel(float *__restrict__
             }
         }
         __syncthreads();
-        // 3. the pair sums: warp w takes rows t = w, w + NW, ...; lane = s
-        for (int t = warp; t < KC; t += NW) {
+        // 3. the pair sums: lane = s, the warp's rows t = warp + NW r together, so row s's
+        //    keys and decays are loaded once per 4 channels for RT rows
+        {
             const int s = lane;
-            float akk = 0.0f, aqk = 0.0f;
-            if (s <= t) {
-                const float *kt = sK + t * P, *qt = sQ + t * P, *gt = sG + t * P;
-                const float *ks = sK + s * P, *gs = sG + s * P;
-                for (int i = 0; i < D; i++) {
-                    const float r = exp2f(gt[i] - gs[i]);
-                    const float kr = ks[i] * r;
-                    akk = fmaf(kr, kt[i], akk);
-                    aqk = fmaf(kr, qt[i], aqk);
+            float akk[RT], aqk[RT];
+#pragma unroll
+            for (int r = 0; r < RT; r++) akk[r] = aqk[r] = 0.0f;
+            for (int i = 0; i < D; i += 4) {
+                const float4 k4 = ld4(sK + s * P + i), g4 = ld4(sG + s * P + i);
+#pragma unroll
+                for (int r = 0; r < RT; r++) {
+                    const int t = warp + NW * r;
+                    const float4 kt = ld4(sK + t * P + i), qt = ld4(sQ + t * P + i), gt = ld4(sG + t * P + i);
+                    float kr = k4.x * exp2f(gt.x - g4.x);
+                    akk[r] = fmaf(kr, kt.x, akk[r]);
+                    aqk[r] = fmaf(kr, qt.x, aqk[r]);
+                    kr = k4.y * exp2f(gt.y - g4.y);
+                    akk[r] = fmaf(kr, kt.y, akk[r]);
+                    aqk[r] = fmaf(kr, qt.y, aqk[r]);
+                    kr = k4.z * exp2f(gt.z - g4.z);
+                    akk[r] = fmaf(kr, kt.z, akk[r]);
+                    aqk[r] = fmaf(kr, qt.z, aqk[r]);
+                    kr = k4.w * exp2f(gt.w - g4.w);
+                    akk[r] = fmaf(kr, kt.w, akk[r]);
+                    aqk[r] = fmaf(kr, qt.w, aqk[r]);
                 }
             }
-            sA[t * (KC + 1) + s] = s < t ? akk * sB[t] : 0.0f;
-            sAQ[t * (KC + 1) + s] = s <= t ? aqk : 0.0f;
+            // s > t lanes computed ratios above 1 (possibly infinite); they are dropped here
+#pragma unroll
+            for (int r = 0; r < RT; r++) {
+                const int t = warp + NW * r;
+                sA[t * PA + s] = s < t ? akk[r] * sB[t] : 0.0f;
+                sAQ[t * PA + s] = s <= t ? aqk[r] : 0.0f;
+            }
         }
         __syncthreads();
-        // 4a. the decayed keys and queries (2^g . k, 2^g . q)
-        for (int e = tid; e < KC * D; e += KTHREADS) {
-            const int t = e / D, i = e % D;
-            const float d = exp2f(sG[t * P + i]);
-            sKG[t * P + i] = sK[t * P + i] * d;
-            sQ[t * P + i] *= d;
+        // 4a. the decayed keys and queries (2^g . k, 2^g . q), four channels at a time
+        for (int e = tid; e < KC * D / 4; e += KTHREADS) {
+            const int t = (e * 4) / D, i = (e * 4) % D;
+            const float4 g = ld4(sG + t * P + i), kk = ld4(sK + t * P + i), qq = ld4(sQ + t * P + i);
+            const float4 d = make_float4(exp2f(g.x), exp2f(g.y), exp2f(g.z), exp2f(g.w));
+            *reinterpret_cast<float4 *>(sKG + t * P + i) = make_float4(kk.x * d.x, kk.y * d.y, kk.z * d.z, kk.w * d.w);
+            *reinterpret_cast<float4 *>(sQ + t * P + i) = make_float4(qq.x * d.x, qq.y * d.y, qq.z * d.z, qq.w * d.w);
         }
         __syncthreads();
-        // 4b. right-hand side: beta_t (v_t - S0^T (2^g_t . k_t)), column j = lane
-        for (int t = warp; t < KC; t += NW) {
-            const float *kg = sKG + t * P;
-            float acc = 0.0f;
-            for (int i = 0; i < D; i++) acc = fmaf(kg[i], sS[i * KSL + lane], acc);
-            sW[t * KSL + lane] = sB[t] * (sV[t * KSL + lane] - acc);
+        // 4b. right-hand side: beta_t (v_t - S0^T (2^g_t . k_t)), column j = lane, RT rows
+        {
+            float acc[RT];
+#pragma unroll
+            for (int r = 0; r < RT; r++) acc[r] = 0.0f;
+            for (int i = 0; i < D; i += 4) {
+                const float s0 = sS[(i + 0) * KSL + lane], s1 = sS[(i + 1) * KSL + lane],
+                            s2 = sS[(i + 2) * KSL + lane], s3 = sS[(i + 3) * KSL + lane];
+#pragma unroll
+                for (int r = 0; r < RT; r++) {
+                    const float4 kg = ld4(sKG + (warp + NW * r) * P + i);
+                    acc[r] = fmaf(kg.x, s0, acc[r]);
+                    acc[r] = fmaf(kg.y, s1, acc[r]);
+                    acc[r] = fmaf(kg.z, s2, acc[r]);
+                    acc[r] = fmaf(kg.w, s3, acc[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RT; r++) {
+                const int t = warp + NW * r;
+                sW[t * KSL + lane] = sB[t] * (sV[t * KSL + lane] - acc[r]);
+            }
         }
         __syncthreads();
         // 5. forward substitution (I + A) W = rhs, one column per lane of warp 0
@@ -159,32 +202,75 @@ __global__ void __launch_bounds__(KTHREADS) kda_chunk_kernel(float *__restrict__
             for (int t = 0; t < KC; t++) {
                 float x = sW[t * KSL + lane];
 #pragma unroll
-                for (int s = 0; s < t; s++) x = fmaf(-sA[t * (KC + 1) + s], w[s], x);
+                for (int s = 0; s < t; s++) x = fmaf(-sA[t * PA + s], w[s], x);
                 w[t] = x;
                 sW[t * KSL + lane] = x;
             }
         }
         __syncthreads();
-        // 6. outputs; meanwhile the keys decayed to the chunk's end, 2^(g_n - g_s) . k_s
+        // 6. outputs (RT rows per warp; Aq is zero above its diagonal and W past n), and
+        //    the keys decayed to the chunk's end, 2^(g_n - g_s) . k_s
         if (o) {
-            for (int t = warp; t < n; t += NW) {
-                const float *qg = sQ + t * P;
-                float acc = 0.0f;
-                for (int i = 0; i < D; i++) acc = fmaf(qg[i], sS[i * KSL + lane], acc);
-                for (int s = 0; s <= t; s++) acc = fmaf(sAQ[t * (KC + 1) + s], sW[s * KSL + lane], acc);
-                o[(((size_t)b * T + c0 + t) * H + h) * D + j0 + lane] = acc;
+            float acc[RT];
+#pragma unroll
+            for (int r = 0; r < RT; r++) acc[r] = 0.0f;
+            for (int i = 0; i < D; i += 4) {
+                const float s0 = sS[(i + 0) * KSL + lane], s1 = sS[(i + 1) * KSL + lane],
+                            s2 = sS[(i + 2) * KSL + lane], s3 = sS[(i + 3) * KSL + lane];
+#pragma unroll
+                for (int r = 0; r < RT; r++) {
+                    const float4 qg = ld4(sQ + (warp + NW * r) * P + i);
+                    acc[r] = fmaf(qg.x, s0, acc[r]);
+                    acc[r] = fmaf(qg.y, s1, acc[r]);
+                    acc[r] = fmaf(qg.z, s2, acc[r]);
+                    acc[r] = fmaf(qg.w, s3, acc[r]);
+                }
+            }
+            for (int s = 0; s < KC; s += 4) {
+                const float w0 = sW[(s + 0) * KSL + lane], w1 = sW[(s + 1) * KSL + lane],
+                            w2 = sW[(s + 2) * KSL + lane], w3 = sW[(s + 3) * KSL + lane];
+#pragma unroll
+                for (int r = 0; r < RT; r++) {
+                    const float4 aq = ld4(sAQ + (warp + NW * r) * PA + s);
+                    acc[r] = fmaf(aq.x, w0, acc[r]);
+                    acc[r] = fmaf(aq.y, w1, acc[r]);
+                    acc[r] = fmaf(aq.z, w2, acc[r]);
+                    acc[r] = fmaf(aq.w, w3, acc[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RT; r++) {
+                const int t = warp + NW * r;
+                if (t < n) o[(((size_t)b * T + c0 + t) * H + h) * D + j0 + lane] = acc[r];
             }
         }
-        for (int e = tid; e < KC * D; e += KTHREADS) {
-            const int t = e / D, i = e % D;
-            sKG[t * P + i] = sK[t * P + i] * exp2f(sG[(KC - 1) * P + i] - sG[t * P + i]);
+        for (int e = tid; e < KC * D / 4; e += KTHREADS) {
+            const int t = (e * 4) / D, i = (e * 4) % D;
+            const float4 g = ld4(sG + t * P + i), gn = ld4(sG + (KC - 1) * P + i), kk = ld4(sK + t * P + i);
+            *reinterpret_cast<float4 *>(sKG + t * P + i) =
+                make_float4(kk.x * exp2f(gn.x - g.x), kk.y * exp2f(gn.y - g.y), kk.z * exp2f(gn.z - g.z),
+                            kk.w * exp2f(gn.w - g.w));
         }
         __syncthreads();
-        // 7. the state at the chunk's end, row i = warp + NW r, column = lane
-        for (int i = warp; i < D; i += NW) {
-            float acc = sS[i * KSL + lane] * exp2f(sG[(KC - 1) * P + i]);
-            for (int s = 0; s < n; s++) acc = fmaf(sKG[s * P + i], sW[s * KSL + lane], acc);
-            sS[i * KSL + lane] = acc;
+        // 7. the state at the chunk's end: warp rows i0 .. i0 + RI - 1, column = lane
+        {
+            const int i0 = warp * RI;
+            float acc[RI];
+#pragma unroll
+            for (int q = 0; q < RI; q++) acc[q] = sS[(i0 + q) * KSL + lane] * exp2f(sG[(KC - 1) * P + i0 + q]);
+            for (int s = 0; s < n; s++) {
+                const float w = sW[s * KSL + lane];
+#pragma unroll
+                for (int q = 0; q < RI; q += 4) {
+                    const float4 ke = ld4(sKG + s * P + i0 + q);
+                    acc[q + 0] = fmaf(ke.x, w, acc[q + 0]);
+                    acc[q + 1] = fmaf(ke.y, w, acc[q + 1]);
+                    acc[q + 2] = fmaf(ke.z, w, acc[q + 2]);
+                    acc[q + 3] = fmaf(ke.w, w, acc[q + 3]);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < RI; q++) sS[(i0 + q) * KSL + lane] = acc[q];
         }
     }
     __syncthreads();
