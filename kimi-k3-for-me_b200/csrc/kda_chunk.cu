@@ -18,6 +18,8 @@
 #include <float.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace k3 {
@@ -286,12 +288,22 @@ static int kda_chunk_launch(float *state, float *o, const float *q, const float 
                             cudaStream_t s)
 {
     const size_t bytes = KdaChunkSmem<D>::BYTES;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(kda_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
-            cudaSuccess)
-            return launch_status();
-        attr = true;
+    // the opt-in to >48 KB of dynamic shared memory, once per device and width (a
+    // function's attributes belong to each device's context)
+    static std::mutex mu;
+    static bool ready[64] = {};
+    int dev = 0;
+    int st = cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!ready[dev]) {
+            st = cuda_status(cudaFuncSetAttribute(kda_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)bytes));
+            if (st) return st;
+            ready[dev] = true;
+        }
     }
     dim3 grid(H, B, D / KSL);
     kda_chunk_kernel<D><<<grid, KTHREADS, bytes, s>>>(state, o, q, k, v, alpha, beta, T, H, qscale);

@@ -847,13 +847,22 @@ extern "C" int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *
         ns = ns_tc;
         sl = split_len;
     } else {
-        static bool attr_set = false;   // one-time opt-in to >48 KB of dynamic shared memory
-        if (!attr_set) {
-            st = k3::cuda_status(cudaFuncSetAttribute(k3::mla_attend_kernel,
-                                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      (int)k3::MLA_SMEM));
-            if (st) return st;
-            attr_set = true;
+        // the opt-in to >48 KB of dynamic shared memory, once per device (a function's
+        // attributes belong to each device's context)
+        static std::mutex attr_mu;
+        static bool attr_set[64] = {};
+        int adev = 0;
+        if ((st = k3::cuda_status(cudaGetDevice(&adev)))) return st;
+        if (adev < 0 || adev >= 64) return K3GPU_EINVAL;
+        {
+            std::lock_guard<std::mutex> lock(attr_mu);
+            if (!attr_set[adev]) {
+                st = k3::cuda_status(cudaFuncSetAttribute(k3::mla_attend_kernel,
+                                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                          (int)k3::MLA_SMEM));
+                if (st) return st;
+                attr_set[adev] = true;
+            }
         }
         k3::mla_attend_kernel<<<dim3(ns, B * T, k3::ceil_div(H, k3::MLA_HT)), k3::MLA_THREADS,
                                 k3::MLA_SMEM, s>>>(
