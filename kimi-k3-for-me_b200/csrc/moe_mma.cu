@@ -499,7 +499,8 @@ static int maps_for(const K3GpuExpertBank &b, CUtensorMap (&out)[4])
     return K3GPU_OK;
 }
 
-static int g_mma_sms = 0;
+static std::mutex g_mma_mu;
+static int g_mma_sms[64] = {};   // per device: its SM count once set up, 0 before
 
 void act_pack_rows_launch(const MoePlan &p, int I, int P, int E, cudaStream_t s)
 {
@@ -515,14 +516,24 @@ int mma_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, i
     CUtensorMap m[4];
     int st = maps_for(bank, m);
     if (st) return st;
-    if (g_mma_sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_mma_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_mma_sms <= 0) g_mma_sms = 148;
-        st = cuda_status(cudaFuncSetAttribute(moe_mma_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM));
-        if (!st) st = cuda_status(cudaFuncSetAttribute(moe_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM));
-        if (st) { g_mma_sms = 0; return st; }
+    // once per device: the shared-memory opt-in (a function's attributes belong to each
+    // device's context) and the SM count the persistent grid is sized by
+    int dev = 0;
+    if ((st = cuda_status(cudaGetDevice(&dev)))) return st;
+    if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
+    int sms = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_mma_mu);
+        if (g_mma_sms[dev] == 0) {
+            int n = 0;
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+            if (n <= 0) n = 148;
+            st = cuda_status(cudaFuncSetAttribute(moe_mma_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM));
+            if (!st) st = cuda_status(cudaFuncSetAttribute(moe_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM));
+            if (st) return st;
+            g_mma_sms[dev] = n;
+        }
+        sms = g_mma_sms[dev];
     }
     const long long pl = L / 2, pi = I / 2, ql = L / 32, qi = I / 32;
     MmaArgs a;
@@ -531,12 +542,12 @@ int mma_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, i
         a.K = L; a.UE = I / 64;
         a.wys = bank.stride / pl; a.wy1 = bank.p1 / pl; a.wy3 = bank.p3 / pl;
         a.sys = bank.stride / ql; a.sy1 = bank.s1 / ql; a.sy3 = bank.s3 / ql;
-        moe_mma_kernel<0><<<g_mma_sms, MM_THREADS, MM_SMEM, s>>>(m[0], m[1], p, bank, a, act, b1, b2);
+        moe_mma_kernel<0><<<sms, MM_THREADS, MM_SMEM, s>>>(m[0], m[1], p, bank, a, act, b1, b2);
     } else {
         a.K = I; a.UE = L / 128;
         a.wys = bank.stride / pi; a.wy1 = bank.p2 / pi; a.wy3 = 0;
         a.sys = bank.stride / qi; a.sy1 = bank.s2 / qi; a.sy3 = 0;
-        moe_mma_kernel<1><<<g_mma_sms, MM_THREADS, MM_SMEM, s>>>(m[2], m[3], p, bank, a, act, b1, b2);
+        moe_mma_kernel<1><<<sms, MM_THREADS, MM_SMEM, s>>>(m[2], m[3], p, bank, a, act, b1, b2);
     }
     return launch_status();
 }

@@ -637,7 +637,8 @@ bool tc_bank_ok(const K3GpuExpertBank &b)
     return b.f16_safe != nullptr && mma_bank_ok(b);
 }
 
-static int g_tc_ready_dev = -1;
+static std::mutex g_tc_mu;
+static bool g_tc_ready[64] = {};   // per device: the shared-memory opt-in is done
 
 int tc_pack_pairs_launch(const MoePlan &p, const float *z, int L, int P, int E, cudaStream_t s)
 {
@@ -669,13 +670,19 @@ int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, in
         if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hl, I, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (st) return st;
+    // the shared-memory opt-in, once per device (a function's attributes belong to each
+    // device's context)
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (g_tc_ready_dev != dev) {
-        st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-        if (!st) st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-        if (st) return st;
-        g_tc_ready_dev = dev;
+    if ((st = cuda_status(cudaGetDevice(&dev)))) return st;
+    if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
+    {
+        std::lock_guard<std::mutex> lock(g_tc_mu);
+        if (!g_tc_ready[dev]) {
+            st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+            if (!st) st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+            if (st) return st;
+            g_tc_ready[dev] = true;
+        }
     }
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
