@@ -24,6 +24,8 @@
 #include <cuda_fp4.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "moe.cuh"
 
 namespace k3 {
@@ -410,17 +412,21 @@ __global__ void mxfp4_dequant_kernel(float *__restrict__ out, const uint8_t *__r
         }
 }
 
-static int g_num_sms = 0;
+// the current device's SM count, looked up once per device
+static std::mutex g_sms_mu;
+static int g_num_sms[64] = {};
 
 static int num_sms()
 {
-    if (g_num_sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lock(g_sms_mu);
+    if (g_num_sms[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        g_num_sms[dev] = n > 0 ? n : 148;
     }
-    return g_num_sms;
+    return g_num_sms[dev];
 }
 
 int moe_check(const K3GpuExpertBank *bank, int T, int topk, int n_routed, int n_shared, int act)
