@@ -676,8 +676,9 @@ int k3_spec_loop_ids(const K3SpecLoop *L, int *ids, int cap);
  * context in the history, most frequent first (at most `branch`), the context backing off
  * to shorter suffixes of at least min_len ids when it has no continuation; nodes are
  * added best-first by the product of relative frequencies along their path, up to
- * max_nodes and max_depth. tok/parent [max_nodes] in the order of
- * k3gpu_accept_tree_greedy (parents first, parent[0] = -1); returns the node count. */
+ * max_nodes (<= 65536) and max_depth. tok/parent [max_nodes] in the order of
+ * k3gpu_accept_tree_greedy (parents first, parent[0] = -1); returns the node count, 0 for
+ * bad arguments. */
 int k3_suffix_drafter_tree(const K3SuffixDrafter *d, int max_nodes, int branch, int max_depth,
                            int min_len, int *tok, int *parent);
 

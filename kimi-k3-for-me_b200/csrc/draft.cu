@@ -401,7 +401,7 @@ extern "C" int k3_suffix_drafter_draft_p3(const K3SuffixDrafter *d, const double
 extern "C" int k3_suffix_drafter_tree(const K3SuffixDrafter *d, int max_nodes, int branch, int max_depth,
                                       int min_len, int *tok, int *parent)
 {
-    if (!d || d->n == 0 || max_nodes < 1 || !tok || !parent) return 0;
+    if (!d || d->n == 0 || max_nodes < 1 || max_nodes > 65536 || !tok || !parent) return 0;
     if (branch < 1) branch = 1;
     if (branch > 16) branch = 16;
     tok[0] = d->seq[d->n - 1];

@@ -78,7 +78,7 @@ extern "C" int k3_state_save(const char *path, const K3StateLayout *s, const int
     if (!path || !s || nseq < 0 || cached < 0 || cached > kv_cap || nseq < cached || nseq > cached + 1)
         return K3GPU_EINVAL;
     if (s->kper < 0 || s->kvpp < 0 || s->ropepp < 0 || s->n_bound < 0 || s->n_mla < 0 || s->loop_count < 0 ||
-        s->loop_count > 8)
+        s->loop_count > 8 || (s->loop_count && s->loop_nv < 0))
         return K3GPU_EINVAL;
     if ((nseq && !seq) || (s->kper && !ks) || (s->n_mla && cached && ((s->kvpp && !kvc) || (s->ropepp && !ropec))))
         return K3GPU_EINVAL;
@@ -155,6 +155,13 @@ extern "C" int k3_state_load(const char *path, const K3StateLayout *expect, int 
     if (!loop_ok || memcmp(h.fp, expect->fp, sizeof h.fp) != 0 || h.n_bound != expect->n_bound ||
         h.n_mla != expect->n_mla || h.kvpp != expect->kvpp || h.ropepp != expect->ropepp || h.kper != expect->kper ||
         h.cached < 0 || h.nseq < h.cached || h.nseq > h.cached + 1) {
+        fclose(f);
+        return K3GPU_EINVAL;
+    }
+    // sizes the rest of the file is read with: never trusted past these bounds, whatever
+    // the caller expects (the loop arrays hold at most 9 counters)
+    if (l.count < 0 || l.count > 8 || (l.count && l.nv < 0) || h.n_bound < 0 || h.n_mla < 0 || h.kper < 0 ||
+        h.kvpp < 0 || h.ropepp < 0) {
         fclose(f);
         return K3GPU_EINVAL;
     }

@@ -149,6 +149,8 @@ def test_suffix_tree_shape_and_verify_masks(k3):
     fresh = k3.SuffixDrafter(8)
     fresh.push([5, 6, 7])                               # nothing repeats: the root alone
     assert fresh.tree() == ([7], [-1])
+    tok = (k3.C.c_int * 1)()
+    assert k3.lib.k3_suffix_drafter_tree(fresh._d, 1 << 20, 4, 8, 1, tok, tok) == 0   # above 65536 nodes
     fresh.close()
 
 

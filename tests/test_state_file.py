@@ -171,3 +171,35 @@ def test_refusals(k3, tmp_path):
     assert load_state(k3, variant("trunc", raw[:-5]), s, 64, s.n_bound, kv_cap)[0] == E
     # the writer refuses a sequence that is not the cached positions plus at most one id
     assert save(k3, str(tmp_path / "w.k3st"), s, seq + [1, 2], cached, ks, kvc, ropec, kv_cap) == E
+
+
+def test_untrusted_loop_record_and_sizes(k3, tmp_path):
+    """Sizes the loader reads with are bounded whatever the caller expects: a loop count
+    outside 0..8 (the counter array holds 9) or a negative slot count is refused, also when
+    the caller passes no counter array; the writer refuses a negative slot count."""
+    rng = np.random.default_rng(6)
+    s = layout(k3, loop=(2, 1, 3, 3, 1e-3))
+    kv_cap, cached = 24, 10
+    seq, ks, kvc, ropec = case(rng, s, kv_cap, cached)
+    p = str(tmp_path / "l.k3st")
+    assert save(k3, p, s, seq, cached, ks, kvc, ropec, kv_cap, [1, 2, 3], [0] * len(seq)) == 0
+    raw = bytearray(open(p, "rb").read())
+    C = k3.C
+    for count, nv in ((20, 3), (-3, 3), (2, -5)):
+        bad = bytearray(raw)
+        bad[104:112] = struct.pack("<2i", count, nv)       # the loop record's count and nv
+        q = str(tmp_path / f"bad{count}_{nv}.k3st")
+        open(q, "wb").write(bytes(bad))
+        e = layout(k3, loop=(count, 1, 3, nv, 1e-3))
+        seq_b = np.zeros(64, np.int32)
+        ks_b = np.zeros(4 * e.kper, np.float32)
+        kvc_b = np.zeros((e.n_mla, kv_cap, e.kvpp), np.float32)
+        ropec_b = np.zeros((e.n_mla, kv_cap, e.ropepp), np.float32)
+        ci, ni = C.c_int(0), C.c_int(0)
+        st = k3.lib.k3_state_load(os.fsencode(q), C.byref(e), seq_b.ctypes.data, 64, ks_b.ctypes.data,
+                                  kvc_b.ctypes.data, ropec_b.ctypes.data, kv_cap, None, None, C.byref(ci),
+                                  C.byref(ni))
+        assert st == k3.K3GPU_EINVAL, (count, nv)
+    neg = layout(k3, loop=(2, 1, 3, -1, 1e-3))
+    assert save(k3, str(tmp_path / "n.k3st"), neg, seq, cached, ks, kvc, ropec, kv_cap, [1, 2, 3],
+                [0] * len(seq)) == k3.K3GPU_EINVAL
