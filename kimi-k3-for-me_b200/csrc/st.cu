@@ -226,8 +226,10 @@ int read_header(int fd, int file, std::unordered_map<std::string, Entry> *index,
         t.file = file;
         t.off = t.bytes = 0;
         if (s.entry(&t)) {
+            // data past the file (each term bounded first, so the sum cannot overflow)
+            if (t.off > *file_bytes || t.bytes > *file_bytes) return K3GPU_EINVAL;
             t.off += 8 + (int64_t)n;
-            if (t.off + t.bytes > *file_bytes) return K3GPU_EINVAL;   // data past the file
+            if (t.off + t.bytes > *file_bytes) return K3GPU_EINVAL;
             (*index)[name] = t;
         }
     } while (s.ok && s.eat(','));
@@ -239,7 +241,8 @@ int read_header(int fd, int file, std::unordered_map<std::string, Entry> *index,
 extern "C" int k3_bank_read_safetensors(const char *const *files, int n_files, int layer, int e0, int n, int L, int I,
                                         uint8_t *host_bank, size_t host_bytes)
 {
-    if (!files || n_files <= 0 || layer < 0 || e0 < 0 || n <= 0 || !host_bank) return K3GPU_EINVAL;
+    if (!files || n_files <= 0 || layer < 0 || e0 < 0 || n <= 0 || e0 > (1 << 20) || n > (1 << 20) || !host_bank)
+        return K3GPU_EINVAL;
     if (L <= 0 || I <= 0 || L % 32 || I % 32) return K3GPU_EINVAL;
     K3GpuExpertBank lay;
     memset(&lay, 0, sizeof lay);

@@ -143,3 +143,13 @@ def test_errors(k3, tmp_path):
     assert lib.k3_bank_read_safetensors(one, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
     missing = (C.c_char_p * 1)(os.fsencode(str(tmp_path / "absent.safetensors")))
     assert lib.k3_bank_read_safetensors(missing, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    # offsets near the top of the 64-bit range (a sum that would wrap), an expert range
+    # whose end would wrap an int
+    p = str(tmp_path / "huge.safetensors")
+    with open(p, "wb") as f:
+        h = b'{"a": {"dtype": "U8", "shape": [1], "data_offsets": [9223372036854775000, 9223372036854775807]}}'
+        f.write(struct.pack("<Q", len(h)) + h + b"\0")
+    one = (C.c_char_p * 1)(os.fsencode(p))
+    assert lib.k3_bank_read_safetensors(one, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
+    assert lib.k3_bank_read_safetensors(arr, 2, LAYER, 2 ** 31 - 2, 4, L, I, buf.ctypes.data, buf.nbytes) == \
+        k3.K3GPU_EINVAL
