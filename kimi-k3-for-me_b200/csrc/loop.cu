@@ -68,12 +68,13 @@ int draft(K3SpecLoop *L, int *d)
     }
 }
 
-// greedy acceptance over a draft tree (k3gpu_accept_tree_greedy): path[0] = 0, the root
-int tree_accept(const int *tok, const int *parent, int n, const int *arg, int *path)
+// greedy acceptance over a draft tree (k3gpu_accept_tree_greedy): path[0] = 0, the root;
+// at most cap nodes (the depth limit the tree was drafted with, plus the root)
+int tree_accept(const int *tok, const int *parent, int n, const int *arg, int *path, int cap)
 {
     int len = 1, node = 0;
     path[0] = 0;
-    for (;;) {
+    while (len < cap) {
         int next = -1;
         for (int c = node + 1; c < n; c++)
             if (parent[c] == node && tok[c] == arg[node]) {
@@ -84,6 +85,7 @@ int tree_accept(const int *tok, const int *parent, int n, const int *arg, int *p
         path[len++] = next;
         node = next;
     }
+    return len;
 }
 
 // append the kept ids to the history, the output and the drafter
@@ -186,7 +188,7 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
         if (n < 1) return K3GPU_EINVAL;
         if (L->verify(L->ctx, L->tok, L->parent, n, base, L->arg) != 0) return K3GPU_ECALLBACK;
         int path[9];
-        const int plen = tree_accept(L->tok, L->parent, n, L->arg, path);
+        const int plen = tree_accept(L->tok, L->parent, n, L->arg, path, c.spec_n + 1);
         const int m = plen - 1, nd = n - 1;
         for (int i = 1; i < plen; i++) emit[emitn++] = L->tok[path[i]];
         emit[emitn++] = L->arg[path[plen - 1]];
