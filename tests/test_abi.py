@@ -58,6 +58,16 @@ def test_argument_checks_need_no_device():
     assert lib.k3gpu_kda_verify(p, p, p, p, p, p, p, 1, 4, 2, 100, 1.0, None) == m.K3GPU_EINVAL
     assert lib.k3gpu_accept_sample(p, p, p, p, None, 1, 4, 10, 0.0, 1, 0, None) == m.K3GPU_EINVAL
     assert lib.k3gpu_mla_absorbed(*([p] * 8), 1, 65, 4, 16, 8, 16, 512, 128, 128, 1.0, p, 0, None) == m.K3GPU_EINVAL
+    # the later entry points refuse before any CUDA call too
+    assert lib.k3gpu_kda_prefill(None, None, p, p, p, p, p, 1, 8, 2, 128, 1.0, None) == m.K3GPU_EINVAL
+    assert lib.k3gpu_kda_prefill(p, None, p, p, p, p, p, 1, 8, 2, 48, 1.0, None) == m.K3GPU_EINVAL   # D
+    assert lib.k3gpu_kda_prefill(p, None, p, p, p, p, p, 1, 0, 2, 128, 1.0, None) == m.K3GPU_EINVAL  # T
+    assert lib.k3gpu_accept_tree_greedy(None, p, p, p, p, p, p, 1, 4, 16, None) == m.K3GPU_EINVAL
+    assert lib.k3gpu_matmul_bf16_batch(None, 8, p, 8, p, 8, 8, 1, None, 0, None) == m.K3GPU_EINVAL
+    assert lib.k3gpu_ep_dispatch(None, p, p, p, 1, 1, p, None) == m.K3GPU_EINVAL
+    assert lib.k3gpu_ep_arena_bytes(0, 16, 64, 8) == 0
+    big_t = 524288 // 384 + 1                           # K3GPU_ROUTER_NOALLOC_MAX_SCORES
+    assert lib.k3gpu_router_noalloc(p, p, p, p, p, big_t, 7168, 384, 8, 1, 1.0, None) == m.K3GPU_ECAPACITY
     assert lib.k3gpu_router_workspace(16, 384) >= 16 * 384 * 4
     assert lib.k3gpu_moe_workspace(72, 8, 1, 7168, 2048, 384) > 72 * 9 * 7168 * 4
     assert m.lib.k3gpu_strerror(m.K3GPU_ECAPACITY).decode().startswith("capacity")
