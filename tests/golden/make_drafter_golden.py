@@ -9,13 +9,17 @@ T-1 and before its commit, exactly as analyze_sequence steps, tools/spec_replay.
   g2[T]      its period pos - last_end (0: none)
   p2[T]      periodic_copy(seq, last_end + 1, g, 8)  (P2, :333-336, 442-449), -1 padded
   f3[T]      draft_features of that P2 draft (P3's feature codes, :371-397), 255 without one
-and the P3 lengths of every draft point under three acceptance tables -- the tool's own
-fit_acceptance_table (:474-503) on these sequences' P2 acceptances, and two seeded random
-tables -- by adaptive_lengths (:525-536; delta 0.1, 0.22, 0.55; cumulative and per
-position) and cost_aware_lengths (:539-568; both tiers, with and without replay):
-  q          [3][234] the tables
-  s<i>/p3a   [3][3][2][n+1] adaptive lengths (table, delta, cumulative 1/0)
-  s<i>/p3c   [3][2][2][n+1] cost-aware lengths (table, tier 8GB/128GB, replay 0/1)
+and the P3 lengths of every draft point under four acceptance tables -- the tool's own
+fit_acceptance_table (:474-503) on these sequences' P2 acceptances, two seeded random
+tables, and the table the study recorded (docs/measurements/spec-replay.json, p3_table) --
+by adaptive_lengths (:525-536; delta 0.1, 0.22, 0.55; cumulative and per position) and
+cost_aware_lengths (:539-568; both tiers, with and without replay):
+  q          [4][234] the tables
+  s<i>/p3a   [4][3][2][n+1] adaptive lengths (table, delta, cumulative 1/0)
+  s<i>/p3c   [4][2][2][n+1] cost-aware lengths (table, tier 8GB/128GB, replay 0/1)
+It also writes tests/golden/study_table.json: the study file's p3_table, cost_model and
+p2_defaults_from_calibration sections, as a user would hand them to
+spec_table.load_study.
 
 Usage: python tests/golden/make_drafter_golden.py [--ref /root/reference]
 """
@@ -23,6 +27,7 @@ from __future__ import annotations
 
 import argparse
 import importlib.util
+import json
 import os
 
 import numpy as np
@@ -103,7 +108,13 @@ def main() -> None:
     A = np.concatenate([f[1] for f in feats])
     R = np.concatenate([f[2] for f in feats])
     q_fit, _ = sr.fit_acceptance_table(F, A, R)
-    qs = np.stack([q_fit, rng.uniform(0.05, 1.0, sr.N_CODES), rng.uniform(0.3, 1.0, sr.N_CODES)])
+    with open(os.path.join(a.ref, "docs", "measurements", "spec-replay.json")) as f:
+        study = json.load(f)
+    q_rec = np.asarray(study["p3_table"]["q"], float)
+    qs = np.stack([q_fit, rng.uniform(0.05, 1.0, sr.N_CODES), rng.uniform(0.3, 1.0, sr.N_CODES), q_rec])
+    sub = {k: study[k] for k in ("p3_table", "cost_model", "p2_defaults_from_calibration")}
+    with open(os.path.join(HERE, "study_table.json"), "w") as f:
+        json.dump(sub, f, indent=1)
     arrays["q"] = qs
     deltas = (0.1, 0.22, 0.55)
     for si in range(len(feats)):

@@ -233,3 +233,47 @@ def test_p3_table_fit_matches_reference_tool(k3):
     q = st.fit_p3_table(np.array(F), A, R)
     assert q.shape == (k3.SPEC_P3_CODES,)
     assert np.array_equal(q, G["q"][0])                  # same operations, same order: exact
+
+
+def _spec_table():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "spec_table", os.path.join(os.path.dirname(HERE), "kimi-k3-for-me_b200", "spec_table.py"))
+    st = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(st)
+    return st
+
+
+def test_study_table_loads_and_drives_p3_as_the_tool(k3, tmp_path):
+    """The table, cost tiers and P2 settings the study recorded (tests/golden/study_table.json,
+    the study file's own sections) load as the library's inputs, and P3 with them gives the
+    tool's lengths at every draft point (table 3 of the golden vectors is that table)."""
+    import json
+    st = _spec_table()
+    path = os.path.join(HERE, "golden", "study_table.json")
+    d = st.load_study(path)
+    assert np.array_equal(d["q"], G["q"][3])
+    assert d["p2_defaults"] == {"8GB": {"min_len": 5, "N": 8}, "128GB": {"min_len": 6, "N": 4}}
+    for ti, (tier, coef) in enumerate(TIERS):
+        c = d["costs"][tier]
+        assert (c["a_T"], c["a_E"], c["a_C"], c["eps"], c["expert_ratio"]) == coef + (0.0, 56.0)
+    costs = [k3.K3SpecCost(**d["costs"][tier]) for tier, _ in TIERS]
+    for si in range(N_SEQ):
+        seq = G[f"s{si}/seq"].tolist()
+        f3, p3a, p3c = G[f"s{si}/f3"], G[f"s{si}/p3a"], G[f"s{si}/p3c"]
+        for T in range(1, len(seq) + 1):
+            codes = f3[T].tolist()
+            assert k3.spec_p3_length(codes, d["q"], 0.22, True) == p3a[3, 1, 1, T]
+            for ti in range(2):
+                assert k3.spec_p3_cost_length(codes, d["q"], costs[ti], 1) == p3c[3, ti, 1, T]
+    # refusals: other buckets, another formula, a short table
+    raw = json.load(open(path))
+    for key, val in (("length_bucket_lower_edges", [1, 2, 3, 4, 5, 6, 8, 9, 12, 16, 24, 32, 64]),
+                     ("code_index", "(length_bucket*3 + depth_bucket)*6 + agreement_bucket"),
+                     ("q", raw["p3_table"]["q"][:200])):
+        bad = json.loads(json.dumps(raw))
+        bad["p3_table"][key] = val
+        q = tmp_path / f"bad_{key}.json"
+        q.write_text(json.dumps(bad))
+        with pytest.raises(ValueError):
+            st.load_study(str(q))
