@@ -4,6 +4,8 @@
 For seeded id sequences with planted repeats (copies of earlier spans, periodic runs), at
 every draft point T (the history seq[0..T), after the tool's SuffixAutomaton.extend of id
 T-1 and before its commit, exactly as analyze_sequence steps, tools/spec_replay.py:408-469):
+  p0[T]      spec_draft(seq, T, 8)  (P0, the engine's drafter, :122-171, the tool's port of
+             src/cli/k3_run.c:450-491), -1 padded, with its length p0n[T]
   p1[T]      eager_draft(seq, T, 8)  (P1, :174-184), -1 padded, with its length
   L2[T]      the suffix automaton's match length (0: none)
   g2[T]      its period pos - last_end (0: none)
@@ -69,6 +71,8 @@ def main() -> None:
     for si, seq in enumerate(sequences(rng)):
         s = [int(v) for v in seq]
         n = len(s)
+        p0 = np.full((n + 1, CAP), -1, np.int32)
+        p0n = np.zeros(n + 1, np.int32)
         p1 = np.full((n + 1, CAP), -1, np.int32)
         p1n = np.zeros(n + 1, np.int32)
         p2 = np.full((n + 1, CAP), -1, np.int32)
@@ -80,6 +84,9 @@ def main() -> None:
         for pos in range(n):
             v = sam.extend(s[pos], pos)
             T = pos + 1
+            d = sr.spec_draft(s, T, CAP)
+            p0[T, :len(d)] = d
+            p0n[T] = len(d)
             d = sr.eager_draft(s, T, CAP)
             p1[T, :len(d)] = d
             p1n[T] = len(d)
@@ -96,6 +103,8 @@ def main() -> None:
                 assert (bl, be) == (sam.length[v], e), (si, T)
             sam.commit(pos)
         arrays[f"s{si}/seq"] = seq
+        arrays[f"s{si}/p0"] = p0
+        arrays[f"s{si}/p0n"] = p0n
         arrays[f"s{si}/p1"] = p1
         arrays[f"s{si}/p1n"] = p1n
         arrays[f"s{si}/p2"] = p2

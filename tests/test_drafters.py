@@ -1,7 +1,8 @@
 """Host drafters from the reference's drafting study (tools/spec_replay.py), CPU only.
 
-P1 (k3_spec_draft_eager) and P2 (the incremental suffix-automaton drafter
-k3_suffix_drafter_*) against golden drafts the reference tool itself produced at every
+P0 (the engine's n-gram drafter, k3_spec_draft_ngram), P1 (k3_spec_draft_eager) and P2
+(the incremental suffix-automaton drafter k3_suffix_drafter_*) against golden drafts the
+reference tool itself produced at every
 draft point of four seeded sequences with planted repeats and periodic runs
 (tests/golden/ref_drafters.npz, made by tests/golden/make_drafter_golden.py), and against
 the oracle's brute-force restatement on random sequences. Drafts are ids: bit-exact.
@@ -25,6 +26,19 @@ N_SEQ = int(G["n_seq"])
 @pytest.fixture(scope="module")
 def k3():
     return load()
+
+
+@pytest.mark.parametrize("si", range(N_SEQ))
+def test_engine_ngram_draft_matches_reference_tool(k3, si):
+    """The engine's drafter (k3_spec_draft_ngram with the engine's n = 4 then 3) against
+    the tool's line-for-line port of src/cli/k3_run.c's spec_draft at every draft point;
+    a smaller cap gives the same draft's prefix."""
+    seq = G[f"s{si}/seq"].tolist()
+    p0, p0n = G[f"s{si}/p0"], G[f"s{si}/p0n"]
+    for T in range(1, len(seq) + 1):
+        want = p0[T, :p0n[T]].tolist()
+        assert k3.spec_draft(seq[:T], 8, 4, 3) == want, T
+        assert k3.spec_draft(seq[:T], 3, 4, 3) == want[:3], T
 
 
 @pytest.mark.parametrize("si", range(N_SEQ))
