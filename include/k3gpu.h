@@ -128,6 +128,36 @@ int k3gpu_bank_scan(K3GpuExpertBank *bank, uint8_t *safe_dev, void *stream);
  * [I][L/32] for w1 and w3; [L][I/2], [L][I/32] for w2). K3GPU_EINVAL for a missing,
  * mis-shaped or unreadable tensor or a malformed header, K3GPU_ECAPACITY when host_bytes
  * is short of n * stride. */
+/* Host C: a tensor index over a checkpoint's safetensors shards, the reference's
+ * k3_st_open / k3_st_find / k3_st_read (src/io/k3_st.h:60-80) for any tensor -- the
+ * trunk's bf16 and fp32 weights as well as the experts' U8 runs. Open reads every
+ * shard's header once (the reference's open takes a directory: every *.safetensors in
+ * it, by name; k3_st_open_files takes the paths); a malformed header, data past a file's
+ * end or a tensor name appearing twice in the set fails the open (NULL). Find is O(1);
+ * read copies the raw stored bytes with pread. Dtype codes are the reference's K3Dtype
+ * (src/io/k3_st.h:36-37). */
+enum { K3_ST_UNKNOWN = 0, K3_ST_U8 = 1, K3_ST_BF16 = 2, K3_ST_F16 = 3, K3_ST_F32 = 4 };
+typedef struct K3StIndex K3StIndex;
+typedef struct K3StTensorInfo {
+    int dtype;                 /* K3_ST_*; K3_ST_UNKNOWN for any other dtype string */
+    char dtype_name[16];       /* the header's dtype string, NUL-terminated          */
+    int ndim;                  /* <= 8                                               */
+    int64_t shape[8];
+    int shard;                 /* index of the file holding it                       */
+    int64_t nbytes;
+} K3StTensorInfo;
+K3StIndex *k3_st_open(const char *dir);
+K3StIndex *k3_st_open_files(const char *const *files, int n_files);
+void k3_st_close(K3StIndex *s);
+/* the indexed tensors (metadata excluded), shard by shard in header order */
+int k3_st_count(const K3StIndex *s);
+const char *k3_st_name(const K3StIndex *s, int i);
+/* K3GPU_OK, or K3GPU_EINVAL for an absent name (a missing weight must stop a load). */
+int k3_st_find(const K3StIndex *s, const char *name, K3StTensorInfo *info);
+/* bytes read (the tensor's nbytes), K3GPU_EINVAL (absent, unreadable) or
+ * K3GPU_ECAPACITY (buf_bytes short of nbytes). */
+int64_t k3_st_read(const K3StIndex *s, const char *name, void *buf, size_t buf_bytes);
+
 int k3_bank_read_safetensors(const char *const *files, int n_files, int layer, int e0, int n,
                              int L, int I, uint8_t *host_bank, size_t host_bytes);
 

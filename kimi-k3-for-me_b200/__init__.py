@@ -125,6 +125,14 @@ SpecVerifyFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.
 SpecCommitFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_int), C.c_int)
 
 
+ST_UNKNOWN, ST_U8, ST_BF16, ST_F16, ST_F32 = range(5)
+
+
+class K3StTensorInfo(C.Structure):
+    _fields_ = [("dtype", I), ("dtype_name", C.c_char * 16), ("ndim", I), ("shape", C.c_int64 * 8),
+                ("shard", I), ("nbytes", C.c_int64)]
+
+
 class K3GpuEpGroup(C.Structure):
     _fields_ = [("arena", VP * EP_MAX_WORLD), ("world", I), ("rank", I), ("cap", I), ("L", I), ("K", I),
                 ("n_local", I)]
@@ -207,6 +215,13 @@ _SIGS = {
     "k3_spec_loop_step": ([VP, VP, VP, VP], I),
     "k3_spec_loop_state": ([VP, VP, VP, VP, VP], I),
     "k3_spec_loop_ids": ([VP, VP, I], I),
+    "k3_st_open": ([C.c_char_p], VP),
+    "k3_st_open_files": ([VP, I], VP),
+    "k3_st_close": ([VP], None),
+    "k3_st_count": ([VP], I),
+    "k3_st_name": ([VP, I], C.c_char_p),
+    "k3_st_find": ([VP, C.c_char_p, VP], I),
+    "k3_st_read": ([VP, C.c_char_p, VP, SZ], C.c_int64),
     "k3_suffix_drafter_features": ([VP, VP, I, VP], I),
     "k3_spec_p3_length": ([VP, I, VP, C.c_double, I], I),
     "k3_spec_p3_cost_length": ([VP, I, VP, VP, I], I),
@@ -830,6 +845,54 @@ class SpecLoop:
         if self._L:
             lib.k3_spec_loop_free(self._L)
             self._L = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 -- interpreter shutdown may have unloaded the library
+            pass
+
+
+class SafetensorsIndex:
+    """A checkpoint's shards indexed by tensor name (k3_st_open / find / read): host C, no
+    GPU. Open a directory (every *.safetensors in it) or a list of shard paths."""
+
+    _NP = {ST_U8: "uint8", ST_BF16: "uint16", ST_F16: "float16", ST_F32: "float32"}
+
+    def __init__(self, where):
+        if isinstance(where, (str, bytes, os.PathLike)):
+            self._s = lib.k3_st_open(os.fsencode(where))
+        else:
+            paths = [os.fsencode(p) for p in where]
+            arr = (C.c_char_p * max(len(paths), 1))(*paths)
+            self._s = lib.k3_st_open_files(arr, len(paths))
+        if not self._s:
+            raise K3Error(f"k3_st_open: cannot index {where!r}")
+
+    def names(self):
+        return [lib.k3_st_name(self._s, i).decode() for i in range(lib.k3_st_count(self._s))]
+
+    def info(self, name):
+        t = K3StTensorInfo()
+        check(lib.k3_st_find(self._s, name.encode(), C.byref(t)), f"k3_st_find({name!r})")
+        return {"dtype": t.dtype, "dtype_name": t.dtype_name.decode(), "shape": list(t.shape[:t.ndim]),
+                "shard": t.shard, "nbytes": t.nbytes}
+
+    def read(self, name):
+        """The stored bytes as a numpy array of the tensor's shape (bf16 as uint16 bit
+        patterns; other dtypes as raw uint8)."""
+        import numpy as np
+        t = self.info(name)
+        buf = np.empty(t["nbytes"], np.uint8)
+        got = lib.k3_st_read(self._s, name.encode(), buf.ctypes.data, buf.nbytes)
+        check(int(got) if got < 0 else 0, f"k3_st_read({name!r})")
+        dt = self._NP.get(t["dtype"])
+        return buf.view(dt).reshape(t["shape"]) if dt else buf
+
+    def close(self) -> None:
+        if self._s:
+            lib.k3_st_close(self._s)
+            self._s = None
 
     def __del__(self):
         try:

@@ -10,6 +10,7 @@
 // for w = w1, w2, w3, with w1/w3 [I][L/2] + [I][L/32] and w2 [L][I/2] + [L][I/32]. The
 // device bank keeps them in the same order (k3gpu_bank_layout), so each expert lands with
 // one read per tensor, or one read per expert when the six are contiguous in the file.
+#include <dirent.h>
 #include <fcntl.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -17,6 +18,7 @@
 #include <string.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -288,4 +290,144 @@ extern "C" int k3_bank_read_safetensors(const char *const *files, int n_files, i
     }
     for (int fd : fds) close(fd);
     return st;
+}
+
+// ---- a tensor index over a shard set (the reference's k3_st_open / find / read) --------
+// One open over the shards' headers, then any tensor by name: the trunk's bf16 and fp32
+// tensors as well as the experts' U8 runs, read raw with pread (no mapping, so resident
+// memory stays what the caller holds).
+struct K3StIndex {
+    std::vector<int> fds;
+    std::unordered_map<std::string, Entry> index;
+    std::vector<std::string> names;   // discovery order: shard by shard, header order
+};
+
+namespace {
+
+int dtype_code(const std::string &d)
+{
+    if (d == "U8") return K3_ST_U8;
+    if (d == "BF16") return K3_ST_BF16;
+    if (d == "F16") return K3_ST_F16;
+    if (d == "F32") return K3_ST_F32;
+    return K3_ST_UNKNOWN;
+}
+
+// header keys in file order, for the discovery order of the index
+std::vector<std::string> header_names(int fd)
+{
+    std::vector<std::string> out;
+    uint8_t nb[8];
+    if (pread(fd, nb, 8, 0) != 8) return out;
+    uint64_t n = 0;
+    for (int i = 7; i >= 0; i--) n = (n << 8) | nb[i];
+    if (n == 0 || n > (1ull << 30)) return out;
+    std::vector<char> h(n);
+    if (pread(fd, h.data(), n, 8) != (ssize_t)n) return out;
+    Scan s{h.data(), h.data() + n};
+    if (!s.eat('{') || s.eat('}')) return out;
+    do {
+        std::string name = s.str();
+        if (!s.ok || !s.eat(':')) break;
+        s.skip_value();
+        if (name != "__metadata__") out.push_back(name);
+    } while (s.ok && s.eat(','));
+    return out;
+}
+
+}  // namespace
+
+extern "C" K3StIndex *k3_st_open_files(const char *const *files, int n_files)
+{
+    if (!files || n_files <= 0) return nullptr;
+    K3StIndex *s = new K3StIndex;
+    bool ok = true;
+    for (int f = 0; f < n_files && ok; f++) {
+        const int fd = files[f] ? open(files[f], O_RDONLY) : -1;
+        if (fd < 0) { ok = false; break; }
+        s->fds.push_back(fd);
+        std::unordered_map<std::string, Entry> one;
+        int64_t fb = 0;
+        if (read_header(fd, f, &one, &fb) != K3GPU_OK) { ok = false; break; }
+        for (const std::string &name : header_names(fd)) {
+            const auto it = one.find(name);
+            if (it == one.end()) continue;                   // an entry without data_offsets
+            // a name already seen, in another shard or earlier in this one: the set is broken
+            if (!s->index.emplace(name, it->second).second) { ok = false; break; }
+            s->names.push_back(name);
+        }
+    }
+    if (!ok) {
+        k3_st_close(s);
+        return nullptr;
+    }
+    return s;
+}
+
+extern "C" K3StIndex *k3_st_open(const char *dir)
+{
+    if (!dir) return nullptr;
+    DIR *d = opendir(dir);
+    if (!d) return nullptr;
+    std::vector<std::string> paths;
+    while (const dirent *e = readdir(d)) {
+        const std::string n = e->d_name;
+        const std::string ext = ".safetensors";
+        if (n.size() > ext.size() && n.compare(n.size() - ext.size(), ext.size(), ext) == 0)
+            paths.push_back(std::string(dir) + "/" + n);
+    }
+    closedir(d);
+    if (paths.empty()) return nullptr;
+    std::sort(paths.begin(), paths.end());                   // shard order by name
+    std::vector<const char *> ptrs;
+    for (const std::string &p : paths) ptrs.push_back(p.c_str());
+    return k3_st_open_files(ptrs.data(), (int)ptrs.size());
+}
+
+extern "C" void k3_st_close(K3StIndex *s)
+{
+    if (!s) return;
+    for (int fd : s->fds) close(fd);
+    delete s;
+}
+
+extern "C" int k3_st_count(const K3StIndex *s) { return s ? (int)s->names.size() : 0; }
+
+extern "C" const char *k3_st_name(const K3StIndex *s, int i)
+{
+    if (!s || i < 0 || i >= (int)s->names.size()) return nullptr;
+    return s->names[(size_t)i].c_str();
+}
+
+extern "C" int k3_st_find(const K3StIndex *s, const char *name, K3StTensorInfo *info)
+{
+    if (!s || !name || !info) return K3GPU_EINVAL;
+    const auto it = s->index.find(name);
+    if (it == s->index.end()) return K3GPU_EINVAL;
+    const Entry &t = it->second;
+    if (t.shape.size() > 8) return K3GPU_EINVAL;
+    memset(info, 0, sizeof *info);
+    info->dtype = dtype_code(t.dtype);
+    snprintf(info->dtype_name, sizeof info->dtype_name, "%s", t.dtype.c_str());
+    info->ndim = (int)t.shape.size();
+    for (size_t i = 0; i < t.shape.size(); i++) info->shape[i] = t.shape[i];
+    info->shard = t.file;
+    info->nbytes = t.bytes;
+    return K3GPU_OK;
+}
+
+extern "C" int64_t k3_st_read(const K3StIndex *s, const char *name, void *buf, size_t buf_bytes)
+{
+    if (!s || !name || !buf) return K3GPU_EINVAL;
+    const auto it = s->index.find(name);
+    if (it == s->index.end()) return K3GPU_EINVAL;
+    const Entry &t = it->second;
+    if ((uint64_t)t.bytes > buf_bytes) return K3GPU_ECAPACITY;
+    int64_t done = 0;
+    while (done < t.bytes) {
+        const ssize_t r = pread(s->fds[(size_t)t.file], (char *)buf + done, (size_t)(t.bytes - done), t.off + done);
+        if (r <= 0) return K3GPU_EINVAL;
+        done += r;
+    }
+    return t.bytes;
 }

@@ -1,4 +1,5 @@
-"""The safetensors expert loader (k3_bank_read_safetensors), CPU only.
+"""The safetensors readers, CPU only: the expert-run loader (k3_bank_read_safetensors) and
+the tensor index over a shard set (k3_st_open / find / read, any tensor by name).
 
 Shards are written here in the checkpoint format the reference documents (src/io/k3_st.h:
 7-13: 8-byte little-endian header length, JSON header, data with offsets relative to the
@@ -153,3 +154,67 @@ def test_errors(k3, tmp_path):
     assert lib.k3_bank_read_safetensors(one, 1, LAYER, 0, 1, L, I, buf.ctypes.data, buf.nbytes) == k3.K3GPU_EINVAL
     assert lib.k3_bank_read_safetensors(arr, 2, LAYER, 2 ** 31 - 2, 4, L, I, buf.ctypes.data, buf.nbytes) == \
         k3.K3GPU_EINVAL
+
+
+def test_tensor_index_reads_any_tensor(k3, tmp_path):
+    """k3_st_open / find / read: every tensor of both shards by name (escaped names, bf16,
+    f32, f16, u8, an empty tensor), in discovery order, opened by directory or by paths;
+    the expert tensors read through it equal what the expert-run reader placed."""
+    rng = np.random.default_rng(7)
+    ex, files = build_shards(tmp_path, rng)
+    trunk = rng.standard_normal((5, 12)).astype(np.float32)
+    bf = (rng.standard_normal(33).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    extra = {"language_model.model.embed_tokens.weight": ("F32", [5, 12], trunk.tobytes()),
+             "language_model.model.norm.weight": ("BF16", [33], bf.tobytes()),
+             "unicode.é€.name": ("I64", [2], np.arange(2, dtype=np.int64).tobytes())}
+    pc = str(tmp_path / "model-00003-of-00003.safetensors")
+    write_shard(pc, extra)
+    for where in (str(tmp_path), files + [pc]):
+        idx = k3.SafetensorsIndex(where)
+        names = idx.names()
+        assert len(names) == len(set(names)) == 4 * 6 + 3 + 3
+        e = idx.info("language_model.model.embed_tokens.weight")
+        assert (e["dtype"], e["shape"], e["nbytes"]) == (k3.ST_F32, [5, 12], trunk.nbytes)
+        np.testing.assert_array_equal(idx.read("language_model.model.embed_tokens.weight"), trunk)
+        np.testing.assert_array_equal(idx.read("language_model.model.norm.weight"), bf)
+        assert idx.info('odd "name" with \\ escapes and é')["shape"] == []
+        assert idx.read('odd "name" with \\ escapes and é').tobytes() == np.float32(1.5).tobytes()
+        assert idx.info("an.empty.tensor")["nbytes"] == 0
+        u = idx.info("unicode.é€.name")
+        assert (u["dtype"], u["dtype_name"]) == (k3.ST_UNKNOWN, "I64")
+        for e_ in range(4):
+            for (w, kind), arr in ex[e_].items():
+                got = idx.read(NAME.format(LAYER, e_, w, kind))
+                assert got.dtype == np.uint8 and got.shape == arr.shape
+                np.testing.assert_array_equal(got, arr)
+        with pytest.raises(k3.K3Error):
+            idx.info("no.such.tensor")
+        C = k3.C
+        small = np.empty(10, np.uint8)
+        assert k3.lib.k3_st_read(idx._s, b"language_model.model.embed_tokens.weight", small.ctypes.data,
+                                 small.nbytes) == k3.K3GPU_ECAPACITY
+        idx.close()
+    # the directory form visits shards by name: shard 1 first, in header order
+    idx = k3.SafetensorsIndex(str(tmp_path))
+    assert idx.info(idx.names()[0])["shard"] == 0
+    assert idx.names()[-1] == "unicode.é€.name"
+    idx.close()
+
+
+def test_tensor_index_refuses_broken_sets(k3, tmp_path):
+    rng = np.random.default_rng(8)
+    ok = tmp_path / "ok"
+    ok.mkdir()
+    ex, files = build_shards(ok, rng)
+    dup = str(tmp_path / "dup.safetensors")
+    write_shard(dup, {NAME.format(LAYER, 0, "w1", "weight_scale"): u8(ex[0][("w1", "weight_scale")])})
+    with pytest.raises(k3.K3Error):
+        k3.SafetensorsIndex(files + [dup])                 # a name in two shards
+    short = str(tmp_path / "short.safetensors")
+    write_shard(short, {"t": ("F32", [4], np.zeros(4, np.float32).tobytes())})
+    with open(short, "r+b") as f:
+        f.truncate(os.path.getsize(short) - 4)
+    with pytest.raises(k3.K3Error):
+        k3.SafetensorsIndex([short])                       # data past the end
+    with pytest.raises(k3.K3Error):
+        k3.SafetensorsIndex(str(tmp_path / "empty_dir_that_does_not_exist"))
