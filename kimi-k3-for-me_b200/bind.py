@@ -146,3 +146,16 @@ class Binder:
         if lm_head:
             f["lm_head"] = self._get("language_model.lm_head.weight", V * E, True)
         return f
+
+
+def to_device(fields, device="cuda"):
+    """The bound arrays as torch tensors on `device` (bf16 bit patterns as int16), keyed as
+    the layer wrappers take them (kda_weights, mla_weights, moe_weights and the decoder
+    layers); entries that are not arrays (kind, dense, an absent gate) are left out."""
+    import torch
+    out = {}
+    for k, v in fields.items():
+        if isinstance(v, np.ndarray):
+            a = v.view(np.int16) if v.dtype == np.uint16 else v
+            out[k] = torch.from_numpy(np.ascontiguousarray(a)).to(device)
+    return out

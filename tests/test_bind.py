@@ -201,3 +201,27 @@ def test_refuses_missing_and_misshaped_tensors(k3, tmp_path):
     with pytest.raises(b.BindError, match="e_score_correction_bias has 5 elements"):
         bd.layer(2)
     idx.close()
+
+
+def test_bound_fields_fill_the_layer_structures(k3, tmp_path):
+    """Every field K3GpuKdaW, K3GpuMlaW, K3GpuMoeW (the K3 form) and the decoder layer
+    structures read comes out of the binder under the same name, so the package's
+    kda_weights / mla_weights / moe_weights and decoder-layer wrappers take to_device's
+    tensors as they are (those wrappers accept only CUDA tensors; here the names and
+    dtypes are checked)."""
+    b = _bind_mod()
+    write(str(tmp_path / "m.safetensors"), tensors(np.random.default_rng(5)))
+    idx = k3.SafetensorsIndex(str(tmp_path))
+    bd = b.Binder(idx, CFG)
+    kda, mla = bd.layer(2), bd.layer(3)
+    layer_fields = {"attn_res_fold", "mlp_res_fold", "in_norm", "post_norm", "gate_W", "gate_bias"}
+    moe_fields = {"down", "up", "sh1", "sh3", "sh2", "gate_W", "gate_bias", "latent_norm"}
+    assert {n for n, _ in k3.K3GpuKdaW._fields_} | layer_fields | moe_fields <= set(kda)
+    assert {n for n, _ in k3.K3GpuMlaW._fields_} | layer_fields | moe_fields <= set(mla)
+    dk = b.to_device(kda, "cpu")
+    assert "kind" not in dk and "dense" not in dk
+    for n, _ in k3.K3GpuKdaW._fields_:
+        assert dk[n].dtype == (torch.int16 if kda[n].dtype == np.uint16 else torch.float32), n
+    assert dk["q"].numel() == CFG["kda_num_heads"] * CFG["kda_head_dim"] * CFG["hidden_size"]
+    assert dk["A_log"].numel() == CFG["kda_num_heads"]
+    idx.close()
