@@ -46,6 +46,7 @@ _KEYS = {
     "situ_linear_beta": ("activation_situ_linear_beta", "situ_linear_beta", float),
 }
 _SWITCHES = ("mla_use_output_gate", "moe_renormalize", "latent_moe_use_norm")
+MAX_TOPK = 64   # the reference's K3_MAX_TOPK (include/k3/k3.h:864), also the router's limit here
 
 
 class ConfigError(ValueError):
@@ -94,6 +95,23 @@ def read_config(src) -> dict:
     if missing:
         raise ConfigError("the config is missing required field(s): " + ", ".join(missing) +
                           " (no defaults are substituted: a config read in part is a different model)")
+    # structural checks (k3_cfg.h:202-240): a config that parses but cannot be this model
+    nl = out["num_hidden_layers"]
+    if nl <= 0 or out["hidden_size"] <= 0 or out["vocab_size"] <= 0:
+        raise ConfigError("non-positive layers, hidden size or vocabulary")
+    if len(out["full_attn_layers"]) >= nl:
+        raise ConfigError(f"{len(out['full_attn_layers'])} of {nl} layers marked full attention: no KDA layer")
+    for i, x in enumerate(out["full_attn_layers"]):
+        if x < 1 or x > nl:
+            raise ConfigError(f"full_attn_layers[{i}] = {x} is outside 1..{nl} (the list is one-based)")
+    if out["num_experts_per_token"] > MAX_TOPK:
+        raise ConfigError(f"top-{out['num_experts_per_token']} routing: at most {MAX_TOPK} is supported")
+    if out["num_experts_per_token"] > out["num_experts"]:
+        raise ConfigError(f"top-{out['num_experts_per_token']} of {out['num_experts']} experts")
+    if out["attn_res_block_size"] <= 0:
+        raise ConfigError(f"attn_res_block_size {out['attn_res_block_size']}")
+    if out["short_conv_kernel_size"] < 1:
+        raise ConfigError(f"short_conv_kernel_size {out['short_conv_kernel_size']}")
     return out
 
 

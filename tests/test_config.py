@@ -9,6 +9,7 @@ refused with every missing key named, never defaulted; the three optional switch
 default on. The layer and MoE configuration structures must carry every field.
 """
 import copy
+import json
 import os
 import sys
 
@@ -106,3 +107,40 @@ def test_structures_carry_every_field(k3):
         assert getattr(mc, n) == pytest.approx(v), n
     with pytest.raises(m.ConfigError):
         m._fill(k3.K3GpuMoeCfg, {"hiden": 1})
+
+
+# the reference loader's field names -> this reader's (canonical) names
+REF_FIELDS = {"hidden": "hidden_size", "n_layers": "num_hidden_layers", "vocab": "vocab_size",
+              "rms_eps": "rms_norm_eps", "kda_heads": "kda_num_heads", "kda_head_dim": "kda_head_dim",
+              "conv_k": "short_conv_kernel_size", "gate_lb": "gate_lower_bound", "n_heads": "num_attention_heads",
+              "q_lora": "q_lora_rank", "kv_lora": "kv_lora_rank", "qk_nope": "qk_nope_head_dim",
+              "qk_rope": "qk_rope_head_dim", "v_head": "v_head_dim", "mla_out_gate": "mla_use_output_gate",
+              "n_experts": "num_experts", "topk": "num_experts_per_token", "n_shared": "num_shared_experts",
+              "latent": "routed_expert_hidden_size", "moe_inter": "moe_intermediate_size",
+              "routed_scale": "routed_scaling_factor", "moe_renorm": "moe_renormalize",
+              "latent_norm": "latent_moe_use_norm", "first_dense": "first_k_dense_replace",
+              "dense_inter": "intermediate_size", "attn_res_block": "attn_res_block_size",
+              "situ_b1": "situ_beta", "situ_b2": "situ_linear_beta", "full_attn": "full_attn_layers"}
+GOLD = json.load(open(os.path.join(HERE, "golden", "cfg_golden.json")))
+
+
+@pytest.mark.parametrize("name", sorted(GOLD))
+def test_reader_matches_reference_loader(name):
+    """Against the reference's own k3_cfg_load on the same document
+    (tests/golden/cfg_golden.json, tests/golden/make_cfg_golden.py): the same refusals, and
+    every parsed field equal (floats as the float32 the loader stores)."""
+    import numpy as np
+    m = _cfg_mod()
+    case = GOLD[name]
+    if case["ref"] == "REFUSED":
+        with pytest.raises(m.ConfigError):
+            m.read_config(copy.deepcopy(case["doc"]))
+        return
+    c = m.read_config(copy.deepcopy(case["doc"]))
+    for rf, mine in REF_FIELDS.items():
+        want, got = case["ref"][rf], c[mine]
+        if isinstance(want, float) or isinstance(got, float):
+            assert np.float32(got) == np.float32(want), rf
+        else:
+            assert (int(got) if isinstance(got, bool) else got) == want, rf
+    assert m.attn_res_stride(c) == case["ref"]["stride"]
