@@ -160,17 +160,24 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        return self.summarize(self.lines)
+
+    @staticmethod
+    def summarize(lines):
+        """Median SM clock under load, the max clock, and every throttle reason seen Active
+        in the samples (csv,noheader,nounits lines of FIELDS); malformed lines are skipped."""
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
+                clk, cmax = float(f[1]), float(f[2])
             except ValueError:
                 continue
+            sm.append(clk)
+            smax = cmax
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)

@@ -1,0 +1,44 @@
+"""Pieces of bench.py's reporting that run without a GPU, CPU only: the clock record
+that decides whether a timed run stands (median SM clock under load, the throttle
+reasons seen Active -- hw_slowdown and the thermal ones reject a run, sw_power_cap is
+kept and noted), and the unique-expert byte count behind the roofline's achieved figure.
+"""
+import importlib.util
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+def line(sm, smax, hw="Not Active", hwt="Not Active", swt="Not Active", cap="Not Active"):
+    return f"0, {sm}, {smax}, 812.40, 0x0000000000000000, {hw}, {hwt}, {swt}, {cap}"
+
+
+def test_clock_summary():
+    b = _bench()
+    s = b.ClockSampler.summarize([line(1965, 1965), line(1950, 1965), line(1965, 1965)])
+    assert s == {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 3}
+    s = b.ClockSampler.summarize([line(1300, 1965, cap="Active"), line(1320, 1965, cap="Active"),
+                                  line(1410, 1965, hw="Active")])
+    assert s["reasons"] == ["hw_slowdown", "sw_power_cap"] and s["sm_mhz"] == 1320.0
+    s = b.ClockSampler.summarize([line(1800, 1965, hwt="Active", swt="Active")])
+    assert s["reasons"] == ["hw_thermal_slowdown", "sw_thermal_slowdown"]
+    # malformed samples are skipped whole: too few fields, a clock or max clock not a number
+    s = b.ClockSampler.summarize(["garbage", line("[N/A]", 1965), line(1500, "[N/A]"), line(1700, 1965)])
+    assert s["samples"] == 1 and s["sm_mhz"] == 1700.0
+    assert b.ClockSampler.summarize([]) == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+
+def test_unique_expert_bytes():
+    b = _bench()
+    idx = np.array([[3, 7], [7, 1], [3, 3]], np.int32)
+    u, nbytes = b.unique_experts_bytes(idx, 1000)
+    assert u == 3 and nbytes == 3000
