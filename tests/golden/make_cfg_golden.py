@@ -12,7 +12,7 @@ non-integral integer, a key present in both text_config and linear_attn_config; 
 reference's own config fixtures (tests/fixtures/cfg/*.json) and the configs inside its
 model fixtures (tiny_k3.json, ref_k3.json).
 
-Usage: python tests/golden/make_cfg_golden.py [--ref /root/reference]
+Usage: python tests/golden/make_cfg_golden.py [--ref <path of the reference checkout>]
 (needs oracle/_ref/cfgdump: `make -C oracle`)
 """
 from __future__ import annotations

@@ -23,7 +23,7 @@ It also writes tests/golden/study_table.json: the study file's p3_table, cost_mo
 p2_defaults_from_calibration sections, as a user would hand them to
 spec_table.load_study.
 
-Usage: python tests/golden/make_drafter_golden.py [--ref /root/reference]
+Usage: python tests/golden/make_drafter_golden.py [--ref <path of the reference checkout>]
 """
 from __future__ import annotations
 

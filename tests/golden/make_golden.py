@@ -13,7 +13,7 @@ Two sources, both the reference's own:
    stored; the tests regenerate the inputs from the seeds with numpy's PCG64 (stable
    across numpy versions), so large inputs never enter the repository.
 
-Usage: python tests/golden/make_golden.py [--ref /root/reference]
+Usage: python tests/golden/make_golden.py [--ref <path of the reference checkout>]
 """
 from __future__ import annotations
 
