@@ -659,9 +659,11 @@ enum {
     K3_DRAFT_EAGER = 2,  /* P1                                                  */
     K3_DRAFT_SUFFIX = 3, /* P2 (min_len)                                        */
     K3_DRAFT_P3 = 4,     /* P3 (p3_q with p3_delta, or p3_cost and p3_replay)   */
-    K3_DRAFT_TREE = 5    /* a draft tree (k3_suffix_drafter_tree: tree_nodes,
+    K3_DRAFT_TREE = 5,   /* a draft tree (k3_suffix_drafter_tree: tree_nodes,
                             tree_branch, depth spec_n, min_len), accepted as
                             k3gpu_accept_tree_greedy does                       */
+    K3_DRAFT_MODEL = 6   /* a second model proposes spec_n ids (the engine's
+                            --draft): k3_spec_loop_set_draft_model             */
 };
 enum { K3_SPEC_LOOP_GEN = 1, K3_SPEC_LOOP_STOP_ID = 2, K3_SPEC_LOOP_CONTEXT = 3 };
 typedef struct K3SpecLoopCfg {
@@ -679,6 +681,8 @@ typedef struct K3SpecLoopCfg {
 typedef struct K3SpecLoopStats {
     long long steps, sweeps, drafted, accepted, dropped, full, partial, cut;
     long long hist[9];
+    /* the draft model's (k3_run.c:2636): rounds, ids proposed, accepted, fed positions dropped */
+    long long draft_rounds, draft_drafted, draft_accepted, draft_dropped;
 } K3SpecLoopStats;
 /* One step's (nd, m, keep) (the engine's spec_trace, :2946-2949) and the positions fed. */
 typedef struct K3SpecStepTrace {
@@ -696,6 +700,13 @@ void k3_spec_loop_free(K3SpecLoop *L);
  * finished K3_SPEC_LOOP_GEN / _STOP_ID / _CONTEXT (this and every later call emit
  * nothing), or a negative status (K3GPU_ECALLBACK when a callback failed). */
 int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStepTrace *trace);
+/* The draft model for K3_DRAFT_MODEL, set before the first step; its callbacks have the
+ * target's signatures (parent always NULL). It reads the conversation once at the first
+ * step (verify then commit of every id); each later drafting step calls dverify once with
+ * the ids it has not seen plus the pending one and then once per further draft with its
+ * own previous id, each call continuing where the previous tentative one ended, and then
+ * dcommit(base, keep) keeps the first `keep` of those tentative positions. */
+int k3_spec_loop_set_draft_model(K3SpecLoop *L, K3SpecVerifyFn dverify, K3SpecCommitFn dcommit, void *dctx);
 /* T, cached, generated count and counters; returns the finished code (0 while running). */
 int k3_spec_loop_state(const K3SpecLoop *L, int *T, int *cached, int *nout, K3SpecLoopStats *stats);
 /* The conversation's ids (ids[0..T), cap >= T); returns T. */

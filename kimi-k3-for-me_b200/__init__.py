@@ -101,7 +101,7 @@ class K3SpecCost(C.Structure):
 
 SPEC_P3_CODES = 234
 
-DRAFT_NONE, DRAFT_NGRAM, DRAFT_EAGER, DRAFT_SUFFIX, DRAFT_P3, DRAFT_TREE = range(6)
+DRAFT_NONE, DRAFT_NGRAM, DRAFT_EAGER, DRAFT_SUFFIX, DRAFT_P3, DRAFT_TREE, DRAFT_MODEL = range(7)
 SPEC_LOOP_GEN, SPEC_LOOP_STOP_ID, SPEC_LOOP_CONTEXT = 1, 2, 3
 
 
@@ -113,7 +113,8 @@ class K3SpecLoopCfg(C.Structure):
 
 class K3SpecLoopStats(C.Structure):
     _fields_ = [(n, C.c_longlong) for n in ("steps", "sweeps", "drafted", "accepted", "dropped", "full",
-                                            "partial", "cut")] + [("hist", C.c_longlong * 9)]
+                                            "partial", "cut")] + [("hist", C.c_longlong * 9)] + \
+               [(n, C.c_longlong) for n in ("draft_rounds", "draft_drafted", "draft_accepted", "draft_dropped")]
 
 
 class K3SpecStepTrace(C.Structure):
@@ -215,6 +216,7 @@ _SIGS = {
     "k3_spec_loop_step": ([VP, VP, VP, VP], I),
     "k3_spec_loop_state": ([VP, VP, VP, VP, VP], I),
     "k3_spec_loop_ids": ([VP, VP, I], I),
+    "k3_spec_loop_set_draft_model": ([VP, VP, VP, VP], I),
     "k3_st_open": ([C.c_char_p], VP),
     "k3_st_open_files": ([VP, I], VP),
     "k3_st_close": ([VP], None),
@@ -764,7 +766,7 @@ class SpecLoop:
 
     def __init__(self, ids, verify, commit, *, cached=0, policy=DRAFT_NGRAM, spec_n=8, min_len=1, gen=64,
                  tmax=None, kv_cap=None, stop_ids=(), p3_q=None, p3_delta=0.22, p3_cost=None, p3_replay=False,
-                 tree_nodes=64, tree_branch=4):
+                 tree_nodes=64, tree_branch=4, draft_verify=None, draft_commit=None):
         ids = [int(v) for v in ids]
         tmax = tmax if tmax is not None else len(ids) + gen + 1
         self._errors = []
@@ -789,8 +791,34 @@ class SpecLoop:
                 self._errors.append(e)
                 return 1
 
+        def wrap_verify(fn):
+            def _cb(_ctx, p, par, n, base, arg):
+                try:
+                    out = fn([p[i] for i in range(n)], base, [par[i] for i in range(n)] if par else None)
+                    if len(out) != n:
+                        raise ValueError(f"verify returned {len(out)} ids for {n} positions")
+                    for i, v in enumerate(out):
+                        arg[i] = int(v)
+                    return 0
+                except Exception as e:  # noqa: BLE001 -- reported by step()
+                    self._errors.append(e)
+                    return 1
+            return _cb
+
+        def wrap_commit(fn):
+            def _cb(_ctx, base, path, keep):
+                try:
+                    fn(base, keep, [path[i] for i in range(keep)] if path else None)
+                    return 0
+                except Exception as e:  # noqa: BLE001
+                    self._errors.append(e)
+                    return 1
+            return _cb
+
         self._L = None
         self._fns = (SpecVerifyFn(_verify), SpecCommitFn(_commit))
+        if draft_verify is not None:
+            self._fns += (SpecVerifyFn(wrap_verify(draft_verify)), SpecCommitFn(wrap_commit(draft_commit)))
         self._stop = (C.c_int * max(len(stop_ids), 1))(*stop_ids)
         self._q = _p3_table(p3_q) if p3_q is not None else None
         self._cost = p3_cost
@@ -803,6 +831,9 @@ class SpecLoop:
                                           C.cast(self._fns[0], VP), C.cast(self._fns[1], VP), None)
         if not self._L:
             raise K3Error("k3_spec_loop_create: bad configuration")
+        if draft_verify is not None:
+            check(lib.k3_spec_loop_set_draft_model(self._L, C.cast(self._fns[2], VP), C.cast(self._fns[3], VP), None),
+                  "k3_spec_loop_set_draft_model")
         self.tmax = tmax
 
     def step(self):

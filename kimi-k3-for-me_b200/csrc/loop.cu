@@ -20,6 +20,10 @@
 // nodes' parents, acceptance follows k3gpu_accept_tree_greedy (a child is accepted when
 // its parent is and its id is the parent's next id; the lowest-index such child wins),
 // and commit gets the accepted path's nodes.
+// With the draft-model policy (the engine's --draft, k3_run.c:2862-2905, 2956-2965) a
+// second model proposes: it trails the target by dlag positions, feeds the ids it has not
+// seen plus the pending one and then chains its own next ids, tentatively, and after the
+// target has decided commits exactly the positions behind the kept ids it fed.
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -38,6 +42,10 @@ struct K3SpecLoop {
     int arg_cap;
     int *tok, *parent;          // the tree draft [tree_nodes]
     K3SuffixDrafter *sam;       // P2 / P3 history
+    K3SpecVerifyFn dverify;     // the draft model (K3_DRAFT_MODEL)
+    K3SpecCommitFn dcommit;
+    void *dctx;
+    int dcached;                // positions the draft model has consumed
     K3SpecLoopStats st;
 };
 
@@ -113,7 +121,7 @@ extern "C" K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *
     if (cfg->tmax < n_ids || cfg->gen < 0 || cfg->spec_n < 0 || cfg->spec_n > 8 || cfg->n_stop < 0 ||
         (cfg->n_stop > 0 && !cfg->stop_ids) || cfg->kv_cap < n_ids)
         return nullptr;
-    if (cfg->policy < K3_DRAFT_NONE || cfg->policy > K3_DRAFT_TREE) return nullptr;
+    if (cfg->policy < K3_DRAFT_NONE || cfg->policy > K3_DRAFT_MODEL) return nullptr;
     if (cfg->policy == K3_DRAFT_TREE && (cfg->tree_nodes < 1 || cfg->tree_nodes > 64 || cfg->tree_branch < 1))
         return nullptr;
     if (cfg->policy == K3_DRAFT_P3 && !cfg->p3_q) return nullptr;
@@ -166,6 +174,7 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
     if (trace) memset(trace, 0, sizeof *trace);
     if (!L) return K3GPU_EINVAL;
     if (L->done) return L->done;
+    if (L->cfg.policy == K3_DRAFT_MODEL && !L->dverify) return K3GPU_EINVAL;
     int emit[9], emitn = 0, keep = 0;
     const int base = L->cached;
     if (!L->started) {
@@ -176,6 +185,13 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
         L->cached = base + n;
         L->started = 1;
         emit[emitn++] = L->arg[n - 1];
+        if (L->cfg.policy == K3_DRAFT_MODEL) {
+            // the draft model reads the whole conversation once (its state is never saved,
+            // so a resumed run replays everything through it, :2847-2853)
+            if (L->dverify(L->dctx, L->seq, nullptr, L->T, 0, L->arg) != 0) return K3GPU_ECALLBACK;
+            if (L->dcommit(L->dctx, 0, nullptr, L->T) != 0) return K3GPU_ECALLBACK;
+            L->dcached = L->T;
+        }
         keep = emit_keep(L, emit, emitn);
         if (trace) *trace = K3SpecStepTrace{0, 0, keep, n};
     } else if (L->cfg.policy == K3_DRAFT_TREE) {
@@ -210,10 +226,33 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
         }
         if (trace) *trace = K3SpecStepTrace{nd, m, keep, n};
     } else {
-        int d[8], nd = 0;
+        int d[8], nd = 0, dlag = 0;
         const K3SpecLoopCfg &c = L->cfg;
-        if (c.policy != K3_DRAFT_NONE && L->T + c.spec_n + 1 < c.tmax && base + c.spec_n + 1 <= c.kv_cap)
+        const bool room = L->T + c.spec_n + 1 < c.tmax && base + c.spec_n + 1 <= c.kv_cap;
+        if (c.policy == K3_DRAFT_MODEL && room && c.spec_n > 0) {
+            dlag = base - L->dcached;
+            if (dlag < 0) return K3GPU_EINVAL;                 // the draft model is ahead
+            if (dlag + c.spec_n > c.spec_n + 1) {              // a backlog past its log: absorb it
+                if (L->dverify(L->dctx, L->seq + L->dcached, nullptr, dlag, L->dcached, L->arg) != 0 ||
+                    L->dcommit(L->dctx, L->dcached, nullptr, dlag) != 0)
+                    return K3GPU_ECALLBACK;
+                L->dcached = base;
+                dlag = 0;
+            }
+            // the unseen ids plus the pending one, then its own next ids, one at a time
+            if (L->dverify(L->dctx, L->seq + L->dcached, nullptr, dlag + 1, L->dcached, L->arg) != 0)
+                return K3GPU_ECALLBACK;
+            d[nd++] = L->arg[dlag];
+            while (nd < c.spec_n) {
+                if (L->dverify(L->dctx, &d[nd - 1], nullptr, 1, base + nd, L->arg) != 0) return K3GPU_ECALLBACK;
+                d[nd] = L->arg[0];
+                nd++;
+            }
+            L->st.draft_rounds++;
+            L->st.draft_drafted += nd;
+        } else if (c.policy != K3_DRAFT_NONE && c.policy != K3_DRAFT_MODEL && room) {
             nd = draft(L, d);
+        }
         int ids[9];
         ids[0] = L->seq[base];
         for (int i = 0; i < nd; i++) ids[1 + i] = d[i];
@@ -237,11 +276,29 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
             if (keep < m + 1) L->st.cut++;
             L->st.hist[m]++;
         }
+        if (c.policy == K3_DRAFT_MODEL && nd > 0) {
+            // the draft model keeps what the target kept of what it fed (:2956-2965)
+            const int dkeep = keep < nd ? keep : nd;
+            if (L->dcommit(L->dctx, base - dlag, nullptr, dlag + dkeep) != 0) return K3GPU_ECALLBACK;
+            L->dcached = base + dkeep;
+            L->st.draft_accepted += m;
+            L->st.draft_dropped += nd - dkeep;
+        }
         if (trace) *trace = K3SpecStepTrace{nd, m, keep, nd + 1};
     }
     L->st.steps++;
     if (append(L, emit, keep, out) != K3GPU_OK) return K3GPU_EINVAL;
     if (n_out) *n_out = keep;
+    return K3GPU_OK;
+}
+
+extern "C" int k3_spec_loop_set_draft_model(K3SpecLoop *L, K3SpecVerifyFn dverify, K3SpecCommitFn dcommit,
+                                            void *dctx)
+{
+    if (!L || !dverify || !dcommit || L->started || L->cfg.policy != K3_DRAFT_MODEL) return K3GPU_EINVAL;
+    L->dverify = dverify;
+    L->dcommit = dcommit;
+    L->dctx = dctx;
     return K3GPU_OK;
 }
 

@@ -432,16 +432,20 @@ def emit_keep(emit, nout, gen, T, tmax, stops):
 
 
 def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, stops, tree_nodes=64,
-              tree_branch=4):
+              tree_branch=4, draft_next=None):
     """The engine's incremental speculative loop (src/cli/k3_run.c:2812-3047) over a greedy
     model given as next_id(context ids) -> id. Policies 0 none, 1 the engine's n-gram
     spec_draft, 2 P1, 3 P2, 5 a suffix draft tree (suffix_tree_draft, depth spec_n) with
     greedy tree acceptance (a child is accepted when its parent is and its id is the
-    parent's next id, the lowest index first). Returns (generated ids,
-    [(nd, m, keep, fed)] per step, the engine's counters, cached, ids)."""
+    parent's next id, the lowest index first), 6 a draft model given as draft_next(context)
+    proposing spec_n ids greedily (the engine's --draft, src/cli/k3_run.c:2862-2905,
+    2956-2965; its draft counters: rounds, ids drafted, accepted, fed positions dropped).
+    Returns (generated ids, [(nd, m, keep, fed)] per step, the engine's counters, cached,
+    ids)."""
     seq = list(ids)
     out, trace = [], []
-    st = dict(steps=0, sweeps=0, drafted=0, accepted=0, dropped=0, full=0, partial=0, cut=0)
+    st = dict(steps=0, sweeps=0, drafted=0, accepted=0, dropped=0, full=0, partial=0, cut=0,
+              draft_rounds=0, draft_drafted=0, draft_accepted=0, draft_dropped=0)
     hist = [0] * 9
     g = 0
     while len(out) < gen or g == 0:
@@ -488,7 +492,15 @@ def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, 
         else:
             d = []
             if policy and T + spec_n + 1 < tmax and base + spec_n + 1 <= kv_cap:   # :2859
-                if policy == 1:
+                if policy == 6:
+                    if spec_n > 0:                            # the draft model's greedy chain
+                        ctx_d = seq[:base + 1]
+                        for _ in range(spec_n):
+                            d.append(draft_next(ctx_d))
+                            ctx_d = ctx_d + [d[-1]]
+                        st["draft_rounds"] += 1
+                        st["draft_drafted"] += spec_n
+                elif policy == 1:
                     buf = np.zeros(max(spec_n, 1), np.int32)
                     nd = orc().orc_spec_draft(np.asarray(seq, np.int32), T, spec_n, 4, 3, buf)
                     d = buf[:nd].tolist()
@@ -510,6 +522,9 @@ def spec_loop(next_id, ids, cached, policy, spec_n, min_len, gen, tmax, kv_cap, 
             emit = d[:m] + [arg[m]]
             keep = emit_keep(emit, len(out), gen, T, tmax, stops)
             cached = base + (keep if nd else 1)
+            if policy == 6 and nd:                            # :2956-2965
+                st["draft_accepted"] += m
+                st["draft_dropped"] += nd - min(keep, nd)
             if nd:                                            # :2945-2955
                 st["sweeps"] += 1
                 st["drafted"] += nd

@@ -229,3 +229,72 @@ def test_loop_errors(k3):
         loop.step()
     assert isinstance(e.value.__cause__, RuntimeError)
     loop.close()
+
+
+class FakeDraft:
+    """A draft model holding its consumed positions: several tentative verify calls, each
+    continuing where the previous one ended, then one commit of the first `keep`."""
+
+    def __init__(self, next_id):
+        self.next_id, self.state, self.pending = next_id, [], []
+
+    def verify(self, ids, base, parent=None):
+        assert parent is None and base == len(self.state) + len(self.pending)
+        out = [self.next_id(self.state + self.pending + ids[:i + 1]) for i in range(len(ids))]
+        self.pending += list(ids)
+        return out
+
+    def commit(self, base, keep, path=None):
+        assert path is None and base == len(self.state) and 0 <= keep <= len(self.pending)
+        self.state += self.pending[:keep]
+        self.pending = []
+
+
+@pytest.mark.parametrize("seed,spec_n,gen,stops,noise", [(31, 8, 120, (), 3), (32, 4, 100, (), 4),
+                                                          (33, 8, 77, (), 2), (34, 6, 150, "late", 3),
+                                                          (35, 3, 90, (), 1)])
+def test_draft_model_loop(k3, seed, spec_n, gen, stops, noise):
+    """The engine's --draft mode: a second model proposes spec_n ids a round. The generated
+    ids equal serial decoding of the target, the trace and every counter equal the engine
+    loop's restatement, and the draft model consumed exactly a prefix of the conversation."""
+    nid = make_model(seed, vocab=12 if stops == "late" else 9)
+    dnid = make_model(seed, vocab=12 if stops == "late" else 9, noise=noise)   # same table, other deviations
+    rng = np.random.default_rng(200 + seed)
+    prompt = rng.integers(0, 9, 24).tolist()
+    prompt += prompt[4:14]
+    if stops == "late":
+        stops = late_stop(nid, prompt, gen)
+    tmax = len(prompt) + gen + 21
+    m, dm = Fake(nid, []), FakeDraft(dnid)
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_MODEL, spec_n=spec_n, gen=gen, tmax=tmax,
+                       stop_ids=stops, draft_verify=dm.verify, draft_commit=dm.commit)
+    out, traces = loop.run()
+    assert out == serial(nid, prompt, gen, tmax, stops)
+    rout, rtrace, rst, rcached, rseq = O.spec_loop(nid, prompt, 0, 6, spec_n, 1, gen, tmax, tmax, set(stops),
+                                                   draft_next=dnid)
+    assert [(t["nd"], t["m"], t["keep"], t["fed"]) for t in traces] == rtrace
+    s = loop.state()
+    assert s["stats"] == rst and s["cached"] == rcached and loop.ids() == rseq
+    assert m.state == rseq[:rcached] and dm.pending == []
+    assert dm.state == rseq[:len(dm.state)] and len(dm.state) >= rcached - 1
+    st = s["stats"]
+    assert st["draft_rounds"] == st["sweeps"] and st["draft_drafted"] == st["drafted"]
+    assert st["draft_accepted"] == st["accepted"] and st["sweeps"] > 0
+    loop.close()
+
+
+def test_draft_model_that_never_agrees_and_a_missing_model(k3):
+    nid = make_model(41)
+    prompt = list(range(9)) * 3
+    m, dm = Fake(nid, []), FakeDraft(lambda ctx: (nid(ctx) + 1) % 9)      # always wrong
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_MODEL, gen=40, draft_verify=dm.verify,
+                       draft_commit=dm.commit)
+    out, traces = loop.run()
+    assert out == serial(nid, prompt, 40, len(prompt) + 41, ())
+    assert loop.state()["stats"]["draft_accepted"] == 0 and loop.state()["stats"]["draft_dropped"] > 0
+    loop.close()
+    m2 = Fake(nid, [])
+    loop = k3.SpecLoop(prompt, m2.verify, m2.commit, policy=k3.DRAFT_MODEL, gen=10)
+    with pytest.raises(k3.K3Error):
+        loop.step()                                                      # no draft model set
+    loop.close()
