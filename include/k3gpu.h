@@ -665,7 +665,7 @@ enum {
     K3_DRAFT_MODEL = 6   /* a second model proposes spec_n ids (the engine's
                             --draft): k3_spec_loop_set_draft_model             */
 };
-enum { K3_SPEC_LOOP_GEN = 1, K3_SPEC_LOOP_STOP_ID = 2, K3_SPEC_LOOP_CONTEXT = 3 };
+enum { K3_SPEC_LOOP_GEN = 1, K3_SPEC_LOOP_STOP_ID = 2, K3_SPEC_LOOP_CONTEXT = 3, K3_SPEC_LOOP_PAUSED = 4 };
 typedef struct K3SpecLoopCfg {
     int policy, spec_n, min_len;   /* spec_n <= 8                                          */
     int gen, tmax, kv_cap;         /* ids to generate; context limit; cache positions      */
@@ -676,6 +676,10 @@ typedef struct K3SpecLoopCfg {
     const K3SpecCost *p3_cost;     /* NULL: the delta rule                                 */
     int p3_replay;
     int tree_nodes, tree_branch;   /* the tree policy: nodes <= 64 per verify, children    */
+    int prefill_chunk;             /* the first step reads the prompt in passes of at most
+                                      this many positions (0: one pass; --prefill-chunk)    */
+    int pause_after;               /* with a checkpoint callback: pause after this many
+                                      checkpoints (0: never; --pause-after)                 */
 } K3SpecLoopCfg;
 /* The engine's spec counters (:2945-2955) and the histogram of accepted prefixes. */
 typedef struct K3SpecLoopStats {
@@ -691,6 +695,10 @@ typedef struct K3SpecStepTrace {
 typedef struct K3SpecLoop K3SpecLoop;
 typedef int (*K3SpecVerifyFn)(void *ctx, const int *ids, const int *parent, int n, int base, int *arg);
 typedef int (*K3SpecCommitFn)(void *ctx, int base, const int *path, int keep);
+/* called after every read-in pass that leaves prompt positions to go, with the positions
+ * read so far: the moment to save a checkpoint of the model's state (--checkpoint,
+ * src/cli/k3_run.c:1225-1231); 0 on success. */
+typedef int (*K3SpecCheckpointFn)(void *ctx, int cached);
 /* ids[0..n_ids): the conversation so far; cached: positions the model has consumed
  * (0 on a fresh run). NULL on a bad configuration. */
 K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *ids, int n_ids, int cached,
@@ -700,6 +708,13 @@ void k3_spec_loop_free(K3SpecLoop *L);
  * finished K3_SPEC_LOOP_GEN / _STOP_ID / _CONTEXT (this and every later call emit
  * nothing), or a negative status (K3GPU_ECALLBACK when a callback failed). */
 int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStepTrace *trace);
+/* The checkpoint callback for the prompt read-in, set before the first step. With it, the
+ * read-in pauses after cfg.pause_after checkpoints or at the first checkpoint after
+ * k3_spec_loop_request_pause (callable from any thread, the engine's SIGINT): the step then
+ * returns K3_SPEC_LOOP_PAUSED having emitted nothing, k3_spec_loop_state's cached is the
+ * positions read, and a new loop created with that `cached` continues the read-in. */
+int k3_spec_loop_set_checkpoint(K3SpecLoop *L, K3SpecCheckpointFn fn, void *ctx);
+void k3_spec_loop_request_pause(K3SpecLoop *L);
 /* The draft model for K3_DRAFT_MODEL, set before the first step; its callbacks have the
  * target's signatures (parent always NULL). It reads the conversation once at the first
  * step (verify then commit of every id); each later drafting step calls dverify once with

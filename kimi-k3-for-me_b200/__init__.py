@@ -102,13 +102,13 @@ class K3SpecCost(C.Structure):
 SPEC_P3_CODES = 234
 
 DRAFT_NONE, DRAFT_NGRAM, DRAFT_EAGER, DRAFT_SUFFIX, DRAFT_P3, DRAFT_TREE, DRAFT_MODEL = range(7)
-SPEC_LOOP_GEN, SPEC_LOOP_STOP_ID, SPEC_LOOP_CONTEXT = 1, 2, 3
+SPEC_LOOP_GEN, SPEC_LOOP_STOP_ID, SPEC_LOOP_CONTEXT, SPEC_LOOP_PAUSED = 1, 2, 3, 4
 
 
 class K3SpecLoopCfg(C.Structure):
     _fields_ = [("policy", I), ("spec_n", I), ("min_len", I), ("gen", I), ("tmax", I), ("kv_cap", I),
                 ("stop_ids", VP), ("n_stop", I), ("p3_q", VP), ("p3_delta", C.c_double), ("p3_cost", VP),
-                ("p3_replay", I), ("tree_nodes", I), ("tree_branch", I)]
+                ("p3_replay", I), ("tree_nodes", I), ("tree_branch", I), ("prefill_chunk", I), ("pause_after", I)]
 
 
 class K3SpecLoopStats(C.Structure):
@@ -124,6 +124,7 @@ class K3SpecStepTrace(C.Structure):
 SpecVerifyFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int, C.c_int,
                            C.POINTER(C.c_int))
 SpecCommitFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_int), C.c_int)
+SpecCheckpointFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int)
 
 
 ST_UNKNOWN, ST_U8, ST_BF16, ST_F16, ST_F32 = range(5)
@@ -217,6 +218,8 @@ _SIGS = {
     "k3_spec_loop_state": ([VP, VP, VP, VP, VP], I),
     "k3_spec_loop_ids": ([VP, VP, I], I),
     "k3_spec_loop_set_draft_model": ([VP, VP, VP, VP], I),
+    "k3_spec_loop_set_checkpoint": ([VP, VP, VP], I),
+    "k3_spec_loop_request_pause": ([VP], None),
     "k3_st_open": ([C.c_char_p], VP),
     "k3_st_open_files": ([VP, I], VP),
     "k3_st_close": ([VP], None),
@@ -766,7 +769,8 @@ class SpecLoop:
 
     def __init__(self, ids, verify, commit, *, cached=0, policy=DRAFT_NGRAM, spec_n=8, min_len=1, gen=64,
                  tmax=None, kv_cap=None, stop_ids=(), p3_q=None, p3_delta=0.22, p3_cost=None, p3_replay=False,
-                 tree_nodes=64, tree_branch=4, draft_verify=None, draft_commit=None):
+                 tree_nodes=64, tree_branch=4, draft_verify=None, draft_commit=None, prefill_chunk=0,
+                 pause_after=0, checkpoint=None):
         ids = [int(v) for v in ids]
         tmax = tmax if tmax is not None else len(ids) + gen + 1
         self._errors = []
@@ -825,7 +829,7 @@ class SpecLoop:
         cfg = K3SpecLoopCfg(policy, spec_n, min_len, gen, tmax, kv_cap if kv_cap is not None else tmax,
                             C.cast(self._stop, VP), len(stop_ids), C.cast(self._q, VP) if self._q else None,
                             float(p3_delta), C.cast(C.pointer(p3_cost), VP) if p3_cost is not None else None,
-                            int(bool(p3_replay)), tree_nodes, tree_branch)
+                            int(bool(p3_replay)), tree_nodes, tree_branch, prefill_chunk, pause_after)
         arr = (C.c_int * max(len(ids), 1))(*ids)
         self._L = lib.k3_spec_loop_create(C.byref(cfg), arr, len(ids), cached,
                                           C.cast(self._fns[0], VP), C.cast(self._fns[1], VP), None)
@@ -834,6 +838,16 @@ class SpecLoop:
         if draft_verify is not None:
             check(lib.k3_spec_loop_set_draft_model(self._L, C.cast(self._fns[2], VP), C.cast(self._fns[3], VP), None),
                   "k3_spec_loop_set_draft_model")
+        if checkpoint is not None:
+            def _ck(_ctx, cached):
+                try:
+                    checkpoint(cached)
+                    return 0
+                except Exception as e:  # noqa: BLE001
+                    self._errors.append(e)
+                    return 1
+            self._ckfn = SpecCheckpointFn(_ck)
+            check(lib.k3_spec_loop_set_checkpoint(self._L, C.cast(self._ckfn, VP), None), "k3_spec_loop_set_checkpoint")
         self.tmax = tmax
 
     def step(self):
@@ -848,6 +862,10 @@ class SpecLoop:
         if st > 0:
             return [], None
         return list(out[:n.value]), {"nd": tr.nd, "m": tr.m, "keep": tr.keep, "fed": tr.fed}
+
+    def request_pause(self):
+        """Pause the prompt read-in at its next checkpoint (the engine's SIGINT)."""
+        lib.k3_spec_loop_request_pause(self._L)
 
     def run(self):
         """Step until finished; returns (generated ids, per-step traces)."""

@@ -28,6 +28,9 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+#include <new>
+
 #include "k3gpu.h"
 
 struct K3SpecLoop {
@@ -46,6 +49,10 @@ struct K3SpecLoop {
     K3SpecCommitFn dcommit;
     void *dctx;
     int dcached;                // positions the draft model has consumed
+    K3SpecCheckpointFn ckpt;    // called at chunk boundaries of the prompt read-in
+    void *ckctx;
+    int ck_written;
+    std::atomic<int> pause_req;
     K3SpecLoopStats st;
 };
 
@@ -112,6 +119,32 @@ int append(K3SpecLoop *L, const int *emit, int keep, int *out)
     return K3GPU_OK;
 }
 
+// read seq[from..to) into a model in passes of at most `chunk` positions (0: one pass),
+// each a verify then a commit of the whole pass (k3_run.c:1189-1240); the last pass's next
+// id goes to *next. With ck, a checkpoint follows every pass that leaves positions to go,
+// and the read-in pauses (returns 1) once pause_after checkpoints are written or a pause
+// was requested. Returns 0 when done, 1 when paused, a negative status on failure.
+int read_in(K3SpecLoop *L, K3SpecVerifyFn verify, K3SpecCommitFn commit, void *ctx, int from, int to, int *done_to,
+            int *next, bool ck)
+{
+    const int chunk = L->cfg.prefill_chunk > 0 ? L->cfg.prefill_chunk : to - from;
+    int i = from;
+    while (i < to) {
+        const int q = to - i < chunk ? to - i : chunk;
+        if (verify(ctx, L->seq + i, nullptr, q, i, L->arg) != 0) return K3GPU_ECALLBACK;
+        if (commit(ctx, i, nullptr, q) != 0) return K3GPU_ECALLBACK;
+        i += q;
+        *done_to = i;
+        if (next) *next = L->arg[q - 1];
+        if (ck && L->ckpt && i < to) {
+            if (L->ckpt(L->ckctx, i) != 0) return K3GPU_ECALLBACK;
+            L->ck_written++;
+            if ((L->cfg.pause_after && L->ck_written >= L->cfg.pause_after) || L->pause_req.load()) return 1;
+        }
+    }
+    return 0;
+}
+
 }  // namespace
 
 extern "C" K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *ids, int n_ids, int cached,
@@ -125,7 +158,8 @@ extern "C" K3SpecLoop *k3_spec_loop_create(const K3SpecLoopCfg *cfg, const int *
     if (cfg->policy == K3_DRAFT_TREE && (cfg->tree_nodes < 1 || cfg->tree_nodes > 64 || cfg->tree_branch < 1))
         return nullptr;
     if (cfg->policy == K3_DRAFT_P3 && !cfg->p3_q) return nullptr;
-    K3SpecLoop *L = (K3SpecLoop *)calloc(1, sizeof(K3SpecLoop));
+    if (cfg->prefill_chunk < 0 || cfg->pause_after < 0) return nullptr;
+    K3SpecLoop *L = new (std::nothrow) K3SpecLoop();
     if (!L) return nullptr;
     L->cfg = *cfg;
     L->verify = verify;
@@ -165,7 +199,7 @@ extern "C" void k3_spec_loop_free(K3SpecLoop *L)
     free(L->tok);
     free(L->parent);
     k3_suffix_drafter_free(L->sam);
-    free(L);
+    delete L;
 }
 
 extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStepTrace *trace)
@@ -178,18 +212,27 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
     int emit[9], emitn = 0, keep = 0;
     const int base = L->cached;
     if (!L->started) {
-        // the first step: every position not yet consumed, never tentative in the engine
+        // the first step: every position not yet consumed, never tentative in the engine,
+        // in passes of at most prefill_chunk positions with checkpoints between them
         const int n = L->T - base;
-        if (L->verify(L->ctx, L->seq + base, nullptr, n, base, L->arg) != 0) return K3GPU_ECALLBACK;
-        if (L->commit(L->ctx, base, nullptr, n) != 0) return K3GPU_ECALLBACK;
-        L->cached = base + n;
+        int next = 0, upto = base;
+        const int r = read_in(L, L->verify, L->commit, L->ctx, base, L->T, &upto, &next, true);
+        L->cached = upto;
+        if (r < 0) return r;
+        if (r == 1) {                 // paused: positions base..upto read, nothing emitted
+            L->done = K3_SPEC_LOOP_PAUSED;
+            if (trace) *trace = K3SpecStepTrace{0, 0, 0, upto - base};
+            return L->done;
+        }
         L->started = 1;
-        emit[emitn++] = L->arg[n - 1];
+        emit[emitn++] = next;
         if (L->cfg.policy == K3_DRAFT_MODEL) {
-            // the draft model reads the whole conversation once (its state is never saved,
-            // so a resumed run replays everything through it, :2847-2853)
-            if (L->dverify(L->dctx, L->seq, nullptr, L->T, 0, L->arg) != 0) return K3GPU_ECALLBACK;
-            if (L->dcommit(L->dctx, 0, nullptr, L->T) != 0) return K3GPU_ECALLBACK;
+            // the draft model reads the whole conversation once, in the same passes (its
+            // state is never saved, so a resumed run replays everything through it,
+            // :2847-2853)
+            int dupto = 0;
+            const int rd = read_in(L, L->dverify, L->dcommit, L->dctx, 0, L->T, &dupto, nullptr, false);
+            if (rd < 0) return rd;
             L->dcached = L->T;
         }
         keep = emit_keep(L, emit, emitn);
@@ -290,6 +333,19 @@ extern "C" int k3_spec_loop_step(K3SpecLoop *L, int *out, int *n_out, K3SpecStep
     if (append(L, emit, keep, out) != K3GPU_OK) return K3GPU_EINVAL;
     if (n_out) *n_out = keep;
     return K3GPU_OK;
+}
+
+extern "C" int k3_spec_loop_set_checkpoint(K3SpecLoop *L, K3SpecCheckpointFn fn, void *ctx)
+{
+    if (!L || L->started) return K3GPU_EINVAL;
+    L->ckpt = fn;
+    L->ckctx = ctx;
+    return K3GPU_OK;
+}
+
+extern "C" void k3_spec_loop_request_pause(K3SpecLoop *L)
+{
+    if (L) L->pause_req.store(1);
 }
 
 extern "C" int k3_spec_loop_set_draft_model(K3SpecLoop *L, K3SpecVerifyFn dverify, K3SpecCommitFn dcommit,

@@ -298,3 +298,64 @@ def test_draft_model_that_never_agrees_and_a_missing_model(k3):
     with pytest.raises(k3.K3Error):
         loop.step()                                                      # no draft model set
     loop.close()
+
+
+def test_prompt_read_in_passes_checkpoints_and_pause(k3):
+    """--prefill-chunk / --checkpoint / --pause-after (src/cli/k3_run.c:1189-1240): the
+    prompt is read in passes of at most N positions, a checkpoint follows every pass that
+    leaves positions to go, and after pause_after checkpoints the step stops having
+    emitted nothing; a new loop created at the positions read continues, and the run as a
+    whole decodes exactly as serial decoding does."""
+    nid = make_model(51)
+    rng = np.random.default_rng(51)
+    prompt = rng.integers(0, 9, 34).tolist()
+    # passes of 7 with checkpoints at 7, 14, 21, 28 (not after the last pass)
+    m, marks = Fake(nid, []), []
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_SUFFIX, gen=30, prefill_chunk=7,
+                       checkpoint=marks.append)
+    out, traces = loop.run()
+    assert m.calls[:5] == [7, 7, 7, 7, 6] and marks == [7, 14, 21, 28]
+    assert traces[0]["fed"] == 34 and out == serial(nid, prompt, 30, len(prompt) + 31, ())
+    loop.close()
+    # pause after 2 checkpoints, then resume from position 14
+    m, marks = Fake(nid, []), []
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_SUFFIX, gen=30, prefill_chunk=7,
+                       pause_after=2, checkpoint=marks.append)
+    assert loop.step() == ([], None)
+    st = loop.state()
+    assert st["done"] == k3.SPEC_LOOP_PAUSED and st["cached"] == 14 and st["nout"] == 0 and marks == [7, 14]
+    assert m.state == prompt[:14]
+    loop.close()
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, cached=14, policy=k3.DRAFT_SUFFIX, gen=30, prefill_chunk=7)
+    out, traces = loop.run()
+    assert traces[0]["fed"] == 20 and out == serial(nid, prompt, 30, len(prompt) + 31, ())
+    loop.close()
+    # a pause requested before the read-in takes effect at the first checkpoint
+    m, marks = Fake(nid, []), []
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, prefill_chunk=10, checkpoint=marks.append)
+    loop.request_pause()
+    loop.step()
+    assert loop.state()["done"] == k3.SPEC_LOOP_PAUSED and loop.state()["cached"] == 10 and marks == [10]
+    loop.close()
+    # without a checkpoint callback pause_after has nothing to pause on: the read-in completes
+    m = Fake(nid, [])
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, gen=5, prefill_chunk=10, pause_after=1)
+    out, _ = loop.run()
+    assert out == serial(nid, prompt, 5, len(prompt) + 6, ())
+    loop.close()
+
+
+def test_draft_model_reads_the_prompt_in_the_same_passes(k3):
+    nid = make_model(52)
+    prompt = np.random.default_rng(52).integers(0, 9, 30).tolist()
+    m, dm = Fake(nid, []), FakeDraft(make_model(52, noise=3))
+    calls = []
+
+    def dverify(ids, base, parent=None):
+        calls.append(len(ids))
+        return dm.verify(ids, base, parent)
+    loop = k3.SpecLoop(prompt, m.verify, m.commit, policy=k3.DRAFT_MODEL, gen=40, prefill_chunk=8,
+                       draft_verify=dverify, draft_commit=dm.commit)
+    out, _ = loop.run()
+    assert calls[:4] == [8, 8, 8, 6] and out == serial(nid, prompt, 40, len(prompt) + 41, ())
+    loop.close()
