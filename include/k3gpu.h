@@ -727,6 +727,20 @@ int k3_spec_loop_state(const K3SpecLoop *L, int *T, int *cached, int *nout, K3Sp
 /* The conversation's ids (ids[0..T), cap >= T); returns T. */
 int k3_spec_loop_ids(const K3SpecLoop *L, int *ids, int cap);
 
+/* The layer loop's execution order (the engine's --loop / --loop-layers A-B /
+ * --loop-count R, src/cli/k3_run.c:2140-2182): layers 0..B, then R - 1 repeats of A..B,
+ * then B+1..n_layers-1. vmap[v] is the physical layer executed at position v; each
+ * executed position owns its own KDA state and MLA cache slot (slot v), as a duplicated
+ * layer would, so a K3ST file's loop record holds nv = the count returned. The span must
+ * be whole AttnRes blocks (A a multiple of the block, B + 1 one too or B the last layer);
+ * preset != 0 takes the block holding the middle layer (--loop) and ignores A, B.
+ * span_out [2] (optional) receives A, B; attn_res_extra (optional) the block-residual
+ * stride's growth, (R - 1) * ceil(span / block). Returns the executed layer count, or
+ * K3GPU_EINVAL / K3GPU_ECAPACITY (vmap_cap short). Adaptive exit (--loop-exit) is not
+ * planned here. */
+int k3_layer_loop_plan(int n_layers, int attn_res_block, int preset, int loop_a, int loop_b, int loop_count,
+                       int *vmap, int vmap_cap, int *span_out, int *attn_res_extra);
+
 /* A draft TREE for tree verification (no counterpart in the reference, whose drafts are
  * chains): node 0 is the pending id; a node's children are the ids that followed its
  * context in the history, most frequent first (at most `branch`), the context backing off

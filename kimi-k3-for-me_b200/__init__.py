@@ -220,6 +220,7 @@ _SIGS = {
     "k3_spec_loop_set_draft_model": ([VP, VP, VP, VP], I),
     "k3_spec_loop_set_checkpoint": ([VP, VP, VP], I),
     "k3_spec_loop_request_pause": ([VP], None),
+    "k3_layer_loop_plan": ([I, I, I, I, I, I, VP, I, VP, VP], I),
     "k3_st_open": ([C.c_char_p], VP),
     "k3_st_open_files": ([VP, I], VP),
     "k3_st_close": ([VP], None),
@@ -758,6 +759,20 @@ class SuffixDrafter:
             self.close()
         except Exception:  # noqa: BLE001 -- interpreter shutdown may have unloaded the library
             pass
+
+
+def layer_loop_plan(n_layers, attn_res_block, loop_count, span=None, preset=False):
+    """(vmap, (A, B), attn_res_extra) of the layer loop (k3_layer_loop_plan): the physical
+    layer executed at each position, each position owning its own state slot."""
+    a, b = span if span is not None else (0, 0)
+    cap = n_layers * max(loop_count, 1)
+    vmap = (C.c_int * cap)()
+    sp = (C.c_int * 2)()
+    extra = C.c_int(0)
+    nv = lib.k3_layer_loop_plan(n_layers, attn_res_block, int(bool(preset)), a, b, loop_count, vmap, cap, sp,
+                                C.byref(extra))
+    check(nv if nv < 0 else 0, "k3_layer_loop_plan")
+    return list(vmap[:nv]), (sp[0], sp[1]), extra.value
 
 
 class SpecLoop:

@@ -374,3 +374,34 @@ extern "C" int k3_spec_loop_ids(const K3SpecLoop *L, int *ids, int cap)
     memcpy(ids, L->seq, sizeof(int) * (size_t)L->T);
     return L->T;
 }
+
+// ---- the layer loop's execution order (--loop / --loop-layers / --loop-count) --------
+extern "C" int k3_layer_loop_plan(int n_layers, int attn_res_block, int preset, int loop_a, int loop_b,
+                                  int loop_count, int *vmap, int vmap_cap, int *span_out, int *attn_res_extra)
+{
+    if (n_layers <= 0 || attn_res_block <= 0 || loop_count < 1 || loop_count > 8 || !vmap) return K3GPU_EINVAL;
+    const int NL = n_layers, blk = attn_res_block;
+    if (preset) {   // the whole block holding the middle layer (k3_run.c:2148-2152)
+        const int mid = NL / 2;
+        loop_a = mid - mid % blk;
+        loop_b = loop_a + blk - 1 < NL - 1 ? loop_a + blk - 1 : NL - 1;
+    }
+    // whole AttnRes blocks within the stack, so every executed layer keeps its position in
+    // its block and the block-boundary snapshots stay where they were trained (:2153-2160)
+    if (loop_a < 0 || loop_b < loop_a || loop_b >= NL || loop_a % blk != 0 ||
+        ((loop_b + 1) % blk != 0 && loop_b != NL - 1))
+        return K3GPU_EINVAL;
+    const int span = loop_b - loop_a + 1, NV = NL + (loop_count - 1) * span;
+    if (vmap_cap < NV) return K3GPU_ECAPACITY;
+    int nv = 0;
+    for (int L = 0; L <= loop_b; L++) vmap[nv++] = L;
+    for (int r = 1; r < loop_count; r++)
+        for (int L = loop_a; L <= loop_b; L++) vmap[nv++] = L;
+    for (int L = loop_b + 1; L < NL; L++) vmap[nv++] = L;
+    if (span_out) {
+        span_out[0] = loop_a;
+        span_out[1] = loop_b;
+    }
+    if (attn_res_extra) *attn_res_extra = (loop_count - 1) * ((span + blk - 1) / blk);
+    return NV;
+}

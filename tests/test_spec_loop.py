@@ -359,3 +359,24 @@ def test_draft_model_reads_the_prompt_in_the_same_passes(k3):
     out, _ = loop.run()
     assert calls[:4] == [8, 8, 8, 6] and out == serial(nid, prompt, 40, len(prompt) + 41, ())
     loop.close()
+
+
+def test_layer_loop_plan(k3):
+    """The --loop / --loop-layers / --loop-count execution order (src/cli/k3_run.c:
+    2140-2182): whole AttnRes blocks only, the middle block as the preset, each executed
+    position its own slot, the stride growth (R - 1) * ceil(span / block)."""
+    vmap, span, extra = k3.layer_loop_plan(12, 3, 2, span=(3, 5))
+    assert vmap == [0, 1, 2, 3, 4, 5, 3, 4, 5, 6, 7, 8, 9, 10, 11] and span == (3, 5) and extra == 1
+    vmap, span, extra = k3.layer_loop_plan(12, 3, 3, span=(3, 8))
+    assert vmap == list(range(9)) + list(range(3, 9)) * 2 + [9, 10, 11] and extra == 4
+    vmap, span, extra = k3.layer_loop_plan(93, 4, 2, preset=True)       # K3: the block holding layer 46
+    assert span == (44, 47) and len(vmap) == 97 and vmap[48:52] == [44, 45, 46, 47] and extra == 1
+    vmap, span, _ = k3.layer_loop_plan(13, 3, 2, span=(12, 12))        # a last, partial block
+    assert vmap == list(range(13)) + [12]
+    for bad in ((4, 5), (3, 4), (2, 5), (3, 12)):                      # cut blocks, past the stack
+        with pytest.raises(k3.K3Error):
+            k3.layer_loop_plan(12, 3, 2, span=bad)
+    with pytest.raises(k3.K3Error):
+        k3.layer_loop_plan(12, 3, 9, span=(3, 5))                      # at most 8 passes
+    vmap, _, extra = k3.layer_loop_plan(12, 3, 1, span=(3, 5))          # one pass: the plain stack
+    assert vmap == list(range(12)) and extra == 0
