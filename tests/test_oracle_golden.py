@@ -213,6 +213,83 @@ def test_mla_tree_mask_equals_chain_on_a_chain():
     np.testing.assert_array_equal(a[:2], c[:2])
 
 
+def _random_tree(rng, T):
+    return [-1] + [int(rng.integers(0, i)) for i in range(1, T)]
+
+
+def test_mla_tree_node_equals_its_ancestor_chain():
+    """What a tree mask means: node i's output equals a plain causal run over just the
+    path root .. i (its ancestors' rows, in order), for every node of random trees."""
+    rng = np.random.default_rng(8)
+    H, qn, qr, vh, kvl, cached = 3, 16, 8, 16, 32, 9
+    for T in (6, 17, 40):
+        parent = _random_tree(rng, T)
+        qn_ = rng.standard_normal((T, H, qn), dtype=np.float32)
+        qr_ = rng.standard_normal((T, H, qr), dtype=np.float32)
+        kvb = rng.standard_normal((H * (qn + vh), kvl), dtype=np.float32) * np.float32(0.2)
+        lat = rng.standard_normal((cached + T, kvl), dtype=np.float32)
+        rope = rng.standard_normal((cached + T, qr), dtype=np.float32)
+        tree = O.mla_absorbed(qn_, qr_, kvb, lat, rope, cached, O.tree_masks(parent), 0.2, vh)
+        for i in range(T):
+            path, j = [], i
+            while j >= 0:
+                path.append(j)
+                j = parent[j]
+            path = path[::-1]
+            n = len(path)
+            lat_c = np.concatenate([lat[:cached], lat[cached + np.array(path)]])
+            rope_c = np.concatenate([rope[:cached], rope[cached + np.array(path)]])
+            chain = O.mla_absorbed(qn_[path], qr_[path], kvb, lat_c, rope_c, cached, O.chain_masks(n), 0.2, vh)
+            np.testing.assert_allclose(tree[i], chain[n - 1], rtol=1e-6, atol=1e-6)
+
+
+def _greedy_walk(lg, tok, parent):
+    """The definition of greedy tree acceptance: from the root, emit the current node's
+    argmax (first index of the maximum); move to the lowest-index child carrying it."""
+    node, emit, path = 0, [], [0]
+    while True:
+        a = int(np.argmax(lg[node]))
+        emit.append(a)
+        kids = [c for c in range(len(parent)) if parent[c] == node and tok[c] == a]
+        if not kids:
+            return emit, path
+        node = kids[0]
+        path.append(node)
+
+
+def test_tree_accept_is_the_greedy_walk_and_a_chain_on_a_chain():
+    rng = np.random.default_rng(9)
+    V = 7
+    for T in (1, 5, 23, 64):
+        for trial in range(20):
+            parent = _random_tree(rng, T)
+            tok = rng.integers(0, V, T).astype(np.int32)
+            lg = rng.standard_normal((T, V), dtype=np.float32)
+            # steer some nodes' argmax onto one of their children so paths get deep
+            for c in range(1, T):
+                if rng.random() < 0.6:
+                    lg[parent[c], tok[c]] = 5.0 + rng.random()
+            emit = np.zeros(T, np.int32)
+            path = np.zeros(T, np.int32)
+            n = O.orc().orc_accept_tree_greedy(emit, path, np.ascontiguousarray(lg), tok,
+                                               np.asarray(parent, np.int32), T, V)
+            want_emit, want_path = _greedy_walk(lg, tok, parent)
+            assert emit[:n].tolist() == want_emit and path[:len(want_path)].tolist() == want_path
+    # a chain-shaped tree accepts exactly as the chain rule does
+    nd = 6
+    d = rng.integers(0, V, nd).astype(np.int32)
+    for m_want in range(nd + 1):
+        lg = rng.standard_normal((nd + 1, V), dtype=np.float32)
+        for i in range(nd + 1):
+            lg[i, d[i] if i < m_want else ((d[i] + 1) % V if i < nd else 3)] = 10.0
+        e1, e2 = np.zeros(nd + 1, np.int32), np.zeros(nd + 1, np.int32)
+        arg, acc, path = np.zeros(nd + 1, np.int32), O.C.c_int(0), np.zeros(nd + 1, np.int32)
+        n1 = O.orc().orc_accept_greedy(e1, O.C.byref(acc), arg, lg, d, nd, V)
+        tok = np.concatenate([[0], d]).astype(np.int32)
+        n2 = O.orc().orc_accept_tree_greedy(e2, path, lg, tok, np.arange(-1, nd, dtype=np.int32), nd + 1, V)
+        assert n1 == n2 == m_want + 1 and e1[:n1].tolist() == e2[:n2].tolist()
+
+
 # ---------------------------------------------------------------------------- MoE --
 def test_latent_moe_composition_vs_reference_k3_moe():
     """orc_moe_routed inside the LatentMoE of the reference's k3_moe
