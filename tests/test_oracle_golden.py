@@ -290,6 +290,49 @@ def test_tree_accept_is_the_greedy_walk_and_a_chain_on_a_chain():
         assert n1 == n2 == m_want + 1 and e1[:n1].tolist() == e2[:n2].tolist()
 
 
+def _mxfp4_decode(packed, scales, rows, cols):
+    """Independent numpy decode of MXFP4: E2M1 magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6}
+    with sign bit 8, low nibble the even element, times 2^(S - 127) per 32 columns."""
+    mag = np.array([0, .5, 1, 1.5, 2, 3, 4, 6], np.float64)
+    p = packed.reshape(rows, cols // 2)
+    nib = np.empty((rows, cols), np.uint8)
+    nib[:, 0::2], nib[:, 1::2] = p & 0xF, p >> 4
+    v = mag[nib & 7] * np.where(nib & 8, -1.0, 1.0)
+    sc = np.exp2(scales.reshape(rows, cols // 32).astype(np.float64) - 127.0)
+    return v * np.repeat(sc, 32, axis=1)
+
+
+def test_swiglu_experts_against_an_independent_restatement():
+    """The SwiGLU experts the benchmark configurations use (no reference implementation;
+    the reference's experts are SiTU-GLU): the checker's expert stream equals a float64
+    numpy restatement -- decode each expert, gate and up from w1 and w3, silu(gate) * up,
+    down through w2, routed contributions weighted in top-k order, shared ones added."""
+    rng = np.random.default_rng(12)
+    L, I, n, ns, k, T = 64, 96, 6, 1, 2, 5
+    bank, lay = O.make_bank(rng, n + ns, L, I, std=0.05, w13_std=0.3)
+    z = rng.standard_normal((T, L), dtype=np.float32)
+    W = rng.standard_normal((n, L), dtype=np.float32) * np.float32(0.05)
+    idx, wt = O.router(z, W, np.zeros(n, np.float32), k)
+    got = O.moe_routed(z, idx, wt, bank, lay, L, I, k, n, ns, 1)
+    stride = int(lay[6])
+
+    def expert(e, x):
+        run = bank[e * stride:(e + 1) * stride]
+        w1 = _mxfp4_decode(run[lay[0]:lay[0] + I * L // 2], run[lay[1]:lay[1] + I * L // 32], I, L)
+        w2 = _mxfp4_decode(run[lay[2]:lay[2] + L * I // 2], run[lay[3]:lay[3] + L * I // 32], L, I)
+        w3 = _mxfp4_decode(run[lay[4]:lay[4] + I * L // 2], run[lay[5]:lay[5] + I * L // 32], I, L)
+        g, u = w1 @ x, w3 @ x
+        return w2 @ (g / (1.0 + np.exp(-g)) * u)
+    want = np.zeros((T, L))
+    for t in range(T):
+        x = z[t].astype(np.float64)
+        for j in range(k):
+            want[t] += float(wt[t, j]) * expert(int(idx[t, j]), x)
+        for s_ in range(ns):
+            want[t] += expert(n + s_, x)
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 1e-5
+
+
 # ---------------------------------------------------------------------------- MoE --
 def test_latent_moe_composition_vs_reference_k3_moe():
     """orc_moe_routed inside the LatentMoE of the reference's k3_moe
