@@ -207,6 +207,30 @@ def cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nthreads
     return dt, out, idx
 
 
+def kda_prefill_cpu_baseline(T_sample=256, H=32, D=128, seed=5):
+    """The reference reads a prompt with k3_kda_step, one position after another for every
+    head (src/core/k3_ops.c:303-360): that chain over a bounded sample on one host thread
+    (the reference's library is built here without OpenMP), as positions per second; None
+    when the reference library was not built."""
+    from oracle import oracle as O
+    lib = O.ref()
+    if lib is None:
+        return None
+    rng = np.random.default_rng(seed)
+    S = rng.standard_normal((H, D, D)).astype(np.float32) * np.float32(0.1)
+    q, k, v = (rng.standard_normal((T_sample, H, D)).astype(np.float32) for _ in range(3))
+    al = rng.uniform(0.9, 0.999, (T_sample, H, D)).astype(np.float32)
+    be = rng.uniform(0.1, 0.9, (T_sample, H)).astype(np.float32)
+    o = np.zeros(D, np.float32)
+    t0 = time.perf_counter()
+    for t in range(T_sample):
+        for h in range(H):
+            lib.k3_kda_step(S[h], o, q[t, h], k[t, h], v[t, h], al[t, h], float(be[t, h]), D, D)
+    dt = time.perf_counter() - t0
+    return {"value": round(T_sample / dt, 1), "unit": "positions/s", "cores": 1, "kind": "reference",
+            "sample": f"{T_sample} positions x {H} heads x {D}: k3_kda_step chained, one thread"}
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -487,6 +511,10 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
             row = hbm_row(us, nbytes, "B=1 T=4096 H=32 D=128 (one prompt)")
             row.update({"positions_per_s": round(B * T / (us * 1e-6), 1), "sequential_us": round(us_seq, 2),
                         "speedup_vs_sequential": round(us_seq / us, 2), "compute": "fp32 CUDA cores"})
+            try:
+                row["cpu_baseline"] = kda_prefill_cpu_baseline(H=H, D=D)
+            except Exception as ex:  # noqa: BLE001 -- the baseline must not cost the row
+                row["cpu_baseline"] = {"error": str(ex)[:120]}
             rows["kda_prefill_4k"] = row
         except Exception as ex:  # noqa: BLE001
             rows["kda_prefill"] = {"error": str(ex)[:200]}

@@ -42,3 +42,17 @@ def test_unique_expert_bytes():
     idx = np.array([[3, 7], [7, 1], [3, 3]], np.int32)
     u, nbytes = b.unique_experts_bytes(idx, 1000)
     assert u == 3 and nbytes == 3000
+
+
+def test_kda_prefill_cpu_baseline_runs_the_reference_step():
+    """The prefill row's CPU baseline times the reference's own k3_kda_step (needs the
+    reference library built under oracle/_ref; skipped where it is not)."""
+    import pytest
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    if O.ref() is None:
+        pytest.skip("oracle/_ref not built")
+    b = _bench()
+    r = b.kda_prefill_cpu_baseline(T_sample=16, H=4, D=128)
+    assert r["unit"] == "positions/s" and r["kind"] == "reference" and r["value"] > 0 and r["cores"] == 1
