@@ -231,6 +231,27 @@ def kda_prefill_cpu_baseline(T_sample=256, H=32, D=128, seed=5):
             "sample": f"{T_sample} positions x {H} heads x {D}: k3_kda_step chained, one thread"}
 
 
+def matmul_bf16_cpu_baseline(T, n_in, n_out, rows=256, seed=6):
+    """The reference's bf16 projection (k3_matmul_bf16_batch_ld, include/k3/k3.h:454) on one
+    host thread over a sample of `rows` output rows, scaled by rows to the full n_out (the
+    cost is linear in them): microseconds for the whole call; None when the reference
+    library was not built."""
+    from oracle import oracle as O
+    lib = O.ref()
+    if lib is None:
+        return None
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((T, n_in)).astype(np.float32)
+    W = ((rng.standard_normal((rows, n_in)).astype(np.float32) * np.float32(0.02)).view(np.uint32) >> 16) \
+        .astype(np.uint16)
+    Y = np.zeros((T, rows), np.float32)
+    t0 = time.perf_counter()
+    lib.k3_matmul_bf16_batch_ld(Y, rows, X, n_in, W.ctypes.data, n_in, rows, T)
+    dt = time.perf_counter() - t0
+    return {"value": round(dt * 1e6 * n_out / rows, 1), "unit": "us per call", "cores": 1, "kind": "reference",
+            "sample": f"{rows} of {n_out} output rows at T={T}, in={n_in}, scaled by rows; one thread"}
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -565,6 +586,10 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
             ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
             us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
             rows["trunk_matmul_bf16"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 7168")
+            try:
+                rows["trunk_matmul_bf16"]["cpu_baseline"] = matmul_bf16_cpu_baseline(T, n_in, n_out)
+            except Exception as ex:  # noqa: BLE001 -- the baseline must not cost the row
+                rows["trunk_matmul_bf16"]["cpu_baseline"] = {"error": str(ex)[:120]}
         except Exception as ex:  # noqa: BLE001
             rows["trunk_matmul_bf16"] = {"error": str(ex)[:200]}
 
@@ -578,6 +603,10 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
             ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
             us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
             rows["lm_head_bf16_c4"] = hbm_row(us, n_out * n_in * 2 + T * (n_in + n_out) * 4, "T=72, 7168 -> 163840")
+            try:
+                rows["lm_head_bf16_c4"]["cpu_baseline"] = matmul_bf16_cpu_baseline(T, n_in, n_out)
+            except Exception as ex:  # noqa: BLE001
+                rows["lm_head_bf16_c4"]["cpu_baseline"] = {"error": str(ex)[:120]}
             del W, Y
         except Exception as ex:  # noqa: BLE001
             rows["lm_head_bf16_c4"] = {"error": str(ex)[:200]}

@@ -56,3 +56,14 @@ def test_kda_prefill_cpu_baseline_runs_the_reference_step():
     b = _bench()
     r = b.kda_prefill_cpu_baseline(T_sample=16, H=4, D=128)
     assert r["unit"] == "positions/s" and r["kind"] == "reference" and r["value"] > 0 and r["cores"] == 1
+
+
+def test_matmul_cpu_baseline_runs_the_reference_projection():
+    import pytest
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    if O.ref() is None:
+        pytest.skip("oracle/_ref not built")
+    r = _bench().matmul_bf16_cpu_baseline(8, 256, 4096, rows=32)
+    assert r["unit"] == "us per call" and r["kind"] == "reference" and r["value"] > 0
