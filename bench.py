@@ -497,6 +497,13 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
             us = timed(lambda: k3.kda_verify(st, q, kk, v, al, be, qs))
             nbytes = st.numel() * 4 + 4 * q.numel() * 4 + be.numel() * 4 + q.numel() * 4
             rows["kda_verify_c3"] = hbm_row(us, nbytes, "B=8 T=9 H=32 D=128")
+            try:   # the reference's k3_kda_step chain over the same 72 positions x 32 heads
+                cb = kda_prefill_cpu_baseline(T_sample=B * T, H=H, D=D)
+                if cb is not None:
+                    cb = dict(cb, value=round(B * T / cb["value"] * 1e6, 1), unit="us per call")
+                rows["kda_verify_c3"]["cpu_baseline"] = cb
+            except Exception as ex:  # noqa: BLE001 -- the baseline must not cost the row
+                rows["kda_verify_c3"]["cpu_baseline"] = {"error": str(ex)[:120]}
             n = torch.full((B,), 5, dtype=torch.int32, device=dev)
             sc = st.clone()
             us = timed(lambda: k3.kda_commit(sc, kk, v, al, be, n))
