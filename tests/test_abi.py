@@ -83,3 +83,17 @@ def test_host_drafter_matches_oracle(seed):
         out = np.zeros(cap, np.int32)
         nd = O.orc().orc_spec_draft(np.asarray(seq, np.int32), len(seq), cap, nmax, nmin, out)
         assert m.spec_draft(seq, cap, nmax, nmin) == out[:nd].tolist()
+
+
+def test_ep_arena_holds_every_region():
+    """The expert-parallel exchange arena (k3gpu_ep_arena_bytes), host arithmetic only: a
+    4 KiB header, then per source rank `cap` received rows [L] fp32, their expert ids and
+    weights [K], and the returned partial rows [L] fp32, each region 256-byte aligned;
+    refused sizes give 0."""
+    m = k3lib.load()
+    a256 = lambda n: (n + 255) // 256 * 256   # noqa: E731
+    for world, cap, L, K in ((2, 64, 7168, 8), (8, 72, 7168, 8), (1, 1, 32, 1), (3, 17, 100, 3)):
+        want = 4096 + 2 * a256(world * cap * L * 4) + 2 * a256(world * cap * K * 4)
+        assert m.lib.k3gpu_ep_arena_bytes(world, cap, L, K) == want
+    assert m.lib.k3gpu_ep_arena_bytes(9, 64, 7168, 8) == 0          # above K3GPU_EP_MAX_WORLD
+    assert m.lib.k3gpu_ep_arena_bytes(2, 0, 7168, 8) == 0
