@@ -586,3 +586,44 @@ def kda_chunked(state, q, k, v, alpha, beta, qscale, chunk=64):
             o[c0:c1, h] = (Q * np.exp(g)) @ S[h] + Aqk @ W
             S[h] = np.exp(g[-1])[:, None] * S[h] + (K * np.exp(g[-1][None, :] - g)).T @ W
     return o.astype(np.float32), S.astype(np.float32)
+
+
+def kda_chunked_factored_f32(state, q, k, v, alpha, beta, qscale, chunk=32, max_range=100.0):
+    """The chunked KDA recurrence as a tensor-core kernel would compute it, in float32: the
+    decay ratios 2^(g_t - g_s) factored about the chunk's middle position m,
+    2^(g_t - g_m) * 2^(g_m - g_s), so the pair sums A = (K 2^(g - g_m)) (K 2^(g_m - g))^T and
+    Aq = (Q 2^(g - g_m)) (K 2^(g_m - g))^T become plain products -- valid while no factor
+    leaves float range, i.e. while the chunk's total log2 decay per channel stays within
+    max_range; a chunk beyond it takes the exact per-pair form. Same algebra as
+    kda_chunked otherwise. Returns (o [T][H][D], state [H][D][D]) float32."""
+    T, H, D = q.shape
+    f = np.float32
+    S = np.asarray(state, f).reshape(H, D, D).copy()
+    o = np.zeros((T, H, D), f)
+    for h in range(H):
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            n = c1 - c0
+            Q = np.asarray(q[c0:c1, h], f) * f(qscale)
+            K = np.asarray(k[c0:c1, h], f)
+            V = np.asarray(v[c0:c1, h], f)
+            B = np.asarray(beta[c0:c1, h], f)
+            g = np.cumsum(np.log2(np.maximum(np.asarray(alpha[c0:c1, h], f), f(1.1754944e-38))), axis=0,
+                          dtype=f)
+            lower = np.tril(np.ones((n, n), bool))
+            if float(np.max(g[0] - g[-1])) <= max_range:
+                gm = g[n // 2]
+                Ka, Kb = K * np.exp2(g - gm), K * np.exp2(gm - g)
+                Akk = np.tril(Ka @ Kb.T, -1) * B[:, None]
+                Aqk = np.where(lower, (Q * np.exp2(g - gm)) @ Kb.T, f(0))
+            else:                                   # the exact per-pair form
+                R = np.exp2(np.where(lower[:, :, None], g[:, None, :] - g[None, :, :], -np.inf)).astype(f)
+                Akk = np.tril(np.einsum("si,ti,tsi->ts", K, K, R), -1) * B[:, None]
+                Aqk = np.einsum("si,ti,tsi->ts", K, Q, R)
+            rhs = B[:, None] * (V - (K * np.exp2(g)) @ S[h])
+            W = np.zeros((n, D), f)
+            for t in range(n):
+                W[t] = rhs[t] - Akk[t, :t] @ W[:t]
+            o[c0:c1, h] = (Q * np.exp2(g)) @ S[h] + Aqk @ W
+            S[h] = np.exp2(g[-1])[:, None] * S[h] + (K * np.exp2(g[-1][None, :] - g)).T @ W
+    return o, S

@@ -62,3 +62,19 @@ def test_full_decay_zero_alpha_is_finite():
     assert np.isfinite(o_ch).all() and np.isfinite(s_ch).all()
     assert rel(o_ch, O.kda_verify(st, q, k, v, al, be, np.float32(0.25))) < 1e-5
     assert rel(s_ch, O.kda_commit(st, k, v, al, be, 20)) < 1e-5
+
+
+@pytest.mark.parametrize("T,H,D,decay", [
+    (128, 2, 128, (0.9, 0.999)), (128, 2, 128, (0.3, 0.7)), (128, 2, 128, (0.05, 0.3)),
+    (96, 2, 64, (0.995, 1.0)), (64, 2, 128, (0.001, 0.01)), (50, 1, 32, (0.5, 0.99)),
+])
+def test_factored_float32_form_equals_sequential(T, H, D, decay):
+    """The form a tensor-core prefill computes -- float32, decay ratios factored about the
+    chunk's middle so the pair sums are plain products, the exact per-pair form where the
+    chunk's decay range passes 100 (log2) -- stays within rel-L2 1e-5 of the sequential
+    recurrence; the strongest decay here (range ~260) takes the fallback."""
+    st, q, k, v, al, be = inputs(T * 3 + D, T, H, D, decay)
+    qs = np.float32(1.0) / np.sqrt(np.float32(D))
+    o_f, s_f = O.kda_chunked_factored_f32(st, q, k, v, al, be, qs, 32)
+    assert rel(o_f, O.kda_verify(st, q, k, v, al, be, qs)) < 1e-5
+    assert rel(s_f, O.kda_commit(st, k, v, al, be, T)) < 1e-5
