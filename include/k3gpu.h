@@ -315,6 +315,10 @@ int k3gpu_accept_greedy(int *emit, int *n_emit, int *arg, const float *logits,
                         const int *drafts, const int *nd_b, int B, int nd, int vocab,
                         void *stream);
 
+/* argmax_ (src/cli/k3_run.c:138-139) per row: arg [rows] = first index of the maximum of
+ * logits [rows][vocab] over non-NaN values (0 when logits[row][0] is NaN). */
+int k3gpu_argmax(int *arg, const float *logits, int rows, int vocab, void *stream);
+
 /* Greedy acceptance over a draft TREE of T nodes (node 0 = the pending token, parent[0]
  * = -1, parent[i] < i; tok[i] the drafted id of node i, tok[0] unused). A child i is
  * accepted when its parent is accepted and tok[i] == argmax of the parent's logits;
@@ -516,6 +520,81 @@ int k3gpu_decoder_layer_mla_verify(float *h, float *block_residual, int *n_block
                                    uint16_t *rope, int cap, const int *cached,
                                    const uint64_t *mask, int max_ctx, int B, int T,
                                    void *workspace, size_t ws_bytes, void *stream);
+
+/* ------------------------------------------------------ model verify forward ---- */
+/* The reference's forward() with arg_all (src/cli/k3_run.c:853-1138) for a whole model of
+ * KDA + MoE and MLA + MoE decoder layers, over B sequences at once, and the commit behind
+ * a speculative sweep (spec_commit :1270-1300 with `cached += keep` :2941-2943).
+ * A sweep of T <= max_T positions per sequence: embed rows (bf16 -> fp32), every layer in
+ * order (k3gpu_decoder_layer_kda_verify / _mla_verify: KDA tentative and logged, MLA
+ * appending its rows at cached[b] + t), the model-level AttnRes over the block snapshots
+ * (:1071-1087), the final RMSNorm, the lm_head over every position and the per-position
+ * argmax (argmax_, :138-139). The commit replays the first keep[b] logged positions into
+ * each KDA layer's state (k3_kda_advance) and advances cached[b]; the MLA rows past it
+ * are overwritten by the next sweep, as in the reference. With a draft tree (parents
+ * given) the accepted path's log and cache rows are first gathered to the front; the
+ * KDA recurrence runs chains only, so a tree needs a model of MLA layers only.
+ * Device memory: one caller-owned arena of k3gpu_model_arena_bytes (every KDA layer's
+ * state, history and log, every MLA layer's bf16 latent and rope caches of kv_cap
+ * positions, the sweep's activations, snapshots, logits [B*max_T][vocab] and the largest
+ * layer workspace); the host object holds pointers, a small pinned staging ring and the
+ * host copy of cached. Not for concurrent calls on one model. */
+typedef struct {
+    K3GpuLayerCfg layer;     /* every layer's configuration (max_blocks: the reference's
+                                k3_attn_res_stride, n_layers / attn_res_block + 2)        */
+    int n_layers, vocab;
+    const int *is_mla;       /* host [n_layers]: 1 for an MLA layer (one-based
+                                full_attn_layers of the config, src/core/k3_ops.c:119-127) */
+} K3GpuModelCfg;
+
+typedef struct {
+    const uint16_t *embed;           /* bf16 [vocab][E]                                    */
+    const uint16_t *lm_head;         /* bf16 [vocab][E]                                    */
+    const float *norm;               /* [E], the final RMSNorm                             */
+    const float *out_res_fold;       /* [E] or NULL: the model-level AttnRes fold           */
+    const K3GpuKdaLayerW *kda;       /* host [n_layers]: the entries of the KDA layers      */
+    const K3GpuMlaLayerW *mla;       /* host [n_layers]: the entries of the MLA layers      */
+} K3GpuModelW;
+
+typedef struct K3GpuModel K3GpuModel;
+
+/* 0 for a configuration the layers refuse, B outside 1..4096, max_T outside 1..64 or
+ * kv_cap < max_T. */
+size_t k3gpu_model_arena_bytes(const K3GpuModelCfg *c, int B, int max_T, int kv_cap);
+/* The weight structures are copied (their device pointers must stay valid); the arena
+ * (256-byte aligned) is laid out and the states zeroed on `stream`. NULL on a bad
+ * argument or a failed host allocation. */
+K3GpuModel *k3gpu_model_create(const K3GpuModelCfg *c, const K3GpuModelW *w, int B, int max_T, int kv_cap,
+                               void *arena, size_t arena_bytes, void *stream);
+void k3gpu_model_free(K3GpuModel *m);
+int k3gpu_model_set_stream(K3GpuModel *m, void *stream);
+/* zero every KDA state and history, cached = 0 (the caches need no clearing) */
+int k3gpu_model_reset(K3GpuModel *m);
+/* ids: DEVICE [B][T]; parent: HOST [T] or NULL (a chain), one tree shape for every
+ * sequence; arg: DEVICE [B][T] or NULL; *logits (optional) receives the model's logits
+ * buffer [B][T][vocab], valid until the next sweep. K3GPU_ECAPACITY when a sequence's
+ * cached + T passes kv_cap. */
+int k3gpu_model_verify(K3GpuModel *m, const int *ids, int T, const int *parent, int *arg,
+                       const float **logits);
+/* keep: HOST [B], 0..T of the last verify; path: HOST [B][T] (a tree sweep only): the
+ * accepted nodes root first along the parents. */
+int k3gpu_model_commit(K3GpuModel *m, const int *keep, const int *path);
+/* the chain commit with the counts already on the device (e.g. n_emit of an on-device
+ * accept); keep_host [B] the same counts for the host copy of cached */
+int k3gpu_model_commit_device(K3GpuModel *m, const int *keep_dev, const int *keep_host);
+/* a prompt ids DEVICE [B][n] read in and committed in passes of max_T; next DEVICE [B]
+ * the argmax after each sequence's last position */
+int k3gpu_model_prefill(K3GpuModel *m, const int *ids, int n, int *next);
+int k3gpu_model_cached(const K3GpuModel *m, int *cached);   /* host [B] */
+/* device views of a layer's state: KDA [B][H][D][D] and [B][3][P][K-1]; MLA caches */
+int k3gpu_model_kda_state(const K3GpuModel *m, int layer, float **state, float **conv_hist);
+int k3gpu_model_mla_cache(const K3GpuModel *m, int layer, uint16_t **lat, uint16_t **rope);
+/* The decode loop's callbacks (K3SpecVerifyFn / K3SpecCommitFn) for a model of B == 1,
+ * ctx = the model: verify uploads the host ids, sweeps and returns every position's argmax
+ * on the host (synchronising the model's stream); a read-in longer than max_T runs in
+ * passes, all but the last committed at once. */
+int k3gpu_model_loop_verify(void *ctx, const int *ids, const int *parent, int n, int base, int *arg);
+int k3gpu_model_loop_commit(void *ctx, int base, const int *path, int keep);
 
 /* ---------------------------------------------------- conversation state ------ */
 /* Host C: the conversation state file, K3ST version 2 byte for byte as the reference's

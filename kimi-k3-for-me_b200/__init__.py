@@ -83,6 +83,15 @@ class K3GpuMlaLayerW(C.Structure):
                 ("moe", C.POINTER(K3GpuMoeW))]
 
 
+class K3GpuModelCfg(C.Structure):
+    _fields_ = [("layer", K3GpuLayerCfg), ("n_layers", I), ("vocab", I), ("is_mla", VP)]
+
+
+class K3GpuModelW(C.Structure):
+    _fields_ = [("embed", VP), ("lm_head", VP), ("norm", VP), ("out_res_fold", VP),
+                ("kda", C.POINTER(K3GpuKdaLayerW)), ("mla", C.POINTER(K3GpuMlaLayerW))]
+
+
 EP_MAX_WORLD = 8
 EP_HANDLE_BYTES = 64
 
@@ -167,6 +176,21 @@ _SIGS = {
     "k3gpu_kda_norm_gate": ([VP, VP, VP, I, I, I, F, VP], I),
     "k3gpu_mla_workspace": ([I, I, I, I, I], SZ),
     "k3gpu_mla_absorbed": ([VP] * 8 + [I] * 9 + [F, VP, SZ, VP], I),
+    "k3gpu_argmax": ([VP, VP, I, I, VP], I),
+    "k3gpu_model_arena_bytes": ([C.POINTER(K3GpuModelCfg), I, I, I], SZ),
+    "k3gpu_model_create": ([C.POINTER(K3GpuModelCfg), C.POINTER(K3GpuModelW), I, I, I, VP, SZ, VP], VP),
+    "k3gpu_model_free": ([VP], None),
+    "k3gpu_model_set_stream": ([VP, VP], I),
+    "k3gpu_model_reset": ([VP], I),
+    "k3gpu_model_verify": ([VP, VP, I, VP, VP, C.POINTER(VP)], I),
+    "k3gpu_model_commit": ([VP, VP, VP], I),
+    "k3gpu_model_commit_device": ([VP, VP, VP], I),
+    "k3gpu_model_prefill": ([VP, VP, I, VP], I),
+    "k3gpu_model_cached": ([VP, VP], I),
+    "k3gpu_model_kda_state": ([VP, I, C.POINTER(VP), C.POINTER(VP)], I),
+    "k3gpu_model_mla_cache": ([VP, I, C.POINTER(VP), C.POINTER(VP)], I),
+    "k3gpu_model_loop_verify": ([VP, VP, VP, I, I, VP], I),
+    "k3gpu_model_loop_commit": ([VP, I, VP, I], I),
     "k3gpu_accept_greedy": ([VP, VP, VP, VP, VP, VP, I, I, I, VP], I),
     "k3gpu_accept_tree_greedy": ([VP] * 7 + [I, I, I, VP], I),
     "k3gpu_accept_sample": ([VP] * 5 + [I, I, I, F, U64, U64, VP], I),
@@ -785,7 +809,7 @@ class SpecLoop:
     def __init__(self, ids, verify, commit, *, cached=0, policy=DRAFT_NGRAM, spec_n=8, min_len=1, gen=64,
                  tmax=None, kv_cap=None, stop_ids=(), p3_q=None, p3_delta=0.22, p3_cost=None, p3_replay=False,
                  tree_nodes=64, tree_branch=4, draft_verify=None, draft_commit=None, prefill_chunk=0,
-                 pause_after=0, checkpoint=None):
+                 pause_after=0, checkpoint=None, native=None):
         ids = [int(v) for v in ids]
         tmax = tmax if tmax is not None else len(ids) + gen + 1
         self._errors = []
@@ -846,8 +870,14 @@ class SpecLoop:
                             float(p3_delta), C.cast(C.pointer(p3_cost), VP) if p3_cost is not None else None,
                             int(bool(p3_replay)), tree_nodes, tree_branch, prefill_chunk, pause_after)
         arr = (C.c_int * max(len(ids), 1))(*ids)
-        self._L = lib.k3_spec_loop_create(C.byref(cfg), arr, len(ids), cached,
-                                          C.cast(self._fns[0], VP), C.cast(self._fns[1], VP), None)
+        if native is not None:     # C callbacks (e.g. k3gpu_model_loop_verify / _commit) and their ctx
+            vfn, cfn, ctx = native
+            self._native = native
+            self._L = lib.k3_spec_loop_create(C.byref(cfg), arr, len(ids), cached, C.cast(vfn, VP),
+                                              C.cast(cfn, VP), ctx)
+        else:
+            self._L = lib.k3_spec_loop_create(C.byref(cfg), arr, len(ids), cached,
+                                              C.cast(self._fns[0], VP), C.cast(self._fns[1], VP), None)
         if not self._L:
             raise K3Error("k3_spec_loop_create: bad configuration")
         if draft_verify is not None:
@@ -963,3 +993,205 @@ class SafetensorsIndex:
             self.close()
         except Exception:  # noqa: BLE001 -- interpreter shutdown may have unloaded the library
             pass
+
+
+# ------------------------------------------------------------ model verify forward --
+def _sibling(name):
+    """A module of this package by file (the directory name is not an identifier)."""
+    import importlib.util
+    import sys
+    key = f"{__name__}_{name}"
+    if key not in sys.modules:
+        spec = importlib.util.spec_from_file_location(key, os.path.join(PKG, name + ".py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[key] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[key]
+
+
+def argmax(logits, stream=None):
+    """argmax_ per row of logits [rows][vocab] on the device (int32 [rows])."""
+    rows, V = logits.reshape(-1, logits.shape[-1]).shape
+    arg = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    check(lib.k3gpu_argmax(ptr(arg), ptr(logits), rows, V, stream_ptr(stream)), "k3gpu_argmax")
+    return arg
+
+
+class Model:
+    """A whole K3-architecture model on the device: the verify forward of k3gpu_model_*
+    (embed, every KDA/MLA + MoE decoder layer, the model-level AttnRes, the final norm, the
+    lm_head and the per-position argmax over B sequences) and its commit.
+
+    Built from a checkpoint directory (config.json + safetensors shards, the released
+    layout) with the package's config reader, tensor index and binder; the routed experts
+    of every MoE layer are read by k3_bank_read_safetensors into one device bank per layer.
+    Or from already bound fields (`from_fields`), for synthetic weights made on the device.
+    The model's state (KDA states and logs, MLA caches, activations) lives in one arena
+    this object allocates with torch; every computation runs in the library's kernels."""
+
+    def __init__(self, cfg: dict, layers: list, top: dict, banks: list, B=1, max_T=64, kv_cap=1024,
+                 device="cuda", stream=None):
+        n = cfg["num_hidden_layers"]
+        if cfg.get("first_k_dense_replace", 0) > 0:
+            raise K3Error("dense MLP layers (first_k_dense_replace > 0) are not on the verify path")
+        self.cfg, self.B, self.max_T, self.kv_cap = cfg, B, max_T, kv_cap
+        self.device = torch.device(device)
+        self.stream = stream
+        self.vocab = cfg["vocab_size"]
+        self._alive = [layers, top, banks]
+        cm = _sibling("config")
+        self.lcfg = cm.layer_cfg(sys_module(), cfg)
+        self._kda = (K3GpuKdaLayerW * n)()
+        self._mla = (K3GpuMlaLayerW * n)()
+        self._moe = []
+        self._is_mla = (C.c_int * n)()
+        use_norm = cfg.get("latent_moe_use_norm", True)
+        for L in range(n):
+            d, bank = layers[L], banks[L]
+            mw = K3GpuMoeW()
+            for f in ("down", "up", "sh1", "sh3", "sh2", "gate_W", "gate_bias"):
+                setattr(mw, f, ptr(d.get(f)))
+            mw.latent_norm = ptr(d["latent_norm"]) if use_norm else None
+            mw.bank = C.pointer(bank.desc)
+            self._moe.append(mw)
+            mla = d["kind"] == "mla"
+            self._is_mla[L] = int(mla)
+            lw = self._mla[L] if mla else self._kda[L]
+            for f in ("attn_res_fold", "mlp_res_fold", "in_norm", "post_norm", "gate_W", "gate_bias"):
+                setattr(lw, f, ptr(d[f]))
+            if mla:
+                lw.mla = mla_weights(d)
+            else:
+                lw.kda = kda_weights(d)
+            lw.bank = C.pointer(bank.desc)
+            lw.moe = C.pointer(mw)
+        self._c = K3GpuModelCfg(self.lcfg, n, self.vocab, C.cast(self._is_mla, VP))
+        self._w = K3GpuModelW(ptr(top["embed"]), ptr(top["lm_head"]), ptr(top["norm"]),
+                              ptr(top.get("out_res_fold")), self._kda, self._mla)
+        need = lib.k3gpu_model_arena_bytes(C.byref(self._c), B, max_T, kv_cap)
+        if need == 0:
+            raise K3Error("k3gpu_model_arena_bytes: configuration refused")
+        self.arena = torch.empty(need + 256, dtype=torch.uint8, device=self.device)
+        base = (self.arena.data_ptr() + 255) & ~255
+        self._m = lib.k3gpu_model_create(C.byref(self._c), C.byref(self._w), B, max_T, kv_cap, VP(base), need,
+                                         stream_ptr(stream))
+        if not self._m:
+            raise K3Error("k3gpu_model_create failed")
+        self.arena_bytes = need
+
+    @classmethod
+    def from_checkpoint(cls, ckpt_dir, B=1, max_T=64, kv_cap=1024, device="cuda", stream=None, scan=True):
+        import glob
+        cm, bm = _sibling("config"), _sibling("bind")
+        cfg = cm.read_config(os.path.join(ckpt_dir, "config.json"))
+        index = SafetensorsIndex(ckpt_dir)
+        binder = bm.Binder(index, cfg)
+        files = sorted(glob.glob(os.path.join(ckpt_dir, "*.safetensors")))
+        n_exp, Lt, I_ = cfg["num_experts"], cfg["routed_expert_hidden_size"], cfg["moe_intermediate_size"]
+        layers, banks = [], []
+        for L in range(cfg["num_hidden_layers"]):
+            f = binder.layer(L)
+            d = bm.to_device(f, device)
+            d["kind"] = f["kind"]
+            if f["kind"] == "mla" and f.get("g") is None:
+                d["g"] = None
+            layers.append(d)
+            host = bank_read_safetensors(files, L, 0, n_exp, Lt, I_)
+            bank = ExpertBank(torch.from_numpy(host).to(device), n_exp, Lt, I_)
+            if scan:
+                bank.scan(stream)
+            banks.append(bank)
+        top = bm.to_device(binder.model(), device)
+        index.close()
+        return cls(cfg, layers, top, banks, B=B, max_T=max_T, kv_cap=kv_cap, device=device, stream=stream)
+
+    def close(self):
+        if getattr(self, "_m", None):
+            lib.k3gpu_model_free(self._m)
+            self._m = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 -- interpreter shutdown may have unloaded the library
+            pass
+
+    def reset(self):
+        check(lib.k3gpu_model_reset(self._m), "k3gpu_model_reset")
+
+    def verify(self, ids, parent=None):
+        """ids int32 [B][T] (device) -> (arg int32 [B][T], logits view [B][T][vocab]);
+        parent: host list [T] (a draft tree shared by the sequences) or None (a chain).
+        The logits view is the model's own buffer, valid until the next sweep."""
+        ids = ids.to(self.device, torch.int32).contiguous()
+        B, T = ids.shape
+        arg = torch.empty((B, T), dtype=torch.int32, device=self.device)
+        lp = VP()
+        par = (C.c_int * T)(*parent) if parent is not None else None
+        check(lib.k3gpu_model_verify(self._m, ptr(ids), T, par, ptr(arg), C.byref(lp)), "k3gpu_model_verify")
+        return arg, self.logits_view(lp.value, B, T)
+
+    def logits_view(self, addr, B, T):
+        off = addr - self.arena.data_ptr()
+        n = B * T * self.vocab
+        return self.arena[off:off + 4 * n].view(torch.float32).view(B, T, self.vocab)
+
+    def commit(self, keep, path=None):
+        """keep: host ints [B]; path: host [B][T] accepted tree nodes (tree sweeps only)."""
+        kk = (C.c_int * self.B)(*[int(v) for v in keep])
+        pp = None
+        if path is not None:
+            flat = [int(v) for row in path for v in row]
+            pp = (C.c_int * len(flat))(*flat)
+        check(lib.k3gpu_model_commit(self._m, kk, pp), "k3gpu_model_commit")
+
+    def prefill(self, ids):
+        """ids int32 [B][n] (device): read in and committed; returns the next ids [B]."""
+        ids = ids.to(self.device, torch.int32).contiguous()
+        nxt = torch.empty(self.B, dtype=torch.int32, device=self.device)
+        check(lib.k3gpu_model_prefill(self._m, ptr(ids), ids.shape[1], ptr(nxt)), "k3gpu_model_prefill")
+        return nxt
+
+    def cached(self):
+        c = (C.c_int * self.B)()
+        check(lib.k3gpu_model_cached(self._m, c), "k3gpu_model_cached")
+        return list(c)
+
+    def kda_state(self, layer):
+        """(state [B][H][D][D], conv history [B][3][P][K-1]) device views of a KDA layer."""
+        st, hi = VP(), VP()
+        check(lib.k3gpu_model_kda_state(self._m, layer, C.byref(st), C.byref(hi)), "k3gpu_model_kda_state")
+        c = self.lcfg
+        H, D, K = c.kda_heads, c.kda_head_dim, c.conv_k
+        return (self._view(st.value, (self.B, H, D, D), torch.float32),
+                self._view(hi.value, (self.B, 3, H * D, K - 1), torch.float32))
+
+    def mla_cache(self, layer):
+        """(latent [B][cap][kv_lora], rope [B][cap][qk_rope]) bf16 bits (int16) views."""
+        lt, rp = VP(), VP()
+        check(lib.k3gpu_model_mla_cache(self._m, layer, C.byref(lt), C.byref(rp)), "k3gpu_model_mla_cache")
+        c = self.lcfg
+        lat = self._view(lt.value, (self.B, self.kv_cap, c.kv_lora), torch.int16)
+        rope = self._view(rp.value, (self.B, self.kv_cap, c.qk_rope), torch.int16) if rp.value else None
+        return lat, rope
+
+    def _view(self, addr, shape, dtype):
+        off = addr - self.arena.data_ptr()
+        n = 1
+        for v in shape:
+            n *= v
+        nb = n * torch.tensor([], dtype=dtype).element_size()
+        return self.arena[off:off + nb].view(dtype).view(*shape)
+
+    def spec_loop(self, ids, **kw):
+        """The engine's decode loop (SpecLoop) with this model's native callbacks (B == 1):
+        every verify and commit runs in the library, nothing in Python between them."""
+        if self.B != 1:
+            raise K3Error("the decode loop drives one sequence")
+        return SpecLoop(ids, None, None, native=(lib.k3gpu_model_loop_verify, lib.k3gpu_model_loop_commit,
+                                                 self._m), **kw)
+
+
+def sys_module():
+    import sys
+    return sys.modules[__name__]

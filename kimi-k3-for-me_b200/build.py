@@ -23,7 +23,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxe
          "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 SOURCES = ["abi.cu", "router.cu", "moe.cu", "moe_mma.cu", "moe_tc.cu", "kda.cu", "mla.cu", "accept.cu",
            "norm.cu", "mmw.cu", "layer.cu", "ep.cu", "draft.cu", "st.cu", "state.cu",
-           "loop.cu", "kda_chunk.cu"]
+           "loop.cu", "kda_chunk.cu", "model.cu"]
 
 
 def _stale(target: str, deps: list[str]) -> bool:

@@ -344,6 +344,14 @@ extern "C" int k3gpu_accept_greedy(int *emit, int *n_emit, int *arg, const float
     return k3::launch_status();
 }
 
+extern "C" int k3gpu_argmax(int *arg, const float *logits, int rows, int vocab, void *stream)
+{
+    if (!arg || !logits || rows <= 0 || vocab <= 0) return K3GPU_EINVAL;
+    k3::argmax_kernel<<<dim3(k3::AM_CLUSTER, (unsigned)std::min(rows, 65535)), k3::AM_THREADS, 0,
+                        k3::as_stream(stream)>>>(arg, logits, vocab, rows);
+    return k3::launch_status();
+}
+
 extern "C" int k3gpu_accept_tree_greedy(int *emit, int *n_emit, int *path, int *arg,
                                         const float *logits, const int *tok, const int *parent,
                                         int B, int T, int vocab, void *stream)

@@ -25,6 +25,11 @@ import subprocess
 import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def reference_dir():
+    """K3_REFERENCE, else a checkout named `reference` beside this repository."""
+    return os.environ.get("K3_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 DUMP = os.path.join(HERE, "..", "..", "oracle", "_ref", "cfgdump")
 
 FLAT = {"hidden_size": 96, "num_hidden_layers": 7, "vocab_size": 300, "rms_norm_eps": 1e-5,
@@ -111,7 +116,8 @@ def run(doc):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=reference_dir(),
+                    help="the reference checkout (default: K3_REFERENCE, else `reference` beside this repository)")
     a = ap.parse_args()
     docs = variants()
     fx = os.path.join(a.ref, "tests", "fixtures")

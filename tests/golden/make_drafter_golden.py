@@ -35,6 +35,11 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def reference_dir():
+    """K3_REFERENCE, else a checkout named `reference` beside this repository."""
+    return os.environ.get("K3_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 CAP = 8
 
 
@@ -60,7 +65,8 @@ def sequences(rng):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=reference_dir(),
+                    help="the reference checkout (default: K3_REFERENCE, else `reference` beside this repository)")
     a = ap.parse_args()
     spec = importlib.util.spec_from_file_location("spec_replay", os.path.join(a.ref, "tools", "spec_replay.py"))
     sr = importlib.util.module_from_spec(spec)

@@ -26,6 +26,11 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def reference_dir():
+    """K3_REFERENCE, else a checkout named `reference` beside this repository."""
+    return os.environ.get("K3_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 from oracle import oracle as O  # noqa: E402
@@ -199,7 +204,8 @@ def gen_moe(lib) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=reference_dir(),
+                    help="the reference checkout (default: K3_REFERENCE, else `reference` beside this repository)")
     a = ap.parse_args()
     O.build()
     lib = O.ref()
