@@ -363,6 +363,51 @@ def run_ep(args, k3, rank, world, dev):
             layer.close()
 
 
+def ep_parity(args, k3, rank, world, dev, layer, x, res):
+    """After the timed steps: the device status word of every rank (no bounded exchange wait
+    ran out, no index was skipped), every owner's rows arrived at every rank, and the last
+    step's outputs and routing on every rank equal the UNSHARDED single-GPU layer's
+    (k3gpu_moe_layer over all 384 experts, rebuilt on rank 0 from the same seeds) on the
+    same tokens. A failure ends the run without a line: such a step is not a measurement."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    status = k3.device_status(dev.index)
+    owners = layer.owners_ok() if hasattr(layer, "owners_ok") else [1] * world
+    xs = [torch.empty_like(x) for _ in range(world)]
+    outs = [torch.empty_like(res["out"]) for _ in range(world)]
+    idxs = [torch.empty_like(res["idx"]) for _ in range(world)]
+    dist.all_gather(xs, x)
+    dist.all_gather(outs, res["out"])
+    dist.all_gather(idxs, res["idx"])
+    verdict = torch.zeros(4, dtype=torch.float64, device=dev)   # status, owners bad, idx bad, rel
+    verdict[0] = float(status)
+    verdict[1] = float(min(owners) == 0)
+    if rank == 0:
+        n_local = N_ROUTED // world
+        parts = [make_bank_device(n_local, L_DIM, I_DIM, args.seed + 7919 * (r + 1), dev)[0] for r in range(world)]
+        parts.append(make_bank_device(N_SHARED, L_DIM, I_DIM, args.seed + 104729, dev)[0])
+        full = torch.cat(parts)
+        del parts
+        kb = k3.ExpertBank(full, N_ROUTED + N_SHARED, L_DIM, I_DIM)
+        if not args.no_tc:
+            kb.scan()
+        _, gate, bias = make_inputs(x.shape[0], args.seed + 1, dev)
+        ref, ridx, _ = k3.moe_layer(torch.cat(xs), gate, bias, kb, TOPK, N_ROUTED, N_SHARED, k3.ACT_SWIGLU)
+        got = torch.cat(outs)
+        verdict[2] = float(not torch.equal(torch.cat(idxs), ridx))
+        verdict[3] = float((got - ref).norm() / ref.norm())
+        del full, kb
+        torch.cuda.empty_cache()
+    dist.all_reduce(verdict, op=dist.ReduceOp.MAX)
+    v = verdict.tolist()
+    parity = {"status_max_over_ranks": int(v[0]), "owners_ok": v[1] == 0, "idx_equal": v[2] == 0,
+              "rel_l2": float(f"{v[3]:.3g}"), "reference": "k3gpu_moe_layer, all experts on one GPU"}
+    if v[0] != 0 or v[1] != 0 or v[2] != 0 or not v[3] < 1e-5:
+        raise SystemExit(f"expert-parallel step failed its check, no line printed: {parity}")
+    return parity
+
+
 def _run_ep_timed(args, k3, rank, world, dev, layer, x, n_local, M, n_unsafe, stream):
     import torch
     import torch.distributed as dist
@@ -430,6 +475,7 @@ def _run_ep_timed(args, k3, rank, world, dev, layer, x, n_local, M, n_unsafe, st
     achieved = gateup_bytes / (ph[2] * 1e-3) / 1e9 if ph[2] > 0 else 0.0
     ach = torch.tensor([achieved], device=dev)
     dist.all_reduce(ach, op=dist.ReduceOp.MIN)
+    parity = ep_parity(args, k3, rank, world, dev, layer, x, res)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(world * M / (dev_ms * 1e-3), 3), "unit": "tok/s",
@@ -450,6 +496,7 @@ def _run_ep_timed(args, k3, rank, world, dev, layer, x, n_local, M, n_unsafe, st
             # + 8 exchange kernels on the peer-memory transport
             "gpu_launches": (14 + (4 if n_unsafe else 0) + (8 if args.ep_transport == "p2p" else 0)) * args.steps,
             "ep_transport": "peer memory (k3gpu_ep_*, NVLink)" if args.ep_transport == "p2p" else "NCCL all_to_all",
+            "ep_parity": parity,
             "clocks": clk,
             "cpu_baseline": None,
         }

@@ -79,7 +79,9 @@ int k3gpu_router(int *idx, float *w, const float *x, const float *W, const float
  * the library until the process exits).
  *   - T * n_experts above the maximum returns K3GPU_ECAPACITY and enqueues nothing.
  *   - The first call on a device looks up that device's copy of the array (set-up, once
- *     per device); make that first call before any stream capture.
+ *     per device); make that first call before any stream capture. After a device reset
+ *     (cudaDeviceReset) the array has a new address: the next call on that device sees
+ *     the new context and repeats the set-up, so make it before any capture too.
  *   - Every call shares the one array: two calls whose kernels overlap on the same GPU
  *     (different streams, or host threads) race and may return wrong results. Calls on
  *     one stream are ordered and safe. Nothing in the array needs clearing: each call
@@ -664,6 +666,10 @@ int k3gpu_ep_return(const K3GpuEpGroup *g, const float *part, unsigned seq, void
 /* ok [world] (device) receives 1 per owner whose rows arrived. */
 int k3gpu_ep_combine(const K3GpuEpGroup *g, float *out, const int *pos, int T, unsigned seq,
                      int *ok, void *stream);
+/* The bound of every exchange wait, in flag polls about 100 ns apart (host, per process,
+ * read at each launch; default 2^24, about 1.7 s; 1 .. 2^30). A wait that runs out records
+ * DEV_TIMEOUT and treats the silent peer's rows as empty. */
+int k3gpu_ep_set_wait_limit(long long polls);
 
 /* ---------------------------------------------------------------- drafter ------ */
 /* Host C (no GPU): the reference's n-gram drafter, spec_draft (src/cli/k3_run.c:450-491),

@@ -223,6 +223,7 @@ _SIGS = {
     "k3gpu_ep_receive": ([C.POINTER(K3GpuEpGroup), C.c_uint, VP], I),
     "k3gpu_ep_return": ([C.POINTER(K3GpuEpGroup), VP, C.c_uint, VP], I),
     "k3gpu_ep_combine": ([C.POINTER(K3GpuEpGroup), VP, VP, I, C.c_uint, VP, VP], I),
+    "k3gpu_ep_set_wait_limit": ([C.c_longlong], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
     "k3_spec_draft_eager": ([VP, I, I, VP], I),
     "k3_bank_read_safetensors": ([C.POINTER(C.c_char_p), I, I, I, I, I, I, VP, SZ], I),

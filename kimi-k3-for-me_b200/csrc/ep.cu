@@ -30,7 +30,8 @@ namespace k3 {
 namespace ep {
 
 constexpr int HDR_BYTES = 4096;                 // recv_cnt, recv_flag, back_flag, eff_cnt
-constexpr long long SPIN = 1LL << 24;           // flag polls (~100 ns apart) before giving up
+constexpr long long SPIN_DEFAULT = 1LL << 24;   // flag polls (~100 ns apart) before giving up: ~1.7 s
+static long long g_spin = SPIN_DEFAULT;          // k3gpu_ep_set_wait_limit
 
 struct Layout {
     size_t x_recv, idx_recv, wt_recv, back, total;
@@ -75,9 +76,9 @@ __device__ __forceinline__ unsigned load_acquire_sys(const unsigned *p)
     return v;
 }
 // bounded wait for *p == seq (flags only grow; a later value also means seq was passed)
-__device__ __forceinline__ bool wait_flag(const unsigned *p, unsigned seq)
+__device__ __forceinline__ bool wait_flag(const unsigned *p, unsigned seq, long long spin)
 {
-    for (long long i = 0; i < SPIN; i++) {
+    for (long long i = 0; i < spin; i++) {
         if ((int)(load_acquire_sys(p) - seq) >= 0) return true;
         __nanosleep(64);
     }
@@ -139,16 +140,17 @@ __global__ void __launch_bounds__(1024) dispatch_meta_kernel(Ptrs P, int *__rest
 }
 
 // grid (T, world), block 256: row t to rank d's x_recv[me][pos[d][t]] when it goes there
+// (vec: 16-byte rows on both sides, chosen per call from L and the caller's pointer)
 __global__ void __launch_bounds__(256) dispatch_rows_kernel(Ptrs P, const int *__restrict__ pos,
                                                              const float *__restrict__ x, int T, int L, int cap,
-                                                             int me, size_t off_x)
+                                                             int me, size_t off_x, int vec)
 {
     const int t = blockIdx.x, d = blockIdx.y;
     const int slot = pos[(size_t)d * T + t];
     if (slot < 0) return;
     float *dst = reinterpret_cast<float *>(P.arena[d] + off_x) + ((size_t)me * cap + slot) * L;
     const float *src = x + (size_t)t * L;
-    if ((L & 3) == 0) {
+    if (vec) {
         const float4 *s4 = reinterpret_cast<const float4 *>(src);
         float4 *d4 = reinterpret_cast<float4 *>(dst);
         for (int i = threadIdx.x; i < L / 4; i += 256) d4[i] = s4[i];
@@ -169,12 +171,13 @@ __global__ void signal_kernel(Ptrs P, int world, int me, unsigned seq, int which
 
 // grid world, block 256 (owner): wait for source s's rows, then mark its unused slots
 // dropped; a source that never signalled counts as empty
-__global__ void __launch_bounds__(256) receive_kernel(char *own, int cap, int K, unsigned seq, size_t off_idx)
+__global__ void __launch_bounds__(256) receive_kernel(char *own, int cap, int K, unsigned seq, size_t off_idx,
+                                                      long long spin)
 {
     __shared__ int n;
     const int s = blockIdx.x;
     if (threadIdx.x == 0) {
-        const bool ok = wait_flag(recv_flag(own) + s, seq);
+        const bool ok = wait_flag(recv_flag(own) + s, seq, spin);
         if (!ok) flag(DEV_TIMEOUT);
         n = ok ? min(max(recv_cnt(own)[s], 0), cap) : 0;
         eff_cnt(own)[s] = n;
@@ -186,14 +189,14 @@ __global__ void __launch_bounds__(256) receive_kernel(char *own, int cap, int K,
 
 // grid (cap, world), block 256 (owner): partial row of (source s, slot) back to s
 __global__ void __launch_bounds__(256) return_rows_kernel(Ptrs P, const float *__restrict__ part, int L, int cap,
-                                                           int me, size_t off_back)
+                                                           int me, size_t off_back, int vec)
 {
     const int slot = blockIdx.x, s = blockIdx.y;
     char *own = P.arena[me];
     if (slot >= eff_cnt(own)[s]) return;
     float *dst = reinterpret_cast<float *>(P.arena[s] + off_back) + ((size_t)me * cap + slot) * L;
     const float *src = part + ((size_t)s * cap + slot) * L;
-    if ((L & 3) == 0) {
+    if (vec) {
         const float4 *s4 = reinterpret_cast<const float4 *>(src);
         float4 *d4 = reinterpret_cast<float4 *>(dst);
         for (int i = threadIdx.x; i < L / 4; i += 256) d4[i] = s4[i];
@@ -203,11 +206,11 @@ __global__ void __launch_bounds__(256) return_rows_kernel(Ptrs P, const float *_
 }
 
 // block world (source): wait for every owner's return; ok[o] = 1 when it arrived
-__global__ void wait_back_kernel(char *own, int world, unsigned seq, int *__restrict__ ok)
+__global__ void wait_back_kernel(char *own, int world, unsigned seq, int *__restrict__ ok, long long spin)
 {
     const int o = threadIdx.x;
     if (o >= world) return;
-    const bool got = wait_flag(back_flag(own) + o, seq);
+    const bool got = wait_flag(back_flag(own) + o, seq, spin);
     if (!got) flag(DEV_TIMEOUT);
     ok[o] = got ? 1 : 0;
 }
@@ -325,7 +328,9 @@ extern "C" int k3gpu_ep_dispatch(const K3GpuEpGroup *g, const float *x, const in
                                                   l.idx_recv, l.wt_recv);
     int st = k3::launch_status();
     if (st) return st;
-    dispatch_rows_kernel<<<dim3(T, g->world), 256, 0, s>>>(P, pos, x, T, g->L, g->cap, g->rank, l.x_recv);
+    // the arena rows start on 16-byte boundaries when L % 4 == 0 (regions are 256-aligned)
+    const int vec = (g->L & 3) == 0 && k3::aligned(x, 16);
+    dispatch_rows_kernel<<<dim3(T, g->world), 256, 0, s>>>(P, pos, x, T, g->L, g->cap, g->rank, l.x_recv, vec);
     if ((st = k3::launch_status())) return st;
     signal_kernel<<<1, 32, 0, s>>>(P, g->world, g->rank, seq, 0);
     return k3::launch_status();
@@ -337,7 +342,7 @@ extern "C" int k3gpu_ep_receive(const K3GpuEpGroup *g, unsigned seq, void *strea
     if (!group_ok(g) || seq == 0) return K3GPU_EINVAL;
     const Layout l = layout(g->world, g->cap, g->L, g->K);
     receive_kernel<<<g->world, 256, 0, k3::as_stream(stream)>>>(static_cast<char *>(g->arena[g->rank]), g->cap, g->K,
-                                                                seq, l.idx_recv);
+                                                                seq, l.idx_recv, g_spin);
     return k3::launch_status();
 }
 
@@ -348,7 +353,8 @@ extern "C" int k3gpu_ep_return(const K3GpuEpGroup *g, const float *part, unsigne
     const Layout l = layout(g->world, g->cap, g->L, g->K);
     cudaStream_t s = k3::as_stream(stream);
     const Ptrs P = ptrs(g);
-    return_rows_kernel<<<dim3(g->cap, g->world), 256, 0, s>>>(P, part, g->L, g->cap, g->rank, l.back);
+    const int vec = (g->L & 3) == 0 && k3::aligned(part, 16);
+    return_rows_kernel<<<dim3(g->cap, g->world), 256, 0, s>>>(P, part, g->L, g->cap, g->rank, l.back, vec);
     int st = k3::launch_status();
     if (st) return st;
     signal_kernel<<<1, 32, 0, s>>>(P, g->world, g->rank, seq, 1);
@@ -363,9 +369,16 @@ extern "C" int k3gpu_ep_combine(const K3GpuEpGroup *g, float *out, const int *po
     const Layout l = layout(g->world, g->cap, g->L, g->K);
     cudaStream_t s = k3::as_stream(stream);
     char *own = static_cast<char *>(g->arena[g->rank]);
-    wait_back_kernel<<<1, 32, 0, s>>>(own, g->world, seq, ok);
+    wait_back_kernel<<<1, 32, 0, s>>>(own, g->world, seq, ok, g_spin);
     int st = k3::launch_status();
     if (st) return st;
     combine_kernel<<<dim3(T, (g->L + 1023) / 1024), 256, 0, s>>>(out, own, pos, ok, T, g->L, g->cap, g->world, l.back);
     return k3::launch_status();
+}
+
+extern "C" int k3gpu_ep_set_wait_limit(long long polls)
+{
+    if (polls < 1 || polls > (1LL << 30)) return K3GPU_EINVAL;
+    k3::ep::g_spin = polls;
+    return K3GPU_OK;
 }

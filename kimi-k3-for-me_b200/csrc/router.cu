@@ -21,6 +21,8 @@
 
 #include <mutex>
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace k3 {
@@ -251,22 +253,57 @@ static __device__ __align__(256) float g_router_noalloc_scores[K3GPU_ROUTER_NOAL
 constexpr int NOALLOC_MAX_DEVICES = 64;
 static std::mutex g_noalloc_mu;
 static float *g_noalloc_addr[NOALLOC_MAX_DEVICES] = {};
+static unsigned long long g_noalloc_ctx[NOALLOC_MAX_DEVICES] = {};   // context id of each lookup
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long *);
+
+// The id of the current context (cuCtxGetId, through the runtime's driver entry points), or
+// 0 when it cannot be read. A device reset replaces the primary context, and with it the
+// array's address, so the id tells a stale lookup from a valid one.
+static unsigned long long current_ctx_id()
+{
+    static CtxGetCurrentFn get_cur = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    CUcontext c = nullptr;
+    unsigned long long id = 0;
+    if (!get_cur || !get_id || get_cur(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
 
 // In host code the array's name is only a host-side stand-in, not a device address, so
 // the kernels get the address cudaGetSymbolAddress returns for the current device. The
-// lookup is the per-device set-up, done by the first call on each device.
+// lookup is the per-device set-up, done by the first call on each device -- and again by
+// the first call after that device's context was replaced (a cudaDeviceReset), whose
+// module, and so the array, has a new address.
 static int noalloc_scores(float **out)
 {
     int dev = 0;
     int st = cuda_status(cudaGetDevice(&dev));
     if (st) return st;
     if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return K3GPU_EINVAL;
+    // (0 when no context is current on this thread yet: the lookup below makes it current
+    // and records its id, so at most one extra lookup follows)
+    const unsigned long long ctx = current_ctx_id();
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
+    if (!g_noalloc_addr[dev] || g_noalloc_ctx[dev] != ctx) {
         void *p = nullptr;
         st = cuda_status(cudaGetSymbolAddress(&p, g_router_noalloc_scores));
         if (st) return st;
         g_noalloc_addr[dev] = static_cast<float *>(p);
+        g_noalloc_ctx[dev] = current_ctx_id();
     }
     *out = g_noalloc_addr[dev];
     return K3GPU_OK;

@@ -140,10 +140,12 @@ struct Scan {
         p = q;
         return integral;
     }
-    void skip_value()
+    // values nested deeper than this are refused (a malformed header, not a stack overflow)
+    static constexpr int MAX_DEPTH = 64;
+    void skip_value(int depth = 0)
     {
         ws();
-        if (p >= e) { ok = false; return; }
+        if (p >= e || depth > MAX_DEPTH) { ok = false; return; }
         if (*p == '"') { str(); return; }
         if (*p == '{') {
             p++;
@@ -151,7 +153,7 @@ struct Scan {
             do {
                 str();
                 if (!eat(':')) { ok = false; return; }
-                skip_value();
+                skip_value(depth + 1);
             } while (ok && eat(','));
             if (!eat('}')) ok = false;
             return;
@@ -159,7 +161,7 @@ struct Scan {
         if (*p == '[') {
             p++;
             if (eat(']')) return;
-            do skip_value();
+            do skip_value(depth + 1);
             while (ok && eat(','));
             if (!eat(']')) ok = false;
             return;

@@ -230,6 +230,12 @@ class P2PMoELayer:
 
     __call__ = forward
 
+    def owners_ok(self):
+        """Per owner rank, whether its rows of the last step arrived (host list; waits for
+        the step). A 0 means that owner's bounded wait ran out and its contribution is
+        missing from the output (k3gpu_device_status also holds the timeout bit)."""
+        return self.ok.tolist()
+
     def close(self):
         """Unmap the peers' arenas and free this rank's (after a barrier, so no rank still
         writes into it)."""

@@ -161,3 +161,70 @@ def test_ep_two_gpus_matches_single_gpu_layer():
                        start_method="spawn")
     assert results["idx_local_ok"]
     assert results["rel"] < 1e-5, results["rel"]
+
+
+
+def test_ep_exchange_wait_runs_out_and_reports():
+    """One GPU, a world of two: rank 0's arena and a second arena on the same GPU standing
+    in for a peer that never signals. With a short wait limit, receive and combine give up
+    on the silent peer: the timeout bit is set, its receive slots are all dropped, its owner
+    flag is 0, and the output holds exactly rank 0's own partial rows. Every wait is
+    bounded, so the kernels return; nothing else waits on them."""
+    import ctypes as C
+
+    from k3lib import load
+
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    k3 = load()
+    lib = k3.lib
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L, K, cap, T, n_local = 64, 2, 8, 5, 4
+    nbytes = lib.k3gpu_ep_arena_bytes(2, cap, L, K)
+    arenas = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    assert all(a.data_ptr() % 256 == 0 for a in arenas)
+    g = k3.K3GpuEpGroup()
+    g.world, g.rank, g.cap, g.L, g.K, g.n_local = 2, 0, cap, L, K, n_local
+    g.arena[0], g.arena[1] = arenas[0].data_ptr(), arenas[1].data_ptr()
+    torch.cuda.synchronize()
+    k3.device_status(0)                                     # clear
+    k3.check(lib.k3gpu_ep_set_wait_limit(2000), "k3gpu_ep_set_wait_limit")
+    try:
+        x = torch.randn((T, L), device=dev)
+        # tokens 0, 2, 4 use an expert of rank 0 (ids 0..3); every token one of rank 1 (4..7)
+        idx = torch.tensor([[1, 5], [6, 7], [0, 4], [5, 6], [3, 7]], dtype=torch.int32, device=dev)
+        wt = torch.full((T, K), 0.5, device=dev)
+        pos = torch.empty(2 * T, dtype=torch.int32, device=dev)
+        sp = k3.stream_ptr()
+        k3.check(lib.k3gpu_ep_dispatch(C.byref(g), k3.ptr(x), k3.ptr(idx), k3.ptr(wt), T, 1, k3.ptr(pos), sp),
+                 "k3gpu_ep_dispatch")
+        k3.check(lib.k3gpu_ep_receive(C.byref(g), 1, sp), "k3gpu_ep_receive")
+        torch.cuda.synchronize()
+        assert k3.device_status(0) & 8, "the receive wait on the silent peer did not run out"
+        xr, ir, wr = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        k3.check(lib.k3gpu_ep_recv_views(C.byref(g), C.byref(xr), C.byref(ir), C.byref(wr)), "views")
+        off = ir.value - arenas[0].data_ptr()
+        recv_idx = arenas[0][off:off + 4 * 2 * cap * K].view(torch.int32).view(2, cap, K).cpu()
+        assert torch.all(recv_idx[1] == -1), "the silent peer's receive slots were not dropped"
+        assert recv_idx[0, :3].tolist() == [[1, -1], [0, -1], [3, -1]]   # tokens 0, 2, 4: local ids
+        assert torch.all(recv_idx[0, 3:] == -1)
+        part = torch.randn((2 * cap, L), device=dev)
+        k3.check(lib.k3gpu_ep_return(C.byref(g), k3.ptr(part), 1, sp), "k3gpu_ep_return")
+        out0 = torch.randn((T, L), device=dev)
+        out = out0.clone()
+        ok = torch.empty(2, dtype=torch.int32, device=dev)
+        k3.check(lib.k3gpu_ep_combine(C.byref(g), k3.ptr(out), k3.ptr(pos), T, 1, k3.ptr(ok), sp),
+                 "k3gpu_ep_combine")
+        torch.cuda.synchronize()
+        assert ok.tolist() == [1, 0]
+        assert k3.device_status(0) & 8, "the combine wait on the silent peer did not run out"
+        want = out0.clone()
+        for t, p in enumerate(pos[:T].tolist()):
+            if p >= 0:
+                want[t] += part[p]
+        assert torch.equal(out, want)
+    finally:
+        lib.k3gpu_ep_set_wait_limit(1 << 24)
+        torch.cuda.synchronize()
+        k3.device_status(0)

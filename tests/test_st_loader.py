@@ -218,3 +218,28 @@ def test_tensor_index_refuses_broken_sets(k3, tmp_path):
         k3.SafetensorsIndex([short])                       # data past the end
     with pytest.raises(k3.K3Error):
         k3.SafetensorsIndex(str(tmp_path / "empty_dir_that_does_not_exist"))
+
+
+def test_deeply_nested_header_is_refused_not_overflowed(k3, tmp_path):
+    """A header whose metadata nests arrays far deeper than any checkpoint (a crafted or
+    corrupt shard) is refused as malformed; nesting within the bound still reads."""
+    import json
+    import struct
+
+    def shard(path, depth):
+        meta = "[" * depth + "1" + "]" * depth
+        body = json.dumps({"t": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]}})
+        hdr = ('{"__metadata__": {"x": %s}, %s' % (meta, body[1:])).encode()
+        with open(path, "wb") as f:
+            f.write(struct.pack("<Q", len(hdr)))
+            f.write(hdr)
+            f.write(np.arange(2, dtype=np.float32).tobytes())
+        return str(path)
+
+    ok = shard(tmp_path / "ok.safetensors", 40)
+    idx = k3.SafetensorsIndex([ok])
+    assert idx.read("t").view(np.float32).tolist() == [0.0, 1.0]
+    idx.close()
+    bad = shard(tmp_path / "deep.safetensors", 200000)
+    with pytest.raises(k3.K3Error):
+        k3.SafetensorsIndex([bad])
