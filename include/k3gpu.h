@@ -252,6 +252,17 @@ int k3gpu_kda_commit(float *state, const float *k, const float *v, const float *
                      const float *beta, const int *n, int B, int T, int H, int D,
                      void *stream);
 
+/* k3gpu_kda_verify over a draft TREE of T nodes (no counterpart in the reference, whose
+ * sweeps are chains): parent DEVICE [T] (parent[0] = -1, parent[t] < t), one tree shape for
+ * the B sequences. Node t reads the state after its own ancestors -- the chain of
+ * k3_kda_step over root .. t on the read-only carried state, recomputed per node with the
+ * chain's float operations, so each output is bit-identical to a chain verify of the
+ * node's path. Committing an accepted path: gather its log rows to the front, then
+ * k3gpu_kda_commit / k3gpu_kda_commit_conv with n = the path length. */
+int k3gpu_kda_verify_tree(float *o, const float *state, const float *q, const float *k,
+                          const float *v, const float *alpha, const float *beta, const int *parent,
+                          int B, int T, int H, int D, float qscale, void *stream);
+
 /* The KDA prologue, src/core/k3_ops.c:2286-2303 for B sequences: from the projection
  * outputs q, k, v [B][T][P] (P = H*D), z [B][T][P] (f_b output, before dt_bias) and
  * b [B][T][H], with the carried ShortConv history hist [B][3][P][K-1] (read only):
@@ -265,6 +276,15 @@ int k3gpu_kda_prologue(float *q, float *k, float *v, float *alpha, float *beta, 
                        const float *k_conv, const float *v_conv, const float *hist,
                        const float *A_log, const float *dt_bias, int B, int T, int H, int D,
                        int K, float lb, void *stream);
+
+/* k3gpu_kda_prologue over a draft tree (parent DEVICE [T], as k3gpu_kda_verify_tree; NULL:
+ * the chain): each node's ShortConv window is its ancestors' pre-conv rows (its parent
+ * newest) and then the carried history. */
+int k3gpu_kda_prologue_tree(float *q, float *k, float *v, float *alpha, float *beta, float *pre,
+                            const float *z, const float *b, const float *q_conv,
+                            const float *k_conv, const float *v_conv, const float *hist,
+                            const float *A_log, const float *dt_bias, const int *parent, int B,
+                            int T, int H, int D, int K, float lb, void *stream);
 
 /* Replaces kda_replay_conv_ (src/core/k3_ops.c:2207-2223): advance the ShortConv history
  * hist [B][3][P][K-1] in place by the first n[b] pre-conv rows of pre [B][T][3][P].
@@ -487,6 +507,13 @@ int k3gpu_kda_layer_verify(float *out, const float *x, const K3GpuKdaW *w,
                            const K3GpuKdaLog *log, int B, int T, void *workspace,
                            size_t ws_bytes, void *stream);
 
+/* k3gpu_kda_layer_verify over a draft tree of T nodes (parent DEVICE [T]; NULL: a chain):
+ * the ShortConv and the recurrence follow each node's ancestors. */
+int k3gpu_kda_layer_verify_tree(float *out, const float *x, const K3GpuKdaW *w,
+                                const K3GpuLayerCfg *c, const float *state, const float *conv_hist,
+                                const K3GpuKdaLog *log, const int *parent, int B, int T,
+                                void *workspace, size_t ws_bytes, void *stream);
+
 size_t k3gpu_decoder_layer_workspace(const K3GpuLayerCfg *c, int B, int T);
 
 /* k3_decoder_layer_inc_log (src/core/k3_ops.c:2594-2602 -> core :2485-2592) for a KDA +
@@ -501,6 +528,14 @@ int k3gpu_decoder_layer_kda_verify(float *h, float *block_residual, int *n_block
                                    const K3GpuLayerCfg *c, int layer_idx, const float *state,
                                    const float *conv_hist, const K3GpuKdaLog *log, int B, int T,
                                    void *workspace, size_t ws_bytes, void *stream);
+
+/* k3gpu_decoder_layer_kda_verify over a draft tree (parent DEVICE [T]; NULL: a chain). */
+int k3gpu_decoder_layer_kda_verify_tree(float *h, float *block_residual, int *n_blocks, int *moe_idx,
+                                        float *moe_wt, const K3GpuKdaLayerW *w,
+                                        const K3GpuLayerCfg *c, int layer_idx, const float *state,
+                                        const float *conv_hist, const K3GpuKdaLog *log,
+                                        const int *parent, int B, int T, void *workspace,
+                                        size_t ws_bytes, void *stream);
 
 /* An MLA + MoE decoder layer (K3LayerW with an MLA block): as K3GpuKdaLayerW with the MLA
  * weights in place of the KDA ones. */
@@ -534,8 +569,9 @@ int k3gpu_decoder_layer_mla_verify(float *h, float *block_residual, int *n_block
  * argmax (argmax_, :138-139). The commit replays the first keep[b] logged positions into
  * each KDA layer's state (k3_kda_advance) and advances cached[b]; the MLA rows past it
  * are overwritten by the next sweep, as in the reference. With a draft tree (parents
- * given) the accepted path's log and cache rows are first gathered to the front; the
- * KDA recurrence runs chains only, so a tree needs a model of MLA layers only.
+ * given) the KDA layers follow each node's ancestors (k3gpu_decoder_layer_kda_verify_tree),
+ * the MLA layers the nodes' ancestor masks, and the commit first gathers the accepted
+ * path's log rows and cache rows to the front.
  * Device memory: one caller-owned arena of k3gpu_model_arena_bytes (every KDA layer's
  * state, history and log, every MLA layer's bf16 latent and rope caches of kv_cap
  * positions, the sweep's activations, snapshots, logits [B*max_T][vocab] and the largest

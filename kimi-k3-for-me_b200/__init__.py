@@ -169,6 +169,8 @@ _SIGS = {
     "k3gpu_moe_phase_timing": ([I], I),
     "k3gpu_moe_phase_ms": ([C.POINTER(F), I], I),
     "k3gpu_kda_verify": ([VP, VP, VP, VP, VP, VP, VP, I, I, I, I, F, VP], I),
+    "k3gpu_kda_verify_tree": ([VP] * 8 + [I, I, I, I, F, VP], I),
+    "k3gpu_kda_prologue_tree": ([VP] * 15 + [I, I, I, I, I, F, VP], I),
     "k3gpu_kda_commit": ([VP, VP, VP, VP, VP, VP, I, I, I, I, VP], I),
     "k3gpu_kda_prefill": ([VP] * 7 + [I, I, I, I, F, VP], I),
     "k3gpu_kda_prologue": ([VP] * 14 + [I, I, I, I, I, F, VP], I),
@@ -413,6 +415,16 @@ def kda_verify(state, q, k, v, alpha, beta, qscale, stream=None):
     return o
 
 
+def kda_verify_tree(state, q, k, v, alpha, beta, parent, qscale, stream=None):
+    """k3gpu_kda_verify over a draft tree; parent int32 [T] (device)."""
+    B, T, H, D = q.shape
+    o = torch.empty_like(q)
+    check(lib.k3gpu_kda_verify_tree(ptr(o), ptr(state), ptr(q), ptr(k), ptr(v), ptr(alpha), ptr(beta),
+                                    ptr(parent), B, T, H, D, float(qscale), stream_ptr(stream)),
+          "k3gpu_kda_verify_tree")
+    return o
+
+
 def kda_commit(state, k, v, alpha, beta, n, stream=None):
     B, T, H, D = k.shape
     check(lib.k3gpu_kda_commit(ptr(state), ptr(k), ptr(v), ptr(alpha), ptr(beta), ptr(n), B, T,
@@ -439,6 +451,21 @@ def kda_prologue(q, k, v, z, b, q_conv, k_conv, v_conv, hist, A_log, dt_bias, H,
                                  ptr(b), ptr(q_conv), ptr(k_conv), ptr(v_conv), ptr(hist),
                                  ptr(A_log), ptr(dt_bias), B, T, H, D, K, float(lb),
                                  stream_ptr(stream)), "k3gpu_kda_prologue")
+    return alpha, beta, pre
+
+
+def kda_prologue_tree(q, k, v, z, b, q_conv, k_conv, v_conv, hist, A_log, dt_bias, parent, H, D, K, lb,
+                      stream=None):
+    """k3gpu_kda_prologue with each node's ShortConv window along its ancestors (parent
+    int32 [T] device, or None: the chain)."""
+    B, T, P = q.shape
+    alpha = torch.empty_like(q)
+    beta = torch.empty((B, T, H), dtype=torch.float32, device=q.device)
+    pre = torch.empty((B, T, 3, P), dtype=torch.float32, device=q.device)
+    check(lib.k3gpu_kda_prologue_tree(ptr(q), ptr(k), ptr(v), ptr(alpha), ptr(beta), ptr(pre), ptr(z),
+                                      ptr(b), ptr(q_conv), ptr(k_conv), ptr(v_conv), ptr(hist),
+                                      ptr(A_log), ptr(dt_bias), ptr(parent), B, T, H, D, K, float(lb),
+                                      stream_ptr(stream)), "k3gpu_kda_prologue_tree")
     return alpha, beta, pre
 
 

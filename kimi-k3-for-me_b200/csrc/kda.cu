@@ -114,6 +114,86 @@ __global__ void __launch_bounds__(D) kda_commit_kernel(float *__restrict__ state
     for (int i = 0; i < D; i++) Sh[(size_t)i * D + j] = Sc[i];
 }
 
+// grid (H, B), block D: node t of a draft tree (parent[0] = -1, parent[t] < t) reads the
+// state after its own ancestors. Per node the chain of k3_kda_step over root .. t runs again
+// from the carried state (verify trees are shallow), with the same float operations in the
+// same order as the chain kernel, so every node's output is bit-identical to a chain verify
+// of its ancestor path. parent is a device array [T] shared by the B sequences.
+template <int D>
+__global__ void __launch_bounds__(D) kda_verify_tree_kernel(float *__restrict__ o,
+                                                           const float *__restrict__ state,
+                                                           const float *__restrict__ q,
+                                                           const float *__restrict__ k,
+                                                           const float *__restrict__ v,
+                                                           const float *__restrict__ al,
+                                                           const float *__restrict__ beta,
+                                                           const int *__restrict__ parent, int T,
+                                                           int H, float qscale)
+{
+    __shared__ float sm[3 * D];
+    __shared__ int path[64];
+    __shared__ int plen;
+    const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
+    const float *Sh = state + (((size_t)b * H + h) * D) * D;
+    const size_t rb = (size_t)b * T * H * D;
+    const float *qb = q + rb, *kb = k + rb, *vb = v + rb, *ab = al + rb;
+    const float *bb = beta + (size_t)b * T * H;
+    float *sk = sm, *sq = sm + D, *sa = sm + 2 * D;
+    for (int t = 0; t < T; t++) {
+        __syncthreads();
+        if (j == 0) {   // t, its parent, ..., the root
+            int n = 0, a = t;
+            while (a >= 0 && n < 64) {
+                path[n++] = a;
+                const int pa = parent[a];
+                if (pa >= a || pa < -1) {
+                    flag(DEV_BAD_INDEX);
+                    break;
+                }
+                a = pa;
+            }
+            plen = n;
+        }
+        __syncthreads();
+        float Sc[D];
+#pragma unroll
+        for (int i = 0; i < D; i++) Sc[i] = Sh[(size_t)i * D + j];
+        for (int pi = plen - 1; pi >= 0; pi--) {
+            const int node = path[pi];
+            const size_t off = ((size_t)node * H + h) * D;
+            __syncthreads();
+            sk[j] = kb[off + j];
+            sa[j] = ab[off + j];
+            if (pi == 0) sq[j] = __fmul_rn(qb[off + j], qscale);
+            __syncthreads();
+            const float bt = bb[(size_t)node * H + h];
+#pragma unroll
+            for (int i = 0; i < D; i++) Sc[i] = __fmul_rn(Sc[i], sa[i]);
+            float u = 0.0f;
+#pragma unroll
+            for (int i = 0; i < D; i++) {
+                const float ki = sk[i];
+                if (ki != 0.0f) u = __fadd_rn(u, __fmul_rn(ki, Sc[i]));
+            }
+            const float err = __fsub_rn(vb[off + j], u);
+#pragma unroll
+            for (int i = 0; i < D; i++) {
+                const float ki = sk[i];
+                if (ki != 0.0f) Sc[i] = __fadd_rn(Sc[i], __fmul_rn(__fmul_rn(ki, bt), err));
+            }
+            if (pi == 0) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int i = 0; i < D; i++) {
+                    const float qi = sq[i];
+                    if (qi != 0.0f) acc = __fadd_rn(acc, __fmul_rn(qi, Sc[i]));
+                }
+                o[rb + off + j] = acc;
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ float silu_f(float a) { return a * sigmoid_cr(a); }
 
 // Block-wide double sum over blockDim.x (a multiple of 32, <= 1024) threads.
@@ -138,7 +218,7 @@ __global__ void __launch_bounds__(256) kda_prologue_kernel(
     const float *__restrict__ z, const float *__restrict__ bproj, const float *__restrict__ qc,
     const float *__restrict__ kc, const float *__restrict__ vc, const float *__restrict__ hist,
     const float *__restrict__ A_log, const float *__restrict__ dt_bias, int T, int H, int D,
-    int K, float lb)
+    int K, float lb, const int *__restrict__ parent)
 {
     __shared__ double red[32];
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
@@ -146,16 +226,40 @@ __global__ void __launch_bounds__(256) kda_prologue_kernel(
     float *rows[3] = {q, k, v};
     const float *w[3] = {qc, kc, vc};
     float buf[3][8];
+    float hist0[3][8];
     float wt[3][8];
 #pragma unroll
     for (int m = 0; m < 3; m++) {
-        for (int j = 0; j < hl; j++)
-            buf[m][j] = hist ? hist[(((size_t)b * 3 + m) * P + c) * hl + j] : 0.0f;
+        for (int j = 0; j < hl; j++) {
+            hist0[m][j] = hist ? hist[(((size_t)b * 3 + m) * P + c) * hl + j] : 0.0f;
+            buf[m][j] = hist0[m][j];
+        }
         for (int j = 0; j < K; j++) wt[m][j] = w[m][(size_t)c * K + j];
     }
     const float a = expf_cr(A_log[h]);
     for (int t = 0; t < T; t++) {
         const size_t rc = ((size_t)b * T + t) * P + c;
+        if (parent) {
+            // a draft tree: the window is the node's ancestors (newest first: its parent),
+            // then the carried history, as a chain along the node's own path would see it;
+            // the ancestors' pre-conv rows were written by this thread at earlier t
+            int an = parent[t];
+            int hh = hl - 1;
+            for (int j = hl - 1; j >= 0; j--) {
+                if (an >= 0 && an < t) {
+#pragma unroll
+                    for (int m = 0; m < 3; m++) buf[m][j] = pre[(((size_t)b * T + an) * 3 + m) * P + c];
+                    const int pa = parent[an];
+                    if (pa >= an) flag(DEV_BAD_INDEX);
+                    an = pa < an ? pa : -1;
+                } else {
+#pragma unroll
+                    for (int m = 0; m < 3; m++) buf[m][j] = hist0[m][hh];
+                    hh--;
+                    an = -1;
+                }
+            }
+        }
         float y[3];
 #pragma unroll
         for (int m = 0; m < 3; m++) {
@@ -164,8 +268,10 @@ __global__ void __launch_bounds__(256) kda_prologue_kernel(
             // taps oldest..newest, w[K-1] on the current input (k3_ops.c:185-195)
             float acc = __fmul_rn(wt[m][hl], cur);
             for (int j = 0; j < hl; j++) acc = __fadd_rn(acc, __fmul_rn(wt[m][j], buf[m][j]));
-            for (int j = 0; j + 1 < hl; j++) buf[m][j] = buf[m][j + 1];
-            if (hl > 0) buf[m][hl - 1] = cur;
+            if (!parent) {
+                for (int j = 0; j + 1 < hl; j++) buf[m][j] = buf[m][j + 1];
+                if (hl > 0) buf[m][hl - 1] = cur;
+            }
             y[m] = __fmul_rn(acc, sigmoid_cr(acc));
         }
         // L2 norm of q and k over the head's D channels: SUM of squares, eps 1e-6
@@ -251,6 +357,19 @@ extern "C" int k3gpu_kda_verify(float *o, const float *state, const float *q, co
     return k3::launch_status();
 }
 
+extern "C" int k3gpu_kda_verify_tree(float *o, const float *state, const float *q, const float *k,
+                                     const float *v, const float *alpha, const float *beta, const int *parent,
+                                     int B, int T, int H, int D, float qscale, void *stream)
+{
+    if (!o || !state || !q || !k || !v || !alpha || !beta || !parent) return K3GPU_EINVAL;
+    if (B <= 0 || T <= 0 || T > 64 || H <= 0 || H > 65535 || B > 65535 || !kda_dim_ok(D))
+        return K3GPU_EINVAL;
+    cudaStream_t s = k3::as_stream(stream);
+    dim3 grid(H, B);
+    K3_KDA_DISPATCH(D, kda_verify_tree_kernel, o, state, q, k, v, alpha, beta, parent, T, H, qscale);
+    return k3::launch_status();
+}
+
 extern "C" int k3gpu_kda_commit(float *state, const float *k, const float *v,
                                 const float *alpha, const float *beta, const int *n, int B,
                                 int T, int H, int D, void *stream)
@@ -264,12 +383,12 @@ extern "C" int k3gpu_kda_commit(float *state, const float *k, const float *v,
     return k3::launch_status();
 }
 
-extern "C" int k3gpu_kda_prologue(float *q, float *k, float *v, float *alpha, float *beta,
-                                  float *pre, const float *z, const float *b,
-                                  const float *q_conv, const float *k_conv,
-                                  const float *v_conv, const float *hist, const float *A_log,
-                                  const float *dt_bias, int B, int T, int H, int D, int K,
-                                  float lb, void *stream)
+extern "C" int k3gpu_kda_prologue_tree(float *q, float *k, float *v, float *alpha, float *beta,
+                                       float *pre, const float *z, const float *b,
+                                       const float *q_conv, const float *k_conv,
+                                       const float *v_conv, const float *hist, const float *A_log,
+                                       const float *dt_bias, const int *parent, int B, int T, int H,
+                                       int D, int K, float lb, void *stream)
 {
     if (!q || !k || !v || !alpha || !beta || !pre || !z || !b || !q_conv || !k_conv ||
         !v_conv || !A_log || !dt_bias)
@@ -280,8 +399,19 @@ extern "C" int k3gpu_kda_prologue(float *q, float *k, float *v, float *alpha, fl
     dim3 grid(H, B);
     k3::kda_prologue_kernel<<<grid, D, 0, k3::as_stream(stream)>>>(
         q, k, v, alpha, beta, pre, z, b, q_conv, k_conv, v_conv, hist, A_log, dt_bias, T, H, D,
-        K, lb);
+        K, lb, parent);
     return k3::launch_status();
+}
+
+extern "C" int k3gpu_kda_prologue(float *q, float *k, float *v, float *alpha, float *beta,
+                                  float *pre, const float *z, const float *b,
+                                  const float *q_conv, const float *k_conv,
+                                  const float *v_conv, const float *hist, const float *A_log,
+                                  const float *dt_bias, int B, int T, int H, int D, int K,
+                                  float lb, void *stream)
+{
+    return k3gpu_kda_prologue_tree(q, k, v, alpha, beta, pre, z, b, q_conv, k_conv, v_conv, hist, A_log,
+                                   dt_bias, nullptr, B, T, H, D, K, lb, stream);
 }
 
 extern "C" int k3gpu_kda_commit_conv(float *hist, const float *pre, const int *n, int B, int T,

@@ -317,6 +317,16 @@ extern "C" int k3gpu_kda_layer_verify(float *out, const float *x, const K3GpuKda
                                       const float *conv_hist, const K3GpuKdaLog *log, int B,
                                       int T, void *workspace, size_t ws_bytes, void *stream)
 {
+    return k3gpu_kda_layer_verify_tree(out, x, w, c, state, conv_hist, log, nullptr, B, T, workspace, ws_bytes,
+                                       stream);
+}
+
+extern "C" int k3gpu_kda_layer_verify_tree(float *out, const float *x, const K3GpuKdaW *w,
+                                           const K3GpuLayerCfg *c, const float *state,
+                                           const float *conv_hist, const K3GpuKdaLog *log,
+                                           const int *parent, int B, int T, void *workspace,
+                                           size_t ws_bytes, void *stream)
+{
     using namespace k3;
     if (!out || !x || !w || !cfg_ok(c) || !state || !conv_hist || !log || !workspace) return K3GPU_EINVAL;
     if (!log->k || !log->v || !log->alpha || !log->beta || !log->pre) return K3GPU_EINVAL;
@@ -337,15 +347,18 @@ extern "C" int k3gpu_kda_layer_verify(float *out, const float *x, const K3GpuKda
     if ((st = mm(s.fa, x, w->f_a, E, D))) return st;       // the shared low-rank pair
     if ((st = mm(s.z, s.fa, w->f_b, D, P))) return st;
     // 2-5. ShortConv + SiLU, L2 norm, beta, decay; the pre-conv rows go to the log
-    if ((st = k3gpu_kda_prologue(s.q, log->k, log->v, log->alpha, log->beta, log->pre, s.z, s.bt, w->q_conv,
-                                 w->k_conv, w->v_conv, conv_hist, w->A_log, w->dt_bias, B, T, H, D, c->conv_k,
-                                 c->gate_lb, stream)))
+    // (with a draft tree, along each node's ancestors)
+    if ((st = k3gpu_kda_prologue_tree(s.q, log->k, log->v, log->alpha, log->beta, log->pre, s.z, s.bt, w->q_conv,
+                                      w->k_conv, w->v_conv, conv_hist, w->A_log, w->dt_bias, parent, B, T, H, D,
+                                      c->conv_k, c->gate_lb, stream)))
         return st;
     // 6. the recurrence on the carried state (read only), q scaled by D^-1/2 in float
     const float qscale = 1.0f / sqrtf((float)D);
-    if ((st = k3gpu_kda_verify(s.o, state, s.q, log->k, log->v, log->alpha, log->beta, B, T, H, D, qscale,
-                               stream)))
-        return st;
+    st = parent ? k3gpu_kda_verify_tree(s.o, state, s.q, log->k, log->v, log->alpha, log->beta, parent, B, T, H, D,
+                                        qscale, stream)
+                : k3gpu_kda_verify(s.o, state, s.q, log->k, log->v, log->alpha, log->beta, B, T, H, D, qscale,
+                                   stream);
+    if (st) return st;
     // 7-9. head RMSNorm, then the gate, then the output projection
     if ((st = mm(s.g, x, w->g, E, P))) return st;
     if ((st = k3gpu_kda_norm_gate(s.o, s.g, w->o_norm, R, H, D, c->rms_eps, stream))) return st;
@@ -520,6 +533,17 @@ extern "C" int k3gpu_decoder_layer_kda_verify(float *h, float *block_residual, i
                                               const float *conv_hist, const K3GpuKdaLog *log, int B, int T,
                                               void *workspace, size_t ws_bytes, void *stream)
 {
+    return k3gpu_decoder_layer_kda_verify_tree(h, block_residual, n_blocks, moe_idx, moe_wt, w, c, layer_idx, state,
+                                               conv_hist, log, nullptr, B, T, workspace, ws_bytes, stream);
+}
+
+extern "C" int k3gpu_decoder_layer_kda_verify_tree(float *h, float *block_residual, int *n_blocks,
+                                                   int *moe_idx, float *moe_wt, const K3GpuKdaLayerW *w,
+                                                   const K3GpuLayerCfg *c, int layer_idx, const float *state,
+                                                   const float *conv_hist, const K3GpuKdaLog *log,
+                                                   const int *parent, int B, int T, void *workspace,
+                                                   size_t ws_bytes, void *stream)
+{
     using namespace k3;
     if (!h || !block_residual || !n_blocks || !moe_idx || !moe_wt || !w || !cfg_ok(c) || !layer_common_ok(c) ||
         !workspace)
@@ -529,7 +553,8 @@ extern "C" int k3gpu_decoder_layer_kda_verify(float *h, float *block_residual, i
     LayerWs ws;
     layer_ws_layout(c, B, T, k3gpu_kda_layer_workspace(c, B, T), &ws, static_cast<char *>(workspace));
     auto attn = [&](float *out, const float *in, void *aws, size_t abytes) {
-        return k3gpu_kda_layer_verify(out, in, &w->kda, c, state, conv_hist, log, B, T, aws, abytes, stream);
+        return k3gpu_kda_layer_verify_tree(out, in, &w->kda, c, state, conv_hist, log, parent, B, T, aws, abytes,
+                                           stream);
     };
     return decoder_layer(h, block_residual, n_blocks, moe_idx, moe_wt, w, c, layer_idx, B, T, ws, attn,
                          as_stream(stream), stream);

@@ -138,7 +138,7 @@ struct K3GpuModel {
     std::vector<K3GpuKdaLog> klog;
     std::vector<uint16_t *> lat, rope;
     std::vector<int> slot;          // per layer: its KDA or MLA slot
-    int *cached, *nb, *ids, *keep, *path, *moe_idx, *arg;
+    int *cached, *nb, *ids, *keep, *path, *moe_idx, *arg, *parent_dev;
     float *h, *br, *nrm, *last, *logits, *moe_wt;
     uint64_t *mask;
     char *ws;
@@ -247,6 +247,7 @@ static size_t model_layout(const K3GpuModelCfg *c, int B, int maxT, int cap, K3G
     char *moe_idx = take((size_t)R * l.topk * 4);
     char *moe_wt = take((size_t)R * l.topk * 4);
     char *mask = take((size_t)maxT * 8);
+    char *parent = take((size_t)maxT * 4);
     char *h = take((size_t)R * E * 4);
     char *br = take((size_t)R * l.max_blocks * E * 4);
     char *nrm = take((size_t)R * E * 4);
@@ -256,7 +257,7 @@ static size_t model_layout(const K3GpuModelCfg *c, int B, int maxT, int cap, K3G
     if (m) {
         m->cached = (int *)cached; m->nb = (int *)nb; m->ids = (int *)ids; m->keep = (int *)keep;
         m->path = (int *)path; m->arg = (int *)arg; m->moe_idx = (int *)moe_idx; m->moe_wt = (float *)moe_wt;
-        m->mask = (uint64_t *)mask; m->h = (float *)h; m->br = (float *)br; m->nrm = (float *)nrm;
+        m->mask = (uint64_t *)mask; m->parent_dev = (int *)parent; m->h = (float *)h; m->br = (float *)br; m->nrm = (float *)nrm;
         m->last = (float *)last; m->logits = (float *)logits; m->ws = wsp; m->ws_bytes = ws;
     }
     return o;
@@ -285,16 +286,17 @@ static bool is_chain(const int *parent, int T)
     return true;
 }
 
-// A staging slot: mask [maxT] u64 | keep [B] | path [B*maxT] | ids [B*maxT] | arg [B*maxT].
+// A staging slot: mask [maxT] u64 | keep [B] | path [B*maxT] | ids [B*maxT] | arg [B*maxT] |
+// parent [maxT].
 struct Stage {
     uint64_t *mask;
-    int *keep, *path, *ids, *arg;
+    int *keep, *path, *ids, *arg, *parent;
     int slot;
 };
 
 static size_t stage_slot_bytes(int B, int maxT)
 {
-    return ((size_t)maxT * 8 + ((size_t)B + 3 * (size_t)B * maxT) * 4 + 255) & ~(size_t)255;
+    return ((size_t)maxT * 8 + ((size_t)B + 3 * (size_t)B * maxT + maxT) * 4 + 255) & ~(size_t)255;
 }
 
 // take the next slot once the copies that last read it have run
@@ -310,6 +312,7 @@ static int stage_acquire(K3GpuModel *m, Stage *st)
     st->path = st->keep + m->B;
     st->ids = st->path + (size_t)m->B * m->maxT;
     st->arg = st->ids + (size_t)m->B * m->maxT;
+    st->parent = st->arg + (size_t)m->B * m->maxT;
     st->slot = i;
     return K3GPU_OK;
 }
@@ -329,10 +332,7 @@ static int model_sweep(K3GpuModel *m, const int *ids_dev, int T, const int *pare
     cudaStream_t s = as_stream(m->stream);
     void *sp = m->stream;
     int st;
-    if (!is_chain(parent, T)) {
-        for (int i = 0; i < m->cfg.n_layers; i++)
-            if (!m->is_mla[i]) return K3GPU_EINVAL;   // the KDA recurrence runs chains only
-    }
+    const bool tree = !is_chain(parent, T);
     int max_ctx = 0;
     for (int b = 0; b < B; b++) max_ctx = std::max(max_ctx, m->cached_host[b] + T);
     if (max_ctx > m->cap) return K3GPU_ECAPACITY;
@@ -340,6 +340,11 @@ static int model_sweep(K3GpuModel *m, const int *ids_dev, int T, const int *pare
     if ((st = stage_acquire(m, &sg))) return st;
     if ((st = build_masks(parent, T, sg.mask))) return st;
     if ((st = cuda_status(cudaMemcpyAsync(m->mask, sg.mask, (size_t)T * 8, cudaMemcpyHostToDevice, s)))) return st;
+    if (tree) {   // the KDA layers follow each node's ancestors
+        std::copy(parent, parent + T, sg.parent);
+        if ((st = cuda_status(cudaMemcpyAsync(m->parent_dev, sg.parent, (size_t)T * 4, cudaMemcpyHostToDevice, s))))
+            return st;
+    }
     if ((st = stage_release(m, sg))) return st;
     if (parent) std::copy(parent, parent + T, m->parent_host.begin());
     embed_kernel<<<R, 256, 0, s>>>(m->h, m->w.embed, ids_dev, E, V);
@@ -352,9 +357,9 @@ static int model_sweep(K3GpuModel *m, const int *ids_dev, int T, const int *pare
                                                 m->lat[sl], m->rope[sl], m->cap, m->cached, m->mask, max_ctx, B, T,
                                                 m->ws, m->ws_bytes, sp);
         } else {
-            st = k3gpu_decoder_layer_kda_verify(m->h, m->br, m->nb, m->moe_idx, m->moe_wt, &m->kda[i], &l, i,
-                                                m->kstate[sl], m->khist[sl], &m->klog[sl], B, T, m->ws, m->ws_bytes,
-                                                sp);
+            st = k3gpu_decoder_layer_kda_verify_tree(m->h, m->br, m->nb, m->moe_idx, m->moe_wt, &m->kda[i], &l, i,
+                                                     m->kstate[sl], m->khist[sl], &m->klog[sl],
+                                                     tree ? m->parent_dev : nullptr, B, T, m->ws, m->ws_bytes, sp);
         }
         if (st) return st;
     }

@@ -240,3 +240,45 @@ def test_batched_sequences_are_independent(k3, ckpt, gold):
     assert outs[0] == ref_ids
     assert outs[1] == solo
     assert k3.device_status() == 0
+
+
+def test_tree_sweep_through_kda_and_mla_layers(k3, model, gold):
+    """A draft TREE over the reference's continuation with decoy branches, verified in one
+    sweep through the 3 KDA layers (recurrence and ShortConv along each node's ancestors)
+    and the MLA layer (ancestor masks): the nodes on the true branch carry the reference's
+    serial logits, a decoy node's logits equal a chain sweep of its own path, the on-device
+    greedy tree walk accepts the true branch, and after the path's commit the stream goes on
+    exactly as the reference's."""
+    prompt, y, ref_lg = gold["base/prompt"].tolist(), gold["base/ids"].tolist(), gold["base/logits"]
+    V = model.vocab
+    w = [(y[1] + 11) % V, (y[1] + 23) % V, (y[2] + 5) % V, (y[3] + 7) % V, 3]
+    #        0     1     2     3     4     5     6     7     8
+    tok = [y[0], w[0], y[1], w[1], w[4], y[2], w[2], w[3], y[3]]
+    parent = [-1, 0, 0, 0, 1, 2, 2, 5, 5]
+    model.reset()
+    assert int(model.prefill(ids_dev(prompt)).item()) == y[0]
+    arg, lg = model.verify(ids_dev(tok), parent=parent)
+    for node, ref_row in ((0, 1), (2, 2), (5, 3), (8, 4)):
+        logits_ok(lg[0, node].cpu().numpy(), ref_lg[ref_row], f"true-branch node {node}")
+        assert int(arg[0, node]) == y[ref_row]
+    tree_lg = lg[0].cpu().numpy().copy()
+    # the decoy node 4 (path 0 -> 1 -> 4) against a chain sweep of that path
+    arg_c, lg_c = model.verify(ids_dev([tok[0], tok[1], tok[4]]))
+    got, ref = tree_lg[4].astype(np.float64), lg_c[0, 2].cpu().numpy().astype(np.float64)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-5
+    # the tree again, accepted on the device, and its path committed
+    arg, lg = model.verify(ids_dev(tok), parent=parent)
+    emit, n_emit, path, _ = k3.accept_tree_greedy(lg, ids_dev(tok), torch.tensor(parent, dtype=torch.int32,
+                                                                                    device="cuda"))
+    n = int(n_emit[0])
+    assert n == 4 and emit[0, :n].tolist() == y[1:5]
+    assert path[0, :n].tolist() == [0, 2, 5, 8]
+    model.commit([n], [path[0].tolist()])
+    out = y[:5]
+    for i in range(5, 14):
+        a, lgs = model.verify(ids_dev([out[-1]]))
+        logits_ok(lgs[0, 0].cpu().numpy(), ref_lg[i], f"step {i} after the tree commit")
+        model.commit([1])
+        out.append(int(a[0, 0]))
+    assert out == y[:14]
+    assert k3.device_status() == 0
