@@ -94,20 +94,25 @@ def quant_mxfp4_torch(w):
     return packed, scales.view(R, Cc // 32).contiguous()
 
 
-def make_bank_device(n_experts, L, I, seed, device):
+def make_bank_device(n_experts, L, I, seed, device, chunk=16):
+    """A device MXFP4 bank in the library's run layout, w1/w2/w3 ~ N(0, 0.02) quantised by
+    the reference generator's rule, drawn `chunk` experts at a time (one torch generator
+    seeded with `seed`: w1 of the chunk, then w2, then w3)."""
     import torch
     offs, stride = bank_layout(L, I)
-    bank = torch.empty(n_experts * stride, dtype=torch.uint8, device=device)
+    bank = torch.zeros(n_experts * stride, dtype=torch.uint8, device=device)
+    view = bank.view(n_experts, stride)
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
-    for e in range(n_experts):
-        base = e * stride
+    for e0 in range(0, n_experts, chunk):
+        n = min(chunk, n_experts - e0)
         for (po, so, rows, cols) in ((offs["p1"], offs["s1"], I, L), (offs["p2"], offs["s2"], L, I),
                                      (offs["p3"], offs["s3"], I, L)):
-            w = torch.randn((rows, cols), generator=gen, device=device) * 0.02
-            p, s = quant_mxfp4_torch(w)
-            bank[base + po: base + po + p.numel()] = p.view(-1)
-            bank[base + so: base + so + s.numel()] = s.view(-1)
+            w = torch.randn((n * rows, cols), generator=gen, device=device) * 0.02
+            p, sc = quant_mxfp4_torch(w)
+            view[e0:e0 + n, po:po + rows * cols // 2] = p.view(n, -1)
+            view[e0:e0 + n, so:so + rows * cols // 32] = sc.view(n, -1)
+            del w, p, sc
     return bank, offs, stride
 
 
@@ -119,6 +124,331 @@ def make_inputs(M, seed, device):
     gate = torch.randn((N_ROUTED, L_DIM), generator=gen, device=device) * 0.02
     bias = torch.randn((N_ROUTED,), generator=gen, device=device) * 0.01
     return x.contiguous(), gate.contiguous(), bias.contiguous()
+
+
+# --------------------------------------------------------- config 4: the model slice ----
+# an 8-layer K3-shaped slice (6 KDA + 2 MLA in the 3:1 pattern, d_model
+# 7168, the config-2 MoE in every layer: 384 routed experts top-8 + 1 shared, FFN 2048
+# SwiGLU, MXFP4), MLA 64 heads / q_lora 1536 / kv_lora 512 / rope 64, KDA 32 heads x 128
+# (config 3), vocab 163840, random init; a 64-node draft tree (branching 4, depth 4) over a
+# 32k-position random-filled compressed cache, B sequences, greedy acceptance.
+C4 = {"hidden_size": 7168, "num_hidden_layers": 8, "vocab_size": 163840, "rms_norm_eps": 1e-5,
+      "kda_num_heads": 32, "kda_head_dim": 128, "short_conv_kernel_size": 4, "gate_lower_bound": -5.0,
+      "num_attention_heads": 64, "q_lora_rank": 1536, "kv_lora_rank": 512, "qk_nope_head_dim": 128,
+      "qk_rope_head_dim": 64, "v_head_dim": 128, "mla_use_output_gate": True, "num_experts": 384,
+      "num_experts_per_token": 8, "num_shared_experts": 1, "routed_expert_hidden_size": 7168,
+      "moe_intermediate_size": 2048, "routed_scaling_factor": 1.0, "moe_renormalize": True,
+      "latent_moe_use_norm": False, "first_k_dense_replace": 0, "intermediate_size": 2048,
+      "attn_res_block_size": 2, "situ_beta": 4.0, "situ_linear_beta": 25.0, "full_attn_layers": [4, 8],
+      "moe_form": "plain", "act": "swiglu"}
+C4_CTX = 32768
+C4_TREE, C4_BRANCH, C4_DEPTH = 64, 4, 4
+
+
+def tree_topology(nodes=C4_TREE, branch=C4_BRANCH, depth=C4_DEPTH, weights=(0.5, 0.25, 0.15, 0.10)):
+    """A draft tree's shape as a suffix drafter grows it: best-first by path probability
+    (child c of a node carries weights[c] of its parent's), at most `branch` children and
+    `depth` levels below the root, `nodes` nodes, parents before children. Returns
+    (parent, chain) where chain is the most probable root-to-depth path (node indices)."""
+    import heapq
+    parent, prob, dep = [-1], [1.0], [0]
+    heap, tick = [], 0
+    for c in range(branch):
+        heapq.heappush(heap, (-weights[c], tick, 0, c))
+        tick += 1
+    first_child = {}
+    while len(parent) < nodes and heap:
+        negp, _, par, c = heapq.heappop(heap)
+        i = len(parent)
+        parent.append(par)
+        prob.append(-negp)
+        dep.append(dep[par] + 1)
+        if c == 0:
+            first_child[par] = i
+        if dep[i] < depth:
+            for cc in range(branch):
+                heapq.heappush(heap, (negp * weights[cc], tick, i, cc))
+                tick += 1
+    chain, n = [0], 0
+    while n in first_child:
+        n = first_child[n]
+        chain.append(n)
+    return parent, chain
+
+
+def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE):
+    """The config-4 slice on the device with random weights: bf16 projections N(0, 0.02),
+    unit norms, AttnRes folds N(0, 0.02), router N(0, 0.02) with bias N(0, 0.01), the KDA
+    decay parameters of the reference's tiny-model recipe, MXFP4 experts N(0, 0.02)."""
+    import torch
+    c = C4
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    E, V = c["hidden_size"], c["vocab_size"]
+    H, D, K = c["kda_num_heads"], c["kda_head_dim"], c["short_conv_kernel_size"]
+    P = H * D
+    Hm, ql, kvl = c["num_attention_heads"], c["q_lora_rank"], c["kv_lora_rank"]
+    nope, rope, vh = c["qk_nope_head_dim"], c["qk_rope_head_dim"], c["v_head_dim"]
+    n, I_ = c["num_experts"], c["moe_intermediate_size"]
+
+    def bf(*shape):
+        return (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16).view(torch.int16)
+
+    def f32(*shape, std=0.02):
+        return torch.randn(shape, generator=g, device=dev) * std
+
+    def ones(k):
+        return torch.ones(k, device=dev)
+
+    layers, banks = [], []
+    for L in range(c["num_hidden_layers"]):
+        mla = (L + 1) in c["full_attn_layers"]
+        d = {"kind": "mla" if mla else "kda", "in_norm": ones(E), "post_norm": ones(E),
+             "attn_res_fold": f32(E), "mlp_res_fold": f32(E), "gate_W": f32(n, E),
+             "gate_bias": f32(n, std=0.01)}
+        if mla:
+            d.update(q_a=bf(ql, E), q_a_norm=ones(ql), q_b=bf(Hm * (nope + rope), ql), kv_a=bf(kvl + rope, E),
+                     kv_a_norm=ones(kvl), kv_b=f32(Hm * (nope + vh), kvl), o=bf(E, Hm * vh), g=bf(Hm * vh, E))
+        else:
+            d.update(q=bf(P, E), k=bf(P, E), v=bf(P, E), g=bf(P, E), o=bf(E, P), f_a=bf(D, E), f_b=bf(P, D),
+                     b=bf(H, E), q_conv=f32(P, K, std=0.4), k_conv=f32(P, K, std=0.4), v_conv=f32(P, K, std=0.4),
+                     A_log=torch.linspace(-0.4, 1.2, H, device=dev), dt_bias=f32(P, std=0.5), o_norm=ones(D))
+        layers.append(d)
+        bank, _, _ = make_bank_device(n + c["num_shared_experts"], E, I_, seed + 1000 + L, dev)
+        kb = k3.ExpertBank(bank, n + c["num_shared_experts"], E, I_)
+        kb.scan()
+        banks.append(kb)
+    top = {"embed": bf(V, E), "lm_head": bf(V, E), "norm": ones(E), "out_res_fold": f32(E)}
+    return k3.Model(dict(c), layers, top, banks, B=B, max_T=max_T, kv_cap=kv_cap, device=dev)
+
+
+def c4_fill_state(model, seed, ctx):
+    """A long conversation's state: KDA states N(0, 0.1) (config 3), ShortConv histories
+    N(0, 1), ctx random bf16 N(0, 1) cache rows per sequence in every MLA layer."""
+    import torch
+    g = torch.Generator(device=model.device)
+    g.manual_seed(seed)
+    for L in range(model.cfg["num_hidden_layers"]):
+        if (L + 1) in model.cfg["full_attn_layers"]:
+            lat, rope = model.mla_cache(L)
+            lat[:, :ctx].copy_(torch.randn(lat[:, :ctx].shape, generator=g, device=model.device)
+                               .to(torch.bfloat16).view(torch.int16))
+            rope[:, :ctx].copy_(torch.randn(rope[:, :ctx].shape, generator=g, device=model.device)
+                                .to(torch.bfloat16).view(torch.int16))
+        else:
+            st, hi = model.kda_state(L)
+            st.copy_(torch.randn(st.shape, generator=g, device=model.device) * 0.1)
+            hi.copy_(torch.randn(hi.shape, generator=g, device=model.device))
+    model.set_cached([ctx] * model.B)
+
+
+def c4_snapshot(model):
+    snap = []
+    for L in range(model.cfg["num_hidden_layers"]):
+        if (L + 1) not in model.cfg["full_attn_layers"]:
+            st, hi = model.kda_state(L)
+            snap.append((st.clone(), hi.clone()))
+    return snap
+
+
+def c4_restore(model, snap, ctx):
+    i = 0
+    for L in range(model.cfg["num_hidden_layers"]):
+        if (L + 1) not in model.cfg["full_attn_layers"]:
+            st, hi = model.kda_state(L)
+            st.copy_(snap[i][0])
+            hi.copy_(snap[i][1])
+            i += 1
+    model.set_cached([ctx] * model.B)
+
+
+def c4_trees(cont, parent, chain, steps, V, seed):
+    """Per step and sequence the tree's ids: node 0 the pending id, the most probable branch
+    the model's own next ids (cont, from an untimed serial run), every other node a random id
+    that differs from its siblings on the branch -- the reference's GATE-4 way of forcing
+    drafts (tests/unit/k3_model.c:359-462), since a random-weight model gives an n-gram
+    drafter nothing to match. Assumes full acceptance: step s starts at cont[s*(depth+1)-1]."""
+    rng = np.random.default_rng(seed)
+    B = len(cont)
+    T = len(parent)
+    depth = len(chain) - 1
+    tok = rng.integers(0, V, size=(steps, B, T)).astype(np.int32)
+    on_chain = {node: j for j, node in enumerate(chain)}
+    for s in range(steps):
+        base = s * (depth + 1)
+        for b in range(B):
+            for j, node in enumerate(chain):
+                tok[s, b, node] = cont[b][base + j]
+            for i in range(1, T):
+                p = parent[i]
+                if p in on_chain and i not in on_chain:
+                    nxt = on_chain[p] + 1
+                    if nxt < len(chain) and tok[s, b, i] == tok[s, b, chain[nxt]]:
+                        tok[s, b, i] = (tok[s, b, i] + 1) % V
+    return tok
+
+
+def run_c4(args, k3, dev, local):
+    """The headline: tree verification steps on the config-4 slice at B sequences. A step is
+    one verify sweep of every sequence's 64-node tree through the 8 layers and the lm_head
+    (k3gpu_model_verify), the on-device greedy tree walk (k3gpu_accept_tree_greedy), the
+    read of the accepted paths and the commit (k3gpu_model_commit: KDA log replay, MLA rows
+    gathered, cached advanced). Accepted tok/s counts every id a step emits (accepted
+    drafts plus the bonus id), over all sequences."""
+    import torch
+    B, steps, warm = args.c4_B, args.steps, args.warmup
+    kv_cap = C4_CTX + (steps + warm + 2) * (C4_DEPTH + 1) + C4_TREE + 8
+    t_build = time.perf_counter()
+    model = make_c4_model(k3, dev, B, args.seed, kv_cap)
+    build_s = time.perf_counter() - t_build
+    parent, chain = tree_topology()
+    parent_dev = torch.tensor(parent, dtype=torch.int32, device=dev)
+    V = C4["vocab_size"]
+    c4_fill_state(model, args.seed + 1, C4_CTX)
+    snap = c4_snapshot(model)
+    # the model's own greedy continuation from a random pending id (untimed, one position per
+    # sweep), so the trees' most probable branch can carry it
+    depth = len(chain) - 1
+    n_cont = (steps + warm + 2) * (depth + 1) + 1
+    rng = np.random.default_rng(args.seed + 2)
+    x = torch.tensor(rng.integers(0, V, size=(B, 1)), dtype=torch.int32, device=dev)
+    cont = [[int(x[b, 0])] for b in range(B)]
+    for _ in range(n_cont):
+        arg, _ = model.verify(x)
+        model.commit([1] * B)
+        x = arg[:, :1].contiguous()
+        for b in range(B):
+            cont[b].append(int(x[b, 0]))
+    c4_restore(model, snap, C4_CTX)
+    tok = c4_trees(cont, parent, chain, warm + steps, V, args.seed + 3)
+    tok_dev = torch.from_numpy(tok).to(dev)
+    stream = torch.cuda.current_stream()
+    n_path_host = torch.empty((B,), dtype=torch.int32).pin_memory()
+    path_host = torch.empty((B, C4_TREE), dtype=torch.int32).pin_memory()
+
+    def step(s, ids):
+        _, lg = model.verify(ids, parent=parent)
+        emit, n_emit, path, _ = k3.accept_tree_greedy(lg, ids, parent_dev)
+        n_path_host.copy_(n_emit, non_blocking=True)
+        path_host.copy_(path, non_blocking=True)
+        stream.synchronize()
+        keep = n_path_host.tolist()
+        model.commit(keep, path_host.tolist())
+        return sum(keep), emit
+
+    accepted = 0
+    for s in range(warm):
+        step(s, tok_dev[s])
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    l0 = k3.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(warm, warm + steps):
+        a, _ = step(s, tok_dev[s])
+        accepted += a
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = k3.launch_count() - l0
+    dev_ms = e0.elapsed_time(e1) / steps
+    status = k3.device_status(dev.index)
+
+    # end to end through the public calls with host buffers: each step's tree ids from pinned
+    # host memory, the emitted ids and their count back to the host
+    c4_restore(model, snap, C4_CTX)
+    tok_host = torch.from_numpy(tok).pin_memory()
+    ids_dev = torch.empty((B, C4_TREE), dtype=torch.int32, device=dev)
+    emit_host = torch.empty((B, C4_TREE), dtype=torch.int32).pin_memory()
+    for s in range(warm):
+        ids_dev.copy_(tok_host[s], non_blocking=True)
+        step(s, ids_dev)
+    acc_e2e = 0
+    e0.record(stream)
+    for s in range(warm, warm + steps):
+        ids_dev.copy_(tok_host[s], non_blocking=True)
+        a, emit = step(s, ids_dev)
+        emit_host.copy_(emit, non_blocking=True)
+        acc_e2e += a
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / steps
+    clk = clocks.stop()
+
+    # the phases of one step (verify, accept + path read, commit) and the dominant kernel:
+    # the gate/up expert stream of the last layer's MoE call, its bytes from that call's
+    # unique experts (all 384 at 16 x 64 tokens)
+    c4_restore(model, snap, C4_CTX)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ph_steps, moe_ph = [], []
+    k3.moe_phase_timing(True)
+    for s in range(warm):
+        ev[0].record(stream)
+        _, lg = model.verify(tok_dev[s], parent=parent)
+        ev[1].record(stream)
+        emit, n_emit, path, _ = k3.accept_tree_greedy(lg, tok_dev[s], parent_dev)
+        keep = n_emit.tolist()
+        ph_path = path.tolist()
+        ev[2].record(stream)
+        moe_ph.append(k3.moe_phase_ms())
+        idx_last = model.last_routing(C4_TREE).cpu().numpy()
+        model.commit(keep, ph_path)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        ph_steps.append([ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])])
+    k3.moe_phase_timing(False)
+    ph = np.median(np.array(ph_steps), axis=0).tolist()
+    mph = np.median(np.array(moe_ph), axis=0).tolist()
+    R = B * C4_TREE
+    E, I_, n_exp = C4["hidden_size"], C4["moe_intermediate_size"], C4["num_experts"]
+    u = len(np.unique(idx_last[idx_last >= 0])) + C4["num_shared_experts"]
+    pairs = R * (TOPK + C4["num_shared_experts"])
+    w13 = 2 * I_ * (E // 2 + E // 32)
+    gateup_bytes = u * w13 + R * E * 4 + pairs * I_ * 4
+    hbm, peak_kind = peaks()
+    achieved = gateup_bytes / (mph[2] * 1e-3) / 1e9 if mph[2] > 0 else 0.0
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
+    if os.path.exists(tp):
+        try:
+            ratio = float(json.load(open(tp))["traffic_over_algorithmic"])
+            traffic = int(ratio * gateup_bytes)
+        except (OSError, ValueError, KeyError, TypeError):
+            traffic = None
+    model.close()
+    del model
+    torch.cuda.empty_cache()
+    full = steps * B * (depth + 1)
+    return {
+        "value": round(accepted / (dev_ms * steps * 1e-3), 2), "ms_per_step": round(dev_ms, 3),
+        "accepted_per_step": round(accepted / steps, 2), "accepted_fraction_of_planted": round(accepted / full, 4),
+        "e2e": {"value": round(acc_e2e / (e2e_ms * steps * 1e-3), 2), "unit": "accepted tok/s",
+                "h2d_bytes_per_step": int(B * C4_TREE * 4), "d2h_bytes_per_step": int(B * 4 + 2 * B * C4_TREE * 4),
+                "ms_per_step": round(e2e_ms, 3)},
+        "verify_step_ms": round(ph[0], 3), "accept_ms": round(ph[1], 3), "commit_ms": round(ph[2], 3),
+        "moe_phase_ms_last_layer": {"router": round(mph[0], 4), "plan": round(mph[1], 4),
+                                    "gateup": round(mph[2], 4), "down": round(mph[3], 4),
+                                    "combine": round(mph[4], 4)},
+        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<0> (gate/up, last layer's MoE call)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(gateup_bytes),
+                     "units": f"{u} experts x {w13} B + rows"},
+        "gpu_launches": int(launches), "device_status": status, "clocks": clk, "build_s": round(build_s, 1),
+        "config": {"workload": f"K3 8-layer slice tree verify (benchmark config 4): B={B} sequences x "
+                               f"{C4_TREE}-node draft tree (branching {C4_BRANCH}, depth {C4_DEPTH}) over a "
+                               f"{C4_CTX}-position cache, greedy acceptance",
+                   "layers": "6 KDA + 2 MLA (3:1), every layer MoE", "d_model": E, "vocab": V,
+                   "moe": "384 routed top-8 + 1 shared, FFN 2048 SwiGLU, MXFP4 (E2M1 + E8M0/32) N(0,0.02)",
+                   "kda": "32 heads x 128", "mla": "64 heads, q_lora 1536, kv_lora 512, nope 128, rope 64, v 128",
+                   "B": B, "tree_nodes": C4_TREE, "tokens_verified_per_step": R, "context": C4_CTX,
+                   "drafts": "forced: each tree's most probable branch (depth 4) is the model's own greedy "
+                             "continuation from an untimed serial run, the other 59 nodes random ids (the "
+                             "reference's GATE-4 method; a random-weight model gives the n-gram drafter nothing "
+                             "to match)",
+                   "weights": "random init: bf16 projections N(0,0.02), MXFP4 experts N(0,0.02)",
+                   "l2": "weights streamed per step (~75 GB) exceed the 126 MB L2; no flush needed"},
+    }
 
 
 def unique_experts_bytes(idx_np, stride_bytes_per_expert):
@@ -530,10 +860,13 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
         return {"us": round(us, 2), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4),
                 "bound": "hbm", "shape": shape}
 
-    # c3 KDA verify + commit: 8 sequences x (1+k = 9), 32 heads x 128
-    if only is None or only == "kda_c3":
+    # c3 KDA verify + commit: 8 sequences x (1+k) for k = 4, 8, 16, 32 heads x 128, and a
+    # rollback to an accepted length drawn U[0, k] per sequence
+    for kk_ in (4, 8, 16):
+        if only is not None and only != "kda_c3":
+            break
         try:
-            B, T, H, D = 8, 9, 32, 128
+            B, T, H, D = 8, 1 + kk_, 32, 128
             st = torch.randn((B, H, D, D), generator=g, device=dev) * 0.1
             q = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
             kk = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
@@ -543,27 +876,29 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
             qs = 1.0 / D ** 0.5
             us = timed(lambda: k3.kda_verify(st, q, kk, v, al, be, qs))
             nbytes = st.numel() * 4 + 4 * q.numel() * 4 + be.numel() * 4 + q.numel() * 4
-            rows["kda_verify_c3"] = hbm_row(us, nbytes, "B=8 T=9 H=32 D=128")
-            try:   # the reference's k3_kda_step chain over the same 72 positions x 32 heads
+            rows[f"kda_verify_c3_k{kk_}"] = hbm_row(us, nbytes, f"B=8 T={T} H=32 D=128")
+            try:   # the reference's k3_kda_step chain over the same B*T positions x 32 heads
                 cb = kda_prefill_cpu_baseline(T_sample=B * T, H=H, D=D)
                 if cb is not None:
                     cb = dict(cb, value=round(B * T / cb["value"] * 1e6, 1), unit="us per call")
-                rows["kda_verify_c3"]["cpu_baseline"] = cb
+                rows[f"kda_verify_c3_k{kk_}"]["cpu_baseline"] = cb
             except Exception as ex:  # noqa: BLE001 -- the baseline must not cost the row
-                rows["kda_verify_c3"]["cpu_baseline"] = {"error": str(ex)[:120]}
-            n = torch.full((B,), 5, dtype=torch.int32, device=dev)
+                rows[f"kda_verify_c3_k{kk_}"]["cpu_baseline"] = {"error": str(ex)[:120]}
+            keep = np.random.default_rng(kk_).integers(0, kk_ + 1, size=B).astype(np.int32)
+            n = torch.from_numpy(keep).to(dev)
             sc = st.clone()
             us = timed(lambda: k3.kda_commit(sc, kk, v, al, be, n))
-            rows["kda_commit_c3"] = hbm_row(us, 2 * st.numel() * 4 + 3 * q.numel() * 4 + be.numel() * 4,
-                                            "B=8 T=9 H=32 D=128, keep 5")
+            rows[f"kda_commit_c3_k{kk_}"] = hbm_row(
+                us, 2 * st.numel() * 4 + 3 * q.numel() * 4 + be.numel() * 4,
+                f"B=8 T={T} H=32 D=128, keep U[0,{kk_}] per sequence: {keep.tolist()}")
         except Exception as ex:  # noqa: BLE001
-            rows["kda_c3"] = {"error": str(ex)[:200]}
+            rows[f"kda_c3_k{kk_}"] = {"error": str(ex)[:200]}
 
-    # KDA prompt read-in: one 4096-position prompt, 32 heads x 128, chunked (one launch)
-    # against the sequential kernels (verify + commit per 64 positions, 128 launches)
+    # KDA prompt read-in (config 3's prefill): one 8192-position prompt, 32 heads x 128,
+    # chunked (one launch) against the sequential kernels (verify + commit per 64 positions)
     if only is None or only == "kda_prefill":
         try:
-            B, T, H, D = 1, 4096, 32, 128
+            B, T, H, D = 1, 8192, 32, 128
             st = torch.randn((B, H, D, D), generator=g, device=dev) * 0.1
             q = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
             kk = torch.nn.functional.normalize(torch.randn((B, T, H, D), generator=g, device=dev), dim=-1)
@@ -583,14 +918,14 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
                     k3.kda_commit(ss, bk, bv, ba, bb, n64)
             us_seq = timed(sequential, n=3)
             nbytes = 5 * q.numel() * 4 + be.numel() * 4 + 2 * st.numel() * 4
-            row = hbm_row(us, nbytes, "B=1 T=4096 H=32 D=128 (one prompt)")
+            row = hbm_row(us, nbytes, "B=1 T=8192 H=32 D=128 (one prompt), 32-position chunks")
             row.update({"positions_per_s": round(B * T / (us * 1e-6), 1), "sequential_us": round(us_seq, 2),
                         "speedup_vs_sequential": round(us_seq / us, 2), "compute": "fp32 CUDA cores"})
             try:
                 row["cpu_baseline"] = kda_prefill_cpu_baseline(H=H, D=D)
             except Exception as ex:  # noqa: BLE001 -- the baseline must not cost the row
                 row["cpu_baseline"] = {"error": str(ex)[:120]}
-            rows["kda_prefill_4k"] = row
+            rows["kda_prefill_8k"] = row
         except Exception as ex:  # noqa: BLE001
             rows["kda_prefill"] = {"error": str(ex)[:200]}
 
@@ -678,6 +1013,124 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
     return rows
 
 
+def measure_c2(args, k3, dev, kb, bank, offs, stride, M, seed, n_unsafe, cpu_tokens=0):
+    """One config-2 point: the MoE layer over M = B(1+k) verify tokens, device-timed, end to
+    end with host buffers, the gate/up stream's roofline and (cpu_tokens > 0) the reference's
+    kernels on a sample of the same step."""
+    import torch
+    x, gate, bias = make_inputs(M, seed, dev)
+    ws = k3.workspace(k3.lib.k3gpu_moe_workspace(M, TOPK, N_SHARED, L_DIM, I_DIM, N_ROUTED), dev)
+    out = torch.empty((M, L_DIM), dtype=torch.float32, device=dev)
+    idx = torch.empty((M, TOPK), dtype=torch.int32, device=dev)
+    wt = torch.empty((M, TOPK), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        k3.moe_layer(x, gate, bias, kb, TOPK, N_ROUTED, N_SHARED, k3.ACT_SWIGLU, ws=ws, out=out,
+                     idx=idx, wt=wt, stream=stream)
+
+    steps = max(args.steps // 2, 5)
+    for _ in range(3):
+        step()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    l0 = k3.launch_count()
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = (k3.launch_count() - l0) // steps
+    dev_ms = ev0.elapsed_time(ev1) / steps
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((M, L_DIM), dtype=torch.float32).pin_memory()
+    idx_host = torch.empty((M, TOPK), dtype=torch.int32).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        k3.moe_layer(x_dev, gate, bias, kb, TOPK, N_ROUTED, N_SHARED, k3.ACT_SWIGLU, ws=ws,
+                     out=out, idx=idx, wt=wt, stream=stream)
+        out_host.copy_(out, non_blocking=True)
+        idx_host.copy_(idx, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / steps
+    k3.moe_phase_timing(True)
+    phases = []
+    for _ in range(5):
+        step()
+        phases.append(k3.moe_phase_ms())
+    k3.moe_phase_timing(False)
+    ph = np.median(np.array(phases), axis=0).tolist()
+    idx_np = idx.cpu().numpy()
+    u = len(np.unique(idx_np)) + N_SHARED
+    pairs = M * (TOPK + N_SHARED)
+    w13 = 2 * I_DIM * (L_DIM // 2 + L_DIM // 32)
+    w2 = L_DIM * (I_DIM // 2 + I_DIM // 32)
+    gateup_bytes = u * w13 + M * L_DIM * 4 + pairs * I_DIM * 4
+    down_bytes = u * w2 + pairs * I_DIM * 4 + pairs * L_DIM * 4
+    hbm, peak_kind = peaks()
+    achieved = gateup_bytes / (ph[2] * 1e-3) / 1e9
+    expert_gbs = (gateup_bytes + down_bytes) / ((ph[2] + ph[3]) * 1e-3) / 1e9
+    row = {"M": M, "tokens_per_expert": round(M * TOPK / N_ROUTED, 2), "tok_s": round(M / (dev_ms * 1e-3), 1),
+           "ms": round(dev_ms, 4), "e2e_tok_s": round(M / (e2e_ms * 1e-3), 1), "e2e_ms": round(e2e_ms, 4),
+           "gateup": {"ms": round(ph[2], 4), "bytes": int(gateup_bytes), "gbs": round(achieved, 1),
+                      "frac_hbm": round(achieved / hbm, 4)},
+           "expert_stream": {"gbs": round(expert_gbs, 1), "frac_hbm": round(expert_gbs / hbm, 4),
+                             "unique_experts": u},
+           "phase_ms": {"router": round(ph[0], 4), "plan": round(ph[1], 4), "gateup": round(ph[2], 4),
+                        "down": round(ph[3], 4), "combine": round(ph[4], 4)},
+           "gpu_launches_per_step": int(launches)}
+    if cpu_tokens > 0:
+        Ts = min(M, cpu_tokens)
+        bank_np = bank.cpu().numpy()
+        r = cpu_reference_run(x.cpu().numpy(), gate.cpu().numpy(), bias.cpu().numpy(), bank_np,
+                              offs, stride, Ts, host_threads())
+        del bank_np
+        if r is not None:
+            dt, ref_out, ref_idx = r
+            got = out.cpu().numpy()[:Ts]
+            row["cpu_baseline"] = {
+                "value": round(Ts / dt, 3), "unit": "tok/s", "cores": host_threads(), "kind": "reference",
+                "isa": "x86-64-v3 (AVX2 + FMA), no OpenMP: pthreads over (token, slot) items",
+                "sample": f"{Ts} of {M} tokens of the same step through the reference's k3_router + "
+                          f"k3_matmul_mxfp4 expert loop ({dt:.2f} s)",
+                "routing_bitexact": bool(np.array_equal(ref_idx, idx_np[:Ts])),
+                "out_rel_l2_vs_gpu": float(np.linalg.norm(got - ref_out) / max(np.linalg.norm(ref_out), 1e-30))}
+    return row
+
+
+C2_SWEEP = [(1, 4), (1, 8), (1, 16), (8, 4), (8, 8), (8, 16), (64, 4), (64, 8), (64, 16)]
+
+
+def c2_rows(args, k3, dev):
+    """BASELINE config 2 at every (B, k): M = B(1+k) in {5, 9, 17, 40, 72, 136, 320, 576, 1088}."""
+    import torch
+    bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, dev)
+    kb = k3.ExpertBank(bank, N_ROUTED + N_SHARED, L_DIM, I_DIM)
+    n_unsafe = kb.scan() if not args.no_tc else None
+    out = {}
+    for B, k in C2_SWEEP:
+        M = B * (1 + k)
+        try:
+            cpu = args.cpu_tokens if (not args.no_cpu and (B, k) == (8, 8)) else 0
+            out[f"B{B}_k{k}"] = measure_c2(args, k3, dev, kb, bank, offs, stride, M, args.seed + 1, n_unsafe, cpu)
+        except Exception as ex:  # noqa: BLE001 -- one failed point must not cost the others
+            out[f"B{B}_k{k}"] = {"M": M, "error": str(ex)[:200]}
+    out["expert_kernels"] = "mma.sync" if args.no_tc else f"tcgen05 ({n_unsafe} experts on mma.sync)"
+    del kb, bank
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args):
     import torch
     k3 = load_pkg()
@@ -695,148 +1148,45 @@ def run_b200(args):
         finally:
             dist.destroy_process_group()
 
-    M = args.B * (1 + args.k)
-    bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, dev)
-    x, gate, bias = make_inputs(M, args.seed + 1, dev)
-    kb = k3.ExpertBank(bank, N_ROUTED + N_SHARED, L_DIM, I_DIM)
-    n_unsafe = kb.scan() if not args.no_tc else None   # certify experts for the tcgen05 kernels
-    ws = k3.workspace(k3.lib.k3gpu_moe_workspace(M, TOPK, N_SHARED, L_DIM, I_DIM, N_ROUTED), dev)
-    out = torch.empty((M, L_DIM), dtype=torch.float32, device=dev)
-    idx = torch.empty((M, TOPK), dtype=torch.int32, device=dev)
-    wt = torch.empty((M, TOPK), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream()
-
-    def step():
-        k3.moe_layer(x, gate, bias, kb, TOPK, N_ROUTED, N_SHARED, k3.ACT_SWIGLU, ws=ws, out=out,
-                     idx=idx, wt=wt, stream=stream)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    dev_ms = ev0.elapsed_time(ev1) / args.steps
-
-    # end to end through the public call with host buffers
-    x_host = x.cpu().pin_memory()
-    out_host = torch.empty((M, L_DIM), dtype=torch.float32).pin_memory()
-    idx_host = torch.empty((M, TOPK), dtype=torch.int32).pin_memory()
-    x_dev = torch.empty_like(x)
-
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        k3.moe_layer(x_dev, gate, bias, kb, TOPK, N_ROUTED, N_SHARED, k3.ACT_SWIGLU, ws=ws,
-                     out=out, idx=idx, wt=wt, stream=stream)
-        out_host.copy_(out, non_blocking=True)
-        idx_host.copy_(idx, non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = ev0.elapsed_time(ev1) / args.steps
-    clk = clocks.stop()
-
-    # roofline of the dominant kernel (gate/up expert stream), timed live with events
-    k3.moe_phase_timing(True)
-    phases = []
-    for _ in range(max(3, min(args.steps, 10))):
-        step()
-        phases.append(k3.moe_phase_ms())
-    k3.moe_phase_timing(False)
-    ph = np.median(np.array(phases), axis=0).tolist()
-    idx_np = idx.cpu().numpy()
-    u_routed = len(np.unique(idx_np))
-    u = u_routed + N_SHARED
-    pairs = M * (TOPK + N_SHARED)
-    w13 = 2 * I_DIM * (L_DIM // 2 + L_DIM // 32)
-    w2 = L_DIM * (I_DIM // 2 + I_DIM // 32)
-    gateup_bytes = u * w13 + M * L_DIM * 4 + pairs * I_DIM * 4
-    down_bytes = u * w2 + pairs * I_DIM * 4 + pairs * L_DIM * 4
     hbm, peak_kind = peaks()
-    achieved = gateup_bytes / (ph[2] * 1e-3) / 1e9
-    expert_gbs = (gateup_bytes + down_bytes) / ((ph[2] + ph[3]) * 1e-3) / 1e9
-    # ncu DRAM bytes of the gate/up kernel over its algorithmic bytes, from a capture of a
-    # smaller case (profiles/), applied to this launch's algorithmic bytes
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
-    if os.path.exists(tp):
-        try:
-            ratio = float(json.load(open(tp))["traffic_over_algorithmic"])
-            traffic = int(ratio * gateup_bytes)
-        except (OSError, ValueError, KeyError, TypeError):
-            traffic = None
-
-    # CPU baseline: the reference's kernels on a bounded sample of the same workload
-    cpu = None
-    if not args.no_cpu:
-        Ts = min(M, args.cpu_tokens)
-        bank_np = bank.cpu().numpy()
-        r = cpu_reference_run(x.cpu().numpy(), gate.cpu().numpy(), bias.cpu().numpy(), bank_np,
-                              offs, stride, Ts, host_threads())
-        del bank_np
-        if r is not None:
-            dt, ref_out, ref_idx = r
-            got = out.cpu().numpy()[:Ts]
-            same_idx = bool(np.array_equal(ref_idx, idx_np[:Ts]))
-            err = float(np.linalg.norm(got - ref_out) / max(np.linalg.norm(ref_out), 1e-30))
-            cpu = {"value": round(Ts / dt, 3), "unit": "tok/s", "cores": host_threads(),
-                   "kind": "reference",
-                   "sample": f"{Ts} of {M} tokens of the same step through the reference's k3_router + "
-                             f"k3_matmul_mxfp4 expert loop ({dt:.2f} s)",
-                   "routing_bitexact": same_idx, "out_rel_l2_vs_gpu": err}
-
-    rows = None if args.no_rows else measure_rows(k3, dev, hbm, peaks_tensor())
-
+    rows = {}
+    if not args.no_rows:
+        rows["moe_layer_c2"] = c2_rows(args, k3, dev)
+        rows.update(measure_rows(k3, dev, hbm, peaks_tensor()))
+    c4 = run_c4(args, k3, dev, local)
+    cpu = None if args.no_cpu else c4_cpu_baseline(args)
     line = {
-        "metric": METRIC, "value": round(M / (dev_ms * 1e-3), 3), "unit": "tok/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms, 4),
+        "metric": METRIC, "value": c4["value"], "unit": "accepted tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": c4["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "MXFP4 weights x fp32 activations, fp32 accumulate", "data": "synthetic (seeded)",
-        "config": workload_config(args, M),
-        "e2e": {"value": round(M / (e2e_ms * 1e-3), 3), "unit": "tok/s",
-                "h2d_bytes_per_step": int(x.numel() * 4),
-                "d2h_bytes_per_step": int(out.numel() * 4 + idx.numel() * 4), "ms_per_step": round(e2e_ms, 4)},
-        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<0> (gate/up)", "achieved": round(achieved, 1),
-                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "traffic": traffic, "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": int(gateup_bytes)},
-        "expert_gemm": {"gbs": round(expert_gbs, 1), "frac": round(expert_gbs / hbm, 4),
-                        "unique_experts": u, "bytes": int(gateup_bytes + down_bytes)},
-        "phase_ms": {"router": round(ph[0], 4), "plan": round(ph[1], 4), "gateup": round(ph[2], 4),
-                     "down": round(ph[3], 4), "combine": round(ph[4], 4)},
-        # router 2 + plan, pack, gate/up, act pack, down, combine (+2 for the mma.sync
-        # kernels when the scan left experts to them)
-        "gpu_launches": (8 + (2 if n_unsafe else 0)) * args.steps,
-        "expert_kernels": "mma.sync" if args.no_tc else f"tcgen05 ({n_unsafe} experts on mma.sync)",
-        "clocks": clk,
-        "cpu_baseline": cpu,
-        "rows": rows,
+        "dtype": "MXFP4 experts and bf16 projections x fp32 activations, fp32 accumulate",
+        "data": "synthetic (seeded random weights, random 32k cache, forced drafts)",
+        "config": c4["config"], "e2e": c4["e2e"], "roofline": c4["roofline"],
+        "verify_step_ms": c4["verify_step_ms"], "accept_ms": c4["accept_ms"], "commit_ms": c4["commit_ms"],
+        "accepted_per_step": c4["accepted_per_step"],
+        "accepted_fraction_of_planted": c4["accepted_fraction_of_planted"],
+        "moe_phase_ms_last_layer": c4["moe_phase_ms_last_layer"],
+        "gpu_launches": c4["gpu_launches"], "device_status": c4["device_status"],
+        "clocks": c4["clocks"], "cpu_baseline": cpu, "build_s": c4["build_s"], "rows": rows,
     }
     print(json.dumps(line))
     return 0
+
+
+def c4_cpu_baseline(args):
+    """Filled in by the reference's own decoder layer on the host (oracle/ref_slice_bench.c)."""
+    return None
 
 
 def main():
     global N_ROUTED
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--B", type=int, default=8, help="sequences per GPU")
+    ap.add_argument("--B", type=int, default=8, help="sequences per GPU (config-2 layer runs)")
+    ap.add_argument("--c4-B", type=int, default=16, help="sequences of the config-4 slice (headline)")
     ap.add_argument("--k", type=int, default=8, help="drafts per sequence")
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--cpu-tokens", type=int, default=72, help="tokens in the CPU baseline sample")

@@ -46,6 +46,9 @@ const char *k3gpu_strerror(int status);
 int k3gpu_last_cuda_error(void);
 /* Library version, major*10000 + minor*100 + patch. */
 int k3gpu_version(void);
+/* Kernels this process has enqueued through the library so far (all threads, all
+ * devices): the difference across a region is the number of the library's launches in it. */
+long long k3gpu_launch_count(void);
 /* Read (host, synchronous on the given device's default stream) and clear the device
  * status word: 0 when no kernel has flagged an out-of-range index since the last call.
  * Bits: 1 an index outside its range was skipped, 2 a count outside its range was
@@ -624,9 +627,15 @@ int k3gpu_model_commit_device(K3GpuModel *m, const int *keep_dev, const int *kee
  * the argmax after each sequence's last position */
 int k3gpu_model_prefill(K3GpuModel *m, const int *ids, int n, int *next);
 int k3gpu_model_cached(const K3GpuModel *m, int *cached);   /* host [B] */
+/* Positions each sequence has consumed (host [B], 0..kv_cap), e.g. after the caller wrote
+ * a resumed session's cache rows and KDA states through the views below. Discards a sweep
+ * awaiting its commit. */
+int k3gpu_model_set_cached(K3GpuModel *m, const int *cached);
 /* device views of a layer's state: KDA [B][H][D][D] and [B][3][P][K-1]; MLA caches */
 int k3gpu_model_kda_state(const K3GpuModel *m, int layer, float **state, float **conv_hist);
 int k3gpu_model_mla_cache(const K3GpuModel *m, int layer, uint16_t **lat, uint16_t **rope);
+/* the routing of the last layer of the last sweep: idx [B*T][topk] (device) */
+int k3gpu_model_last_routing(const K3GpuModel *m, const int **idx);
 /* The decode loop's callbacks (K3SpecVerifyFn / K3SpecCommitFn) for a model of B == 1,
  * ctx = the model: verify uploads the host ids, sweeps and returns every position's argmax
  * on the host (synchronising the model's stream); a read-in longer than max_T runs in

@@ -153,6 +153,8 @@ _SIGS = {
     "k3gpu_strerror": ([I], C.c_char_p),
     "k3gpu_last_cuda_error": ([], I),
     "k3gpu_version": ([], I),
+    "k3gpu_launch_count": ([], C.c_longlong),
+    "k3gpu_model_last_routing": ([VP, C.POINTER(VP)], I),
     "k3gpu_device_status": ([I, C.POINTER(I)], I),
     "k3gpu_router_workspace": ([I, I], SZ),
     "k3gpu_router": ([VP, VP, VP, VP, VP, I, I, I, I, I, F, VP, SZ, VP], I),
@@ -189,6 +191,7 @@ _SIGS = {
     "k3gpu_model_commit_device": ([VP, VP, VP], I),
     "k3gpu_model_prefill": ([VP, VP, I, VP], I),
     "k3gpu_model_cached": ([VP, VP], I),
+    "k3gpu_model_set_cached": ([VP, VP], I),
     "k3gpu_model_kda_state": ([VP, I, C.POINTER(VP), C.POINTER(VP)], I),
     "k3gpu_model_mla_cache": ([VP, I, C.POINTER(VP), C.POINTER(VP)], I),
     "k3gpu_model_loop_verify": ([VP, VP, VP, I, I, VP], I),
@@ -1037,6 +1040,11 @@ def _sibling(name):
     return sys.modules[key]
 
 
+def launch_count() -> int:
+    """The library's kernel launches so far in this process (k3gpu_launch_count)."""
+    return int(lib.k3gpu_launch_count())
+
+
 def argmax(logits, stream=None):
     """argmax_ per row of logits [rows][vocab] on the device (int32 [rows])."""
     rows, V = logits.reshape(-1, logits.shape[-1]).shape
@@ -1069,6 +1077,12 @@ class Model:
         self._alive = [layers, top, banks]
         cm = _sibling("config")
         self.lcfg = cm.layer_cfg(sys_module(), cfg)
+        # "plain": the benchmark configurations' MoE (router and experts at the hidden width,
+        # the shared experts in the same bank, SwiGLU); otherwise the K3 LatentMoE form
+        plain = cfg.get("moe_form", "latent") == "plain"
+        if plain:
+            self.lcfg.latent, self.lcfg.shared_inter = 0, 0
+            self.lcfg.act = ACT_SWIGLU if cfg.get("act", "swiglu") == "swiglu" else ACT_SITU
         self._kda = (K3GpuKdaLayerW * n)()
         self._mla = (K3GpuMlaLayerW * n)()
         self._moe = []
@@ -1076,12 +1090,14 @@ class Model:
         use_norm = cfg.get("latent_moe_use_norm", True)
         for L in range(n):
             d, bank = layers[L], banks[L]
-            mw = K3GpuMoeW()
-            for f in ("down", "up", "sh1", "sh3", "sh2", "gate_W", "gate_bias"):
-                setattr(mw, f, ptr(d.get(f)))
-            mw.latent_norm = ptr(d["latent_norm"]) if use_norm else None
-            mw.bank = C.pointer(bank.desc)
-            self._moe.append(mw)
+            mw = None
+            if not plain:
+                mw = K3GpuMoeW()
+                for f in ("down", "up", "sh1", "sh3", "sh2", "gate_W", "gate_bias"):
+                    setattr(mw, f, ptr(d.get(f)))
+                mw.latent_norm = ptr(d["latent_norm"]) if use_norm else None
+                mw.bank = C.pointer(bank.desc)
+                self._moe.append(mw)
             mla = d["kind"] == "mla"
             self._is_mla[L] = int(mla)
             lw = self._mla[L] if mla else self._kda[L]
@@ -1092,7 +1108,7 @@ class Model:
             else:
                 lw.kda = kda_weights(d)
             lw.bank = C.pointer(bank.desc)
-            lw.moe = C.pointer(mw)
+            lw.moe = C.pointer(mw) if mw is not None else None
         self._c = K3GpuModelCfg(self.lcfg, n, self.vocab, C.cast(self._is_mla, VP))
         self._w = K3GpuModelW(ptr(top["embed"]), ptr(top["lm_head"]), ptr(top["norm"]),
                               ptr(top.get("out_res_fold")), self._kda, self._mla)
@@ -1180,10 +1196,22 @@ class Model:
         check(lib.k3gpu_model_prefill(self._m, ptr(ids), ids.shape[1], ptr(nxt)), "k3gpu_model_prefill")
         return nxt
 
+    def set_cached(self, cached):
+        """Positions consumed per sequence (host ints [B]), after writing states and cache
+        rows through kda_state / mla_cache (a resumed session)."""
+        c = (C.c_int * self.B)(*[int(v) for v in cached])
+        check(lib.k3gpu_model_set_cached(self._m, c), "k3gpu_model_set_cached")
+
     def cached(self):
         c = (C.c_int * self.B)()
         check(lib.k3gpu_model_cached(self._m, c), "k3gpu_model_cached")
         return list(c)
+
+    def last_routing(self, T):
+        """The last layer's routing of the last sweep of T positions: int32 [B*T][topk] view."""
+        p = VP()
+        check(lib.k3gpu_model_last_routing(self._m, C.byref(p)), "k3gpu_model_last_routing")
+        return self._view(p.value, (self.B * T, self.lcfg.topk), torch.int32)
 
     def kda_state(self, layer):
         """(state [B][H][D][D], conv history [B][3][P][K-1]) device views of a KDA layer."""

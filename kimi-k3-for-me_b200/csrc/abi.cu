@@ -6,7 +6,10 @@
 namespace k3 {
 thread_local int g_last_cuda_error = 0;
 __device__ unsigned int g_device_status = 0;
+std::atomic<long long> g_launches{0};
 }  // namespace k3
+
+extern "C" long long k3gpu_launch_count(void) { return k3::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char *k3gpu_strerror(int status)
 {

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "k3gpu.h"
 
 namespace k3 {
@@ -32,8 +34,16 @@ inline int cuda_status(cudaError_t e)
     return K3GPU_ECUDA;
 }
 
-// Check the launch just enqueued (configuration errors surface here, not at sync).
-inline int launch_status() { return cuda_status(cudaGetLastError()); }
+// Kernels this process has enqueued through the library (k3gpu_launch_count).
+extern std::atomic<long long> g_launches;
+
+// Check the launch just enqueued (configuration errors surface here, not at sync); every
+// kernel launch of the library is followed by this call, which also counts it.
+inline int launch_status()
+{
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cuda_status(cudaGetLastError());
+}
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -607,6 +607,26 @@ extern "C" int k3gpu_model_prefill(K3GpuModel *m, const int *ids, int n, int *ne
     return cuda_status(cudaMemcpyAsync(next, m->arg, (size_t)B * 4, cudaMemcpyDeviceToDevice, s));
 }
 
+extern "C" int k3gpu_model_set_cached(K3GpuModel *m, const int *cached)
+{
+    using namespace k3;
+    if (!m || !cached) return K3GPU_EINVAL;
+    for (int b = 0; b < m->B; b++)
+        if (cached[b] < 0 || cached[b] > m->cap) return K3GPU_EINVAL;
+    Stage sg;
+    int st;
+    if ((st = stage_acquire(m, &sg))) return st;
+    std::copy(cached, cached + m->B, sg.keep);
+    if ((st = cuda_status(cudaMemcpyAsync(m->cached, sg.keep, (size_t)m->B * 4, cudaMemcpyHostToDevice,
+                                          as_stream(m->stream)))))
+        return st;
+    if ((st = stage_release(m, sg))) return st;
+    std::copy(cached, cached + m->B, m->cached_host.begin());
+    m->last_T = 0;
+    m->pre_committed = 0;
+    return K3GPU_OK;
+}
+
 extern "C" int k3gpu_model_cached(const K3GpuModel *m, int *cached)
 {
     if (!m || !cached) return K3GPU_EINVAL;
@@ -619,6 +639,13 @@ extern "C" int k3gpu_model_kda_state(const K3GpuModel *m, int layer, float **sta
     if (!m || layer < 0 || layer >= m->cfg.n_layers || m->is_mla[layer]) return K3GPU_EINVAL;
     if (state) *state = m->kstate[m->slot[layer]];
     if (conv_hist) *conv_hist = m->khist[m->slot[layer]];
+    return K3GPU_OK;
+}
+
+extern "C" int k3gpu_model_last_routing(const K3GpuModel *m, const int **idx)
+{
+    if (!m || !idx) return K3GPU_EINVAL;
+    *idx = m->moe_idx;
     return K3GPU_OK;
 }
 

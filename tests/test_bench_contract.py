@@ -67,3 +67,29 @@ def test_matmul_cpu_baseline_runs_the_reference_projection():
         pytest.skip("oracle/_ref not built")
     r = _bench().matmul_bf16_cpu_baseline(8, 256, 4096, rows=32)
     assert r["unit"] == "us per call" and r["kind"] == "reference" and r["value"] > 0
+
+
+def test_c4_tree_and_forced_drafts():
+    """The config-4 draft tree: 64 nodes, parents before children, at most 4 children and 4
+    levels, its most probable branch 4 deep; the forced trees carry the continuation on that
+    branch, and no sibling of a branch node repeats the branch's id there."""
+    b = _bench()
+    parent, chain = b.tree_topology()
+    assert len(parent) == 64 and parent[0] == -1
+    assert all(0 <= parent[i] < i for i in range(1, 64))
+    assert max(np.bincount([p for p in parent if p >= 0])) <= 4
+    assert len(chain) == 5 and all(parent[chain[j + 1]] == chain[j] for j in range(4))
+    depth = [0] * 64
+    for i in range(1, 64):
+        depth[i] = depth[parent[i]] + 1
+    assert max(depth) == 4
+    cont = [list(range(100 * b_, 100 * b_ + 40)) for b_ in range(3)]
+    tok = b.c4_trees(cont, parent, chain, steps=3, V=1000, seed=0)
+    for s in range(3):
+        for q in range(3):
+            assert [tok[s, q, n] for n in chain] == cont[q][5 * s:5 * s + 5]
+            for i in range(1, 64):
+                if parent[i] in chain and i not in chain:
+                    j = chain.index(parent[i]) + 1
+                    if j < 5:
+                        assert tok[s, q, i] != tok[s, q, chain[j]]
