@@ -116,11 +116,16 @@ def make_bank_device(n_experts, L, I, seed, device, chunk=16):
     return bank, offs, stride
 
 
+FP32_ACTS = False   # --fp32-acts: full fp32 activations instead of bf16 ones
+
+
 def make_inputs(M, seed, device):
     import torch
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
-    x = torch.randn((M, L_DIM), generator=gen, device=device).to(torch.bfloat16).float()
+    x = torch.randn((M, L_DIM), generator=gen, device=device)
+    if not FP32_ACTS:
+        x = x.to(torch.bfloat16).float()
     gate = torch.randn((N_ROUTED, L_DIM), generator=gen, device=device) * 0.02
     bias = torch.randn((N_ROUTED,), generator=gen, device=device) * 0.01
     return x.contiguous(), gate.contiguous(), bias.contiguous()
@@ -339,6 +344,14 @@ def run_c4(args, k3, dev, local):
     accepted = 0
     for s in range(warm):
         step(s, tok_dev[s])
+    if args.profile_c4:   # one step inside an NVTX range, for an ncu launch list
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("c4_step")
+        step(warm, tok_dev[warm])
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        model.close()
+        return None
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
@@ -435,20 +448,26 @@ def run_c4(args, k3, dev, local):
                      "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(gateup_bytes),
                      "units": f"{u} experts x {w13} B + rows"},
         "gpu_launches": int(launches), "device_status": status, "clocks": clk, "build_s": round(build_s, 1),
-        "config": {"workload": f"K3 8-layer slice tree verify (benchmark config 4): B={B} sequences x "
-                               f"{C4_TREE}-node draft tree (branching {C4_BRANCH}, depth {C4_DEPTH}) over a "
-                               f"{C4_CTX}-position cache, greedy acceptance",
-                   "layers": "6 KDA + 2 MLA (3:1), every layer MoE", "d_model": E, "vocab": V,
-                   "moe": "384 routed top-8 + 1 shared, FFN 2048 SwiGLU, MXFP4 (E2M1 + E8M0/32) N(0,0.02)",
-                   "kda": "32 heads x 128", "mla": "64 heads, q_lora 1536, kv_lora 512, nope 128, rope 64, v 128",
-                   "B": B, "tree_nodes": C4_TREE, "tokens_verified_per_step": R, "context": C4_CTX,
-                   "drafts": "forced: each tree's most probable branch (depth 4) is the model's own greedy "
-                             "continuation from an untimed serial run, the other 59 nodes random ids (the "
-                             "reference's GATE-4 method; a random-weight model gives the n-gram drafter nothing "
-                             "to match)",
-                   "weights": "random init: bf16 projections N(0,0.02), MXFP4 experts N(0,0.02)",
-                   "l2": "weights streamed per step (~75 GB) exceed the 126 MB L2; no flush needed"},
+        "config": c4_config(B, R),
     }
+
+
+def c4_config(B, R=None):
+    R = R if R is not None else B * C4_TREE
+    E, V = C4["hidden_size"], C4["vocab_size"]
+    return {"workload": f"K3 8-layer slice tree verify (benchmark config 4): B={B} sequences x "
+                        f"{C4_TREE}-node draft tree (branching {C4_BRANCH}, depth {C4_DEPTH}) over a "
+                        f"{C4_CTX}-position cache, greedy acceptance",
+            "layers": "6 KDA + 2 MLA (3:1), every layer MoE", "d_model": E, "vocab": V,
+            "moe": "384 routed top-8 + 1 shared, FFN 2048 SwiGLU, MXFP4 (E2M1 + E8M0/32) N(0,0.02)",
+            "kda": "32 heads x 128", "mla": "64 heads, q_lora 1536, kv_lora 512, nope 128, rope 64, v 128",
+            "B": B, "tree_nodes": C4_TREE, "tokens_verified_per_step": R, "context": C4_CTX,
+            "drafts": "forced: each tree's most probable branch (depth 4) is the model's own greedy "
+                      "continuation from an untimed serial run, the other 59 nodes random ids (the "
+                      "reference's GATE-4 method; a random-weight model gives the n-gram drafter nothing "
+                      "to match)",
+            "weights": "random init: bf16 projections N(0,0.02), MXFP4 experts N(0,0.02)",
+            "l2": "weights streamed per step (~75 GB) exceed the 126 MB L2; no flush needed"}
 
 
 def unique_experts_bytes(idx_np, stride_bytes_per_expert):
@@ -591,7 +610,8 @@ def host_threads():
 
 # ----------------------------------------------------------------------- arms ------
 def run_reference(args):
-    """--impl reference: the reference's own C kernels on all host threads."""
+    """--impl reference: the reference engine's own CPU path for the headline workload
+    (config 4, c4_reference_sample) on the host cores, one bounded sample per step."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
@@ -601,37 +621,41 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable":
                           "oracle/_ref/libk3ref_bench.so was not built (reference sources absent when built)"}))
         return 0
-    M = args.B * (1 + args.k)
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    bank, offs, stride = (make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, dev)
-                          if dev == "cuda" else make_bank_cpu(args.seed))
-    x, gate, bias = make_inputs(M, args.seed + 1, dev)
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "reference", "unavailable": "the 9 GB expert bank is drawn on the GPU box"}))
+        return 0
+    bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, "cuda")
     bank_np = bank.cpu().numpy()
-    x_np, gate_np, bias_np = x.cpu().numpy(), gate.cpu().numpy(), bias.cpu().numpy()
     del bank
+    torch.cuda.empty_cache()
     nth = host_threads()
-    T = min(M, args.ref_tokens) if args.ref_tokens else M
-    for _ in range(args.warmup):
-        cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nth)
-    times = []
-    for _ in range(args.steps):
-        dt, _, _ = cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nth)
-        times.append(dt)
-    ms = 1000.0 * statistics.median(times)
-    val = T / (ms / 1000.0)
+    for i in range(min(args.warmup, 1)):
+        c4_reference_sample(args, bank_np, offs, stride, nth, args.seed + 100 + i)
+    samples = []
+    for i in range(args.steps):
+        r = c4_reference_sample(args, bank_np, offs, stride, nth, args.seed + i)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": "a reference layer sample failed (out of memory)"}))
+            return 0
+        samples.append(r)
+    steps_s = [r["step_s"] for r in samples]
+    step = statistics.median(steps_s)
+    val = (C4_DEPTH + 1) / step
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "tok/s",
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "accepted tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms * M / T, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f64-accumulate MXFP4 x fp32 (reference CPU)",
-        "data": "synthetic (seeded)",
-        "config": workload_config(args, M),
-        "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": nth, "kind": "reference",
-                         "sample": f"{T} of {M} tokens per step through the reference's k3_router + "
-                                   f"k3_matmul_mxfp4 expert loop, {nth} host threads, no OpenMP"},
-        "e2e": {"value": round(val, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-        "all_step_ms": [round(1000 * t, 3) for t in times],
+        "ms_per_step": round(1000 * step, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 / MXFP4 weights x fp32 activations, double accumulate (reference CPU)",
+        "data": "synthetic (seeded random weights, random 32k cache, forced drafts)",
+        "config": c4_config(args.c4_B),
+        "cpu_baseline": {"value": round(val, 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
+                         "sample": c4_sample_text(nth)},
+        "e2e": {"value": round(val, 4), "unit": "accepted tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "all_step_s": [round(x, 3) for x in steps_s],
+        "layer_s_median": {k: round(statistics.median([r[k] for r in samples]), 4)
+                           for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")},
+        "note": "one sequence at a time (the reference engine serves one sequence and drafts chains); "
+                "the GPU arm verifies B sequences' 64-node trees per step",
     }
     print(json.dumps(line))
     return 0
@@ -1150,10 +1174,12 @@ def run_b200(args):
 
     hbm, peak_kind = peaks()
     rows = {}
-    if not args.no_rows:
+    if not args.no_rows and not args.profile_c4:
         rows["moe_layer_c2"] = c2_rows(args, k3, dev)
         rows.update(measure_rows(k3, dev, hbm, peaks_tensor()))
     c4 = run_c4(args, k3, dev, local)
+    if c4 is None:        # --profile-c4
+        return 0
     cpu = None if args.no_cpu else c4_cpu_baseline(args)
     line = {
         "metric": METRIC, "value": c4["value"], "unit": "accepted tok/s",
@@ -1173,9 +1199,68 @@ def run_b200(args):
     return 0
 
 
+def c4_reference_sample(args, bank_np=None, offs=None, stride=None, nth=None, seed=0):
+    """The reference engine verifying the same accepted branch on the host: one sequence's
+    sweep of the 5-position chain (the pending id and the 4 drafts that are accepted -- the
+    reference drafts chains only) through its own kernels, timed layer by layer on a bounded
+    sample and summed over the slice: 6 x (KDA layer + MoE) + 2 x (MLA layer over the 32k
+    cache + MoE) + the lm_head over 5 positions (a 4096-row sample scaled to 163840 rows).
+    The KDA and MLA layers are k3_kda_layer_log and k3_mla_cached (latent, absorbed) at K3
+    dimensions (oracle/ref_slice_bench.c), serial as the reference runs without OpenMP; the
+    MoE is its k3_router + k3_matmul_mxfp4 expert loop over all host threads
+    (oracle/ref_moe_bench.c) on the config's 385-expert bank. Returns a dict with the step
+    seconds and the accepted tok/s it implies (5 ids per step), or None when the reference
+    library was not built."""
+    from oracle import oracle as O
+    lib = O.ref_bench()
+    if lib is None:
+        return None
+    for f in ("ref_c4_kda", "ref_c4_mla", "ref_c4_lm_rows"):
+        getattr(lib, f).restype = C.c_double
+        getattr(lib, f).argtypes = [C.c_int, C.c_int, C.c_uint] if f == "ref_c4_mla" else [C.c_int, C.c_uint]
+    T = C4_DEPTH + 1
+    lm_rows = 4096
+    t_kda = lib.ref_c4_kda(T, seed + 1)
+    t_mla = lib.ref_c4_mla(T, C4_CTX, seed + 2)
+    t_lm = lib.ref_c4_lm_rows(T, lm_rows, seed + 3) * C4["vocab_size"] / lm_rows
+    t_moe = None
+    if bank_np is not None:
+        rng = np.random.default_rng(seed + 4)
+        x = rng.standard_normal((T, L_DIM), dtype=np.float32)
+        gate = rng.standard_normal((N_ROUTED, L_DIM), dtype=np.float32) * np.float32(0.02)
+        bias = rng.standard_normal(N_ROUTED, dtype=np.float32) * np.float32(0.01)
+        r = cpu_reference_run(x, gate, bias, bank_np, offs, stride, T, nth)
+        t_moe = r[0] if r is not None else None
+    if min(t_kda, t_mla, t_lm) < 0 or t_moe is None:
+        return None
+    n_kda, n_mla = 6, 2
+    step = n_kda * (t_kda + t_moe) + n_mla * (t_mla + t_moe) + t_lm
+    return {"step_s": step, "value": T / step, "kda_s": t_kda, "mla_s": t_mla, "moe_s": t_moe, "lm_head_s": t_lm}
+
+
+def c4_sample_text(nth):
+    return (f"one sequence verifying the accepted 5-position branch: the reference's k3_kda_layer_log and "
+            f"k3_mla_cached (latent, absorbed, 32768 cached positions) at K3 dims timed once each (serial, no "
+            f"OpenMP), its k3_router + k3_matmul_mxfp4 MoE over 5 tokens on {nth} host threads, the lm_head "
+            f"over a 4096-row sample scaled to 163840, summed as 6 x (KDA + MoE) + 2 x (MLA + MoE) + lm_head")
+
+
 def c4_cpu_baseline(args):
-    """Filled in by the reference's own decoder layer on the host (oracle/ref_slice_bench.c)."""
-    return None
+    """The reference on the host beside our run (rank 0, N = 1): one bounded sample."""
+    import torch
+    bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, "cuda")
+    bank_np = bank.cpu().numpy()
+    del bank
+    torch.cuda.empty_cache()
+    nth = host_threads()
+    r = c4_reference_sample(args, bank_np, offs, stride, nth, args.seed)
+    del bank_np
+    if r is None:
+        return None
+    return {"value": round(r["value"], 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
+            "isa": "x86-64-v3 (AVX2 + FMA), no OpenMP",
+            "sample": c4_sample_text(nth), "step_s": round(r["step_s"], 3),
+            "layer_s": {k: round(r[k], 4) for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")}}
 
 
 def main():
@@ -1200,6 +1285,14 @@ def main():
                     choices=["kda_c3", "kda_prefill", "mla_absorbed_c4", "trunk_matmul_bf16", "lm_head_bf16_c4",
                              "accept_greedy_vocab"],
                     help="time one of the other rows alone and print it (for profiling captures)")
+    ap.add_argument("--only-c2", type=int, nargs=2, metavar=("B", "K"), default=None,
+                    help="time the config-2 layer at one (B, k) point alone and print its row (small cases "
+                         "for captures with --n-routed)")
+    ap.add_argument("--fp32-acts", action="store_true",
+                    help="with --only-c2: full fp32 activations (the model's post-norm rows) instead of bf16")
+    ap.add_argument("--profile-c4", action="store_true",
+                    help="build the config-4 slice, run the warm-up steps, then one step inside the NVTX range "
+                         "'c4_step' and exit (for an ncu launch list with --nvtx-include c4_step/)")
     ap.add_argument("--n-routed", type=int, default=N_ROUTED,
                     help="routed experts (smaller values give small cases for ncu captures)")
     args = ap.parse_args()
@@ -1208,6 +1301,18 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.only_c2:
+        import torch
+        k3 = load_pkg()
+        dev = torch.device("cuda", 0)
+        bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, dev)
+        kb = k3.ExpertBank(bank, N_ROUTED + N_SHARED, L_DIM, I_DIM)
+        n_unsafe = kb.scan() if not args.no_tc else None
+        B, k = args.only_c2
+        global FP32_ACTS
+        FP32_ACTS = args.fp32_acts
+        print(json.dumps(measure_c2(args, k3, dev, kb, bank, offs, stride, B * (1 + k), args.seed + 1, n_unsafe)))
+        return 0
     if args.only_row:
         k3 = load_pkg()
         hbm, _ = peaks()
