@@ -209,8 +209,11 @@ int k3gpu_moe_layer(float *out, int *idx, float *wt, const float *x, const float
                     float routed_scale, void *workspace, size_t ws_bytes, void *stream);
 
 /* Expert-kernel selection (host, per process): 0 (default) runs the tensor-core expert
- * stream wherever L and I are multiples of 512 and the CUDA-core stream elsewhere; 1
- * forces the CUDA-core stream everywhere (the two agree to fp32 rounding). */
+ * stream wherever L and I are multiples of 512 and the CUDA-core stream elsewhere, the
+ * tcgen05 kernels in the pass shape the call's routed tokens per expert select (8 tokens a
+ * pass while experts see few, 32 once they see 12 or more on average); 1 forces the
+ * CUDA-core stream everywhere; 2 and 3 force the tcgen05 dense (32-token) and sparse
+ * (8-token) pass shapes. All agree to fp32 rounding. */
 int k3gpu_moe_select_kernels(int which);
 
 /* Per-phase timing of the MoE calls, for roofline reporting. When enabled (host, per

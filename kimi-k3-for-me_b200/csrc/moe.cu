@@ -481,12 +481,13 @@ int moe_launch(float *out, const float *z, const int *idx, const float *wt,
         const bool sync_path = !tc || bank->n_f16_unsafe > 0;
         if ((st = tc_pack_pairs_launch(p, z, bank->L, P, E, s))) return st;
         phase_mark(2, s);
-        if (tc && (st = tc_phase_launch(0, p, *bank, P, act, b1, b2, s))) return st;
+        const double tpe = (double)T * topk / (double)(n_routed > 0 ? n_routed : 1);
+        if (tc && (st = tc_phase_launch(0, p, *bank, P, act, b1, b2, s, tpe))) return st;
         if (sync_path && (st = mma_phase_launch(0, p, *bank, act, b1, b2, s))) return st;
         phase_mark(3, s);
         act_pack_rows_launch(p, bank->I, P, E, s);
         if ((st = launch_status())) return st;
-        if (tc && (st = tc_phase_launch(1, p, *bank, P, act, b1, b2, s))) return st;
+        if (tc && (st = tc_phase_launch(1, p, *bank, P, act, b1, b2, s, tpe))) return st;
         if (sync_path && (st = mma_phase_launch(1, p, *bank, act, b1, b2, s))) return st;
     } else {
         const int grid = num_sms() * 2;
@@ -547,8 +548,9 @@ extern "C" int k3gpu_bank_scan(K3GpuExpertBank *bank, uint8_t *safe_dev, void *s
 
 extern "C" int k3gpu_moe_select_kernels(int which)
 {
-    if (which != 0 && which != 1) return K3GPU_EINVAL;
-    k3::g_use_mma = which == 0;
+    if (which < 0 || which > 3) return K3GPU_EINVAL;
+    k3::g_use_mma = which != 1;
+    k3::g_tc_shape = which == 2 ? 2 : which == 3 ? 1 : 0;
     return K3GPU_OK;
 }
 

@@ -91,9 +91,13 @@ bool tc_bank_ok(const K3GpuExpertBank &b);
 int tc_bank_scan(const K3GpuExpertBank &b, uint8_t *safe, cudaStream_t s);
 int tc_pack_pairs_launch(const MoePlan &p, const float *z, int L, int P, int E, cudaStream_t s);
 void act_pack_rows_launch(const MoePlan &p, int I, int P, int E, cudaStream_t s);
-// tcgen05 kernels on the certified experts (phase 0 = gate/up, 1 = down)
+// tcgen05 kernels on the certified experts (phase 0 = gate/up, 1 = down), in the pass shape
+// the call's routed tokens per expert select (tc_dense_for; k3gpu_moe_select_kernels 2 / 3
+// force the dense / sparse shape)
+extern int g_tc_shape;
+bool tc_dense_for(double tokens_per_expert);
 int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, int P, int act,
-                    float b1, float b2, cudaStream_t s);
+                    float b1, float b2, cudaStream_t s, double tokens_per_expert);
 // mma.sync kernels on the experts the tcgen05 kernels do not take
 int mma_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, int act,
                      float b1, float b2, cudaStream_t s);

@@ -36,44 +36,56 @@ namespace k3 {
 constexpr int TC_DEQ_WARPS = 8;          // warps 0..7: decode (two per TMEM lane quarter)
 constexpr int TC_EPI_WARP0 = 8;          // warps 8..11: epilogue
 constexpr int TC_TMA_WARP = 12;
-constexpr int TC_MMA_WARP0 = 13;         // warps 13..16: MMA issuers, one K quarter of a stage each
-constexpr int TC_NMMA = 4;
-constexpr int TC_THREADS = (TC_MMA_WARP0 + TC_NMMA) * 32;
+constexpr int TC_MMA_WARP0 = 13;         // warps 13..: MMA issuers
 constexpr int TC_KC = 512;               // K elements per shared-memory stage
-constexpr int TC_NP = 8;                 // tokens per pass
-constexpr int TC_N = 2 * TC_NP;          // MMA N: the pass's 8 hi rows, then their 8 lo rows
 constexpr int TC_W_BYTES = 128 * 256;    // packed weights of a stage (32 KB)
 constexpr int TC_S_BYTES = 128 * 16;     // E8M0 bytes of a stage
-constexpr int TC_B_BYTES = (TC_KC / 64) * TC_NP * 128;  // 8 KB: one piece, 8 atoms x 8 rows x 128 B
-constexpr int TC_STAGE = TC_W_BYTES + TC_S_BYTES + 2 * TC_B_BYTES + 1024 - TC_S_BYTES % 1024;
-// Four stages: the weight bytes in flight per SM, not any unit's rate, set the stream's
-// pace (at the loaded latency of ~3.4 us, 3 x 32 KB of weights allow ~30 GB/s per SM)
-constexpr int TC_NS = 4;
-constexpr int TC_NA = 3;                 // TMEM A buffers (128 columns = 256 K each)
-// a B atom pair in shared memory: 64 K x 8 hi rows, then the same 8 rows' lo halves, so
-// one N = 16 MMA (SBO = 1024 between the two 8-row groups) yields the hi products in D
-// columns 0..7 and the lo products in 8..15; without lo halves columns 8..15 are unused
-constexpr int TC_ATOM = 2 * TC_NP * 128;
-// TMEM: two stage-partial sets of four 16-column D (one per issuer), three A buffers
-template <int PHASE> struct TcTmem {
-    static constexpr int NA = TC_NA;
-    static constexpr int PW = TC_N;                         // D columns per issuer
-    static constexpr int PCOLS = TC_NMMA * PW;              // one stage-partial set
-    static constexpr int ACOL0 = 2 * PCOLS;                 // first A column
+
+// The pass shape. Sparse (a verify step: most experts see one to three tokens): up to 8
+// tokens a pass, four issuers (two per K half of a stage, each its own accumulator), three
+// TMEM A buffers and four stages -- the weight bytes in flight per SM, not any unit's rate,
+// set the stream's pace (at the loaded latency of ~3.4 us, 3 x 32 KB allow ~30 GB/s per
+// SM), and the half-height activation tile is what leaves room for the fourth stage.
+// Dense (many tokens an expert, e.g. a 64-node tree over 16 sequences: ~21 tokens per
+// expert): up to 32 tokens a pass so each weight is decoded once for all of its expert's
+// tokens -- the decode, not the tensor pipe, bounds the sparse shape once an expert needs
+// several passes -- at the cost of one issuer per K half (an N = 64 MMA keeps the pipe busy
+// from one thread), two A buffers and two stages.
+template <int NP_, int NMMA_, int NA_, int NS_, int TAB_> struct TcShape {
+    static constexpr int NP = NP_;                      // tokens per pass
+    static constexpr int N = 2 * NP;                    // MMA N: the pass's hi rows, then their lo rows
+    static constexpr int NMMA = NMMA_;                  // issuers: NMMA / 2 per K half
+    static constexpr int MPI = 32 / NMMA;               // K16 MMAs per issuer per stage
+    static constexpr int NA = NA_;                      // TMEM A buffers (128 columns = 256 K each)
+    static constexpr int NS = NS_;                      // shared-memory stages
+    static constexpr int TAB = TAB_;                    // active-expert entries kept in shared memory
+    static constexpr int B_BYTES = (TC_KC / 64) * NP * 128;   // one activation piece of a stage
+    static constexpr int STAGE = TC_W_BYTES + TC_S_BYTES + 2 * B_BYTES + 1024 - TC_S_BYTES % 1024;
+    // a B atom: 64 K x NP hi rows, then the same rows' lo halves (SBO = 1024 between 8-row
+    // groups), so one N = 2 NP MMA yields the hi products in D columns 0..NP-1 and the lo
+    // products in NP..2NP-1; without lo halves the upper columns are unused
+    static constexpr int ATOM = 2 * NP * 128;
+    static constexpr int PW = N;                        // D columns per issuer
+    static constexpr int PCOLS = NMMA * PW;             // one stage-partial set
+    static constexpr int ACOL0 = 2 * PCOLS;             // first A column
+    static constexpr int XCH_BYTES = 64 * NP * 4;       // gate/up exchange in the epilogue
+    // barriers: full[NS] empty[NS] aready[NA] afree[NA] pfree[2] (stage partials)
+    static constexpr int NBAR = 2 * NS + 2 * NA + 2;
+    // after the expert table: the E8M0 byte -> f16x2 scale pair table (256 entries)
+    static constexpr int SMEM = NS * STAGE + XCH_BYTES + NBAR * 8 + 16 + TAB * 16 + 256 * 4;
+    static constexpr int THREADS = (TC_MMA_WARP0 + NMMA) * 32;
     static_assert(ACOL0 + NA * 128 <= 512, "TMEM columns");
+    static_assert(STAGE % 1024 == 0, "stage alignment");
+    static_assert((NS * STAGE + XCH_BYTES + (NBAR + 2) * 8) % 16 == 0, "int4 expert table alignment");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+    static_assert(NMMA == 2 || NMMA == 4, "issuers per K half");
+    static_assert(NP == 8 || NP % 16 == 0, "pass width");
 };
-constexpr int TC_XCH_BYTES = 64 * TC_NP * 4;   // gate/up exchange in the epilogue
-// barriers: full[NS] empty[NS] aready[NA] afree[NA] pfree[2] (stage partials)
-constexpr int TC_NBAR = 2 * TC_NS + 2 * TC_NA + 2;
-constexpr int TC_TAB = 1024;             // active-expert table entries kept in shared memory
-// after the expert table: the E8M0 byte -> f16x2 scale pair table (256 entries)
-constexpr int TC_SMEM = TC_NS * TC_STAGE + TC_XCH_BYTES + TC_NBAR * 8 + 16 + TC_TAB * 16 + 256 * 4;
+using TcSparse = TcShape<8, 4, 3, 4, 1024>;
+using TcDense = TcShape<32, 2, 2, 2, 512>;
 constexpr long long TC_SPIN = 1LL << 22;
 constexpr int TC_SUSPEND_NS = 1000;
 
-static_assert(TC_STAGE % 1024 == 0, "stage alignment");
-static_assert((TC_NS * TC_STAGE + TC_XCH_BYTES + (TC_NBAR + 2) * 8) % 16 == 0, "int4 expert table alignment");
-static_assert(TC_SMEM <= 227 * 1024, "shared memory");
 
 __device__ __forceinline__ uint32_t s_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -200,8 +212,8 @@ struct TcArgs {
     const uint8_t *safe;       // per-expert: 1 when every scale byte is in 104..140 or 255
 };
 
-template <int PHASE>   // 0 = gate/up (activation fused), 1 = down
-__global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_constant__ CUtensorMap wmap,
+template <int PHASE, class CF>   // PHASE 0 = gate/up (activation fused), 1 = down; CF the pass shape
+__global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                                                                const __grid_constant__ CUtensorMap smap,
                                                                const __grid_constant__ CUtensorMap bhmap,
                                                                const __grid_constant__ CUtensorMap blmap,
@@ -215,24 +227,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         if (threadIdx.x == 0) flag(DEV_BAD_INDEX);
         return;
     }
-    float *xch = reinterpret_cast<float *>(smem + (size_t)TC_NS * TC_STAGE);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)TC_NS * TC_STAGE + TC_XCH_BYTES);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + TC_NBAR);
-    int4 *tab = reinterpret_cast<int4 *>(bars + TC_NBAR + 2);   // [TC_TAB] {e, cnt, off, flags}
-    uint32_t *stab = reinterpret_cast<uint32_t *>(tab + TC_TAB);   // [256] scale_h2 of each byte
-    uint64_t *b_full = bars, *b_empty = bars + TC_NS;
-    uint64_t *b_aready = bars + 2 * TC_NS, *b_afree = bars + 2 * TC_NS + TC_NA;
-    uint64_t *b_pfree = bars + 2 * TC_NS + 2 * TC_NA;   // partial buffers: epilogue -> MMA
+    float *xch = reinterpret_cast<float *>(smem + (size_t)CF::NS * CF::STAGE);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)CF::NS * CF::STAGE + CF::XCH_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + CF::NBAR);
+    int4 *tab = reinterpret_cast<int4 *>(bars + CF::NBAR + 2);   // [CF::TAB] {e, cnt, off, flags}
+    uint32_t *stab = reinterpret_cast<uint32_t *>(tab + CF::TAB);   // [256] scale_h2 of each byte
+    uint64_t *b_full = bars, *b_empty = bars + CF::NS;
+    uint64_t *b_aready = bars + 2 * CF::NS, *b_afree = bars + 2 * CF::NS + CF::NA;
+    uint64_t *b_pfree = bars + 2 * CF::NS + 2 * CF::NA;   // partial buffers: epilogue -> MMA
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < TC_NS; s++) {
+        for (int s = 0; s < CF::NS; s++) {
             bar_init(s_addr(&b_full[s]), 1);
-            bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + TC_NMMA);   // decode warps + MMA commits
+            bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + CF::NMMA);   // decode warps + MMA commits
         }
-        for (int a = 0; a < TC_NA; a++) {
+        for (int a = 0; a < CF::NA; a++) {
             bar_init(s_addr(&b_aready[a]), 4);                  // the four warps of that K half
-            bar_init(s_addr(&b_afree[a]), 2);                   // commits of the half's two issuers
+            bar_init(s_addr(&b_afree[a]), CF::NMMA / 2);        // commits of the half's issuers
         }
         for (int d = 0; d < 2; d++) {
             bar_init(s_addr(&b_pfree[d]), 4);                   // epilogue warps
@@ -242,13 +254,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     // the active experts of this call, once per CTA: {expert, tokens, first pair, flags}
     // with flags bit 0 = some input row has a lo half, bit 1 = left to the mma.sync path
     const int na = *p.n_active;
-    for (int a = tid; a < na && a < TC_TAB; a += TC_THREADS) {
+    for (int a = tid; a < na && a < CF::TAB; a += CF::THREADS) {
         const int e = p.act[a];
         const int lo = p.elo[(PHASE == 0 ? 0 : bank.n_experts) + e];
         const int skip = (ta.safe && !ta.safe[e]) ? 2 : 0;
         tab[a] = make_int4(e, p.cnt[e], p.off[e], (lo ? 1 : 0) | skip);
     }
-    for (int b = tid; b < 256; b += TC_THREADS)   // only certified bytes are ever looked up
+    for (int b = tid; b < 256; b += CF::THREADS)   // only certified bytes are ever looked up
         stab[b] = (b == 255 || (b >= 104 && b <= 140)) ? scale_h2((uint32_t)b) : 0u;
     if (warp == 0) {   // 512 TMEM columns: partial sets at 0 and 64, A buffers from 128
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
@@ -274,14 +286,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
             if (ent.w & 2) continue;                                                         \
             const int e = ent.x, ub = u % ta.UE, nt = ent.y, q0 = ent.z;                      \
             const bool lo_any = (ent.w & 1) != 0;                                            \
-            for (int tb = 0; tb < nt && !failed; tb += TC_NP, unit_i++) {                    \
-                const int npt = min(TC_NP, nt - tb);                                         \
+            for (int tb = 0; tb < nt && !failed; tb += CF::NP, unit_i++) {                    \
+                const int npt = min(CF::NP, nt - tb);                                         \
                 __VA_ARGS__                                                                  \
             }                                                                                \
         }                                                                                    \
     }
     auto unit_entry = [&](int a) -> int4 {
-        if (a < TC_TAB) return tab[a];
+        if (a < CF::TAB) return tab[a];
         const int e = p.act[a];
         const int lo = p.elo[(PHASE == 0 ? 0 : bank.n_experts) + e];
         return make_int4(e, p.cnt[e], p.off[e], (lo ? 1 : 0) | ((ta.safe && !ta.safe[e]) ? 2 : 0));
@@ -294,14 +306,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
             asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
             TC_FOR_UNITS({
                 for (int kc = 0; kc < NK && !failed; kc++, item++) {
-                    const int st = item % TC_NS;
-                    const uint32_t par = (uint32_t)((item / TC_NS) & 1);
+                    const int st = item % CF::NS;
+                    const uint32_t par = (uint32_t)((item / CF::NS) & 1);
                     if (!bar_wait(s_addr(&b_empty[st]), par ^ 1u)) { failed = true; break; }
-                    unsigned char *sw = smem + (size_t)st * TC_STAGE;
+                    unsigned char *sw = smem + (size_t)st * CF::STAGE;
                     unsigned char *ssb = sw + TC_W_BYTES;
                     unsigned char *sbh = sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024);
                     const uint32_t full = s_addr(&b_full[st]);
-                    bar_expect(full, (uint32_t)(TC_W_BYTES + TC_S_BYTES + TC_B_BYTES * (lo_any ? 2 : 1)));
+                    bar_expect(full, (uint32_t)(TC_W_BYTES + TC_S_BYTES + CF::B_BYTES * (lo_any ? 2 : 1)));
                     const int x0 = kc * 256, xs = kc * 16;
                     if (PHASE == 0) {
                         const int y1 = (int)(e * ta.wys + ta.wy1 + ub * 64), y3 = (int)(e * ta.wys + ta.wy3 + ub * 64);
@@ -321,36 +333,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
                     // belong to the next one or lie past the tensor: those columns are
                     // never read back; out-of-range rows are filled with zeros)
                     for (int a = 0; a < TC_KC / 64; a++) {
-                        tma2d(s_addr(sbh + a * TC_ATOM), &bhmap, kc * TC_KC + a * 64, q0 + tb, full);
-                        if (lo_any) tma2d(s_addr(sbh + a * TC_ATOM + TC_NP * 128), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
+                        tma2d(s_addr(sbh + a * CF::ATOM), &bhmap, kc * TC_KC + a * 64, q0 + tb, full);
+                        if (lo_any) tma2d(s_addr(sbh + a * CF::ATOM + CF::NP * 128), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
                     }
                 }
             });
             if (failed) flag(DEV_TIMEOUT);
         }
-    } else if (warp >= TC_MMA_WARP0 && warp < TC_MMA_WARP0 + TC_NMMA) {
+    } else if (warp >= TC_MMA_WARP0 && warp < TC_MMA_WARP0 + CF::NMMA) {
         // One thread issues an MMA about every 55 clocks however small N is, while the
         // tensor pipe finishes an M128 x N16 x K16 step in about 9: four issuer warps, each
         // with its own accumulator, keep the pipe fed. Issuer i takes K steps 8j..8j+7 of
         // stage half h (i = 2h + j); every stage starts fresh partials (double-buffered)
         // that the epilogue warps sum in fp32.
         if (lane == 0) {
-            const int mi = warp - TC_MMA_WARP0, h = mi >> 1, j = mi & 1;
-            const uint32_t idesc = f16_idesc(TC_N);
-            using TM = TcTmem<PHASE>;
-            // this issuer's eight B offsets, in 16-byte descriptor units: the descriptor of a
+            constexpr int PER_HALF = CF::NMMA / 2;
+            const int mi = warp - TC_MMA_WARP0, h = mi / PER_HALF, j = mi % PER_HALF;
+            const uint32_t idesc = f16_idesc(CF::N);
+            using TM = CF;
+            // this issuer's MPI B offsets, in 16-byte descriptor units: the descriptor of a
             // stage's tile is built once and advanced by these (the 14-bit start field does
             // not carry: shared addresses stay below 256 KB)
-            uint32_t boff16[8];
+            uint32_t boff16[CF::MPI];
 _Pragma("unroll")
-            for (int t = 0; t < 8; t++) {
-                const int kk = h * 256 + (j * 8 + t) * 16;
-                boff16[t] = (uint32_t)(((kk >> 6) * TC_ATOM + (kk & 63) * 2) >> 4);
+            for (int t = 0; t < CF::MPI; t++) {
+                const int kk = h * 256 + (j * CF::MPI + t) * 16;
+                boff16[t] = (uint32_t)(((kk >> 6) * CF::ATOM + (kk & 63) * 2) >> 4);
             }
             TC_FOR_UNITS({
                 for (int kc = 0; kc < NK && !failed; kc++, item++) {
-                    const int st = item % TC_NS;
-                    const uint32_t par = (uint32_t)((item / TC_NS) & 1);
+                    const int st = item % CF::NS;
+                    const uint32_t par = (uint32_t)((item / CF::NS) & 1);
                     const int pb = item & 1;
                     const int fill = 2 * item + h;   // the A buffer the decode warps filled
                     const int ab = fill % TM::NA;
@@ -360,13 +373,13 @@ _Pragma("unroll")
                     if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t dtm = tmem + (uint32_t)(pb * TM::PCOLS + mi * TM::PW);
-                    const unsigned char *sw = smem + (size_t)st * TC_STAGE;
+                    const unsigned char *sw = smem + (size_t)st * CF::STAGE;
                     const uint32_t bh = s_addr(sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
-                    const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * 128 + j * 64);
+                    const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * 128 + j * CF::MPI * 8);
                     const uint64_t dh = sw128_desc(bh);
-                    // the atom pair's hi and lo rows as one N = 16 operand
+                    // the atom's hi and lo rows as one N = 2 NP operand
 _Pragma("unroll")
-                    for (int t = 0; t < 8; t++)                   // K16 steps of this quarter
+                    for (int t = 0; t < CF::MPI; t++)             // K16 steps of this issuer
                         mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
                     mma_commit(s_addr(&b_afree[ab]));
                     mma_commit(s_addr(&b_empty[st]));   // also tells the epilogue (no pfull commit)
@@ -387,18 +400,18 @@ _Pragma("unroll")
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         TC_FOR_UNITS({
             for (int kc = 0; kc < NK && !failed; kc++, item++) {
-                const int st = item % TC_NS;
-                const uint32_t par = (uint32_t)((item / TC_NS) & 1);
+                const int st = item % CF::NS;
+                const uint32_t par = (uint32_t)((item / CF::NS) & 1);
                 // the A buffer this warp fills: half h of this stage
                 const int fill = 2 * item + h;
-                const int ab = fill % TcTmem<PHASE>::NA;
-                const uint32_t apar = (uint32_t)((fill / TcTmem<PHASE>::NA) & 1);
+                const int ab = fill % CF::NA;
+                const uint32_t apar = (uint32_t)((fill / CF::NA) & 1);
                 if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
                 if (!bar_wait(s_addr(&b_afree[ab]), apar ^ 1u)) { failed = true; break; }
-                const unsigned char *sw = smem + (size_t)st * TC_STAGE;
+                const unsigned char *sw = smem + (size_t)st * CF::STAGE;
                 const unsigned char *row = sw + boxbase + h * hbox + boxrow * 128;
                 const uint2 sc = *reinterpret_cast<const uint2 *>(sw + TC_W_BYTES + r * 16 + h * 8);
-                const uint32_t atm = tmem + lane_addr + (uint32_t)(TcTmem<PHASE>::ACOL0 + ab * 128);
+                const uint32_t atm = tmem + lane_addr + (uint32_t)(CF::ACOL0 + ab * 128);
                 // 8 groups of 32 in this K half, four at a time: the four loads go first (a
                 // load placed after a tcgen05.st would wait for it)
 _Pragma("unroll")
@@ -442,23 +455,23 @@ _Pragma("unroll")
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         TC_FOR_UNITS({
             // the pass's per-token metadata, one token per lane, fetched before the stages
-            const int nl = lane & (TC_NP - 1);
+            const int nl = lane & (CF::NP - 1);
             const bool vl = nl < npt;
             const int ex_l = vl ? Xe[q0 + tb + nl] : 0;
             const int dst_l = (PHASE == 1 && vl) ? p.pair_dst[q0 + tb + nl] : 0;
-            float acc[TC_NP];
+            float acc[CF::NP];
 _Pragma("unroll")
-            for (int n = 0; n < TC_NP; n++) acc[n] = 0.0f;
+            for (int n = 0; n < CF::NP; n++) acc[n] = 0.0f;
             for (int kc = 0; kc < NK && !failed; kc++, item++) {
                 const int pb = item & 1;
                 // empty[st] completes once all four issuers' MMAs of the stage are done: the
                 // partials are final. (The MMAs run at most two stages ahead of this wait --
                 // they need pfree -- so the phase cannot be lapped.)
-                if (!bar_wait(s_addr(&b_empty[item % TC_NS]), (uint32_t)((item / TC_NS) & 1))) { failed = true; break; }
+                if (!bar_wait(s_addr(&b_empty[item % CF::NS]), (uint32_t)((item / CF::NS) & 1))) { failed = true; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                using TM = TcTmem<PHASE>;
+                using TM = CF;
                 const uint32_t pt = tmem + lane_addr + (uint32_t)(pb * TM::PCOLS);
-                {
+                if constexpr (CF::NMMA == 4) {
                     // four issuers x (hi products in columns 0..7, lo products in 8..15)
                     uint32_t d0[16], d1[16], d2[16], d3[16];
                     tmem_ld16(pt, d0);
@@ -467,13 +480,33 @@ _Pragma("unroll")
                     tmem_ld16(pt + 3 * TM::PW, d3);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 _Pragma("unroll")
-                    for (int n = 0; n < TC_NP; n++) {
+                    for (int n = 0; n < CF::NP; n++) {
                         float v = (__uint_as_float(d0[n]) + __uint_as_float(d1[n])) +
                                   (__uint_as_float(d2[n]) + __uint_as_float(d3[n]));
                         if (lo_any)
-                            v += (__uint_as_float(d0[n + TC_NP]) + __uint_as_float(d1[n + TC_NP])) +
-                                 (__uint_as_float(d2[n + TC_NP]) + __uint_as_float(d3[n + TC_NP]));
+                            v += (__uint_as_float(d0[n + CF::NP]) + __uint_as_float(d1[n + CF::NP])) +
+                                 (__uint_as_float(d2[n + CF::NP]) + __uint_as_float(d3[n + CF::NP]));
                         acc[n] += v;
+                    }
+                } else {
+                    // two issuers (one per K half), 16 tokens at a time: hi products in
+                    // columns c..c+15, their lo products NP columns further
+_Pragma("unroll")
+                    for (int c = 0; c < CF::NP; c += 16) {
+                        uint32_t h0[16], h1[16], l0[16], l1[16];
+                        tmem_ld16(pt + c, h0);
+                        tmem_ld16(pt + TM::PW + c, h1);
+                        if (lo_any) {
+                            tmem_ld16(pt + CF::NP + c, l0);
+                            tmem_ld16(pt + TM::PW + CF::NP + c, l1);
+                        }
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+_Pragma("unroll")
+                        for (int n = 0; n < 16; n++) {
+                            float v = __uint_as_float(h0[n]) + __uint_as_float(h1[n]);
+                            if (lo_any) v += __uint_as_float(l0[n]) + __uint_as_float(l1[n]);
+                            acc[c + n] += v;
+                        }
                     }
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -484,17 +517,17 @@ _Pragma("unroll")
             if (PHASE == 0) {
                 // lanes 64..127 hold the up rows: hand them to the gate lanes 0..63
                 if (r >= 64)
-                    for (int n = 0; n < TC_NP; n++) xch[(r - 64) * TC_NP + n] = acc[n];
+                    for (int n = 0; n < CF::NP; n++) xch[(r - 64) * CF::NP + n] = acc[n];
                 asm volatile("bar.sync 2, 128;" ::: "memory");
                 if (r < 64) {
-                    // n runs over all TC_NP with a warp-uniform guard: acc stays in registers
+                    // n runs over all CF::NP with a warp-uniform guard: acc stays in registers
 _Pragma("unroll")
-                    for (int n = 0; n < TC_NP; n++) {
+                    for (int n = 0; n < CF::NP; n++) {
                         if (n < npt) {
                             const int q = q0 + tb + n;
                             const int ex = __shfl_sync(0xffffffffu, ex_l, n);
                             const float gv = ldexpf(acc[n], ex);
-                            const float uv = ldexpf(xch[r * TC_NP + n], ex);
+                            const float uv = ldexpf(xch[r * CF::NP + n], ex);
                             const float hv = act == K3GPU_ACT_SITU ? act_situ(gv, uv, b1, b2) : act_swiglu(gv, uv);
                             p.H[(size_t)q * bank.I + ub * 64 + r] = hv;
                         }
@@ -503,7 +536,7 @@ _Pragma("unroll")
                 asm volatile("bar.sync 2, 128;" ::: "memory");
             } else {
 _Pragma("unroll")
-                for (int n = 0; n < TC_NP; n++) {
+                for (int n = 0; n < CF::NP; n++) {
                     if (n < npt) {
                         const int ex = __shfl_sync(0xffffffffu, ex_l, n);
                         const int dst = __shfl_sync(0xffffffffu, dst_l, n);
@@ -638,7 +671,8 @@ bool tc_bank_ok(const K3GpuExpertBank &b)
 }
 
 static std::mutex g_tc_mu;
-static bool g_tc_ready[64] = {};   // per device: the shared-memory opt-in is done
+static bool g_tc_ready[64][2] = {};   // per device and shape: the shared-memory opt-in is done
+int g_tc_shape = 0;                   // 0: by tokens per expert, 1: sparse always, 2: dense always
 
 int tc_pack_pairs_launch(const MoePlan &p, const float *z, int L, int P, int E, cudaStream_t s)
 {
@@ -647,8 +681,9 @@ int tc_pack_pairs_launch(const MoePlan &p, const float *z, int L, int P, int E, 
     return launch_status();
 }
 
-int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, int P, int act, float b1,
-                    float b2, cudaStream_t s)
+template <class CF>
+static int tc_shape_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, int P, int act, float b1,
+                           float b2, cudaStream_t s, int shape_id)
 {
     const int L = bank.L, I = bank.I;
     const unsigned long long bytes = (unsigned long long)bank.n_experts * (unsigned long long)bank.stride;
@@ -659,29 +694,32 @@ int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, in
                     CU_TENSOR_MAP_SWIZZLE_128B);
         if (!st) st = tc_map(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, L / 32, (long long)(bytes / (L / 32)), 16, 64,
                              CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zh, L, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zl, L, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zh, L, P, 64, CF::NP, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.zl, L, P, 64, CF::NP, CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
         st = tc_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, I / 2, (long long)(bytes / (I / 2)), 128, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B);
         if (!st) st = tc_map(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, bank.base, I / 32, (long long)(bytes / (I / 32)), 16, 128,
                              CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hh, I, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hl, I, P, 64, TC_NP, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hh, I, P, 64, CF::NP, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st) st = tc_map(&bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.hl, I, P, 64, CF::NP, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (st) return st;
-    // the shared-memory opt-in, once per device (a function's attributes belong to each
-    // device's context)
+    // the shared-memory opt-in, once per device and shape (a function's attributes belong to
+    // each device's context)
     int dev = 0;
     if ((st = cuda_status(cudaGetDevice(&dev)))) return st;
     if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
     {
         std::lock_guard<std::mutex> lock(g_tc_mu);
-        if (!g_tc_ready[dev]) {
-            st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-            if (!st) st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+        if (!g_tc_ready[dev][shape_id]) {
+            st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<0, CF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  CF::SMEM));
+            if (!st)
+                st = cuda_status(cudaFuncSetAttribute(moe_tc_kernel<1, CF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      CF::SMEM));
             if (st) return st;
-            g_tc_ready[dev] = true;
+            g_tc_ready[dev][shape_id] = true;
         }
     }
     int sms = 148;
@@ -693,14 +731,31 @@ int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, in
         a.K = L; a.UE = I / 64;
         a.wys = bank.stride / pl; a.wy1 = bank.p1 / pl; a.wy3 = bank.p3 / pl;
         a.sys = bank.stride / ql; a.sy1 = bank.s1 / ql; a.sy3 = bank.s3 / ql;
-        moe_tc_kernel<0><<<sms, TC_THREADS, TC_SMEM, s>>>(wm, sm, bh, bl, p, bank, a, act, b1, b2);
+        moe_tc_kernel<0, CF><<<sms, CF::THREADS, CF::SMEM, s>>>(wm, sm, bh, bl, p, bank, a, act, b1, b2);
     } else {
         a.K = I; a.UE = L / 128;
         a.wys = bank.stride / pi; a.wy1 = bank.p2 / pi; a.wy3 = 0;
         a.sys = bank.stride / qi; a.sy1 = bank.s2 / qi; a.sy3 = 0;
-        moe_tc_kernel<1><<<sms, TC_THREADS, TC_SMEM, s>>>(wm, sm, bh, bl, p, bank, a, act, b1, b2);
+        moe_tc_kernel<1, CF><<<sms, CF::THREADS, CF::SMEM, s>>>(wm, sm, bh, bl, p, bank, a, act, b1, b2);
     }
     return launch_status();
+}
+
+// The pass shape by the call's tokens per routed expert: the sparse shape while most experts
+// need one pass of 8, the dense one once they need several (TC_DENSE_MIN and up on average).
+constexpr double TC_DENSE_MIN = 12.0;
+
+bool tc_dense_for(double tokens_per_expert)
+{
+    return g_tc_shape == 2 || (g_tc_shape == 0 && tokens_per_expert >= TC_DENSE_MIN);
+}
+
+int tc_phase_launch(int phase, const MoePlan &p, const K3GpuExpertBank &bank, int P, int act, float b1,
+                    float b2, cudaStream_t s, double tokens_per_expert)
+{
+    if (tc_dense_for(tokens_per_expert))
+        return tc_shape_launch<TcDense>(phase, p, bank, P, act, b1, b2, s, 1);
+    return tc_shape_launch<TcSparse>(phase, p, bank, P, act, b1, b2, s, 0);
 }
 
 int tc_bank_scan(const K3GpuExpertBank &b, uint8_t *safe, cudaStream_t s)

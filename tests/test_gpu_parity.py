@@ -168,6 +168,36 @@ def test_moe_expert_kernels_fp32_inputs_many_tokens(k3, which):
     assert_clean(k3)
 
 
+@pytest.mark.parametrize("shape", [2, 3], ids=["dense32", "sparse8"])
+@pytest.mark.parametrize("fp32_inputs", [False, True], ids=["bf16in", "fp32in"])
+def test_moe_tcgen05_pass_shapes_many_tokens(k3, shape, fp32_inputs):
+    """The tcgen05 expert kernels forced into each pass shape on a certified bank with many
+    tokens per expert: 8 routed experts top-3 over 100 tokens (37.5 an expert on average,
+    so the dense shape's 32-token pass needs a second pass on some and the sparse shape
+    five), with and without live lo halves, and the automatic choice beside them."""
+    L, I, n, ns, k, T = 1024, 512, 8, 1, 3, 100
+    rng = np.random.default_rng(61 + shape)
+    bank, lay = O.make_bank(rng, n + ns, L, I, std=0.05, w13_std=0.1)
+    x = rng.standard_normal((T, L), dtype=np.float32)
+    if not fp32_inputs:
+        x = GI.bf16_round(x)
+    W = rng.standard_normal((n, L), dtype=np.float32) * np.float32(0.02)
+    bias = rng.standard_normal(n, dtype=np.float32) * np.float32(0.01)
+    kb = k3.ExpertBank(dev(bank), n + ns, L, I)
+    assert kb.scan() == 0
+    ri, rw = O.router(x, W, bias, k)
+    ref = O.moe_routed(x, ri, rw, bank, lay, L, I, k, n, ns, 1)
+    for which in (shape, 0):
+        k3.check(k3.lib.k3gpu_moe_select_kernels(which), "select")
+        try:
+            out, idx, wt = k3.moe_layer(dev(x), dev(W), dev(bias), kb, k, n, ns, 1)
+        finally:
+            k3.check(k3.lib.k3gpu_moe_select_kernels(0), "select")
+        np.testing.assert_array_equal(host(idx), ri)
+        assert rel_l2(host(out), ref) < 1e-5, (which, rel_l2(host(out), ref))
+    assert_clean(k3)
+
+
 @pytest.mark.parametrize("fp32_inputs", [False, True], ids=["bf16in", "fp32in"])
 def test_moe_tcgen05_path_vs_oracle(k3, fp32_inputs):
     """The tcgen05 expert kernels (bank certified by k3gpu_bank_scan): benchmark config-2
