@@ -16,6 +16,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libk3gpu.so")
+SHIM = os.path.join(PKG, "libk3shim.so")   # the reference's host-pointer k3_* names over LIB
+SHIM_OPS = os.path.join(PKG, "libk3shim_ops.so")   # the same without k3_router (the op suite's gate)
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -50,6 +52,11 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if force or _stale(LIB, objs):
         subprocess.run([NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", LIB,
                         "-lcudart"], check=True)
+    shim_src = os.path.join(CSRC, "shim.cu")
+    for out, extra in ((SHIM, []), (SHIM_OPS, ["-DK3SHIM_NO_ROUTER"])):
+        if force or _stale(out, [shim_src, LIB] + headers):
+            subprocess.run([NVCC, *ARCH, *FLAGS, *extra, "-shared", shim_src, "-o", out, "-L" + PKG, "-lk3gpu",
+                            "-Xlinker", "-rpath,$ORIGIN", "-lcudart"], check=True)
     return LIB
 
 

@@ -97,3 +97,20 @@ def test_ep_arena_holds_every_region():
         assert m.lib.k3gpu_ep_arena_bytes(world, cap, L, K) == want
     assert m.lib.k3gpu_ep_arena_bytes(9, 64, 7168, 8) == 0          # above K3GPU_EP_MAX_WORLD
     assert m.lib.k3gpu_ep_arena_bytes(2, 0, 7168, 8) == 0
+
+
+def test_shim_exports_the_reference_names():
+    """libk3shim.so carries the reference's own host-pointer names over the GPU kernels (the
+    op-suite build the same without k3_router), resolving to the library's C ABI."""
+    m = k3lib.load()
+    pkg = os.path.dirname(m.LIB_PATH)
+    for lib, names in (("libk3shim.so", ["k3_router", "k3_rmsnorm", "k3_attn_res", "k3_kda_step",
+                                          "k3_mxfp4_dequant"]),
+                       ("libk3shim_ops.so", ["k3_rmsnorm", "k3_attn_res", "k3_kda_step", "k3_mxfp4_dequant"])):
+        out = subprocess.run(["nm", "-D", "--defined-only", os.path.join(pkg, lib)], capture_output=True, text=True,
+                             check=True).stdout
+        exported = set(re.findall(r" T (\w+)$", out, flags=re.M))
+        assert set(names) <= exported, (lib, sorted(exported))
+        if lib == "libk3shim_ops.so":
+            assert "k3_router" not in exported
+        C.CDLL(os.path.join(pkg, lib))      # loads, its dependency on libk3gpu.so resolves
