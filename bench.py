@@ -181,10 +181,13 @@ def tree_topology(nodes=C4_TREE, branch=C4_BRANCH, depth=C4_DEPTH, weights=(0.5,
     return parent, chain
 
 
-def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE):
+def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1):
     """The config-4 slice on the device with random weights: bf16 projections N(0, 0.02),
     unit norms, AttnRes folds N(0, 0.02), router N(0, 0.02) with bias N(0, 0.01), the KDA
-    decay parameters of the reference's tiny-model recipe, MXFP4 experts N(0, 0.02)."""
+    decay parameters of the reference's tiny-model recipe, MXFP4 experts N(0, 0.02).
+    world > 1: this rank keeps routed experts rank * 384/world .. of every layer's bank (the
+    bank drawn whole, then sliced, so the experts are those of the one-GPU model) and the
+    shared expert as a bank of its own; returns (model, shared banks), else (model, None)."""
     import torch
     c = C4
     g = torch.Generator(device=dev)
@@ -205,7 +208,7 @@ def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE):
     def ones(k):
         return torch.ones(k, device=dev)
 
-    layers, banks = [], []
+    layers, banks, shared = [], [], []
     for L in range(c["num_hidden_layers"]):
         mla = (L + 1) in c["full_attn_layers"]
         d = {"kind": "mla" if mla else "kda", "in_norm": ones(E), "post_norm": ones(E),
@@ -219,12 +222,23 @@ def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE):
                      b=bf(H, E), q_conv=f32(P, K, std=0.4), k_conv=f32(P, K, std=0.4), v_conv=f32(P, K, std=0.4),
                      A_log=torch.linspace(-0.4, 1.2, H, device=dev), dt_bias=f32(P, std=0.5), o_norm=ones(D))
         layers.append(d)
-        bank, _, _ = make_bank_device(n + c["num_shared_experts"], E, I_, seed + 1000 + L, dev)
-        kb = k3.ExpertBank(bank, n + c["num_shared_experts"], E, I_)
+        ns = c["num_shared_experts"]
+        bank, _, stride = make_bank_device(n + ns, E, I_, seed + 1000 + L, dev)
+        if world > 1:
+            nl = n // world
+            view = bank.view(n + ns, stride)
+            kb = k3.ExpertBank(view[rank * nl:(rank + 1) * nl].reshape(-1).clone(), nl, E, I_)
+            sb = k3.ExpertBank(view[n:n + ns].reshape(-1).clone(), ns, E, I_)
+            sb.scan()
+            shared.append(sb)
+            del view, bank
+        else:
+            kb = k3.ExpertBank(bank, n + ns, E, I_)
         kb.scan()
         banks.append(kb)
     top = {"embed": bf(V, E), "lm_head": bf(V, E), "norm": ones(E), "out_res_fold": f32(E)}
-    return k3.Model(dict(c), layers, top, banks, B=B, max_T=max_T, kv_cap=kv_cap, device=dev)
+    model = k3.Model(dict(c), layers, top, banks, B=B, max_T=max_T, kv_cap=kv_cap, device=dev)
+    return model, (shared if world > 1 else None)
 
 
 def c4_fill_state(model, seed, ctx):
@@ -293,30 +307,44 @@ def c4_trees(cont, parent, chain, steps, V, seed):
     return tok
 
 
-def run_c4(args, k3, dev, local):
-    """The headline: tree verification steps on the config-4 slice at B sequences. A step is
-    one verify sweep of every sequence's 64-node tree through the 8 layers and the lm_head
-    (k3gpu_model_verify), the on-device greedy tree walk (k3gpu_accept_tree_greedy), the
-    read of the accepted paths and the commit (k3gpu_model_commit: KDA log replay, MLA rows
-    gathered, cached advanced). Accepted tok/s counts every id a step emits (accepted
-    drafts plus the bonus id), over all sequences."""
+def run_c4(args, k3, dev, local, rank=0, world=1):
+    """The headline: tree verification steps on the config-4 slice at B sequences per GPU. A
+    step is one verify sweep of every sequence's 64-node tree through the 8 layers and the
+    lm_head (k3gpu_model_verify), the on-device greedy tree walk (k3gpu_accept_tree_greedy),
+    the read of the accepted paths and the commit (k3gpu_model_commit: KDA log replay, MLA
+    rows gathered, cached advanced). Accepted tok/s counts every id a step emits (accepted
+    drafts plus the bonus id), over all sequences of all ranks. world > 1: the same slice
+    with every layer's 384 routed experts split 384/world per GPU (config 5's sharding), the
+    token rows exchanged through peer memory inside the model's MoE steps
+    (k3gpu_moe_layer_ep); each rank verifies its own B sequences (weak scaling), times are
+    the max over ranks, and one sweep is checked against the unsharded model on rank 0."""
     import torch
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
     B, steps, warm = args.c4_B, args.steps, args.warmup
     kv_cap = C4_CTX + (steps + warm + 2) * (C4_DEPTH + 1) + C4_TREE + 8
     t_build = time.perf_counter()
-    model = make_c4_model(k3, dev, B, args.seed, kv_cap)
+    model, shared = make_c4_model(k3, dev, B, args.seed, kv_cap, rank=rank, world=world)
+    exchange = None
+    if world > 1:
+        exchange = load_ep().EpExchange(k3, B * C4_TREE, C4["hidden_size"], C4["num_experts_per_token"],
+                                        C4["num_experts"] // world)
+        model.set_ep(exchange, shared)
     build_s = time.perf_counter() - t_build
     parent, chain = tree_topology()
     parent_dev = torch.tensor(parent, dtype=torch.int32, device=dev)
     V = C4["vocab_size"]
-    c4_fill_state(model, args.seed + 1, C4_CTX)
+    seed_r = args.seed + 7919 * rank          # this rank's own sequences
+    c4_fill_state(model, seed_r + 1, C4_CTX)
     snap = c4_snapshot(model)
     # the model's own greedy continuation from a random pending id (untimed, one position per
     # sweep), so the trees' most probable branch can carry it
     depth = len(chain) - 1
     n_cont = (steps + warm + 2) * (depth + 1) + 1
-    rng = np.random.default_rng(args.seed + 2)
-    x = torch.tensor(rng.integers(0, V, size=(B, 1)), dtype=torch.int32, device=dev)
+    rng = np.random.default_rng(seed_r + 2)
+    x0 = torch.tensor(rng.integers(0, V, size=(B, 1)), dtype=torch.int32, device=dev)
+    x = x0
     cont = [[int(x[b, 0])] for b in range(B)]
     for _ in range(n_cont):
         arg, _ = model.verify(x)
@@ -325,7 +353,7 @@ def run_c4(args, k3, dev, local):
         for b in range(B):
             cont[b].append(int(x[b, 0]))
     c4_restore(model, snap, C4_CTX)
-    tok = c4_trees(cont, parent, chain, warm + steps, V, args.seed + 3)
+    tok = c4_trees(cont, parent, chain, warm + steps, V, seed_r + 3)
     tok_dev = torch.from_numpy(tok).to(dev)
     stream = torch.cuda.current_stream()
     n_path_host = torch.empty((B,), dtype=torch.int32).pin_memory()
@@ -341,21 +369,43 @@ def run_c4(args, k3, dev, local):
         model.commit(keep, path_host.tolist())
         return sum(keep), emit
 
-    accepted = 0
+    def sync_all():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        return float(t.item())
+
     for s in range(warm):
         step(s, tok_dev[s])
     if args.profile_c4:   # one step inside an NVTX range, for an ncu launch list
-        torch.cuda.synchronize()
+        sync_all()
         torch.cuda.nvtx.range_push("c4_step")
         step(warm, tok_dev[warm])
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
+        if exchange:
+            exchange.close()
         model.close()
         return None
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    torch.cuda.synchronize()
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    accepted = 0
+    sync_all()
     l0 = k3.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -363,10 +413,13 @@ def run_c4(args, k3, dev, local):
         a, _ = step(s, tok_dev[s])
         accepted += a
     e1.record(stream)
-    torch.cuda.synchronize()
+    sync_all()
     launches = k3.launch_count() - l0
-    dev_ms = e0.elapsed_time(e1) / steps
-    status = k3.device_status(dev.index)
+    dev_ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    accepted = sum_over_ranks(accepted)
+    status = int(max_over_ranks(k3.device_status(dev.index)))
+    owners_ok = min(model.ep_owners_ok()) if exchange else 1
+    owners_ok = -max_over_ranks(-owners_ok)
 
     # end to end through the public calls with host buffers: each step's tree ids from pinned
     # host memory, the emitted ids and their count back to the host
@@ -378,6 +431,7 @@ def run_c4(args, k3, dev, local):
         ids_dev.copy_(tok_host[s], non_blocking=True)
         step(s, ids_dev)
     acc_e2e = 0
+    sync_all()
     e0.record(stream)
     for s in range(warm, warm + steps):
         ids_dev.copy_(tok_host[s], non_blocking=True)
@@ -385,17 +439,19 @@ def run_c4(args, k3, dev, local):
         emit_host.copy_(emit, non_blocking=True)
         acc_e2e += a
     e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / steps
-    clk = clocks.stop()
+    sync_all()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    acc_e2e = sum_over_ranks(acc_e2e)
+    clk = clocks.stop() if clocks else None
 
     # the phases of one step (verify, accept + path read, commit) and the dominant kernel:
-    # the gate/up expert stream of the last layer's MoE call, its bytes from that call's
-    # unique experts (all 384 at 16 x 64 tokens)
+    # the gate/up expert stream of the last layer's (local) expert call, its bytes from that
+    # call's unique experts on this rank
     c4_restore(model, snap, C4_CTX)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     ph_steps, moe_ph = [], []
     k3.moe_phase_timing(True)
+    idx_last = None
     for s in range(warm):
         ev[0].record(stream)
         _, lg = model.verify(tok_dev[s], parent=parent)
@@ -405,7 +461,7 @@ def run_c4(args, k3, dev, local):
         ph_path = path.tolist()
         ev[2].record(stream)
         moe_ph.append(k3.moe_phase_ms())
-        idx_last = model.last_routing(C4_TREE).cpu().numpy()
+        idx_last = model.last_routing(C4_TREE).clone()
         model.commit(keep, ph_path)
         ev[3].record(stream)
         torch.cuda.synchronize()
@@ -414,50 +470,105 @@ def run_c4(args, k3, dev, local):
     ph = np.median(np.array(ph_steps), axis=0).tolist()
     mph = np.median(np.array(moe_ph), axis=0).tolist()
     R = B * C4_TREE
-    E, I_, n_exp = C4["hidden_size"], C4["moe_intermediate_size"], C4["num_experts"]
-    u = len(np.unique(idx_last[idx_last >= 0])) + C4["num_shared_experts"]
-    pairs = R * (TOPK + C4["num_shared_experts"])
+    E, I_, n_exp, ns = C4["hidden_size"], C4["moe_intermediate_size"], C4["num_experts"], C4["num_shared_experts"]
     w13 = 2 * I_ * (E // 2 + E // 32)
-    gateup_bytes = u * w13 + R * E * 4 + pairs * I_ * 4
+    if dist:
+        # this rank's experts in the last layer's call: those some rank's tokens chose
+        alls = [torch.empty_like(idx_last) for _ in range(world)]
+        dist.all_gather(alls, idx_last)
+        g_idx = torch.cat(alls).cpu().numpy()
+        nl = n_exp // world
+        mine = g_idx[(g_idx >= rank * nl) & (g_idx < (rank + 1) * nl)]
+        u = len(np.unique(mine))
+        rows = int(((g_idx // nl) == rank).any(axis=1).sum())
+        gateup_bytes = u * w13 + rows * E * 4 + int(mine.size) * I_ * 4
+    else:
+        il = idx_last.cpu().numpy()
+        u = len(np.unique(il[il >= 0])) + ns
+        pairs = R * (TOPK + ns)
+        gateup_bytes = u * w13 + R * E * 4 + pairs * I_ * 4
     hbm, peak_kind = peaks()
     achieved = gateup_bytes / (mph[2] * 1e-3) / 1e9 if mph[2] > 0 else 0.0
+    achieved = -max_over_ranks(-achieved)        # the slowest rank's stream
     traffic = None
     tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and world == 1:
         try:
             ratio = float(json.load(open(tp))["traffic_over_algorithmic"])
             traffic = int(ratio * gateup_bytes)
         except (OSError, ValueError, KeyError, TypeError):
             traffic = None
+    parity = c4_ep_parity(args, k3, dev, model, snap, tok_dev[warm], parent, rank, world, dist) if dist else None
+    if exchange:
+        exchange.close()
     model.close()
     del model
     torch.cuda.empty_cache()
-    full = steps * B * (depth + 1)
+    full = steps * B * (depth + 1) * world
     return {
         "value": round(accepted / (dev_ms * steps * 1e-3), 2), "ms_per_step": round(dev_ms, 3),
         "accepted_per_step": round(accepted / steps, 2), "accepted_fraction_of_planted": round(accepted / full, 4),
         "e2e": {"value": round(acc_e2e / (e2e_ms * steps * 1e-3), 2), "unit": "accepted tok/s",
-                "h2d_bytes_per_step": int(B * C4_TREE * 4), "d2h_bytes_per_step": int(B * 4 + 2 * B * C4_TREE * 4),
-                "ms_per_step": round(e2e_ms, 3)},
+                "h2d_bytes_per_step": int(B * C4_TREE * 4 * world),
+                "d2h_bytes_per_step": int((B * 4 + 2 * B * C4_TREE * 4) * world), "ms_per_step": round(e2e_ms, 3)},
         "verify_step_ms": round(ph[0], 3), "accept_ms": round(ph[1], 3), "commit_ms": round(ph[2], 3),
         "moe_phase_ms_last_layer": {"router": round(mph[0], 4), "plan": round(mph[1], 4),
                                     "gateup": round(mph[2], 4), "down": round(mph[3], 4),
                                     "combine": round(mph[4], 4)},
-        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<0> (gate/up, last layer's MoE call)",
+        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<0> (gate/up, last layer's expert call)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(gateup_bytes),
-                     "units": f"{u} experts x {w13} B + rows"},
+                     "units": f"{u} experts x {w13} B + rows" + (" (rank 0's; min over ranks)" if dist else "")},
         "gpu_launches": int(launches), "device_status": status, "clocks": clk, "build_s": round(build_s, 1),
-        "config": c4_config(B, R),
+        "ep": None if not dist else {"transport": "peer memory inside the model's MoE steps (k3gpu_moe_layer_ep)",
+                                     "experts_per_gpu": n_exp // world, "owners_ok": bool(owners_ok >= 1),
+                                     "parity": parity},
+        "config": c4_config(B, R, world),
     }
 
 
-def c4_config(B, R=None):
+def c4_ep_parity(args, k3, dev, model, snap, ids, parent, rank, world, dist):
+    """One tree sweep of the expert-parallel model against the unsharded model on rank 0
+    (the same weights, rank 0's state and tree): argmax equal at every node, logits within
+    rel-L2 1e-3. A failed check ends the run without a line."""
+    import torch
+    c4_restore(model, snap, C4_CTX)
+    arg, lg = model.verify(ids, parent=parent)
+    torch.cuda.synchronize()
+    arg_ep, lg_ep = arg.cpu(), lg.float().cpu()
+    model.commit([0] * model.B, [[0] * C4_TREE for _ in range(model.B)])
+    verdict = torch.zeros(3, dtype=torch.float64, device=dev)
+    if rank == 0:
+        full, _ = make_c4_model(k3, dev, model.B, args.seed, model.kv_cap)
+        c4_fill_state(full, args.seed + 1, C4_CTX)
+        a1, l1 = full.verify(ids, parent=parent)
+        torch.cuda.synchronize()
+        verdict[0] = float((a1.cpu() != arg_ep).sum())
+        verdict[1] = float((l1.float().cpu() - lg_ep).norm() / l1.float().cpu().norm())
+        full.close()
+        del full
+        torch.cuda.empty_cache()
+    verdict[2] = float(k3.device_status(dev.index))
+    dist.all_reduce(verdict, op=dist.ReduceOp.MAX)
+    v = verdict.tolist()
+    out = {"argmax_mismatches": int(v[0]), "logits_rel_l2": float(f"{v[1]:.3g}"), "status_max": int(v[2]),
+           "reference": "the unsharded slice on one GPU, rank 0's state and tree"}
+    # the north star's logits bound (rel-L2 1e-3): the expert sum runs per owner, then across
+    # owners, and eight random layers carry the fp32 reordering to the logits
+    if v[0] != 0 or not v[1] < 1e-3 or v[2] != 0:
+        raise SystemExit(f"expert-parallel model failed its check, no line printed: {out}")
+    return out
+
+
+def c4_config(B, R=None, world=1):
     R = R if R is not None else B * C4_TREE
     E, V = C4["hidden_size"], C4["vocab_size"]
+    ep = "" if world == 1 else (f", expert parallel over {world} GPUs ({C4['num_experts'] // world} experts per GPU, "
+                                f"config 5's sharding), B sequences per GPU")
     return {"workload": f"K3 8-layer slice tree verify (benchmark config 4): B={B} sequences x "
                         f"{C4_TREE}-node draft tree (branching {C4_BRANCH}, depth {C4_DEPTH}) over a "
-                        f"{C4_CTX}-position cache, greedy acceptance",
+                        f"{C4_CTX}-position cache, greedy acceptance{ep}",
+            "parallelism": f"ep{world}" if world > 1 else "single",
             "layers": "6 KDA + 2 MLA (3:1), every layer MoE", "d_model": E, "vocab": V,
             "moe": "384 routed top-8 + 1 shared, FFN 2048 SwiGLU, MXFP4 (E2M1 + E8M0/32) N(0,0.02)",
             "kda": "32 heads x 128", "mla": "64 heads, q_lora 1536, kv_lora 512, nope 128, rope 64, v 128",
@@ -647,7 +758,7 @@ def run_reference(args):
         "ms_per_step": round(1000 * step, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 / MXFP4 weights x fp32 activations, double accumulate (reference CPU)",
         "data": "synthetic (seeded random weights, random 32k cache, forced drafts)",
-        "config": c4_config(args.c4_B),
+        "config": c4_config(args.c4_B, None, args.gpus),
         "cpu_baseline": {"value": round(val, 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
                          "sample": c4_sample_text(nth)},
         "e2e": {"value": round(val, 4), "unit": "accepted tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -1166,9 +1277,14 @@ def run_b200(args):
     if world > 1:
         from datetime import timedelta
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
         try:
-            return run_ep(args, k3, rank, world, dev)
+            if args.ep_workload == "c2":
+                return run_ep(args, k3, rank, world, dev)
+            c4 = run_c4(args, k3, dev, local, rank, world)
+            if rank == 0 and c4 is not None:
+                print(json.dumps(c4_line(args, c4, world, None, None)))
+            return 0
         finally:
             dist.destroy_process_group()
 
@@ -1181,9 +1297,14 @@ def run_b200(args):
     if c4 is None:        # --profile-c4
         return 0
     cpu = None if args.no_cpu else c4_cpu_baseline(args)
+    print(json.dumps(c4_line(args, c4, 1, cpu, rows)))
+    return 0
+
+
+def c4_line(args, c4, world, cpu, rows):
     line = {
         "metric": METRIC, "value": c4["value"], "unit": "accepted tok/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": c4["ms_per_step"],
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": c4["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "MXFP4 experts and bf16 projections x fp32 activations, fp32 accumulate",
         "data": "synthetic (seeded random weights, random 32k cache, forced drafts)",
@@ -1193,10 +1314,9 @@ def run_b200(args):
         "accepted_fraction_of_planted": c4["accepted_fraction_of_planted"],
         "moe_phase_ms_last_layer": c4["moe_phase_ms_last_layer"],
         "gpu_launches": c4["gpu_launches"], "device_status": c4["device_status"],
-        "clocks": c4["clocks"], "cpu_baseline": cpu, "build_s": c4["build_s"], "rows": rows,
+        "clocks": c4["clocks"], "cpu_baseline": cpu, "build_s": c4["build_s"], "ep": c4["ep"], "rows": rows,
     }
-    print(json.dumps(line))
-    return 0
+    return line
 
 
 def c4_reference_sample(args, bank_np=None, offs=None, stride=None, nth=None, seed=0):
@@ -1279,6 +1399,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-rows", action="store_true", help="skip the other rows' kernel timings")
     ap.add_argument("--no-tc", action="store_true", help="skip the bank scan: mma.sync expert kernels only")
+    ap.add_argument("--ep-workload", default="c4", choices=["c4", "c2"],
+                    help="--gpus N > 1: the config-4 slice expert parallel (default) or one config-2 layer")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="--gpus N > 1: token rows through peer memory (default) or NCCL all-to-all")
     ap.add_argument("--only-row", default=None,

@@ -714,6 +714,39 @@ int k3gpu_ep_return(const K3GpuEpGroup *g, const float *part, unsigned seq, void
 /* ok [world] (device) receives 1 per owner whose rows arrived. */
 int k3gpu_ep_combine(const K3GpuEpGroup *g, float *out, const int *pos, int T, unsigned seq,
                      int *ok, void *stream);
+/* The single-layer MoE (k3gpu_moe_layer) with its routed experts split over the ranks of g:
+ * this rank's tokens are routed on the replicated gate (global expert ids), their rows
+ * exchanged through peer memory (k3gpu_ep_dispatch / _receive / _return / _combine), this
+ * rank's n_local experts (local, the experts rank * n_local .. + n_local - 1) run on what it
+ * received, the replicated shared experts (shared, n_shared of them, may be NULL when 0) on
+ * its own tokens, and out [T][L] = shared + the owners' partial sums in owner order. Every
+ * rank calls it with the same seq, in the same order (seq 1, 2, ... per exchange step);
+ * topk == g->K, n_routed == world * n_local, T <= g->cap. ok [world] (device) as
+ * k3gpu_ep_combine. Equal to k3gpu_moe_layer over the whole bank to fp32 rounding (the
+ * sum runs per owner, then across owners). */
+size_t k3gpu_moe_layer_ep_workspace(const K3GpuEpGroup *g, int T, int n_shared, int I, int n_routed);
+int k3gpu_moe_layer_ep(float *out, int *idx, float *wt, const float *x, const float *gate_W,
+                       const float *bias, const K3GpuExpertBank *local, const K3GpuExpertBank *shared,
+                       const K3GpuEpGroup *g, unsigned seq, int T, int topk, int n_routed, int n_shared,
+                       int act, float b1, float b2, int renorm, float routed_scale, int *ok,
+                       void *workspace, size_t ws_bytes, void *stream);
+
+/* The whole model (k3gpu_model_*, above) with its MoE steps expert parallel. */
+/* Expert parallel: every layer's MoE step splits its routed experts over the ranks of g
+ * (k3gpu_moe_layer_ep), each rank running its own sequences. Set once after create; every
+ * layer's bank then holds this rank's routed experts (g->n_local of them, the single-layer
+ * MoE form) and shared [n_layers] (host array) the replicated shared experts of each layer.
+ * Every rank must make the same sequence of sweeps (the layers' exchanges pair up by
+ * step number). g->cap >= B * max_T. workspace (256-byte aligned, caller-owned) of
+ * k3gpu_model_ep_workspace bytes. k3gpu_model_ep_status reads the last exchange's per-owner
+ * flags (host [world]; synchronises the model's stream): a 0 is an owner whose bounded wait
+ * ran out. */
+size_t k3gpu_model_ep_workspace(const K3GpuModel *m, const K3GpuEpGroup *g);
+int k3gpu_model_set_ep(K3GpuModel *m, const K3GpuEpGroup *g, const K3GpuExpertBank *const *shared,
+                       void *workspace, size_t ws_bytes);
+int k3gpu_model_ep_status(const K3GpuModel *m, int *ok_host);
+
+
 /* The bound of every exchange wait, in flag polls about 100 ns apart (host, per process,
  * read at each launch; default 2^24, about 1.7 s; 1 .. 2^30). A wait that runs out records
  * DEV_TIMEOUT and treats the silent peer's rows as empty. */

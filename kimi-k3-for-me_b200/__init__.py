@@ -229,6 +229,12 @@ _SIGS = {
     "k3gpu_ep_return": ([C.POINTER(K3GpuEpGroup), VP, C.c_uint, VP], I),
     "k3gpu_ep_combine": ([C.POINTER(K3GpuEpGroup), VP, VP, I, C.c_uint, VP, VP], I),
     "k3gpu_ep_set_wait_limit": ([C.c_longlong], I),
+    "k3gpu_moe_layer_ep_workspace": ([C.POINTER(K3GpuEpGroup), I, I, I, I], SZ),
+    "k3gpu_moe_layer_ep": ([VP, VP, VP, VP, VP, VP, C.POINTER(K3GpuExpertBank), C.POINTER(K3GpuExpertBank),
+                            C.POINTER(K3GpuEpGroup), C.c_uint, I, I, I, I, I, F, F, I, F, VP, VP, SZ, VP], I),
+    "k3gpu_model_ep_workspace": ([VP, C.POINTER(K3GpuEpGroup)], SZ),
+    "k3gpu_model_set_ep": ([VP, C.POINTER(K3GpuEpGroup), VP, VP, SZ], I),
+    "k3gpu_model_ep_status": ([VP, VP], I),
     "k3_spec_draft_ngram": ([VP, I, I, I, I, VP], I),
     "k3_spec_draft_eager": ([VP, I, I, VP], I),
     "k3_bank_read_safetensors": ([C.POINTER(C.c_char_p), I, I, I, I, I, I, VP, SZ], I),
@@ -1238,6 +1244,29 @@ class Model:
             n *= v
         nb = n * torch.tensor([], dtype=dtype).element_size()
         return self.arena[off:off + nb].view(dtype).view(*shape)
+
+    def set_ep(self, exchange, shared_banks):
+        """Make every layer's MoE step expert parallel over `exchange` (ep.EpExchange): each
+        layer's bank must hold this rank's routed experts, shared_banks[L] the replicated
+        shared experts of layer L. Every rank must then make the same sweeps."""
+        g = exchange.desc
+        need = lib.k3gpu_model_ep_workspace(self._m, C.byref(g))
+        if need == 0:
+            raise K3Error("k3gpu_model_ep_workspace: the exchange does not fit this model")
+        self.ep_ws = torch.empty(need + 256, dtype=torch.uint8, device=self.device)
+        base = (self.ep_ws.data_ptr() + 255) & ~255
+        self._ep_shared = (C.POINTER(K3GpuExpertBank) * len(shared_banks))(
+            *[C.pointer(b.desc) for b in shared_banks])
+        self._ep_keep = (exchange, shared_banks)
+        check(lib.k3gpu_model_set_ep(self._m, C.byref(g), C.cast(self._ep_shared, VP), VP(base), need),
+              "k3gpu_model_set_ep")
+
+    def ep_owners_ok(self):
+        """The last exchange's per-owner flags (1 = that owner's rows arrived)."""
+        world = self._ep_keep[0].world
+        ok = (C.c_int * world)()
+        check(lib.k3gpu_model_ep_status(self._m, ok), "k3gpu_model_ep_status")
+        return list(ok)
 
     def spec_loop(self, ids, **kw):
         """The engine's decode loop (SpecLoop) with this model's native callbacks (B == 1):

@@ -382,3 +382,107 @@ extern "C" int k3gpu_ep_set_wait_limit(long long polls)
     k3::ep::g_spin = polls;
     return K3GPU_OK;
 }
+
+// ---- the expert-parallel MoE layer: route, exchange, local and shared experts, combine ----
+namespace k3 {
+namespace ep {
+
+// sidx[t][j] = j, swt[t][j] = 1 for the shared experts of every token
+__global__ void shared_slots_kernel(int *__restrict__ sidx, float *__restrict__ swt, int n, int n_shared)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        sidx[i] = i % n_shared;
+        swt[i] = 1.0f;
+    }
+}
+
+struct MoeEpWs {
+    char *router, *local, *shared;
+    int *pos, *sidx;
+    float *part, *swt;
+    size_t router_bytes, local_bytes, shared_bytes, total;
+};
+
+static MoeEpWs moe_ep_layout(const K3GpuEpGroup *g, int T, int n_shared, int I, int n_routed, char *base)
+{
+    MoeEpWs w{};
+    size_t o = 0;
+    auto take = [&](size_t b) {
+        char *r = base ? base + o : nullptr;
+        o += a256(b);
+        return r;
+    };
+    const int R = g->world * g->cap;
+    w.router_bytes = k3gpu_router_workspace(T, n_routed);
+    w.router = take(w.router_bytes);
+    w.local_bytes = k3gpu_moe_workspace(R, g->K, 0, g->L, I, g->n_local);
+    w.local = take(w.local_bytes);
+    w.shared_bytes = n_shared > 0 ? k3gpu_moe_workspace(T, n_shared, 0, g->L, I, n_shared) : 0;
+    w.shared = take(w.shared_bytes);
+    w.pos = (int *)take((size_t)g->world * T * 4);
+    w.part = (float *)take((size_t)R * g->L * 4);
+    w.sidx = (int *)take((size_t)T * (n_shared > 0 ? n_shared : 1) * 4);
+    w.swt = (float *)take((size_t)T * (n_shared > 0 ? n_shared : 1) * 4);
+    w.total = o;
+    return w;
+}
+
+}  // namespace ep
+}  // namespace k3
+
+extern "C" size_t k3gpu_moe_layer_ep_workspace(const K3GpuEpGroup *g, int T, int n_shared, int I, int n_routed)
+{
+    if (!k3::ep::group_ok(g) || T <= 0 || T > g->cap || n_shared < 0 || I <= 0 || n_routed <= 0) return 0;
+    return k3::ep::moe_ep_layout(g, T, n_shared, I, n_routed, nullptr).total;
+}
+
+extern "C" int k3gpu_moe_layer_ep(float *out, int *idx, float *wt, const float *x, const float *gate_W,
+                                  const float *bias, const K3GpuExpertBank *local, const K3GpuExpertBank *shared,
+                                  const K3GpuEpGroup *g, unsigned seq, int T, int topk, int n_routed, int n_shared,
+                                  int act, float b1, float b2, int renorm, float routed_scale, int *ok,
+                                  void *workspace, size_t ws_bytes, void *stream)
+{
+    using namespace k3::ep;
+    if (!out || !idx || !wt || !x || !gate_W || !local || !ok || !workspace || !group_ok(g) || seq == 0)
+        return K3GPU_EINVAL;
+    if (T <= 0 || T > g->cap || topk != g->K || n_routed != g->world * g->n_local || local->n_experts != g->n_local ||
+        local->L != g->L || n_shared < 0 || (n_shared > 0 && (!shared || shared->n_experts != n_shared ||
+                                                              shared->L != g->L || shared->I != local->I)))
+        return K3GPU_EINVAL;
+    const size_t need = k3gpu_moe_layer_ep_workspace(g, T, n_shared, local->I, n_routed);
+    if (!need) return K3GPU_EINVAL;
+    if (ws_bytes < need) return K3GPU_ECAPACITY;
+    const MoeEpWs w = moe_ep_layout(g, T, n_shared, local->I, n_routed, static_cast<char *>(workspace));
+    cudaStream_t s = k3::as_stream(stream);
+    int st;
+    // 1. the replicated gate on this rank's tokens (global expert ids)
+    if ((st = k3gpu_router(idx, wt, x, gate_W, bias, T, g->L, n_routed, topk, renorm, routed_scale, w.router,
+                           w.router_bytes, stream)))
+        return st;
+    // 2. every token row once to each owner of one of its experts
+    if ((st = k3gpu_ep_dispatch(g, x, idx, wt, T, seq, w.pos, stream))) return st;
+    // 3. the shared experts on this rank's own tokens while the rows travel (out = shared)
+    if (n_shared > 0) {
+        shared_slots_kernel<<<k3::ceil_div((long long)T * n_shared, 256), 256, 0, s>>>(w.sidx, w.swt, T * n_shared,
+                                                                                       n_shared);
+        if ((st = k3::launch_status())) return st;
+        if ((st = k3gpu_moe_experts(out, x, w.sidx, w.swt, shared, T, n_shared, n_shared, 0, act, b1, b2, nullptr,
+                                    0.0f, w.shared, w.shared_bytes, stream)))
+            return st;
+    } else if ((st = k3::cuda_status(cudaMemsetAsync(out, 0, (size_t)T * g->L * 4, s)))) {
+        return st;
+    }
+    // 4. this rank's experts over the fixed receive region (dropped slots skipped)
+    if ((st = k3gpu_ep_receive(g, seq, stream))) return st;
+    float *xr;
+    int *ir;
+    float *wr;
+    if ((st = k3gpu_ep_recv_views(g, &xr, &ir, &wr))) return st;
+    if ((st = k3gpu_moe_experts(w.part, xr, ir, wr, local, g->world * g->cap, topk, g->n_local, 0, act, b1, b2,
+                                nullptr, 0.0f, w.local, w.local_bytes, stream)))
+        return st;
+    // 5. the partial rows home, added per token in owner order
+    if ((st = k3gpu_ep_return(g, w.part, seq, stream))) return st;
+    return k3gpu_ep_combine(g, out, w.pos, T, seq, ok, stream);
+}

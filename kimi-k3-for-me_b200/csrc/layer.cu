@@ -458,6 +458,8 @@ static size_t layer_ws_layout(const K3GpuLayerCfg *c, int B, int T, size_t attn_
 }
 }  // namespace k3
 
+#include "layer.cuh"
+
 namespace k3 {
 static bool layer_common_ok(const K3GpuLayerCfg *c)
 {
@@ -469,7 +471,7 @@ static bool layer_common_ok(const K3GpuLayerCfg *c)
 template <class LW, class Attn>
 static int decoder_layer(float *h, float *block_residual, int *n_blocks, int *moe_idx, float *moe_wt, const LW *w,
                          const K3GpuLayerCfg *c, int layer_idx, int B, int T, const LayerWs &ws, Attn attn,
-                         cudaStream_t s, void *stream)
+                         cudaStream_t s, void *stream, const LayerEp *ep)
 {
     const int E = c->hidden, R = B * T, maxb = c->max_blocks;
     const long long n = (long long)R * E;
@@ -500,7 +502,11 @@ static int decoder_layer(float *h, float *block_residual, int *n_blocks, int *mo
     if ((st = k3gpu_rmsnorm(ws.hin, h, w->post_norm, R, E, c->rms_eps, stream))) return st;
     // the MoE: the K3 form (latent projections, dense shared expert) or the single-layer
     // form (router and experts at the hidden width)
-    if (w->moe) {
+    if (ep) {        // the routed experts split over the ranks of ep->g, rows through peer memory
+        st = k3gpu_moe_layer_ep(ws.tmp, moe_idx, moe_wt, ws.hin, w->gate_W, w->gate_bias, w->bank, ep->shared, ep->g,
+                                ep->seq, R, c->topk, c->n_routed, c->n_shared, c->act, c->situ_b1, c->situ_b2,
+                                c->renorm, c->routed_scale, ep->ok, ep->ws, ep->ws_bytes, stream);
+    } else if (w->moe) {
         const K3GpuMoeCfg mc = moe_cfg_of(c);
         st = k3gpu_moe_prefill(ws.tmp, moe_idx, moe_wt, ws.hin, w->moe, &mc, R, ws.moe, ws.moe_bytes, stream);
     } else {
@@ -544,6 +550,15 @@ extern "C" int k3gpu_decoder_layer_kda_verify_tree(float *h, float *block_residu
                                                    const int *parent, int B, int T, void *workspace,
                                                    size_t ws_bytes, void *stream)
 {
+    return k3::decoder_layer_kda(h, block_residual, n_blocks, moe_idx, moe_wt, w, c, layer_idx, state, conv_hist, log,
+                                 parent, B, T, workspace, ws_bytes, stream, nullptr);
+}
+
+int k3::decoder_layer_kda(float *h, float *block_residual, int *n_blocks, int *moe_idx, float *moe_wt,
+                          const K3GpuKdaLayerW *w, const K3GpuLayerCfg *c, int layer_idx, const float *state,
+                          const float *conv_hist, const K3GpuKdaLog *log, const int *parent, int B, int T,
+                          void *workspace, size_t ws_bytes, void *stream, const LayerEp *ep)
+{
     using namespace k3;
     if (!h || !block_residual || !n_blocks || !moe_idx || !moe_wt || !w || !cfg_ok(c) || !layer_common_ok(c) ||
         !workspace)
@@ -557,7 +572,7 @@ extern "C" int k3gpu_decoder_layer_kda_verify_tree(float *h, float *block_residu
                                            stream);
     };
     return decoder_layer(h, block_residual, n_blocks, moe_idx, moe_wt, w, c, layer_idx, B, T, ws, attn,
-                         as_stream(stream), stream);
+                         as_stream(stream), stream, ep);
 }
 
 extern "C" size_t k3gpu_decoder_layer_mla_workspace(const K3GpuLayerCfg *c, int B, int T, int max_ctx)
@@ -572,6 +587,15 @@ extern "C" int k3gpu_decoder_layer_mla_verify(float *h, float *block_residual, i
                                               uint16_t *rope, int cap, const int *cached,
                                               const uint64_t *mask, int max_ctx, int B, int T,
                                               void *workspace, size_t ws_bytes, void *stream)
+{
+    return k3::decoder_layer_mla(h, block_residual, n_blocks, moe_idx, moe_wt, w, c, layer_idx, lat, rope, cap, cached,
+                                 mask, max_ctx, B, T, workspace, ws_bytes, stream, nullptr);
+}
+
+int k3::decoder_layer_mla(float *h, float *block_residual, int *n_blocks, int *moe_idx, float *moe_wt,
+                          const K3GpuMlaLayerW *w, const K3GpuLayerCfg *c, int layer_idx, uint16_t *lat,
+                          uint16_t *rope, int cap, const int *cached, const uint64_t *mask, int max_ctx, int B,
+                          int T, void *workspace, size_t ws_bytes, void *stream, const LayerEp *ep)
 {
     using namespace k3;
     if (!h || !block_residual || !n_blocks || !moe_idx || !moe_wt || !w || !mla_cfg_ok(c) ||
@@ -588,5 +612,5 @@ extern "C" int k3gpu_decoder_layer_mla_verify(float *h, float *block_residual, i
                                       stream);
     };
     return decoder_layer(h, block_residual, n_blocks, moe_idx, moe_wt, w, c, layer_idx, B, T, ws, attn,
-                         as_stream(stream), stream);
+                         as_stream(stream), stream, ep);
 }

@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "layer.cuh"
 
 namespace k3 {
 
@@ -154,6 +155,15 @@ struct K3GpuModel {
     int stage_next = 0;
     std::vector<int> cached_host;
     int last_T, last_tree, pre_committed;   // the sweep awaiting its commit
+    // expert parallel (k3gpu_model_set_ep): every layer's MoE step exchanges rows with the
+    // other ranks; seq numbers the exchange steps, the same on every rank
+    bool ep_on = false;
+    K3GpuEpGroup ep_group{};
+    std::vector<const K3GpuExpertBank *> ep_shared;
+    int *ep_ok = nullptr;
+    char *ep_ws = nullptr;
+    size_t ep_ws_bytes = 0;
+    unsigned ep_seq = 0;
     std::vector<int> parent_host;
     std::vector<uint64_t> mask_host;
     ~K3GpuModel()
@@ -352,14 +362,23 @@ static int model_sweep(K3GpuModel *m, const int *ids_dev, int T, const int *pare
     if ((st = cuda_status(cudaMemsetAsync(m->nb, 0, (size_t)R * 4, s)))) return st;
     for (int i = 0; i < m->cfg.n_layers; i++) {
         const int sl = m->slot[i];
+        LayerEp ep;
+        if (m->ep_on) {
+            ep.g = &m->ep_group;
+            ep.shared = m->ep_shared[i];
+            ep.seq = ++m->ep_seq;
+            ep.ok = m->ep_ok;
+            ep.ws = m->ep_ws;
+            ep.ws_bytes = m->ep_ws_bytes;
+        }
+        const LayerEp *epp = m->ep_on ? &ep : nullptr;
         if (m->is_mla[i]) {
-            st = k3gpu_decoder_layer_mla_verify(m->h, m->br, m->nb, m->moe_idx, m->moe_wt, &m->mla[i], &l, i,
-                                                m->lat[sl], m->rope[sl], m->cap, m->cached, m->mask, max_ctx, B, T,
-                                                m->ws, m->ws_bytes, sp);
+            st = decoder_layer_mla(m->h, m->br, m->nb, m->moe_idx, m->moe_wt, &m->mla[i], &l, i, m->lat[sl],
+                                   m->rope[sl], m->cap, m->cached, m->mask, max_ctx, B, T, m->ws, m->ws_bytes, sp, epp);
         } else {
-            st = k3gpu_decoder_layer_kda_verify_tree(m->h, m->br, m->nb, m->moe_idx, m->moe_wt, &m->kda[i], &l, i,
-                                                     m->kstate[sl], m->khist[sl], &m->klog[sl],
-                                                     tree ? m->parent_dev : nullptr, B, T, m->ws, m->ws_bytes, sp);
+            st = decoder_layer_kda(m->h, m->br, m->nb, m->moe_idx, m->moe_wt, &m->kda[i], &l, i, m->kstate[sl],
+                                   m->khist[sl], &m->klog[sl], tree ? m->parent_dev : nullptr, B, T, m->ws,
+                                   m->ws_bytes, sp, epp);
         }
         if (st) return st;
     }
@@ -705,4 +724,51 @@ extern "C" int k3gpu_model_loop_commit(void *ctx, int base, const int *path, int
     if (kq < 0 || kq > m->last_T || base + m->pre_committed != m->cached_host[0]) return K3GPU_EINVAL;
     m->pre_committed = 0;
     return k3::model_commit_host(m, &kq, path);
+}
+
+// ---- expert parallel ----
+extern "C" size_t k3gpu_model_ep_workspace(const K3GpuModel *m, const K3GpuEpGroup *g)
+{
+    if (!m || !g) return 0;
+    const K3GpuLayerCfg &l = m->cfg.layer;
+    const size_t moe = k3gpu_moe_layer_ep_workspace(g, m->B * m->maxT, l.n_shared, l.moe_inter, l.n_routed);
+    if (!moe) return 0;
+    return ((moe + 255) & ~(size_t)255) + 256;   // + the per-owner flags
+}
+
+extern "C" int k3gpu_model_set_ep(K3GpuModel *m, const K3GpuEpGroup *g, const K3GpuExpertBank *const *shared,
+                                  void *workspace, size_t ws_bytes)
+{
+    using namespace k3;
+    if (!m || !g || !workspace || (m->cfg.layer.n_shared > 0 && !shared)) return K3GPU_EINVAL;
+    const K3GpuLayerCfg &l = m->cfg.layer;
+    if (g->world < 1 || g->world > K3GPU_EP_MAX_WORLD || g->cap < m->B * m->maxT || g->L != l.hidden ||
+        g->K != l.topk || g->n_local * g->world != l.n_routed)
+        return K3GPU_EINVAL;
+    for (int i = 0; i < m->cfg.n_layers; i++) {
+        const K3GpuExpertBank *b = m->is_mla[i] ? m->mla[i].bank : m->kda[i].bank;
+        const bool latent = m->is_mla[i] ? m->mla[i].moe != nullptr : m->kda[i].moe != nullptr;
+        if (latent || !b || b->n_experts != g->n_local) return K3GPU_EINVAL;   // the single-layer MoE form only
+        if (l.n_shared > 0 && (!shared[i] || shared[i]->n_experts != l.n_shared)) return K3GPU_EINVAL;
+    }
+    const size_t need = k3gpu_model_ep_workspace(m, g);
+    if (!need) return K3GPU_EINVAL;
+    if (ws_bytes < need || !aligned(workspace, 256)) return ws_bytes < need ? K3GPU_ECAPACITY : K3GPU_EINVAL;
+    m->ep_group = *g;
+    m->ep_shared.assign(m->cfg.n_layers, nullptr);
+    if (l.n_shared > 0) m->ep_shared.assign(shared, shared + m->cfg.n_layers);
+    m->ep_ok = static_cast<int *>(workspace);
+    m->ep_ws = static_cast<char *>(workspace) + 256;
+    m->ep_ws_bytes = need - 256;
+    m->ep_on = true;
+    return K3GPU_OK;
+}
+
+extern "C" int k3gpu_model_ep_status(const K3GpuModel *m, int *ok_host)
+{
+    if (!m || !ok_host || !m->ep_on) return K3GPU_EINVAL;
+    const int st = k3::cuda_status(cudaMemcpyAsync(ok_host, m->ep_ok, (size_t)m->ep_group.world * 4,
+                                                   cudaMemcpyDeviceToHost, k3::as_stream(m->stream)));
+    if (st) return st;
+    return k3::cuda_status(cudaStreamSynchronize(k3::as_stream(m->stream)));
 }

@@ -140,6 +140,60 @@ class EPMoELayer:
     __call__ = forward
 
 
+class EpExchange:
+    """The peer-memory exchange of one rank: its arena (k3gpu_ep_arena_alloc), every other
+    rank's arena mapped by CUDA IPC (the process group carries the handles once), and the
+    K3GpuEpGroup the k3gpu_ep_* and k3gpu_moe_layer_ep calls take. cap: the most token rows
+    a rank sends in one exchange step."""
+
+    def __init__(self, k3, cap, L, K, n_local, group=None):
+        import ctypes as C
+        self.k3, self.C = k3, C
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        if self.world > k3.EP_MAX_WORLD:
+            raise ValueError(f"at most {k3.EP_MAX_WORLD} ranks")
+        lib = k3.lib
+        nbytes = lib.k3gpu_ep_arena_bytes(self.world, cap, L, K)
+        arena = C.c_void_p()
+        k3.check(lib.k3gpu_ep_arena_alloc(C.byref(arena), nbytes), "k3gpu_ep_arena_alloc")
+        self.arena = arena
+        h = (C.c_uint8 * k3.EP_HANDLE_BYTES)()
+        k3.check(lib.k3gpu_ep_ipc_handle(arena, h), "k3gpu_ep_ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        g = k3.K3GpuEpGroup()
+        g.world, g.rank, g.cap, g.L, g.K, g.n_local = self.world, self.rank, cap, L, K, n_local
+        self.peers = []
+        for r in range(self.world):
+            if r == self.rank:
+                g.arena[r] = arena.value
+                continue
+            hb = (C.c_uint8 * k3.EP_HANDLE_BYTES).from_buffer_copy(handles[r])
+            peer = C.c_void_p()
+            k3.check(lib.k3gpu_ep_ipc_open(hb, C.byref(peer)), "k3gpu_ep_ipc_open")
+            g.arena[r] = peer.value
+            self.peers.append(peer)
+        self.desc = g
+        # every rank's arena exists and is mapped before the first dispatch writes into it
+        dist.barrier(group=group)
+
+    def close(self):
+        """Unmap the peers' arenas and free this rank's, after a barrier (no rank still
+        writes into it)."""
+        import torch
+        lib = self.k3.lib
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.peers:
+            lib.k3gpu_ep_ipc_close(p)
+        self.peers = []
+        if self.arena is not None:
+            lib.k3gpu_ep_arena_free(self.arena)
+            self.arena = None
+
+
 class P2PMoELayer:
     """The routed experts sharded across `group`, token rows exchanged through peer memory
     by the library's k3gpu_ep_* kernels (no collective on the data path).
