@@ -9,10 +9,12 @@
 // that accumulator over the K range of a unit, so results agree with the reference's
 // double sums to about 1e-5 relative (the sweep's logits tolerance is 1e-3 rel-L2).
 //
-// A verify sweep has T <= 256 positions: every output row block is a weight stream. One
-// persistent CTA per SM walks units (128 output rows, one K split), 7 warps:
+// A chain sweep has T <= 128 positions: every output row block is a weight stream; a tree
+// sweep over a batch (T ~ 1024) is a real GEMM. One persistent CTA per SM walks units (128
+// output rows x one tile of at most 128 positions x one K split; one tile when T <= 128,
+// else T split into equal tiles), 7 warps:
 //   warp 0     TMA: a 64-K stage = one 128-byte-swizzled box of 128 weight rows (16 KB)
-//              and one box per activation piece (Np rows, Np = T rounded up to 16)
+//              and one box per activation piece (Np rows, Np = the tile rounded up to 16)
 //   warps 1-2  MMA issuers: issuer i owns K16 steps 2i, 2i+1 of every stage and its own
 //              fp32 accumulator in TMEM (two issuers: one thread issues an MMA about every
 //              55-75 clocks); tcgen05.mma kind::f16 with bf16 A and B from shared memory
@@ -34,7 +36,8 @@ constexpr int THREADS = 7 * 32;
 constexpr int KB = 64;                    // K per stage: one 128-byte swizzled box row
 constexpr int W_BYTES = 128 * 128;        // 128 weight rows x 128 bytes
 constexpr int MAX_NS = 8;
-constexpr int MAX_NP = 256;               // positions per pass (MMA N <= 256)
+constexpr int TILE_T = 128;               // positions per tile when T is larger
+constexpr int PASS_T = 2048;              // positions per launch (bounds the workspace)
 constexpr int MAX_SPLIT = 8;
 constexpr long long SPIN = 1LL << 22;
 constexpr int SUSPEND_NS = 1000;
@@ -116,6 +119,7 @@ struct Args {
     const int *lo_flag;  // 1 when some activation needs its lo piece
     int T, Np, in, out, ldy;
     int nsplit, kst;     // K splits; 64-K stages per split
+    int ttiles, Tpad;    // position tiles of Np rows; rows of each activation piece
     int n_units, NS, stage_bytes;
     int dbuf;            // Np <= 128: two accumulator sets, so a unit's epilogue overlaps the next unit
 };
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
             asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
             int item = 0;
             for (int u = blockIdx.x; u < a.n_units && !failed; u += gridDim.x) {
-                const int rb = u / a.nsplit, ks = u % a.nsplit;
+                const int rb = u / (a.nsplit * a.ttiles), tt = (u / a.nsplit) % a.ttiles, ks = u % a.nsplit;
                 const int kb1 = min(nkb, (ks + 1) * a.kst);
                 for (int kb = ks * a.kst; kb < kb1; kb++, item++) {
                     const int st = item % a.NS;
@@ -172,7 +176,8 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
                     const uint32_t full = s_addr(&b_full[st]);
                     bar_expect(full, (uint32_t)(W_BYTES + P * a.Np * 128));
                     tma2d(s_addr(sw), &wmap, kb * KB, rb * 128, full);
-                    for (int p = 0; p < P; p++) tma2d(s_addr(sw + W_BYTES + p * a.Np * 128), &xmap, kb * KB, p * a.Np, full);
+                    for (int p = 0; p < P; p++)
+                        tma2d(s_addr(sw + W_BYTES + p * a.Np * 128), &xmap, kb * KB, p * a.Tpad + tt * a.Np, full);
                 }
             }
             if (failed) flag(DEV_TIMEOUT);
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         int unit_i = 0;
         for (int u = blockIdx.x; u < a.n_units && !failed; u += gridDim.x, unit_i++) {
-            const int rb = u / a.nsplit, ks = u % a.nsplit;
+            const int rb = u / (a.nsplit * a.ttiles), tt = (u / a.nsplit) % a.ttiles, ks = u % a.nsplit;
             const int row = rb * 128 + r;
             const int db = a.dbuf ? (unit_i & 1) : 0, use = a.dbuf ? (unit_i >> 1) : unit_i;
             if (!bar_wait(s_addr(&b_dfull[db]), (uint32_t)(use & 1))) { failed = true; break; }
@@ -234,7 +239,7 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
                 if (row < a.out) {
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
-                        const int t = c0 + j;
+                        const int t = tt * a.Np + c0 + j;
                         if (t < a.T) {
                             const float y = __fadd_rn(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
                             if (a.part) a.part[((size_t)ks * a.T + t) * a.out + row] = y;
@@ -257,10 +262,10 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
     }
 }
 
-// hi/lo bf16 pieces of X, [2][Np][in_pad], zero past T and past in; lo_flag = 1 when any
+// hi/lo bf16 pieces of X, [2][Tpad][in_pad], zero past T and past in; lo_flag = 1 when any
 // lo != 0 (one plain store per block that saw one: every writer writes the same value)
 __global__ void __launch_bounds__(256) split_kernel(__nv_bfloat16 *__restrict__ xp, int *__restrict__ lo_flag,
-                                                   const float *__restrict__ X, int ldx, int T, int Np,
+                                                   const float *__restrict__ X, int ldx, int T, int Tpad,
                                                    int in, int in_pad)
 {
     const int t = blockIdx.y;
@@ -271,7 +276,7 @@ __global__ void __launch_bounds__(256) split_kernel(__nv_bfloat16 *__restrict__ 
         const __nv_bfloat16 hi = __float2bfloat16_rn(x);
         const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
         xp[(size_t)t * in_pad + k] = hi;
-        xp[((size_t)Np + t) * in_pad + k] = lo;
+        xp[((size_t)Tpad + t) * in_pad + k] = lo;
         nz = __bfloat16_as_ushort(lo) & 0x7FFF;
     }
     if (__syncthreads_or(nz) && threadIdx.x == 0) *lo_flag = 1;
@@ -342,36 +347,41 @@ static int bf16_map(CUtensorMap *m, const void *base, long long cols, long long 
 }
 
 struct Plan {
-    int Np, in_pad, nkb, nsplit, kst, rowblocks, n_units;
+    int Np, ttiles, Tpad, in_pad, nkb, nsplit, kst, rowblocks, n_units;
     size_t xp_bytes, part_bytes;
 };
 
-static Plan plan(int Tc, int in, int out, int sms)
+// One launch over Tc <= PASS_T positions; at most max_split K splits.
+static Plan plan(int Tc, int in, int out, int sms, int max_split)
 {
     Plan p;
-    p.Np = (Tc + 15) / 16 * 16;
+    p.ttiles = Tc <= TILE_T ? 1 : (Tc + TILE_T - 1) / TILE_T;
+    p.Np = ((Tc + p.ttiles - 1) / p.ttiles + 15) / 16 * 16;
+    p.Tpad = p.ttiles * p.Np;
     p.in_pad = (in + KB - 1) / KB * KB;
     p.nkb = p.in_pad / KB;
     p.rowblocks = (out + 127) / 128;
     // K splits: minimise the busiest CTA's stages (units are handed out round-robin), with
     // a cost per unit (accumulator drain) and, when split, the partial-sum pass
-    const int max_ns = std::max(1, std::min(MAX_SPLIT, p.nkb / 4));
+    const int max_ns = std::max(1, std::min(max_split, p.nkb / 4));
     double best = 1e300;
     p.kst = p.nkb;
     for (int ns = 1; ns <= max_ns; ns++) {
         const int kst = (p.nkb + ns - 1) / ns;
         const int nsr = (p.nkb + kst - 1) / kst;
-        const long long per_cta = ((long long)p.rowblocks * nsr + sms - 1) / sms;
+        const long long per_cta = ((long long)p.rowblocks * p.ttiles * nsr + sms - 1) / sms;
         double cost = (double)per_cta * (kst + 2.0);
         if (nsr > 1) cost += 3.0 + (double)nsr * Tc * out * 4.0 / 2.5e6;   // stage ~ 0.45 us
         if (cost < best - 1e-9) { best = cost; p.kst = kst; }
     }
     p.nsplit = (p.nkb + p.kst - 1) / p.kst;                    // every split non-empty
-    p.n_units = p.rowblocks * p.nsplit;
-    p.xp_bytes = (size_t)2 * MAX_NP * p.in_pad * 2;
-    p.part_bytes = (size_t)MAX_SPLIT * MAX_NP * out * 4;
+    p.n_units = p.rowblocks * p.ttiles * p.nsplit;
+    p.xp_bytes = (size_t)2 * p.Tpad * p.in_pad * 2;
+    p.part_bytes = p.nsplit > 1 ? (size_t)p.nsplit * Tc * out * 4 : 0;
     return p;
 }
+
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 static int g_attr_dev = -1;
 static std::mutex g_attr_mu;
@@ -381,9 +391,17 @@ static std::mutex g_attr_mu;
 
 extern "C" size_t k3gpu_matmul_bf16_workspace(int T, int in, int out)
 {
+    using namespace k3::mmw;
     if (T <= 0 || in <= 0 || out <= 0) return 0;
-    const k3::mmw::Plan p = k3::mmw::plan(std::min(T, k3::mmw::MAX_NP), in, out, 148);
-    return ((p.xp_bytes + 255) & ~(size_t)255) + ((p.part_bytes + 255) & ~(size_t)255) + 256;
+    // the largest pass and, when T is not a multiple of it, the last one
+    size_t xp = 0, part = 0;
+    for (int Tc : {std::min(T, PASS_T), T % PASS_T}) {
+        if (Tc <= 0) continue;
+        const Plan p = plan(Tc, in, out, 148, MAX_SPLIT);
+        xp = std::max(xp, p.xp_bytes);
+        part = std::max(part, p.part_bytes);
+    }
+    return align256(xp) + align256(part) + 256;
 }
 
 extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ldx, const uint16_t *W, int in,
@@ -407,29 +425,34 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
             g_attr_dev = dev;
         }
     }
-    const Plan full = plan(std::min(T, MAX_NP), in, out, sms);
     char *ws = static_cast<char *>(workspace);
-    __nv_bfloat16 *xp = reinterpret_cast<__nv_bfloat16 *>(ws);
-    float *part = reinterpret_cast<float *>(ws + ((full.xp_bytes + 255) & ~(size_t)255));
-    int *lo_flag = reinterpret_cast<int *>(ws + ((full.xp_bytes + 255) & ~(size_t)255) +
-                                           ((full.part_bytes + 255) & ~(size_t)255));
     CUtensorMap wm;
     if ((st = bf16_map(&wm, W, in, out, 128))) return st;
-    for (int t0 = 0; t0 < T; t0 += MAX_NP) {           // passes of up to 256 positions
-        const int Tc = std::min(MAX_NP, T - t0);
-        const Plan p = plan(Tc, in, out, sms);
+    for (int t0 = 0; t0 < T; t0 += PASS_T) {           // launches of up to PASS_T positions
+        const int Tc = std::min(PASS_T, T - t0);
+        // the K splits this workspace holds partials for (the SM count may differ from the
+        // one the workspace query assumed)
+        const size_t xp_b = align256(plan(Tc, in, out, sms, 1).xp_bytes);
+        const size_t room = ws_bytes - 256 - xp_b;
+        const int max_split = (int)std::max<size_t>(1, std::min<size_t>(MAX_SPLIT, room / ((size_t)Tc * out * 4)));
+        const Plan p = plan(Tc, in, out, sms, max_split);
+        __nv_bfloat16 *xp = reinterpret_cast<__nv_bfloat16 *>(ws);
+        float *part = reinterpret_cast<float *>(ws + xp_b);
+        // the flag sits in the last 256 bytes, past any partials this launch writes
+        int *lo_flag = reinterpret_cast<int *>((reinterpret_cast<uintptr_t>(ws + ws_bytes - 256) + 15) & ~(uintptr_t)15);
         if ((st = k3::cuda_status(cudaMemsetAsync(lo_flag, 0, sizeof(int), s)))) return st;
-        split_kernel<<<dim3((p.in_pad + 255) / 256, p.Np), 256, 0, s>>>(xp, lo_flag, X + (size_t)t0 * ldx, ldx, Tc,
-                                                                         p.Np, in, p.in_pad);
+        split_kernel<<<dim3((p.in_pad + 255) / 256, p.Tpad), 256, 0, s>>>(xp, lo_flag, X + (size_t)t0 * ldx, ldx, Tc,
+                                                                          p.Tpad, in, p.in_pad);
         if ((st = k3::launch_status())) return st;
         CUtensorMap xm;
-        if ((st = bf16_map(&xm, xp, p.in_pad, 2LL * p.Np, p.Np))) return st;
+        if ((st = bf16_map(&xm, xp, p.in_pad, 2LL * p.Tpad, p.Np))) return st;
         Args a;
         a.Y = p.nsplit == 1 ? Y + (size_t)t0 * ldy : nullptr;
         a.part = p.nsplit == 1 ? nullptr : part;
         a.lo_flag = lo_flag;
         a.T = Tc; a.Np = p.Np; a.in = in; a.out = out; a.ldy = ldy;
         a.nsplit = p.nsplit; a.kst = p.kst; a.n_units = p.n_units;
+        a.ttiles = p.ttiles; a.Tpad = p.Tpad;
         a.dbuf = p.Np <= 128 ? 1 : 0;
         a.stage_bytes = W_BYTES + 2 * p.Np * 128;
         a.NS = std::min(MAX_NS, (200 * 1024) / a.stage_bytes);

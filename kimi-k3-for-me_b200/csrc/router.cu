@@ -1,17 +1,21 @@
 // router.cu -- the MoE router (k3_router, src/core/k3_ops.c:1624-1719 of the reference)
 // for a whole verify batch.
 //
-// Scores: every (token, expert) score is ONE double chain over i = 0..hidden-1, in order,
-// inside one thread -- the reference's chain (its 8-expert blocking changes issue order
-// only). A float times a float is exact in double, so fma(w, x, acc) == acc + w*x rounded
-// once, exactly the reference's `acc += (double)w * (double)x`. The chain length sets the
-// floor (hidden dependent FMAs), so the kernel's job is to keep every chain issuing: a CTA
-// owns 24 experts x 8 tokens (one chain per thread), K tiles of 128 columns arrive by
-// cp.async two tiles ahead, and each tile is widened to double once in shared memory.
-// Measured on B200 the loop runs at about 20 clocks a step against the 8-clock FMA
-// latency: each warp-step moves four shared-memory wavefronts (operands re-read by the
-// lanes that share an expert or token), and the float-to-double widening is slow. Register
-// blocking over tokens and a widened copy made once per call are the way down.
+// Scores: every (token, expert) score is ONE double chain over i = 0..hidden-1, in order
+// -- the reference's chain (its 8-expert blocking changes issue order only). A float times
+// a float is exact in double, so fma(w, x, acc) == acc + w*x rounded once, exactly the
+// reference's `acc += (double)w * (double)x`. Which chains a thread runs side by side is
+// free, so a thread owns a block of A tokens x B experts (up to 16 independent chains).
+//
+// What bounds the kernel on B200 is operand delivery, not the FP64 pipe (64 FMA/clock/SM):
+// shared memory hands each lane at most ~128 bytes per clock per SM, one double per two
+// FMAs at B = 2 if every lane read its own. So the A tokens of a thread are WARP-UNIFORM
+// (every lane of a warp reads the same x doubles: broadcast loads) and only the B experts
+// differ by lane; 4 warps of a CTA take 4 token groups against the same 32 B experts. K
+// tiles of 32 columns arrive by cp.async three tiles ahead, as floats in [row][36] rows
+// (conflict-free float4 reads), and are widened once per CTA into a [k][row] double tile;
+// one barrier per tile. The tile shape per call comes from a small cost model over the SM
+// count (FP64 issue per scheduler against shared-memory wavefronts per SM).
 //
 // Selection: one warp per token, repeated max with the first-index tie rule, taken
 // entries set to -inf, weights from the unbiased scores, renormalised by one double sum
@@ -27,15 +31,22 @@
 
 namespace k3 {
 
-constexpr int RT_E = 24;     // experts per CTA (384 experts x 72 tokens -> 144 CTAs)
-constexpr int RT_T = 8;      // tokens per CTA
-constexpr int RT_R = RT_E + RT_T;
-constexpr int RT_THREADS = RT_E * RT_T;   // one chain per thread
-constexpr int RT_K = 128;    // hidden columns per tile
-constexpr int RT_NS = 3;     // cp.async stages (float tiles in flight)
-constexpr int RT_LD = RT_K + 2;   // double tile row stride: rows land on distinct banks
-constexpr int RT_F_TILE = RT_R * RT_K;                      // floats per stage
-constexpr int RT_SMEM = RT_NS * RT_F_TILE * 4 + 2 * RT_R * RT_LD * 8;
+constexpr int RB_K = 32;          // hidden columns per tile
+constexpr int RB_FLD = RB_K + 4;  // float stage row stride (16-byte rows on distinct banks)
+constexpr int RB_NS = 4;          // cp.async stages: tiles kt+1..kt+3 in flight
+constexpr int RB_THREADS = 128;   // 4 warps, one token group each
+
+// CTA tile of the scores kernel: A tokens per warp (A even), B experts per lane.
+template <int A, int B>
+struct RbTile {
+    static constexpr int TT = 4 * A;                        // tokens per CTA
+    static constexpr int TE = 32 * B;                       // experts per CTA
+    static constexpr int ROWS = TT + TE;                    // rows of a tile
+    static constexpr int PIECES = ROWS * RB_K / 4;          // float4 pieces per tile
+    static constexpr int FSTAGE = ROWS * RB_FLD;            // floats per stage
+    static constexpr int SMEM = RB_NS * FSTAGE * 4 + 2 * RB_K * ROWS * 8;
+    static_assert(A % 2 == 0 && (B == 1 || B == 2), "tile shape");
+};
 
 // one cp.async of V floats (V = 4: 16 bytes; V = 1: 4 bytes), zero-filled when !valid
 template <int V>
@@ -49,95 +60,110 @@ __device__ __forceinline__ void cp_async_f(float *dst, const float *src, bool va
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
 }
 
-// eight chain steps from registers: acc += w[i] * x[i], i = 0..7 in order
-__device__ __forceinline__ double chain8(double acc, const double2 (&w)[4], const double2 (&x)[4])
-{
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        asm volatile("fma.rn.f64 %0, %1, %2, %0;" : "+d"(acc) : "d"(w[i].x), "d"(x[i].x));
-        asm volatile("fma.rn.f64 %0, %1, %2, %0;" : "+d"(acc) : "d"(w[i].y), "d"(x[i].y));
-    }
-    return acc;
-}
-
-__device__ __forceinline__ void load8(double2 (&w)[4], double2 (&x)[4], const double *wr, const double *xr)
-{
-    const uint32_t ws = (uint32_t)__cvta_generic_to_shared(wr), xs = (uint32_t)__cvta_generic_to_shared(xr);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(w[i].x), "=d"(w[i].y) : "r"(ws + 16 * i));
-        asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(x[i].x), "=d"(x[i].y) : "r"(xs + 16 * i));
-    }
-}
-
-template <int V>   // V = 4 when hidden % 4 == 0 and x, W are 16-byte aligned, else 1
-__global__ void __launch_bounds__(RT_THREADS) router_scores_kernel(float *__restrict__ score,
+template <int A, int B, int V>   // V = 4 when hidden % 4 == 0 and x, W are 16-byte aligned, else 1
+__global__ void __launch_bounds__(RB_THREADS) router_scores_kernel(float *__restrict__ score,
                                                                    const float *__restrict__ x,
                                                                    const float *__restrict__ W,
                                                                    int T, int hidden, int n)
 {
+    using Tl = RbTile<A, B>;
     extern __shared__ __align__(16) unsigned char rsm[];
-    float *fst = reinterpret_cast<float *>(rsm);                            // [NS][R][K]
-    double *dt = reinterpret_cast<double *>(rsm + RT_NS * RT_F_TILE * 4);   // [2][R][LD]
-    const int e0 = blockIdx.x * RT_E, t0 = blockIdx.y * RT_T;
-    const int tid = threadIdx.x;
-    const int tl = tid & 7;          // token of this thread's chain
-    const int el = tid >> 3;         // expert of this thread's chain
-    const int nt = (hidden + RT_K - 1) / RT_K;
-    constexpr int CPR = RT_K / V;    // copies per tile row
+    float *fst = reinterpret_cast<float *>(rsm);                              // [NS][ROWS][FLD]
+    double *dt = reinterpret_cast<double *>(rsm + RB_NS * Tl::FSTAGE * 4);    // [2][K][ROWS]
+    const int t0 = blockIdx.y * Tl::TT, e0 = blockIdx.x * Tl::TE;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int trow = warp * A;                 // this warp's first token row in the tile
+    const int erow = Tl::TT + B * lane;        // this lane's first expert row
+    const int nt = (hidden + RB_K - 1) / RB_K;
 
+    // tile kt's floats into stage kt % NS (an empty group past the end keeps the count)
     auto issue = [&](int kt) {
         if (kt < nt) {
-            float *f = fst + (kt % RT_NS) * RT_F_TILE;
-            const int k0 = kt * RT_K;
-            for (int i = tid; i < RT_R * CPR; i += RT_THREADS) {
-                const int r = i / CPR, c = (i % CPR) * V;
-                const bool is_w = r < RT_E;
-                const int row = is_w ? e0 + r : t0 + (r - RT_E);
-                const bool ok = (is_w ? row < n : row < T) && k0 + c < hidden;
-                const float *src = is_w ? W : x;
+            float *f = fst + (kt % RB_NS) * Tl::FSTAGE;
+            const int k0 = kt * RB_K;
+            for (int i = tid; i < Tl::ROWS * (RB_K / V); i += RB_THREADS) {
+                const int r = i / (RB_K / V), c = (i % (RB_K / V)) * V;
+                const bool is_x = r < Tl::TT;
+                const int row = is_x ? t0 + r : e0 + (r - Tl::TT);
+                const bool ok = (is_x ? row < T : row < n) && k0 + c < hidden;
+                const float *src = is_x ? x : W;
                 if (ok) src += (size_t)row * hidden + k0 + c;
-                cp_async_f<V>(f + r * RT_K + c, src, ok);
+                cp_async_f<V>(f + r * RB_FLD + c, src, ok);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    for (int kt = 0; kt < RT_NS - 1; kt++) issue(kt);
-
-    double acc = 0.0;
-    for (int kt = 0; kt < nt; kt++) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(RT_NS - 2) : "memory");
-        __syncthreads();                       // tile kt landed for every thread's copies
-        issue(kt + RT_NS - 1);                 // into the stage tile kt-1 used
-        const float *f = fst + (kt % RT_NS) * RT_F_TILE;
-        double *d = dt + (kt & 1) * RT_R * RT_LD;
-        for (int i = tid; i < RT_F_TILE / 4; i += RT_THREADS) {   // widen once, 4 at a time
-            const float4 v = reinterpret_cast<const float4 *>(f)[i];
-            double *o = d + (i / (RT_K / 4)) * RT_LD + (i % (RT_K / 4)) * 4;
-            reinterpret_cast<double2 *>(o)[0] = make_double2(v.x, v.y);
-            reinterpret_cast<double2 *>(o)[1] = make_double2(v.z, v.w);
+    // tile kt's floats widened into double buffer kt & 1, [k][row]
+    auto widen = [&](int kt) {
+        const float *f = fst + (kt % RB_NS) * Tl::FSTAGE;
+        double *d = dt + (kt & 1) * RB_K * Tl::ROWS;
+        for (int p = tid; p < Tl::PIECES; p += RB_THREADS) {
+            const int r = p % Tl::ROWS, c = 4 * (p / Tl::ROWS);
+            const float4 v = *reinterpret_cast<const float4 *>(f + r * RB_FLD + c);
+            d[(c + 0) * Tl::ROWS + r] = (double)v.x;
+            d[(c + 1) * Tl::ROWS + r] = (double)v.y;
+            d[(c + 2) * Tl::ROWS + r] = (double)v.z;
+            d[(c + 3) * Tl::ROWS + r] = (double)v.w;
         }
-        __syncthreads();
-        const double *wr = d + el * RT_LD;
-        const double *xr = d + (RT_E + tl) * RT_LD;
-        const int kn = min(RT_K, hidden - kt * RT_K);
-        if (kn == RT_K) {
-            double2 wa[4], xa[4], wb[4], xb[4];
-            load8(wa, xa, wr, xr);
+    };
+
+    double acc[A][B];
 #pragma unroll
-            for (int c = 0; c < RT_K; c += 16) {
-                load8(wb, xb, wr + c + 8, xr + c + 8);
-                acc = chain8(acc, wa, xa);
-                if (c + 16 < RT_K) load8(wa, xa, wr + c + 16, xr + c + 16);
-                acc = chain8(acc, wb, xb);
-            }
+    for (int a = 0; a < A; a++)
+#pragma unroll
+        for (int b = 0; b < B; b++) acc[a][b] = 0.0;
+
+    auto step = [&](const double *dk) {
+        double xv[A], wv[B];
+#pragma unroll
+        for (int i = 0; i < A; i += 2) {   // the same address in every lane: a broadcast
+            const double2 v = *reinterpret_cast<const double2 *>(dk + trow + i);
+            xv[i] = v.x;
+            xv[i + 1] = v.y;
+        }
+        if (B == 2) {
+            const double2 v = *reinterpret_cast<const double2 *>(dk + erow);
+            wv[0] = v.x;
+            wv[B - 1] = v.y;
         } else {
-            for (int c = 0; c < kn; c++) acc = fma(wr[c], xr[c], acc);
+            wv[0] = dk[erow];
+        }
+#pragma unroll
+        for (int a = 0; a < A; a++)
+#pragma unroll
+            for (int b = 0; b < B; b++) acc[a][b] = __fma_rn(wv[b], xv[a], acc[a][b]);
+    };
+
+    for (int kt = 0; kt < RB_NS - 1; kt++) issue(kt);
+    asm volatile("cp.async.wait_group %0;" ::"n"(RB_NS - 2) : "memory");
+    __syncthreads();                           // tile 0 landed for every thread's copies
+    widen(0);
+    for (int kt = 0; kt < nt; kt++) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(RB_NS - 3) : "memory");
+        // tile kt+1 landed; widen(kt) done and compute(kt-1) finished in every warp
+        __syncthreads();
+        issue(kt + RB_NS - 1);                 // into the stage tile kt-1 used
+        if (kt + 1 < nt) widen(kt + 1);        // into the buffer compute(kt-1) read
+        const double *d = dt + (kt & 1) * RB_K * Tl::ROWS;
+        const int kn = min(RB_K, hidden - kt * RB_K);
+        if (kn == RB_K) {
+#pragma unroll 8
+            for (int k = 0; k < RB_K; k++) step(d + k * Tl::ROWS);
+        } else {
+            for (int k = 0; k < kn; k++) step(d + k * Tl::ROWS);
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    const int t = t0 + tl, e = e0 + el;
-    if (t < T && e < n) score[(size_t)t * n + e] = sigmoid_cr(__double2float_rn(acc));
+#pragma unroll
+    for (int a = 0; a < A; a++) {
+        const int t = t0 + trow + a;
+        if (t >= T) continue;
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            const int e = e0 + B * lane + b;
+            if (e < n) score[(size_t)t * n + e] = sigmoid_cr(__double2float_rn(acc[a][b]));
+        }
+    }
 }
 
 // One warp per token; scores [T][n] -> idx/w [T][topk]. Each lane keeps the selection
@@ -205,35 +231,72 @@ __global__ void __launch_bounds__(128) router_topk_kernel(int *__restrict__ idx,
 }
 
 // The opt-in to more than 48 KB of dynamic shared memory, once per device and variant.
-static int router_smem_optin(bool v4)
+template <int A, int B, int V>
+static int router_smem_optin()
 {
     static std::mutex mu;
-    static bool done[64][2] = {};
+    static bool done[64] = {};
     int dev = 0;
     int st = cuda_status(cudaGetDevice(&dev));
     if (st) return st;
     if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
     std::lock_guard<std::mutex> lock(mu);
-    if (!done[dev][v4]) {
-        st = cuda_status(v4 ? cudaFuncSetAttribute(router_scores_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM)
-                            : cudaFuncSetAttribute(router_scores_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM));
+    if (!done[dev]) {
+        st = cuda_status(cudaFuncSetAttribute(router_scores_kernel<A, B, V>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, RbTile<A, B>::SMEM));
         if (st) return st;
-        done[dev][v4] = true;
+        done[dev] = true;
     }
     return K3GPU_OK;
+}
+
+template <int A, int B>
+static int scores_launch(bool v4, float *score, const float *x, const float *W, int T, int hidden, int n,
+                         cudaStream_t s)
+{
+    using Tl = RbTile<A, B>;
+    int st = v4 ? router_smem_optin<A, B, 4>() : router_smem_optin<A, B, 1>();
+    if (st) return st;
+    dim3 g(ceil_div(n, Tl::TE), ceil_div(T, Tl::TT));
+    if (v4) router_scores_kernel<A, B, 4><<<g, RB_THREADS, Tl::SMEM, s>>>(score, x, W, T, hidden, n);
+    else router_scores_kernel<A, B, 1><<<g, RB_THREADS, Tl::SMEM, s>>>(score, x, W, T, hidden, n);
+    return launch_status();
+}
+
+// Estimated clocks per hidden column of tile shape (a, b): the FP64 issue of the warps
+// sharing one scheduler (2 clocks per warp FMA), the shared-memory wavefronts of the warps
+// sharing one SM (a/2 broadcast loads of one wavefront, b doubles per lane at 2 wavefronts
+// per 8 bytes x 32 lanes), and one chain step: an FMA latency (about 8 clocks) and its issue.
+static double scores_cost(int a, int b, int T, int n, int sms)
+{
+    const double warps = 4.0 * ceil_div(T, 4 * a) * ceil_div(n, 32 * b);
+    const double fp64 = ceil(warps / (4.0 * sms)) * 2.0 * a * b;
+    const double lds = ceil(warps / sms) * (a / 2 + 2 * b);
+    return fmax(fmax(fp64, lds), 10.0);
 }
 
 int router_launch(int *idx, float *w, const float *x, const float *W, const float *bias, int T,
                   int hidden, int n, int topk, int renorm, float routed_scale, float *score,
                   cudaStream_t s)
 {
-    dim3 g1(ceil_div(n, RT_E), ceil_div(T, RT_T));
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const bool v4 = hidden % 4 == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)W & 15u) == 0;
-    int st0 = router_smem_optin(v4);
-    if (st0) return st0;
-    if (v4) router_scores_kernel<4><<<g1, RT_THREADS, RT_SMEM, s>>>(score, x, W, T, hidden, n);
-    else router_scores_kernel<1><<<g1, RT_THREADS, RT_SMEM, s>>>(score, x, W, T, hidden, n);
-    int st = launch_status();
+    static const int shapes[][2] = {{8, 2}, {6, 2}, {4, 2}, {4, 1}, {2, 1}};
+    int best = 0;
+    double bc = 1e300;
+    for (int i = 0; i < 5; i++) {
+        const double c = scores_cost(shapes[i][0], shapes[i][1], T, n, sms);
+        if (c < bc) { bc = c; best = i; }
+    }
+    int st;
+    switch (best) {
+    case 0: st = scores_launch<8, 2>(v4, score, x, W, T, hidden, n, s); break;
+    case 1: st = scores_launch<6, 2>(v4, score, x, W, T, hidden, n, s); break;
+    case 2: st = scores_launch<4, 2>(v4, score, x, W, T, hidden, n, s); break;
+    case 3: st = scores_launch<4, 1>(v4, score, x, W, T, hidden, n, s); break;
+    default: st = scores_launch<2, 1>(v4, score, x, W, T, hidden, n, s); break;
+    }
     if (st) return st;
     router_topk_kernel<<<ceil_div(T, 4), 128, 0, s>>>(idx, w, score, bias, T, n, topk, renorm,
                                                       routed_scale);

@@ -51,8 +51,11 @@ def wdev(Wb):
     return torch.from_numpy(Wb.view(np.int16)).cuda()
 
 
+# the last three: a tree batch's position tiles (1024 = 8 tiles), two launches with a ragged
+# second (2100 = 2048 + 52), and K splits over many position tiles of a narrow output
 @pytest.mark.parametrize("T,n_in,n_out", [(72, 7168, 1024), (5, 512, 300), (200, 1024, 256),
-                                          (300, 256, 130), (9, 520, 64), (1, 2048, 7168)])
+                                          (300, 256, 130), (9, 520, 64), (1, 2048, 7168),
+                                          (1024, 1024, 512), (2100, 256, 130), (1000, 7168, 64)])
 def test_matmul_bf16_fp32_activations(k3, T, n_in, n_out):
     rng = np.random.default_rng(T * 131 + n_in + n_out)
     X = rng.standard_normal((T, n_in), dtype=np.float32)
