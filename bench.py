@@ -587,6 +587,16 @@ def unique_experts_bytes(idx_np, stride_bytes_per_expert):
 
 
 # ------------------------------------------------------------------------ clocks ---
+def sm_max_mhz(gpu_index=0):
+    """The GPU's maximum SM clock (nvidia-smi clocks.max.sm), 1965 MHz when it cannot be read."""
+    try:
+        r = subprocess.run(["nvidia-smi", "-i", str(gpu_index), "--query-gpu=clocks.max.sm",
+                            "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=20)
+        return float(r.stdout.strip().splitlines()[0])
+    except (OSError, ValueError, IndexError, subprocess.SubprocessError):
+        return 1965.0
+
+
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -1135,6 +1145,50 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
         except Exception as ex:  # noqa: BLE001
             rows["lm_head_bf16_c4"] = {"error": str(ex)[:200]}
 
+    # a tree batch's projection: T = 1024 positions (c4: 16 sequences x 64 nodes) through a
+    # 7168 -> 4096 bf16 matrix; a real GEMM, graded as tensor work (hi and lo products)
+    if only is None or only == "trunk_matmul_bf16_t1024":
+        try:
+            T, n_in, n_out = 1024, 7168, 4096
+            X = torch.randn((T, n_in), generator=g, device=dev)
+            W = (torch.randn((n_out, n_in), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            Y = torch.empty((T, n_out), device=dev)
+            ws = k3.workspace(k3.lib.k3gpu_matmul_bf16_workspace(T, n_in, n_out), dev)
+            us = timed(lambda: k3.matmul_bf16(X, W, out=Y, ws=ws))
+            tf = 4.0 * T * n_in * n_out / (us * 1e-6) / 1e12
+            rows["trunk_matmul_bf16_t1024"] = {"us": round(us, 2), "tflops": round(tf, 1),
+                                               "frac_tensor": round(tf / tflops_peak, 4), "bound": "tensor",
+                                               "flops": "4*T*in*out (the hi and lo products)",
+                                               "shape": "T=1024, 7168 -> 4096"}
+            del W, Y
+        except Exception as ex:  # noqa: BLE001
+            rows["trunk_matmul_bf16_t1024"] = {"error": str(ex)[:200]}
+
+    # the router over 384 experts x 7168: a verify step of config 2 (72 tokens) and the c4
+    # sweep (1024 tokens); each score one in-order double chain, graded against FP64 issue
+    # (64 FMA per clock per SM at the clock this run saw)
+    if only is None or only == "router":
+        try:
+            n, hidden, topk = 384, 7168, 8
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            rr = {}
+            for T in (72, 1024):
+                x = torch.randn((T, hidden), generator=g, device=dev)
+                W = torch.randn((n, hidden), generator=g, device=dev) * 0.02
+                bias = torch.randn((n,), generator=g, device=dev) * 0.01
+                ws = k3.workspace(k3.lib.k3gpu_router_workspace(T, n), dev)
+                us = timed(lambda: k3.router(x, W, bias, topk, ws=ws))
+                mhz = sm_max_mhz(torch.cuda.current_device())
+                floor_us = T * n * hidden / (64.0 * sms * mhz)
+                rr[f"T{T}"] = {"us": round(us, 2), "dfma_per_s": round(T * n * hidden / (us * 1e-6), 0),
+                               "fp64_floor_us": round(floor_us, 2), "frac_fp64": round(floor_us / us, 4),
+                               "sm_mhz": mhz}
+            rows["router"] = dict(rr, bound="fp64 issue (64 FMA/clock/SM at the max SM clock); shared-memory "
+                                            "operand delivery in practice",
+                                  shape="384 experts x 7168, top-8")
+        except Exception as ex:  # noqa: BLE001
+            rows["router"] = {"error": str(ex)[:200]}
+
     # greedy accept over the K3 vocabulary: 8 sequences x 9 positions x 163840
     if only is None or only == "accept_greedy_vocab":
         try:
@@ -1405,7 +1459,7 @@ def main():
                     help="--gpus N > 1: token rows through peer memory (default) or NCCL all-to-all")
     ap.add_argument("--only-row", default=None,
                     choices=["kda_c3", "kda_prefill", "mla_absorbed_c4", "trunk_matmul_bf16", "lm_head_bf16_c4",
-                             "accept_greedy_vocab"],
+                             "trunk_matmul_bf16_t1024", "router", "accept_greedy_vocab"],
                     help="time one of the other rows alone and print it (for profiling captures)")
     ap.add_argument("--only-c2", type=int, nargs=2, metavar=("B", "K"), default=None,
                     help="time the config-2 layer at one (B, k) point alone and print its row (small cases "

@@ -61,6 +61,14 @@ inline size_t plan_bytes(int T, int S, int E, int L, int I, MoePlan *p, char *ba
     return o;
 }
 
+// 2^e exactly, for the row exponents of the expert paths (e in -127..127: the packers clamp
+// e to -126..127 and scale by 2^-e). x * pow2f(e) rounds once, so it equals ldexpf(x, e)
+// bit for bit, at a fraction of its cost (the epilogues scale every output this way).
+__device__ __forceinline__ float pow2f(int e)
+{
+    return e >= -126 ? __int_as_float((e + 127) << 23) : __int_as_float(0x00400000);   // 2^-127
+}
+
 __device__ __forceinline__ float act_situ(float g, float u, float b1, float b2)
 {
     const float a = b1 * tanhf(g / b1) * (1.0f / (1.0f + expf(-g)));

@@ -351,14 +351,14 @@ __global__ void __launch_bounds__(MM_THREADS, 1) moe_mma_kernel(const __grid_con
                     const int q = q0 + tok;
                     if (PHASE == 0) {
                         const int ex = Xe[q];
-                        const float gv = ldexpf(D[c][j], ex), uv = ldexpf(D[c][2 + j], ex);
+                        const float gv = __fmul_rn(D[c][j], pow2f(ex)), uv = __fmul_rn(D[c][2 + j], pow2f(ex));
                         const float hv = act == K3GPU_ACT_SITU ? act_situ(gv, uv, b1, b2) : act_swiglu(gv, uv);
                         p.H[(size_t)q * bank.I + ub * 64 + 8 * warp + g] = hv;
                     } else {
                         const int ex = Xe[q];
                         const size_t o = (size_t)p.pair_dst[q] * bank.L + ub * 128 + 16 * warp + g;
-                        p.contrib[o] = ldexpf(D[c][j], ex);
-                        p.contrib[o + 8] = ldexpf(D[c][2 + j], ex);
+                        p.contrib[o] = __fmul_rn(D[c][j], pow2f(ex));
+                        p.contrib[o + 8] = __fmul_rn(D[c][2 + j], pow2f(ex));
                     }
                 }
             }
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(256) act_pack_kernel(__half *__restrict__ hi, 
     if (m > 0.f && m <= 3.4e38f) e = max(-126, min(127, ilogbf(m) - 14));
     int any = 0;
     for (int i = threadIdx.x; i < K; i += 256) {
-        const float y = ldexpf(xr[i], -e);
+        const float y = __fmul_rn(xr[i], pow2f(-e));
         const __half h = __float2half_rn(y);
         const __half l = __float2half_rn(y - __half2float(h));
         hi[(size_t)row * K + i] = h;

@@ -50,14 +50,27 @@ constexpr int TC_S_BYTES = 128 * 16;     // E8M0 bytes of a stage
 // expert): up to 32 tokens a pass so each weight is decoded once for all of its expert's
 // tokens -- the decode, not the tensor pipe, bounds the sparse shape once an expert needs
 // several passes -- at the cost of one issuer per K half (an N = 64 MMA keeps the pipe busy
-// from one thread), two A buffers and two stages.
-template <int NP_, int NMMA_, int NA_, int NS_, int TAB_> struct TcShape {
+// from one thread), two A buffers, and split rings: at 32 tokens a stage's activation tile
+// (64 KB of hi and lo rows) is twice its weights, and in one ring a stage's weights stay
+// resident until its MMAs finish. Split, the weights and scales (NS stages) return to the
+// TMA as soon as the decode warps have read them, and the activation tiles come in K halves
+// (NBH slots, their own producer warp) that each half's issuer frees: 96 KB of weights in
+// flight per SM instead of 64 KB, over a shorter lifetime.
+template <int NP_, int NMMA_, int NA_, int NS_, int TAB_, int NBH_ = 0> struct TcShape {
     static constexpr int NP = NP_;                      // tokens per pass
     static constexpr int N = 2 * NP;                    // MMA N: the pass's hi rows, then their lo rows
     static constexpr int NMMA = NMMA_;                  // issuers: NMMA / 2 per K half
     static constexpr int MPI = 32 / NMMA;               // K16 MMAs per issuer per stage
-    static constexpr int NA = NA_;                      // TMEM A buffers (128 columns = 256 K each)
-    static constexpr int NS = NS_;                      // shared-memory stages
+    static constexpr int NA = NA_;                      // TMEM A buffers (ACOLS columns each)
+    static constexpr int NS = NS_;                      // shared-memory stages (split: weight stages)
+    static constexpr int NBH = NBH_;                    // split rings: activation half-stage slots
+    static constexpr bool SPLIT = NBH_ > 0;
+    // split rings: a K half's A rows in two 64-column sub-buffers (128 K each), so the issuer
+    // runs one sub-buffer's MMAs while the decode warps fill the other, and the next item's
+    // decode starts as soon as the first is free: decode and MMA issue overlap instead of
+    // taking turns on one buffer per half
+    static constexpr int SUBS = SPLIT ? 2 : 1;          // A buffers per K half of a stage
+    static constexpr int ACOLS = 128 / SUBS;
     static constexpr int TAB = TAB_;                    // active-expert entries kept in shared memory
     static constexpr int B_BYTES = (TC_KC / 64) * NP * 128;   // one activation piece of a stage
     static constexpr int STAGE = TC_W_BYTES + TC_S_BYTES + 2 * B_BYTES + 1024 - TC_S_BYTES % 1024;
@@ -65,24 +78,30 @@ template <int NP_, int NMMA_, int NA_, int NS_, int TAB_> struct TcShape {
     // groups), so one N = 2 NP MMA yields the hi products in D columns 0..NP-1 and the lo
     // products in NP..2NP-1; without lo halves the upper columns are unused
     static constexpr int ATOM = 2 * NP * 128;
+    static constexpr int WSTAGE = TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024);   // split: weights + scales
+    static constexpr int BHALF = (256 / 64) * ATOM;     // split: the activation atoms of one K half
+    static constexpr int RINGS = SPLIT ? NS * WSTAGE + NBH * BHALF : NS * STAGE;
     static constexpr int PW = N;                        // D columns per issuer
     static constexpr int PCOLS = NMMA * PW;             // one stage-partial set
     static constexpr int ACOL0 = 2 * PCOLS;             // first A column
     static constexpr int XCH_BYTES = 64 * NP * 4;       // gate/up exchange in the epilogue
-    // barriers: full[NS] empty[NS] aready[NA] afree[NA] pfree[2] (stage partials)
-    static constexpr int NBAR = 2 * NS + 2 * NA + 2;
+    // barriers: full[NS] empty[NS] (split: [bfull bempty][NBH]) aready[NA] afree[NA] pfree[2]
+    // (split: pfull[2], the issuers' stage partials final)
+    static constexpr int NBAR = 2 * NS + 2 * NBH + 2 * NA + 2 + (SPLIT ? 2 : 0);
     // after the expert table: the E8M0 byte -> f16x2 scale pair table (256 entries)
-    static constexpr int SMEM = NS * STAGE + XCH_BYTES + NBAR * 8 + 16 + TAB * 16 + 256 * 4;
-    static constexpr int THREADS = (TC_MMA_WARP0 + NMMA) * 32;
-    static_assert(ACOL0 + NA * 128 <= 512, "TMEM columns");
-    static_assert(STAGE % 1024 == 0, "stage alignment");
-    static_assert((NS * STAGE + XCH_BYTES + (NBAR + 2) * 8) % 16 == 0, "int4 expert table alignment");
+    static constexpr int SMEM = RINGS + XCH_BYTES + NBAR * 8 + 16 + TAB * 16 + 256 * 4;
+    // split: one more warp, the activation producer
+    static constexpr int THREADS = (TC_MMA_WARP0 + NMMA + (SPLIT ? 1 : 0)) * 32;
+    static_assert(ACOL0 + NA * ACOLS <= 512, "TMEM columns");
+    static_assert(MPI % SUBS == 0, "MMAs per sub-buffer");
+    static_assert(STAGE % 1024 == 0 && WSTAGE % 1024 == 0 && BHALF % 1024 == 0, "stage alignment");
+    static_assert((RINGS + XCH_BYTES + (NBAR + 2) * 8) % 16 == 0, "int4 expert table alignment");
     static_assert(SMEM <= 227 * 1024, "shared memory");
     static_assert(NMMA == 2 || NMMA == 4, "issuers per K half");
     static_assert(NP == 8 || NP % 16 == 0, "pass width");
 };
 using TcSparse = TcShape<8, 4, 3, 4, 1024>;
-using TcDense = TcShape<32, 2, 2, 2, 512>;
+using TcDense = TcShape<32, 2, 4, 3, 512, 3>;
 constexpr long long TC_SPIN = 1LL << 22;
 constexpr int TC_SUSPEND_NS = 1000;
 
@@ -227,20 +246,30 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
         if (threadIdx.x == 0) flag(DEV_BAD_INDEX);
         return;
     }
-    float *xch = reinterpret_cast<float *>(smem + (size_t)CF::NS * CF::STAGE);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)CF::NS * CF::STAGE + CF::XCH_BYTES);
+    float *xch = reinterpret_cast<float *>(smem + (size_t)CF::RINGS);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)CF::RINGS + CF::XCH_BYTES);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + CF::NBAR);
     int4 *tab = reinterpret_cast<int4 *>(bars + CF::NBAR + 2);   // [CF::TAB] {e, cnt, off, flags}
     uint32_t *stab = reinterpret_cast<uint32_t *>(tab + CF::TAB);   // [256] scale_h2 of each byte
-    uint64_t *b_full = bars, *b_empty = bars + CF::NS;
-    uint64_t *b_aready = bars + 2 * CF::NS, *b_afree = bars + 2 * CF::NS + CF::NA;
-    uint64_t *b_pfree = bars + 2 * CF::NS + 2 * CF::NA;   // partial buffers: epilogue -> MMA
+    uint64_t *b_full = bars, *b_empty = bars + CF::NS;   // split: the weight ring
+    uint64_t *b_bfull = bars + 2 * CF::NS, *b_bempty = b_bfull + CF::NBH;   // split: the activation ring
+    uint64_t *b_aready = bars + 2 * CF::NS + 2 * CF::NBH, *b_afree = b_aready + CF::NA;
+    uint64_t *b_pfree = b_afree + CF::NA;                 // partial buffers: epilogue -> MMA
+    uint64_t *b_pfull = b_pfree + 2;                      // split: partial buffers: MMA -> epilogue
+    // a stage's weights (and, in one ring, its activation tile) and a split activation slot
+    auto wstage = [&](int st) { return smem + (size_t)st * (CF::SPLIT ? CF::WSTAGE : CF::STAGE); };
+    auto bslot = [&](int b) { return smem + (size_t)CF::NS * CF::WSTAGE + (size_t)b * CF::BHALF; };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < CF::NS; s++) {
             bar_init(s_addr(&b_full[s]), 1);
-            bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + CF::NMMA);   // decode warps + MMA commits
+            // decode warps (+ the MMA commits when the stage also holds the activations)
+            bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + (CF::SPLIT ? 0 : CF::NMMA));
+        }
+        for (int b = 0; b < CF::NBH; b++) {
+            bar_init(s_addr(&b_bfull[b]), 1);
+            bar_init(s_addr(&b_bempty[b]), CF::NMMA / 2);       // commits of that K half's issuers
         }
         for (int a = 0; a < CF::NA; a++) {
             bar_init(s_addr(&b_aready[a]), 4);                  // the four warps of that K half
@@ -248,6 +277,7 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
         }
         for (int d = 0; d < 2; d++) {
             bar_init(s_addr(&b_pfree[d]), 4);                   // epilogue warps
+            if (CF::SPLIT) bar_init(s_addr(&b_pfull[d]), CF::NMMA);   // every issuer's commit
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -309,11 +339,11 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
                     const int st = item % CF::NS;
                     const uint32_t par = (uint32_t)((item / CF::NS) & 1);
                     if (!bar_wait(s_addr(&b_empty[st]), par ^ 1u)) { failed = true; break; }
-                    unsigned char *sw = smem + (size_t)st * CF::STAGE;
+                    unsigned char *sw = wstage(st);
                     unsigned char *ssb = sw + TC_W_BYTES;
                     unsigned char *sbh = sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024);
                     const uint32_t full = s_addr(&b_full[st]);
-                    bar_expect(full, (uint32_t)(TC_W_BYTES + TC_S_BYTES + CF::B_BYTES * (lo_any ? 2 : 1)));
+                    bar_expect(full, (uint32_t)(TC_W_BYTES + TC_S_BYTES + (CF::SPLIT ? 0 : CF::B_BYTES * (lo_any ? 2 : 1))));
                     const int x0 = kc * 256, xs = kc * 16;
                     if (PHASE == 0) {
                         const int y1 = (int)(e * ta.wys + ta.wy1 + ub * 64), y3 = (int)(e * ta.wys + ta.wy3 + ub * 64);
@@ -332,9 +362,34 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
                     // activation tiles: 8 atoms of 64 K x 16 pair rows (rows past the expert
                     // belong to the next one or lie past the tensor: those columns are
                     // never read back; out-of-range rows are filled with zeros)
-                    for (int a = 0; a < TC_KC / 64; a++) {
+                    for (int a = 0; a < (CF::SPLIT ? 0 : TC_KC / 64); a++) {
                         tma2d(s_addr(sbh + a * CF::ATOM), &bhmap, kc * TC_KC + a * 64, q0 + tb, full);
                         if (lo_any) tma2d(s_addr(sbh + a * CF::ATOM + CF::NP * 128), &blmap, kc * TC_KC + a * 64, q0 + tb, full);
+                    }
+                }
+            });
+            if (failed) flag(DEV_TIMEOUT);
+        }
+    } else if (CF::SPLIT && warp == TC_MMA_WARP0 + CF::NMMA) {
+        // split rings: the activation producer, one K half (4 atoms) per slot
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&bhmap) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&blmap) : "memory");
+            TC_FOR_UNITS({
+                for (int kc = 0; kc < NK && !failed; kc++, item++) {
+                    for (int h = 0; h < 2 && !failed; h++) {
+                        const int fill = 2 * item + h;
+                        const int slot = fill % (CF::SPLIT ? CF::NBH : 1);
+                        const uint32_t par = (uint32_t)((fill / (CF::SPLIT ? CF::NBH : 1)) & 1);
+                        if (!bar_wait(s_addr(&b_bempty[slot]), par ^ 1u)) { failed = true; break; }
+                        unsigned char *sb = bslot(slot);
+                        const uint32_t full = s_addr(&b_bfull[slot]);
+                        bar_expect(full, (uint32_t)(4 * CF::NP * 128 * (lo_any ? 2 : 1)));
+                        for (int a = 0; a < 4; a++) {
+                            const int x = kc * TC_KC + h * 256 + a * 64;
+                            tma2d(s_addr(sb + a * CF::ATOM), &bhmap, x, q0 + tb, full);
+                            if (lo_any) tma2d(s_addr(sb + a * CF::ATOM + CF::NP * 128), &blmap, x, q0 + tb, full);
+                        }
                     }
                 }
             });
@@ -357,7 +412,7 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
             uint32_t boff16[CF::MPI];
 _Pragma("unroll")
             for (int t = 0; t < CF::MPI; t++) {
-                const int kk = h * 256 + (j * CF::MPI + t) * 16;
+                const int kk = (CF::SPLIT ? 0 : h * 256) + (j * CF::MPI + t) * 16;   // split: K inside the half
                 boff16[t] = (uint32_t)(((kk >> 6) * CF::ATOM + (kk & 63) * 2) >> 4);
             }
             TC_FOR_UNITS({
@@ -365,24 +420,42 @@ _Pragma("unroll")
                     const int st = item % CF::NS;
                     const uint32_t par = (uint32_t)((item / CF::NS) & 1);
                     const int pb = item & 1;
-                    const int fill = 2 * item + h;   // the A buffer the decode warps filled
-                    const int ab = fill % TM::NA;
-                    const uint32_t apar = (uint32_t)((fill / TM::NA) & 1);
+                    const int hfill = 2 * item + h;   // this half's place in the activation ring
+                    // split: this half's activation slot
+                    const int bslot_i = hfill % (CF::SPLIT ? CF::NBH : 1);
+                    const uint32_t bpar = (uint32_t)((hfill / (CF::SPLIT ? CF::NBH : 1)) & 1);
                     if (!bar_wait(s_addr(&b_pfree[pb]), (uint32_t)(((item >> 1) & 1) ^ 1))) { failed = true; break; }
-                    if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
-                    if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    if (CF::SPLIT) {
+                        if (!bar_wait(s_addr(&b_bfull[bslot_i]), bpar)) { failed = true; break; }
+                    } else {
+                        if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
+                    }
                     const uint32_t dtm = tmem + (uint32_t)(pb * TM::PCOLS + mi * TM::PW);
-                    const unsigned char *sw = smem + (size_t)st * CF::STAGE;
-                    const uint32_t bh = s_addr(sw + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
-                    const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * 128 + j * CF::MPI * 8);
+                    const uint32_t bh = CF::SPLIT ? s_addr(bslot(bslot_i))
+                                                  : s_addr(wstage(st) + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
                     const uint64_t dh = sw128_desc(bh);
-                    // the atom's hi and lo rows as one N = 2 NP operand
+                    constexpr int PS = CF::MPI / CF::SUBS;   // MMAs per sub-buffer
 _Pragma("unroll")
-                    for (int t = 0; t < CF::MPI; t++)             // K16 steps of this issuer
-                        mma_ts(dtm, atm + (uint32_t)(t * 8), dh + boff16[t], idesc, t ? 1u : 0u);
-                    mma_commit(s_addr(&b_afree[ab]));
-                    mma_commit(s_addr(&b_empty[st]));   // also tells the epilogue (no pfull commit)
+                    for (int sb = 0; sb < CF::SUBS; sb++) {
+                        const int fill = hfill * CF::SUBS + sb;   // the A buffer the decode warps filled
+                        const int ab = fill % TM::NA;
+                        const uint32_t apar = (uint32_t)((fill / TM::NA) & 1);
+                        if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * TM::ACOLS + (CF::SUBS == 1 ? j * CF::MPI * 8 : 0));
+                        // the atom's hi and lo rows as one N = 2 NP operand
+_Pragma("unroll")
+                        for (int t = sb * PS; t < (sb + 1) * PS; t++)   // K16 steps of this issuer
+                            mma_ts(dtm, atm + (uint32_t)((t - sb * PS) * 8), dh + boff16[t], idesc, t ? 1u : 0u);
+                        mma_commit(s_addr(&b_afree[ab]));
+                    }
+                    if (failed) break;
+                    if (CF::SPLIT) {
+                        mma_commit(s_addr(&b_bempty[bslot_i]));
+                        mma_commit(s_addr(&b_pfull[pb]));   // the epilogue's signal
+                    } else {
+                        mma_commit(s_addr(&b_empty[st]));   // also tells the epilogue (no pfull commit)
+                    }
                 }
             });
             if (failed) flag(DEV_TIMEOUT);
@@ -402,49 +475,52 @@ _Pragma("unroll")
             for (int kc = 0; kc < NK && !failed; kc++, item++) {
                 const int st = item % CF::NS;
                 const uint32_t par = (uint32_t)((item / CF::NS) & 1);
-                // the A buffer this warp fills: half h of this stage
-                const int fill = 2 * item + h;
-                const int ab = fill % CF::NA;
-                const uint32_t apar = (uint32_t)((fill / CF::NA) & 1);
                 if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
-                if (!bar_wait(s_addr(&b_afree[ab]), apar ^ 1u)) { failed = true; break; }
-                const unsigned char *sw = smem + (size_t)st * CF::STAGE;
+                const unsigned char *sw = wstage(st);
                 const unsigned char *row = sw + boxbase + h * hbox + boxrow * 128;
                 const uint2 sc = *reinterpret_cast<const uint2 *>(sw + TC_W_BYTES + r * 16 + h * 8);
-                const uint32_t atm = tmem + lane_addr + (uint32_t)(CF::ACOL0 + ab * 128);
-                // 8 groups of 32 in this K half, four at a time: the four loads go first (a
-                // load placed after a tcgen05.st would wait for it)
+                constexpr int GS = 8 / CF::SUBS;                  // groups of 32 K per sub-buffer
 _Pragma("unroll")
-                for (int g4 = 0; g4 < 8; g4 += 4) {
-                uint4 pks[4];
+                for (int sb = 0; sb < CF::SUBS; sb++) {
+                    // the A buffer this warp fills: sub-buffer sb of half h of this stage
+                    const int fill = (2 * item + h) * CF::SUBS + sb;
+                    const int ab = fill % CF::NA;
+                    const uint32_t apar = (uint32_t)((fill / CF::NA) & 1);
+                    if (!bar_wait(s_addr(&b_afree[ab]), apar ^ 1u)) { failed = true; break; }
+                    const uint32_t atm = tmem + lane_addr + (uint32_t)(CF::ACOL0 + ab * CF::ACOLS);
+                    // the groups of 32 in this sub-buffer, four at a time: the four loads go
+                    // first (a load placed after a tcgen05.st would wait for it)
 _Pragma("unroll")
-                for (int i = 0; i < 4; i++) pks[i] = *reinterpret_cast<const uint4 *>(row + (((g4 + i) ^ swz) << 4));
+                    for (int g4 = sb * GS; g4 < (sb + 1) * GS; g4 += 4) {
+                        uint4 pks[4];
 _Pragma("unroll")
-                for (int i = 0; i < 4; i++) {
-                    const int g8 = g4 + i;
-                    const uint4 pk = pks[i];
-                    const uint32_t S = ((g8 < 4 ? sc.x : sc.y) >> (8 * (g8 & 3))) & 0xFFu;
-                    const uint32_t s2 = stab[S];          // one shared load instead of ~8 ALU ops
-                    uint32_t v[16];
-                    uint32_t t4[4];
-                    cvt4h(pk.x, t4);
-                    v[0] = hmul2u(t4[0], s2); v[1] = hmul2u(t4[1], s2); v[2] = hmul2u(t4[2], s2); v[3] = hmul2u(t4[3], s2);
-                    cvt4h(pk.y, t4);
-                    v[4] = hmul2u(t4[0], s2); v[5] = hmul2u(t4[1], s2); v[6] = hmul2u(t4[2], s2); v[7] = hmul2u(t4[3], s2);
-                    cvt4h(pk.z, t4);
-                    v[8] = hmul2u(t4[0], s2); v[9] = hmul2u(t4[1], s2); v[10] = hmul2u(t4[2], s2); v[11] = hmul2u(t4[3], s2);
-                    cvt4h(pk.w, t4);
-                    v[12] = hmul2u(t4[0], s2); v[13] = hmul2u(t4[1], s2); v[14] = hmul2u(t4[2], s2); v[15] = hmul2u(t4[3], s2);
-                    tmem_st16(atm + (uint32_t)(g8 * 16), v);
+                        for (int i = 0; i < 4; i++) pks[i] = *reinterpret_cast<const uint4 *>(row + (((g4 + i) ^ swz) << 4));
+_Pragma("unroll")
+                        for (int i = 0; i < 4; i++) {
+                            const int g8 = g4 + i;
+                            const uint4 pk = pks[i];
+                            const uint32_t S = ((g8 < 4 ? sc.x : sc.y) >> (8 * (g8 & 3))) & 0xFFu;
+                            const uint32_t s2 = stab[S];          // one shared load instead of ~8 ALU ops
+                            uint32_t v[16];
+                            uint32_t t4[4];
+                            cvt4h(pk.x, t4);
+                            v[0] = hmul2u(t4[0], s2); v[1] = hmul2u(t4[1], s2); v[2] = hmul2u(t4[2], s2); v[3] = hmul2u(t4[3], s2);
+                            cvt4h(pk.y, t4);
+                            v[4] = hmul2u(t4[0], s2); v[5] = hmul2u(t4[1], s2); v[6] = hmul2u(t4[2], s2); v[7] = hmul2u(t4[3], s2);
+                            cvt4h(pk.z, t4);
+                            v[8] = hmul2u(t4[0], s2); v[9] = hmul2u(t4[1], s2); v[10] = hmul2u(t4[2], s2); v[11] = hmul2u(t4[3], s2);
+                            cvt4h(pk.w, t4);
+                            v[12] = hmul2u(t4[0], s2); v[13] = hmul2u(t4[1], s2); v[14] = hmul2u(t4[2], s2); v[15] = hmul2u(t4[3], s2);
+                            tmem_st16(atm + (uint32_t)((g8 - sb * GS) * 16), v);
+                        }
+                    }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(s_addr(&b_aready[ab]));
                 }
-                }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) {
-                    bar_arrive(s_addr(&b_aready[ab]));
-                    bar_arrive(s_addr(&b_empty[st]));
-                }
+                if (failed) break;
+                if (lane == 0) bar_arrive(s_addr(&b_empty[st]));
             }
         });
         if (failed && lane == 0) flag(DEV_TIMEOUT);
@@ -467,7 +543,11 @@ _Pragma("unroll")
                 // empty[st] completes once all four issuers' MMAs of the stage are done: the
                 // partials are final. (The MMAs run at most two stages ahead of this wait --
                 // they need pfree -- so the phase cannot be lapped.)
-                if (!bar_wait(s_addr(&b_empty[item % CF::NS]), (uint32_t)((item / CF::NS) & 1))) { failed = true; break; }
+                if (CF::SPLIT) {   // both issuers' commits of this item
+                    if (!bar_wait(s_addr(&b_pfull[pb]), (uint32_t)((item >> 1) & 1))) { failed = true; break; }
+                } else {
+                    if (!bar_wait(s_addr(&b_empty[item % CF::NS]), (uint32_t)((item / CF::NS) & 1))) { failed = true; break; }
+                }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 using TM = CF;
                 const uint32_t pt = tmem + lane_addr + (uint32_t)(pb * TM::PCOLS);
@@ -515,24 +595,38 @@ _Pragma("unroll")
             }
             if (failed) break;
             if (PHASE == 0) {
-                // lanes 64..127 hold the up rows: hand them to the gate lanes 0..63
-                if (r >= 64)
-                    for (int n = 0; n < CF::NP; n++) xch[(r - 64) * CF::NP + n] = acc[n];
-                asm volatile("bar.sync 2, 128;" ::: "memory");
-                if (r < 64) {
-                    // n runs over all CF::NP with a warp-uniform guard: acc stays in registers
+                // lanes 0..63 hold the gate rows, 64..127 the up rows of the same 64 rows:
+                // each side hands the other half of its tokens over (gate values of odd
+                // tokens, up values of even ones; [side][token / 2][row], conflict-free), so
+                // all 128 threads apply the activation, to half the tokens each. The unit's
+                // next MMAs wait on this tail, so it must be short.
+                const int rr = r & 63, side = r >> 6;   // side is warp-uniform
 _Pragma("unroll")
-                    for (int n = 0; n < CF::NP; n++) {
-                        if (n < npt) {
-                            const int q = q0 + tb + n;
-                            const int ex = __shfl_sync(0xffffffffu, ex_l, n);
-                            const float gv = ldexpf(acc[n], ex);
-                            const float uv = ldexpf(xch[r * CF::NP + n], ex);
-                            const float hv = act == K3GPU_ACT_SITU ? act_situ(gv, uv, b1, b2) : act_swiglu(gv, uv);
-                            p.H[(size_t)q * bank.I + ub * 64 + r] = hv;
-                        }
-                    }
+                for (int n = 0; n < CF::NP; n++)
+                    if ((n & 1) != side) xch[(side * (CF::NP / 2) + n / 2) * 64 + rr] = acc[n];
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                // this side's tokens n = 2k + side: every activation first, unguarded (the
+                // NP/2 chains are independent and interleave), the guarded stores after;
+                // acc is indexed by compile-time k only, so it stays in registers
+                float gv[CF::NP / 2], uv[CF::NP / 2], hv[CF::NP / 2];
+_Pragma("unroll")
+                for (int k = 0; k < CF::NP / 2; k++) {
+                    const float mine = side ? acc[2 * k + 1] : acc[2 * k];
+                    const float other = xch[((1 - side) * (CF::NP / 2) + k) * 64 + rr];
+                    const float p2 = pow2f(__shfl_sync(0xffffffffu, ex_l, 2 * k + side));
+                    gv[k] = __fmul_rn(side ? other : mine, p2);
+                    uv[k] = __fmul_rn(side ? mine : other, p2);
                 }
+                if (act == K3GPU_ACT_SITU) {
+_Pragma("unroll")
+                    for (int k = 0; k < CF::NP / 2; k++) hv[k] = act_situ(gv[k], uv[k], b1, b2);
+                } else {
+_Pragma("unroll")
+                    for (int k = 0; k < CF::NP / 2; k++) hv[k] = act_swiglu(gv[k], uv[k]);
+                }
+_Pragma("unroll")
+                for (int k = 0; k < CF::NP / 2; k++)
+                    if (2 * k + side < npt) p.H[(size_t)(q0 + tb + 2 * k + side) * bank.I + ub * 64 + rr] = hv[k];
                 asm volatile("bar.sync 2, 128;" ::: "memory");
             } else {
 _Pragma("unroll")
@@ -540,7 +634,7 @@ _Pragma("unroll")
                     if (n < npt) {
                         const int ex = __shfl_sync(0xffffffffu, ex_l, n);
                         const int dst = __shfl_sync(0xffffffffu, dst_l, n);
-                        p.contrib[(size_t)dst * bank.L + ub * 128 + r] = ldexpf(acc[n], ex);
+                        p.contrib[(size_t)dst * bank.L + ub * 128 + r] = __fmul_rn(acc[n], pow2f(ex));
                     }
                 }
             }
@@ -584,7 +678,7 @@ __global__ void __launch_bounds__(256) tc_pack_pairs_kernel(__half *__restrict__
     if (m > 0.f && m <= 3.4e38f) e = max(-126, min(127, ilogbf(m) - 14));
     int any = 0;
     for (int i = threadIdx.x; i < K; i += 256) {
-        const float y = ldexpf(xr[i], -e);
+        const float y = __fmul_rn(xr[i], pow2f(-e));
         const __half h = __float2half_rn(y);
         const __half l = __float2half_rn(y - __half2float(h));
         hi[(size_t)q * K + i] = h;

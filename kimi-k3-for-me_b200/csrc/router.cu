@@ -12,9 +12,11 @@
 // FMAs at B = 2 if every lane read its own. So the A tokens of a thread are WARP-UNIFORM
 // (every lane of a warp reads the same x doubles: broadcast loads) and only the B experts
 // differ by lane; 4 warps of a CTA take 4 token groups against the same 32 B experts. K
-// tiles of 32 columns arrive by cp.async three tiles ahead, as floats in [row][36] rows
-// (conflict-free float4 reads), and are widened once per CTA into a [k][row] double tile;
-// one barrier per tile. The tile shape per call comes from a small cost model over the SM
+// tiles of 32 columns arrive by cp.async as floats in [row][36] rows (conflict-free float4
+// reads), as many tiles ahead as a 110 KB budget holds (two CTAs per SM): small shapes stream
+// W with few CTAs, so their bytes in flight per CTA must cover the DRAM latency by
+// themselves. Each tile is widened once per CTA into a [k][row] double tile; one barrier per
+// tile. The tile shape per call comes from a small cost model over the SM
 // count (FP64 issue per scheduler against shared-memory wavefronts per SM).
 //
 // Selection: one warp per token, repeated max with the first-index tie rule, taken
@@ -33,8 +35,8 @@ namespace k3 {
 
 constexpr int RB_K = 32;          // hidden columns per tile
 constexpr int RB_FLD = RB_K + 4;  // float stage row stride (16-byte rows on distinct banks)
-constexpr int RB_NS = 4;          // cp.async stages: tiles kt+1..kt+3 in flight
 constexpr int RB_THREADS = 128;   // 4 warps, one token group each
+constexpr int RB_BUDGET = 110 * 1024;   // shared memory per CTA
 
 // CTA tile of the scores kernel: A tokens per warp (A even), B experts per lane.
 template <int A, int B>
@@ -44,7 +46,10 @@ struct RbTile {
     static constexpr int ROWS = TT + TE;                    // rows of a tile
     static constexpr int PIECES = ROWS * RB_K / 4;          // float4 pieces per tile
     static constexpr int FSTAGE = ROWS * RB_FLD;            // floats per stage
-    static constexpr int SMEM = RB_NS * FSTAGE * 4 + 2 * RB_K * ROWS * 8;
+    static constexpr int DTILE = 2 * RB_K * ROWS * 8;       // the two double tiles
+    static constexpr int NS_FIT = (RB_BUDGET - DTILE) / (FSTAGE * 4);
+    static constexpr int NS = NS_FIT < 3 ? 3 : (NS_FIT > 16 ? 16 : NS_FIT);   // cp.async stages
+    static constexpr int SMEM = NS * FSTAGE * 4 + DTILE;
     static_assert(A % 2 == 0 && (B == 1 || B == 2), "tile shape");
 };
 
@@ -69,7 +74,7 @@ __global__ void __launch_bounds__(RB_THREADS) router_scores_kernel(float *__rest
     using Tl = RbTile<A, B>;
     extern __shared__ __align__(16) unsigned char rsm[];
     float *fst = reinterpret_cast<float *>(rsm);                              // [NS][ROWS][FLD]
-    double *dt = reinterpret_cast<double *>(rsm + RB_NS * Tl::FSTAGE * 4);    // [2][K][ROWS]
+    double *dt = reinterpret_cast<double *>(rsm + Tl::NS * Tl::FSTAGE * 4);    // [2][K][ROWS]
     const int t0 = blockIdx.y * Tl::TT, e0 = blockIdx.x * Tl::TE;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int trow = warp * A;                 // this warp's first token row in the tile
@@ -79,7 +84,7 @@ __global__ void __launch_bounds__(RB_THREADS) router_scores_kernel(float *__rest
     // tile kt's floats into stage kt % NS (an empty group past the end keeps the count)
     auto issue = [&](int kt) {
         if (kt < nt) {
-            float *f = fst + (kt % RB_NS) * Tl::FSTAGE;
+            float *f = fst + (kt % Tl::NS) * Tl::FSTAGE;
             const int k0 = kt * RB_K;
             for (int i = tid; i < Tl::ROWS * (RB_K / V); i += RB_THREADS) {
                 const int r = i / (RB_K / V), c = (i % (RB_K / V)) * V;
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(RB_THREADS) router_scores_kernel(float *__rest
     };
     // tile kt's floats widened into double buffer kt & 1, [k][row]
     auto widen = [&](int kt) {
-        const float *f = fst + (kt % RB_NS) * Tl::FSTAGE;
+        const float *f = fst + (kt % Tl::NS) * Tl::FSTAGE;
         double *d = dt + (kt & 1) * RB_K * Tl::ROWS;
         for (int p = tid; p < Tl::PIECES; p += RB_THREADS) {
             const int r = p % Tl::ROWS, c = 4 * (p / Tl::ROWS);
@@ -134,15 +139,15 @@ __global__ void __launch_bounds__(RB_THREADS) router_scores_kernel(float *__rest
             for (int b = 0; b < B; b++) acc[a][b] = __fma_rn(wv[b], xv[a], acc[a][b]);
     };
 
-    for (int kt = 0; kt < RB_NS - 1; kt++) issue(kt);
-    asm volatile("cp.async.wait_group %0;" ::"n"(RB_NS - 2) : "memory");
+    for (int kt = 0; kt < Tl::NS - 1; kt++) issue(kt);
+    asm volatile("cp.async.wait_group %0;" ::"n"(Tl::NS - 2) : "memory");
     __syncthreads();                           // tile 0 landed for every thread's copies
     widen(0);
     for (int kt = 0; kt < nt; kt++) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(RB_NS - 3) : "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(Tl::NS - 3) : "memory");
         // tile kt+1 landed; widen(kt) done and compute(kt-1) finished in every warp
         __syncthreads();
-        issue(kt + RB_NS - 1);                 // into the stage tile kt-1 used
+        issue(kt + Tl::NS - 1);                 // into the stage tile kt-1 used
         if (kt + 1 < nt) widen(kt + 1);        // into the buffer compute(kt-1) read
         const double *d = dt + (kt & 1) * RB_K * Tl::ROWS;
         const int kn = min(RB_K, hidden - kt * RB_K);
