@@ -1,21 +1,28 @@
 #!/usr/bin/env python3
-"""Benchmark: one K3-shaped MoE layer in verify mode (benchmark configuration 2).
+"""Benchmark: speculative verification on the K3-shaped 8-layer slice (benchmark config 4).
 
-A step is one verify pass of the layer over B*(1+k) tokens -- B sequences, each feeding
-its pending token plus k drafts -- through the library's C ABI: the sigmoid router with
-bias-steered top-8 over 384 experts, the grouped MXFP4 expert FFN (d_model 7168, FFN
-2048, SwiGLU) with the shared expert, and the top-k-ordered combine. Weights are
-N(0, 0.02) quantised to packed E2M1 + E8M0/32 (the reference's quantisation rule),
-activations bf16 N(0, 1), router bias N(0, 0.01); all synthetic and seeded.
+A step is one verify sweep of B = 16 sequences, each scoring a 64-node draft tree
+(branching 4, depth 4) against a 32,768-position MLA cache, through the library's C ABI:
+embed -> 6 KDA + 2 MLA decoder layers (each with a 384-expert top-8 + shared MXFP4 MoE,
+d_model 7168, FFN 2048 SwiGLU) -> final norm -> lm_head (vocab 163,840) -> per-node argmax
+-> the greedy tree walk on the device -> the commit (KDA log replay along the accepted
+path, MLA rows gathered, cached advanced). Weights, cache and drafts are synthetic and
+seeded; each tree's most probable branch carries the model's own greedy continuation, so
+every step accepts its 4 drafts plus the bonus id (the reference's GATE 4 forcing).
 
-value  verified tokens/s with inputs resident in HBM (device-timed, CUDA events)
-e2e    the same through the public call with host buffers: pinned host x -> device,
-       the layer, device -> host of the layer output and routing
-N > 1  expert parallel: 384 experts sharded 384/N per GPU, each rank verifies its own
-       B*(1+k) tokens (weak scaling), NCCL all-to-all dispatch and combine.
+value  accepted ids per second over all sequences (device-timed, CUDA events)
+e2e    the same through the public calls with the draft ids copied from pinned host memory
+       and the accepted ids read back inside the timed region
+rows   config 2 (one MoE layer at every M = B(1+k)), config 3 (KDA verify / commit, the
+       chunked prefill), the MLA attention, trunk matmuls, lm_head, router and accept,
+       each with its roofline fraction and, where the reference has the kernel, its CPU
+       baseline; integer outputs carry FNV-1a fingerprints
+N > 1  expert parallel: every layer's 384 routed experts split 384/N per GPU, token rows
+       exchanged through peer memory inside the model's MoE steps; each rank verifies its
+       own 16 sequences (weak scaling); the max over ranks of the device time.
 
---impl reference times the reference engine's own C kernels (k3_router, k3_matmul_mxfp4,
-compiled from its sources into oracle/_ref) on the host cores, same workload.
+--impl reference times the reference engine's own C kernels (compiled from its sources
+into oracle/_ref) on the host cores for the same slice, one sequence's chain at a time.
 """
 from __future__ import annotations
 
@@ -452,6 +459,7 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
     ph_steps, moe_ph = [], []
     k3.moe_phase_timing(True)
     idx_last = None
+    emitted = []          # every sequence's emitted ids, step by step (the stream's fingerprint)
     for s in range(warm):
         ev[0].record(stream)
         _, lg = model.verify(tok_dev[s], parent=parent)
@@ -459,6 +467,8 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
         emit, n_emit, path, _ = k3.accept_tree_greedy(lg, tok_dev[s], parent_dev)
         keep = n_emit.tolist()
         ph_path = path.tolist()
+        emit_np = emit.cpu().numpy()
+        emitted += [emit_np[b, :keep[b]] for b in range(B)]
         ev[2].record(stream)
         moe_ph.append(k3.moe_phase_ms())
         idx_last = model.last_routing(C4_TREE).clone()
@@ -520,6 +530,8 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
                      "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(gateup_bytes),
                      "units": f"{u} experts x {w13} B + rows" + (" (rank 0's; min over ranks)" if dist else "")},
         "gpu_launches": int(launches), "device_status": status, "clocks": clk, "build_s": round(build_s, 1),
+        "fnv_accepted_ids": {"hash": fnv1a64(np.concatenate(emitted).astype(np.int32)),
+                             "over": f"{warm} untimed steps x {B} sequences of rank {rank}: emitted ids, int32"},
         "ep": None if not dist else {"transport": "peer memory inside the model's MoE steps (k3gpu_moe_layer_ep)",
                                      "experts_per_gpu": n_exp // world, "owners_ok": bool(owners_ok >= 1),
                                      "parity": parity},
@@ -720,6 +732,18 @@ def matmul_bf16_cpu_baseline(T, n_in, n_out, rows=256, seed=6):
     dt = time.perf_counter() - t0
     return {"value": round(dt * 1e6 * n_out / rows, 1), "unit": "us per call", "cores": 1, "kind": "reference",
             "sample": f"{rows} of {n_out} output rows at T={T}, in={n_in}, scaled by rows; one thread"}
+
+
+def fnv1a64(a) -> str:
+    """FNV-1a (64-bit) over an array's bytes, the fingerprint the reference's benchmarks
+    print beside each output (benchmarks/bench_router.c:65-88): equal hashes mean
+    bit-identical outputs, so a GPU row and a CPU row over the same inputs compare at a
+    glance. Used on integer outputs (routing indices, accepted ids), which the path must
+    reproduce bit for bit."""
+    h = 0xcbf29ce484222325
+    for byte in np.ascontiguousarray(a).tobytes():
+        h = ((h ^ byte) * 0x100000001b3) & 0xFFFFFFFFFFFFFFFF
+    return f"{h:016x}"
 
 
 def host_threads():
@@ -1277,7 +1301,7 @@ def measure_c2(args, k3, dev, kb, bank, offs, stride, M, seed, n_unsafe, cpu_tok
                              "unique_experts": u},
            "phase_ms": {"router": round(ph[0], 4), "plan": round(ph[1], 4), "gateup": round(ph[2], 4),
                         "down": round(ph[3], 4), "combine": round(ph[4], 4)},
-           "gpu_launches_per_step": int(launches)}
+           "gpu_launches_per_step": int(launches), "fnv_routing": fnv1a64(idx_np)}
     if cpu_tokens > 0:
         Ts = min(M, cpu_tokens)
         bank_np = bank.cpu().numpy()
@@ -1293,6 +1317,7 @@ def measure_c2(args, k3, dev, kb, bank, offs, stride, M, seed, n_unsafe, cpu_tok
                 "sample": f"{Ts} of {M} tokens of the same step through the reference's k3_router + "
                           f"k3_matmul_mxfp4 expert loop ({dt:.2f} s)",
                 "routing_bitexact": bool(np.array_equal(ref_idx, idx_np[:Ts])),
+                "fnv_routing": fnv1a64(ref_idx.astype(np.int32)), "fnv_routing_gpu_same_tokens": fnv1a64(idx_np[:Ts]),
                 "out_rel_l2_vs_gpu": float(np.linalg.norm(got - ref_out) / max(np.linalg.norm(ref_out), 1e-30))}
     return row
 
@@ -1366,6 +1391,7 @@ def c4_line(args, c4, world, cpu, rows):
         "verify_step_ms": c4["verify_step_ms"], "accept_ms": c4["accept_ms"], "commit_ms": c4["commit_ms"],
         "accepted_per_step": c4["accepted_per_step"],
         "accepted_fraction_of_planted": c4["accepted_fraction_of_planted"],
+        "fnv_accepted_ids": c4["fnv_accepted_ids"],
         "moe_phase_ms_last_layer": c4["moe_phase_ms_last_layer"],
         "gpu_launches": c4["gpu_launches"], "device_status": c4["device_status"],
         "clocks": c4["clocks"], "cpu_baseline": cpu, "build_s": c4["build_s"], "ep": c4["ep"], "rows": rows,

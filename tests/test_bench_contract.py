@@ -93,3 +93,15 @@ def test_c4_tree_and_forced_drafts():
                     j = chain.index(parent[i]) + 1
                     if j < 5:
                         assert tok[s, q, i] != tok[s, q, chain[j]]
+
+
+def test_fnv1a64_known_answers():
+    """The output fingerprint is 64-bit FNV-1a over the bytes: the published test vectors of
+    the hash (offset basis for the empty input, 'a', 'foobar') and an int32 array's bytes."""
+    b = _bench()
+    assert b.fnv1a64(np.zeros(0, np.uint8)) == "cbf29ce484222325"
+    assert b.fnv1a64(np.frombuffer(b"a", np.uint8)) == "af63dc4c8601ec8c"
+    assert b.fnv1a64(np.frombuffer(b"foobar", np.uint8)) == "85944171f73967e8"
+    ids = np.array([1, 2, 3], np.int32)
+    assert b.fnv1a64(ids) == b.fnv1a64(np.frombuffer(ids.tobytes(), np.uint8))
+    assert b.fnv1a64(ids) != b.fnv1a64(ids[::-1])
