@@ -56,7 +56,7 @@ constexpr int TC_S_BYTES = 128 * 16;     // E8M0 bytes of a stage
 // TMA as soon as the decode warps have read them, and the activation tiles come in K halves
 // (NBH slots, their own producer warp) that each half's issuer frees: 96 KB of weights in
 // flight per SM instead of 64 KB, over a shorter lifetime.
-template <int NP_, int NMMA_, int NA_, int NS_, int TAB_, int NBH_ = 0> struct TcShape {
+template <int NP_, int NMMA_, int NA_, int NS_, int TAB_, int NBH_, int SUBS_> struct TcShape {
     static constexpr int NP = NP_;                      // tokens per pass
     static constexpr int N = 2 * NP;                    // MMA N: the pass's hi rows, then their lo rows
     static constexpr int NMMA = NMMA_;                  // issuers: NMMA / 2 per K half
@@ -65,11 +65,14 @@ template <int NP_, int NMMA_, int NA_, int NS_, int TAB_, int NBH_ = 0> struct T
     static constexpr int NS = NS_;                      // shared-memory stages (split: weight stages)
     static constexpr int NBH = NBH_;                    // split rings: activation half-stage slots
     static constexpr bool SPLIT = NBH_ > 0;
-    // split rings: a K half's A rows in two 64-column sub-buffers (128 K each), so the issuer
-    // runs one sub-buffer's MMAs while the decode warps fill the other, and the next item's
-    // decode starts as soon as the first is free: decode and MMA issue overlap instead of
-    // taking turns on one buffer per half
-    static constexpr int SUBS = SPLIT ? 2 : 1;          // A buffers per K half of a stage
+    // a K half's A rows in SUBS sub-buffers (two: 64 columns = 128 K each), so an issuer runs
+    // one sub-buffer's MMAs while the decode warps fill the other, and the next stage's decode
+    // starts as soon as the first is free: decode and MMA issue overlap instead of taking
+    // turns on one buffer per half. Each half owns its sub-buffers (NA = 2 SUBS): buffers
+    // that the halves took turns in let one half's decode warps run a rotation ahead of its
+    // own issuers and pass a parity wait meant for an earlier phase.
+    static constexpr int SUBS = SUBS_;                  // A buffers per K half of a stage
+    static constexpr int SUB_STEPS = 16 / SUBS;         // K16 steps per sub-buffer
     static constexpr int ACOLS = 128 / SUBS;
     static constexpr int TAB = TAB_;                    // active-expert entries kept in shared memory
     static constexpr int B_BYTES = (TC_KC / 64) * NP * 128;   // one activation piece of a stage
@@ -85,23 +88,38 @@ template <int NP_, int NMMA_, int NA_, int NS_, int TAB_, int NBH_ = 0> struct T
     static constexpr int PCOLS = NMMA * PW;             // one stage-partial set
     static constexpr int ACOL0 = 2 * PCOLS;             // first A column
     static constexpr int XCH_BYTES = 64 * NP * 4;       // gate/up exchange in the epilogue
-    // barriers: full[NS] empty[NS] (split: [bfull bempty][NBH]) aready[NA] afree[NA] pfree[2]
-    // (split: pfull[2], the issuers' stage partials final)
-    static constexpr int NBAR = 2 * NS + 2 * NBH + 2 * NA + 2 + (SPLIT ? 2 : 0);
-    // after the expert table: the E8M0 byte -> f16x2 scale pair table (256 entries)
-    static constexpr int SMEM = RINGS + XCH_BYTES + NBAR * 8 + 16 + TAB * 16 + 256 * 4;
+    // barriers: full[NS] empty[NS] (split: bfull[NBH][2] bempty[NBH]) aready[NA][2] afree[NA]
+    // pfree[2] (split: pfull[2], the issuers' stage partials final). The two K halves take
+    // turns in the A buffers (sparse: 3 buffers, 2 fills an item) and in the activation slots
+    // (split: 3 slots, 2 fills an item), so each buffer and slot has one full/ready barrier
+    // PER HALF: a half's issuer then sees only its own fills' phases, one after another. On
+    // a barrier both halves' fills completed, an issuer running an item ahead could test a
+    // parity whose phase still belonged to the other half's earlier fill and pass at once.
+    static constexpr int NBAR_RAW = 2 * NS + 3 * NBH + 3 * NA + 2 + (SPLIT ? 2 : 0);
+    static constexpr int NBAR = (NBAR_RAW + 1) & ~1;   // keeps the int4 table 16-byte aligned
+    // items between two uses of one A buffer (one activation slot) by the same half: its
+    // k-th use waits for phase parity (k / PERIOD) & 1 of that half's barrier
+    static constexpr int A_PERIOD = 1;                  // a half fills each of its buffers every stage
+    static constexpr int B_PERIOD = NBH > 0 ? NBH : 1;
+    // after the expert table: the E8M0 byte -> f16x2 scale pair table (256 entries), then
+    // the work items' prefix over the active experts (TAB + 1 ints)
+    static constexpr int SMEM = RINGS + XCH_BYTES + NBAR * 8 + 16 + TAB * 16 + 256 * 4 + (TAB + 1) * 4;
     // split: one more warp, the activation producer
     static constexpr int THREADS = (TC_MMA_WARP0 + NMMA + (SPLIT ? 1 : 0)) * 32;
     static_assert(ACOL0 + NA * ACOLS <= 512, "TMEM columns");
-    static_assert(MPI % SUBS == 0, "MMAs per sub-buffer");
     static_assert(STAGE % 1024 == 0 && WSTAGE % 1024 == 0 && BHALF % 1024 == 0, "stage alignment");
     static_assert((RINGS + XCH_BYTES + (NBAR + 2) * 8) % 16 == 0, "int4 expert table alignment");
     static_assert(SMEM <= 227 * 1024, "shared memory");
     static_assert(NMMA == 2 || NMMA == 4, "issuers per K half");
     static_assert(NP == 8 || NP % 16 == 0, "pass width");
+    static_assert(NA == 2 * SUBS, "A buffers: each K half owns SUBS of them");
+    static_assert(MPI % SUB_STEPS == 0 || SUB_STEPS % MPI == 0, "issuer steps against sub-buffers");
+    // issuers of one half that read each sub-buffer (its afree count)
+    static constexpr int SUB_READERS = MPI >= SUB_STEPS ? 1 : SUB_STEPS / MPI;
+    static_assert(NBH == 0 || NBH % 2 == 1, "activation slots: an odd rotation");
 };
-using TcSparse = TcShape<8, 4, 3, 4, 1024>;
-using TcDense = TcShape<32, 2, 4, 3, 512, 3>;
+using TcSparse = TcShape<8, 4, 4, 4, 512, 0, 2>;
+using TcDense = TcShape<32, 2, 4, 3, 512, 3, 2>;
 constexpr long long TC_SPIN = 1LL << 22;
 constexpr int TC_SUSPEND_NS = 1000;
 
@@ -252,8 +270,10 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
     int4 *tab = reinterpret_cast<int4 *>(bars + CF::NBAR + 2);   // [CF::TAB] {e, cnt, off, flags}
     uint32_t *stab = reinterpret_cast<uint32_t *>(tab + CF::TAB);   // [256] scale_h2 of each byte
     uint64_t *b_full = bars, *b_empty = bars + CF::NS;   // split: the weight ring
-    uint64_t *b_bfull = bars + 2 * CF::NS, *b_bempty = b_bfull + CF::NBH;   // split: the activation ring
-    uint64_t *b_aready = bars + 2 * CF::NS + 2 * CF::NBH, *b_afree = b_aready + CF::NA;
+    uint64_t *b_bfull = bars + 2 * CF::NS;                // split: the activation ring, [slot][half]
+    uint64_t *b_bempty = b_bfull + 2 * CF::NBH;           // [slot]
+    uint64_t *b_aready = b_bempty + CF::NBH;              // [A buffer][half]
+    uint64_t *b_afree = b_aready + 2 * CF::NA;            // [A buffer]
     uint64_t *b_pfree = b_afree + CF::NA;                 // partial buffers: epilogue -> MMA
     uint64_t *b_pfull = b_pfree + 2;                      // split: partial buffers: MMA -> epilogue
     // a stage's weights (and, in one ring, its activation tile) and a split activation slot
@@ -268,12 +288,14 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
             bar_init(s_addr(&b_empty[s]), TC_DEQ_WARPS + (CF::SPLIT ? 0 : CF::NMMA));
         }
         for (int b = 0; b < CF::NBH; b++) {
-            bar_init(s_addr(&b_bfull[b]), 1);
-            bar_init(s_addr(&b_bempty[b]), CF::NMMA / 2);       // commits of that K half's issuers
+            bar_init(s_addr(&b_bfull[2 * b]), 1);
+            bar_init(s_addr(&b_bfull[2 * b + 1]), 1);
+            bar_init(s_addr(&b_bempty[b]), CF::NMMA / 2);       // commits of the filling half's issuers
         }
         for (int a = 0; a < CF::NA; a++) {
-            bar_init(s_addr(&b_aready[a]), 4);                  // the four warps of that K half
-            bar_init(s_addr(&b_afree[a]), CF::NMMA / 2);        // commits of the half's issuers
+            bar_init(s_addr(&b_aready[2 * a]), 4);              // the four decode warps of K half 0
+            bar_init(s_addr(&b_aready[2 * a + 1]), 4);          // ... of K half 1
+            bar_init(s_addr(&b_afree[a]), CF::SUB_READERS);     // commits of the issuers that read it
         }
         for (int d = 0; d < 2; d++) {
             bar_init(s_addr(&b_pfree[d]), 4);                   // epilogue warps
@@ -292,6 +314,40 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
     }
     for (int b = tid; b < 256; b += CF::THREADS)   // only certified bytes are ever looked up
         stab[b] = (b == 255 || (b >= 104 && b <= 140)) ? scale_h2((uint32_t)b) : 0u;
+    // Work items: one per (expert, unit, pass of NP tokens), expert-major, so an expert with
+    // many tokens (the shared expert sees every token of the call) spreads its passes over
+    // as many CTAs as other experts' units instead of lengthening the CTAs that drew its
+    // units; a unit's passes are consecutive items, run side by side on neighbouring CTAs,
+    // so its weights come from HBM once and from L2 for the others. wpre[a] = the first item
+    // of active expert a (experts left to the mma.sync kernel have none). Past TAB active
+    // experts the items fall back to one per (expert, unit) with all its passes.
+    int *wpre = reinterpret_cast<int *>(stab + 256);
+    const bool by_pass = na <= CF::TAB;
+    if (by_pass && warp == 0) {
+        __syncwarp();
+        const int per = (na + 31) / 32, a0 = min(na, lane * per), a1 = min(na, a0 + per);
+        int sum = 0;
+        for (int a = a0; a < a1; a++) {
+            const int e = p.act[a];
+            const bool skip = ta.safe && !ta.safe[e];
+            sum += skip ? 0 : ta.UE * ((p.cnt[e] + CF::NP - 1) / CF::NP);
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int run = incl - sum;   // items before this lane's first expert
+        for (int a = a0; a < a1; a++) {
+            wpre[a] = run;
+            const int e = p.act[a];
+            const bool skip = ta.safe && !ta.safe[e];
+            run += skip ? 0 : ta.UE * ((p.cnt[e] + CF::NP - 1) / CF::NP);
+        }
+        if (lane == 31) wpre[na] = incl;
+        __syncwarp();   // warp 0 converged again before its tcgen05.alloc (a .sync.aligned op)
+    }
     if (warp == 0) {   // 512 TMEM columns: partial sets at 0 and 64, A buffers from 128
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s_addr(tmem_slot))
                      : "memory");
@@ -303,20 +359,44 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
     const uint32_t tmem = *tmem_slot;
 
     const int K = ta.K, NK = K / TC_KC, G = K / 32;
-    const int n_units = *p.n_active * ta.UE;
+    const int n_work = by_pass ? wpre[na] : na * ta.UE;
     const int *Xe = PHASE == 0 ? p.ze : p.he;
     bool failed = false;
+    // work item w -> active expert a, unit ub, passes [p0, p1)
+    auto work_of = [&](int w, int &a, int &ub, int &p0, int &p1) {
+        if (!by_pass) {
+            a = w / ta.UE;
+            ub = w % ta.UE;
+            p0 = 0;
+            p1 = 1 << 30;
+            return;
+        }
+        int lo = 0, hi = na - 1;   // the last a with wpre[a] <= w
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (wpre[mid] <= w) lo = mid;
+            else hi = mid - 1;
+        }
+        a = lo;
+        const int local = w - wpre[a], np = (wpre[a + 1] - wpre[a]) / ta.UE;
+        ub = local / np;
+        p0 = local % np;
+        p1 = p0 + 1;
+    };
 
-// the unit/pass/stage sequence every role walks identically
+// the work item/pass/stage sequence every role walks identically
 #define TC_FOR_UNITS(...)                                                                   \
     {                                                                                        \
-        int item = 0, unit_i = 0;                                                            \
-        for (int u = blockIdx.x; u < n_units && !failed; u += gridDim.x) {                  \
-            const int4 ent = unit_entry(u / ta.UE);                                          \
+        int item = 0;                                                                        \
+        for (int w = blockIdx.x; w < n_work && !failed; w += gridDim.x) {                   \
+            int a_, ub, p0_, p1_;                                                            \
+            work_of(w, a_, ub, p0_, p1_);                                                    \
+            const int4 ent = unit_entry(a_);                                                 \
             if (ent.w & 2) continue;                                                         \
-            const int e = ent.x, ub = u % ta.UE, nt = ent.y, q0 = ent.z;                      \
+            const int e = ent.x, nt = ent.y, q0 = ent.z;                                     \
             const bool lo_any = (ent.w & 1) != 0;                                            \
-            for (int tb = 0; tb < nt && !failed; tb += CF::NP, unit_i++) {                    \
+            const int tb_end = (int)min((long long)nt, (long long)p1_ * CF::NP);             \
+            for (int tb = p0_ * CF::NP; tb < tb_end && !failed; tb += CF::NP) {              \
                 const int npt = min(CF::NP, nt - tb);                                         \
                 __VA_ARGS__                                                                  \
             }                                                                                \
@@ -328,7 +408,6 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
         const int lo = p.elo[(PHASE == 0 ? 0 : bank.n_experts) + e];
         return make_int4(e, p.cnt[e], p.off[e], (lo ? 1 : 0) | ((ta.safe && !ta.safe[e]) ? 2 : 0));
     };
-    (void)na;
 
     if (warp == TC_TMA_WARP) {
         if (lane == 0) {
@@ -383,7 +462,7 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
                         const uint32_t par = (uint32_t)((fill / (CF::SPLIT ? CF::NBH : 1)) & 1);
                         if (!bar_wait(s_addr(&b_bempty[slot]), par ^ 1u)) { failed = true; break; }
                         unsigned char *sb = bslot(slot);
-                        const uint32_t full = s_addr(&b_bfull[slot]);
+                        const uint32_t full = s_addr(&b_bfull[2 * slot + h]);
                         bar_expect(full, (uint32_t)(4 * CF::NP * 128 * (lo_any ? 2 : 1)));
                         for (int a = 0; a < 4; a++) {
                             const int x = kc * TC_KC + h * 256 + a * 64;
@@ -406,14 +485,14 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
             const int mi = warp - TC_MMA_WARP0, h = mi / PER_HALF, j = mi % PER_HALF;
             const uint32_t idesc = f16_idesc(CF::N);
             using TM = CF;
-            // this issuer's MPI B offsets, in 16-byte descriptor units: the descriptor of a
-            // stage's tile is built once and advanced by these (the 14-bit start field does
-            // not carry: shared addresses stay below 256 KB)
-            uint32_t boff16[CF::MPI];
+            // the B offsets of the half's 16 K16 steps, in 16-byte descriptor units: the
+            // descriptor of a stage's tile is built once and advanced by these (the 14-bit
+            // start field does not carry: shared addresses stay below 256 KB)
+            uint32_t boffh[16];
 _Pragma("unroll")
-            for (int t = 0; t < CF::MPI; t++) {
-                const int kk = (CF::SPLIT ? 0 : h * 256) + (j * CF::MPI + t) * 16;   // split: K inside the half
-                boff16[t] = (uint32_t)(((kk >> 6) * CF::ATOM + (kk & 63) * 2) >> 4);
+            for (int sx = 0; sx < 16; sx++) {
+                const int kk = (CF::SPLIT ? 0 : h * 256) + sx * 16;   // split: K inside the half
+                boffh[sx] = (uint32_t)(((kk >> 6) * CF::ATOM + (kk & 63) * 2) >> 4);
             }
             TC_FOR_UNITS({
                 for (int kc = 0; kc < NK && !failed; kc++, item++) {
@@ -423,10 +502,10 @@ _Pragma("unroll")
                     const int hfill = 2 * item + h;   // this half's place in the activation ring
                     // split: this half's activation slot
                     const int bslot_i = hfill % (CF::SPLIT ? CF::NBH : 1);
-                    const uint32_t bpar = (uint32_t)((hfill / (CF::SPLIT ? CF::NBH : 1)) & 1);
+                    const uint32_t bpar = (uint32_t)((item / CF::B_PERIOD) & 1);   // this half's uses of the slot
                     if (!bar_wait(s_addr(&b_pfree[pb]), (uint32_t)(((item >> 1) & 1) ^ 1))) { failed = true; break; }
                     if (CF::SPLIT) {
-                        if (!bar_wait(s_addr(&b_bfull[bslot_i]), bpar)) { failed = true; break; }
+                        if (!bar_wait(s_addr(&b_bfull[2 * bslot_i + h]), bpar)) { failed = true; break; }
                     } else {
                         if (!bar_wait(s_addr(&b_full[st]), par)) { failed = true; break; }
                     }
@@ -434,19 +513,27 @@ _Pragma("unroll")
                     const uint32_t bh = CF::SPLIT ? s_addr(bslot(bslot_i))
                                                   : s_addr(wstage(st) + TC_W_BYTES + 1024 * ((TC_S_BYTES + 1023) / 1024));
                     const uint64_t dh = sw128_desc(bh);
-                    constexpr int PS = CF::MPI / CF::SUBS;   // MMAs per sub-buffer
+                    // this issuer's K16 steps j*MPI .. (j+1)*MPI-1 of the half, sub-buffer by
+                    // sub-buffer (dense: one issuer reads both of its half's sub-buffers;
+                    // sparse: issuer j reads sub-buffer j)
+                    constexpr int SS = CF::SUB_STEPS;
+                    const int s_lo = j * CF::MPI, s_hi = s_lo + CF::MPI;
 _Pragma("unroll")
                     for (int sb = 0; sb < CF::SUBS; sb++) {
+                        if ((sb + 1) * SS <= s_lo || sb * SS >= s_hi) continue;   // not this issuer's
                         const int fill = hfill * CF::SUBS + sb;   // the A buffer the decode warps filled
                         const int ab = fill % TM::NA;
-                        const uint32_t apar = (uint32_t)((fill / TM::NA) & 1);
-                        if (!bar_wait(s_addr(&b_aready[ab]), apar)) { failed = true; break; }
+                        const uint32_t apar = (uint32_t)((item / TM::A_PERIOD) & 1);   // this half's uses of ab
+                        if (!bar_wait(s_addr(&b_aready[2 * ab + h]), apar)) { failed = true; break; }
                         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * TM::ACOLS + (CF::SUBS == 1 ? j * CF::MPI * 8 : 0));
+                        const uint32_t atm = tmem + (uint32_t)(TM::ACOL0 + ab * TM::ACOLS);
                         // the atom's hi and lo rows as one N = 2 NP operand
 _Pragma("unroll")
-                        for (int t = sb * PS; t < (sb + 1) * PS; t++)   // K16 steps of this issuer
-                            mma_ts(dtm, atm + (uint32_t)((t - sb * PS) * 8), dh + boff16[t], idesc, t ? 1u : 0u);
+                        for (int st16 = 0; st16 < SS; st16++) {   // K16 steps of this sub-buffer
+                            const int sx = sb * SS + st16;
+                            if (sx < s_lo || sx >= s_hi) continue;
+                            mma_ts(dtm, atm + (uint32_t)(st16 * 8), dh + boffh[sx], idesc, sx != s_lo ? 1u : 0u);
+                        }
                         mma_commit(s_addr(&b_afree[ab]));
                     }
                     if (failed) break;
@@ -517,7 +604,7 @@ _Pragma("unroll")
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     __syncwarp();
-                    if (lane == 0) bar_arrive(s_addr(&b_aready[ab]));
+                    if (lane == 0) bar_arrive(s_addr(&b_aready[2 * ab + h]));
                 }
                 if (failed) break;
                 if (lane == 0) bar_arrive(s_addr(&b_empty[st]));
