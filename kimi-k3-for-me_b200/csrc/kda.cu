@@ -10,6 +10,8 @@
 // The carried state is only read during verify; commit replays the logged operands.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace k3 {
@@ -114,11 +116,23 @@ __global__ void __launch_bounds__(D) kda_commit_kernel(float *__restrict__ state
     for (int i = 0; i < D; i++) Sh[(size_t)i * D + j] = Sc[i];
 }
 
-// grid (H, B), block D: node t of a draft tree (parent[0] = -1, parent[t] < t) reads the
-// state after its own ancestors. Per node the chain of k3_kda_step over root .. t runs again
-// from the carried state (verify trees are shallow), with the same float operations in the
-// same order as the chain kernel, so every node's output is bit-identical to a chain verify
-// of its ancestor path. parent is a device array [T] shared by the B sequences.
+// grid (H, B), block D: node t of a draft tree (parent[0] = -1, parent[t] < t; a parent of
+// -1 means the carried state) reads the state after its own ancestors, with the same float
+// operations in the same order as the chain kernel, so every node's output is bit-identical
+// to a chain verify of its ancestor path. parent is a device array [T] shared by the B
+// sequences.
+//
+// Most nodes of a draft tree are leaves, and a leaf's output needs its parent's state, not
+// its own: o = (decay(S) + k (beta (v - u))^T)^T q is two passes over the parent's column
+// (u first, then o, the updated entries recomputed on the fly and never stored). So only
+// the INTERNAL nodes step the register-held column forward, visited in depth-first preorder
+// (a child of the node just stepped costs one step; any other internal node re-runs its
+// path from the carried state), and after each one its leaf children are evaluated from
+// its state, KT_LEAVES at a time side by side (independent chains in one thread). A
+// 64-node tree of branching 4 and depth 4 then costs ~20 steps and 12 leaf passes instead
+// of one chain of depth + 1 steps per node.
+constexpr int KT_LEAVES_MAX = 4;
+
 template <int D>
 __global__ void __launch_bounds__(D) kda_verify_tree_kernel(float *__restrict__ o,
                                                            const float *__restrict__ state,
@@ -130,41 +144,97 @@ __global__ void __launch_bounds__(D) kda_verify_tree_kernel(float *__restrict__ 
                                                            const int *__restrict__ parent, int T,
                                                            int H, float qscale)
 {
-    __shared__ float sm[3 * D];
-    __shared__ int path[64];
-    __shared__ int plen;
+    constexpr int KT_LEAVES = KT_LEAVES_MAX;
+    extern __shared__ float Ss[];                       // [D][D]: a parked state column per thread
+    __shared__ float sm[3 * D];                         // one stepped node: k, q * qscale, alpha
+    __shared__ __align__(16) float lk[KT_LEAVES][D], la[KT_LEAVES][D], lq[KT_LEAVES][D];
+    __shared__ int par[64], nch[64];
+    __shared__ int items[66], n_items;                  // internal nodes in preorder (-1: the carried state)
+    __shared__ int leaf[64], leaf0[66];                 // leaves grouped by item
+    __shared__ int path[64], plen;
     const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
     const float *Sh = state + (((size_t)b * H + h) * D) * D;
     const size_t rb = (size_t)b * T * H * D;
     const float *qb = q + rb, *kb = k + rb, *vb = v + rb, *ab = al + rb;
     const float *bb = beta + (size_t)b * T * H;
     float *sk = sm, *sq = sm + D, *sa = sm + 2 * D;
-    for (int t = 0; t < T; t++) {
-        __syncthreads();
-        if (j == 0) {   // t, its parent, ..., the root
-            int n = 0, a = t;
-            while (a >= 0 && n < 64) {
-                path[n++] = a;
-                const int pa = parent[a];
-                if (pa >= a || pa < -1) {
-                    flag(DEV_BAD_INDEX);
-                    break;
-                }
-                a = pa;
+
+    if (j == 0) {
+        // parents checked once (a bad one is flagged and read as the carried state)
+        for (int t = 0; t < T; t++) {
+            int pa = parent[t];
+            if (pa >= t || pa < -1) {
+                flag(DEV_BAD_INDEX);
+                pa = -1;
             }
-            plen = n;
+            par[t] = pa;
+            nch[t] = 0;
+        }
+        for (int t = 0; t < T; t++)
+            if (par[t] >= 0) nch[par[t]]++;
+        // depth-first preorder over the nodes, children in ascending order (an explicit
+        // stack: every node is pushed once); internal nodes become items, each followed by
+        // its leaf children. The carried state is item 0 when some root is a leaf.
+        int stack[64], sp = 0, ni = 0, nl = 0;
+        bool root_leaf = false;
+        for (int t = 0; t < T; t++) root_leaf |= par[t] < 0 && nch[t] == 0;
+        if (root_leaf) {
+            items[ni] = -1;
+            leaf0[ni++] = nl;
+            for (int t = 0; t < T; t++)
+                if (par[t] < 0 && nch[t] == 0) leaf[nl++] = t;
+        }
+        for (int t = T - 1; t >= 0; t--)
+            if (par[t] < 0 && nch[t] > 0) stack[sp++] = t;
+        while (sp > 0) {
+            const int n = stack[--sp];
+            items[ni] = n;
+            leaf0[ni++] = nl;
+            for (int c = n + 1; c < T; c++)
+                if (par[c] == n && nch[c] == 0) leaf[nl++] = c;
+            for (int c = T - 1; c > n; c--)
+                if (par[c] == n && nch[c] > 0) stack[sp++] = c;
+        }
+        leaf0[ni] = nl;
+        n_items = ni;
+    }
+    __syncthreads();
+
+    float Sc[D];
+    int cur = -2;   // the node whose state Sc holds (-1: the carried state, -2: none yet)
+    const int ni = n_items;
+    for (int it = 0; it < ni; it++) {
+        const int n = items[it];
+        // the nodes to step, root-most first: n alone when Sc holds its parent's state, else
+        // n's whole path from the carried state (its ancestors were emitted when visited)
+        const bool reload = n < 0 || par[n] != cur;
+        __syncthreads();
+        if (j == 0) {
+            int len = 0;
+            if (n >= 0 && !reload) path[len++] = n;
+            else
+                for (int a = n; a >= 0 && len < 64; a = par[a]) path[len++] = a;
+            for (int x = 0; x < len / 2; x++) {   // root-most first
+                const int tmp = path[x];
+                path[x] = path[len - 1 - x];
+                path[len - 1 - x] = tmp;
+            }
+            plen = len;
         }
         __syncthreads();
-        float Sc[D];
+        if (reload) {
 #pragma unroll
-        for (int i = 0; i < D; i++) Sc[i] = Sh[(size_t)i * D + j];
-        for (int pi = plen - 1; pi >= 0; pi--) {
+            for (int i = 0; i < D; i++) Sc[i] = Sh[(size_t)i * D + j];
+        }
+        const int pl = plen;
+        for (int pi = 0; pi < pl; pi++) {   // one k3_kda_step per node; the last one emits
             const int node = path[pi];
+            const bool emit = pi == pl - 1;
             const size_t off = ((size_t)node * H + h) * D;
             __syncthreads();
             sk[j] = kb[off + j];
             sa[j] = ab[off + j];
-            if (pi == 0) sq[j] = __fmul_rn(qb[off + j], qscale);
+            if (emit) sq[j] = __fmul_rn(qb[off + j], qscale);
             __syncthreads();
             const float bt = bb[(size_t)node * H + h];
 #pragma unroll
@@ -181,7 +251,7 @@ __global__ void __launch_bounds__(D) kda_verify_tree_kernel(float *__restrict__ 
                 const float ki = sk[i];
                 if (ki != 0.0f) Sc[i] = __fadd_rn(Sc[i], __fmul_rn(__fmul_rn(ki, bt), err));
             }
-            if (pi == 0) {
+            if (emit) {
                 float acc = 0.0f;
 #pragma unroll
                 for (int i = 0; i < D; i++) {
@@ -191,6 +261,89 @@ __global__ void __launch_bounds__(D) kda_verify_tree_kernel(float *__restrict__ 
                 o[rb + off + j] = acc;
             }
         }
+        cur = n;
+        if (leaf0[it] == leaf0[it + 1]) continue;
+        // this item's leaf children, KT_LEAVES side by side. The column is parked in shared
+        // memory ([i][j]: conflict-free) for the leaf passes, which then hold no 128-entry
+        // register array, and taken back afterwards (the barriers between make the reload
+        // real, so Sc is dead while the leaves run)
+#pragma unroll
+        for (int i = 0; i < D; i++) Ss[i * D + j] = Sc[i];
+        for (int l0 = leaf0[it]; l0 < leaf0[it + 1]; l0 += KT_LEAVES) {
+            const int nl = min(KT_LEAVES, leaf0[it + 1] - l0);
+            __syncthreads();
+#pragma unroll
+            for (int c = 0; c < KT_LEAVES; c++) {
+                if (c < nl) {
+                    const size_t off = ((size_t)leaf[l0 + c] * H + h) * D;
+                    lk[c][j] = kb[off + j];
+                    la[c][j] = ab[off + j];
+                    lq[c][j] = __fmul_rn(qb[off + j], qscale);
+                } else {   // an absent leaf: zero k and q rows (no update, no output)
+                    lk[c][j] = 0.0f;
+                    la[c][j] = 1.0f;
+                    lq[c][j] = 0.0f;
+                }
+            }
+            __syncthreads();
+            float u[KT_LEAVES], bt[KT_LEAVES], vj[KT_LEAVES];
+#pragma unroll
+            for (int c = 0; c < KT_LEAVES; c++) {
+                const int node = c < nl ? leaf[l0 + c] : 0;
+                u[c] = 0.0f;
+                bt[c] = c < nl ? bb[(size_t)node * H + h] : 0.0f;
+                vj[c] = c < nl ? vb[((size_t)node * H + h) * D + j] : 0.0f;
+            }
+            // u = (decayed S)^T k, the decayed entries recomputed; four rows at a time, the
+            // leaves' k and alpha as float4 broadcasts
+#pragma unroll 2
+            for (int i0 = 0; i0 < D; i0 += 4) {
+                float sv[4];
+#pragma unroll
+                for (int r = 0; r < 4; r++) sv[r] = Ss[(i0 + r) * D + j];
+#pragma unroll
+                for (int c = 0; c < KT_LEAVES; c++) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(&lk[c][i0]);
+                    const float4 a4 = *reinterpret_cast<const float4 *>(&la[c][i0]);
+                    const float kv[4] = {k4.x, k4.y, k4.z, k4.w}, av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                    for (int r = 0; r < 4; r++)
+                        if (kv[r] != 0.0f) u[c] = __fadd_rn(u[c], __fmul_rn(kv[r], __fmul_rn(sv[r], av[r])));
+                }
+            }
+            float err[KT_LEAVES], acc[KT_LEAVES];
+#pragma unroll
+            for (int c = 0; c < KT_LEAVES; c++) {
+                err[c] = __fsub_rn(vj[c], u[c]);
+                acc[c] = 0.0f;
+            }
+            // o = (updated S)^T q, each updated entry formed as the chain forms it
+#pragma unroll 2
+            for (int i0 = 0; i0 < D; i0 += 4) {
+                float sv[4];
+#pragma unroll
+                for (int r = 0; r < 4; r++) sv[r] = Ss[(i0 + r) * D + j];
+#pragma unroll
+                for (int c = 0; c < KT_LEAVES; c++) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(&lk[c][i0]);
+                    const float4 a4 = *reinterpret_cast<const float4 *>(&la[c][i0]);
+                    const float4 q4 = *reinterpret_cast<const float4 *>(&lq[c][i0]);
+                    const float kv[4] = {k4.x, k4.y, k4.z, k4.w}, av[4] = {a4.x, a4.y, a4.z, a4.w};
+                    const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                    for (int r = 0; r < 4; r++) {
+                        float sx = __fmul_rn(sv[r], av[r]);
+                        if (kv[r] != 0.0f) sx = __fadd_rn(sx, __fmul_rn(__fmul_rn(kv[r], bt[c]), err[c]));
+                        if (qv[r] != 0.0f) acc[c] = __fadd_rn(acc[c], __fmul_rn(qv[r], sx));
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < KT_LEAVES; c++)
+                if (c < nl) o[rb + ((size_t)leaf[l0 + c] * H + h) * D + j] = acc[c];
+        }
+#pragma unroll
+        for (int i = 0; i < D; i++) Sc[i] = Ss[i * D + j];
     }
 }
 
@@ -366,7 +519,28 @@ extern "C" int k3gpu_kda_verify_tree(float *o, const float *state, const float *
         return K3GPU_EINVAL;
     cudaStream_t s = k3::as_stream(stream);
     dim3 grid(H, B);
-    K3_KDA_DISPATCH(D, kda_verify_tree_kernel, o, state, q, k, v, alpha, beta, parent, T, H, qscale);
+    const size_t smem = (size_t)D * D * sizeof(float);   // the parked state columns
+    if (D == 128) {   // 64 KB: above the default dynamic shared-memory limit, opted in once per device
+        static std::mutex mu;
+        static bool done[64] = {};
+        int dev = 0;
+        int st = k3::cuda_status(cudaGetDevice(&dev));
+        if (st) return st;
+        if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
+        std::lock_guard<std::mutex> lock(mu);
+        if (!done[dev]) {
+            st = k3::cuda_status(cudaFuncSetAttribute(k3::kda_verify_tree_kernel<128>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            if (st) return st;
+            done[dev] = true;
+        }
+    }
+    switch (D) {
+    case 16: k3::kda_verify_tree_kernel<16><<<grid, 16, smem, s>>>(o, state, q, k, v, alpha, beta, parent, T, H, qscale); break;
+    case 32: k3::kda_verify_tree_kernel<32><<<grid, 32, smem, s>>>(o, state, q, k, v, alpha, beta, parent, T, H, qscale); break;
+    case 64: k3::kda_verify_tree_kernel<64><<<grid, 64, smem, s>>>(o, state, q, k, v, alpha, beta, parent, T, H, qscale); break;
+    default: k3::kda_verify_tree_kernel<128><<<grid, 128, smem, s>>>(o, state, q, k, v, alpha, beta, parent, T, H, qscale); break;
+    }
     return k3::launch_status();
 }
 

@@ -46,11 +46,39 @@ def path_of(parent, t):
     return p[::-1]
 
 
-@pytest.mark.parametrize("D,T", [(128, 17), (64, 40), (32, 64)])
-def test_kda_verify_tree_bitexact_on_every_path(k3, D, T):
+def best_first_tree(T=64, branch=4, depth=4):
+    """The benchmark's draft-tree shape: nodes grown best-first under a branching and depth
+    cap (most nodes are leaves, internal nodes at every depth)."""
+    parent, dep = [-1], [0]
+    frontier = [0]
+    while len(parent) < T and frontier:
+        p = frontier.pop(0)
+        for _ in range(branch):
+            if len(parent) >= T:
+                break
+            parent.append(p)
+            dep.append(dep[p] + 1)
+            if dep[-1] < depth:
+                frontier.append(len(parent) - 1)
+    return parent
+
+
+TREES = {
+    "random": None,
+    "best_first": lambda rng, T: best_first_tree(T),
+    "star": lambda rng, T: [-1] + [0] * (T - 1),
+    # several roots on the carried state, some of them leaves
+    "forest": lambda rng, T: [-1] + [(-1 if i % 5 == 0 else int(rng.integers(max(0, i - 3), i))) for i in range(1, T)],
+}
+
+
+@pytest.mark.parametrize("D,T,kind", [(128, 17, "random"), (64, 40, "random"), (32, 64, "random"),
+                                      (128, 64, "best_first"), (128, 33, "star"), (64, 45, "forest"),
+                                      (16, 64, "best_first")])
+def test_kda_verify_tree_bitexact_on_every_path(k3, D, T, kind):
     rng = np.random.default_rng(D + T)
     B, H = 2, 3
-    parent = random_tree(rng, T)
+    parent = random_tree(rng, T) if TREES[kind] is None else TREES[kind](rng, T)
     st = rng.standard_normal((B, H, D, D), dtype=np.float32) * np.float32(0.1)
     q = GI.bf16_round(GI.l2n(rng.standard_normal((B, T, H, D), dtype=np.float32)))
     k = GI.bf16_round(GI.l2n(rng.standard_normal((B, T, H, D), dtype=np.float32)))
@@ -58,6 +86,8 @@ def test_kda_verify_tree_bitexact_on_every_path(k3, D, T):
     al = rng.uniform(0.9, 0.999, (B, T, H, D)).astype(np.float32)
     be = (1.0 / (1.0 + np.exp(-rng.standard_normal((B, T, H))))).astype(np.float32)
     k[0, 2, 1, :5] = 0.0                       # zero rows are skipped as in the chain
+    k[1, T - 1, 2, 3:9] = 0.0                  # (a leaf's too)
+    q[1, T - 2, 0, :7] = 0.0
     qs = np.float32(1.0) / np.sqrt(np.float32(D))
     o = k3.kda_verify_tree(dev(st), dev(q), dev(k), dev(v), dev(al), dev(be),
                            dev(np.asarray(parent, np.int32)), qs).cpu().numpy()
