@@ -266,18 +266,32 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
 // lo != 0 (one plain store per block that saw one: every writer writes the same value)
 __global__ void __launch_bounds__(256) split_kernel(__nv_bfloat16 *__restrict__ xp, int *__restrict__ lo_flag,
                                                    const float *__restrict__ X, int ldx, int T, int Tpad,
-                                                   int in, int in_pad)
+                                                   int in, int in_pad, int vec)
 {
+    // eight columns a thread: two 16-byte loads (vec: X rows 16-byte aligned) and one
+    // 16-byte store per piece (in_pad is a multiple of 64, xp 16-byte aligned)
     const int t = blockIdx.y;
-    const int k = blockIdx.x * 256 + threadIdx.x;
+    const int k0 = (blockIdx.x * 256 + threadIdx.x) * 8;
     int nz = 0;
-    if (k < in_pad) {
-        const float x = (t < T && k < in) ? X[(size_t)t * ldx + k] : 0.0f;
-        const __nv_bfloat16 hi = __float2bfloat16_rn(x);
-        const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
-        xp[(size_t)t * in_pad + k] = hi;
-        xp[((size_t)Tpad + t) * in_pad + k] = lo;
-        nz = __bfloat16_as_ushort(lo) & 0x7FFF;
+    if (k0 < in_pad) {
+        float x[8];
+        const float *xr = X + (size_t)t * ldx + k0;
+        if (vec && t < T && k0 + 8 <= in) {
+            const float4 a = *reinterpret_cast<const float4 *>(xr), b = *reinterpret_cast<const float4 *>(xr + 4);
+            x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) x[i] = (t < T && k0 + i < in) ? xr[i] : 0.0f;
+        }
+        __align__(16) __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            hi[i] = __float2bfloat16_rn(x[i]);
+            lo[i] = __float2bfloat16_rn(__fsub_rn(x[i], __bfloat162float(hi[i])));
+            nz |= __bfloat16_as_ushort(lo[i]) & 0x7FFF;
+        }
+        *reinterpret_cast<uint4 *>(xp + (size_t)t * in_pad + k0) = *reinterpret_cast<const uint4 *>(hi);
+        *reinterpret_cast<uint4 *>(xp + ((size_t)Tpad + t) * in_pad + k0) = *reinterpret_cast<const uint4 *>(lo);
     }
     if (__syncthreads_or(nz) && threadIdx.x == 0) *lo_flag = 1;
 }
@@ -410,6 +424,7 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
     using namespace k3::mmw;
     if (!Y || !X || !W || !workspace || T <= 0 || in <= 0 || out <= 0) return K3GPU_EINVAL;
     if (in % 8 || ldy < out || ldx < in || (reinterpret_cast<uintptr_t>(W) & 15u)) return K3GPU_EINVAL;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return K3GPU_EINVAL;   // the pieces are stored 16 bytes at a time
     if (ws_bytes < k3gpu_matmul_bf16_workspace(T, in, out)) return K3GPU_ECAPACITY;
     cudaStream_t s = k3::as_stream(stream);
     int dev = 0, st = k3::cuda_status(cudaGetDevice(&dev));
@@ -441,8 +456,10 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
         // the flag sits in the last 256 bytes, past any partials this launch writes
         int *lo_flag = reinterpret_cast<int *>((reinterpret_cast<uintptr_t>(ws + ws_bytes - 256) + 15) & ~(uintptr_t)15);
         if ((st = k3::cuda_status(cudaMemsetAsync(lo_flag, 0, sizeof(int), s)))) return st;
-        split_kernel<<<dim3((p.in_pad + 255) / 256, p.Tpad), 256, 0, s>>>(xp, lo_flag, X + (size_t)t0 * ldx, ldx, Tc,
-                                                                          p.Tpad, in, p.in_pad);
+        const float *Xt = X + (size_t)t0 * ldx;
+        const int vec = (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(Xt) & 15u) == 0;
+        split_kernel<<<dim3((p.in_pad + 2047) / 2048, p.Tpad), 256, 0, s>>>(xp, lo_flag, Xt, ldx, Tc, p.Tpad, in,
+                                                                           p.in_pad, vec);
         if ((st = k3::launch_status())) return st;
         CUtensorMap xm;
         if ((st = bf16_map(&xm, xp, p.in_pad, 2LL * p.Tpad, p.Np))) return st;

@@ -171,6 +171,114 @@ __global__ void __launch_bounds__(RB_THREADS) router_scores_kernel(float *__rest
     }
 }
 
+// Small batches: one chain per thread. When the whole call fits one wave of CTAs (a verify
+// step of a few sequences: T <= ~72 at 384 experts), every CTA walks all hidden columns
+// whatever its tile shape, so the time is the per-column cost of one CTA's walk. This form
+// keeps that short: a CTA owns 24 experts x 8 tokens (192 chains), 128-column K tiles (a
+// quarter of the barriers of the 32-column tiles above) arrive by cp.async two tiles
+// ahead and are widened to double once in shared memory, and each thread runs its chain
+// from registers loaded eight columns ahead.
+constexpr int RW_E = 24;     // experts per CTA
+constexpr int RW_T = 8;      // tokens per CTA
+constexpr int RW_R = RW_E + RW_T;
+constexpr int RW_THREADS = RW_E * RW_T;
+constexpr int RW_K = 128;    // hidden columns per tile
+constexpr int RW_NS = 3;     // cp.async stages
+constexpr int RW_LD = RW_K + 2;   // double tile row stride: rows land on distinct banks
+constexpr int RW_F_TILE = RW_R * RW_K;
+constexpr int RW_SMEM = RW_NS * RW_F_TILE * 4 + 2 * RW_R * RW_LD * 8;
+
+// eight chain steps from registers: acc += w[i] * x[i], i = 0..7 in order
+__device__ __forceinline__ double chain8(double acc, const double2 (&w)[4], const double2 (&x)[4])
+{
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        asm volatile("fma.rn.f64 %0, %1, %2, %0;" : "+d"(acc) : "d"(w[i].x), "d"(x[i].x));
+        asm volatile("fma.rn.f64 %0, %1, %2, %0;" : "+d"(acc) : "d"(w[i].y), "d"(x[i].y));
+    }
+    return acc;
+}
+
+__device__ __forceinline__ void load8(double2 (&w)[4], double2 (&x)[4], const double *wr, const double *xr)
+{
+    const uint32_t ws = (uint32_t)__cvta_generic_to_shared(wr), xs = (uint32_t)__cvta_generic_to_shared(xr);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(w[i].x), "=d"(w[i].y) : "r"(ws + 16 * i));
+        asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(x[i].x), "=d"(x[i].y) : "r"(xs + 16 * i));
+    }
+}
+
+template <int V>   // V = 4 when hidden % 4 == 0 and x, W are 16-byte aligned, else 1
+__global__ void __launch_bounds__(RW_THREADS) router_scores_wave_kernel(float *__restrict__ score,
+                                                                        const float *__restrict__ x,
+                                                                        const float *__restrict__ W,
+                                                                        int T, int hidden, int n)
+{
+    extern __shared__ __align__(16) unsigned char rsm[];
+    float *fst = reinterpret_cast<float *>(rsm);                            // [NS][R][K]
+    double *dt = reinterpret_cast<double *>(rsm + RW_NS * RW_F_TILE * 4);   // [2][R][LD]
+    const int e0 = blockIdx.x * RW_E, t0 = blockIdx.y * RW_T;
+    const int tid = threadIdx.x;
+    const int tl = tid & 7;          // token of this thread's chain
+    const int el = tid >> 3;         // expert of this thread's chain
+    const int nt = (hidden + RW_K - 1) / RW_K;
+    constexpr int CPR = RW_K / V;    // copies per tile row
+
+    auto issue = [&](int kt) {
+        if (kt < nt) {
+            float *f = fst + (kt % RW_NS) * RW_F_TILE;
+            const int k0 = kt * RW_K;
+            for (int i = tid; i < RW_R * CPR; i += RW_THREADS) {
+                const int r = i / CPR, c = (i % CPR) * V;
+                const bool is_w = r < RW_E;
+                const int row = is_w ? e0 + r : t0 + (r - RW_E);
+                const bool ok = (is_w ? row < n : row < T) && k0 + c < hidden;
+                const float *src = is_w ? W : x;
+                if (ok) src += (size_t)row * hidden + k0 + c;
+                cp_async_f<V>(f + r * RW_K + c, src, ok);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int kt = 0; kt < RW_NS - 1; kt++) issue(kt);
+
+    double acc = 0.0;
+    for (int kt = 0; kt < nt; kt++) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(RW_NS - 2) : "memory");
+        __syncthreads();                       // tile kt landed for every thread's copies
+        issue(kt + RW_NS - 1);                 // into the stage tile kt-1 used
+        const float *f = fst + (kt % RW_NS) * RW_F_TILE;
+        double *d = dt + (kt & 1) * RW_R * RW_LD;
+        for (int i = tid; i < RW_F_TILE / 4; i += RW_THREADS) {   // widen once, 4 at a time
+            const float4 v = reinterpret_cast<const float4 *>(f)[i];
+            double *o = d + (i / (RW_K / 4)) * RW_LD + (i % (RW_K / 4)) * 4;
+            reinterpret_cast<double2 *>(o)[0] = make_double2(v.x, v.y);
+            reinterpret_cast<double2 *>(o)[1] = make_double2(v.z, v.w);
+        }
+        __syncthreads();
+        const double *wr = d + el * RW_LD;
+        const double *xr = d + (RW_E + tl) * RW_LD;
+        const int kn = min(RW_K, hidden - kt * RW_K);
+        if (kn == RW_K) {
+            double2 wa[4], xa[4], wb[4], xb[4];
+            load8(wa, xa, wr, xr);
+#pragma unroll
+            for (int c = 0; c < RW_K; c += 16) {
+                load8(wb, xb, wr + c + 8, xr + c + 8);
+                acc = chain8(acc, wa, xa);
+                if (c + 16 < RW_K) load8(wa, xa, wr + c + 16, xr + c + 16);
+                acc = chain8(acc, wb, xb);
+            }
+        } else {
+            for (int c = 0; c < kn; c++) acc = fma(wr[c], xr[c], acc);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    const int t = t0 + tl, e = e0 + el;
+    if (t < T && e < n) score[(size_t)t * n + e] = sigmoid_cr(__double2float_rn(acc));
+}
+
 // One warp per token; scores [T][n] -> idx/w [T][topk]. Each lane keeps the selection
 // scores of experts lane, lane+32, ... in registers (n <= 1024).
 __global__ void __launch_bounds__(128) router_topk_kernel(int *__restrict__ idx,
@@ -255,6 +363,25 @@ static int router_smem_optin()
     return K3GPU_OK;
 }
 
+// The same opt-in for the one-wave kernel.
+static int wave_smem_optin(bool v4)
+{
+    static std::mutex mu;
+    static bool done[64][2] = {};
+    int dev = 0;
+    int st = cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    if (dev < 0 || dev >= 64) return K3GPU_EINVAL;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev][v4]) {
+        st = cuda_status(v4 ? cudaFuncSetAttribute(router_scores_wave_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, RW_SMEM)
+                            : cudaFuncSetAttribute(router_scores_wave_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, RW_SMEM));
+        if (st) return st;
+        done[dev][v4] = true;
+    }
+    return K3GPU_OK;
+}
+
 template <int A, int B>
 static int scores_launch(bool v4, float *score, const float *x, const float *W, int T, int hidden, int n,
                          cudaStream_t s)
@@ -287,6 +414,16 @@ int router_launch(int *idx, float *w, const float *x, const float *W, const floa
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const bool v4 = hidden % 4 == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)W & 15u) == 0;
+    const dim3 gw(ceil_div(n, RW_E), ceil_div(T, RW_T));
+    if ((long long)gw.x * gw.y <= sms) {   // one wave of one-chain-per-thread CTAs
+        int st = wave_smem_optin(v4);
+        if (st) return st;
+        if (v4) router_scores_wave_kernel<4><<<gw, RW_THREADS, RW_SMEM, s>>>(score, x, W, T, hidden, n);
+        else router_scores_wave_kernel<1><<<gw, RW_THREADS, RW_SMEM, s>>>(score, x, W, T, hidden, n);
+        if ((st = launch_status())) return st;
+        router_topk_kernel<<<ceil_div(T, 4), 128, 0, s>>>(idx, w, score, bias, T, n, topk, renorm, routed_scale);
+        return launch_status();
+    }
     static const int shapes[][2] = {{8, 2}, {6, 2}, {4, 2}, {4, 1}, {2, 1}};
     int best = 0;
     double bc = 1e300;

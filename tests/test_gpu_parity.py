@@ -65,7 +65,7 @@ def test_router_fixture(k3):
     np.testing.assert_allclose(host(w), ops["router/topk_weight"], atol=1e-5, rtol=1e-4)
 
 
-@pytest.mark.parametrize("T", [72, 320])
+@pytest.mark.parametrize("T", [5, 72, 320, 1024])   # the one-wave kernel (5, 72) and the tiled one
 def test_router_c2_batches_vs_oracle(k3, T):
     rng = np.random.default_rng(100 + T)
     x = GI.bf16_round(rng.standard_normal((T, 7168), dtype=np.float32))
