@@ -317,7 +317,8 @@ def c4_trees(cont, parent, chain, steps, V, seed):
 def run_c4(args, k3, dev, local, rank=0, world=1):
     """The headline: tree verification steps on the config-4 slice at B sequences per GPU. A
     step is one verify sweep of every sequence's 64-node tree through the 8 layers and the
-    lm_head (k3gpu_model_verify), the on-device greedy tree walk (k3gpu_accept_tree_greedy),
+    lm_head fused with the argmax (k3gpu_model_verify_greedy), the on-device greedy tree walk
+    (k3gpu_accept_tree_greedy on those argmaxes),
     the read of the accepted paths and the commit (k3gpu_model_commit: KDA log replay, MLA
     rows gathered, cached advanced). Accepted tok/s counts every id a step emits (accepted
     drafts plus the bonus id), over all sequences of all ranks. world > 1: the same slice
@@ -354,7 +355,7 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
     x = x0
     cont = [[int(x[b, 0])] for b in range(B)]
     for _ in range(n_cont):
-        arg, _ = model.verify(x)
+        arg, _ = model.verify(x, logits=False)
         model.commit([1] * B)
         x = arg[:, :1].contiguous()
         for b in range(B):
@@ -367,8 +368,8 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
     path_host = torch.empty((B, C4_TREE), dtype=torch.int32).pin_memory()
 
     def step(s, ids):
-        _, lg = model.verify(ids, parent=parent)
-        emit, n_emit, path, _ = k3.accept_tree_greedy(lg, ids, parent_dev)
+        arg, _ = model.verify(ids, parent=parent, logits=False)   # lm_head fused with the argmax
+        emit, n_emit, path, _ = k3.accept_tree_greedy(None, ids, parent_dev, arg=arg)
         n_path_host.copy_(n_emit, non_blocking=True)
         path_host.copy_(path, non_blocking=True)
         stream.synchronize()
@@ -462,9 +463,9 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
     emitted = []          # every sequence's emitted ids, step by step (the stream's fingerprint)
     for s in range(warm):
         ev[0].record(stream)
-        _, lg = model.verify(tok_dev[s], parent=parent)
+        arg, _ = model.verify(tok_dev[s], parent=parent, logits=False)
         ev[1].record(stream)
-        emit, n_emit, path, _ = k3.accept_tree_greedy(lg, tok_dev[s], parent_dev)
+        emit, n_emit, path, _ = k3.accept_tree_greedy(None, tok_dev[s], parent_dev, arg=arg)
         keep = n_emit.tolist()
         ph_path = path.tolist()
         emit_np = emit.cpu().numpy()

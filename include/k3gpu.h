@@ -338,7 +338,8 @@ int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *q_rope,
  * maximum of logits [B][nd+1][vocab]; m = longest prefix with arg[b][i] == d[b][i]
  * (drafts [B][nd]); emit[b][0..m) = d, emit[b][m] = arg[b][m] (the bonus token);
  * n_emit[b] = m + 1. nd_b [B] (device, may be NULL = nd for all) limits each sequence's
- * draft count. emit/arg are [B][nd+1]. */
+ * draft count. emit/arg are [B][nd+1]. logits may be NULL when arg already holds every
+ * position's argmax (k3gpu_model_verify_greedy). */
 int k3gpu_accept_greedy(int *emit, int *n_emit, int *arg, const float *logits,
                         const int *drafts, const int *nd_b, int B, int nd, int vocab,
                         void *stream);
@@ -353,7 +354,8 @@ int k3gpu_argmax(int *arg, const float *logits, int rows, int vocab, void *strea
  * among accepted children of one node the lowest index wins. The accepted path is
  * emitted in order, then the bonus argmax of its last node. logits [B][T][vocab];
  * parent/tok are device arrays [T] and [B][T]; path [B][T] receives the accepted node
- * indices (root first), emit [B][T] the emitted ids, n_emit [B] their count. */
+ * indices (root first), emit [B][T] the emitted ids, n_emit [B] their count. logits may be
+ * NULL when arg [B][T] already holds every node's argmax (k3gpu_model_verify_greedy). */
 int k3gpu_accept_tree_greedy(int *emit, int *n_emit, int *path, int *arg,
                              const float *logits, const int *tok, const int *parent, int B,
                              int T, int vocab, void *stream);
@@ -382,6 +384,17 @@ size_t k3gpu_matmul_bf16_workspace(int T, int in, int out);
 int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ldx, const uint16_t *W,
                             int in, int out, int T, void *workspace, size_t ws_bytes,
                             void *stream);
+
+/* The lm_head fused with the greedy argmax (the verify sweep's logits and argmax_,
+ * src/cli/k3_run.c:1089-1130 and :138-139): arg[t] = first index of the maximum over
+ * o < vocab of sum_i W[o*in + i] * X[t*ldx + i] among non-NaN values, 0 when the value at
+ * o = 0 is NaN (the sequential scan finds nothing greater than NaN), for t < T, without
+ * writing the [T][vocab] logits. The products are those of k3gpu_matmul_bf16_batch run
+ * with one K split; each 128-row block's epilogue keeps its best (value, row) per position
+ * and a second kernel merges the blocks in order. W bf16 bits [vocab][in] as there. */
+size_t k3gpu_lm_head_argmax_workspace(int T, int in, int vocab);
+int k3gpu_lm_head_argmax(int *arg, const float *X, int ldx, const uint16_t *W, int in, int vocab, int T,
+                         void *workspace, size_t ws_bytes, void *stream);
 
 /* ------------------------------------------------------- norms and AttnRes ------ */
 /* k3_rmsnorm (src/core/k3_ops.c:132-140) over T rows: x, y [T][n] (y may be x), w [n];
@@ -620,6 +633,9 @@ int k3gpu_model_reset(K3GpuModel *m);
  * cached + T passes kv_cap. */
 int k3gpu_model_verify(K3GpuModel *m, const int *ids, int T, const int *parent, int *arg,
                        const float **logits);
+/* The same sweep for greedy acceptance: the lm_head fused with the argmax
+ * (k3gpu_lm_head_argmax), arg DEVICE [B][T] filled, no logits written. */
+int k3gpu_model_verify_greedy(K3GpuModel *m, const int *ids, int T, const int *parent, int *arg);
 /* keep: HOST [B], 0..T of the last verify; path: HOST [B][T] (a tree sweep only): the
  * accepted nodes root first along the parents. */
 int k3gpu_model_commit(K3GpuModel *m, const int *keep, const int *path);

@@ -187,6 +187,7 @@ _SIGS = {
     "k3gpu_model_set_stream": ([VP, VP], I),
     "k3gpu_model_reset": ([VP], I),
     "k3gpu_model_verify": ([VP, VP, I, VP, VP, C.POINTER(VP)], I),
+    "k3gpu_model_verify_greedy": ([VP, VP, I, VP, VP], I),
     "k3gpu_model_commit": ([VP, VP, VP], I),
     "k3gpu_model_commit_device": ([VP, VP, VP], I),
     "k3gpu_model_prefill": ([VP, VP, I, VP], I),
@@ -202,6 +203,8 @@ _SIGS = {
     "k3gpu_rmsnorm": ([VP, VP, VP, I, I, F, VP], I),
     "k3gpu_matmul_bf16_workspace": ([I, I, I], SZ),
     "k3gpu_matmul_bf16_batch": ([VP, I, VP, I, VP, I, I, I, VP, SZ, VP], I),
+    "k3gpu_lm_head_argmax_workspace": ([I, I, I], SZ),
+    "k3gpu_lm_head_argmax": ([VP, VP, I, VP, I, I, I, VP, SZ, VP], I),
     "k3gpu_attn_res": ([VP, VP, VP, VP, VP, I, I, I, F, VP], I),
     "k3gpu_moe_prefill_workspace": ([C.POINTER(K3GpuMoeCfg), I], SZ),
     "k3gpu_moe_prefill": ([VP, VP, VP, VP, C.POINTER(K3GpuMoeW), C.POINTER(K3GpuMoeCfg), I, VP, SZ, VP], I),
@@ -507,23 +510,37 @@ def mla_absorbed(q_nope, q_rope, kv_b, lat, rope, cached, mask, v_head, max_ctx,
 
 
 # ------------------------------------------------------------------------ accept ---
-def accept_greedy(logits, drafts, nd_b=None, stream=None):
-    B, T, V = logits.shape
+def accept_greedy(logits, drafts, nd_b=None, stream=None, arg=None):
+    """Greedy chain acceptance from logits [B][nd+1][vocab], or, with logits None, from arg
+    [B][nd+1] already holding every position's argmax (Model.verify(..., logits=False))."""
+    if logits is None:
+        B, T = arg.shape
+        V, dev = 0, arg.device
+    else:
+        B, T, V = logits.shape
+        dev = logits.device
+        arg = torch.empty((B, T), dtype=torch.int32, device=dev)
     nd = T - 1
-    emit = torch.empty((B, T), dtype=torch.int32, device=logits.device)
-    arg = torch.empty((B, T), dtype=torch.int32, device=logits.device)
-    n_emit = torch.empty((B,), dtype=torch.int32, device=logits.device)
+    emit = torch.empty((B, T), dtype=torch.int32, device=dev)
+    n_emit = torch.empty((B,), dtype=torch.int32, device=dev)
     check(lib.k3gpu_accept_greedy(ptr(emit), ptr(n_emit), ptr(arg), ptr(logits), ptr(drafts),
                                   ptr(nd_b), B, nd, V, stream_ptr(stream)), "k3gpu_accept_greedy")
     return emit, n_emit, arg
 
 
-def accept_tree_greedy(logits, tok, parent, stream=None):
-    B, T, V = logits.shape
-    emit = torch.empty((B, T), dtype=torch.int32, device=logits.device)
-    path = torch.empty((B, T), dtype=torch.int32, device=logits.device)
-    arg = torch.empty((B, T), dtype=torch.int32, device=logits.device)
-    n_emit = torch.empty((B,), dtype=torch.int32, device=logits.device)
+def accept_tree_greedy(logits, tok, parent, stream=None, arg=None):
+    """Greedy acceptance over a draft tree from logits [B][T][vocab], or, with logits None,
+    from arg [B][T] already holding every node's argmax (Model.verify(..., logits=False))."""
+    if logits is None:
+        B, T = arg.shape
+        V, dev = 0, arg.device
+    else:
+        B, T, V = logits.shape
+        dev = logits.device
+        arg = torch.empty((B, T), dtype=torch.int32, device=dev)
+    emit = torch.empty((B, T), dtype=torch.int32, device=dev)
+    path = torch.empty((B, T), dtype=torch.int32, device=dev)
+    n_emit = torch.empty((B,), dtype=torch.int32, device=dev)
     check(lib.k3gpu_accept_tree_greedy(ptr(emit), ptr(n_emit), ptr(path), ptr(arg), ptr(logits),
                                        ptr(tok), ptr(parent), B, T, V, stream_ptr(stream)),
           "k3gpu_accept_tree_greedy")
@@ -544,6 +561,20 @@ def matmul_bf16(X, W, out=None, ws=None, stream=None):
                                       n_out, T, ptr(ws), ws.numel(), stream_ptr(stream)),
           "k3gpu_matmul_bf16_batch")
     return Y
+
+
+def lm_head_argmax(X, W, ws=None, stream=None):
+    """The lm_head fused with the greedy argmax: arg int32 [T] = first index of the maximum
+    of X [T][in] . W^T (W bf16 [vocab][in]) over non-NaN values, 0 when the value at index
+    0 is NaN; the logits are never written."""
+    T, n_in = X.shape
+    vocab = W.shape[0]
+    arg = torch.empty(T, dtype=torch.int32, device=X.device)
+    need = lib.k3gpu_lm_head_argmax_workspace(T, n_in, vocab)
+    ws = ws if ws is not None else workspace(need, X.device)
+    check(lib.k3gpu_lm_head_argmax(arg.data_ptr(), X.data_ptr(), X.stride(0), ptr(W), n_in, vocab, T, ptr(ws),
+                                   ws.numel(), stream_ptr(stream)), "k3gpu_lm_head_argmax")
+    return arg
 
 
 # ------------------------------------------------------------- decoder layer -------
@@ -1169,15 +1200,19 @@ class Model:
     def reset(self):
         check(lib.k3gpu_model_reset(self._m), "k3gpu_model_reset")
 
-    def verify(self, ids, parent=None):
+    def verify(self, ids, parent=None, logits=True):
         """ids int32 [B][T] (device) -> (arg int32 [B][T], logits view [B][T][vocab]);
         parent: host list [T] (a draft tree shared by the sequences) or None (a chain).
-        The logits view is the model's own buffer, valid until the next sweep."""
+        The logits view is the model's own buffer, valid until the next sweep. logits=False:
+        the lm_head fused with the argmax (greedy acceptance needs no logits) -> (arg, None)."""
         ids = ids.to(self.device, torch.int32).contiguous()
         B, T = ids.shape
         arg = torch.empty((B, T), dtype=torch.int32, device=self.device)
-        lp = VP()
         par = (C.c_int * T)(*parent) if parent is not None else None
+        if not logits:
+            check(lib.k3gpu_model_verify_greedy(self._m, ptr(ids), T, par, ptr(arg)), "k3gpu_model_verify_greedy")
+            return arg, None
+        lp = VP()
         check(lib.k3gpu_model_verify(self._m, ptr(ids), T, par, ptr(arg), C.byref(lp)), "k3gpu_model_verify")
         return arg, self.logits_view(lp.value, B, T)
 

@@ -331,14 +331,16 @@ extern "C" int k3gpu_accept_greedy(int *emit, int *n_emit, int *arg, const float
                                    const int *drafts, const int *nd_b, int B, int nd, int vocab,
                                    void *stream)
 {
-    if (!emit || !n_emit || !arg || !logits || (!drafts && nd > 0)) return K3GPU_EINVAL;
-    if (B <= 0 || nd < 0 || nd > 1024 || vocab <= 0) return K3GPU_EINVAL;
+    if (!emit || !n_emit || !arg || (!drafts && nd > 0)) return K3GPU_EINVAL;
+    if (B <= 0 || nd < 0 || nd > 1024 || (logits && vocab <= 0)) return K3GPU_EINVAL;
     cudaStream_t s = k3::as_stream(stream);
     const long long rows = (long long)B * (nd + 1);
-    k3::argmax_kernel<<<dim3(k3::AM_CLUSTER, (unsigned)std::min(rows, 65535LL)), k3::AM_THREADS, 0, s>>>(
-        arg, logits, vocab, rows);
-    int st = k3::launch_status();
-    if (st) return st;
+    int st;
+    if (logits) {   // else arg already holds every position's argmax (k3gpu_model_verify_greedy)
+        k3::argmax_kernel<<<dim3(k3::AM_CLUSTER, (unsigned)std::min(rows, 65535LL)), k3::AM_THREADS, 0, s>>>(
+            arg, logits, vocab, rows);
+        if ((st = k3::launch_status())) return st;
+    }
     k3::accept_chain_kernel<<<k3::ceil_div(B, 128), 128, 0, s>>>(emit, n_emit, arg, drafts, nd_b,
                                                                   B, nd);
     return k3::launch_status();
@@ -356,14 +358,16 @@ extern "C" int k3gpu_accept_tree_greedy(int *emit, int *n_emit, int *path, int *
                                         const float *logits, const int *tok, const int *parent,
                                         int B, int T, int vocab, void *stream)
 {
-    if (!emit || !n_emit || !path || !arg || !logits || !tok || !parent) return K3GPU_EINVAL;
-    if (B <= 0 || T <= 0 || T > 4096 || vocab <= 0) return K3GPU_EINVAL;
+    if (!emit || !n_emit || !path || !arg || !tok || !parent) return K3GPU_EINVAL;
+    if (B <= 0 || T <= 0 || T > 4096 || (logits && vocab <= 0)) return K3GPU_EINVAL;
     cudaStream_t s = k3::as_stream(stream);
     const long long rows = (long long)B * T;
-    k3::argmax_kernel<<<dim3(k3::AM_CLUSTER, (unsigned)std::min(rows, 65535LL)), k3::AM_THREADS, 0, s>>>(
-        arg, logits, vocab, rows);
-    int st = k3::launch_status();
-    if (st) return st;
+    int st;
+    if (logits) {   // else arg already holds every node's argmax (k3gpu_model_verify_greedy)
+        k3::argmax_kernel<<<dim3(k3::AM_CLUSTER, (unsigned)std::min(rows, 65535LL)), k3::AM_THREADS, 0, s>>>(
+            arg, logits, vocab, rows);
+        if ((st = k3::launch_status())) return st;
+    }
     k3::accept_tree_kernel<<<k3::ceil_div(B, 128), 128, 0, s>>>(emit, n_emit, path, arg, tok,
                                                                  parent, B, T);
     return k3::launch_status();

@@ -122,7 +122,22 @@ struct Args {
     int ttiles, Tpad;    // position tiles of Np rows; rows of each activation piece
     int n_units, NS, stage_bytes;
     int dbuf;            // Np <= 128: two accumulator sets, so a unit's epilogue overlaps the next unit
+    // the fused greedy argmax (one split only): instead of Y, each unit writes its 128-row
+    // block's best (value, row) per position to best_v/best_i [T][nrb] and, for row block 0,
+    // whether row 0 is NaN to nan0 [T]
+    float *best_v;
+    int *best_i, *nan0;
+    int nrb;
 };
+
+// (v, i) beats (bv, bi): a candidate (i >= 0) over none, a larger value, or an equal value
+// at a smaller index -- the sequential scan's first maximum
+__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi)
+{
+    if (i < 0) return false;
+    if (bi < 0) return true;
+    return v > bv || (v == bv && i < bi);
+}
 
 __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                                                             const __grid_constant__ CUtensorMap xmap, Args a)
@@ -135,6 +150,8 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)a.NS * a.stage_bytes);
     uint64_t *b_full = bars, *b_empty = bars + MAX_NS, *b_dfull = bars + 2 * MAX_NS, *b_dfree = b_dfull + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * MAX_NS + 4);
+    float *red_v = reinterpret_cast<float *>(tmem_slot + 4);   // fused argmax: [4 warps][16 positions]
+    int *red_i = reinterpret_cast<int *>(red_v + 64);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < a.NS; s++) {
@@ -236,6 +253,43 @@ __global__ void __launch_bounds__(THREADS, 1) mmw_tc_kernel(const __grid_constan
                 tmem_ld16(tmem + lane_addr + dcol + (uint32_t)c0, v0);
                 tmem_ld16(tmem + lane_addr + 256u + dcol + (uint32_t)c0, v1);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (a.best_v) {
+                    // the block's best row per position: each warp over its 32 rows by
+                    // shuffles, then warp 0 over the four warps in row order
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const float y = __fadd_rn(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
+                        float bv = y;
+                        int bi = (row < a.out && y == y) ? row : -1;   // NaN is never a candidate
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                            if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                        }
+                        if (lane == 0) { red_v[q * 16 + j] = bv; red_i[q * 16 + j] = bi; }
+                        const int t = tt * a.Np + c0 + j;
+                        if (row == 0 && t < a.T) a.nan0[t] = y != y;
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    if (q == 0 && lane < 16) {
+                        float bv = red_v[lane];
+                        int bi = red_i[lane];
+#pragma unroll
+                        for (int w = 1; w < 4; w++)
+                            if (am_better(red_v[w * 16 + lane], red_i[w * 16 + lane], bv, bi)) {
+                                bv = red_v[w * 16 + lane];
+                                bi = red_i[w * 16 + lane];
+                            }
+                        const int t = tt * a.Np + c0 + lane;
+                        if (t < a.T) {
+                            a.best_v[(size_t)t * a.nrb + rb] = bv;
+                            a.best_i[(size_t)t * a.nrb + rb] = bi;
+                        }
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    continue;
+                }
                 if (row < a.out) {
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
@@ -294,6 +348,32 @@ __global__ void __launch_bounds__(256) split_kernel(__nv_bfloat16 *__restrict__ 
         *reinterpret_cast<uint4 *>(xp + ((size_t)Tpad + t) * in_pad + k0) = *reinterpret_cast<const uint4 *>(lo);
     }
     if (__syncthreads_or(nz) && threadIdx.x == 0) *lo_flag = 1;
+}
+
+// The fused argmax's second half: one warp per position merges the row blocks' bests
+// (blocks in ascending order hold ascending rows, so the first maximum wins on ties) and
+// applies the sequential scan's rule for a NaN at row 0: arg = 0 (no value compares greater
+// than NaN), as when every value is NaN.
+__global__ void __launch_bounds__(256) argmax_merge_kernel(int *__restrict__ arg, const float *__restrict__ best_v,
+                                                           const int *__restrict__ best_i,
+                                                           const int *__restrict__ nan0, int T, int nrb)
+{
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    float bv = 0.0f;
+    int bi = -1;
+    for (int b = lane; b < nrb; b += 32) {
+        const float v = best_v[(size_t)t * nrb + b];
+        const int i = best_i[(size_t)t * nrb + b];
+        if (am_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) arg[t] = (nan0[t] || bi < 0) ? 0 : bi;
 }
 
 // Y[t][o] = sum over splits in order; block (x, t) covers 4 * 256 outputs of row t
@@ -418,15 +498,13 @@ extern "C" size_t k3gpu_matmul_bf16_workspace(int T, int in, int out)
     return align256(xp) + align256(part) + 256;
 }
 
-extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ldx, const uint16_t *W, int in,
-                                       int out, int T, void *workspace, size_t ws_bytes, void *stream)
+// The bf16 trunk matmul over T positions in launches of PASS_T; with arg set, the lm_head
+// fused with the greedy argmax (one K split, no Y): arg [T] receives each position's first
+// maximum, the row blocks' bests staged in the workspace after the activation pieces.
+static int matmul_run(float *Y, int ldy, const float *X, int ldx, const uint16_t *W, int in, int out, int T,
+                      void *workspace, size_t ws_bytes, cudaStream_t s, int *arg)
 {
     using namespace k3::mmw;
-    if (!Y || !X || !W || !workspace || T <= 0 || in <= 0 || out <= 0) return K3GPU_EINVAL;
-    if (in % 8 || ldy < out || ldx < in || (reinterpret_cast<uintptr_t>(W) & 15u)) return K3GPU_EINVAL;
-    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return K3GPU_EINVAL;   // the pieces are stored 16 bytes at a time
-    if (ws_bytes < k3gpu_matmul_bf16_workspace(T, in, out)) return K3GPU_ECAPACITY;
-    cudaStream_t s = k3::as_stream(stream);
     int dev = 0, st = k3::cuda_status(cudaGetDevice(&dev));
     if (st) return st;
     int sms = 148;
@@ -443,13 +521,14 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
     char *ws = static_cast<char *>(workspace);
     CUtensorMap wm;
     if ((st = bf16_map(&wm, W, in, out, 128))) return st;
+    const int nrb = (out + 127) / 128;
     for (int t0 = 0; t0 < T; t0 += PASS_T) {           // launches of up to PASS_T positions
         const int Tc = std::min(PASS_T, T - t0);
         // the K splits this workspace holds partials for (the SM count may differ from the
-        // one the workspace query assumed)
+        // one the workspace query assumed); one split when the argmax is fused
         const size_t xp_b = align256(plan(Tc, in, out, sms, 1).xp_bytes);
         const size_t room = ws_bytes - 256 - xp_b;
-        const int max_split = (int)std::max<size_t>(1, std::min<size_t>(MAX_SPLIT, room / ((size_t)Tc * out * 4)));
+        const int max_split = arg ? 1 : (int)std::max<size_t>(1, std::min<size_t>(MAX_SPLIT, room / ((size_t)Tc * out * 4)));
         const Plan p = plan(Tc, in, out, sms, max_split);
         __nv_bfloat16 *xp = reinterpret_cast<__nv_bfloat16 *>(ws);
         float *part = reinterpret_cast<float *>(ws + xp_b);
@@ -464,8 +543,12 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
         CUtensorMap xm;
         if ((st = bf16_map(&xm, xp, p.in_pad, 2LL * p.Tpad, p.Np))) return st;
         Args a;
-        a.Y = p.nsplit == 1 ? Y + (size_t)t0 * ldy : nullptr;
-        a.part = p.nsplit == 1 ? nullptr : part;
+        a.Y = (!arg && p.nsplit == 1) ? Y + (size_t)t0 * ldy : nullptr;
+        a.part = (!arg && p.nsplit > 1) ? part : nullptr;
+        a.best_v = arg ? reinterpret_cast<float *>(ws + xp_b) : nullptr;
+        a.best_i = arg ? reinterpret_cast<int *>(ws + xp_b + align256((size_t)Tc * nrb * 4)) : nullptr;
+        a.nan0 = arg ? reinterpret_cast<int *>(ws + xp_b + 2 * align256((size_t)Tc * nrb * 4)) : nullptr;
+        a.nrb = nrb;
         a.lo_flag = lo_flag;
         a.T = Tc; a.Np = p.Np; a.in = in; a.out = out; a.ldy = ldy;
         a.nsplit = p.nsplit; a.kst = p.kst; a.n_units = p.n_units;
@@ -474,14 +557,46 @@ extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ld
         a.stage_bytes = W_BYTES + 2 * p.Np * 128;
         a.NS = std::min(MAX_NS, (200 * 1024) / a.stage_bytes);
         // at least 120 KB, so one CTA per SM: each allocates all 512 TMEM columns
-        const int smem = std::max(120 * 1024, a.NS * a.stage_bytes + (2 * MAX_NS + 4) * 8 + 16);
+        const int smem = std::max(120 * 1024, a.NS * a.stage_bytes + (2 * MAX_NS + 4) * 8 + 16 + 512);
         mmw_tc_kernel<<<std::min(p.n_units, sms), THREADS, smem, s>>>(wm, xm, a);
         if ((st = k3::launch_status())) return st;
-        if (p.nsplit > 1) {
+        if (arg) {
+            argmax_merge_kernel<<<(unsigned)((Tc + 7) / 8), 256, 0, s>>>(arg + t0, a.best_v, a.best_i, a.nan0, Tc, nrb);
+            if ((st = k3::launch_status())) return st;
+        } else if (p.nsplit > 1) {
             reduce_kernel<<<dim3((unsigned)((out + 1023) / 1024), (unsigned)Tc), 256, 0, s>>>(
                 Y + (size_t)t0 * ldy, part, Tc, out, ldy, p.nsplit);
             if ((st = k3::launch_status())) return st;
         }
     }
     return K3GPU_OK;
+}
+
+extern "C" int k3gpu_matmul_bf16_batch(float *Y, int ldy, const float *X, int ldx, const uint16_t *W, int in,
+                                       int out, int T, void *workspace, size_t ws_bytes, void *stream)
+{
+    if (!Y || !X || !W || !workspace || T <= 0 || in <= 0 || out <= 0) return K3GPU_EINVAL;
+    if (in % 8 || ldy < out || ldx < in || (reinterpret_cast<uintptr_t>(W) & 15u)) return K3GPU_EINVAL;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return K3GPU_EINVAL;   // the pieces are stored 16 bytes at a time
+    if (ws_bytes < k3gpu_matmul_bf16_workspace(T, in, out)) return K3GPU_ECAPACITY;
+    return matmul_run(Y, ldy, X, ldx, W, in, out, T, workspace, ws_bytes, k3::as_stream(stream), nullptr);
+}
+
+extern "C" size_t k3gpu_lm_head_argmax_workspace(int T, int in, int vocab)
+{
+    using namespace k3::mmw;
+    if (T <= 0 || in <= 0 || vocab <= 0) return 0;
+    const int Tc = std::min(T, PASS_T), nrb = (vocab + 127) / 128;
+    return align256(plan(Tc, in, vocab, 148, 1).xp_bytes) + 2 * align256((size_t)Tc * nrb * 4) +
+           align256((size_t)Tc * 4) + 256;
+}
+
+extern "C" int k3gpu_lm_head_argmax(int *arg, const float *X, int ldx, const uint16_t *W, int in, int vocab, int T,
+                                    void *workspace, size_t ws_bytes, void *stream)
+{
+    if (!arg || !X || !W || !workspace || T <= 0 || in <= 0 || vocab <= 0) return K3GPU_EINVAL;
+    if (in % 8 || ldx < in || (reinterpret_cast<uintptr_t>(W) & 15u)) return K3GPU_EINVAL;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return K3GPU_EINVAL;
+    if (ws_bytes < k3gpu_lm_head_argmax_workspace(T, in, vocab)) return K3GPU_ECAPACITY;
+    return matmul_run(nullptr, vocab, X, ldx, W, in, vocab, T, workspace, ws_bytes, k3::as_stream(stream), arg);
 }

@@ -248,6 +248,7 @@ static size_t model_layout(const K3GpuModelCfg *c, int B, int maxT, int cap, K3G
     if (any_mla) ws_mla = mla_ws_any_ctx(&l, B, maxT, cap);
     ws = std::max(ws, ws_mla);
     ws = std::max(ws, k3gpu_matmul_bf16_workspace(R, E, V));
+    ws = std::max(ws, k3gpu_lm_head_argmax_workspace(R, E, V));
     char *cached = take((size_t)B * 4);
     char *nb = take((size_t)R * 4);
     char *ids = take((size_t)R * 4);
@@ -334,7 +335,8 @@ static int stage_release(K3GpuModel *m, const Stage &st)
 }
 
 // one sweep of T <= maxT positions per sequence from the device ids [B][T]; logit_rows 0:
-// logits and argmax for every position, 1: for each sequence's last position only
+// logits and argmax for every position, 1: for each sequence's last position only, 2: the
+// argmax of every position from the lm_head fused with it (no logits written)
 static int model_sweep(K3GpuModel *m, const int *ids_dev, int T, const int *parent, int logit_rows)
 {
     const K3GpuLayerCfg &l = m->cfg.layer;
@@ -393,6 +395,7 @@ static int model_sweep(K3GpuModel *m, const int *ids_dev, int T, const int *pare
     }
     // lm_head over every position (a verify sweep), or over each sequence's last one (a
     // read-in pass: only the next id after the pass is needed)
+    if (logit_rows == 2) return k3gpu_lm_head_argmax(m->arg, m->nrm, E, m->w.lm_head, E, V, R, m->ws, m->ws_bytes, sp);
     if (logit_rows == 0) {
         if ((st = k3gpu_matmul_bf16_batch(m->logits, V, m->nrm, E, m->w.lm_head, E, V, R, m->ws, m->ws_bytes, sp)))
             return st;
@@ -580,6 +583,19 @@ extern "C" int k3gpu_model_verify(K3GpuModel *m, const int *ids, int T, const in
     m->pre_committed = 0;
     if (logits) *logits = m->logits;
     if (!arg) return K3GPU_OK;
+    return cuda_status(cudaMemcpyAsync(arg, m->arg, (size_t)m->B * T * 4, cudaMemcpyDeviceToDevice,
+                                       as_stream(m->stream)));
+}
+
+extern "C" int k3gpu_model_verify_greedy(K3GpuModel *m, const int *ids, int T, const int *parent, int *arg)
+{
+    using namespace k3;
+    if (!m || !ids || !arg || T <= 0 || T > m->maxT) return K3GPU_EINVAL;
+    int st = model_sweep(m, ids, T, parent, 2);
+    if (st) return st;
+    m->last_T = T;
+    m->last_tree = parent != nullptr;
+    m->pre_committed = 0;
     return cuda_status(cudaMemcpyAsync(arg, m->arg, (size_t)m->B * T * 4, cudaMemcpyDeviceToDevice,
                                        as_stream(m->stream)));
 }

@@ -95,3 +95,61 @@ def test_matmul_bf16_argument_checks(k3):
     # workspace too small
     assert lib.k3gpu_matmul_bf16_batch(Y.data_ptr(), 4, X.data_ptr(), 12, W.data_ptr(), 8, 4, 2,
                                        ws.data_ptr(), 16, None) == k3.K3GPU_ECAPACITY
+
+
+def first_argmax(logits):
+    """argmax_ (src/cli/k3_run.c:138-139) per row: best = 0, then every later value that
+    compares greater -- so the first maximum, NaN never chosen, and 0 when row[0] is NaN."""
+    out = np.zeros(logits.shape[0], np.int32)
+    for t, row in enumerate(logits):
+        if not (np.isnan(row[0]) or np.isnan(row).all()):
+            out[t] = int(np.nanargmax(row))   # the first occurrence of the non-NaN maximum
+    return out
+
+
+@pytest.mark.parametrize("T,vocab", [(37, 1000), (130, 4096)])
+def test_lm_head_argmax_exact_ties_and_nans(k3, T, vocab):
+    """The lm_head fused with the argmax on integer-valued inputs, whose logits are exact
+    in any summation order: the first maximum wins on ties inside a 128-row block and
+    across blocks, NaN logits are never chosen, and a NaN at id 0 gives 0 -- as argmax_
+    finds them on the written logits. A partial last row block (vocab % 128 != 0) too."""
+    rng = np.random.default_rng(T + vocab)
+    n_in = 512
+    X = rng.integers(-2, 3, (T, n_in)).astype(np.float32)
+    Wf = rng.integers(-3, 4, (vocab, n_in)).astype(np.float32)
+    Wf[700 % vocab] = Wf[5] = 3.0                      # the largest rows, tied, in two blocks
+    Wf[9] = Wf[5]                                      # and inside block 0
+    X[3] = np.nan                                      # a position whose logits are all NaN
+    X[4, :] = 0.0                                      # a position whose logits all tie at 0
+    Wb = bf16_bits(Wf)
+    logits = (X.astype(np.float64) @ Wf.T.astype(np.float64)).astype(np.float32)
+    want = first_argmax(logits)
+    got = k3.lm_head_argmax(torch.from_numpy(X).cuda(), torch.from_numpy(Wb.view(np.int16)).cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got, want)
+    # against the written logits' argmax, through the unfused matmul
+    Y = k3.matmul_bf16(torch.from_numpy(X).cuda(), torch.from_numpy(Wb.view(np.int16)).cuda())
+    np.testing.assert_array_equal(got, k3.argmax(Y).cpu().numpy())
+    # a NaN at id 0 alone: every position gives 0
+    Wf0 = Wf.copy()
+    Wf0[0, 7] = np.nan
+    got0 = k3.lm_head_argmax(torch.from_numpy(X).cuda(), torch.from_numpy(bf16_bits(Wf0).view(np.int16)).cuda())
+    assert (got0.cpu().numpy() == 0).all()
+    assert k3.device_status(0) == 0
+
+
+def test_lm_head_argmax_random_matches_written_logits(k3):
+    """Random fp32 activations (two bf16 pieces) over a config-4-sized vocabulary slice: the
+    fused argmax equals the argmax of the unfused matmul's logits wherever the two largest
+    logits are not within the matmuls' rounding of each other."""
+    rng = np.random.default_rng(77)
+    T, n_in, vocab = 72, 7168, 16384
+    X = rng.standard_normal((T, n_in)).astype(np.float32)
+    Wb = bf16_bits(rng.standard_normal((vocab, n_in)).astype(np.float32) * np.float32(0.02))
+    Wd = torch.from_numpy(Wb.view(np.int16)).cuda()
+    got = k3.lm_head_argmax(torch.from_numpy(X).cuda(), Wd).cpu().numpy()
+    Y = k3.matmul_bf16(torch.from_numpy(X).cuda(), Wd).cpu().numpy()
+    want = first_argmax(Y)
+    top2 = np.sort(Y, axis=1)[:, -2:]
+    close = (top2[:, 1] - top2[:, 0]) <= 1e-4 * np.abs(top2[:, 1])
+    assert ((got == want) | close).all()
+    assert (got == want).mean() > 0.95

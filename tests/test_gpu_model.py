@@ -95,6 +95,29 @@ def test_serial_stream_and_logits(k3, model, gold):
     assert k3.device_status() == 0
 
 
+def test_greedy_sweep_fused_argmax_gives_the_reference_ids(k3, model, gold):
+    """The same serial stream with the lm_head fused with the argmax (no logits written,
+    k3gpu_model_verify_greedy): every id equal to the reference's, and the fused argmax of a
+    whole-prompt sweep equal to the argmax of that sweep's written logits."""
+    model.reset()
+    prompt, ref_ids = gold["base/prompt"].tolist(), gold["base/ids"]
+    arg_l, lg = model.verify(ids_dev(prompt))
+    want = arg_l.clone()
+    arg_f, none = model.verify(ids_dev(prompt), logits=False)   # the sweep is tentative: same state
+    assert none is None
+    np.testing.assert_array_equal(arg_f.cpu().numpy(), want.cpu().numpy())
+    model.reset()
+    model.prefill(ids_dev(prompt[:-1]))
+    pending, got = prompt[-1], []
+    for i in range(len(ref_ids)):
+        arg, _ = model.verify(ids_dev([pending]), logits=False)
+        got.append(int(arg[0, 0]))
+        model.commit([1])
+        pending = got[-1]
+    assert got == ref_ids.tolist()
+    assert k3.device_status() == 0
+
+
 def test_native_loop_equals_reference_and_state(k3, model, gold):
     """The engine's decode loop in C (k3_spec_loop) over the model's native callbacks, the
     reference's drafter at spec 4: the same 64 ids, no sweep fired (as in the reference
