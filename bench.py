@@ -188,15 +188,18 @@ def tree_topology(nodes=C4_TREE, branch=C4_BRANCH, depth=C4_DEPTH, weights=(0.5,
     return parent, chain
 
 
-def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1):
+def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1, cfg=None, rank_banks=False):
     """The config-4 slice on the device with random weights: bf16 projections N(0, 0.02),
     unit norms, AttnRes folds N(0, 0.02), router N(0, 0.02) with bias N(0, 0.01), the KDA
     decay parameters of the reference's tiny-model recipe, MXFP4 experts N(0, 0.02).
     world > 1: this rank keeps routed experts rank * 384/world .. of every layer's bank (the
     bank drawn whole, then sliced, so the experts are those of the one-GPU model) and the
     shared expert as a bank of its own; returns (model, shared banks), else (model, None)."""
+    # cfg: another configuration of the same layer shapes (config 5's deep stack); rank_banks:
+    # each rank draws its own routed experts (rank-seeded) and every rank the same shared
+    # expert, instead of slicing one full bank (a 93-layer stack's full banks fit no GPU)
     import torch
-    c = C4
+    c = cfg if cfg is not None else C4
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     E, V = c["hidden_size"], c["vocab_size"]
@@ -230,6 +233,17 @@ def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1):
                      A_log=torch.linspace(-0.4, 1.2, H, device=dev), dt_bias=f32(P, std=0.5), o_norm=ones(D))
         layers.append(d)
         ns = c["num_shared_experts"]
+        if rank_banks:
+            nl = n // world
+            kb = k3.ExpertBank(make_bank_device(nl + (ns if world == 1 else 0), E, I_, seed + 1000 + L + 7919 * rank,
+                                                dev)[0], nl + (ns if world == 1 else 0), E, I_)
+            if world > 1:
+                sb = k3.ExpertBank(make_bank_device(ns, E, I_, seed + 500000 + L, dev)[0], ns, E, I_)
+                sb.scan()
+                shared.append(sb)
+            kb.scan()
+            banks.append(kb)
+            continue
         bank, _, stride = make_bank_device(n + ns, E, I_, seed + 1000 + L, dev)
         if world > 1:
             nl = n // world
@@ -244,6 +258,7 @@ def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1):
         kb.scan()
         banks.append(kb)
     top = {"embed": bf(V, E), "lm_head": bf(V, E), "norm": ones(E), "out_res_fold": f32(E)}
+    torch.cuda.empty_cache()   # the bank draws' temporaries, before the model's one large arena
     model = k3.Model(dict(c), layers, top, banks, B=B, max_T=max_T, kv_cap=kv_cap, device=dev)
     return model, (shared if world > 1 else None)
 
@@ -268,12 +283,17 @@ def c4_fill_state(model, seed, ctx):
     model.set_cached([ctx] * model.B)
 
 
-def c4_snapshot(model):
+def c4_snapshot(model, host=False):
+    """The KDA states and histories of every layer (host=True: in pinned host memory, for a
+    stack whose states would not fit twice on the device)."""
     snap = []
     for L in range(model.cfg["num_hidden_layers"]):
         if (L + 1) not in model.cfg["full_attn_layers"]:
             st, hi = model.kda_state(L)
-            snap.append((st.clone(), hi.clone()))
+            if host:
+                snap.append((st.cpu().pin_memory(), hi.cpu().pin_memory()))
+            else:
+                snap.append((st.clone(), hi.clone()))
     return snap
 
 
@@ -540,6 +560,240 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
     }
 
 
+C5_SEQS, C5_K, C5_CTX, C5_EXPERTS_PER_GPU = 64, 8, 8192, 48
+
+
+def c5_cfg(n_layers, world):
+    """Config 5's stack: config-2 layers (d 7168, FFN 2048 SwiGLU experts top-8 + 1 shared) in
+    the 3:1 KDA:MLA pattern (every fourth layer MLA) with the slice's attention shapes, 48
+    routed experts per GPU (384 at 8 GPUs)."""
+    c = dict(C4)
+    c["num_hidden_layers"] = n_layers
+    c["full_attn_layers"] = [L for L in range(4, n_layers + 1, 4)]
+    c["num_experts"] = C5_EXPERTS_PER_GPU * world
+    return c
+
+
+def run_c5(args, k3, dev, local, rank=0, world=1):
+    """Config 5: the full-depth stack (args.c5_layers layers; 93 fit one B200 beside the 8k
+    caches at 48 experts per GPU), 64 sequences over all ranks each verifying a chain of its
+    pending id and k = 8 drafts against an 8k-position cache: 576 tokens per step. A step is
+    the greedy sweep (k3gpu_model_verify_greedy), the on-device chain acceptance from its
+    argmaxes (k3gpu_accept_greedy), the read of the accepted counts and the commit. The drafts
+    are forced as in config 4: each chain is the model's own greedy continuation (an untimed
+    serial run), so every step accepts all 8 drafts plus the bonus id. world > 1: each rank
+    holds 48 routed experts of every layer (rank-seeded) and verifies 64/world sequences;
+    the token rows cross through peer memory inside every layer's MoE step."""
+    import torch
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    if C5_SEQS % world:
+        raise SystemExit(f"--gpus must divide {C5_SEQS}")
+    B, steps, warm, T = C5_SEQS // world, args.steps, args.warmup, C5_K + 1
+    cfg = c5_cfg(args.c5_layers, world)
+    kv_cap = C5_CTX + (steps + warm + 2) * T + 8
+    t_build = time.perf_counter()
+    model, shared = make_c4_model(k3, dev, B, args.seed, kv_cap, max_T=T, rank=rank, world=world, cfg=cfg,
+                                  rank_banks=True)
+    exchange = None
+    if world > 1:
+        exchange = load_ep().EpExchange(k3, B * T, cfg["hidden_size"], cfg["num_experts_per_token"],
+                                        C5_EXPERTS_PER_GPU)
+        model.set_ep(exchange, shared)
+    build_s = time.perf_counter() - t_build
+    V = cfg["vocab_size"]
+    seed_r = args.seed + 7919 * rank
+    c4_fill_state(model, seed_r + 1, C5_CTX)
+    snap = c4_snapshot(model, host=True)
+    rng = np.random.default_rng(seed_r + 2)
+    pending = torch.tensor(rng.integers(0, V, size=(B,)), dtype=torch.int32, device=dev)
+    # The drafts are the model's own greedy continuation. A deep random stack turns the
+    # last-bit differences between a one-position sweep and a nine-position one into
+    # different argmaxes, so the continuation is taken from the nine-position verify itself:
+    # its fixed point (Jacobi: drafts := the sweep's own argmaxes, shifted; after i rounds
+    # the first i drafts are final), committed whole before the next step's chain is formed.
+    # The timed steps replay these sweeps bit for bit and accept every draft.
+    chains = torch.empty((warm + steps, B, T), dtype=torch.int32, device=dev)
+    jacobi_rounds = []
+    for s in range(warm + steps):
+        ids = torch.cat([pending[:, None], torch.zeros((B, T - 1), dtype=torch.int32, device=dev)], dim=1)
+        for r in range(T + 1):
+            arg, _ = model.verify(ids, logits=False)
+            moved = torch.tensor([float((ids[:, 1:] != arg[:, :-1]).any())], device=dev)
+            if dist:
+                dist.all_reduce(moved, op=dist.ReduceOp.MAX)
+            if moved.item() == 0:
+                break
+            ids = torch.cat([ids[:, :1], arg[:, :-1]], dim=1).contiguous()
+        jacobi_rounds.append(r + 1)
+        chains[s] = ids
+        model.commit([T] * B)
+        pending = arg[:, -1].clone()
+    c4_restore(model, snap, C5_CTX)
+    stream = torch.cuda.current_stream()
+    n_host = torch.empty((B,), dtype=torch.int32).pin_memory()
+
+    def step(ids):
+        arg, _ = model.verify(ids, logits=False)
+        emit, n_emit, _ = k3.accept_greedy(None, ids[:, 1:].contiguous(), arg=arg)
+        n_host.copy_(n_emit, non_blocking=True)
+        stream.synchronize()
+        keep = n_host.tolist()
+        model.commit(keep)
+        return sum(keep), emit
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        return float(t.item())
+
+    for s in range(warm):
+        step(chains[s])
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    accepted = 0
+    sync_all()
+    l0 = k3.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(warm, warm + steps):
+        a, _ = step(chains[s])
+        accepted += a
+    e1.record(stream)
+    sync_all()
+    launches = k3.launch_count() - l0
+    dev_ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    accepted = sum_over_ranks(accepted)
+    status = int(max_over_ranks(k3.device_status(dev.index)))
+    owners_ok = min(model.ep_owners_ok()) if exchange else 1
+    owners_ok = -max_over_ranks(-owners_ok)
+    # end to end: each step's chain ids from pinned host memory, the emitted ids back
+    c4_restore(model, snap, C5_CTX)
+    chains_host = chains.cpu().pin_memory()
+    ids_dev = torch.empty((B, T), dtype=torch.int32, device=dev)
+    emit_host = torch.empty((B, T), dtype=torch.int32).pin_memory()
+    for s in range(warm):
+        ids_dev.copy_(chains_host[s], non_blocking=True)
+        step(ids_dev)
+    acc_e2e = 0
+    sync_all()
+    e0.record(stream)
+    for s in range(warm, warm + steps):
+        ids_dev.copy_(chains_host[s], non_blocking=True)
+        a, emit = step(ids_dev)
+        emit_host.copy_(emit, non_blocking=True)
+        acc_e2e += a
+    e1.record(stream)
+    sync_all()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    acc_e2e = sum_over_ranks(acc_e2e)
+    clk = clocks.stop() if clocks else None
+    # the last layer's local expert phases over a few untimed steps, and the ids they emit
+    c4_restore(model, snap, C5_CTX)
+    k3.moe_phase_timing(True)
+    moe_ph, emitted = [], []
+    idx_last = None
+    for s in range(warm):
+        arg, _ = model.verify(chains[s], logits=False)
+        emit, n_emit, _ = k3.accept_greedy(None, chains[s][:, 1:].contiguous(), arg=arg)
+        keep = n_emit.tolist()
+        moe_ph.append(k3.moe_phase_ms())
+        idx_last = model.last_routing(T).clone()
+        e_np = emit.cpu().numpy()
+        emitted += [e_np[b, :keep[b]] for b in range(B)]
+        model.commit(keep)
+    k3.moe_phase_timing(False)
+    mph = np.median(np.array(moe_ph), axis=0).tolist()
+    E, I_ = cfg["hidden_size"], cfg["moe_intermediate_size"]
+    w13 = 2 * I_ * (E // 2 + E // 32)
+    if dist:
+        alls = [torch.empty_like(idx_last) for _ in range(world)]
+        dist.all_gather(alls, idx_last)
+        g_idx = torch.cat(alls).cpu().numpy()
+        nl = C5_EXPERTS_PER_GPU
+        mine = g_idx[(g_idx >= rank * nl) & (g_idx < (rank + 1) * nl)]
+        u = len(np.unique(mine))
+        rows = int(((g_idx // nl) == rank).any(axis=1).sum())
+        gateup_bytes = u * w13 + rows * E * 4 + int(mine.size) * I_ * 4
+    else:
+        il = idx_last.cpu().numpy()
+        u = len(np.unique(il[il >= 0])) + cfg["num_shared_experts"]
+        gateup_bytes = u * w13 + B * T * E * 4 + B * T * (TOPK + 1) * I_ * 4
+    hbm, peak_kind = peaks()
+    achieved = gateup_bytes / (mph[2] * 1e-3) / 1e9 if mph[2] > 0 else 0.0
+    achieved = -max_over_ranks(-achieved)
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
+    if os.path.exists(tp) and world == 1:
+        try:
+            traffic = int(float(json.load(open(tp))["traffic_over_algorithmic"]) * gateup_bytes)
+        except (OSError, ValueError, KeyError, TypeError):
+            traffic = None
+    if exchange:
+        exchange.close()
+    model.close()
+    del model
+    torch.cuda.empty_cache()
+    full = steps * B * T * world
+    return {
+        "value": round(accepted / (dev_ms * steps * 1e-3), 2), "ms_per_step": round(dev_ms, 3),
+        "accepted_per_step": round(accepted / steps, 2), "accepted_fraction_of_planted": round(accepted / full, 4),
+        "e2e": {"value": round(acc_e2e / (e2e_ms * steps * 1e-3), 2), "unit": "accepted tok/s",
+                "h2d_bytes_per_step": int(B * T * 4 * world), "d2h_bytes_per_step": int((B * 4 + B * T * 4) * world),
+                "ms_per_step": round(e2e_ms, 3)},
+        "moe_phase_ms_last_layer": {"router": round(mph[0], 4), "plan": round(mph[1], 4), "gateup": round(mph[2], 4),
+                                    "down": round(mph[3], 4), "combine": round(mph[4], 4)},
+        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<0> (gate/up, last layer's local expert call)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(gateup_bytes),
+                     "units": f"{u} experts x {w13} B + rows" + (" (slowest rank)" if dist else "")},
+        "fnv_accepted_ids": {"hash": fnv1a64(np.concatenate(emitted).astype(np.int32)),
+                             "over": f"{warm} untimed steps x {B} sequences of rank {rank}: emitted ids, int32"},
+        "gpu_launches": int(launches), "device_status": status, "clocks": clk, "build_s": round(build_s, 1),
+        "planting_sweeps_per_step": round(float(np.mean(jacobi_rounds)), 2),
+        "ep": None if not dist else {"transport": "peer memory inside every layer's MoE step (k3gpu_moe_layer_ep)",
+                                     "experts_per_gpu": C5_EXPERTS_PER_GPU, "owners_ok": bool(owners_ok >= 1)},
+        "config": c5_config(args.c5_layers, world),
+    }
+
+
+def c5_config(n_layers, world):
+    n_mla = n_layers // 4
+    return {"workload": f"K3 full-depth stack (benchmark config 5): {n_layers} layers ({n_layers - n_mla} KDA + "
+                        f"{n_mla} MLA, 3:1), {C5_SEQS} sequences each verifying a k={C5_K} chain "
+                        f"({C5_SEQS * (C5_K + 1)} tokens per step) over an {C5_CTX}-position cache, greedy acceptance",
+            "parallelism": f"ep{world}" if world > 1 else "single", "layers": n_layers,
+            "layers_note": f"{n_layers} layers of {C5_EXPERTS_PER_GPU} routed experts per GPU with the 8k caches "
+                           "fit one B200 (~165 GB); the stack is the same at every GPU count",
+            "d_model": C4["hidden_size"], "vocab": C4["vocab_size"],
+            "moe": f"{C5_EXPERTS_PER_GPU * world} routed top-8 ({C5_EXPERTS_PER_GPU} per GPU) + 1 shared, FFN 2048 "
+                   "SwiGLU, MXFP4 (E2M1 + E8M0/32) N(0,0.02)",
+            "kda": "32 heads x 128", "mla": "64 heads, q_lora 1536, kv_lora 512, nope 128, rope 64, v 128",
+            "sequences_per_gpu": C5_SEQS // world, "tokens_verified_per_step": C5_SEQS * (C5_K + 1),
+            "context": C5_CTX,
+            "drafts": "forced: every chain is the model's own greedy continuation, the fixed point of an "
+                      "untimed Jacobi run of the same nine-position verify (the reference's GATE-4 method)",
+            "weights": "random init: bf16 projections N(0,0.02), MXFP4 experts N(0,0.02)",
+            "l2": "weights streamed per step (~130 GB) exceed the 126 MB L2; no flush needed"}
+
+
 def c4_ep_parity(args, k3, dev, model, snap, ids, parent, rank, world, dist):
     """One tree sweep of the expert-parallel model against the unsharded model on rank 0
     (the same weights, rank 0's state and tree): argmax equal at every node, logits within
@@ -669,8 +923,9 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU baseline ---
-def cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nthreads):
+def cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nthreads, n_routed=None):
     """The reference's kernels over T tokens on the host; returns (seconds, out, idx)."""
+    n_routed = N_ROUTED if n_routed is None else n_routed
     from oracle import oracle as O
     lib = O.ref_bench()
     if lib is None:
@@ -682,7 +937,7 @@ def cpu_reference_run(x_np, gate_np, bias_np, bank_np, offs, stride, T, nthreads
     wt = np.zeros((T, TOPK), np.float32)
     t0 = time.perf_counter()
     rc = lib.ref_moe_layer(out, idx, wt, np.ascontiguousarray(x_np[:T]), gate_np,
-                           bias_np.ctypes.data, bank_np, lay, T, L_DIM, I_DIM, N_ROUTED, N_SHARED,
+                           bias_np.ctypes.data, bank_np, lay, T, L_DIM, I_DIM, n_routed, N_SHARED,
                            TOPK, 1, 4.0, 25.0, nthreads)
     dt = time.perf_counter() - t0
     if rc != 0:
@@ -770,6 +1025,8 @@ def run_reference(args):
     if not torch.cuda.is_available():
         print(json.dumps({"impl": "reference", "unavailable": "the 9 GB expert bank is drawn on the GPU box"}))
         return 0
+    if args.workload == "c5":
+        return run_reference_c5(args)
     bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, "cuda")
     bank_np = bank.cpu().numpy()
     del bank
@@ -802,6 +1059,43 @@ def run_reference(args):
                            for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")},
         "note": "one sequence at a time (the reference engine serves one sequence and drafts chains); "
                 "the GPU arm verifies B sequences' 64-node trees per step",
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_reference_c5(args):
+    """--impl reference for config 5: the reference's per-sequence chain through the stack
+    (c5_reference_sample), one bounded sample per step, on the host cores."""
+    bank_np, offs, stride = c5_bank_np(args)
+    nth = host_threads()
+    for i in range(min(args.warmup, 1)):
+        c5_reference_sample(args, bank_np, offs, stride, nth, args.seed + 100 + i)
+    samples = []
+    for i in range(args.steps):
+        r = c5_reference_sample(args, bank_np, offs, stride, nth, args.seed + i)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": "a reference layer sample failed"}))
+            return 0
+        samples.append(r)
+    steps_s = [r["step_s"] for r in samples]
+    step = statistics.median(steps_s)
+    val = (C5_K + 1) / step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "accepted tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * step, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 / MXFP4 weights x fp32 activations, double accumulate (reference CPU)",
+        "data": "synthetic (seeded random weights, random 8k caches, forced drafts)",
+        "config": c5_config(args.c5_layers, args.gpus),
+        "cpu_baseline": {"value": round(val, 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
+                         "sample": c5_sample_text(args, nth)},
+        "e2e": {"value": round(val, 4), "unit": "accepted tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "all_step_s": [round(x, 3) for x in steps_s],
+        "layer_s_median": {k: round(statistics.median([r[k] for r in samples]), 4)
+                           for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")},
+        "note": "one sequence at a time (the reference engine serves one sequence); the GPU arm verifies "
+                f"{C5_SEQS} sequences' chains per step",
     }
     print(json.dumps(line))
     return 0
@@ -1359,6 +1653,11 @@ def run_b200(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
         try:
+            if args.workload == "c5":
+                c5 = run_c5(args, k3, dev, local, rank, world)
+                if rank == 0:
+                    print(json.dumps(c5_line(args, c5, world, None, None)))
+                return 0
             if args.ep_workload == "c2":
                 return run_ep(args, k3, rank, world, dev)
             c4 = run_c4(args, k3, dev, local, rank, world)
@@ -1369,6 +1668,21 @@ def run_b200(args):
             dist.destroy_process_group()
 
     hbm, peak_kind = peaks()
+    if args.workload == "c5":
+        c5 = run_c5(args, k3, dev, local)   # first: the stack takes ~160 of the 178 GiB
+        rows = {}
+        if not args.no_rows:
+            c4 = run_c4(args, k3, dev, local)
+            rows["c4_slice_tree_verify"] = {k: c4[k] for k in ("value", "ms_per_step", "accepted_per_step",
+                                                               "accepted_fraction_of_planted", "e2e", "roofline",
+                                                               "verify_step_ms", "accept_ms", "commit_ms",
+                                                               "moe_phase_ms_last_layer", "fnv_accepted_ids")}
+            rows["c4_slice_tree_verify"]["config"] = c4["config"]
+            rows["moe_layer_c2"] = c2_rows(args, k3, dev)
+            rows.update(measure_rows(k3, dev, hbm, peaks_tensor()))
+        cpu = None if args.no_cpu else c5_cpu_baseline(args)
+        print(json.dumps(c5_line(args, c5, 1, cpu, rows)))
+        return 0
     rows = {}
     if not args.no_rows and not args.profile_c4:
         rows["moe_layer_c2"] = c2_rows(args, k3, dev)
@@ -1396,6 +1710,24 @@ def c4_line(args, c4, world, cpu, rows):
         "moe_phase_ms_last_layer": c4["moe_phase_ms_last_layer"],
         "gpu_launches": c4["gpu_launches"], "device_status": c4["device_status"],
         "clocks": c4["clocks"], "cpu_baseline": cpu, "build_s": c4["build_s"], "ep": c4["ep"], "rows": rows,
+    }
+    return line
+
+
+def c5_line(args, c5, world, cpu, rows):
+    line = {
+        "metric": METRIC, "value": c5["value"], "unit": "accepted tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": c5["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "MXFP4 experts and bf16 projections x fp32 activations, fp32 accumulate",
+        "data": "synthetic (seeded random weights, random 8k caches, forced drafts)",
+        "config": c5["config"], "e2e": c5["e2e"], "roofline": c5["roofline"],
+        "accepted_per_step": c5["accepted_per_step"],
+        "accepted_fraction_of_planted": c5["accepted_fraction_of_planted"],
+        "fnv_accepted_ids": c5["fnv_accepted_ids"], "moe_phase_ms_last_layer": c5["moe_phase_ms_last_layer"],
+        "gpu_launches": c5["gpu_launches"], "device_status": c5["device_status"], "clocks": c5["clocks"],
+        "cpu_baseline": cpu, "build_s": c5["build_s"], "planting_sweeps_per_step": c5["planting_sweeps_per_step"],
+        "ep": c5["ep"], "rows": rows,
     }
     return line
 
@@ -1464,6 +1796,70 @@ def c4_cpu_baseline(args):
             "layer_s": {k: round(r[k], 4) for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")}}
 
 
+def c5_reference_sample(args, bank_np, offs, stride, nth, seed=0):
+    """The reference engine verifying one sequence's k = 8 chain (its pending id and 8 drafts,
+    all accepted) through the config-5 stack on the host: its k3_kda_layer_log and
+    k3_mla_cached (latent, absorbed, 8192 cached positions) at K3 dimensions timed once each
+    (serial, as the reference runs without OpenMP), its k3_router + k3_matmul_mxfp4 MoE over
+    the 9 tokens on all host threads with a 48-routed-expert bank, the lm_head over a
+    4096-row sample scaled to 163840 rows; summed over the layers as the stack has them.
+    Returns the step seconds and the accepted tok/s they imply (9 ids a step)."""
+    from oracle import oracle as O
+    lib = O.ref_bench()
+    if lib is None:
+        return None
+    for f in ("ref_c4_kda", "ref_c4_mla", "ref_c4_lm_rows"):
+        getattr(lib, f).restype = C.c_double
+        getattr(lib, f).argtypes = [C.c_int, C.c_int, C.c_uint] if f == "ref_c4_mla" else [C.c_int, C.c_uint]
+    T, n_layers = C5_K + 1, args.c5_layers
+    n_mla = n_layers // 4
+    lm_rows = 4096
+    t_kda = lib.ref_c4_kda(T, seed + 1)
+    t_mla = lib.ref_c4_mla(T, C5_CTX, seed + 2)
+    t_lm = lib.ref_c4_lm_rows(T, lm_rows, seed + 3) * C4["vocab_size"] / lm_rows
+    rng = np.random.default_rng(seed + 4)
+    x = rng.standard_normal((T, L_DIM), dtype=np.float32)
+    gate = rng.standard_normal((C5_EXPERTS_PER_GPU, L_DIM), dtype=np.float32) * np.float32(0.02)
+    bias = rng.standard_normal(C5_EXPERTS_PER_GPU, dtype=np.float32) * np.float32(0.01)
+    r = cpu_reference_run(x, gate, bias, bank_np, offs, stride, T, nth, n_routed=C5_EXPERTS_PER_GPU)
+    if r is None or min(t_kda, t_mla, t_lm) < 0:
+        return None
+    t_moe = r[0]
+    step = (n_layers - n_mla) * (t_kda + t_moe) + n_mla * (t_mla + t_moe) + t_lm
+    return {"step_s": step, "value": T / step, "kda_s": t_kda, "mla_s": t_mla, "moe_s": t_moe, "lm_head_s": t_lm}
+
+
+def c5_sample_text(args, nth):
+    n_mla = args.c5_layers // 4
+    return (f"one sequence verifying its 9-position chain (pending id + 8 accepted drafts): the reference's "
+            f"k3_kda_layer_log and k3_mla_cached (latent, absorbed, {C5_CTX} cached positions) at K3 dims timed "
+            f"once each (serial, no OpenMP), its k3_router + k3_matmul_mxfp4 MoE over 9 tokens on {nth} host "
+            f"threads with {C5_EXPERTS_PER_GPU} routed experts, the lm_head over a 4096-row sample scaled to "
+            f"163840, summed as {args.c5_layers - n_mla} x (KDA + MoE) + {n_mla} x (MLA + MoE) + lm_head")
+
+
+def c5_bank_np(args):
+    import torch
+    bank, offs, stride = make_bank_device(C5_EXPERTS_PER_GPU + N_SHARED, L_DIM, I_DIM, args.seed, "cuda")
+    bank_np = bank.cpu().numpy()
+    del bank
+    torch.cuda.empty_cache()
+    return bank_np, offs, stride
+
+
+def c5_cpu_baseline(args):
+    """The reference on the host beside our run (rank 0, N = 1): one bounded sample."""
+    bank_np, offs, stride = c5_bank_np(args)
+    nth = host_threads()
+    r = c5_reference_sample(args, bank_np, offs, stride, nth, args.seed)
+    if r is None:
+        return None
+    return {"value": round(r["value"], 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
+            "isa": "x86-64-v3 (AVX2 + FMA), no OpenMP", "sample": c5_sample_text(args, nth),
+            "step_s": round(r["step_s"], 3),
+            "layer_s": {k: round(r[k], 4) for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")}}
+
+
 def main():
     global N_ROUTED
     ap = argparse.ArgumentParser()
@@ -1480,6 +1876,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-rows", action="store_true", help="skip the other rows' kernel timings")
     ap.add_argument("--no-tc", action="store_true", help="skip the bank scan: mma.sync expert kernels only")
+    ap.add_argument("--workload", default="c5", choices=["c4", "c5"],
+                    help="the headline: config 5's full-depth expert-parallel stack (default; config 4's slice "
+                         "tree verification is a row beside it at one GPU) or config 4 alone")
+    ap.add_argument("--c5-layers", type=int, default=93,
+                    help="layers of the config-5 stack (93, the K3 depth, fit one B200 at 48 experts per GPU)")
     ap.add_argument("--ep-workload", default="c4", choices=["c4", "c2"],
                     help="--gpus N > 1: the config-4 slice expert parallel (default) or one config-2 layer")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
@@ -1500,6 +1901,10 @@ def main():
                     help="routed experts (smaller values give small cases for ncu captures)")
     args = ap.parse_args()
     N_ROUTED = args.n_routed
+    if args.workload == "c5" and "torch" not in sys.modules:
+        # the stack fills ~160 of the 178 GiB: the expert draws' temporaries must not strand
+        # reserved segments that the model's one large arena then cannot use
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
     if args.impl == "reference":
