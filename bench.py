@@ -664,6 +664,16 @@ def run_c5(args, k3, dev, local, rank=0, world=1):
 
     for s in range(warm):
         step(chains[s])
+    if args.profile_c4:   # one step inside an NVTX range, for an ncu launch list
+        sync_all()
+        torch.cuda.nvtx.range_push("c5_step")
+        step(chains[warm])
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        if exchange:
+            exchange.close()
+        model.close()
+        return None
     clocks = ClockSampler(local) if rank == 0 else None
     if clocks:
         clocks.start()
@@ -1670,6 +1680,8 @@ def run_b200(args):
     hbm, peak_kind = peaks()
     if args.workload == "c5":
         c5 = run_c5(args, k3, dev, local)   # first: the stack takes ~160 of the 178 GiB
+        if c5 is None:                      # --profile-c4: one profiled step
+            return 0
         rows = {}
         if not args.no_rows:
             c4 = run_c4(args, k3, dev, local)
@@ -1895,8 +1907,9 @@ def main():
     ap.add_argument("--fp32-acts", action="store_true",
                     help="with --only-c2: full fp32 activations (the model's post-norm rows) instead of bf16")
     ap.add_argument("--profile-c4", action="store_true",
-                    help="build the config-4 slice, run the warm-up steps, then one step inside the NVTX range "
-                         "'c4_step' and exit (for an ncu launch list with --nvtx-include c4_step/)")
+                    help="build the headline workload, run the warm-up steps, then one step inside the NVTX range "
+                         "'c4_step' (--workload c4) or 'c5_step' (c5) and exit (for an ncu launch list with "
+                         "--nvtx-include c5_step/)")
     ap.add_argument("--n-routed", type=int, default=N_ROUTED,
                     help="routed experts (smaller values give small cases for ncu captures)")
     args = ap.parse_args()

@@ -7,7 +7,7 @@
 // sources (exp in float), then out = sum_s p_s * v_s accumulated in float in source order.
 // The decoder layer (src/core/k3_ops.c:2514-2557) builds each position's source stack as
 // its block-residual snapshots followed by its running residual; the kernel reads that
-// stack in place. The double sums are block reductions here (a fixed tree, not the
+// stack in place. The double sums are warp reductions here (a fixed tree, not the
 // reference's sequential order), so the float results agree to an ulp, not bit for bit.
 #include "common.cuh"
 
@@ -46,17 +46,29 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(float *__restrict
 
 constexpr int AR_MAXSRC = 256;   // the reference's per-call score buffer is unbounded; 256 here
 
-// One CTA per position t: sources block_residual[t][0..nb) then cur[t].
+// warp-wide double sum; every lane gets the total
+__device__ __forceinline__ double warp_sum_d(double v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One CTA per position t: sources block_residual[t][0..nb) then cur[t]. A deep stack gives a
+// position dozens of sources (one snapshot per two layers), so the scores are spread over
+// the warps -- warp w takes sources w, w + 8, ...: its sum of squares, the reciprocal, the
+// dot of the normalised source with the fold, each a warp reduction (no block barrier per
+// source), the second pass over the source mostly from L1 -- and the weighted sum reads
+// every source once more. vec: rows 16-byte aligned and n % 4 == 0 (float4 loads).
 __global__ void __launch_bounds__(NORM_THREADS) attn_res_kernel(float *__restrict__ out,
                                                                 const float *__restrict__ block_residual,
                                                                 const float *__restrict__ cur,
                                                                 const float *__restrict__ fold,
                                                                 const int *__restrict__ n_blocks,
-                                                                int maxb, int n, float eps)
+                                                                int maxb, int n, float eps, int vec)
 {
-    __shared__ double red[NORM_THREADS / 32];
     __shared__ float p[AR_MAXSRC];
-    const int t = blockIdx.x;
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int nb = n_blocks[t];
     if (nb < 0 || nb > maxb || nb + 1 > AR_MAXSRC) {
         if (threadIdx.x == 0) flag(DEV_BAD_COUNT);
@@ -67,17 +79,37 @@ __global__ void __launch_bounds__(NORM_THREADS) attn_res_kernel(float *__restric
     auto source = [&](int s) -> const float * {
         return s < nb ? block_residual + ((size_t)t * maxb + s) * n : cur + (size_t)t * n;
     };
-    for (int s = 0; s < nsrc; s++) {
+    for (int s = warp; s < nsrc; s += NORM_THREADS / 32) {
         const float *v = source(s);
         double ss = 0.0;
-        for (int i = threadIdx.x; i < n; i += NORM_THREADS) ss += (double)v[i] * (double)v[i];
-        ss = block_sum(ss, red);
+        if (vec) {
+            for (int i = 4 * lane; i < n; i += 128) {
+                const float4 x = *reinterpret_cast<const float4 *>(v + i);
+                ss += (double)x.x * (double)x.x;
+                ss += (double)x.y * (double)x.y;
+                ss += (double)x.z * (double)x.z;
+                ss += (double)x.w * (double)x.w;
+            }
+        } else {
+            for (int i = lane; i < n; i += 32) ss += (double)v[i] * (double)v[i];
+        }
+        ss = warp_sum_d(ss);
         const float inv = __double2float_rn(1.0 / sqrt(ss / (double)n + (double)eps));
         double acc = 0.0;
-        for (int i = threadIdx.x; i < n; i += NORM_THREADS)
-            acc += (double)__fmul_rn(v[i], inv) * (double)fold[i];
-        acc = block_sum(acc, red);
-        if (threadIdx.x == 0) p[s] = __double2float_rn(acc);
+        if (vec) {
+            for (int i = 4 * lane; i < n; i += 128) {
+                const float4 x = *reinterpret_cast<const float4 *>(v + i);
+                const float4 f = *reinterpret_cast<const float4 *>(fold + i);
+                acc += (double)__fmul_rn(x.x, inv) * (double)f.x;
+                acc += (double)__fmul_rn(x.y, inv) * (double)f.y;
+                acc += (double)__fmul_rn(x.z, inv) * (double)f.z;
+                acc += (double)__fmul_rn(x.w, inv) * (double)f.w;
+            }
+        } else {
+            for (int i = lane; i < n; i += 32) acc += (double)__fmul_rn(v[i], inv) * (double)fold[i];
+        }
+        acc = warp_sum_d(acc);
+        if (lane == 0) p[s] = __double2float_rn(acc);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -92,10 +124,25 @@ __global__ void __launch_bounds__(NORM_THREADS) attn_res_kernel(float *__restric
     }
     __syncthreads();
     float *o = out + (size_t)t * n;
-    for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
-        float a = 0.0f;
-        for (int s = 0; s < nsrc; s++) a = __fadd_rn(a, __fmul_rn(p[s], source(s)[i]));
-        o[i] = a;
+    if (vec) {
+        for (int i = 4 * threadIdx.x; i < n; i += 4 * NORM_THREADS) {
+            float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int s = 0; s < nsrc; s++) {
+                const float4 x = *reinterpret_cast<const float4 *>(source(s) + i);
+                const float ps = p[s];
+                a.x = __fadd_rn(a.x, __fmul_rn(ps, x.x));
+                a.y = __fadd_rn(a.y, __fmul_rn(ps, x.y));
+                a.z = __fadd_rn(a.z, __fmul_rn(ps, x.z));
+                a.w = __fadd_rn(a.w, __fmul_rn(ps, x.w));
+            }
+            *reinterpret_cast<float4 *>(o + i) = a;
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
+            float a = 0.0f;
+            for (int s = 0; s < nsrc; s++) a = __fadd_rn(a, __fmul_rn(p[s], source(s)[i]));
+            o[i] = a;
+        }
     }
 }
 
@@ -116,7 +163,9 @@ extern "C" int k3gpu_attn_res(float *out, const float *block_residual, const flo
     if (!out || !cur || !fold || !n_blocks || T <= 0 || n <= 0 || maxb < 0) return K3GPU_EINVAL;
     if (maxb > 0 && !block_residual) return K3GPU_EINVAL;
     if (maxb + 1 > k3::AR_MAXSRC) return K3GPU_ECAPACITY;
+    const auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const int vec = (n & 3) == 0 && al16(cur) && al16(fold) && al16(out) && (!block_residual || al16(block_residual));
     k3::attn_res_kernel<<<T, k3::NORM_THREADS, 0, k3::as_stream(stream)>>>(out, block_residual, cur, fold,
-                                                                          n_blocks, maxb, n, eps);
+                                                                          n_blocks, maxb, n, eps, vec);
     return k3::launch_status();
 }

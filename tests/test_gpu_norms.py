@@ -51,11 +51,13 @@ def test_rmsnorm_rows_vs_oracle(k3, n):
     close(xd.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("n", [512, 7168])
-def test_attn_res_source_stacks_vs_oracle(k3, n):
-    rng = np.random.default_rng(7 + n)
-    T, maxb = 6, 4
-    nb = np.array([0, 1, 2, 3, 4, 2], np.int32)
+@pytest.mark.parametrize("n,maxb", [(512, 4), (7168, 4), (7168, 48), (510, 12)])
+def test_attn_res_source_stacks_vs_oracle(k3, n, maxb):
+    """Up to 49 sources (a 93-layer stack's snapshots: several per warp) and a width that
+    is not a multiple of four (scalar loads)."""
+    rng = np.random.default_rng(7 + n + maxb)
+    T = 6
+    nb = np.array([0, 1, 2, 3, maxb, maxb // 2], np.int32)
     br = rng.standard_normal((T, maxb, n), dtype=np.float32)
     cur = rng.standard_normal((T, n), dtype=np.float32) * np.float32(2.0)
     fold = (rng.standard_normal(n) * 0.05).astype(np.float32)
