@@ -188,7 +188,8 @@ def tree_topology(nodes=C4_TREE, branch=C4_BRANCH, depth=C4_DEPTH, weights=(0.5,
     return parent, chain
 
 
-def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1, cfg=None, rank_banks=False):
+def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1, cfg=None, rank_banks=False,
+                  gather_ranks=0):
     """The config-4 slice on the device with random weights: bf16 projections N(0, 0.02),
     unit norms, AttnRes folds N(0, 0.02), router N(0, 0.02) with bias N(0, 0.01), the KDA
     decay parameters of the reference's tiny-model recipe, MXFP4 experts N(0, 0.02).
@@ -197,7 +198,9 @@ def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1, cfg=
     shared expert as a bank of its own; returns (model, shared banks), else (model, None)."""
     # cfg: another configuration of the same layer shapes (config 5's deep stack); rank_banks:
     # each rank draws its own routed experts (rank-seeded) and every rank the same shared
-    # expert, instead of slicing one full bank (a 93-layer stack's full banks fit no GPU)
+    # expert, instead of slicing one full bank (a 93-layer stack's full banks fit no GPU);
+    # gather_ranks = G (with world 1): one GPU holds all G ranks' draws as one bank, the
+    # unsharded twin of a G-rank model
     import torch
     c = cfg if cfg is not None else C4
     g = torch.Generator(device=dev)
@@ -233,6 +236,18 @@ def make_c4_model(k3, dev, B, seed, kv_cap, max_T=C4_TREE, rank=0, world=1, cfg=
                      A_log=torch.linspace(-0.4, 1.2, H, device=dev), dt_bias=f32(P, std=0.5), o_norm=ones(D))
         layers.append(d)
         ns = c["num_shared_experts"]
+        if gather_ranks:
+            nl = n // gather_ranks
+            stride = k3.ExpertBank.layout(E, I_).stride
+            bank = torch.empty((n + ns) * stride, dtype=torch.uint8, device=dev)
+            view = bank.view(n + ns, stride)
+            for r in range(gather_ranks):
+                view[r * nl:(r + 1) * nl] = make_bank_device(nl, E, I_, seed + 1000 + L + 7919 * r, dev)[0].view(nl, stride)
+            view[n:n + ns] = make_bank_device(ns, E, I_, seed + 500000 + L, dev)[0].view(ns, stride)
+            kb = k3.ExpertBank(bank, n + ns, E, I_)
+            kb.scan()
+            banks.append(kb)
+            continue
         if rank_banks:
             nl = n // world
             kb = k3.ExpertBank(make_bank_device(nl + (ns if world == 1 else 0), E, I_, seed + 1000 + L + 7919 * rank,
@@ -574,6 +589,56 @@ def c5_cfg(n_layers, world):
     return c
 
 
+def c5_ep_parity(args, k3, dev, rank, world, dist, n_layers=4):
+    """Before the stack is built: one chain sweep of a 4-layer stack of config 5's shapes,
+    expert parallel over the ranks exactly as the stack runs (48 rank-drawn experts per GPU,
+    the rows through peer memory), against the same 4 layers unsharded on rank 0 (every
+    rank's experts drawn again by their seeds into one bank): argmax equal at every position
+    of rank 0's sequences, logits within rel-L2 1e-3. A failed check ends the run."""
+    import torch
+    cfg = c5_cfg(n_layers, world)
+    B, T = C5_SEQS // world, C5_K + 1
+    seed = args.seed + 77
+    model, shared = make_c4_model(k3, dev, B, seed, C5_CTX + 16, max_T=T, rank=rank, world=world, cfg=cfg,
+                                  rank_banks=True)
+    exchange = load_ep().EpExchange(k3, B * T, cfg["hidden_size"], cfg["num_experts_per_token"],
+                                    C5_EXPERTS_PER_GPU)
+    model.set_ep(exchange, shared)
+    c4_fill_state(model, seed + 1 + 7919 * rank, C5_CTX)
+    rng = np.random.default_rng(seed + 2 + 7919 * rank)
+    ids = torch.tensor(rng.integers(0, cfg["vocab_size"], size=(B, T)), dtype=torch.int32, device=dev)
+    arg, lg = model.verify(ids)
+    torch.cuda.synchronize()
+    arg_ep, lg_ep = arg.cpu(), lg.float().cpu()
+    status = k3.device_status(dev.index)
+    owners = min(model.ep_owners_ok())
+    exchange.close()
+    model.close()
+    del model, shared
+    torch.cuda.empty_cache()
+    verdict = torch.zeros(4, dtype=torch.float64, device=dev)
+    if rank == 0:
+        full, _ = make_c4_model(k3, dev, B, seed, C5_CTX + 16, max_T=T, cfg=cfg, gather_ranks=world)
+        c4_fill_state(full, seed + 1, C5_CTX)
+        a1, l1 = full.verify(ids)
+        torch.cuda.synchronize()
+        verdict[0] = float((a1.cpu() != arg_ep).sum())
+        verdict[1] = float((l1.float().cpu() - lg_ep).norm() / l1.float().cpu().norm())
+        full.close()
+        del full
+        torch.cuda.empty_cache()
+    verdict[2] = float(status)
+    verdict[3] = float(1 - owners)
+    dist.all_reduce(verdict, op=dist.ReduceOp.MAX)
+    v = verdict.tolist()
+    out = {"argmax_mismatches": int(v[0]), "logits_rel_l2": float(f"{v[1]:.3g}"), "status_max": int(v[2]),
+           "owners_ok": v[3] == 0, "positions": B * T,
+           "reference": f"the same {n_layers} layers unsharded on one GPU (all ranks' experts), rank 0's state and ids"}
+    if v[0] != 0 or not v[1] < 1e-3 or v[2] != 0 or v[3] != 0:
+        raise SystemExit(f"expert-parallel stack failed its check, no line printed: {out}")
+    return out
+
+
 def run_c5(args, k3, dev, local, rank=0, world=1):
     """Config 5: the full-depth stack (args.c5_layers layers; 93 fit one B200 beside the 8k
     caches at 48 experts per GPU), 64 sequences over all ranks each verifying a chain of its
@@ -591,6 +656,7 @@ def run_c5(args, k3, dev, local, rank=0, world=1):
     if C5_SEQS % world:
         raise SystemExit(f"--gpus must divide {C5_SEQS}")
     B, steps, warm, T = C5_SEQS // world, args.steps, args.warmup, C5_K + 1
+    parity = c5_ep_parity(args, k3, dev, rank, world, dist) if dist and not args.profile_c4 else None
     cfg = c5_cfg(args.c5_layers, world)
     kv_cap = C5_CTX + (steps + warm + 2) * T + 8
     t_build = time.perf_counter()
@@ -779,7 +845,8 @@ def run_c5(args, k3, dev, local, rank=0, world=1):
         "gpu_launches": int(launches), "device_status": status, "clocks": clk, "build_s": round(build_s, 1),
         "planting_sweeps_per_step": round(float(np.mean(jacobi_rounds)), 2),
         "ep": None if not dist else {"transport": "peer memory inside every layer's MoE step (k3gpu_moe_layer_ep)",
-                                     "experts_per_gpu": C5_EXPERTS_PER_GPU, "owners_ok": bool(owners_ok >= 1)},
+                                     "experts_per_gpu": C5_EXPERTS_PER_GPU, "owners_ok": bool(owners_ok >= 1),
+                                     "parity": parity},
         "config": c5_config(args.c5_layers, world),
     }
 
