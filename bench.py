@@ -808,13 +808,23 @@ def run_c5(args, k3, dev, local, rank=0, world=1):
         u = len(np.unique(mine))
         rows = int(((g_idx // nl) == rank).any(axis=1).sum())
         gateup_bytes = u * w13 + rows * E * 4 + int(mine.size) * I_ * 4
+        pairs = int(mine.size) + B * T                       # local routed pairs + the shared expert's
     else:
         il = idx_last.cpu().numpy()
         u = len(np.unique(il[il >= 0])) + cfg["num_shared_experts"]
         gateup_bytes = u * w13 + B * T * E * 4 + B * T * (TOPK + 1) * I_ * 4
+        pairs = B * T * (TOPK + 1)
+    # the gate/up call's algorithmic flops: 2 x (gate + up rows) x hidden per (token, expert)
+    gateup_flops = 2.0 * pairs * 2 * I_ * E
     hbm, peak_kind = peaks()
-    achieved = gateup_bytes / (mph[2] * 1e-3) / 1e9 if mph[2] > 0 else 0.0
-    achieved = -max_over_ranks(-achieved)
+    tf_peak = peaks_tensor()
+    t_s = mph[2] * 1e-3 if mph[2] > 0 else float("inf")
+    achieved = -max_over_ranks(-(gateup_bytes / t_s / 1e9))
+    achieved_tf = -max_over_ranks(-(gateup_flops / t_s / 1e12))
+    # which roof bounds the call: its intensity against the ridge of the measured peaks (at
+    # 96 tokens an expert it is past the ridge, a contraction; at 12, a weight stream)
+    intensity = gateup_flops / max(gateup_bytes, 1)
+    tensor_bound = intensity > tf_peak * 1e12 / (hbm * 1e9)
     traffic = None
     tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
     if os.path.exists(tp) and world == 1:
@@ -836,10 +846,21 @@ def run_c5(args, k3, dev, local, rank=0, world=1):
                 "ms_per_step": round(e2e_ms, 3)},
         "moe_phase_ms_last_layer": {"router": round(mph[0], 4), "plan": round(mph[1], 4), "gateup": round(mph[2], 4),
                                     "down": round(mph[3], 4), "combine": round(mph[4], 4)},
-        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<0> (gate/up, last layer's local expert call)",
-                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(gateup_bytes),
-                     "units": f"{u} experts x {w13} B + rows" + (" (slowest rank)" if dist else "")},
+        "roofline": {"bound": "tensor" if tensor_bound else "hbm",
+                     "kernel": "moe_tc_kernel<0> (gate/up, last layer's local expert call)",
+                     "achieved": round(achieved_tf if tensor_bound else achieved, 1),
+                     "peak": tf_peak if tensor_bound else hbm, "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                     "frac": round(achieved_tf / tf_peak if tensor_bound else achieved / hbm, 4),
+                     "traffic": traffic, "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": int(gateup_bytes), "algorithmic_flops_per_launch": gateup_flops,
+                     "intensity_flop_per_byte": round(intensity, 1),
+                     "ridge_flop_per_byte": round(tf_peak * 1e12 / (hbm * 1e9), 1),
+                     "hbm": {"achieved_gbs": round(achieved, 1), "frac": round(achieved / hbm, 4)},
+                     "tensor": {"achieved_tflops": round(achieved_tf, 1), "frac": round(achieved_tf / tf_peak, 4),
+                                "note": "algorithmic flops; the kernel issues twice as many (fp32 rows as f16 hi "
+                                        "and lo pieces)"},
+                     "units": f"{u} experts x {w13} B + rows, {pairs} (token, expert) pairs"
+                              + (" (slowest rank)" if dist else "")},
         "fnv_accepted_ids": {"hash": fnv1a64(np.concatenate(emitted).astype(np.int32)),
                              "over": f"{warm} untimed steps x {B} sequences of rank {rank}: emitted ids, int32"},
         "gpu_launches": int(launches), "device_status": status, "clocks": clk, "build_s": round(build_s, 1),
