@@ -578,6 +578,15 @@ def run_c4(args, k3, dev, local, rank=0, world=1):
 C5_SEQS, C5_K, C5_CTX, C5_EXPERTS_PER_GPU = 64, 8, 8192, 48
 
 
+def roofline_bound(flops, nbytes, tflops_peak, gbs_peak):
+    """(tensor_bound, intensity, ridge): a call whose algorithmic flops per algorithmic byte
+    exceed the ridge of the measured peaks (TFLOP/s over GB/s, in flop/B) is bounded by the
+    tensor pipe, else by HBM."""
+    intensity = flops / max(nbytes, 1)
+    ridge = tflops_peak * 1e12 / (gbs_peak * 1e9)
+    return intensity > ridge, intensity, ridge
+
+
 def c5_cfg(n_layers, world):
     """Config 5's stack: config-2 layers (d 7168, FFN 2048 SwiGLU experts top-8 + 1 shared) in
     the 3:1 KDA:MLA pattern (every fourth layer MLA) with the slice's attention shapes, 48
@@ -823,8 +832,7 @@ def run_c5(args, k3, dev, local, rank=0, world=1):
     achieved_tf = -max_over_ranks(-(gateup_flops / t_s / 1e12))
     # which roof bounds the call: its intensity against the ridge of the measured peaks (at
     # 96 tokens an expert it is past the ridge, a contraction; at 12, a weight stream)
-    intensity = gateup_flops / max(gateup_bytes, 1)
-    tensor_bound = intensity > tf_peak * 1e12 / (hbm * 1e9)
+    tensor_bound, intensity, ridge = roofline_bound(gateup_flops, gateup_bytes, tf_peak, hbm)
     traffic = None
     tp = os.path.join(ROOT, "profiles", "moe_gateup_traffic.json")
     if os.path.exists(tp) and world == 1:
@@ -853,8 +861,7 @@ def run_c5(args, k3, dev, local, rank=0, world=1):
                      "frac": round(achieved_tf / tf_peak if tensor_bound else achieved / hbm, 4),
                      "traffic": traffic, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": int(gateup_bytes), "algorithmic_flops_per_launch": gateup_flops,
-                     "intensity_flop_per_byte": round(intensity, 1),
-                     "ridge_flop_per_byte": round(tf_peak * 1e12 / (hbm * 1e9), 1),
+                     "intensity_flop_per_byte": round(intensity, 1), "ridge_flop_per_byte": round(ridge, 1),
                      "hbm": {"achieved_gbs": round(achieved, 1), "frac": round(achieved / hbm, 4)},
                      "tensor": {"achieved_tflops": round(achieved_tf, 1), "frac": round(achieved_tf / tf_peak, 4),
                                 "note": "algorithmic flops; the kernel issues twice as many (fp32 rows as f16 hi "

@@ -105,3 +105,20 @@ def test_fnv1a64_known_answers():
     ids = np.array([1, 2, 3], np.int32)
     assert b.fnv1a64(ids) == b.fnv1a64(np.frombuffer(ids.tobytes(), np.uint8))
     assert b.fnv1a64(ids) != b.fnv1a64(ids[::-1])
+
+
+def test_config5_stack_and_roofline_bound():
+    """Config 5's stack: MLA every fourth layer (the 3:1 pattern, one-based), 48 routed
+    experts per GPU; the roofline bound chosen by intensity against the measured ridge."""
+    b = _bench()
+    c = b.c5_cfg(93, 8)
+    assert c["num_hidden_layers"] == 93 and c["num_experts"] == 384
+    assert c["full_attn_layers"] == list(range(4, 93, 4)) and len(c["full_attn_layers"]) == 23
+    assert b.c5_cfg(8, 1)["full_attn_layers"] == [4, 8] and b.c5_cfg(8, 1)["num_experts"] == 48
+    cfg = b.c5_config(93, 2)
+    assert cfg["layers"] == 93 and cfg["sequences_per_gpu"] == 32 and cfg["tokens_verified_per_step"] == 576
+    # config 5 at one GPU: 5184 pairs over 49 experts (past the ridge); at two: a weight stream
+    w13 = 2 * 2048 * (7168 // 2 + 7168 // 32)
+    t1, i1, r1 = b.roofline_bound(2.0 * 5184 * 2 * 2048 * 7168, 49 * w13, 1654.4, 6543.4)
+    t2, i2, _ = b.roofline_bound(2.0 * 2592 * 2 * 2048 * 7168, 48 * w13, 1654.4, 6543.4)
+    assert t1 and not t2 and i2 < r1 < i1 and abs(r1 - 252.8) < 0.1
