@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    const int K = ta.K, NK = K / TC_KC, G = K / 32;
+    const int K = ta.K, NK = K / TC_KC;
     const int n_work = by_pass ? wpre[na] : na * ta.UE;
     const int *Xe = PHASE == 0 ? p.ze : p.he;
     bool failed = false;
@@ -395,6 +395,7 @@ __global__ void __launch_bounds__(CF::THREADS, 1) moe_tc_kernel(const __grid_con
             if (ent.w & 2) continue;                                                         \
             const int e = ent.x, nt = ent.y, q0 = ent.z;                                     \
             const bool lo_any = (ent.w & 1) != 0;                                            \
+            (void)e; (void)q0; (void)lo_any;   /* not every role reads them */                \
             const int tb_end = (int)min((long long)nt, (long long)p1_ * CF::NP);             \
             for (int tb = p0_ * CF::NP; tb < tb_end && !failed; tb += CF::NP) {              \
                 const int npt = min(CF::NP, nt - tb);                                         \
