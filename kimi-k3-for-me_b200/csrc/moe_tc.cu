@@ -42,15 +42,15 @@ constexpr int TC_W_BYTES = 128 * 256;    // packed weights of a stage (32 KB)
 constexpr int TC_S_BYTES = 128 * 16;     // E8M0 bytes of a stage
 
 // The pass shape. Sparse (a verify step: most experts see one to three tokens): up to 8
-// tokens a pass, four issuers (two per K half of a stage, each its own accumulator), three
-// TMEM A buffers and four stages -- the weight bytes in flight per SM, not any unit's rate,
+// tokens a pass, four issuers (two per K half of a stage, each its own accumulator and its
+// own 128-K A sub-buffer) and four stages -- the weight bytes in flight per SM, not any unit's rate,
 // set the stream's pace (at the loaded latency of ~3.4 us, 3 x 32 KB allow ~30 GB/s per
 // SM), and the half-height activation tile is what leaves room for the fourth stage.
 // Dense (many tokens an expert, e.g. a 64-node tree over 16 sequences: ~21 tokens per
 // expert): up to 32 tokens a pass so each weight is decoded once for all of its expert's
 // tokens -- the decode, not the tensor pipe, bounds the sparse shape once an expert needs
 // several passes -- at the cost of one issuer per K half (an N = 64 MMA keeps the pipe busy
-// from one thread), two A buffers, and split rings: at 32 tokens a stage's activation tile
+// from one thread, two A sub-buffers per half), and split rings: at 32 tokens a stage's activation tile
 // (64 KB of hi and lo rows) is twice its weights, and in one ring a stage's weights stay
 // resident until its MMAs finish. Split, the weights and scales (NS stages) return to the
 // TMA as soon as the decode warps have read them, and the activation tiles come in K halves
@@ -89,12 +89,12 @@ template <int NP_, int NMMA_, int NA_, int NS_, int TAB_, int NBH_, int SUBS_> s
     static constexpr int ACOL0 = 2 * PCOLS;             // first A column
     static constexpr int XCH_BYTES = 64 * NP * 4;       // gate/up exchange in the epilogue
     // barriers: full[NS] empty[NS] (split: bfull[NBH][2] bempty[NBH]) aready[NA][2] afree[NA]
-    // pfree[2] (split: pfull[2], the issuers' stage partials final). The two K halves take
-    // turns in the A buffers (sparse: 3 buffers, 2 fills an item) and in the activation slots
-    // (split: 3 slots, 2 fills an item), so each buffer and slot has one full/ready barrier
-    // PER HALF: a half's issuer then sees only its own fills' phases, one after another. On
-    // a barrier both halves' fills completed, an issuer running an item ahead could test a
-    // parity whose phase still belonged to the other half's earlier fill and pass at once.
+    // pfree[2] (split: pfull[2], the issuers' stage partials final). Every parity wait has
+    // one waiter role that sees every phase of its barrier in order: each half owns its A
+    // sub-buffers, and the activation slots, which the halves take turns in (3 slots, 2
+    // fills an item), have one full barrier PER HALF. On a barrier both halves' fills
+    // completed, a waiter running an item ahead could test a parity whose phase still
+    // belonged to the other half's earlier fill and pass at once.
     static constexpr int NBAR_RAW = 2 * NS + 3 * NBH + 3 * NA + 2 + (SPLIT ? 2 : 0);
     static constexpr int NBAR = (NBAR_RAW + 1) & ~1;   // keeps the int4 table 16-byte aligned
     // items between two uses of one A buffer (one activation slot) by the same half: its
