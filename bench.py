@@ -1613,6 +1613,25 @@ def measure_rows(k3, dev, hbm, tflops_peak, only=None):
         except Exception as ex:  # noqa: BLE001
             rows["router"] = {"error": str(ex)[:200]}
 
+    # AttnRes at the config-5 sweep (576 positions x 7168): a stack 24 sources deep (the
+    # 93-layer stack's average) and 48 deep (its last layers); every source read once
+    if only is None or only == "attn_res_c5":
+        try:
+            T, n = 576, 7168
+            ar = {}
+            for nsrc in (24, 48):
+                br = torch.randn((T, nsrc - 1, n), generator=g, device=dev)
+                cur = torch.randn((T, n), generator=g, device=dev)
+                fold = torch.randn((n,), generator=g, device=dev) * 0.05
+                nb = torch.full((T,), nsrc - 1, dtype=torch.int32, device=dev)
+                us = timed(lambda: k3.attn_res(br, cur, fold, nb, 1e-5))
+                ar[f"sources{nsrc}"] = hbm_row(us, (nsrc * T * n + T * n + n + T) * 4,
+                                               f"T={T} n={n}, {nsrc} sources")
+                del br, cur
+            rows["attn_res_c5"] = ar
+        except Exception as ex:  # noqa: BLE001
+            rows["attn_res_c5"] = {"error": str(ex)[:200]}
+
     # greedy accept over the K3 vocabulary: 8 sequences x 9 positions x 163840
     if only is None or only == "accept_greedy_vocab":
         try:
@@ -1994,7 +2013,7 @@ def main():
                     help="--gpus N > 1: token rows through peer memory (default) or NCCL all-to-all")
     ap.add_argument("--only-row", default=None,
                     choices=["kda_c3", "kda_prefill", "mla_absorbed_c4", "trunk_matmul_bf16", "lm_head_bf16_c4",
-                             "trunk_matmul_bf16_t1024", "router", "accept_greedy_vocab"],
+                             "trunk_matmul_bf16_t1024", "router", "attn_res_c5", "accept_greedy_vocab"],
                     help="time one of the other rows alone and print it (for profiling captures)")
     ap.add_argument("--only-c2", type=int, nargs=2, metavar=("B", "K"), default=None,
                     help="time the config-2 layer at one (B, k) point alone and print its row (small cases "

@@ -51,16 +51,37 @@ def test_rmsnorm_rows_vs_oracle(k3, n):
     close(xd.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("n,maxb", [(512, 4), (7168, 4), (7168, 48), (510, 12)])
+@pytest.mark.parametrize("n,maxb", [(512, 4), (7168, 4), (7168, 48), (510, 12), (8192, 6), (3000, 9)])
 def test_attn_res_source_stacks_vs_oracle(k3, n, maxb):
-    """Up to 49 sources (a 93-layer stack's snapshots: several per warp) and a width that
-    is not a multiple of four (scalar loads)."""
+    """Up to 49 sources (a 93-layer stack's snapshots); rows held in registers (the
+    single-pass kernel, widths up to 7168 with ragged last columns at 3000) and the two-pass
+    kernel (8192 wide, and a width that is not a multiple of four: scalar loads)."""
     rng = np.random.default_rng(7 + n + maxb)
     T = 6
     nb = np.array([0, 1, 2, 3, maxb, maxb // 2], np.int32)
     br = rng.standard_normal((T, maxb, n), dtype=np.float32)
     cur = rng.standard_normal((T, n), dtype=np.float32) * np.float32(2.0)
     fold = (rng.standard_normal(n) * 0.05).astype(np.float32)
+    got = k3.attn_res(dev(br), dev(cur), dev(fold), dev(nb), 1e-5).cpu().numpy()
+    for t in range(T):
+        src = np.ascontiguousarray(np.concatenate([br[t, :nb[t]], cur[t:t + 1]]))
+        ref = np.empty(n, np.float32)
+        O.orc().orc_attn_res(ref, src, fold, src.shape[0], n, 1e-5)
+        close(got[t], ref)
+
+
+@pytest.mark.parametrize("n", [7168, 8192])
+def test_attn_res_spread_scores_vs_oracle(k3, n):
+    """Sources of very different scales and a large fold: the scores span tens of units and
+    the maximum rises at several sources, so the single-pass kernel rescales its sums
+    (7168) -- held to the same bar as the two-pass kernel (8192)."""
+    rng = np.random.default_rng(11 + n)
+    T, maxb = 8, 30
+    nb = np.array([30, 29, 17, 5, 1, 0, 30, 12], np.int32)
+    scale = rng.uniform(0.1, 10.0, (T, maxb, 1)).astype(np.float32)
+    br = (rng.standard_normal((T, maxb, n), dtype=np.float32) * scale).astype(np.float32)
+    cur = rng.standard_normal((T, n), dtype=np.float32)
+    fold = rng.standard_normal(n).astype(np.float32) * np.float32(0.3)
     got = k3.attn_res(dev(br), dev(cur), dev(fold), dev(nb), 1e-5).cpu().numpy()
     for t in range(T):
         src = np.ascontiguousarray(np.concatenate([br[t, :nb[t]], cur[t:t + 1]]))
