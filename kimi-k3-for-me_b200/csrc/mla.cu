@@ -9,7 +9,8 @@
 //            shared memory 32 at a time, and keeps an online-softmax state per head:
 //            running max, running sum and u = sum p * lat. Partial states go to the
 //            workspace.
-//   combine  merges the slices of each (node, head) and applies out = W_uv[h] u.
+//   merge    merges the slices of each (node, head) into u (over q_abs's buffer).
+//   out      out = W_uv[h] u, a register-tiled product per head.
 //
 // Scores are fp32 dot products of fp32 queries with the bf16 cache (the cache is the
 // compressed latent the reference stores in fp32; here it is held in bf16 in HBM, half
@@ -64,34 +65,84 @@ static size_t mla_ws_layout(int B, int T, int H, int kvl, int qr, int ns, MlaWs 
     return o;
 }
 
-// grid (H, ceil(B*T / QA_TT)), block 256: qabs[bt][h][j] = sum_i W[h*kvd + i][j] *
-// q_nope[bt][h][i], i ascending (one fma chain per output). A block reads its head's W_uk
-// once for QA_TT query nodes.
-constexpr int QA_TT = 16;
+// grid (H, ceil(B*T / QB_T), ceil(kvl / QB_J)), block 256: qabs[bt][h][j] = sum_i
+// W[h*kvd + i][j] * q_nope[bt][h][i], i ascending (one fma chain per output). A block
+// computes 64 query nodes x 128 columns of one head, the operands staged through shared
+// memory 32 values of i at a time (the next chunk's loads in flight during this chunk's
+// fmas); thread (ty, tx) holds the 8 x 4 outputs of nodes 8 ty.. and columns 4 tx.. in
+// registers (two broadcast float4 loads and one float4 load per 32 fmas).
+constexpr int QB_T = 64, QB_J = 128, QB_K = 32, QB_AS = QB_T + 4;
 __global__ void __launch_bounds__(256) mla_qabs_kernel(float *__restrict__ qabs,
                                                        const float *__restrict__ q_nope,
                                                        const float *__restrict__ kv_b, int BT, int H,
                                                        int qn, int vh, int kvl)
 {
-    __shared__ float sq[QA_TT][256];
-    const int h = blockIdx.x, bt0 = blockIdx.y * QA_TT;
-    const int nt = min(QA_TT, BT - bt0);
+    __shared__ __align__(16) float As[QB_K][QB_AS];  // q_nope chunk [i][node], padded rows
+    __shared__ __align__(16) float Bs[QB_K][QB_J];   // W_uk chunk [i][column]
+    const int h = blockIdx.x, bt0 = blockIdx.y * QB_T, j0 = blockIdx.z * QB_J;
     const int kvd = qn + vh;
-    for (int x = threadIdx.x; x < QA_TT * qn; x += blockDim.x) {
-        const int t = x / qn, i = x % qn;
-        sq[t][i] = t < nt ? q_nope[((size_t)(bt0 + t) * H + h) * qn + i] : 0.0f;
-    }
-    __syncthreads();
-    for (int j = threadIdx.x; j < kvl; j += blockDim.x) {
-        float acc[QA_TT];
+    const int ty = threadIdx.x >> 5, tx = threadIdx.x & 31;
+    float acc[8][4];
 #pragma unroll
-        for (int t = 0; t < QA_TT; t++) acc[t] = 0.0f;
-        for (int i = 0; i < qn; i++) {
-            const float wv = kv_b[((size_t)h * kvd + i) * kvl + j];
+    for (int r = 0; r < 8; r++)
 #pragma unroll
-            for (int t = 0; t < QA_TT; t++) acc[t] = fmaf(wv, sq[t][i], acc[t]);
+        for (int c = 0; c < 4; c++) acc[r][c] = 0.0f;
+    // a chunk's operands: 8 values of q_nope and 16 of W_uk per thread, all loads issued
+    // before any is used; the next chunk's are in flight during this chunk's fmas
+    float ra[QB_K * QB_T / 256], rb[QB_K * QB_J / 256];
+    auto fetch = [&](int i0) {
+        const int kn = min(QB_K, qn - i0);
+#pragma unroll
+        for (int k = 0; k < QB_K * QB_T / 256; k++) {
+            const int x = threadIdx.x + 256 * k, i = x % QB_K, t = x / QB_K;
+            ra[k] = (bt0 + t < BT && i < kn) ? q_nope[((size_t)(bt0 + t) * H + h) * qn + i0 + i] : 0.0f;
         }
-        for (int t = 0; t < nt; t++) qabs[((size_t)(bt0 + t) * H + h) * kvl + j] = acc[t];
+#pragma unroll
+        for (int k = 0; k < QB_K * QB_J / 256; k++) {
+            const int x = threadIdx.x + 256 * k, j = x % QB_J, i = x / QB_J;
+            rb[k] = (j0 + j < kvl && i < kn) ? kv_b[((size_t)h * kvd + i0 + i) * kvl + j0 + j] : 0.0f;
+        }
+    };
+    fetch(0);
+    for (int i0 = 0; i0 < qn; i0 += QB_K) {
+        const int kn = min(QB_K, qn - i0);
+        __syncthreads();
+        // a warp read 32 consecutive i of one node (coalesced) and stores them down a
+        // column of As (the padded rows keep that at 4-way bank conflicts)
+#pragma unroll
+        for (int k = 0; k < QB_K * QB_T / 256; k++) {
+            const int x = threadIdx.x + 256 * k;
+            As[x % QB_K][x / QB_K] = ra[k];
+        }
+#pragma unroll
+        for (int k = 0; k < QB_K * QB_J / 256; k++) {
+            const int x = threadIdx.x + 256 * k;
+            Bs[x / QB_J][x % QB_J] = rb[k];
+        }
+        __syncthreads();
+        if (i0 + QB_K < qn) fetch(i0 + QB_K);
+#pragma unroll 4
+        for (int i = 0; i < kn; i++) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(&As[i][ty * 8]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&As[i][ty * 8 + 4]);
+            const float4 b4 = *reinterpret_cast<const float4 *>(&Bs[i][tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int r = 0; r < 8; r++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) acc[r][c] = fmaf(bv[c], av[r], acc[r][c]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        const int t = bt0 + ty * 8 + r;
+        if (t >= BT) break;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int j = j0 + tx * 4 + c;
+            if (j < kvl) qabs[((size_t)t * H + h) * kvl + j] = acc[r][c];
+        }
     }
 }
 
@@ -219,69 +270,137 @@ __global__ void __launch_bounds__(MLA_THREADS) mla_attend_kernel(
     }
 }
 
-// grid (H, ceil(B*T / CB_TT)), block 256: merge the slices of CB_TT query nodes of head h,
-// then out = W_uv[h] u (a block reads its head's W_uv once). Per output the operation order
-// is the same as one node at a time: merge weights serially, u[j] as one fma chain over
-// the slices, out[r] as 32 lane chains over j then a butterfly.
-constexpr int CB_TT = 8;
-__global__ void __launch_bounds__(256) mla_combine_kernel(float *__restrict__ out, MlaWs w,
-                                                          const float *__restrict__ kv_b,
-                                                          const int *__restrict__ cached, int T,
-                                                          int BT, int H, int qn, int vh, int kvl,
-                                                          int nsplit, int split_len)
+// grid (ceil(H / MG_H), B*T), block 256: merge the slices of one query node for MG_H heads
+// into u[node][h][:] (written over q_abs, which the attention has consumed). The merge
+// weights of each (node, head) come from one thread in slice order -- the maximum,
+// exp(m_s - M), the weighted sum of the slice sums, the reciprocal -- then u[j] = sum_s
+// w_s u_s[j] is one fma chain over the slices; each slice's loads for the thread's 8 heads
+// x 2 columns are issued together (coalesced over j).
+constexpr int MG_H = 8, MG_J = MLA_MAXL / 256;
+__global__ void __launch_bounds__(256) mla_merge_kernel(float *__restrict__ u, MlaWs w,
+                                                        const int *__restrict__ cached, int T, int H,
+                                                        int kvl, int nsplit, int split_len)
 {
-    __shared__ float su[CB_TT][MLA_MAXL];
-    __shared__ float sw[CB_TT][MLA_MAXSPLIT];
-    __shared__ int snu[CB_TT];
-    const int h = blockIdx.x, bt0 = blockIdx.y * CB_TT;
-    const int nt = min(CB_TT, BT - bt0);
-    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0 && wid < nt) {
-        const int bt = bt0 + wid;
-        const int n_ctx = cached[bt / T] + T;
-        const int nsu = max(0, min(nsplit, (n_ctx + split_len - 1) / split_len));
-        const size_t base = ((size_t)bt * H + h) * nsplit;
+    __shared__ float sw[MG_H][MLA_MAXSPLIT];
+    const int bt = blockIdx.y, h0 = blockIdx.x * MG_H;
+    const int n_ctx = cached[bt / T] + T;
+    const int nsu = max(0, min(nsplit, (n_ctx + split_len - 1) / split_len));
+    if (threadIdx.x < MG_H && h0 + (int)threadIdx.x < H) {
+        const int r = threadIdx.x;
+        const size_t base = ((size_t)bt * H + h0 + r) * nsplit;
         float M = -INFINITY;
         for (int s = 0; s < nsu; s++) M = fmaxf(M, w.pm[base + s]);
         float Lsum = 0.0f;
         for (int s = 0; s < nsu; s++) {
             const float f = w.pm[base + s] == -INFINITY ? 0.0f : __expf(w.pm[base + s] - M);
-            sw[wid][s] = f;
+            sw[r][s] = f;
             Lsum += f * w.pl[base + s];
         }
         const float inv = Lsum > 0.0f ? 1.0f / Lsum : 0.0f;
-        for (int s = 0; s < nsu; s++) sw[wid][s] *= inv;
-        snu[wid] = nsu;
+        for (int s = 0; s < nsu; s++) sw[r][s] *= inv;
     }
     __syncthreads();
-    for (int t = 0; t < nt; t++) {
-        const size_t base = ((size_t)(bt0 + t) * H + h) * nsplit;
-        const int nsu = snu[t];
-        for (int j = threadIdx.x; j < kvl; j += blockDim.x) {
-            float a = 0.0f;
-            for (int s = 0; s < nsu; s++) a = fmaf(sw[t][s], w.pu[(base + s) * kvl + j], a);
-            su[t][j] = a;
+    float a[MG_H][MG_J];
+#pragma unroll
+    for (int r = 0; r < MG_H; r++)
+#pragma unroll
+        for (int q = 0; q < MG_J; q++) a[r][q] = 0.0f;
+    for (int s = 0; s < nsu; s++) {
+        float v[MG_H][MG_J];
+#pragma unroll
+        for (int r = 0; r < MG_H; r++)
+#pragma unroll
+            for (int q = 0; q < MG_J; q++) {
+                const int j = threadIdx.x + 256 * q;
+                v[r][q] = (h0 + r < H && j < kvl) ? w.pu[(((size_t)bt * H + h0 + r) * nsplit + s) * kvl + j] : 0.0f;
+            }
+#pragma unroll
+        for (int r = 0; r < MG_H; r++)
+#pragma unroll
+            for (int q = 0; q < MG_J; q++) a[r][q] = fmaf(sw[r][s], v[r][q], a[r][q]);
+    }
+#pragma unroll
+    for (int r = 0; r < MG_H; r++)
+#pragma unroll
+        for (int q = 0; q < MG_J; q++) {
+            const int j = threadIdx.x + 256 * q;
+            if (h0 + r < H && j < kvl) u[((size_t)bt * H + h0 + r) * kvl + j] = a[r][q];
         }
-    }
-    __syncthreads();
+}
+
+// grid (H, ceil(B*T / OB_T), ceil(vh / OB_R)), block 256: out[node][h][r] = sum_j
+// W_uv[h][r][j] u[node][h][j], one fma chain over j ascending. A block computes 64 nodes x
+// 128 rows of one head, the operands staged through shared memory 32 values of j at a time
+// (the next chunk's loads in flight during this chunk's fmas, both read coalesced over j
+// and stored down columns of padded rows); thread (ty, tx) holds nodes 8 ty.. x rows 4 tx..
+constexpr int OB_T = 64, OB_R = 128, OB_K = 32;
+constexpr int OB_AS = OB_T + 4, OB_BS = OB_R + 4;
+__global__ void __launch_bounds__(256, 2) mla_out_kernel(float *__restrict__ out, const float *__restrict__ u,
+                                                      const float *__restrict__ kv_b, int BT, int H, int qn,
+                                                      int vh, int kvl)
+{
+    __shared__ __align__(16) float As[OB_K][OB_AS];   // u chunk [j][node]
+    __shared__ __align__(16) float Bs[OB_K][OB_BS];   // W_uv chunk [j][row]
+    const int h = blockIdx.x, bt0 = blockIdx.y * OB_T, r0 = blockIdx.z * OB_R;
     const int kvd = qn + vh;
-    for (int r = wid; r < vh; r += blockDim.x / 32) {
-        const float *wr = kv_b + ((size_t)h * kvd + qn + r) * kvl;
-        float a[CB_TT];
+    const int ty = threadIdx.x >> 5, tx = threadIdx.x & 31;
+    float acc[8][4];
 #pragma unroll
-        for (int t = 0; t < CB_TT; t++) a[t] = 0.0f;
-        for (int j = lane; j < kvl; j += 32) {
-            const float wv = wr[j];
+    for (int r = 0; r < 8; r++)
 #pragma unroll
-            for (int t = 0; t < CB_TT; t++) a[t] = fmaf(wv, su[t][j], a[t]);
+        for (int c = 0; c < 4; c++) acc[r][c] = 0.0f;
+    float ra[OB_K * OB_T / 256], rb[OB_K * OB_R / 256];
+    auto fetch = [&](int j0) {
+        const int kn = min(OB_K, kvl - j0);
+#pragma unroll
+        for (int k = 0; k < OB_K * OB_T / 256; k++) {
+            const int x = threadIdx.x + 256 * k, j = x % OB_K, t = x / OB_K;
+            ra[k] = (bt0 + t < BT && j < kn) ? u[((size_t)(bt0 + t) * H + h) * kvl + j0 + j] : 0.0f;
         }
 #pragma unroll
-        for (int t = 0; t < CB_TT; t++) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) a[t] += __shfl_xor_sync(0xffffffffu, a[t], o);
+        for (int k = 0; k < OB_K * OB_R / 256; k++) {
+            const int x = threadIdx.x + 256 * k, j = x % OB_K, r = x / OB_K;
+            rb[k] = (j < kn && r0 + r < vh) ? kv_b[((size_t)h * kvd + qn + r0 + r) * kvl + j0 + j] : 0.0f;
         }
-        if (lane == 0)
-            for (int t = 0; t < nt; t++) out[((size_t)(bt0 + t) * H + h) * vh + r] = a[t];
+    };
+    fetch(0);
+    for (int j0 = 0; j0 < kvl; j0 += OB_K) {
+        const int kn = min(OB_K, kvl - j0);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < OB_K * OB_T / 256; k++) {
+            const int x = threadIdx.x + 256 * k;
+            As[x % OB_K][x / OB_K] = ra[k];
+        }
+#pragma unroll
+        for (int k = 0; k < OB_K * OB_R / 256; k++) {
+            const int x = threadIdx.x + 256 * k;
+            Bs[x % OB_K][x / OB_K] = rb[k];
+        }
+        __syncthreads();
+        if (j0 + OB_K < kvl) fetch(j0 + OB_K);
+#pragma unroll 4
+        for (int j = 0; j < kn; j++) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(&As[j][ty * 8]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&As[j][ty * 8 + 4]);
+            const float4 b4 = *reinterpret_cast<const float4 *>(&Bs[j][tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int r = 0; r < 8; r++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) acc[r][c] = fmaf(bv[c], av[r], acc[r][c]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        const int t = bt0 + ty * 8 + r;
+        if (t >= BT) break;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int rr = r0 + tx * 4 + c;
+            if (rr < vh) out[((size_t)t * H + h) * vh + rr] = acc[r][c];
+        }
     }
 }
 
@@ -292,7 +411,7 @@ __global__ void __launch_bounds__(256) mla_combine_kernel(float *__restrict__ ou
 //   S [rows x positions] = [q_abs | q_rope] . [lat | rope]^T        (K = kvl + qr)
 //   u [rows x kvl]      += softmax(S) . lat                          (K = positions)
 // A CTA takes 128 query rows, one half of u's kvl columns and one slice of positions
-// (flash-decoding: slices merge in mla_combine_kernel), 128 positions per tile:
+// (flash-decoding: slices merge in mla_merge_kernel), 128 positions per tile:
 //   warp 0      TMA, score ring: per tile and 64-column atom, Q hi, Q lo and the cache atom
 //   warp 1      TMA, value ring: the tile's latent atoms of this half, two per stage
 //   warp 2      score MMAs (one thread): S = Qhi.C + Qlo.C into one of two TMEM buffers
@@ -809,8 +928,8 @@ extern "C" int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *
                                           static_cast<char *>(workspace));
     if (ws_bytes < need) return K3GPU_ECAPACITY;
     cudaStream_t s = k3::as_stream(stream);
-    k3::mla_qabs_kernel<<<dim3(H, k3::ceil_div(B * T, k3::QA_TT)), 256, 0, s>>>(w.qabs, q_nope, kv_b, B * T, H,
-                                                                               qk_nope, v_head, kv_lora);
+    k3::mla_qabs_kernel<<<dim3(H, k3::ceil_div(B * T, k3::QB_T), k3::ceil_div(kv_lora, k3::QB_J)), 256, 0, s>>>(
+        w.qabs, q_nope, kv_b, B * T, H, qk_nope, v_head, kv_lora);
     int st = k3::launch_status();
     if (st) return st;
     int ns = ns_cc, sl = k3::MLA_SPLIT;
@@ -869,7 +988,11 @@ extern "C" int k3gpu_mla_absorbed(float *out, const float *q_nope, const float *
             w, q_rope, lat, rope, cached, mask, T, H, qk_rope, kv_lora, cap, ns, scale);
         if ((st = k3::launch_status())) return st;
     }
-    k3::mla_combine_kernel<<<dim3(H, k3::ceil_div(B * T, k3::CB_TT)), 256, 0, s>>>(
-        out, w, kv_b, cached, T, B * T, H, qk_nope, v_head, kv_lora, ns, sl);
+    // the merged slices go over q_abs (its last reader, the attention, has run)
+    k3::mla_merge_kernel<<<dim3(k3::ceil_div(H, k3::MG_H), B * T), 256, 0, s>>>(w.qabs, w, cached, T, H, kv_lora,
+                                                                                 ns, sl);
+    if ((st = k3::launch_status())) return st;
+    k3::mla_out_kernel<<<dim3(H, k3::ceil_div(B * T, k3::OB_T), k3::ceil_div(v_head, k3::OB_R)), 256, 0, s>>>(
+        out, w.qabs, kv_b, B * T, H, qk_nope, v_head, kv_lora);
     return k3::launch_status();
 }

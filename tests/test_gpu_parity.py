@@ -426,6 +426,25 @@ def test_mla_absorbed_tensor_core(k3, kvl, qr, B, T, H, cached, tree, qscale):
     assert_clean(k3)
 
 
+# Dozens of context slices to merge, output rows in two 128-row tiles (v_head 160) and a
+# q_nope width that leaves a partial 32-wide chunk (40). qk_rope 16 runs the CUDA-core
+# attention (512 positions a slice: 40 slices), qk_rope 0 with kv_lora 128 the tcgen05 one
+# (47 slices).
+@pytest.mark.parametrize("qr,cached", [(16, 20000), (0, 6000)], ids=["cuda_core_40", "tcgen05_47"])
+def test_mla_absorbed_many_slices(k3, qr, cached):
+    B, T, H, qn, vh, kvl = 1, 3, 4, 40, 160, 128
+    qnope, qrope, kvb, lat, rope, cap = mla_case(29 + qr, B, T, H, qn, qr, vh, kvl, [cached])
+    masks = O.chain_masks(T)
+    scale = 1.0 / np.sqrt(qn + qr)
+    out = k3.mla_absorbed(dev(qnope), dev(qrope), dev(kvb), dev(to_bf16_bits(lat).view(np.int16)),
+                          dev(to_bf16_bits(rope).view(np.int16)), dev(np.array([cached], np.int32)),
+                          dev(masks.view(np.int64)), vh, cap, scale)
+    got = host(out)
+    ref = O.mla_absorbed(qnope[0], qrope[0], kvb, lat[0], rope[0], cached, masks, scale, vh)
+    assert rel_l2(got[0], ref) < 1e-4, rel_l2(got[0], ref)
+    assert_clean(k3)
+
+
 # ------------------------------------------------------------------------- accept --
 def test_accept_greedy_every_acceptance_count(k3):
     B, nd, V = 6, 5, 1000
