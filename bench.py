@@ -1056,7 +1056,7 @@ def kda_prefill_cpu_baseline(T_sample=256, H=32, D=128, seed=5):
     (the reference's library is built here without OpenMP), as positions per second; None
     when the reference library was not built."""
     from oracle import oracle as O
-    lib = O.ref()
+    lib = O.ref_timed()
     if lib is None:
         return None
     rng = np.random.default_rng(seed)
@@ -1071,6 +1071,7 @@ def kda_prefill_cpu_baseline(T_sample=256, H=32, D=128, seed=5):
             lib.k3_kda_step(S[h], o, q[t, h], k[t, h], v[t, h], al[t, h], float(be[t, h]), D, D)
     dt = time.perf_counter() - t0
     return {"value": round(T_sample / dt, 1), "unit": "positions/s", "cores": 1, "kind": "reference",
+            "isa": O.ISA_TEXT[O.ref_bench_isa()],
             "sample": f"{T_sample} positions x {H} heads x {D}: k3_kda_step chained, one thread"}
 
 
@@ -1080,7 +1081,7 @@ def matmul_bf16_cpu_baseline(T, n_in, n_out, rows=256, seed=6):
     cost is linear in them): microseconds for the whole call; None when the reference
     library was not built."""
     from oracle import oracle as O
-    lib = O.ref()
+    lib = O.ref_timed()
     if lib is None:
         return None
     rng = np.random.default_rng(seed)
@@ -1092,6 +1093,7 @@ def matmul_bf16_cpu_baseline(T, n_in, n_out, rows=256, seed=6):
     lib.k3_matmul_bf16_batch_ld(Y, rows, X, n_in, W.ctypes.data, n_in, rows, T)
     dt = time.perf_counter() - t0
     return {"value": round(dt * 1e6 * n_out / rows, 1), "unit": "us per call", "cores": 1, "kind": "reference",
+            "isa": O.ISA_TEXT[O.ref_bench_isa()],
             "sample": f"{rows} of {n_out} output rows at T={T}, in={n_in}, scaled by rows; one thread"}
 
 
@@ -1157,7 +1159,7 @@ def run_reference(args):
         "data": "synthetic (seeded random weights, random 32k cache, forced drafts)",
         "config": c4_config(args.c4_B, None, args.gpus),
         "cpu_baseline": {"value": round(val, 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
-                         "sample": c4_sample_text(nth)},
+                         "isa": O.ISA_TEXT[O.ref_bench_isa()] + ", no OpenMP", "sample": c4_sample_text(nth)},
         "e2e": {"value": round(val, 4), "unit": "accepted tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "all_step_s": [round(x, 3) for x in steps_s],
         "layer_s_median": {k: round(statistics.median([r[k] for r in samples]), 4)
@@ -1172,6 +1174,7 @@ def run_reference(args):
 def run_reference_c5(args):
     """--impl reference for config 5: the reference's per-sequence chain through the stack
     (c5_reference_sample), one bounded sample per step, on the host cores."""
+    from oracle import oracle as O
     bank_np, offs, stride = c5_bank_np(args)
     nth = host_threads()
     for i in range(min(args.warmup, 1)):
@@ -1194,7 +1197,7 @@ def run_reference_c5(args):
         "data": "synthetic (seeded random weights, random 8k caches, forced drafts)",
         "config": c5_config(args.c5_layers, args.gpus),
         "cpu_baseline": {"value": round(val, 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
-                         "sample": c5_sample_text(args, nth)},
+                         "isa": O.ISA_TEXT[O.ref_bench_isa()] + ", no OpenMP", "sample": c5_sample_text(args, nth)},
         "e2e": {"value": round(val, 4), "unit": "accepted tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "all_step_s": [round(x, 3) for x in steps_s],
         "layer_s_median": {k: round(statistics.median([r[k] for r in samples]), 4)
@@ -1728,11 +1731,12 @@ def measure_c2(args, k3, dev, kb, bank, offs, stride, M, seed, n_unsafe, cpu_tok
                               offs, stride, Ts, host_threads())
         del bank_np
         if r is not None:
+            from oracle import oracle as O
             dt, ref_out, ref_idx = r
             got = out.cpu().numpy()[:Ts]
             row["cpu_baseline"] = {
                 "value": round(Ts / dt, 3), "unit": "tok/s", "cores": host_threads(), "kind": "reference",
-                "isa": "x86-64-v3 (AVX2 + FMA), no OpenMP: pthreads over (token, slot) items",
+                "isa": O.ISA_TEXT[O.ref_bench_isa()] + ", no OpenMP: pthreads over (token, slot) items",
                 "sample": f"{Ts} of {M} tokens of the same step through the reference's k3_router + "
                           f"k3_matmul_mxfp4 expert loop ({dt:.2f} s)",
                 "routing_bitexact": bool(np.array_equal(ref_idx, idx_np[:Ts])),
@@ -1907,6 +1911,7 @@ def c4_sample_text(nth):
 def c4_cpu_baseline(args):
     """The reference on the host beside our run (rank 0, N = 1): one bounded sample."""
     import torch
+    from oracle import oracle as O
     bank, offs, stride = make_bank_device(N_ROUTED + N_SHARED, L_DIM, I_DIM, args.seed, "cuda")
     bank_np = bank.cpu().numpy()
     del bank
@@ -1917,7 +1922,7 @@ def c4_cpu_baseline(args):
     if r is None:
         return None
     return {"value": round(r["value"], 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
-            "isa": "x86-64-v3 (AVX2 + FMA), no OpenMP",
+            "isa": O.ISA_TEXT[O.ref_bench_isa()] + ", no OpenMP",
             "sample": c4_sample_text(nth), "step_s": round(r["step_s"], 3),
             "layer_s": {k: round(r[k], 4) for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")}}
 
@@ -1975,13 +1980,14 @@ def c5_bank_np(args):
 
 def c5_cpu_baseline(args):
     """The reference on the host beside our run (rank 0, N = 1): one bounded sample."""
+    from oracle import oracle as O
     bank_np, offs, stride = c5_bank_np(args)
     nth = host_threads()
     r = c5_reference_sample(args, bank_np, offs, stride, nth, args.seed)
     if r is None:
         return None
     return {"value": round(r["value"], 4), "unit": "accepted tok/s", "cores": nth, "kind": "reference",
-            "isa": "x86-64-v3 (AVX2 + FMA), no OpenMP", "sample": c5_sample_text(args, nth),
+            "isa": O.ISA_TEXT[O.ref_bench_isa()] + ", no OpenMP", "sample": c5_sample_text(args, nth),
             "step_s": round(r["step_s"], 3),
             "layer_s": {k: round(r[k], 4) for k in ("kda_s", "mla_s", "moe_s", "lm_head_s")}}
 

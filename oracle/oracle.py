@@ -21,6 +21,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 _orc = None
 _ref = None
+_ref4 = None
 _refb = None
 
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
@@ -92,37 +93,104 @@ def orc():
     return _orc
 
 
+def _load_ref(path):
+    lib = C.CDLL(path)
+    I, F = C.c_int, C.c_float
+    lib.k3_router.argtypes = [i32p, f32p, f32p, f32p, C.c_void_p, I, I, I, I, F]
+    lib.k3_matmul_mxfp4.argtypes = [f32p, f32p, u8p, u8p, I, I, I]
+    lib.k3_mxfp4_dequant.argtypes = [f32p, u8p, u8p, I, I, I]
+    lib.k3_kda_step.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, F, I, I]
+    lib.k3_situ_glu.argtypes = [f32p, f32p, I, F, F]
+    lib.k3_rmsnorm.argtypes = [f32p, f32p, f32p, I, F]
+    lib.k3_shortconv.argtypes = [f32p, f32p, f32p, C.c_void_p, I, I, I]
+    lib.k3_kda_decay.argtypes = [f32p, f32p, f32p, f32p, f32p, I, I, F]
+    lib.k3_matmul_bf16_batch_ld.argtypes = [f32p, I, f32p, I, C.c_void_p, I, I, I]
+    for n in ("k3_router", "k3_matmul_mxfp4", "k3_mxfp4_dequant", "k3_kda_step",
+              "k3_situ_glu", "k3_rmsnorm", "k3_shortconv", "k3_kda_decay",
+              "k3_matmul_bf16_batch_ld"):
+        getattr(lib, n).restype = None
+    return lib
+
+
 def ref():
-    """The reference engine's own numeric core, or None when it was not built here."""
+    """The reference engine's own numeric core (the x86-64-v3 build the parity checks use),
+    or None when it was not built here."""
     global _ref
     if _ref is None:
         path = os.path.join(HERE, "_ref", "libk3ref.so")
         if not os.path.exists(path):
             return None
-        lib = C.CDLL(path)
-        I, F = C.c_int, C.c_float
-        lib.k3_router.argtypes = [i32p, f32p, f32p, f32p, C.c_void_p, I, I, I, I, F]
-        lib.k3_matmul_mxfp4.argtypes = [f32p, f32p, u8p, u8p, I, I, I]
-        lib.k3_mxfp4_dequant.argtypes = [f32p, u8p, u8p, I, I, I]
-        lib.k3_kda_step.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, F, I, I]
-        lib.k3_situ_glu.argtypes = [f32p, f32p, I, F, F]
-        lib.k3_rmsnorm.argtypes = [f32p, f32p, f32p, I, F]
-        lib.k3_shortconv.argtypes = [f32p, f32p, f32p, C.c_void_p, I, I, I]
-        lib.k3_kda_decay.argtypes = [f32p, f32p, f32p, f32p, f32p, I, I, F]
-        lib.k3_matmul_bf16_batch_ld.argtypes = [f32p, I, f32p, I, C.c_void_p, I, I, I]
-        for n in ("k3_router", "k3_matmul_mxfp4", "k3_mxfp4_dequant", "k3_kda_step",
-                  "k3_situ_glu", "k3_rmsnorm", "k3_shortconv", "k3_kda_decay",
-                  "k3_matmul_bf16_batch_ld"):
-            getattr(lib, n).restype = None
-        _ref = lib
+        _ref = _load_ref(path)
     return _ref
 
 
+def ref_timed():
+    """The build of the reference's numeric core that the timed CPU baselines call: the
+    x86-64-v4 one (its AVX-512 paths) when ref_bench_isa() picks it, else ref()."""
+    global _ref4
+    if ref_bench_isa() != "v4":
+        return ref()
+    if _ref4 is None:
+        _ref4 = _load_ref(os.path.join(HERE, "_ref", "v4", "libk3ref4.so"))
+    return _ref4
+
+
+def ref_v4_if_runnable():
+    """The x86-64-v4 build of the numeric core when it was built and this host runs it
+    (for holding it to the v3 build), else None."""
+    global _ref4
+    path = os.path.join(HERE, "_ref", "v4", "libk3ref4.so")
+    if not (os.path.exists(path) and host_has_x86_64_v4()):
+        return None
+    if _ref4 is None:
+        _ref4 = _load_ref(path)
+    return _ref4
+
+
+V4_FLAGS = ("avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl")
+
+
+def host_has_x86_64_v4():
+    """True when this host's CPU reports the AVX-512 subsets of x86-64-v4 (/proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    have = set(line.split(":", 1)[1].split())
+                    return all(x in have for x in V4_FLAGS)
+    except OSError:
+        pass
+    return False
+
+
+def ref_bench_isa(variant=None):
+    """Which build of the timed reference baselines ref_bench() loads: "v4" (the reference's
+    AVX-512 paths) when the host has them and _ref/v4 was built, else "v3" (AVX2 + FMA).
+    K3_REF_ISA=v3 or v4 forces one (v4 only where the host runs it)."""
+    want = variant or os.environ.get("K3_REF_ISA", "")
+    v4 = os.path.join(HERE, "_ref", "v4", "libk3ref_bench.so")
+    if want == "v3":
+        return "v3"
+    if os.path.exists(v4) and host_has_x86_64_v4():
+        return "v4"
+    return "v3"
+
+
+ISA_TEXT = {"v3": "x86-64-v3 (AVX2 + FMA)", "v4": "x86-64-v4 (AVX-512: the reference's __AVX512F__ paths)"}
+
+
+def ref_bench_path(variant=None):
+    isa = ref_bench_isa(variant)
+    return os.path.join(HERE, "_ref", "v4", "libk3ref_bench.so") if isa == "v4" else \
+        os.path.join(HERE, "_ref", "libk3ref_bench.so")
+
+
 def ref_bench():
-    """The reference-kernel CPU baseline harness, or None when it was not built here."""
+    """The reference-kernel CPU baseline harness (the build ref_bench_isa() names), or None
+    when it was not built here."""
     global _refb
     if _refb is None:
-        path = os.path.join(HERE, "_ref", "libk3ref_bench.so")
+        path = ref_bench_path()
         if not os.path.exists(path):
             return None
         lib = C.CDLL(path)

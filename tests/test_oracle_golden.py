@@ -409,3 +409,48 @@ def test_reference_library_matches_goldens_when_built():
     x, W, b = GI.router_inputs(case)
     idx, w = O.router(x, W, b, case["topk"], lib=lib)
     np.testing.assert_array_equal(idx, g[case["name"] + "/idx"])
+
+
+def test_reference_isa_builds_agree_bit_for_bit():
+    """The x86-64-v4 build of the reference's numeric core (its AVX-512 paths), which the
+    timed CPU baselines use on hosts that have them, gives the same bits as the x86-64-v3
+    build that the parity checks use, as the reference's floating-point contract promises
+    for its ISA paths (src/core/k3_ops.c:8-25): the router, the MXFP4 matmul, the batched
+    bf16 matmul and the KDA step."""
+    v3, v4 = O.ref(), O.ref_v4_if_runnable()
+    if v3 is None or v4 is None:
+        pytest.skip("needs both reference builds and an x86-64-v4 host")
+    for case in GI.ROUTER_CASES:
+        x, W, b = GI.router_inputs(case)
+        i3, w3 = O.router(x, W, b, case["topk"], lib=v3)
+        i4, w4 = O.router(x, W, b, case["topk"], lib=v4)
+        np.testing.assert_array_equal(i3, i4)
+        np.testing.assert_array_equal(w3.view(np.uint32), w4.view(np.uint32))
+    for case in GI.MXFP4_CASES:
+        packed, scales, x = GI.mxfp4_inputs(case)
+        rows, n_in = case["rows"], case["in"]
+        y = [np.zeros(rows, np.float32) for _ in range(2)]
+        for lib, out in zip((v3, v4), y):
+            lib.k3_matmul_mxfp4(out, x, packed, scales, n_in, rows, 32)
+        np.testing.assert_array_equal(y[0].view(np.uint32), y[1].view(np.uint32))
+    rng = np.random.default_rng(41)
+    T, n_in, n_out = 9, 1024, 96
+    X = rng.standard_normal((T, n_in)).astype(np.float32)
+    Wb = ((rng.standard_normal((n_out, n_in)).astype(np.float32) * np.float32(0.02)).view(np.uint32) >> 16) \
+        .astype(np.uint16)
+    Y = [np.zeros((T, n_out), np.float32) for _ in range(2)]
+    for lib, out in zip((v3, v4), Y):
+        lib.k3_matmul_bf16_batch_ld(out, n_out, X, n_in, Wb.ctypes.data, n_in, n_out, T)
+    np.testing.assert_array_equal(Y[0].view(np.uint32), Y[1].view(np.uint32))
+    D = 128
+    S0 = (rng.standard_normal((D, D)) * 0.1).astype(np.float32)
+    q, k, v = (rng.standard_normal(D).astype(np.float32) for _ in range(3))
+    al = rng.uniform(0.9, 0.999, D).astype(np.float32)
+    outs = []
+    for lib in (v3, v4):
+        S, o = S0.copy(), np.zeros(D, np.float32)
+        for _ in range(4):
+            lib.k3_kda_step(S, o, q, k, v, al, 0.4, D, D)
+        outs.append((S, o))
+    np.testing.assert_array_equal(outs[0][0].view(np.uint32), outs[1][0].view(np.uint32))
+    np.testing.assert_array_equal(outs[0][1].view(np.uint32), outs[1][1].view(np.uint32))
