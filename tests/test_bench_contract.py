@@ -122,3 +122,37 @@ def test_config5_stack_and_roofline_bound():
     t1, i1, r1 = b.roofline_bound(2.0 * 5184 * 2 * 2048 * 7168, 49 * w13, 1654.4, 6543.4)
     t2, i2, _ = b.roofline_bound(2.0 * 2592 * 2 * 2048 * 7168, 48 * w13, 1654.4, 6543.4)
     assert t1 and not t2 and i2 < r1 < i1 and abs(r1 - 252.8) < 0.1
+
+
+def test_reference_build_choice_follows_the_host_cpu(monkeypatch, tmp_path):
+    """The timed reference baselines load the x86-64-v4 build only where it was built and the
+    host reports the AVX-512 subsets; K3_REF_ISA=v3 forces the v3 build; every baseline line
+    names the ISA it timed."""
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    flags_v4 = "flags\t\t: fpu sse2 avx2 fma avx512f avx512bw avx512cd avx512dq avx512vl\n"
+    flags_v3 = "flags\t\t: fpu sse2 avx2 fma\n"
+    real_open = open
+
+    def fake_cpuinfo(text):
+        def opener(path, *a, **k):
+            if path == "/proc/cpuinfo":
+                p = tmp_path / "cpuinfo"
+                p.write_text(text)
+                return real_open(p, *a, **k)
+            return real_open(path, *a, **k)
+        return opener
+
+    import builtins
+    monkeypatch.setattr(builtins, "open", fake_cpuinfo(flags_v3))
+    assert not O.host_has_x86_64_v4()
+    assert O.ref_bench_isa() == "v3"
+    monkeypatch.setattr(builtins, "open", fake_cpuinfo(flags_v4))
+    assert O.host_has_x86_64_v4()
+    built = os.path.exists(os.path.join(ROOT, "oracle", "_ref", "v4", "libk3ref_bench.so"))
+    assert O.ref_bench_isa() == ("v4" if built else "v3")
+    monkeypatch.setenv("K3_REF_ISA", "v3")
+    assert O.ref_bench_isa() == "v3"
+    assert O.ref_bench_path().endswith(os.path.join("_ref", "libk3ref_bench.so"))
+    assert set(O.ISA_TEXT) == {"v3", "v4"}
